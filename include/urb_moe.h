@@ -1,0 +1,225 @@
+/*
+ * urb_moe.h — C ABI of the B200 routed-expert (MoE) hot path.
+ *
+ * This is the drop-in boundary for Urbilateria's routed-expert feed-forward path.  Every entry
+ * point names the reference interface it replaces (paths relative to the Urbilateria source
+ * tree, v0.2.4).  The ABI is plain C: handles, host pointers, sizes and int status codes; no
+ * C++ or CUDA types cross it.  A Rust `build.rs` links liburb_moe.a (built by nvcc for
+ * sm_100a) and binds these symbols with `extern "C"`.
+ *
+ * Conventions
+ *  - Weights are row-major [rows, cols]; y = W x (src/model/matrix.rs:33-38).
+ *  - MXFP4: packed[row*ceil(cols/2) + col/2], even column = low nibble; one E8M0 scale per
+ *    `group_size` columns: scales[row*ceil(cols/group) + col/group] (src/math/mxfp.rs:1418-1423).
+ *  - MXFP8: values[row*cols + col] (E4M3FN); scales[(row/block_rows)*ceil(cols/block_cols) +
+ *    col/block_cols] (src/math/mxfp.rs:434-440).
+ *  - Batched inputs/outputs are token-major: x [batch, cols], y [batch, rows]
+ *    (src/math/mxfp.rs:1544-1549).
+ *  - Functions without a `_device` suffix take HOST pointers and return when the results are
+ *    in host memory.  `_device` variants take device pointers, enqueue on the context stream
+ *    and report errors through a device status word (see urb_status_*), so they can be
+ *    captured in a CUDA graph.
+ *  - Thread safety: a context serialises its calls with an internal mutex; use one context
+ *    per host thread for concurrency.  Every call is stream-ordered on the context stream.
+ *
+ * Numerics: weights are decoded exactly (E2M1/E4M3 x E8M0 -> f16 with a per-row power-of-two
+ * offset, BF16 kept as bf16); activations enter the tensor cores as an exact-to-2^-22 hi+lo
+ * split; products are exact and accumulate in fp32.  Results match the reference's ordered-F64
+ * CPU outputs to relative L2 <= 1e-3.  Router logits are computed with the reference's
+ * sequential F64 order and are bit-identical; top-k indices, the token permutation and the
+ * per-expert counts are bit-identical to the reference.
+ */
+#ifndef URB_MOE_H
+#define URB_MOE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define URB_API __attribute__((visibility("default")))
+#else
+#define URB_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes.  1-4 mirror MxError / RouteError / MatrixError variants
+ * (src/math/mxfp.rs:17-23, src/math/routing.rs:16-21, src/model/weight.rs:5-48). */
+typedef enum urb_status {
+    URB_OK = 0,
+    URB_ERR_SHAPE = 1,             /* MxError::Shape, MatrixError::InputLength/InvalidShape */
+    URB_ERR_INVALID_SCALE = 2,     /* MxError::InvalidScale (E8M0 0xFF) */
+    URB_ERR_NONFINITE = 3,         /* MxError::NonFinite, RouteError::NonFinite */
+    URB_ERR_INVALID_GEOMETRY = 4,  /* RouteError::InvalidGeometry */
+    URB_ERR_CUDA = 5,              /* CUDA runtime failure (see urb_last_error) */
+    URB_ERR_TIMEOUT = 6,           /* a bounded device wait gave up */
+    URB_ERR_NCCL = 7,              /* NCCL failure in the expert-parallel path */
+    URB_ERR_UNSUPPORTED = 8,       /* configuration outside what this build implements */
+    URB_ERR_INVALID_ARGUMENT = 9,  /* null handle / pointer */
+} urb_status;
+
+typedef enum urb_format {
+    URB_FMT_F32 = 0,   /* DenseMatrix (src/model/matrix.rs) */
+    URB_FMT_BF16 = 1,  /* Bf16Matrix (src/model/bf16.rs) */
+    URB_FMT_MXFP8 = 2, /* MxFp8Matrix with E8M0 scales (src/math/mxfp.rs:321) */
+    URB_FMT_MXFP4 = 3, /* MxFp4Matrix (src/math/mxfp.rs:1363) */
+} urb_format;
+
+typedef struct urb_ctx urb_ctx;
+typedef struct urb_mat urb_mat;
+typedef struct urb_layer urb_layer;
+
+/* ---- context ---------------------------------------------------------------------------- */
+
+/* Creates a context on CUDA `device` with its own stream.  Replaces the process-wide Rayon
+ * pool set-up `configure_threads` (src/execution.rs:59). */
+URB_API int urb_ctx_create(int device, urb_ctx **out);
+URB_API int urb_ctx_destroy(urb_ctx *ctx);
+/* Use the caller's cudaStream_t (passed as void*) instead of the context stream. */
+URB_API int urb_ctx_set_stream(urb_ctx *ctx, void *cuda_stream);
+URB_API void *urb_ctx_stream(urb_ctx *ctx);
+/* Copies the last error message (NUL-terminated) into buf; returns the status it belongs to. */
+URB_API int urb_last_error(urb_ctx *ctx, char *buf, size_t len);
+/* Waits for all work on the context stream. */
+URB_API int urb_ctx_synchronize(urb_ctx *ctx);
+
+/* ---- weight matrices (resident in HBM) --------------------------------------------------- */
+
+/* MxFp4Matrix::from_packed (src/math/mxfp.rs:1371-1443): validates shape (Shape) and every
+ * scale (InvalidScale for 0xFF), then keeps the matrix resident on the device.  `packed` and
+ * `scales` may be host or device pointers. */
+URB_API int urb_mxfp4_upload(urb_ctx *ctx, size_t rows, size_t cols, size_t group_size,
+                     const uint8_t *packed, size_t packed_len, const uint8_t *scales,
+                     size_t scales_len, urb_mat **out);
+/* MxFp8Matrix::from_packed (src/math/mxfp.rs:331-425): E4M3 NaN codes -> NonFinite,
+ * 0xFF scales -> InvalidScale. */
+URB_API int urb_mxfp8_upload(urb_ctx *ctx, size_t rows, size_t cols, size_t block_rows,
+                     size_t block_cols, const uint8_t *values, size_t values_len,
+                     const uint8_t *scales, size_t scales_len, urb_mat **out);
+/* Bf16Matrix::from_le_bytes-style constructor (src/model/bf16.rs): bits as little-endian u16. */
+URB_API int urb_bf16_upload(urb_ctx *ctx, size_t rows, size_t cols, const uint16_t *values,
+                    size_t values_len, urb_mat **out);
+/* DenseMatrix::new (src/model/matrix.rs). */
+URB_API int urb_f32_upload(urb_ctx *ctx, size_t rows, size_t cols, const float *values,
+                   size_t values_len, urb_mat **out);
+URB_API int urb_mat_free(urb_mat *mat);
+/* WeightMatrix::{rows, cols, resident_bytes} (src/model/weight.rs:69-90, 306-320).
+ * resident_bytes counts the payload bytes of the reference format. */
+URB_API int urb_mat_info(const urb_mat *mat, int *format, size_t *rows, size_t *cols,
+                 size_t *resident_bytes);
+
+/* ---- matrix-level products ---------------------------------------------------------------- */
+
+/* WeightMatrix::matvec_rows (src/model/weight.rs:155-203; MxFp4Matrix::matvec_rows
+ * src/math/mxfp.rs:1725-1780): y[0..count) = W[start..start+count) x.  Errors: Shape (bad row
+ * range), NonFinite (non-finite input; for MXFP8 also non-finite output, mxfp.rs:712). */
+URB_API int urb_matvec_rows(urb_ctx *ctx, const urb_mat *mat, size_t start, size_t count,
+                    const float *x, size_t x_len, float *y);
+/* WeightMatrix::matmul_rows (src/model/weight.rs:106-153): x [batch, cols] -> y [batch, rows],
+ * including the reference's output-finiteness rule for its <=12-token chunks. */
+URB_API int urb_matmul_rows(urb_ctx *ctx, const urb_mat *mat, const float *x, size_t batch,
+                    size_t x_len, float *y);
+/* WeightMatrix::matmul_row_range (src/model/weight.rs:155-203). */
+URB_API int urb_matmul_row_range(urb_ctx *ctx, const urb_mat *mat, size_t start, size_t count,
+                         const float *x, size_t batch, size_t x_len, float *y);
+/* WeightMatrix::{matvec_fp32_accum, matmul_rows_fp32_accum} (src/model/weight.rs:205-303):
+ * the FP32-accumulation boundary of DeepSeek-V4.1.  Same device arithmetic (fp32 accumulate). */
+URB_API int urb_matmul_rows_fp32_accum(urb_ctx *ctx, const urb_mat *mat, const float *x, size_t batch,
+                               size_t x_len, float *y);
+/* Device-pointer form: d_x [batch, cols] f32 -> d_y [batch, rows] f32, stream-ordered.
+ * d_status (device int32, may be NULL) receives URB_ERR_NONFINITE if an input is non-finite. */
+URB_API int urb_matmul_rows_device(urb_ctx *ctx, const urb_mat *mat, const float *d_x, size_t batch,
+                           float *d_y, int32_t *d_status);
+
+/* GatedMlp::forward (src/model/mlp.rs:90-99) for `tokens` rows: down(silu(gate x) * (up x)).
+ * x, out [tokens, hidden] f32 host pointers. */
+URB_API int urb_gated_mlp_forward(urb_ctx *ctx, const urb_mat *gate, const urb_mat *up,
+                                  const urb_mat *down, const float *x, size_t tokens, float *out);
+URB_API int urb_gated_mlp_forward_device(urb_ctx *ctx, const urb_mat *gate, const urb_mat *up,
+                                         const urb_mat *down, const float *d_x, size_t tokens,
+                                         float *d_out, int32_t *d_status);
+
+/* ---- routing -------------------------------------------------------------------------------- */
+
+/* MoeGeometry (src/models/glm/moe_geometry.rs:1-9). */
+typedef struct urb_moe_geometry {
+    uint32_t top_k;
+    uint32_t n_group;
+    uint32_t topk_group;
+    int32_t normalize;
+    float routed_scaling_factor;
+} urb_moe_geometry;
+
+/* route_noaux_tc (src/math/routing.rs:38-155) for `tokens` rows of logits [tokens, experts].
+ * Outputs [tokens, top_k] in selection order: expert ids, weights, selection scores (NULL ok). */
+URB_API int urb_route_noaux_tc(urb_ctx *ctx, const float *logits, const float *bias, size_t tokens,
+                       size_t experts, const urb_moe_geometry *geometry, int32_t *out_expert,
+                       float *out_weight, float *out_score);
+/* route_softmax_top_k (src/models/qwen3_8/moe.rs:91-159). */
+URB_API int urb_route_softmax_top_k(urb_ctx *ctx, const float *logits, size_t tokens, size_t experts,
+                            uint32_t top_k, int32_t *out_expert, float *out_weight);
+/* Ragged token->expert grouping (src/models/qwen3_6/runtime.rs:1083-1132): experts ascending,
+ * tokens ascending within an expert.  expert_ids [tokens, top_k]; outputs counts [experts],
+ * offsets [experts+1], perm_token / perm_slot [tokens*top_k]. */
+URB_API int urb_group_routes(urb_ctx *ctx, const int32_t *expert_ids, size_t tokens, uint32_t top_k,
+                     size_t experts, int32_t *counts, int32_t *offsets, int32_t *perm_token,
+                     int32_t *perm_slot);
+
+/* ---- MoE layer ------------------------------------------------------------------------------ */
+
+/* RuntimeMoeLayer::new (src/models/glm/runtime/moe.rs:88-129): router [experts, hidden],
+ * correction bias [experts], per-expert gate/up [inter, hidden] and down [hidden, inter]
+ * matrices, optional shared expert (NULL for none), geometry.  The layer references the
+ * matrices; they must outlive it. */
+URB_API int urb_moe_layer_create(urb_ctx *ctx, const urb_mat *router, const float *bias, size_t experts,
+                         const urb_mat *const *gate, const urb_mat *const *up,
+                         const urb_mat *const *down, const urb_mat *shared_gate,
+                         const urb_mat *shared_up, const urb_mat *shared_down,
+                         const urb_moe_geometry *geometry, urb_layer **out);
+URB_API int urb_moe_layer_free(urb_layer *layer);
+
+/* RuntimeMoeLayer::forward (src/models/glm/runtime/moe.rs:138-176), batched over `tokens`
+ * (one call per MoE layer, not per projection).  x, out [tokens, hidden] f32 host pointers.
+ * Optional outputs (NULL to skip): route expert/weight/score [tokens, top_k] in selection
+ * order, router logits [tokens, experts], counts [experts], perm_token/perm_slot
+ * [tokens*top_k] (the grouped order of src/models/qwen3_6/runtime.rs:1123-1132). */
+URB_API int urb_moe_forward(urb_ctx *ctx, urb_layer *layer, const float *x, size_t tokens, float *out,
+                    int32_t *route_expert, float *route_weight, float *route_score,
+                    float *router_logits, int32_t *counts, int32_t *perm_token,
+                    int32_t *perm_slot);
+/* Device-pointer form of urb_moe_forward (inputs resident in HBM, stream-ordered, no host
+ * synchronisation; graph-capturable).  d_status as in urb_matmul_rows_device. */
+URB_API int urb_moe_forward_device(urb_ctx *ctx, urb_layer *layer, const float *d_x, size_t tokens,
+                           float *d_out, int32_t *d_route_expert, float *d_route_weight,
+                           int32_t *d_status);
+
+/* ---- measurement -------------------------------------------------------------------------- */
+
+/* Kernel families timed by the optional per-launch profiler (CUDA events on the launch
+ * stream, around each launch; off by default).  Replaces the reference's ProfileStage spans
+ * (src/profiling.rs:75-136) for the device path. */
+typedef enum urb_kernel_kind {
+    URB_K_ROW_SHIFT = 0,
+    URB_K_ROUTER_LOGITS = 1,
+    URB_K_ROUTE = 2,
+    URB_K_PERMUTE = 3,
+    URB_K_GATE_UP = 4,
+    URB_K_DOWN = 5,
+    URB_K_COMBINE = 6,
+    URB_K_PRODUCT = 7,
+    URB_K_COUNT = 8
+} urb_kernel_kind;
+URB_API int urb_profile_enable(urb_ctx *ctx, int on);
+/* Synchronises pending events; returns the total device time and launch count of `kind`. */
+URB_API int urb_profile_read(urb_ctx *ctx, int kind, double *total_ms, int64_t *launches);
+URB_API int urb_profile_reset(urb_ctx *ctx);
+
+/* Device status helpers for the `_device` forms. */
+URB_API int urb_status_read(urb_ctx *ctx, const int32_t *d_status, int32_t *out);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* URB_MOE_H */

@@ -1,0 +1,111 @@
+/*
+ * urb_oracle.h — CPU oracle for the routed-expert (MoE) hot path.
+ *
+ * TEST INFRASTRUCTURE ONLY.  This library restates, in plain C++17, the CPU arithmetic of
+ * Urbilateria v0.2.4 (a pure-Rust runtime that cannot be compiled in this image) so that the
+ * CUDA path can be checked against it.  Only tests/, __graft_entry__.smoke() and bench.py's CPU
+ * baseline leg load it.  The product library (liburb_moe.so) never links or calls it.
+ *
+ * Every function cites the reference file:line it follows.  Parity of this restatement is
+ * pinned by the known-answer tests in tests/test_oracle_golden.py, which replay the reference's
+ * own unit-test vectors (src/math/mxfp.rs, src/math/routing.rs, src/model/mlp.rs,
+ * src/models/qwen3_8/moe.rs) against it.
+ *
+ * Status codes are shared with the product C ABI (include/urb_moe.h).
+ */
+#ifndef URB_ORACLE_H
+#define URB_ORACLE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Weight formats of WeightMatrix (src/model/weight.rs:54-61) that the MoE path uses. */
+enum {
+    URBO_F32 = 0,
+    URBO_BF16 = 1,
+    URBO_MXFP8 = 2, /* E4M3 values + E8M0 block scales (src/math/mxfp.rs:321-877) */
+    URBO_MXFP4 = 3, /* packed E2M1 nibbles + E8M0 group scales (src/math/mxfp.rs:1363-1847) */
+};
+
+enum {
+    URBO_OK = 0,
+    URBO_ERR_SHAPE = 1,
+    URBO_ERR_INVALID_SCALE = 2,
+    URBO_ERR_NONFINITE = 3,
+    URBO_ERR_INVALID_GEOMETRY = 4,
+};
+
+typedef struct urbo_matrix {
+    int32_t format;
+    size_t rows, cols;
+    size_t group_size;             /* MXFP4: scale run along the input dimension */
+    size_t block_rows, block_cols; /* MXFP8: scale block */
+    const void *values;            /* f32 | bf16 bits (u16) | E4M3 bytes | packed nibbles */
+    const uint8_t *scales;         /* E8M0 bytes (MX formats) */
+} urbo_matrix;
+
+/* Codecs (src/math/mxfp.rs:44-79, 247-275). */
+float urbo_decode_e8m0(uint8_t code);   /* 0xFF is not validated here */
+float urbo_decode_e4m3fn(uint8_t code);
+float urbo_decode_e2m1(uint8_t code);
+uint8_t urbo_encode_e4m3fn(float value);
+float urbo_expf(float value);           /* the libm expf the Rust reference links */
+
+/* Constructor validation: shape, then payload (mxfp.rs:1400-1443, 394-425). */
+int urbo_validate(const urbo_matrix *m);
+
+/* WeightMatrix::matvec_rows / MxFp4Matrix::matvec_rows etc.  y has `count` entries. */
+int urbo_matvec_rows(const urbo_matrix *m, size_t start, size_t count, const float *x, float *y,
+                     int threads);
+/* WeightMatrix::matmul_rows (src/model/weight.rs:106-153): x [batch, cols] -> y [batch, rows]. */
+int urbo_matmul_rows(const urbo_matrix *m, const float *x, size_t batch, float *y, int threads);
+/* MxFp4Matrix::matvec_rows_fp32 (src/math/mxfp.rs:1658-1723), FP32 accumulation boundary. */
+int urbo_mxfp4_matvec_rows_fp32(const urbo_matrix *m, size_t start, size_t count, const float *x,
+                                float *y, int threads);
+
+/* route_noaux_tc (src/math/routing.rs:38-155).  Outputs top_k entries in selection order. */
+int urbo_route_noaux_tc(const float *logits, const float *bias, size_t experts, size_t top_k,
+                        size_t n_group, size_t topk_group, int normalize, float scaling,
+                        int32_t *out_expert, float *out_weight, float *out_score);
+/* route_softmax_top_k (src/models/qwen3_8/moe.rs:91-159). */
+int urbo_route_softmax_top_k(const float *logits, size_t experts, size_t top_k,
+                             int32_t *out_expert, float *out_weight);
+
+/* silu (src/math/ops.rs:36-38) and GatedMlp::forward (src/model/mlp.rs:90-99). */
+float urbo_silu(float v);
+int urbo_gated_mlp_forward(const urbo_matrix *gate, const urbo_matrix *up,
+                           const urbo_matrix *down, const float *x, float *y, int threads);
+
+/* Ragged grouping: experts ascending, tokens ascending within an expert
+ * (src/models/qwen3_6/runtime.rs:1083-1132).  expert_ids is [tokens, top_k] in selection
+ * order.  counts/offsets have `experts` / `experts + 1` entries; perm_token / perm_slot have
+ * tokens*top_k entries: the token and the selection rank of each grouped route. */
+int urbo_group_routes(const int32_t *expert_ids, size_t tokens, size_t top_k, size_t experts,
+                      int32_t *counts, int32_t *offsets, int32_t *perm_token, int32_t *perm_slot);
+
+/* One GLM RuntimeMoeLayer::forward per token (src/models/glm/runtime/moe.rs:138-176):
+ * BF16/any router -> route_noaux_tc -> shared GatedMlp -> routed GatedMlps in selection
+ * order -> f64 combine.  x and out are [tokens, hidden]; route outputs [tokens, top_k]. */
+typedef struct urbo_moe_layer {
+    const urbo_matrix *router;
+    const float *bias;
+    size_t experts;
+    const urbo_matrix *gate, *up, *down;      /* arrays of `experts` matrices */
+    const urbo_matrix *shared_gate, *shared_up, *shared_down;
+    size_t top_k, n_group, topk_group;
+    int normalize;
+    float routed_scaling_factor;
+} urbo_moe_layer;
+
+int urbo_moe_layer_forward(const urbo_moe_layer *layer, const float *x, size_t tokens,
+                           float *out, int32_t *route_expert, float *route_weight,
+                           float *route_score, float *router_logits, int threads);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

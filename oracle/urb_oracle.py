@@ -1,0 +1,245 @@
+"""ctypes wrapper of the CPU oracle (oracle/liburb_oracle.so).
+
+TEST INFRASTRUCTURE ONLY: tests/, ``__graft_entry__.smoke()`` and bench.py's CPU-baseline leg
+import this module to check or time the CUDA path.  The product package ``urbilateria_b200``
+never imports it.  The C++ it wraps restates Urbilateria v0.2.4's CPU arithmetic
+(src/math/mxfp.rs, src/model/bf16.rs, src/math/routing.rs, src/model/mlp.rs,
+src/models/glm/runtime/moe.rs, src/models/qwen3_6/runtime.rs); see urb_oracle.h.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB_PATH = os.path.join(_HERE, "liburb_oracle.so")
+
+F32, BF16, MXFP8, MXFP4 = 0, 1, 2, 3
+OK, ERR_SHAPE, ERR_INVALID_SCALE, ERR_NONFINITE, ERR_INVALID_GEOMETRY = 0, 1, 2, 3, 4
+
+
+class OracleMatrix(ctypes.Structure):
+    _fields_ = [
+        ("format", ctypes.c_int32),
+        ("rows", ctypes.c_size_t),
+        ("cols", ctypes.c_size_t),
+        ("group_size", ctypes.c_size_t),
+        ("block_rows", ctypes.c_size_t),
+        ("block_cols", ctypes.c_size_t),
+        ("values", ctypes.c_void_p),
+        ("scales", ctypes.c_void_p),
+    ]
+
+
+class OracleMoeLayer(ctypes.Structure):
+    _fields_ = [
+        ("router", ctypes.POINTER(OracleMatrix)),
+        ("bias", ctypes.c_void_p),
+        ("experts", ctypes.c_size_t),
+        ("gate", ctypes.POINTER(OracleMatrix)),
+        ("up", ctypes.POINTER(OracleMatrix)),
+        ("down", ctypes.POINTER(OracleMatrix)),
+        ("shared_gate", ctypes.POINTER(OracleMatrix)),
+        ("shared_up", ctypes.POINTER(OracleMatrix)),
+        ("shared_down", ctypes.POINTER(OracleMatrix)),
+        ("top_k", ctypes.c_size_t),
+        ("n_group", ctypes.c_size_t),
+        ("topk_group", ctypes.c_size_t),
+        ("normalize", ctypes.c_int),
+        ("routed_scaling_factor", ctypes.c_float),
+    ]
+
+
+def build() -> str:
+    """Compile the oracle with its Makefile (idempotent)."""
+    subprocess.run(["make", "-s", "-C", _HERE], check=True)
+    return _LIB_PATH
+
+
+_lib = None
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(_LIB_PATH):
+            build()
+        _lib = ctypes.CDLL(_LIB_PATH)
+        _lib.urbo_decode_e8m0.restype = ctypes.c_float
+        _lib.urbo_decode_e4m3fn.restype = ctypes.c_float
+        _lib.urbo_decode_e2m1.restype = ctypes.c_float
+        _lib.urbo_encode_e4m3fn.restype = ctypes.c_uint8
+        _lib.urbo_encode_e4m3fn.argtypes = [ctypes.c_float]
+        _lib.urbo_expf.restype = ctypes.c_float
+        _lib.urbo_expf.argtypes = [ctypes.c_float]
+        _lib.urbo_silu.restype = ctypes.c_float
+        _lib.urbo_silu.argtypes = [ctypes.c_float]
+        _lib.urbo_route_noaux_tc.argtypes = [
+            ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_size_t, ctypes.c_size_t,
+            ctypes.c_size_t, ctypes.c_int, ctypes.c_float, ctypes.c_void_p, ctypes.c_void_p,
+            ctypes.c_void_p]
+        _lib.urbo_route_softmax_top_k.argtypes = [
+            ctypes.c_void_p, ctypes.c_size_t, ctypes.c_size_t, ctypes.c_void_p, ctypes.c_void_p]
+        _lib.urbo_matvec_rows.argtypes = [
+            ctypes.POINTER(OracleMatrix), ctypes.c_size_t, ctypes.c_size_t, ctypes.c_void_p,
+            ctypes.c_void_p, ctypes.c_int]
+        _lib.urbo_mxfp4_matvec_rows_fp32.argtypes = _lib.urbo_matvec_rows.argtypes
+        _lib.urbo_matmul_rows.argtypes = [
+            ctypes.POINTER(OracleMatrix), ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p,
+            ctypes.c_int]
+        _lib.urbo_validate.argtypes = [ctypes.POINTER(OracleMatrix)]
+        _lib.urbo_gated_mlp_forward.argtypes = [
+            ctypes.POINTER(OracleMatrix), ctypes.POINTER(OracleMatrix),
+            ctypes.POINTER(OracleMatrix), ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int]
+        _lib.urbo_group_routes.argtypes = [
+            ctypes.c_void_p, ctypes.c_size_t, ctypes.c_size_t, ctypes.c_size_t,
+            ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
+        _lib.urbo_moe_layer_forward.argtypes = [
+            ctypes.POINTER(OracleMoeLayer), ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p,
+            ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int]
+    return _lib
+
+
+def default_threads() -> int:
+    return max(1, os.cpu_count() or 1)
+
+
+class OracleError(Exception):
+    def __init__(self, code: int):
+        super().__init__({1: "Shape", 2: "InvalidScale", 3: "NonFinite",
+                          4: "InvalidGeometry"}.get(code, str(code)))
+        self.code = code
+
+
+def _check(rc: int):
+    if rc != OK:
+        raise OracleError(rc)
+
+
+def _ptr(a: np.ndarray) -> int:
+    return a.ctypes.data
+
+
+class Matrix:
+    """One reference WeightMatrix held as numpy arrays (keeps the buffers alive)."""
+
+    def __init__(self, fmt, rows, cols, values, scales=None, group_size=32, block_rows=1,
+                 block_cols=32, validate=True):
+        self.fmt, self.rows, self.cols = fmt, rows, cols
+        self.values = np.ascontiguousarray(values)
+        self.scales = None if scales is None else np.ascontiguousarray(scales, dtype=np.uint8)
+        self.group_size, self.block_rows, self.block_cols = group_size, block_rows, block_cols
+        self.c = OracleMatrix(fmt, rows, cols, group_size, block_rows, block_cols,
+                              _ptr(self.values), 0 if self.scales is None else _ptr(self.scales))
+        if validate:
+            _check(lib().urbo_validate(ctypes.byref(self.c)))
+
+    # WeightMatrix::matvec_rows
+    def matvec_rows(self, start, count, x, threads=None):
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        if x.size != self.cols:
+            raise OracleError(ERR_SHAPE)
+        y = np.empty(count, dtype=np.float32)
+        _check(lib().urbo_matvec_rows(ctypes.byref(self.c), start, count, _ptr(x), _ptr(y),
+                                      threads or default_threads()))
+        return y
+
+    def matvec(self, x, threads=None):
+        return self.matvec_rows(0, self.rows, x, threads)
+
+    def matvec_fp32(self, x, start=0, count=None, threads=None):
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        count = self.rows if count is None else count
+        y = np.empty(count, dtype=np.float32)
+        _check(lib().urbo_mxfp4_matvec_rows_fp32(ctypes.byref(self.c), start, count, _ptr(x),
+                                                 _ptr(y), threads or default_threads()))
+        return y
+
+    # WeightMatrix::matmul_rows: x [batch, cols] -> [batch, rows]
+    def matmul_rows(self, x, batch, threads=None):
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        if x.size != batch * self.cols:
+            raise OracleError(ERR_SHAPE)
+        y = np.empty((batch, self.rows), dtype=np.float32)
+        _check(lib().urbo_matmul_rows(ctypes.byref(self.c), _ptr(x), batch, _ptr(y),
+                                      threads or default_threads()))
+        return y
+
+
+def route_noaux_tc(logits, bias, top_k, n_group=1, topk_group=1, normalize=True, scaling=1.0):
+    logits = np.ascontiguousarray(logits, dtype=np.float32)
+    bias = np.ascontiguousarray(bias, dtype=np.float32)
+    e = np.empty(top_k, dtype=np.int32)
+    w = np.empty(top_k, dtype=np.float32)
+    s = np.empty(top_k, dtype=np.float32)
+    _check(lib().urbo_route_noaux_tc(_ptr(logits), _ptr(bias), logits.size, top_k, n_group,
+                                     topk_group, int(normalize), scaling, _ptr(e), _ptr(w),
+                                     _ptr(s)))
+    return e, w, s
+
+
+def route_softmax_top_k(logits, top_k):
+    logits = np.ascontiguousarray(logits, dtype=np.float32)
+    e = np.empty(top_k, dtype=np.int32)
+    w = np.empty(top_k, dtype=np.float32)
+    _check(lib().urbo_route_softmax_top_k(_ptr(logits), logits.size, top_k, _ptr(e), _ptr(w)))
+    return e, w
+
+
+def gated_mlp_forward(gate: Matrix, up: Matrix, down: Matrix, x, threads=None):
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    y = np.empty(down.rows, dtype=np.float32)
+    _check(lib().urbo_gated_mlp_forward(ctypes.byref(gate.c), ctypes.byref(up.c),
+                                        ctypes.byref(down.c), _ptr(x), _ptr(y),
+                                        threads or default_threads()))
+    return y
+
+
+def group_routes(expert_ids: np.ndarray, experts: int):
+    ids = np.ascontiguousarray(expert_ids, dtype=np.int32)
+    tokens, top_k = ids.shape
+    counts = np.empty(experts, dtype=np.int32)
+    offsets = np.empty(experts + 1, dtype=np.int32)
+    perm_token = np.empty(tokens * top_k, dtype=np.int32)
+    perm_slot = np.empty(tokens * top_k, dtype=np.int32)
+    _check(lib().urbo_group_routes(_ptr(ids), tokens, top_k, experts, _ptr(counts),
+                                   _ptr(offsets), _ptr(perm_token), _ptr(perm_slot)))
+    return counts, offsets, perm_token, perm_slot
+
+
+class MoeLayer:
+    """GLM RuntimeMoeLayer composition (glm/runtime/moe.rs:138-176) over oracle matrices."""
+
+    def __init__(self, router: Matrix, bias, gates, ups, downs, shared, top_k=8, n_group=1,
+                 topk_group=1, normalize=True, scaling=2.5):
+        self.router, self.bias = router, np.ascontiguousarray(bias, dtype=np.float32)
+        self.experts = router.rows
+        self._g = (OracleMatrix * self.experts)(*[m.c for m in gates])
+        self._u = (OracleMatrix * self.experts)(*[m.c for m in ups])
+        self._d = (OracleMatrix * self.experts)(*[m.c for m in downs])
+        self._keep = (gates, ups, downs, shared)
+        self.hidden = router.cols
+        self.top_k = top_k
+        self.c = OracleMoeLayer(
+            ctypes.pointer(router.c), _ptr(self.bias), self.experts,
+            ctypes.cast(self._g, ctypes.POINTER(OracleMatrix)),
+            ctypes.cast(self._u, ctypes.POINTER(OracleMatrix)),
+            ctypes.cast(self._d, ctypes.POINTER(OracleMatrix)),
+            ctypes.pointer(shared[0].c), ctypes.pointer(shared[1].c), ctypes.pointer(shared[2].c),
+            top_k, n_group, topk_group, int(normalize), scaling)
+
+    def forward(self, x, threads=None):
+        x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1, self.hidden)
+        t = x.shape[0]
+        out = np.empty_like(x)
+        e = np.empty((t, self.top_k), dtype=np.int32)
+        w = np.empty((t, self.top_k), dtype=np.float32)
+        s = np.empty((t, self.top_k), dtype=np.float32)
+        logits = np.empty((t, self.experts), dtype=np.float32)
+        _check(lib().urbo_moe_layer_forward(ctypes.byref(self.c), _ptr(x), t, _ptr(out), _ptr(e),
+                                            _ptr(w), _ptr(s), _ptr(logits),
+                                            threads or default_threads()))
+        return out, e, w, s, logits

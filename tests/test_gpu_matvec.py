@@ -1,0 +1,147 @@
+"""Parity of the device matrix products (C ABI) with the CPU oracle.
+
+Bar: relative L2 <= 1e-3 and max-abs <= 2e-2 (outputs normalised to unit RMS) against the
+reference's f32 outputs; decoded weights bit-exact; error variants as in the reference.
+"""
+import numpy as np
+import pytest
+
+import urbilateria_b200 as urb
+from urbilateria_b200 import synthetic as syn
+
+from helpers import assert_close, bf16_pair, mxfp4_pair, mxfp8_pair
+
+pytestmark = pytest.mark.gpu
+
+
+def test_mxfp4_decode_is_exact_and_low_nibble_first(oracle, ctx):
+    # Identity batch: y[t][r] = W[r][t], a single exact product per output.
+    g = syn.rng(11)
+    rows, cols = 35, 160
+    dev, orc = mxfp4_pair(oracle, ctx, g, rows, cols, lo=112, hi=134)
+    eye = np.eye(cols, dtype=np.float32)
+    got = dev.matmul_rows(eye, cols)
+    want = np.stack([orc.matvec(eye[c]) for c in range(cols)])
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
+def test_mxfp8_decode_is_exact(oracle, ctx):
+    g = syn.rng(12)
+    rows, cols = 33, 96
+    dev, orc = mxfp8_pair(oracle, ctx, g, rows, cols, lo=110, hi=130)
+    eye = np.eye(cols, dtype=np.float32)
+    got = dev.matmul_rows(eye, cols)
+    want = np.stack([orc.matvec(eye[c]) for c in range(cols)])
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
+def test_bf16_decode_is_exact(oracle, ctx):
+    g = syn.rng(13)
+    dev, orc = bf16_pair(oracle, ctx, g, 20, 136)
+    eye = np.eye(136, dtype=np.float32)
+    got = dev.matmul_rows(eye, 136)
+    want = np.stack([orc.matvec(eye[c]) for c in range(136)])
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
+def test_c0_mxfp4_matvec_4096x7168(oracle, ctx):
+    # W 4096x7168, E8M0 119..127, x ~ N(0,1).
+    g = syn.rng(2024)
+    dev, orc = mxfp4_pair(oracle, ctx, g, 4096, 7168)
+    x = syn.normal_f32(g, 7168)
+    assert_close(dev.matvec(x), orc.matvec(x))
+
+
+@pytest.mark.parametrize("rows,cols", [(1, 32), (17, 129), (35, 2049), (300, 1000), (64, 4096)])
+def test_mxfp4_odd_shapes(oracle, ctx, rows, cols):
+    g = syn.rng(rows * 1000 + cols)
+    dev, orc = mxfp4_pair(oracle, ctx, g, rows, cols)
+    for batch in (1, 3, 12, 13):
+        x = syn.normal_f32(g, (batch, cols))
+        assert_close(dev.matmul_rows(x, batch), orc.matmul_rows(x, batch))
+
+
+@pytest.mark.parametrize("group", [8, 16, 33, 128])
+def test_mxfp4_other_group_sizes_use_generic_path(oracle, ctx, group):
+    g = syn.rng(group)
+    dev, orc = mxfp4_pair(oracle, ctx, g, 40, 300, group=group)
+    x = syn.normal_f32(g, (3, 300))
+    assert_close(dev.matmul_rows(x, 3), orc.matmul_rows(x, 3))
+
+
+def test_mxfp4_wide_scale_range_uses_generic_path(oracle, ctx):
+    g = syn.rng(5)
+    dev, orc = mxfp4_pair(oracle, ctx, g, 16, 256, lo=60, hi=190)
+    x = syn.normal_f32(g, 256)
+    assert_close(dev.matvec(x), orc.matvec(x))
+
+
+@pytest.mark.parametrize("block", [(1, 32), (128, 128), (32, 64)])
+def test_mxfp8_blocks(oracle, ctx, block):
+    g = syn.rng(block[0] * 7 + block[1])
+    dev, orc = mxfp8_pair(oracle, ctx, g, 300, 1536, *block)
+    for batch in (1, 5, 12):
+        x = syn.normal_f32(g, (batch, 1536))
+        assert_close(dev.matmul_rows(x, batch), orc.matmul_rows(x, batch))
+
+
+def test_bf16_and_f32(oracle, ctx):
+    g = syn.rng(21)
+    dev, orc = bf16_pair(oracle, ctx, g, 768, 2048)
+    x = syn.normal_bf16_as_f32(g, (4, 2048))
+    assert_close(dev.matmul_rows(x, 4), orc.matmul_rows(x, 4))
+    w = syn.normal_f32(g, (50, 70))
+    d = urb.DenseMatrix.new(50, 70, w, ctx=ctx)
+    o = oracle.Matrix(oracle.F32, 50, 70, w)
+    x = syn.normal_f32(g, 70)
+    assert_close(d.matvec(x), o.matvec(x))
+
+
+def test_row_ranges(oracle, ctx):
+    g = syn.rng(31)
+    dev, orc = mxfp4_pair(oracle, ctx, g, 100, 256)
+    x = syn.normal_f32(g, 256)
+    for start, count in [(0, 100), (5, 20), (17, 1), (99, 1), (16, 64)]:
+        assert_close(dev.matvec_rows(start, count, x), orc.matvec_rows(start, count, x))
+    xb = syn.normal_f32(g, (3, 256))
+    assert_close(dev.matmul_row_range(7, 50, xb, 3),
+                 np.stack([orc.matvec_rows(7, 50, xb[t]) for t in range(3)]))
+
+
+def test_error_variants(ctx):
+    g = syn.rng(41)
+    packed, scales = syn.mxfp4_matrix(g, 4, 64)
+    bad = scales.copy()
+    bad[1, 1] = 0xFF
+    with pytest.raises(urb.UrbError) as e:
+        urb.MxFp4Matrix.from_packed(4, 64, 32, packed, bad, ctx=ctx)
+    assert e.value.kind == "InvalidScale"
+    with pytest.raises(urb.UrbError) as e:
+        urb.MxFp4Matrix.from_packed(4, 64, 32, packed[:, :10], scales, ctx=ctx)
+    assert e.value.kind == "Shape"
+    vals = np.full((4, 64), 0x38, np.uint8)
+    vals[2, 3] = 0xFF
+    with pytest.raises(urb.UrbError) as e:
+        urb.MxFp8Matrix.from_packed(4, 64, 1, 32, vals, np.full((4, 2), 127, np.uint8), ctx=ctx)
+    assert e.value.kind == "NonFinite"
+    m = urb.MxFp4Matrix.from_packed(4, 64, 32, packed, scales, ctx=ctx)
+    x = np.ones(64, np.float32)
+    x[5] = np.nan
+    with pytest.raises(urb.UrbError) as e:
+        m.matvec(x)
+    assert e.value.kind == "NonFinite"
+    with pytest.raises(urb.UrbError) as e:
+        m.matvec(np.ones(63, np.float32))
+    assert e.value.kind == "Shape"
+    with pytest.raises(urb.UrbError) as e:
+        m.matvec_rows(2, 3, np.ones(64, np.float32))
+    assert e.value.kind == "Shape"
+
+
+def test_mxfp8_nonfinite_output_is_rejected(ctx):
+    # E4M3 448 * 2^127 overflows f32: the reference rejects MXFP8 outputs that are not finite.
+    vals = np.full((1, 32), 0x7E, np.uint8)
+    m = urb.MxFp8Matrix.from_packed(1, 32, 1, 32, vals, np.array([[254]], np.uint8), ctx=ctx)
+    with pytest.raises(urb.UrbError) as e:
+        m.matvec(np.ones(32, np.float32))
+    assert e.value.kind == "NonFinite"

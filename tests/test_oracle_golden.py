@@ -1,0 +1,317 @@
+"""Pins the CPU oracle to the reference's own known-answer tests.
+
+Each test replays a unit test of Urbilateria v0.2.4 (file:line cited) against the C++ oracle
+(oracle/urb_oracle.cpp).  Where the reference test computes its expectation with a scalar
+formula (ordered F64 / ordered F32 sums), the formula is re-implemented here independently in
+numpy and compared bit for bit.
+"""
+import math
+import struct
+
+import numpy as np
+import pytest
+
+
+def f32(x):
+    return np.float32(x)
+
+
+def bits(v):
+    return struct.unpack("<I", struct.pack("<f", float(v)))[0]
+
+
+# --- codecs ------------------------------------------------------------------------------------
+
+def test_real_checkpoint_fp8_prefix_decodes_exactly(oracle):
+    # src/math/mxfp.rs:2210-2214
+    lib = oracle.lib()
+    assert lib.urbo_decode_e4m3fn(0xE0) == -32.0
+    assert lib.urbo_decode_e8m0(115) == 2.0 ** -12
+    assert f32(lib.urbo_decode_e4m3fn(0xE0)) * f32(lib.urbo_decode_e8m0(115)) == f32(-0.0078125)
+
+
+def test_e8m0_decode_matches_power_of_two_exhaustively(oracle):
+    # src/math/mxfp.rs:2217-2224
+    lib = oracle.lib()
+    for code in range(0xFF):
+        assert bits(lib.urbo_decode_e8m0(code)) == bits(np.ldexp(np.float32(1.0), code - 127))
+
+
+def test_e4m3_decode_matches_ocp_definition_exhaustively(oracle):
+    # src/math/mxfp.rs:2236-2300 checks the AVX2 decode against the scalar definition for all
+    # 256 codes; the oracle's decode is checked against the OCP E4M3FN definition (ml_dtypes).
+    ml_dtypes = pytest.importorskip("ml_dtypes")
+    lib = oracle.lib()
+    ref = np.arange(256, dtype=np.uint8).view(ml_dtypes.float8_e4m3fn).astype(np.float32)
+    for code in range(256):
+        got = lib.urbo_decode_e4m3fn(code)
+        if code & 0x7F == 0x7F:
+            assert math.isnan(got)
+        else:
+            assert bits(got) == bits(ref[code]), hex(code)
+
+
+def test_e4m3_encoder_roundtrips_every_finite_code(oracle):
+    # encode_e4m3fn_finite (src/math/mxfp.rs:247-275) inverts the decoder on finite codes.
+    lib = oracle.lib()
+    for code in range(256):
+        if code & 0x7F == 0x7F:
+            continue
+        v = lib.urbo_decode_e4m3fn(code)
+        enc = lib.urbo_encode_e4m3fn(v)
+        if v == 0.0:
+            assert enc == 0  # -0.0 encodes to +0 (code 0) in the reference
+        else:
+            assert enc == code
+
+
+def test_e2m1_table_low_nibble_first_golden(oracle):
+    # src/math/mxfp.rs:2583-2591: packed [0x8c], scale 120 -> row [-0.015625, 0.0]; 0xFF rejected.
+    m = oracle.Matrix(oracle.MXFP4, 1, 2, np.array([0x8C], np.uint8), np.array([120], np.uint8),
+                      group_size=2)
+    row = [m.matvec(np.array([1.0, 0.0], np.float32))[0],
+           m.matvec(np.array([0.0, 1.0], np.float32))[0]]
+    assert row == [-0.015625, 0.0]
+    with pytest.raises(oracle.OracleError) as e:
+        oracle.Matrix(oracle.MXFP4, 1, 2, np.array([0x8C], np.uint8), np.array([0xFF], np.uint8),
+                      group_size=2)
+    assert e.value.code == oracle.ERR_INVALID_SCALE
+
+
+def test_fp8_block_scales_follow_both_matrix_axes(oracle):
+    # src/math/mxfp.rs:2668-2675
+    m = oracle.Matrix(oracle.MXFP8, 3, 3, np.full(9, 0x38, np.uint8),
+                      np.array([127, 128, 129, 130], np.uint8), block_rows=2, block_cols=2)
+    eye = np.eye(3, dtype=np.float32)
+    rows = np.stack([m.matvec(eye[c]) for c in range(3)], axis=1)
+    assert list(rows[0]) == [1.0, 1.0, 2.0]
+    assert list(rows[2]) == [4.0, 4.0, 8.0]
+
+
+# --- ordered dot products --------------------------------------------------------------------
+
+def _input(cols):
+    # ((index * 29 % 127) as f32 - 63.0) / 131.0
+    return ((np.arange(cols) * 29 % 127).astype(np.float32) - f32(63.0)) / f32(131.0)
+
+
+E2M1 = np.array([0, .5, 1, 1.5, 2, 3, 4, 6, 0, -.5, -1, -1.5, -2, -3, -4, -6], np.float32)
+
+
+def _e8m0(code):
+    return np.float32(2.0 ** (int(code) - 127)) if code else np.float32(2.0 ** -127)
+
+
+def test_fp8_scalar_blocks_preserve_ordered_dot_bits_across_partial_blocks(oracle):
+    # src/math/mxfp.rs:2678-2716
+    import ml_dtypes
+    rows = 35
+    for block_rows, block_cols in [(32, 32), (128, 128)]:
+        for cols in [1, 31, 32, 65, 129, 2049]:
+            idx = np.arange(rows * cols)
+            values = (((idx * 79 + 17) % 127) | ((idx % 2) * 128)).astype(np.uint8)
+            scale_cols = -(-cols // block_cols)
+            ns = -(-rows // block_rows) * scale_cols
+            scales = (115 + np.arange(ns) % 19).astype(np.uint8)
+            x = _input(cols)
+            m = oracle.Matrix(oracle.MXFP8, rows, cols, values, scales, block_rows=block_rows,
+                              block_cols=block_cols)
+            got = m.matvec_rows(1, rows - 2, x)
+            dec = values.view(ml_dtypes.float8_e4m3fn).astype(np.float32).reshape(rows, cols)
+            for i, r in enumerate(range(1, rows - 1)):
+                acc = 0.0
+                for c in range(cols):
+                    w = dec[r, c] * _e8m0(scales[(r // block_rows) * scale_cols + c // block_cols])
+                    acc += float(np.float32(w)) * float(x[c])
+                assert bits(got[i]) == bits(np.float32(acc)), (block_rows, cols, r)
+
+
+def test_fp4_fp32_groups_preserve_ordered_dot_bits_across_odd_nibble_boundaries(oracle):
+    # src/math/mxfp.rs:2719-2759
+    rows = 35
+    for cols in [1, 31, 32, 65, 2049]:
+        for group in [1, 3, 7, 32, 33]:
+            row_bytes = -(-cols // 2)
+            groups = -(-cols // group)
+            packed = ((np.arange(rows * row_bytes) * 83 + 11) % 256).astype(np.uint8)
+            scales = (115 + np.arange(rows * groups) % 19).astype(np.uint8)
+            x = _input(cols)
+            m = oracle.Matrix(oracle.MXFP4, rows, cols, packed, scales, group_size=group)
+            got = m.matvec_fp32(x, start=1, count=rows - 2)
+            for i, r in enumerate(range(1, rows - 1)):
+                acc = np.float32(0.0)
+                for c in range(cols):
+                    byte = packed[r * row_bytes + c // 2]
+                    code = byte & 15 if c % 2 == 0 else byte >> 4
+                    s = _e8m0(scales[r * groups + c // group])
+                    acc = np.float32(acc + np.float32(np.float32(E2M1[code] * s) * x[c]))
+                assert bits(got[i]) == bits(acc), (cols, group, r)
+
+
+ADVERSARIAL = np.array([0.0, -0.0, np.float32(1.4e-45), -np.float32(1.4e-45),
+                        np.finfo(np.float32).tiny, -np.finfo(np.float32).tiny, 0.5, -0.5,
+                        np.finfo(np.float32).max / np.float32(8), -np.finfo(np.float32).max / np.float32(8),
+                        16777216.0, 1.0, -16777216.0], dtype=np.float32)
+
+
+def _f64_ordered(packed, scales, x, group):
+    acc = 0.0
+    for c in range(x.size):
+        byte = packed[c // 2]
+        code = byte & 15 if c % 2 == 0 else byte >> 4
+        w = np.float32(E2M1[code] * _e8m0(scales[c // group]))
+        acc += float(w) * float(x[c])
+    return np.float32(acc)
+
+
+@pytest.mark.parametrize("group", [8, 10, 16, 32, 34, 128])
+def test_fp4_ordered_matches_formula_for_extreme_scales_and_partial_groups(oracle, group):
+    # src/math/mxfp.rs:2763-2834 (the scalar formula is the expectation there).
+    with np.errstate(all="ignore"):
+        for cols in [1, 7, 8, 9, 15, 16, 17, 31, 32, 33, 65, 129]:
+            x = ADVERSARIAL[np.arange(cols) % ADVERSARIAL.size]
+            for scale in [0, 1, 2, 125, 126, 127, 128, 251, 252, 253, 254]:
+                for code in (0, 1, 7, 8, 9, 15):
+                    packed = np.full(-(-cols // 2), code | ((15 - code) << 4), np.uint8)
+                    scales = np.full(-(-cols // group), scale, np.uint8)
+                    m = oracle.Matrix(oracle.MXFP4, 1, cols, packed, scales, group_size=group)
+                    got = m.matvec(x)[0]
+                    want = _f64_ordered(packed, scales, x, group)
+                    if np.isnan(want):
+                        assert np.isnan(got)
+                    else:
+                        assert bits(got) == bits(want), (cols, scale, code)
+    m = oracle.Matrix(oracle.MXFP4, 1, 32, np.full(16, 0x22, np.uint8), np.array([127], np.uint8))
+    for bad in [np.inf, -np.inf, np.nan]:
+        x = np.ones(32, np.float32)
+        x[7] = bad
+        with pytest.raises(oracle.OracleError) as e:
+            m.matvec_fp32(x)
+        assert e.value.code == oracle.ERR_NONFINITE
+
+
+def test_mxfp8_fma_lanes_within_fp32_accumulation_error(oracle):
+    # src/math/mxfp.rs:2296-2343: |actual - F64| <= 64 eps sum|p|.
+    import ml_dtypes
+    rows, cols = 17, 97
+    codes = np.array([0x00, 0x07, 0x18, 0x38, 0x48, 0x70, 0x7E, 0xB8, 0xFE], np.uint8)
+    values = codes[(np.arange(rows * cols) * 17) % codes.size]
+    scale_cols = -(-cols // 32)
+    scales = (119 + (np.arange(rows * scale_cols) * 13) % 17).astype(np.uint8)
+    x = ((np.arange(cols) * 29 % 127).astype(np.float32) - f32(63)) / f32(128)
+    m = oracle.Matrix(oracle.MXFP8, rows, cols, values, scales, block_rows=1, block_cols=32)
+    got = m.matvec(x)
+    dec = values.view(ml_dtypes.float8_e4m3fn).astype(np.float64).reshape(rows, cols)
+    for r in range(rows):
+        w = dec[r] * np.array([2.0 ** (int(scales[r * scale_cols + c // 32]) - 127)
+                               for c in range(cols)])
+        p = w * x.astype(np.float64)
+        err = abs(float(got[r]) - p.sum())
+        assert err <= 64 * np.finfo(np.float32).eps * max(np.abs(p).sum(), 1.0)
+
+
+def test_batched_equals_independent_matvec_bits(oracle):
+    # src/math/mxfp.rs:2595-2665 (MXFP4) and :2347 (MXFP8): batched == per-token, bitwise.
+    g = np.random.default_rng(7)
+    rows, cols = 17, 129
+    packed = g.integers(0, 256, (rows, 65), dtype=np.uint8)
+    scales = g.integers(118, 128, (rows, 5), dtype=np.uint8)
+    m4 = oracle.Matrix(oracle.MXFP4, rows, cols, packed, scales, group_size=32)
+    v8 = g.integers(0, 0x7E, (rows, 128), dtype=np.uint8)
+    s8 = g.integers(118, 128, (rows, 4), dtype=np.uint8)
+    m8 = oracle.Matrix(oracle.MXFP8, rows, 128, v8, s8, block_rows=1, block_cols=32)
+    for m, c in ((m4, cols), (m8, 128)):
+        for batch in [2, 3, 7, 12, 13, 25]:
+            x = g.standard_normal((batch, c)).astype(np.float32)
+            got = m.matmul_rows(x, batch)
+            want = np.stack([m.matvec(x[t]) for t in range(batch)])
+            assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
+# --- routing -----------------------------------------------------------------------------------
+
+def test_correction_bias_changes_selection_but_not_gate_weight(oracle):
+    # src/math/routing.rs:162-174
+    e, w, _ = oracle.route_noaux_tc([2.0, 1.0, 0.0, -1.0], [0.0] * 4, 2, 1, 1, False, 1.0)
+    assert list(e) == [0, 1]
+    e, w, _ = oracle.route_noaux_tc([2.0, 1.0, 0.0, -1.0], [0.0, 0.0, 2.0, 0.0], 2, 1, 1,
+                                    False, 1.0)
+    assert list(e) == [2, 0]
+    assert abs(w[0] - 0.5) < 1e-6
+
+
+def test_normalized_weights_sum_to_routed_scale(oracle):
+    # src/math/routing.rs:176-181
+    _, w, _ = oracle.route_noaux_tc([3.0, 2.0, 1.0, 0.0], [0.0] * 4, 3, 1, 1, True, 2.5)
+    assert abs(float(np.sum(w, dtype=np.float32)) - 2.5) < 1e-6
+
+
+def test_grouped_router_masks_losing_groups(oracle):
+    # src/math/routing.rs:183-196
+    e, _, _ = oracle.route_noaux_tc([3.0, 2.0, -3.0, -4.0, 1.0, 0.5, 0.0, -1.0], [0.0] * 8,
+                                    2, 2, 1, True, 1.0)
+    assert all(x < 4 for x in e)
+
+
+def test_normalization_epsilon_matches_underflowed_router(oracle):
+    # src/math/routing.rs:198-204
+    e, w, _ = oracle.route_noaux_tc([-1000.0] * 4, [0.0] * 4, 2, 1, 1, True, 2.5)
+    assert len(e) == 2 and all(x == 0.0 for x in w)
+
+
+def test_896_expert_tie_order(oracle):
+    # src/models/kimi_k3/moe.rs:778-796 (tie order of the same noaux_tc selection rule).
+    bias = np.zeros(896, np.float32)
+    bias[895] = 1.0
+    e, w, s = oracle.route_noaux_tc(np.zeros(896, np.float32), bias, 16, 1, 1, True, 1.0)
+    assert e[0] == 895 and list(e[1:]) == list(range(15))
+    assert s[0] == 1.5
+    assert all(abs(x - 1.0 / 16.0) < 1e-7 for x in w)
+
+
+def test_softmax_router_tie_break_and_renormalisation(oracle):
+    # src/models/qwen3_8/moe.rs:446-466
+    e, w = oracle.route_softmax_top_k([2.0, 2.0, 2.0, 1.0], 2)
+    assert list(e) == [0, 1] and all(abs(x - 0.5) < 1e-7 for x in w)
+    e, w = oracle.route_softmax_top_k(np.log(np.array([4.0, 2.0, 1.0], np.float32)), 2)
+    assert list(e) == [0, 1]
+    assert abs(w[0] - 2 / 3) < 1e-6 and abs(w[1] - 1 / 3) < 1e-6
+
+
+def test_route_geometry_errors(oracle):
+    # src/math/routing.rs:47-99 validation order.
+    with pytest.raises(oracle.OracleError) as e:
+        oracle.route_noaux_tc([0.0, np.nan], [0.0, 0.0], 1, 1, 1, True, 1.0)
+    assert e.value.code == oracle.ERR_NONFINITE
+    with pytest.raises(oracle.OracleError) as e:
+        oracle.route_noaux_tc([0.0] * 4, [0.0] * 4, 1, 3, 1, True, 1.0)
+    assert e.value.code == oracle.ERR_INVALID_GEOMETRY
+    with pytest.raises(oracle.OracleError) as e:
+        oracle.route_noaux_tc([0.0] * 4, [0.0] * 4, 1, 1, 1, True, 0.0)
+    assert e.value.code == oracle.ERR_INVALID_GEOMETRY
+
+
+# --- SwiGLU / grouping -----------------------------------------------------------------------
+
+def test_gated_mlp_matches_explicit_formula(oracle):
+    # src/model/mlp.rs:107-117
+    gate = oracle.Matrix(oracle.F32, 2, 2, np.array([1, 0, 0, 1], np.float32))
+    up = oracle.Matrix(oracle.F32, 2, 2, np.array([2, 0, 0, 3], np.float32))
+    down = oracle.Matrix(oracle.F32, 2, 2, np.array([1, 1, 1, -1], np.float32))
+    out = oracle.gated_mlp_forward(gate, up, down, np.array([1.0, -2.0], np.float32))
+    silu = lambda v: v / (1 + math.exp(-v))
+    first, second = silu(1.0) * 2.0, silu(-2.0) * -6.0
+    assert abs(out[0] - (first + second)) < 1e-6
+    assert abs(out[1] - (first - second)) < 1e-6
+
+
+def test_grouping_is_experts_then_tokens_ascending(oracle):
+    # src/models/qwen3_6/runtime.rs:1123-1132: BTreeMap by expert over token-major routes.
+    g = np.random.default_rng(3)
+    ids = np.stack([g.choice(37, 6, replace=False) for _ in range(50)]).astype(np.int32)
+    counts, offsets, pt, ps = oracle.group_routes(ids, 37)
+    order = sorted(range(ids.size), key=lambda i: (ids.flat[i], i))
+    assert list(pt) == [i // 6 for i in order]
+    assert list(ps) == [i % 6 for i in order]
+    assert list(counts) == list(np.bincount(ids.ravel(), minlength=37))
+    assert offsets[-1] == ids.size

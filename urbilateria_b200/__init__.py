@@ -1,0 +1,417 @@
+"""urbilateria_b200 — B200-native routed-expert (MoE) hot path of Urbilateria.
+
+The product is the C-ABI library liburb_moe.so (include/urb_moe.h; CUDA kernels for sm_100a).
+This package is its Python host mirror: the class and method names, argument meaning and
+error variants follow the reference's Rust API so that code written against
+``MxFp4Matrix::matvec`` / ``GatedMlp::forward`` / ``route_noaux_tc`` /
+``RuntimeMoeLayer::forward`` reads the same here.  Every call runs on the GPU; nothing falls
+back to the CPU.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+from typing import List, Optional, Sequence
+
+import numpy as np
+
+from . import native
+from .native import MoeGeometry as _CGeometry
+
+__all__ = [
+    "UrbError", "MxError", "Context", "MxFp4Matrix", "MxFp8Matrix", "Bf16Matrix", "DenseMatrix",
+    "GatedMlp", "RouteChoice", "MoeGeometry", "route_noaux_tc", "route_softmax_top_k",
+    "group_routes", "RuntimeMoeLayer", "default_context",
+]
+
+
+class UrbError(Exception):
+    """A non-zero urb_status.  ``kind`` is the reference error variant name."""
+
+    def __init__(self, code: int, message: str = ""):
+        self.code = code
+        self.kind = native.STATUS_NAMES.get(code, str(code))
+        super().__init__("%s%s" % (self.kind, (": " + message) if message else ""))
+
+
+MxError = UrbError  # MxError::{Shape, InvalidScale, NonFinite} map onto UrbError.kind
+
+
+def _ptr(a: Optional[np.ndarray]) -> int:
+    return 0 if a is None else a.ctypes.data
+
+
+class Context:
+    """One CUDA device and stream (urb_ctx)."""
+
+    def __init__(self, device: int = 0):
+        self.lib = native.load()
+        h = ctypes.c_void_p()
+        rc = self.lib.urb_ctx_create(device, ctypes.byref(h))
+        if rc != native.OK:
+            raise UrbError(rc, "urb_ctx_create(device=%d)" % device)
+        self.h = h
+        self.device = device
+
+    def check(self, rc: int):
+        if rc != native.OK:
+            buf = ctypes.create_string_buffer(512)
+            self.lib.urb_last_error(self.h, buf, 512)
+            raise UrbError(rc, buf.value.decode(errors="replace"))
+
+    def synchronize(self):
+        self.check(self.lib.urb_ctx_synchronize(self.h))
+
+    @property
+    def stream(self) -> int:
+        return self.lib.urb_ctx_stream(self.h) or 0
+
+    def set_stream(self, stream: int):
+        self.check(self.lib.urb_ctx_set_stream(self.h, ctypes.c_void_p(stream)))
+
+    def close(self):
+        if getattr(self, "h", None):
+            self.lib.urb_ctx_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+_default = None
+
+
+def default_context() -> Context:
+    global _default
+    if _default is None:
+        _default = Context(0)
+    return _default
+
+
+class _Matrix:
+    """Common WeightMatrix surface (src/model/weight.rs:69-320)."""
+
+    fmt = -1
+
+    def __init__(self, ctx: Context, handle: ctypes.c_void_p, rows: int, cols: int):
+        self.ctx, self.h, self._rows, self._cols = ctx, handle, rows, cols
+
+    def rows(self) -> int:
+        return self._rows
+
+    def cols(self) -> int:
+        return self._cols
+
+    def resident_bytes(self) -> int:
+        v = ctypes.c_size_t()
+        self.ctx.check(self.ctx.lib.urb_mat_info(self.h, None, None, None, ctypes.byref(v)))
+        return v.value
+
+    def matvec_rows(self, start: int, count: int, x) -> np.ndarray:
+        x = np.ascontiguousarray(x, dtype=np.float32).ravel()
+        y = np.empty(count, dtype=np.float32)
+        self.ctx.check(self.ctx.lib.urb_matvec_rows(self.ctx.h, self.h, start, count, _ptr(x),
+                                                    x.size, _ptr(y)))
+        return y
+
+    def matvec(self, x) -> np.ndarray:
+        return self.matvec_rows(0, self._rows, x)
+
+    def matmul_rows(self, x, batch: int) -> np.ndarray:
+        """x [batch, cols] (flat or 2-D) -> [batch, rows] token-major."""
+        x = np.ascontiguousarray(x, dtype=np.float32).ravel()
+        y = np.empty((batch, self._rows), dtype=np.float32)
+        self.ctx.check(self.ctx.lib.urb_matmul_rows(self.ctx.h, self.h, _ptr(x), batch, x.size,
+                                                    _ptr(y)))
+        return y
+
+    def matmul_row_range(self, start: int, count: int, x, batch: int) -> np.ndarray:
+        x = np.ascontiguousarray(x, dtype=np.float32).ravel()
+        y = np.empty((batch, count), dtype=np.float32)
+        self.ctx.check(self.ctx.lib.urb_matmul_row_range(self.ctx.h, self.h, start, count,
+                                                         _ptr(x), batch, x.size, _ptr(y)))
+        return y
+
+    def matmul_rows_fp32_accum(self, x, batch: int) -> np.ndarray:
+        x = np.ascontiguousarray(x, dtype=np.float32).ravel()
+        y = np.empty((batch, self._rows), dtype=np.float32)
+        self.ctx.check(self.ctx.lib.urb_matmul_rows_fp32_accum(self.ctx.h, self.h, _ptr(x),
+                                                               batch, x.size, _ptr(y)))
+        return y
+
+    def matvec_fp32_accum(self, x) -> np.ndarray:
+        return self.matmul_rows_fp32_accum(x, 1)[0]
+
+    def matmul_rows_device(self, d_x: int, batch: int, d_y: int, d_status: int = 0):
+        """Device pointers (e.g. torch tensor.data_ptr()); stream-ordered, no host sync."""
+        self.ctx.check(self.ctx.lib.urb_matmul_rows_device(self.ctx.h, self.h, d_x, batch, d_y,
+                                                           d_status or None))
+
+    def free(self):
+        if self.h:
+            self.ctx.lib.urb_mat_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
+class MxFp4Matrix(_Matrix):
+    """MxFp4Matrix (src/math/mxfp.rs:1363-1847), resident in HBM."""
+
+    fmt = native.FMT_MXFP4
+
+    @classmethod
+    def from_packed(cls, rows: int, cols: int, group_size: int, packed, scale_bytes,
+                    ctx: Optional[Context] = None):
+        ctx = ctx or default_context()
+        packed = np.ascontiguousarray(packed, dtype=np.uint8).ravel()
+        scales = np.ascontiguousarray(scale_bytes, dtype=np.uint8).ravel()
+        h = ctypes.c_void_p()
+        ctx.check(ctx.lib.urb_mxfp4_upload(ctx.h, rows, cols, group_size, _ptr(packed),
+                                           packed.size, _ptr(scales), scales.size,
+                                           ctypes.byref(h)))
+        return cls(ctx, h, rows, cols)
+
+
+class MxFp8Matrix(_Matrix):
+    """MxFp8Matrix with E8M0 block scales (src/math/mxfp.rs:321-877), resident in HBM."""
+
+    fmt = native.FMT_MXFP8
+
+    @classmethod
+    def from_packed(cls, rows: int, cols: int, block_rows: int, block_cols: int, values,
+                    scale_bytes, ctx: Optional[Context] = None):
+        ctx = ctx or default_context()
+        values = np.ascontiguousarray(values, dtype=np.uint8).ravel()
+        scales = np.ascontiguousarray(scale_bytes, dtype=np.uint8).ravel()
+        h = ctypes.c_void_p()
+        ctx.check(ctx.lib.urb_mxfp8_upload(ctx.h, rows, cols, block_rows, block_cols,
+                                           _ptr(values), values.size, _ptr(scales), scales.size,
+                                           ctypes.byref(h)))
+        return cls(ctx, h, rows, cols)
+
+
+class Bf16Matrix(_Matrix):
+    """Bf16Matrix (src/model/bf16.rs): bf16 bit patterns as uint16, row-major."""
+
+    fmt = native.FMT_BF16
+
+    @classmethod
+    def from_bits(cls, rows: int, cols: int, bits, ctx: Optional[Context] = None):
+        ctx = ctx or default_context()
+        bits = np.ascontiguousarray(bits, dtype=np.uint16).ravel()
+        h = ctypes.c_void_p()
+        ctx.check(ctx.lib.urb_bf16_upload(ctx.h, rows, cols, _ptr(bits), bits.size,
+                                          ctypes.byref(h)))
+        return cls(ctx, h, rows, cols)
+
+
+class DenseMatrix(_Matrix):
+    """DenseMatrix (src/model/matrix.rs), f32 row-major."""
+
+    fmt = native.FMT_F32
+
+    @classmethod
+    def new(cls, rows: int, cols: int, data, ctx: Optional[Context] = None):
+        ctx = ctx or default_context()
+        data = np.ascontiguousarray(data, dtype=np.float32).ravel()
+        h = ctypes.c_void_p()
+        ctx.check(ctx.lib.urb_f32_upload(ctx.h, rows, cols, _ptr(data), data.size,
+                                         ctypes.byref(h)))
+        return cls(ctx, h, rows, cols)
+
+
+class GatedMlp:
+    """GatedMlp (src/model/mlp.rs:38-99): down(silu(gate x) * (up x))."""
+
+    def __init__(self, gate: _Matrix, up: _Matrix, down: _Matrix):
+        if gate.rows() != up.rows() or gate.cols() != up.cols():
+            raise UrbError(native.ERR_SHAPE, "gate and up shapes differ")
+        if down.cols() != gate.rows() or down.rows() != gate.cols():
+            raise UrbError(native.ERR_SHAPE, "down must map intermediate back to hidden")
+        self.gate, self.up, self.down = gate, up, down
+        self.ctx = gate.ctx
+
+    def hidden_size(self) -> int:
+        return self.gate.cols()
+
+    def intermediate_size(self) -> int:
+        return self.gate.rows()
+
+    def resident_bytes(self) -> int:
+        return self.gate.resident_bytes() + self.up.resident_bytes() + self.down.resident_bytes()
+
+    def forward_batch(self, x, tokens: int) -> np.ndarray:
+        x = np.ascontiguousarray(x, dtype=np.float32).ravel()
+        out = np.empty((tokens, self.hidden_size()), dtype=np.float32)
+        self.ctx.check(self.ctx.lib.urb_gated_mlp_forward(self.ctx.h, self.gate.h, self.up.h,
+                                                          self.down.h, _ptr(x), tokens,
+                                                          _ptr(out)))
+        return out
+
+    def forward(self, x) -> np.ndarray:
+        return self.forward_batch(x, 1)[0]
+
+
+@dataclass
+class RouteChoice:
+    """RouteChoice (src/math/routing.rs:8-15)."""
+    expert: int
+    weight: float
+    selection_score: float
+
+
+@dataclass
+class MoeGeometry:
+    top_k: int = 8
+    n_group: int = 1
+    topk_group: int = 1
+    normalize: bool = True
+    routed_scaling_factor: float = 1.0
+
+    def c(self) -> _CGeometry:
+        return _CGeometry(self.top_k, self.n_group, self.topk_group, int(self.normalize),
+                          self.routed_scaling_factor)
+
+
+def route_noaux_tc(logits, correction_bias, top_k: int, n_group: int, topk_group: int,
+                   normalize: bool, routed_scaling_factor: float,
+                   ctx: Optional[Context] = None):
+    """route_noaux_tc (src/math/routing.rs:38-155).  1-D logits -> List[RouteChoice];
+    2-D [tokens, experts] -> (experts, weights, scores) arrays [tokens, top_k]."""
+    ctx = ctx or default_context()
+    lg = np.ascontiguousarray(logits, dtype=np.float32)
+    single = lg.ndim == 1
+    lg2 = lg.reshape(1, -1) if single else lg
+    bias = np.ascontiguousarray(correction_bias, dtype=np.float32).ravel()
+    t, e = lg2.shape
+    if bias.size != e:
+        raise UrbError(native.ERR_SHAPE, "%d logits but %d bias values" % (e, bias.size))
+    geo = MoeGeometry(top_k, n_group, topk_group, normalize, routed_scaling_factor).c()
+    k = max(top_k, 1)
+    ids = np.empty((t, k), dtype=np.int32)
+    w = np.empty((t, k), dtype=np.float32)
+    s = np.empty((t, k), dtype=np.float32)
+    ctx.check(ctx.lib.urb_route_noaux_tc(ctx.h, _ptr(lg2), _ptr(bias), t, e, ctypes.byref(geo),
+                                         _ptr(ids), _ptr(w), _ptr(s)))
+    if single:
+        return [RouteChoice(int(ids[0, i]), float(w[0, i]), float(s[0, i])) for i in range(top_k)]
+    return ids, w, s
+
+
+def route_softmax_top_k(logits, top_k: int, ctx: Optional[Context] = None):
+    """route_softmax_top_k (src/models/qwen3_8/moe.rs:91-159)."""
+    ctx = ctx or default_context()
+    lg = np.ascontiguousarray(logits, dtype=np.float32)
+    single = lg.ndim == 1
+    lg2 = lg.reshape(1, -1) if single else lg
+    t, e = lg2.shape
+    ids = np.empty((t, max(top_k, 1)), dtype=np.int32)
+    w = np.empty((t, max(top_k, 1)), dtype=np.float32)
+    ctx.check(ctx.lib.urb_route_softmax_top_k(ctx.h, _ptr(lg2), t, e, top_k, _ptr(ids),
+                                              _ptr(w)))
+    if single:
+        return [(int(ids[0, i]), float(w[0, i])) for i in range(top_k)]
+    return ids, w
+
+
+def group_routes(expert_ids, experts: int, ctx: Optional[Context] = None):
+    """Ragged grouping (src/models/qwen3_6/runtime.rs:1083-1132): experts ascending, tokens
+    ascending.  Returns (counts, offsets, perm_token, perm_slot)."""
+    ctx = ctx or default_context()
+    ids = np.ascontiguousarray(expert_ids, dtype=np.int32)
+    t, k = ids.shape
+    counts = np.empty(experts, dtype=np.int32)
+    offsets = np.empty(experts + 1, dtype=np.int32)
+    pt = np.empty(max(t * k, 1), dtype=np.int32)
+    ps = np.empty(max(t * k, 1), dtype=np.int32)
+    ctx.check(ctx.lib.urb_group_routes(ctx.h, _ptr(ids), t, k, experts, _ptr(counts),
+                                       _ptr(offsets), _ptr(pt), _ptr(ps)))
+    return counts, offsets, pt[:t * k], ps[:t * k]
+
+
+class RuntimeMoeLayer:
+    """RuntimeMoeLayer (src/models/glm/runtime/moe.rs:73-176), all experts resident in HBM."""
+
+    def __init__(self, router: _Matrix, correction_bias, experts: Sequence[GatedMlp],
+                 shared: Optional[GatedMlp], geometry: MoeGeometry):
+        self.ctx = router.ctx
+        self.router = router
+        self.bias = np.ascontiguousarray(correction_bias, dtype=np.float32).ravel()
+        self.experts = list(experts)
+        self.shared = shared
+        self.geometry = geometry
+        n = len(self.experts)
+        arr = lambda ms: (ctypes.c_void_p * n)(*[m.h.value for m in ms])
+        self._g = arr([e.gate for e in self.experts])
+        self._u = arr([e.up for e in self.experts])
+        self._d = arr([e.down for e in self.experts])
+        self._geo = geometry.c()
+        h = ctypes.c_void_p()
+        sg = shared.gate.h if shared else None
+        su = shared.up.h if shared else None
+        sd = shared.down.h if shared else None
+        self.ctx.check(self.ctx.lib.urb_moe_layer_create(
+            self.ctx.h, router.h, _ptr(self.bias), n, self._g, self._u, self._d, sg, su, sd,
+            ctypes.byref(self._geo), ctypes.byref(h)))
+        self.h = h
+
+    def hidden_size(self) -> int:
+        return self.router.cols()
+
+    def expert_count(self) -> int:
+        return self.router.rows()
+
+    def forward_batch(self, x, tokens: int, details: bool = False):
+        """x [tokens, hidden] -> (out [tokens, hidden], expert ids, weights[, extras])."""
+        x = np.ascontiguousarray(x, dtype=np.float32).ravel()
+        H, E, K = self.hidden_size(), self.expert_count(), self.geometry.top_k
+        out = np.empty((tokens, H), dtype=np.float32)
+        ids = np.empty((tokens, K), dtype=np.int32)
+        w = np.empty((tokens, K), dtype=np.float32)
+        s = np.empty((tokens, K), dtype=np.float32)
+        extra = {}
+        logits = counts = pt = ps = None
+        if details:
+            logits = np.empty((tokens, E), dtype=np.float32)
+            counts = np.empty(E, dtype=np.int32)
+            pt = np.empty(tokens * K, dtype=np.int32)
+            ps = np.empty(tokens * K, dtype=np.int32)
+            extra = dict(router_logits=logits, counts=counts, perm_token=pt, perm_slot=ps)
+        self.ctx.check(self.ctx.lib.urb_moe_forward(
+            self.ctx.h, self.h, _ptr(x), tokens, _ptr(out), _ptr(ids), _ptr(w), _ptr(s),
+            _ptr(logits), _ptr(counts), _ptr(pt), _ptr(ps)))
+        extra["selection_score"] = s
+        return out, ids, w, extra
+
+    def forward(self, x):
+        """Single token: (Vec<f32>, Vec<RouteChoice>) as in the reference."""
+        out, ids, w, extra = self.forward_batch(x, 1)
+        s = extra["selection_score"]
+        routes = [RouteChoice(int(ids[0, i]), float(w[0, i]), float(s[0, i]))
+                  for i in range(self.geometry.top_k)]
+        return out[0], routes
+
+    def forward_device(self, d_x: int, tokens: int, d_out: int, d_ids: int = 0, d_w: int = 0,
+                       d_status: int = 0):
+        self.ctx.check(self.ctx.lib.urb_moe_forward_device(
+            self.ctx.h, self.h, d_x, tokens, d_out, d_ids or None, d_w or None,
+            d_status or None))
+
+    def free(self):
+        if getattr(self, "h", None):
+            self.ctx.lib.urb_moe_layer_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass

@@ -1,0 +1,435 @@
+// layer.cu — MoE layer C ABI: construction checks of RuntimeMoeLayer::new and the forward
+// pipeline (src/models/glm/runtime/moe.rs:88-176), all stream-ordered on the device:
+//   row shifts -> exact router logits -> route_noaux_tc -> grouping -> grouped gate/up with
+//   fused SwiGLU -> grouped down -> weighted f64 combine.
+#include <cmath>
+#include <cstring>
+
+#include "urb_internal.cuh"
+#include "urb_moe_internal.cuh"
+
+namespace urb {
+namespace {
+
+size_t div_ceil(size_t a, size_t b) { return (a + b - 1) / b; }
+
+struct Carve {
+    uint8_t *base;
+    size_t off = 0;
+    template <class T>
+    T *take(size_t n) {
+        off = (off + 255) & ~size_t(255);
+        T *p = reinterpret_cast<T *>(base + off);
+        off += n * sizeof(T);
+        return p;
+    }
+};
+
+constexpr int kCap = 4;  // tokens per segment: hi/lo halves fill one 8-column n-block
+
+size_t max_segments(size_t tokens, size_t K, size_t experts) {
+    size_t TK = tokens * K;
+    return std::min(TK, experts) + TK / kCap + div_ceil(tokens, kCap) + 2;
+}
+
+}  // namespace
+
+int moe_forward_device(Layer *L, const float *d_x, int T, float *d_out, MoeWork *wout,
+                       int32_t *d_status, cudaStream_t st) {
+    Ctx *ctx = L->ctx;
+    const size_t E = L->experts, K = L->geo.top_k, H = L->hidden, I = L->inter;
+    const size_t TK = size_t(T) * K, cols = TK + T;
+    const size_t nseg = max_segments(T, K, E);
+    size_t need = T * 4 + T * E * 4 + TK * 12 + E * 8 + 8 + TK * 12 + 2 * nseg * sizeof(Seg) +
+                  64 + cols * 8 + cols * I * 4 + cols * H * 4 + 32 * 256;
+    int rc;
+    uint8_t *ws = static_cast<uint8_t *>(workspace(ctx, need, &rc));
+    if (!ws) return rc;
+    Carve cv{ws};
+    MoeWork w{};
+    w.shift = cv.take<int32_t>(T);
+    w.logits = cv.take<float>(size_t(T) * E);
+    w.ids = cv.take<int32_t>(TK);
+    w.w = cv.take<float>(TK);
+    w.score = cv.take<float>(TK);
+    w.counts = cv.take<int32_t>(E);
+    w.offsets = cv.take<int32_t>(E + 1);
+    w.perm_token = cv.take<int32_t>(TK);
+    w.perm_slot = cv.take<int32_t>(TK);
+    w.inv = cv.take<int32_t>(TK);
+    w.segs_gu = cv.take<Seg>(nseg);
+    w.segs_dn = cv.take<Seg>(nseg);
+    w.scalars = cv.take<int>(4);
+    w.col_src = cv.take<int32_t>(cols);
+    w.maxexp = cv.take<int32_t>(cols);
+    w.h = cv.take<float>(cols * I);
+    w.y = cv.take<float>(cols * H);
+    w.status = d_status;
+
+    prof_begin(ctx, URB_K_ROW_SHIFT, st);
+    rc = launch_row_shift(d_x, T, int(H), int(H), w.shift, d_status, st);
+    prof_end(ctx, st);
+    if (rc) return cuda_fail(ctx, cudaGetLastError(), "row shift");
+    prof_begin(ctx, URB_K_ROUTER_LOGITS, st);
+    rc = launch_router_logits(L->router, d_x, T, w.logits, st);
+    prof_end(ctx, st);
+    if (rc) return cuda_fail(ctx, cudaGetLastError(), "router logits");
+    prof_begin(ctx, URB_K_ROUTE, st);
+    rc = launch_route_noaux(ctx, w.logits, L->d_bias, T, int(E), L->geo, w.ids, w.w, w.score,
+                            d_status, st);
+    prof_end(ctx, st);
+    if (rc) return rc;
+
+    const Mat *g0 = L->gate[0], *d0 = L->down[0];
+    void **tb = L->d_tables;
+    PermArgs p{};
+    p.ids = w.ids;
+    p.tokens = T;
+    p.top_k = int(K);
+    p.experts = int(E);
+    p.cap = kCap;
+    p.counts = w.counts;
+    p.offsets = w.offsets;
+    p.perm_token = w.perm_token;
+    p.perm_slot = w.perm_slot;
+    p.inv = w.inv;
+    p.segs_gu = w.segs_gu;
+    p.segs_dn = w.segs_dn;
+    p.nsegs_gu = w.scalars;
+    p.total_rows_gu = w.scalars + 1;
+    p.nsegs_dn = w.scalars + 2;
+    p.total_rows_dn = w.scalars + 3;
+    p.col_src = w.col_src;
+    p.maxexp = w.maxexp;
+    p.gate_tiles = reinterpret_cast<const uint8_t *const *>(tb);
+    p.up_tiles = reinterpret_cast<const uint8_t *const *>(tb + E);
+    p.down_tiles = reinterpret_cast<const uint8_t *const *>(tb + 2 * E);
+    p.gate_rexp = reinterpret_cast<const int8_t *const *>(tb + 3 * E);
+    p.up_rexp = reinterpret_cast<const int8_t *const *>(tb + 4 * E);
+    p.down_rexp = reinterpret_cast<const int8_t *const *>(tb + 5 * E);
+    p.shared_in_pass = L->sg ? 1 : 0;
+    if (L->sg) {
+        p.sh_gate_tiles = L->sg->tiles; p.sh_gate_rexp = L->sg->row_exp;
+        p.sh_up_tiles = L->su->tiles; p.sh_up_rexp = L->su->row_exp;
+        p.sh_down_tiles = L->sd->tiles; p.sh_down_rexp = L->sd->row_exp;
+    }
+    p.hidden = int(H);
+    p.inter = int(I);
+    p.gu_rbs = g0->rbs;
+    p.gu_kslices = g0->kslices;
+    p.dn_rbs = d0->rbs;
+    p.dn_kslices = d0->kslices;
+    p.status = d_status;
+    prof_begin(ctx, URB_K_PERMUTE, st);
+    rc = launch_permute(ctx, p, st);
+    prof_end(ctx, st);
+    if (rc) return rc;
+
+    // Upper bound of work rows per SM picks how many warps share a row block.
+    const long est_rows_gu = long(std::min(nseg, TK + div_ceil(T, kCap))) * 16 * g0->rbs;
+    const long est_per_sm = est_rows_gu / std::max(1, ctx->num_sms);
+    const int ksplit = est_per_sm < 64 ? 8 : (est_per_sm < 256 ? 2 : 1);
+
+    GroupArgs gu{};
+    gu.segs = w.segs_gu;
+    gu.nsegs = w.scalars;
+    gu.total_rows = w.scalars + 1;
+    gu.src = d_x;
+    gu.src_stride = int(H);
+    gu.col_src = w.col_src;
+    gu.src_shift = w.shift;
+    gu.out = w.h;
+    gu.out_stride = int(I);
+    gu.out_maxexp = w.maxexp;
+    gu.hilo = 1;
+    prof_begin(ctx, URB_K_GATE_UP, st);
+    rc = launch_grouped_ex(ctx, L->fmt, true, ksplit, gu, 2 * kCap, g0->kslices, st);
+    prof_end(ctx, st);
+    if (rc) return rc;
+
+    GroupArgs dn{};
+    dn.segs = w.segs_dn;
+    dn.nsegs = w.scalars + 2;
+    dn.total_rows = w.scalars + 3;
+    dn.src = w.h;
+    dn.src_stride = int(I);
+    dn.col_src = nullptr;
+    dn.src_shift = nullptr;
+    dn.src_maxexp = w.maxexp;
+    dn.out = w.y;
+    dn.out_stride = int(H);
+    dn.hilo = 1;
+    prof_begin(ctx, URB_K_DOWN, st);
+    rc = launch_grouped_ex(ctx, L->fmt, false, ksplit == 8 ? 2 : ksplit, dn, 2 * kCap,
+                           d0->kslices, st);
+    prof_end(ctx, st);
+    if (rc) return rc;
+
+    prof_begin(ctx, URB_K_COMBINE, st);
+    rc = launch_combine(ctx, w.y, L->sg ? w.y + TK * H : nullptr, w.w, w.inv, T, int(K), int(H),
+                        d_out, st);
+    prof_end(ctx, st);
+    if (rc) return rc;
+    if (wout) *wout = w;
+    return URB_OK;
+}
+
+// GatedMlp::forward (src/model/mlp.rs:90-99) for `T` tokens on the device: one grouped pair
+// pass (gate/up with fused SwiGLU) and one grouped down pass, host-built segments.
+int gated_mlp_device(Ctx *ctx, const Mat *g, const Mat *u, const Mat *d, const float *d_x, int T,
+                     float *d_out, int32_t *d_status, cudaStream_t st) {
+    const size_t H = g->cols, I = g->rows;
+    const int nseg = int(div_ceil(T, kCap));
+    int rc;
+    size_t need = T * 4 + 2 * nseg * sizeof(Seg) + 64 + T * 4 + size_t(T) * I * 4 + 8 * 256;
+    uint8_t *ws = static_cast<uint8_t *>(workspace(ctx, need, &rc));
+    if (!ws) return rc;
+    Carve cv{ws};
+    int32_t *shift = cv.take<int32_t>(T);
+    Seg *segs = cv.take<Seg>(2 * nseg);
+    int *sc = cv.take<int>(4);
+    int32_t *maxexp = cv.take<int32_t>(T);
+    float *h = cv.take<float>(size_t(T) * I);
+    std::vector<Seg> hs(2 * nseg);
+    for (int i = 0; i < nseg; ++i) {
+        Seg &a = hs[i], &b = hs[nseg + i];
+        a.tiles_a = g->tiles; a.rexp_a = g->row_exp; a.tiles_b = u->tiles; a.rexp_b = u->row_exp;
+        a.rbs = g->rbs; a.rows = int(I); a.kslices = g->kslices; a.cols = int(H);
+        a.col_begin = i * kCap; a.ntok = std::min(kCap, T - i * kCap);
+        a.row_begin = i * 16 * g->rbs; a.pad = 0;
+        b.tiles_a = d->tiles; b.rexp_a = d->row_exp; b.tiles_b = nullptr; b.rexp_b = nullptr;
+        b.rbs = d->rbs; b.rows = int(H); b.kslices = d->kslices; b.cols = int(I);
+        b.col_begin = a.col_begin; b.ntok = a.ntok; b.row_begin = i * 16 * d->rbs; b.pad = 0;
+    }
+    int hsc[4] = {nseg, nseg * 16 * g->rbs, nseg, nseg * 16 * d->rbs};
+    URB_CUDA(ctx, cudaMemcpyAsync(segs, hs.data(), hs.size() * sizeof(Seg), cudaMemcpyHostToDevice, st));
+    URB_CUDA(ctx, cudaMemcpyAsync(sc, hsc, sizeof(hsc), cudaMemcpyHostToDevice, st));
+    if (launch_row_shift(d_x, T, int(H), int(H), shift, d_status, st))
+        return cuda_fail(ctx, cudaGetLastError(), "row shift");
+    std::vector<int32_t> neg(T, -1000);
+    URB_CUDA(ctx, cudaMemcpyAsync(maxexp, neg.data(), size_t(T) * 4, cudaMemcpyHostToDevice, st));
+    GroupArgs a{};
+    a.segs = segs; a.nsegs = sc; a.total_rows = sc + 1;
+    a.src = d_x; a.src_stride = int(H); a.src_shift = shift;
+    a.out = h; a.out_stride = int(I); a.out_maxexp = maxexp; a.hilo = 1;
+    const long per_sm_gu = long(hsc[1]) / std::max(1, ctx->num_sms);
+    prof_begin(ctx, URB_K_GATE_UP, st);
+    rc = launch_grouped_ex(ctx, g->format, true, per_sm_gu < 64 ? 8 : per_sm_gu < 256 ? 2 : 1, a,
+                           2 * kCap, g->kslices, st);
+    prof_end(ctx, st);
+    if (rc) return rc;
+    GroupArgs b{};
+    b.segs = segs + nseg; b.nsegs = sc + 2; b.total_rows = sc + 3;
+    b.src = h; b.src_stride = int(I); b.src_maxexp = maxexp;
+    b.out = d_out; b.out_stride = int(H); b.hilo = 1;
+    const long per_sm_dn = long(hsc[3]) / std::max(1, ctx->num_sms);
+    prof_begin(ctx, URB_K_DOWN, st);
+    rc = launch_grouped_ex(ctx, d->format, false, per_sm_dn < 64 ? 8 : per_sm_dn < 256 ? 2 : 1,
+                           b, 2 * kCap, d->kslices, st);
+    prof_end(ctx, st);
+    return rc;
+}
+
+}  // namespace urb
+
+using namespace urb;
+
+extern "C" {
+
+int urb_moe_layer_create(urb_ctx *ctx, const urb_mat *router, const float *bias, size_t experts,
+                         const urb_mat *const *gate, const urb_mat *const *up,
+                         const urb_mat *const *down, const urb_mat *sg, const urb_mat *su,
+                         const urb_mat *sd, const urb_moe_geometry *geo, urb_layer **out) {
+    if (!ctx || !router || !bias || !gate || !up || !down || !geo || !out)
+        return URB_ERR_INVALID_ARGUMENT;
+    std::lock_guard<std::recursive_mutex> lk(ctx->mu);
+    cudaSetDevice(ctx->device);
+    *out = nullptr;
+    // RuntimeMoeLayer::new (glm/runtime/moe.rs:88-129).
+    if (router->rows == 0 || router->cols == 0)
+        return set_error(ctx, URB_ERR_INVALID_GEOMETRY, "router dimensions must be non-zero");
+    if (experts != router->rows)
+        return set_error(ctx, URB_ERR_SHAPE, "router rows differ from the correction bias length");
+    for (size_t e = 0; e < experts; ++e)
+        if (!std::isfinite(bias[e]))
+            return set_error(ctx, URB_ERR_INVALID_GEOMETRY, "correction bias contains NaN or infinity");
+    const size_t H = router->cols;
+    bool have_shared = sg && su && sd;
+    if (!have_shared && (sg || su || sd))
+        return set_error(ctx, URB_ERR_INVALID_ARGUMENT, "shared expert needs gate, up and down");
+    if (have_shared && sg->cols != H)
+        return set_error(ctx, URB_ERR_SHAPE, "router hidden size differs from the shared expert");
+    // route_noaux_tc on zero logits validates the geometry (moe.rs:113-121).
+    if (!std::isfinite(geo->routed_scaling_factor))
+        return set_error(ctx, URB_ERR_NONFINITE, "routed_scaling_factor is not finite");
+    if (geo->routed_scaling_factor <= 0.0f || geo->n_group == 0 || experts % geo->n_group ||
+        geo->top_k == 0 || geo->top_k > experts || geo->topk_group == 0 ||
+        geo->topk_group > geo->n_group || experts / geo->n_group < 2 ||
+        size_t(geo->topk_group) * (experts / geo->n_group) < geo->top_k)
+        return set_error(ctx, URB_ERR_INVALID_GEOMETRY, "invalid noaux_tc geometry");
+    if (geo->top_k > 64) return set_error(ctx, URB_ERR_UNSUPPORTED, "top_k above 64");
+    if (router->format != URB_FMT_BF16 && router->format != URB_FMT_F32)
+        return set_error(ctx, URB_ERR_UNSUPPORTED, "router must be BF16 or F32 for exact logits");
+    // GatedMlp::new_mixed shape contract (src/model/mlp.rs:60-81) for every expert, plus this
+    // build's requirement that all experts share one tiled format and shape.
+    const int fmt = gate[0]->format;
+    const size_t I = gate[0]->rows;
+    auto check_mlp = [&](const urb_mat *g, const urb_mat *u, const urb_mat *d) -> int {
+        if (!g || !u || !d) return URB_ERR_INVALID_ARGUMENT;
+        if (g->rows != u->rows || g->cols != u->cols) return URB_ERR_SHAPE;
+        if (d->cols != g->rows || d->rows != g->cols) return URB_ERR_SHAPE;
+        if (g->cols != H || g->rows != I) return URB_ERR_SHAPE;
+        if (!g->tiled || !u->tiled || !d->tiled) return URB_ERR_UNSUPPORTED;
+        if (g->format != fmt || u->format != fmt || d->format != fmt) return URB_ERR_UNSUPPORTED;
+        return URB_OK;
+    };
+    for (size_t e = 0; e < experts; ++e) {
+        int rc = check_mlp(gate[e], up[e], down[e]);
+        if (rc) return set_error(ctx, rc, "routed expert shape/format is not supported");
+    }
+    if (have_shared) {
+        int rc = check_mlp(sg, su, sd);
+        if (rc) return set_error(ctx, rc, "shared expert shape/format is not supported");
+    }
+    urb_layer *L = new urb_layer();
+    L->ctx = ctx;
+    L->router = router;
+    L->experts = experts;
+    L->hidden = H;
+    L->inter = I;
+    L->fmt = fmt;
+    L->geo = *geo;
+    L->gate.assign(gate, gate + experts);
+    L->up.assign(up, up + experts);
+    L->down.assign(down, down + experts);
+    if (have_shared) { L->sg = sg; L->su = su; L->sd = sd; }
+    std::vector<void *> tables(6 * experts);
+    for (size_t e = 0; e < experts; ++e) {
+        tables[e] = gate[e]->tiles;
+        tables[experts + e] = up[e]->tiles;
+        tables[2 * experts + e] = down[e]->tiles;
+        tables[3 * experts + e] = gate[e]->row_exp;
+        tables[4 * experts + e] = up[e]->row_exp;
+        tables[5 * experts + e] = down[e]->row_exp;
+    }
+    cudaError_t err = cudaMalloc(&L->d_tables, tables.size() * sizeof(void *));
+    if (err == cudaSuccess) err = cudaMalloc(&L->d_bias, experts * 4);
+    if (err == cudaSuccess)
+        err = cudaMemcpy(L->d_tables, tables.data(), tables.size() * sizeof(void *), cudaMemcpyHostToDevice);
+    if (err == cudaSuccess) err = cudaMemcpy(L->d_bias, bias, experts * 4, cudaMemcpyDefault);
+    if (err != cudaSuccess) {
+        urb_moe_layer_free(L);
+        return cuda_fail(ctx, err, "layer tables");
+    }
+    *out = L;
+    return URB_OK;
+}
+
+int urb_moe_layer_free(urb_layer *L) {
+    if (!L) return URB_ERR_INVALID_ARGUMENT;
+    if (L->ctx) {
+        cudaSetDevice(L->ctx->device);
+        cudaStreamSynchronize(L->ctx->stream);
+    }
+    if (L->d_tables) cudaFree(L->d_tables);
+    if (L->d_bias) cudaFree(L->d_bias);
+    delete L;
+    return URB_OK;
+}
+
+int urb_moe_forward_device(urb_ctx *ctx, urb_layer *L, const float *d_x, size_t tokens,
+                           float *d_out, int32_t *d_route_expert, float *d_route_weight,
+                           int32_t *d_status) {
+    if (!ctx || !L || !d_x || !d_out) return URB_ERR_INVALID_ARGUMENT;
+    std::lock_guard<std::recursive_mutex> lk(ctx->mu);
+    cudaSetDevice(ctx->device);
+    if (tokens == 0) return URB_OK;
+    MoeWork w{};
+    int rc = moe_forward_device(L, d_x, int(tokens), d_out, &w, d_status, ctx->stream);
+    if (rc) return rc;
+    size_t TK = tokens * L->geo.top_k;
+    if (d_route_expert)
+        URB_CUDA(ctx, cudaMemcpyAsync(d_route_expert, w.ids, TK * 4, cudaMemcpyDeviceToDevice, ctx->stream));
+    if (d_route_weight)
+        URB_CUDA(ctx, cudaMemcpyAsync(d_route_weight, w.w, TK * 4, cudaMemcpyDeviceToDevice, ctx->stream));
+    return URB_OK;
+}
+
+int urb_moe_forward(urb_ctx *ctx, urb_layer *L, const float *x, size_t tokens, float *out,
+                    int32_t *route_expert, float *route_weight, float *route_score,
+                    float *router_logits, int32_t *counts, int32_t *perm_token,
+                    int32_t *perm_slot) {
+    if (!ctx || !L || !x || !out) return URB_ERR_INVALID_ARGUMENT;
+    std::lock_guard<std::recursive_mutex> lk(ctx->mu);
+    cudaSetDevice(ctx->device);
+    if (tokens == 0) return URB_OK;
+    cudaStream_t st = ctx->stream;
+    const size_t H = L->hidden, TK = tokens * L->geo.top_k, E = L->experts;
+    float *d_io = nullptr;
+    URB_CUDA(ctx, cudaMallocAsync(&d_io, 2 * tokens * H * 4, st));
+    float *d_x = d_io, *d_out = d_io + tokens * H;
+    URB_CUDA(ctx, cudaMemsetAsync(ctx->d_status, 0, 4, st));
+    URB_CUDA(ctx, cudaMemcpyAsync(d_x, x, tokens * H * 4, cudaMemcpyDefault, st));
+    MoeWork w{};
+    int rc = moe_forward_device(L, d_x, int(tokens), d_out, &w, ctx->d_status, st);
+    if (rc) {
+        cudaFreeAsync(d_io, st);
+        return rc;
+    }
+    int32_t status = 0;
+    URB_CUDA(ctx, cudaMemcpyAsync(out, d_out, tokens * H * 4, cudaMemcpyDefault, st));
+    if (route_expert) URB_CUDA(ctx, cudaMemcpyAsync(route_expert, w.ids, TK * 4, cudaMemcpyDefault, st));
+    if (route_weight) URB_CUDA(ctx, cudaMemcpyAsync(route_weight, w.w, TK * 4, cudaMemcpyDefault, st));
+    if (route_score) URB_CUDA(ctx, cudaMemcpyAsync(route_score, w.score, TK * 4, cudaMemcpyDefault, st));
+    if (router_logits) URB_CUDA(ctx, cudaMemcpyAsync(router_logits, w.logits, tokens * E * 4, cudaMemcpyDefault, st));
+    if (counts) URB_CUDA(ctx, cudaMemcpyAsync(counts, w.counts, E * 4, cudaMemcpyDefault, st));
+    if (perm_token) URB_CUDA(ctx, cudaMemcpyAsync(perm_token, w.perm_token, TK * 4, cudaMemcpyDefault, st));
+    if (perm_slot) URB_CUDA(ctx, cudaMemcpyAsync(perm_slot, w.perm_slot, TK * 4, cudaMemcpyDefault, st));
+    URB_CUDA(ctx, cudaMemcpyAsync(&status, ctx->d_status, 4, cudaMemcpyDeviceToHost, st));
+    cudaFreeAsync(d_io, st);
+    URB_CUDA(ctx, cudaStreamSynchronize(st));
+    if (status) return set_error(ctx, status, "MoE forward rejected its input");
+    return URB_OK;
+}
+
+int urb_gated_mlp_forward(urb_ctx *ctx, const urb_mat *g, const urb_mat *u, const urb_mat *d,
+                          const float *x, size_t tokens, float *out) {
+    if (!ctx || !g || !u || !d || !x || !out) return URB_ERR_INVALID_ARGUMENT;
+    std::lock_guard<std::recursive_mutex> lk(ctx->mu);
+    cudaSetDevice(ctx->device);
+    // GatedMlp::new_mixed (src/model/mlp.rs:60-81).
+    if (g->rows != u->rows || g->cols != u->cols || d->cols != g->rows || d->rows != g->cols)
+        return set_error(ctx, URB_ERR_SHAPE, "gated MLP projections have inconsistent shapes");
+    if (!g->tiled || !u->tiled || !d->tiled || g->format != u->format)
+        return set_error(ctx, URB_ERR_UNSUPPORTED, "gated MLP needs tiled gate/up of one format");
+    if (tokens == 0) return URB_OK;
+    for (size_t i = 0; i < tokens * g->cols; ++i)
+        if (!std::isfinite(x[i])) return set_error(ctx, URB_ERR_NONFINITE, "gated MLP input is not finite");
+    cudaStream_t st = ctx->stream;
+    float *d_io = nullptr;
+    const size_t H = g->cols;
+    URB_CUDA(ctx, cudaMallocAsync(&d_io, 2 * tokens * H * 4, st));
+    URB_CUDA(ctx, cudaMemcpyAsync(d_io, x, tokens * H * 4, cudaMemcpyDefault, st));
+    int rc = gated_mlp_device(ctx, g, u, d, d_io, int(tokens), d_io + tokens * H, nullptr, st);
+    if (rc == URB_OK)
+        URB_CUDA(ctx, cudaMemcpyAsync(out, d_io + tokens * H, tokens * H * 4, cudaMemcpyDefault, st));
+    cudaFreeAsync(d_io, st);
+    URB_CUDA(ctx, cudaStreamSynchronize(st));
+    return rc;
+}
+
+int urb_gated_mlp_forward_device(urb_ctx *ctx, const urb_mat *g, const urb_mat *u,
+                                 const urb_mat *d, const float *d_x, size_t tokens, float *d_out,
+                                 int32_t *d_status) {
+    if (!ctx || !g || !u || !d || !d_x || !d_out) return URB_ERR_INVALID_ARGUMENT;
+    std::lock_guard<std::recursive_mutex> lk(ctx->mu);
+    cudaSetDevice(ctx->device);
+    if (g->rows != u->rows || g->cols != u->cols || d->cols != g->rows || d->rows != g->cols)
+        return set_error(ctx, URB_ERR_SHAPE, "gated MLP projections have inconsistent shapes");
+    if (!g->tiled || !u->tiled || !d->tiled || g->format != u->format)
+        return set_error(ctx, URB_ERR_UNSUPPORTED, "gated MLP needs tiled gate/up of one format");
+    if (tokens == 0) return URB_OK;
+    return gated_mlp_device(ctx, g, u, d, d_x, int(tokens), d_out, d_status, ctx->stream);
+}
+
+}  // extern "C"

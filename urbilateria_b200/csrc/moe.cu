@@ -1,0 +1,212 @@
+// moe.cu — the MoE layer on one GPU: grouping (permutation/histogram), the two grouped expert
+// passes, and the weighted combine.
+//
+// Reference composition (src/models/glm/runtime/moe.rs:138-176): router logits -> route_noaux_tc
+// -> shared GatedMlp -> every routed GatedMlp in selection order -> f64 combine.  Here the
+// routed experts run grouped: routes are sorted experts-ascending / tokens-ascending
+// (src/models/qwen3_6/runtime.rs:1123-1132), each expert's token run is one or more segments of
+// a grouped pass, and the combine adds the route-weighted expert outputs per token in the
+// reference's selection order with f64 accumulation.
+#include "urb_internal.cuh"
+#include "urb_moe_internal.cuh"
+
+namespace urb {
+namespace {
+
+constexpr int kPermThreads = 1024;
+
+// Single-CTA grouping kernel.  See urb_moe_internal.cuh for the outputs.
+__global__ void __launch_bounds__(kPermThreads) k_permute(PermArgs p) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    const int E = p.experts, TK = p.tokens * p.top_k;
+    int *cnt = reinterpret_cast<int *>(smem);                 // [E]
+    int *off = cnt + E;                                        // [E+1]
+    int *running = off + E + 1;                                // [E]
+    uint16_t *wcnt = reinterpret_cast<uint16_t *>(running + E);  // [32][E]
+    __shared__ int warp_sums[32];
+    __shared__ int bad;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    if (tid == 0) bad = 0;
+    for (int e = tid; e < E; e += kPermThreads) { cnt[e] = 0; running[e] = 0; }
+    for (int i = tid; i < 32 * E; i += kPermThreads) wcnt[i] = 0;
+    __syncthreads();
+    for (int i = tid; i < TK; i += kPermThreads) {
+        int e = p.ids[i];
+        if (e < 0 || e >= E) bad = 1; else atomicAdd(&cnt[e], 1);
+    }
+    __syncthreads();
+    if (bad) {
+        if (tid == 0 && p.status) atomicCAS(p.status, 0, int32_t(URB_ERR_SHAPE));
+        if (tid == 0 && p.nsegs_gu) { *p.nsegs_gu = 0; *p.total_rows_gu = 0; *p.nsegs_dn = 0; *p.total_rows_dn = 0; }
+        return;
+    }
+    // Exclusive scan of counts (E <= 32 * 1024).
+    {
+        int per = (E + kPermThreads - 1) / kPermThreads;
+        int b = tid * per, s = 0;
+        for (int e = b; e < min(E, b + per); ++e) s += cnt[e];
+        int incl = s;
+        for (int o = 1; o < 32; o <<= 1) {
+            int v = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += v;
+        }
+        if (lane == 31) warp_sums[warp] = incl;
+        __syncthreads();
+        if (warp == 0) {
+            int v = warp_sums[lane];
+            for (int o = 1; o < 32; o <<= 1) {
+                int u = __shfl_up_sync(0xffffffffu, v, o);
+                if (lane >= o) v += u;
+            }
+            warp_sums[lane] = v;
+        }
+        __syncthreads();
+        int base = incl - s + (warp ? warp_sums[warp - 1] : 0);
+        for (int e = b; e < min(E, b + per); ++e) { off[e] = base; base += cnt[e]; }
+        if (tid == 0) off[E] = TK;
+        __syncthreads();
+    }
+    // Stable placement, token-major route order -> (expert asc, token asc).
+    for (int base = 0; base < TK; base += kPermThreads) {
+        const int i = base + tid;
+        const int e = i < TK ? p.ids[i] : -1;
+        const unsigned peers = __match_any_sync(0xffffffffu, e);
+        const int rank_w = __popc(peers & ((1u << lane) - 1));
+        if (e >= 0 && rank_w == 0) wcnt[warp * E + e] = uint16_t(__popc(peers));
+        __syncthreads();
+        if (e >= 0) {
+            int before = 0;
+            for (int w = 0; w < warp; ++w) before += wcnt[w * E + e];
+            const int pos = off[e] + running[e] + before + rank_w;
+            p.perm_token[pos] = i / p.top_k;
+            p.perm_slot[pos] = i % p.top_k;
+            p.inv[i] = pos;
+        }
+        __syncthreads();
+        for (int x = tid; x < E; x += kPermThreads) {
+            int s = 0;
+            for (int w = 0; w < 32; ++w) { s += wcnt[w * E + x]; wcnt[w * E + x] = 0; }
+            running[x] += s;
+        }
+        __syncthreads();
+    }
+    // Segments: routed experts ascending, each cut into chunks of `cap` tokens, then the
+    // shared expert's chunks.  (Skipped when only the grouping itself is requested.)
+    const int cap = p.cap;
+    if (p.segs_gu) {
+        int per = (E + kPermThreads - 1) / kPermThreads;
+        int b = tid * per, s = 0;
+        for (int e = b; e < min(E, b + per); ++e) s += (cnt[e] + cap - 1) / cap;
+        int incl = s;
+        for (int o = 1; o < 32; o <<= 1) {
+            int v = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += v;
+        }
+        __syncthreads();
+        if (lane == 31) warp_sums[warp] = incl;
+        __syncthreads();
+        if (warp == 0) {
+            int v = warp_sums[lane];
+            for (int o = 1; o < 32; o <<= 1) {
+                int u = __shfl_up_sync(0xffffffffu, v, o);
+                if (lane >= o) v += u;
+            }
+            warp_sums[lane] = v;
+        }
+        __syncthreads();
+        int sidx = incl - s + (warp ? warp_sums[warp - 1] : 0);
+        for (int e = b; e < min(E, b + per); ++e) {
+            for (int j = 0; j * cap < cnt[e]; ++j, ++sidx) {
+                Seg gu, dn;
+                gu.tiles_a = p.gate_tiles[e]; gu.rexp_a = p.gate_rexp[e];
+                gu.tiles_b = p.up_tiles[e]; gu.rexp_b = p.up_rexp[e];
+                gu.rbs = p.gu_rbs; gu.rows = p.inter; gu.kslices = p.gu_kslices; gu.cols = p.hidden;
+                gu.col_begin = off[e] + j * cap; gu.ntok = min(cap, cnt[e] - j * cap);
+                gu.row_begin = sidx * 16 * p.gu_rbs; gu.pad = e;
+                dn.tiles_a = p.down_tiles[e]; dn.rexp_a = p.down_rexp[e];
+                dn.tiles_b = nullptr; dn.rexp_b = nullptr;
+                dn.rbs = p.dn_rbs; dn.rows = p.hidden; dn.kslices = p.dn_kslices; dn.cols = p.inter;
+                dn.col_begin = gu.col_begin; dn.ntok = gu.ntok;
+                dn.row_begin = sidx * 16 * p.dn_rbs; dn.pad = e;
+                p.segs_gu[sidx] = gu;
+                p.segs_dn[sidx] = dn;
+            }
+        }
+        __syncthreads();
+        if (tid == kPermThreads - 1) {
+            int routed = sidx;  // thread owning the last experts ends at the total
+            int nseg = routed;
+            if (p.shared_in_pass) {
+                for (int j = 0; j * cap < p.tokens; ++j, ++nseg) {
+                    Seg gu, dn;
+                    gu.tiles_a = p.sh_gate_tiles; gu.rexp_a = p.sh_gate_rexp;
+                    gu.tiles_b = p.sh_up_tiles; gu.rexp_b = p.sh_up_rexp;
+                    gu.rbs = p.gu_rbs; gu.rows = p.inter; gu.kslices = p.gu_kslices; gu.cols = p.hidden;
+                    gu.col_begin = TK + j * cap; gu.ntok = min(cap, p.tokens - j * cap);
+                    gu.row_begin = nseg * 16 * p.gu_rbs; gu.pad = -1;
+                    dn.tiles_a = p.sh_down_tiles; dn.rexp_a = p.sh_down_rexp;
+                    dn.tiles_b = nullptr; dn.rexp_b = nullptr;
+                    dn.rbs = p.dn_rbs; dn.rows = p.hidden; dn.kslices = p.dn_kslices; dn.cols = p.inter;
+                    dn.col_begin = gu.col_begin; dn.ntok = gu.ntok;
+                    dn.row_begin = nseg * 16 * p.dn_rbs; dn.pad = -1;
+                    p.segs_gu[nseg] = gu;
+                    p.segs_dn[nseg] = dn;
+                }
+            }
+            *p.nsegs_gu = nseg;
+            *p.nsegs_dn = nseg;
+            *p.total_rows_gu = nseg * 16 * p.gu_rbs;
+            *p.total_rows_dn = nseg * 16 * p.dn_rbs;
+        }
+    }
+    // Activation-column sources of the gate/up pass and SwiGLU max-exponent reset.
+    if (p.col_src)
+        for (int c = tid; c < TK + p.tokens; c += kPermThreads) {
+            p.col_src[c] = c < TK ? p.perm_token[c] : c - TK;
+            p.maxexp[c] = -1000;
+        }
+    for (int e = tid; e < E; e += kPermThreads) {
+        if (p.counts) p.counts[e] = cnt[e];
+        if (p.offsets) p.offsets[e] = off[e];
+    }
+    if (tid == 0 && p.offsets) p.offsets[E] = TK;
+}
+
+// out[t][h] = f32( f64(shared) + sum_k f64(w[t][k]) * f64(y[inv[t,k]][h]) ), k in selection
+// order (glm/runtime/moe.rs:165-175).
+__global__ void k_combine(const float *y, const float *shared_y, const float *w,
+                          const int32_t *inv, int tokens, int top_k, int hidden, float *out) {
+    const int t = blockIdx.y;
+    const int h = blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= tokens || h >= hidden) return;
+    double acc = shared_y ? double(shared_y[size_t(t) * hidden + h]) : 0.0;
+    for (int k = 0; k < top_k; ++k) {
+        const int pos = inv[t * top_k + k];
+        acc += double(w[t * top_k + k]) * double(y[size_t(pos) * hidden + h]);
+    }
+    out[size_t(t) * hidden + h] = float(acc);
+}
+
+}  // namespace
+
+int launch_permute(Ctx *ctx, const PermArgs &p, cudaStream_t st) {
+    size_t smem = size_t(p.experts) * 4 * 3 + 4 + size_t(32) * p.experts * 2;
+    smem = (smem + 15) & ~size_t(15);
+    if (smem > 200 * 1024) return set_error(ctx, URB_ERR_UNSUPPORTED, "too many experts for the grouping kernel");
+    URB_CUDA(ctx, cudaFuncSetAttribute(k_permute, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
+    k_permute<<<1, kPermThreads, smem, st>>>(p);
+    URB_CUDA(ctx, cudaGetLastError());
+    return URB_OK;
+}
+
+int launch_combine(Ctx *ctx, const float *y, const float *shared_y, const float *w,
+                   const int32_t *inv, int tokens, int top_k, int hidden, float *out,
+                   cudaStream_t st) {
+    if (tokens <= 0) return URB_OK;
+    dim3 grid(unsigned((hidden + 255) / 256), unsigned(tokens));
+    k_combine<<<grid, 256, 0, st>>>(y, shared_y, w, inv, tokens, top_k, hidden, out);
+    URB_CUDA(ctx, cudaGetLastError());
+    return URB_OK;
+}
+
+}  // namespace urb

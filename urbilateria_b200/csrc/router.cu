@@ -1,0 +1,275 @@
+// router.cu — bit-exact expert routing.
+//
+//  * Router logits: the reference evaluates each logit as a sequential F64 sum, in column
+//    order, of exact f64 products bf16(w) * x, starting from -0.0, rounded once to f32
+//    (src/model/bf16.rs:494-525 via glm/runtime/moe.rs:154).  A product of a bf16 and an f32
+//    is exact in f64, so fma(w, x, acc) equals the reference's multiply-then-add; one thread
+//    owns one (token, expert) chain and performs exactly the reference's additions, so the
+//    logits are bit-identical.
+//  * route_noaux_tc (src/math/routing.rs:38-155) and route_softmax_top_k
+//    (src/models/qwen3_8/moe.rs:91-159): one warp per token, IEEE f32 arithmetic in the
+//    reference's order, libm-exact expf, total_cmp ranking with the lower id winning ties.
+#include "expf_glibc.cuh"
+#include "urb_internal.cuh"
+
+namespace urb {
+namespace {
+
+constexpr int kRouterKc = 128;  // columns staged per step
+
+template <bool BF16>
+__global__ void __launch_bounds__(256) k_router_logits(const void *w, int experts, int cols,
+                                                       const float *x, int tokens,
+                                                       float *logits) {
+    __shared__ double ws[32][kRouterKc + 1];
+    __shared__ double xs[8][kRouterKc];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int e0 = blockIdx.x * 32, t0 = blockIdx.y * 8;
+    const int e = e0 + lane, t = t0 + warp;
+    double acc = -0.0;
+    for (int c0 = 0; c0 < cols; c0 += kRouterKc) {
+        const int kc = min(kRouterKc, cols - c0);
+        __syncthreads();
+        for (int i = threadIdx.x; i < 32 * kRouterKc; i += 256) {
+            int r = i / kRouterKc, c = i % kRouterKc;
+            double v = 0.0;
+            if (e0 + r < experts && c < kc) {
+                size_t idx = size_t(e0 + r) * cols + c0 + c;
+                v = BF16 ? double(__uint_as_float(uint32_t(static_cast<const uint16_t *>(w)[idx]) << 16))
+                         : double(static_cast<const float *>(w)[idx]);
+            }
+            ws[r][c] = v;
+        }
+        for (int i = threadIdx.x; i < 8 * kRouterKc; i += 256) {
+            int r = i / kRouterKc, c = i % kRouterKc;
+            xs[r][c] = (t0 + r < tokens && c < kc) ? double(x[size_t(t0 + r) * cols + c0 + c]) : 0.0;
+        }
+        __syncthreads();
+        // Exactly the reference's additions: columns c0 .. c0+kc-1 in order.
+        for (int c = 0; c < kc; ++c) acc = fma(ws[lane][c], xs[warp][c], acc);
+    }
+    if (e < experts && t < tokens) logits[size_t(t) * experts + e] = float(acc);
+}
+
+__device__ __forceinline__ bool better(int32_t ka, int ia, int32_t kb, int ib) {
+    return ka > kb || (ka == kb && ia < ib);
+}
+
+// Warp argmax over (key desc, id asc).
+__device__ __forceinline__ void warp_best(int32_t &key, int &id) {
+    for (int o = 16; o > 0; o >>= 1) {
+        int32_t k2 = __shfl_xor_sync(0xffffffffu, key, o);
+        int i2 = __shfl_xor_sync(0xffffffffu, id, o);
+        if (better(k2, i2, key, id)) { key = k2; id = i2; }
+    }
+}
+
+__device__ __forceinline__ void set_status(int32_t *status, int code) {
+    if (status) atomicCAS(status, 0, int32_t(code));
+}
+
+// One warp per token.  Shared memory per warp (warp_bytes): gate[E], sel[E], group score
+// [n_group] floats, then one flag byte per expert (1 allowed, 2 taken, 0 masked).
+__global__ void k_route_noaux(const float *logits, const float *bias, int tokens, int E,
+                              int top_k, int n_group, int topk_group, int normalize,
+                              float scaling, ExpfTable tab, int32_t *out_e, float *out_w,
+                              float *out_s, int32_t *status, int warp_bytes) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int t = blockIdx.x * (blockDim.x >> 5) + warp;
+    if (t >= tokens) return;
+    float *gate = reinterpret_cast<float *>(smem + size_t(warp) * warp_bytes);
+    float *sel = gate + E;
+    float *gscore = sel + E;
+    uint8_t *flags = reinterpret_cast<uint8_t *>(gscore + n_group);
+    const float *lg = logits + size_t(t) * E;
+    bool bad = false;
+    for (int i = lane; i < E; i += 32) {
+        float l = lg[i], b = bias[i];
+        bad |= !isfinite(l) || !isfinite(b);
+        float ex = expf_libm(-l, tab);  // routing.rs:103: 1 / (1 + exp(-logit))
+        float gv = __fdiv_rn(1.0f, __fadd_rn(1.0f, ex));
+        gate[i] = gv;
+        sel[i] = __fadd_rn(gv, b);
+        flags[i] = 1;
+    }
+    if (__any_sync(0xffffffffu, bad)) {
+        if (lane == 0) set_status(status, URB_ERR_NONFINITE);
+        return;
+    }
+    __syncwarp();
+    if (n_group > 1) {
+        // routing.rs:112-129: group score = sum of the two largest selections (total order).
+        const int gs = E / n_group;
+        for (int grp = lane; grp < n_group; grp += 32) {
+            int32_t k1 = INT32_MIN, k2 = INT32_MIN;
+            float v1 = 0.0f, v2 = 0.0f;
+            for (int i = grp * gs; i < (grp + 1) * gs; ++i) {
+                int32_t k = total_key(sel[i]);
+                if (k > k1) { k2 = k1; v2 = v1; k1 = k; v1 = sel[i]; }
+                else if (k > k2) { k2 = k; v2 = sel[i]; }
+            }
+            gscore[grp] = __fadd_rn(v1, v2);
+        }
+        __syncwarp();
+        // Groups ranked by score desc, lower group id first; the best topk_group stay allowed.
+        for (int grp = lane; grp < n_group; grp += 32) {
+            const int32_t kg = total_key(gscore[grp]);
+            int rank = 0;
+            for (int o = 0; o < n_group; ++o)
+                if (better(total_key(gscore[o]), o, kg, grp)) ++rank;
+            const uint8_t allowed = rank < topk_group ? 1 : 0;
+            for (int i = grp * gs; i < (grp + 1) * gs; ++i) flags[i] = allowed;
+        }
+        __syncwarp();
+    }
+    // routing.rs:131-141: top_k by selection desc, lower id wins ties.
+    float den = -0.0f;
+    int32_t chosen_e[64];
+    for (int r = 0; r < top_k; ++r) {
+        int32_t key = INT32_MIN;
+        int id = INT32_MAX;
+        for (int i = lane; i < E; i += 32) {
+            if (flags[i] == 1) {
+                int32_t k = total_key(sel[i]);
+                if (better(k, i, key, id)) { key = k; id = i; }
+            }
+        }
+        warp_best(key, id);
+        if (id == INT32_MAX) {  // fewer allowed experts than top_k
+            if (lane == 0) set_status(status, URB_ERR_INVALID_GEOMETRY);
+            return;
+        }
+        if (lane == (id & 31)) flags[id] = 2;
+        __syncwarp();
+        if (r < 64) chosen_e[r] = id;
+        if (lane == 0) den = __fadd_rn(den, gate[id]);
+    }
+    if (lane == 0) {
+        den = __fadd_rn(den, 1e-20f);  // routing.rs:143-146
+        if (normalize && !isfinite(den)) {
+            set_status(status, URB_ERR_NONFINITE);
+            return;
+        }
+        for (int r = 0; r < top_k; ++r) {
+            int id = chosen_e[r];
+            float w = normalize ? __fdiv_rn(gate[id], den) : gate[id];
+            out_e[size_t(t) * top_k + r] = id;
+            out_w[size_t(t) * top_k + r] = __fmul_rn(w, scaling);
+            if (out_s) out_s[size_t(t) * top_k + r] = sel[id];
+        }
+    }
+}
+
+// route_softmax_top_k (src/models/qwen3_8/moe.rs:108-158).  One warp per token.
+__global__ void k_route_softmax(const float *logits, int tokens, int E, int top_k,
+                                ExpfTable tab, int32_t *out_e, float *out_w, int32_t *status) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int t = blockIdx.x * (blockDim.x >> 5) + warp;
+    if (t >= tokens) return;
+    float *p = reinterpret_cast<float *>(smem) + size_t(warp) * E;
+    uint8_t *taken = smem + size_t(blockDim.x >> 5) * E * 4 + size_t(warp) * E;
+    const float *lg = logits + size_t(t) * E;
+    float mx = -INFINITY;
+    bool bad = false;
+    for (int i = lane; i < E; i += 32) {
+        float l = lg[i];
+        bad |= !isfinite(l);
+        mx = fmaxf(mx, l);
+        taken[i] = 0;
+    }
+    if (__any_sync(0xffffffffu, bad)) {
+        if (lane == 0) set_status(status, URB_ERR_NONFINITE);
+        return;
+    }
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    for (int i = lane; i < E; i += 32) p[i] = expf_libm(__fsub_rn(lg[i], mx), tab);
+    __syncwarp();
+    float den = 0.0f;
+    if (lane == 0)
+        for (int i = 0; i < E; ++i) den = __fadd_rn(den, p[i]);
+    den = __shfl_sync(0xffffffffu, den, 0);
+    if (!isfinite(den) || den <= 0.0f) {
+        if (lane == 0) set_status(status, URB_ERR_NONFINITE);
+        return;
+    }
+    for (int i = lane; i < E; i += 32) p[i] = __fdiv_rn(p[i], den);
+    __syncwarp();
+    int32_t chosen[64];
+    float selected = 0.0f;
+    for (int r = 0; r < top_k; ++r) {
+        int32_t key = INT32_MIN;
+        int id = INT32_MAX;
+        for (int i = lane; i < E; i += 32)
+            if (!taken[i]) {
+                int32_t k = total_key(p[i]);
+                if (better(k, i, key, id)) { key = k; id = i; }
+            }
+        warp_best(key, id);
+        if (lane == (id & 31)) taken[id] = 1;
+        __syncwarp();
+        if (r < 64) chosen[r] = id;
+        if (lane == 0) selected = __fadd_rn(selected, p[id]);
+    }
+    if (lane == 0) {
+        if (!isfinite(selected) || selected <= 0.0f) {
+            set_status(status, URB_ERR_NONFINITE);
+            return;
+        }
+        for (int r = 0; r < top_k; ++r) {
+            float w = __fdiv_rn(p[chosen[r]], selected);
+            if (!isfinite(w)) set_status(status, URB_ERR_NONFINITE);
+            out_e[size_t(t) * top_k + r] = chosen[r];
+            out_w[size_t(t) * top_k + r] = w;
+        }
+    }
+}
+
+ExpfTable table_of(const Ctx *ctx) { return ExpfTable{ctx->expf_keys, ctx->expf_vals, ctx->expf_index}; }
+
+}  // namespace
+
+int launch_router_logits(const Mat *router, const float *d_x, int tokens, float *d_logits,
+                         cudaStream_t st) {
+    if (tokens <= 0) return URB_OK;
+    dim3 grid(unsigned((router->rows + 31) / 32), unsigned((tokens + 7) / 8));
+    if (router->format == URB_FMT_BF16)
+        k_router_logits<true><<<grid, 256, 0, st>>>(router->raw_values, int(router->rows),
+                                                    int(router->cols), d_x, tokens, d_logits);
+    else if (router->format == URB_FMT_F32)
+        k_router_logits<false><<<grid, 256, 0, st>>>(router->raw_values, int(router->rows),
+                                                     int(router->cols), d_x, tokens, d_logits);
+    else
+        return URB_ERR_UNSUPPORTED;
+    return cudaGetLastError() == cudaSuccess ? URB_OK : URB_ERR_CUDA;
+}
+
+int launch_route_noaux(Ctx *ctx, const float *d_logits, const float *d_bias, int tokens,
+                       int experts, const urb_moe_geometry &g, int32_t *d_expert,
+                       float *d_weight, float *d_score, int32_t *d_status, cudaStream_t st) {
+    if (tokens <= 0) return URB_OK;
+    int warps = 4;
+    int warp_bytes = int(((2 * size_t(experts) + g.n_group) * 4 + experts + 15) & ~size_t(15));
+    size_t smem = size_t(warps) * warp_bytes;
+    k_route_noaux<<<(tokens + warps - 1) / warps, warps * 32, smem, st>>>(
+        d_logits, d_bias, tokens, experts, int(g.top_k), int(g.n_group), int(g.topk_group),
+        g.normalize, g.routed_scaling_factor, table_of(ctx), d_expert, d_weight, d_score,
+        d_status, warp_bytes);
+    URB_CUDA(ctx, cudaGetLastError());
+    return URB_OK;
+}
+
+int launch_route_softmax(Ctx *ctx, const float *d_logits, int tokens, int experts, int top_k,
+                         int32_t *d_expert, float *d_weight, int32_t *d_status,
+                         cudaStream_t st) {
+    if (tokens <= 0) return URB_OK;
+    int warps = 4;
+    size_t smem = size_t(warps) * experts * 5;
+    k_route_softmax<<<(tokens + warps - 1) / warps, warps * 32, smem, st>>>(
+        d_logits, tokens, experts, top_k, table_of(ctx), d_expert, d_weight, d_status);
+    URB_CUDA(ctx, cudaGetLastError());
+    return URB_OK;
+}
+
+}  // namespace urb

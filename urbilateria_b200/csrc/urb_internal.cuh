@@ -1,0 +1,177 @@
+// urb_internal.cuh — definitions shared by the CUDA translation units of liburb_moe.
+//
+// Device layout of a resident weight matrix ("tiled layout", built at upload):
+//   The matrix is cut into tiles of 16 rows x 128 columns (rows padded to 16, columns to 128
+//   with zero weights).  Tiles are stored row-block-major: tile(rb, s) at (rb*kslices + s).
+//   Inside a tile, the bytes are ordered for the mma.sync m16n8k16 A fragment: lane
+//   t = 4g + q owns one 32-column group (columns 128s + 32q .. +31) of two rows,
+//   16rb+g and 16rb+g+8, stored back to back (MXFP4: 16 B + 16 B, MXFP8: 32 B + 32 B,
+//   BF16: 64 B + 64 B).  MX tiles end with 64 B of E8M0 scales: lane t's two scale bytes
+//   (row g, row g+8) at 2t.  So one warp reads one tile as one contiguous block.
+//   A per-row exponent offset E0 (int8) makes every decoded weight exact in f16:
+//   w_f16 = e2m1|e4m3 * 2^(scale-127-E0), and the epilogue multiplies by 2^E0.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/urb_moe.h"
+
+namespace urb {
+
+constexpr int kWarpSize = 32;
+constexpr int kTileRows = 16;
+constexpr int kTileCols = 128;
+
+// Bytes of one tile's weight payload and the whole tile (payload + scales) per format.
+__host__ __device__ constexpr int tile_payload_bytes(int fmt) {
+    return fmt == URB_FMT_MXFP4 ? 1024 : fmt == URB_FMT_MXFP8 ? 2048 : 4096;
+}
+__host__ __device__ constexpr int tile_bytes(int fmt) {
+    return tile_payload_bytes(fmt) + ((fmt == URB_FMT_MXFP4 || fmt == URB_FMT_MXFP8) ? 64 : 0);
+}
+
+struct Ctx;
+
+// Device-resident matrix.
+struct Mat {
+    Ctx *ctx = nullptr;
+    int format = 0;
+    size_t rows = 0, cols = 0;
+    size_t group_size = 0, block_rows = 0, block_cols = 0;
+    size_t resident_bytes = 0;  // reference payload bytes (WeightMatrix::resident_bytes)
+    // Tiled fast path.
+    bool tiled = false;
+    int rbs = 0, kslices = 0;
+    uint8_t *tiles = nullptr;
+    int8_t *row_exp = nullptr;  // [rbs*16]
+    // Generic path: the reference layout on the device (used when !tiled).
+    void *raw_values = nullptr;
+    uint8_t *raw_scales = nullptr;
+};
+
+// One unit of grouped work: a matrix (or a gate/up pair) applied to a contiguous run of
+// columns of the activation list.
+struct Seg {
+    const uint8_t *tiles_a;
+    const int8_t *rexp_a;
+    const uint8_t *tiles_b;  // pair partner (up projection) or nullptr
+    const int8_t *rexp_b;
+    int rbs;        // row blocks of the (each) matrix
+    int rows;       // real rows (outputs written only below this)
+    int kslices;    // 128-column slices
+    int cols;       // real input columns
+    int col_begin;  // first activation column of this segment
+    int ntok;       // tokens in this segment
+    int row_begin;  // prefix of 16*rbs over preceding segments (work space coordinate)
+    int pad;
+};
+
+// Arguments of one grouped pass.
+struct GroupArgs {
+    const Seg *segs;
+    const int *nsegs;         // device scalar: number of segments
+    const int *total_rows;    // device scalar: sum of 16*rbs
+    const float *src;         // activation rows (f32), row stride src_stride
+    int src_stride;
+    const int32_t *col_src;   // activation column -> src row (nullptr: identity)
+    const int32_t *src_shift; // src row -> power-of-two shift that puts max|x| in [2^14, 2^15)
+    const int32_t *src_maxexp;// alternative to src_shift: src row -> ilogb(max|x|) or -1000
+    float *out;               // output rows, stride out_stride, indexed by activation column
+    int out_stride;
+    int32_t *out_maxexp;      // SwiGLU: per output row ilogb(max|h|) (atomicMax), or nullptr
+    int hilo;                 // 1: two f16/bf16 columns (hi, lo) per token
+};
+
+struct Ctx {
+    int device = 0;
+    int num_sms = 148;
+    cudaStream_t stream = nullptr;
+    bool own_stream = false;
+    std::recursive_mutex mu;
+    std::string last_error;
+    int last_status = 0;
+    // Grow-only device workspace.
+    void *ws = nullptr;
+    size_t ws_size = 0;
+    // Pinned host staging.
+    void *pinned = nullptr;
+    size_t pinned_size = 0;
+    int32_t *d_status = nullptr;  // device status word for host-pointer calls
+    // glibc-expf exception table (see expf_glibc.cuh).
+    const uint32_t *expf_keys = nullptr;
+    const uint32_t *expf_vals = nullptr;
+    const uint32_t *expf_index = nullptr;
+    int expf_count = 0;
+    // Optional per-launch profiler (urb_profile_*).
+    bool prof = false;
+    struct ProfRec { int kind; cudaEvent_t a, b; };
+    std::vector<ProfRec> prof_pending;
+    std::vector<cudaEvent_t> prof_free;
+    double prof_ms[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    long long prof_n[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    int prof_open = -1;
+    cudaEvent_t prof_open_ev = nullptr;
+};
+
+// Brackets one launch for the profiler (no-op when profiling is off).
+void prof_begin(Ctx *ctx, int kind, cudaStream_t st);
+void prof_end(Ctx *ctx, cudaStream_t st);
+
+int set_error(Ctx *ctx, int status, const std::string &msg);
+int cuda_fail(Ctx *ctx, cudaError_t err, const char *what);
+void *workspace(Ctx *ctx, size_t bytes, int *status);
+void *pinned_staging(Ctx *ctx, size_t bytes, int *status);
+
+#define URB_CUDA(ctx, expr)                                                  \
+    do {                                                                     \
+        cudaError_t _e = (expr);                                             \
+        if (_e != cudaSuccess) return ::urb::cuda_fail((ctx), _e, #expr);    \
+    } while (0)
+
+// ---- kernels exposed across translation units (host launchers) -------------------------
+
+// upload.cu
+int upload_matrix(Ctx *ctx, Mat *m, const void *values, const uint8_t *scales);
+// skinny.cu: grouped register-dequant tensor-core pass over segments on the device.
+// ksplit: warps cooperating on one 16-row block (1, 2 or 8); max_cols <= 16.
+int launch_grouped_ex(Ctx *ctx, int fmt, bool pair, int ksplit, const GroupArgs &args,
+                      int max_cols, int kslices_max, cudaStream_t stream);
+// generic.cu: fallback for matrices without the tiled layout (CUDA cores, fp32).
+int launch_generic_matmul(Ctx *ctx, const Mat *m, size_t start, size_t count, const float *d_x,
+                          size_t batch, float *d_y, cudaStream_t stream);
+// prep: per-row shift and non-finite check.
+int launch_row_shift(const float *d_src, int rows, int cols, int stride, int32_t *d_shift,
+                     int32_t *d_status, cudaStream_t stream);
+// router.cu
+int launch_router_logits(const Mat *router, const float *d_x, int tokens, float *d_logits,
+                         cudaStream_t stream);
+int launch_route_noaux(Ctx *ctx, const float *d_logits, const float *d_bias, int tokens,
+                       int experts, const urb_moe_geometry &g, int32_t *d_expert,
+                       float *d_weight, float *d_score, int32_t *d_status, cudaStream_t stream);
+int launch_route_softmax(Ctx *ctx, const float *d_logits, int tokens, int experts, int top_k,
+                         int32_t *d_expert, float *d_weight, int32_t *d_status,
+                         cudaStream_t stream);
+// expf_glibc.cu
+int expf_table_init(Ctx *ctx);
+
+// ---- device helpers ----------------------------------------------------------------------
+#if defined(__CUDACC__)
+// Rust f32::total_cmp as a signed-integer key (IEEE totalOrder on the bit pattern).
+__device__ __forceinline__ int32_t total_key(float v) {
+    int32_t b = __float_as_int(v);
+    return b ^ int32_t(uint32_t(b >> 31) >> 1);
+}
+#endif
+
+}  // namespace urb
+
+struct urb_ctx : urb::Ctx {};
+struct urb_mat : urb::Mat {};
+struct urb_layer;

@@ -1,0 +1,67 @@
+// urb_moe_internal.cuh — MoE-layer structures shared by moe.cu and api.cu.
+#pragma once
+#include "urb_internal.cuh"
+
+namespace urb {
+
+// Inputs/outputs of the single-CTA grouping kernel.
+struct PermArgs {
+    const int32_t *ids;  // [tokens, top_k] expert ids in selection order
+    int tokens, top_k, experts, cap;
+    int32_t *counts;      // [experts] or nullptr
+    int32_t *offsets;     // [experts+1] or nullptr
+    int32_t *perm_token;  // [tokens*top_k] grouped order: token of each route
+    int32_t *perm_slot;   // [tokens*top_k] grouped order: selection rank of each route
+    int32_t *inv;         // [tokens*top_k] (token, rank) -> grouped position
+    Seg *segs_gu, *segs_dn;
+    int *nsegs_gu, *total_rows_gu, *nsegs_dn, *total_rows_dn;
+    int32_t *col_src;     // [tokens*top_k + tokens] gate/up activation column -> x row
+    int32_t *maxexp;      // [tokens*top_k + tokens] reset to -1000
+    const uint8_t *const *gate_tiles, *const *up_tiles, *const *down_tiles;
+    const int8_t *const *gate_rexp, *const *up_rexp, *const *down_rexp;
+    const uint8_t *sh_gate_tiles, *sh_up_tiles, *sh_down_tiles;
+    const int8_t *sh_gate_rexp, *sh_up_rexp, *sh_down_rexp;
+    int shared_in_pass;
+    int hidden, inter, gu_rbs, gu_kslices, dn_rbs, dn_kslices;
+    int32_t *status;
+};
+
+int launch_permute(Ctx *ctx, const PermArgs &p, cudaStream_t st);
+int launch_combine(Ctx *ctx, const float *y, const float *shared_y, const float *w,
+                   const int32_t *inv, int tokens, int top_k, int hidden, float *out,
+                   cudaStream_t st);
+
+struct Layer {
+    Ctx *ctx = nullptr;
+    const Mat *router = nullptr;
+    float *d_bias = nullptr;
+    size_t experts = 0, hidden = 0, inter = 0;
+    int fmt = 0;
+    std::vector<const Mat *> gate, up, down;
+    const Mat *sg = nullptr, *su = nullptr, *sd = nullptr;
+    urb_moe_geometry geo{};
+    // Device pointer tables [experts] for gate/up/down tiles and row exponents.
+    void **d_tables = nullptr;
+};
+
+// Device workspace of one forward, carved from the context workspace.
+struct MoeWork {
+    int32_t *shift;       // [T]
+    float *logits;        // [T, E]
+    int32_t *ids;         // [T, K]
+    float *w, *score;     // [T, K]
+    int32_t *counts, *offsets, *perm_token, *perm_slot, *inv;
+    Seg *segs_gu, *segs_dn;
+    int *scalars;         // nsegs_gu, total_rows_gu, nsegs_dn, total_rows_dn
+    int32_t *col_src, *maxexp;
+    float *h;             // [TK+T, inter]
+    float *y;             // [TK+T, hidden]
+    int32_t *status;
+};
+
+int moe_forward_device(Layer *L, const float *d_x, int tokens, float *d_out, MoeWork *work_out,
+                       int32_t *d_status, cudaStream_t st);
+
+}  // namespace urb
+
+struct urb_layer : urb::Layer {};
