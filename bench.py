@@ -32,7 +32,8 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-HIDDEN, INTER, EXPERTS, TOP_K, TOKENS, SCALE = 7168, 2048, 256, 8, 128, 2.5
+HIDDEN, INTER, TOP_K, TOKENS, SCALE = 7168, 2048, 8, 128, 2.5
+EXPERTS = 256
 SEED = 20261201
 
 
@@ -45,52 +46,57 @@ def peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks/throttle reasons sampled during the timed region."""
+    """SM clock and throttle reasons sampled through NVML during the timed region (read-only)."""
 
-    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
-
-    def __init__(self, device: int):
-        self.device, self.rows, self.proc = device, [], None
+    def __init__(self, device: int, period_s: float = 0.05):
+        self.device, self.period, self.rows = device, period_s, []
+        self._stop = threading.Event()
 
     def __enter__(self):
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", str(self.device), "--query-gpu=" + self.Q,
-                 "--format=csv,noheader,nounits", "-lms", "100"],
-                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.t = threading.Thread(target=self._read, daemon=True)
+            import pynvml as nv
+            nv.nvmlInit()
+            self.nv = nv
+            self.h = nv.nvmlDeviceGetHandleByIndex(self.device)
+            self.max_mhz = nv.nvmlDeviceGetMaxClockInfo(self.h, nv.NVML_CLOCK_SM)
+            self.t = threading.Thread(target=self._run, daemon=True)
             self.t.start()
-        except (OSError, FileNotFoundError):
-            self.proc = None
+        except Exception as e:  # no NVML: report no samples
+            self.nv, self.err = None, str(e)
         return self
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.rows.append([c.strip() for c in line.split(",")])
+    def _run(self):
+        nv = self.nv
+        while not self._stop.is_set():
+            try:
+                mhz = nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM)
+                reasons = nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                self.rows.append((mhz, reasons))
+            except Exception:
+                pass
+            self._stop.wait(self.period)
 
     def __exit__(self, *a):
-        if self.proc:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
+        self._stop.set()
+        if self.nv:
+            self.t.join(timeout=2)
 
     def summary(self):
-        mhz = [float(r[1]) for r in self.rows if len(r) > 8 and r[1].replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in self.rows if len(r) > 8 and r[2].replace(".", "").isdigit()]
-        reasons = set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for r in self.rows:
-            if len(r) > 8:
-                for n, v in zip(names, r[5:9]):
-                    if v.lower() == "active":
-                        reasons.add(n)
-        return {"sm_mhz": statistics.median(mhz) if mhz else None,
-                "sm_max_mhz": max(mx) if mx else None, "reasons": sorted(reasons),
-                "samples": len(self.rows)}
+        if not self.nv:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        nv = self.nv
+        names = {"hw_slowdown": getattr(nv, "nvmlClocksEventReasonHwSlowdown", 0x8),
+                 "hw_thermal_slowdown": getattr(nv, "nvmlClocksEventReasonHwThermalSlowdown", 0x40),
+                 "sw_thermal_slowdown": getattr(nv, "nvmlClocksEventReasonSwThermalSlowdown", 0x20),
+                 "sw_power_cap": getattr(nv, "nvmlClocksEventReasonSwPowerCap", 0x4)}
+        seen = set()
+        for _, r in self.rows:
+            for n, bit in names.items():
+                if r & bit:
+                    seen.add(n)
+        mhz = [m for m, _ in self.rows]
+        return {"sm_mhz": statistics.median(mhz) if mhz else None, "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(seen), "samples": len(mhz)}
 
 
 def make_weights(seed: int, experts: int, keep_host: bool):
@@ -168,6 +174,39 @@ def run_reference(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
+def bench_matvec(urb, ctx, stream, local, pk_hbm, copies=20, reps=5):
+    """Config 0 (MXFP4 matvec 4096x7168, E8M0 119..127, x ~ N(0,1)): 20 distinct weight copies
+    (312 MB > 2x L2) are used round-robin so every launch streams from HBM."""
+    import torch
+    from urbilateria_b200 import synthetic as syn
+    g = syn.rng(SEED + 7)
+    rows, cols = 4096, 7168
+    mats = [urb.MxFp4Matrix.from_packed(rows, cols, 32, *syn.mxfp4_matrix(g, rows, cols), ctx=ctx)
+            for _ in range(copies)]
+    x = torch.from_numpy(syn.normal_f32(g, cols)).to(f"cuda:{local}")
+    y = torch.empty(rows, device=f"cuda:{local}")
+    for m in mats[:3]:
+        m.matmul_rows_device(x.data_ptr(), 1, y.data_ptr())
+    stream.synchronize()
+    ctx.lib.urb_profile_reset(ctx.h)
+    ctx.lib.urb_profile_enable(ctx.h, 1)
+    for _ in range(reps):
+        for m in mats:
+            m.matmul_rows_device(x.data_ptr(), 1, y.data_ptr())
+    ctx.lib.urb_profile_enable(ctx.h, 0)
+    import ctypes
+    t, n = ctypes.c_double(), ctypes.c_int64()
+    ctx.lib.urb_profile_read(ctx.h, 7, ctypes.byref(t), ctypes.byref(n))
+    ms = t.value / max(1, n.value)
+    nbytes = rows * cols // 2 + rows * cols // 32 + cols * 4 + rows * 4
+    gbs = nbytes / (ms / 1e3) / 1e9
+    for m in mats:
+        m.free()
+    return {"kernel": "k_grouped<MXFP4> matvec", "us_per_launch": ms * 1e3,
+            "bytes_per_launch": nbytes, "achieved_gbs": gbs, "frac_of_measured_hbm": gbs / pk_hbm,
+            "launches": n.value, "l2": "20 distinct 15.6 MB weight copies round-robin"}
+
+
 def workload_config(world):
     return {"workload": "C2 MXFP4 MoE layer: hidden 7168, 256+1 experts, inter 2048, top-8 "
                         "noaux_tc x2.5, 128-token chunk per GPU",
@@ -186,7 +225,13 @@ def main():
     ap.add_argument("--ref-step-s", type=float, default=4.0)
     ap.add_argument("--cpu-sample-s", type=float, default=12.0)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-matvec", action="store_true")
+    ap.add_argument("--experts", type=int, default=256,
+                    help="routed experts (256 = config 2; smaller only for profiling captures)")
     args = ap.parse_args()
+    global EXPERTS
+    EXPERTS = args.experts
 
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", str(args.gpus)))
@@ -271,6 +316,8 @@ def main():
         torch.cuda.synchronize()
         ms = min(ms, e0.elapsed_time(e1))
 
+    matvec = None if args.no_matvec else bench_matvec(urb, ctx, stream, local, pk_hbm)
+
     # End to end through the host-pointer ABI (pinned host input/output).
     hx = torch.from_numpy(x).pin_memory()
     hout = torch.empty_like(hx).pin_memory()
@@ -282,17 +329,19 @@ def main():
                                           hid.data_ptr(), hw.data_ptr(), None, None, None, None,
                                           None))
 
-    for _ in range(2):
-        e2e_step()
-    if dist:
-        dist.barrier()
-    torch.cuda.synchronize()
-    e0.record(stream)
-    for _ in range(args.steps):
-        e2e_step()
-    e1.record(stream)
-    torch.cuda.synchronize()
-    ms_e2e = e0.elapsed_time(e1)
+    ms_e2e = float("nan")
+    if not args.no_e2e:
+        for _ in range(2):
+            e2e_step()
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for _ in range(args.steps):
+            e2e_step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms_e2e = e0.elapsed_time(e1)
 
     if dist:
         t = torch.tensor([ms, ms_e2e], device=f"cuda:{local}")
@@ -329,7 +378,7 @@ def main():
             "roofline": roofline,
             "layer_hbm_gbs": layer_bytes / (ms / args.steps / 1e3) / 1e9,
             "down_gbs": dn_bytes / (dn.get("ms_per_launch", float("nan")) / 1e3) / 1e9,
-            "touched_experts": touched, "kernels": kern,
+            "touched_experts": touched, "kernels": kern, "matvec_c0": matvec,
             "gpu_launches": 7 * args.steps,
             "clocks": clk.summary()}
 

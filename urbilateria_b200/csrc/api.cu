@@ -362,6 +362,7 @@ int urb_mat_free(urb_mat *m) {
         cudaStreamSynchronize(m->ctx->stream);
     }
     if (m->tiles) cudaFree(m->tiles);
+    if (m->tc_tiles) cudaFree(m->tc_tiles);
     if (m->row_exp) cudaFree(m->row_exp);
     if (m->raw_values) cudaFree(m->raw_values);
     if (m->raw_scales) cudaFree(m->raw_scales);
@@ -498,7 +499,6 @@ static int check_noaux_geometry(urb_ctx *ctx, size_t experts, const urb_moe_geom
     if (g->top_k == 0 || g->top_k > experts) return set_error(ctx, URB_ERR_INVALID_GEOMETRY, "top_k outside 1..=experts");
     if (g->topk_group == 0 || g->topk_group > g->n_group) return set_error(ctx, URB_ERR_INVALID_GEOMETRY, "topk_group outside 1..=n_group");
     if (experts / g->n_group < 2) return set_error(ctx, URB_ERR_INVALID_GEOMETRY, "noaux_tc needs two experts per group");
-    if (g->top_k > 64) return set_error(ctx, URB_ERR_UNSUPPORTED, "top_k above 64");
     return URB_OK;
 }
 
@@ -549,7 +549,6 @@ int urb_route_softmax_top_k(urb_ctx *ctx, const float *logits, size_t tokens, si
     // qwen3_8/moe.rs:95-106.
     if (experts == 0 || top_k == 0 || top_k > experts)
         return set_error(ctx, URB_ERR_INVALID_GEOMETRY, "top_k outside 1..=experts");
-    if (top_k > 64) return set_error(ctx, URB_ERR_UNSUPPORTED, "top_k above 64");
     if (!all_finite(logits, tokens * experts))
         return set_error(ctx, URB_ERR_NONFINITE, "router logits contain NaN/infinity");
     if (tokens == 0) return URB_OK;

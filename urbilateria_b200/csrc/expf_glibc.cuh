@@ -4,8 +4,9 @@
 // (src/models/qwen3_8/moe.rs:113) call Rust's f32::exp, i.e. libm `expf`.  The device computes
 // (float)exp((double)x), a single rounding of a double exponential, and overrides it with the
 // libm result for the inputs recorded by the build step gen_expf_table.c (where libm is not
-// correctly rounded, or where e^x sits within 2^-48 of a float midpoint).  Lookup: a 65537-entry
-// index over the top 16 bits of the input, then a short scan of the sorted keys.
+// correctly rounded, or where e^x sits within 2^-48 of a float midpoint).  Lookup: a
+// (2^20+1)-entry index over the top 20 bits of the input (0.16 keys per bucket on average),
+// then a short scan of the sorted keys.
 #pragma once
 #include <stdint.h>
 
@@ -20,7 +21,7 @@ struct ExpfTable {
 __device__ __forceinline__ float expf_libm(float x, const ExpfTable &t) {
     uint32_t k = __float_as_uint(x);
     if (t.index) {
-        uint32_t b = k >> 16;
+        uint32_t b = k >> 12;
         for (uint32_t i = t.index[b], e = t.index[b + 1]; i < e; ++i)
             if (t.keys[i] == k) return __uint_as_float(t.vals[i]);
     }

@@ -66,9 +66,10 @@ __global__ void k_generic(RawMat m, size_t start, size_t count, const float *x, 
     if (lane == 0) y[t * count + i] = float(acc);
 }
 
-// One block per row: shift = 14 - ilogb(max|v|) (0 for an all-zero row); flags non-finite.
+// One block per row: shift = 14 - ilogb(max|v|) (0 for an all-zero row); flags non-finite;
+// with lofree, checks that every shifted value is exact in one f16 (or bf16) column.
 __global__ void k_row_shift(const float *src, int cols, int stride, int32_t *shift,
-                            int32_t *status) {
+                            int32_t *status, int32_t *lofree, int bf16_check) {
     const float *p = src + size_t(blockIdx.x) * stride;
     float m = 0.0f;
     bool bad = false;
@@ -78,8 +79,8 @@ __global__ void k_row_shift(const float *src, int cols, int stride, int32_t *shi
         m = fmaxf(m, fabsf(v));
     }
     __shared__ float red[32];
-    __shared__ int badf;
-    if (threadIdx.x == 0) badf = 0;
+    __shared__ int badf, sh, inexact;
+    if (threadIdx.x == 0) { badf = 0; inexact = 0; }
     for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
     __syncthreads();
     if (bad) badf = 1;
@@ -88,9 +89,21 @@ __global__ void k_row_shift(const float *src, int cols, int stride, int32_t *shi
     if (threadIdx.x == 0) {
         float mm = 0.0f;
         for (int w = 0; w < int(blockDim.x >> 5); ++w) mm = fmaxf(mm, red[w]);
-        shift[blockIdx.x] = (mm > 0.0f && isfinite(mm)) ? 14 - ilogbf(mm) : 0;
+        sh = (mm > 0.0f && isfinite(mm)) ? 14 - ilogbf(mm) : 0;
+        shift[blockIdx.x] = sh;
         if (badf && status) atomicCAS(status, 0, int32_t(URB_ERR_NONFINITE));
     }
+    if (!lofree) return;
+    __syncthreads();
+    bool ok = true;
+    for (int c = threadIdx.x; c < cols; c += blockDim.x) {
+        float v = ldexpf(p[c], sh);
+        float r = bf16_check ? __bfloat162float(__float2bfloat16_rn(v)) : __half2float(__float2half_rn(v));
+        ok &= (r == v);
+    }
+    if (!ok) inexact = 1;
+    __syncthreads();
+    if (threadIdx.x == 0 && inexact) atomicAnd(lofree, 0);
 }
 
 }  // namespace
@@ -107,9 +120,9 @@ int launch_generic_matmul(Ctx *ctx, const Mat *mt, size_t start, size_t count, c
 }
 
 int launch_row_shift(const float *d_src, int rows, int cols, int stride, int32_t *d_shift,
-                     int32_t *d_status, cudaStream_t st) {
+                     int32_t *d_status, cudaStream_t st, int32_t *d_lofree, int bf16_check) {
     if (rows <= 0) return URB_OK;
-    k_row_shift<<<rows, 256, 0, st>>>(d_src, cols, stride, d_shift, d_status);
+    k_row_shift<<<rows, 256, 0, st>>>(d_src, cols, stride, d_shift, d_status, d_lofree, bf16_check);
     return cudaGetLastError() == cudaSuccess ? URB_OK : URB_ERR_CUDA;
 }
 

@@ -3,6 +3,7 @@
 //   row shifts -> exact router logits -> route_noaux_tc -> grouping -> grouped gate/up with
 //   fused SwiGLU -> grouped down -> weighted f64 combine.
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 
 #include "urb_internal.cuh"
@@ -30,6 +31,11 @@ constexpr int kCap = 4;  // tokens per segment: hi/lo halves fill one 8-column n
 size_t max_segments(size_t tokens, size_t K, size_t experts) {
     size_t TK = tokens * K;
     return std::min(TK, experts) + TK / kCap + div_ceil(tokens, kCap) + 2;
+}
+
+size_t max_tc_segments(size_t tokens, size_t K, size_t experts) {
+    size_t TK = tokens * K;
+    return std::min(TK, experts) + TK / kTcCapGu + div_ceil(tokens, kTcCapGu) + 2;
 }
 
 }  // namespace
@@ -64,10 +70,29 @@ int moe_forward_device(Layer *L, const float *d_x, int T, float *d_out, MoeWork 
     w.maxexp = cv.take<int32_t>(cols);
     w.h = cv.take<float>(cols * I);
     w.y = cv.take<float>(cols * H);
+    w.lofree = cv.take<int32_t>(1);
+    const size_t ntseg = max_tc_segments(T, K, E);
+    const size_t ks_gu = div_ceil(H, 64), ks_dn = div_ceil(I, 64);
+    const size_t npad_sum = 2 * cols + 16 * ntseg;
+    if (L->use_tc) {
+        w.tsegs_gu = cv.take<TcSeg>(ntseg);
+        w.tsegs_dn = cv.take<TcSeg>(ntseg);
+        w.tscalars = cv.take<int>(4);
+        w.bbuf_gu = cv.take<uint8_t>(ks_gu * 128 * npad_sum + 1024);
+        w.bbuf_dn = cv.take<uint8_t>(ks_dn * 128 * npad_sum + 1024);
+    }
+    if (cv.off > ctx->ws_size) {
+        // Grow to the exact size of this forward (nothing has been enqueued yet) and restart.
+        if (!workspace(ctx, cv.off, &rc)) return rc;
+        return moe_forward_device(L, d_x, T, d_out, wout, d_status, st);
+    }
     w.status = d_status;
+    const int one = 1;
+    URB_CUDA(ctx, cudaMemcpyAsync(w.lofree, &one, 4, cudaMemcpyHostToDevice, st));
 
     prof_begin(ctx, URB_K_ROW_SHIFT, st);
-    rc = launch_row_shift(d_x, T, int(H), int(H), w.shift, d_status, st);
+    rc = launch_row_shift(d_x, T, int(H), int(H), w.shift, d_status, st, w.lofree,
+                          L->fmt == URB_FMT_BF16 ? 1 : 0);
     prof_end(ctx, st);
     if (rc) return cuda_fail(ctx, cudaGetLastError(), "row shift");
     prof_begin(ctx, URB_K_ROUTER_LOGITS, st);
@@ -120,10 +145,87 @@ int moe_forward_device(Layer *L, const float *d_x, int T, float *d_out, MoeWork 
     p.dn_rbs = d0->rbs;
     p.dn_kslices = d0->kslices;
     p.status = d_status;
+    p.lofree = w.lofree;
     prof_begin(ctx, URB_K_PERMUTE, st);
     rc = launch_permute(ctx, p, st);
     prof_end(ctx, st);
     if (rc) return rc;
+
+    if (L->use_tc) {
+        TcBuildArgs bb{};
+        bb.counts = w.counts;
+        bb.offsets = w.offsets;
+        bb.lofree = w.lofree;
+        bb.tokens = T;
+        bb.top_k = int(K);
+        bb.experts = int(E);
+        bb.gate_tc = reinterpret_cast<const uint8_t *const *>(tb + 6 * E);
+        bb.up_tc = reinterpret_cast<const uint8_t *const *>(tb + 7 * E);
+        bb.down_tc = reinterpret_cast<const uint8_t *const *>(tb + 8 * E);
+        bb.gate_rexp = p.gate_rexp;
+        bb.up_rexp = p.up_rexp;
+        bb.down_rexp = p.down_rexp;
+        bb.has_shared = L->sg ? 1 : 0;
+        if (L->sg) {
+            bb.sh_gate_tc = L->sg->tc_tiles; bb.sh_gate_rexp = L->sg->row_exp;
+            bb.sh_up_tc = L->su->tc_tiles; bb.sh_up_rexp = L->su->row_exp;
+            bb.sh_down_tc = L->sd->tc_tiles; bb.sh_down_rexp = L->sd->row_exp;
+        }
+        bb.hidden = int(H);
+        bb.inter = int(I);
+        bb.gu = w.tsegs_gu;
+        bb.dn = w.tsegs_dn;
+        bb.scalars = w.tscalars;
+        bb.status = d_status;
+        rc = launch_build_tc_segs(ctx, bb, st);
+        if (rc) return rc;
+
+        TcArgs ga{};
+        ga.segs = w.tsegs_gu;
+        ga.nsegs = w.tscalars;
+        ga.total_units = w.tscalars + 1;
+        ga.nmax = 128;
+        ga.bbuf = w.bbuf_gu;
+        ga.src = d_x;
+        ga.src_stride = int(H);
+        ga.col_src = w.col_src;
+        ga.src_shift = w.shift;
+        ga.out = w.h;
+        ga.out_stride = int(I);
+        ga.out_maxexp = w.maxexp;
+        ga.status = d_status;
+        prof_begin(ctx, URB_K_GATE_UP, st);
+        rc = launch_tc_grouped(ctx, L->fmt, true, ga, int(ntseg), int(ks_gu), st);
+        prof_end(ctx, st);
+        if (rc) return rc;
+
+        TcArgs da{};
+        da.segs = w.tsegs_dn;
+        da.nsegs = w.tscalars + 2;
+        da.total_units = w.tscalars + 3;
+        da.nmax = 256;
+        da.bbuf = w.bbuf_dn;
+        da.src = w.h;
+        da.src_stride = int(I);
+        da.col_src = nullptr;
+        da.src_shift = nullptr;
+        da.src_maxexp = w.maxexp;
+        da.out = w.y;
+        da.out_stride = int(H);
+        da.status = d_status;
+        prof_begin(ctx, URB_K_DOWN, st);
+        rc = launch_tc_grouped(ctx, L->fmt, false, da, int(ntseg), int(ks_dn), st);
+        prof_end(ctx, st);
+        if (rc) return rc;
+
+        prof_begin(ctx, URB_K_COMBINE, st);
+        rc = launch_combine(ctx, w.y, L->sg ? w.y + TK * H : nullptr, w.w, w.inv, T, int(K),
+                            int(H), d_out, st, d_status);
+        prof_end(ctx, st);
+        if (rc) return rc;
+        if (wout) *wout = w;
+        return URB_OK;
+    }
 
     // Upper bound of work rows per SM picks how many warps share a row block.
     const long est_rows_gu = long(std::min(nseg, TK + div_ceil(T, kCap))) * 16 * g0->rbs;
@@ -142,6 +244,7 @@ int moe_forward_device(Layer *L, const float *d_x, int T, float *d_out, MoeWork 
     gu.out_stride = int(I);
     gu.out_maxexp = w.maxexp;
     gu.hilo = 1;
+    gu.lofree = w.lofree;  // bf16-exact tokens: 8 per segment in one f16 column each
     prof_begin(ctx, URB_K_GATE_UP, st);
     rc = launch_grouped_ex(ctx, L->fmt, true, ksplit, gu, 2 * kCap, g0->kslices, st);
     prof_end(ctx, st);
@@ -160,14 +263,14 @@ int moe_forward_device(Layer *L, const float *d_x, int T, float *d_out, MoeWork 
     dn.out_stride = int(H);
     dn.hilo = 1;
     prof_begin(ctx, URB_K_DOWN, st);
-    rc = launch_grouped_ex(ctx, L->fmt, false, ksplit == 8 ? 2 : ksplit, dn, 2 * kCap,
+    rc = launch_grouped_ex(ctx, L->fmt, false, ksplit == 8 ? 2 : ksplit, dn, 4 * kCap,
                            d0->kslices, st);
     prof_end(ctx, st);
     if (rc) return rc;
 
     prof_begin(ctx, URB_K_COMBINE, st);
     rc = launch_combine(ctx, w.y, L->sg ? w.y + TK * H : nullptr, w.w, w.inv, T, int(K), int(H),
-                        d_out, st);
+                        d_out, st, d_status);
     prof_end(ctx, st);
     if (rc) return rc;
     if (wout) *wout = w;
@@ -267,7 +370,6 @@ int urb_moe_layer_create(urb_ctx *ctx, const urb_mat *router, const float *bias,
         geo->topk_group > geo->n_group || experts / geo->n_group < 2 ||
         size_t(geo->topk_group) * (experts / geo->n_group) < geo->top_k)
         return set_error(ctx, URB_ERR_INVALID_GEOMETRY, "invalid noaux_tc geometry");
-    if (geo->top_k > 64) return set_error(ctx, URB_ERR_UNSUPPORTED, "top_k above 64");
     if (router->format != URB_FMT_BF16 && router->format != URB_FMT_F32)
         return set_error(ctx, URB_ERR_UNSUPPORTED, "router must be BF16 or F32 for exact logits");
     // GatedMlp::new_mixed shape contract (src/model/mlp.rs:60-81) for every expert, plus this
@@ -303,7 +405,7 @@ int urb_moe_layer_create(urb_ctx *ctx, const urb_mat *router, const float *bias,
     L->up.assign(up, up + experts);
     L->down.assign(down, down + experts);
     if (have_shared) { L->sg = sg; L->su = su; L->sd = sd; }
-    std::vector<void *> tables(6 * experts);
+    std::vector<void *> tables(9 * experts);
     for (size_t e = 0; e < experts; ++e) {
         tables[e] = gate[e]->tiles;
         tables[experts + e] = up[e]->tiles;
@@ -311,7 +413,13 @@ int urb_moe_layer_create(urb_ctx *ctx, const urb_mat *router, const float *bias,
         tables[3 * experts + e] = gate[e]->row_exp;
         tables[4 * experts + e] = up[e]->row_exp;
         tables[5 * experts + e] = down[e]->row_exp;
+        tables[6 * experts + e] = gate[e]->tc_tiles;
+        tables[7 * experts + e] = up[e]->tc_tiles;
+        tables[8 * experts + e] = down[e]->tc_tiles;
     }
+    const char *path = std::getenv("URB_MOE_PATH");
+    L->use_tc = (fmt == URB_FMT_MXFP4 || fmt == URB_FMT_MXFP8) &&
+                !(path && std::strcmp(path, "mma") == 0);
     cudaError_t err = cudaMalloc(&L->d_tables, tables.size() * sizeof(void *));
     if (err == cudaSuccess) err = cudaMalloc(&L->d_bias, experts * 4);
     if (err == cudaSuccess)

@@ -26,7 +26,7 @@ __global__ void __launch_bounds__(kPermThreads) k_permute(PermArgs p) {
     __shared__ int warp_sums[32];
     __shared__ int bad;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    if (tid == 0) bad = 0;
+    if (tid == 0) bad = (p.status && *p.status) ? 1 : 0;  // an earlier stage failed
     for (int e = tid; e < E; e += kPermThreads) { cnt[e] = 0; running[e] = 0; }
     for (int i = tid; i < 32 * E; i += kPermThreads) wcnt[i] = 0;
     __syncthreads();
@@ -36,8 +36,15 @@ __global__ void __launch_bounds__(kPermThreads) k_permute(PermArgs p) {
     }
     __syncthreads();
     if (bad) {
+        // Empty grouping: every later stage sees zero work.
         if (tid == 0 && p.status) atomicCAS(p.status, 0, int32_t(URB_ERR_SHAPE));
         if (tid == 0 && p.nsegs_gu) { *p.nsegs_gu = 0; *p.total_rows_gu = 0; *p.nsegs_dn = 0; *p.total_rows_dn = 0; }
+        for (int e = tid; e < E; e += kPermThreads) {
+            if (p.counts) p.counts[e] = 0;
+            if (p.offsets) p.offsets[e] = 0;
+        }
+        if (tid == 0 && p.offsets) p.offsets[E] = 0;
+        for (int i = tid; i < TK; i += kPermThreads) p.inv[i] = 0;
         return;
     }
     // Exclusive scan of counts (E <= 32 * 1024).
@@ -92,7 +99,7 @@ __global__ void __launch_bounds__(kPermThreads) k_permute(PermArgs p) {
     }
     // Segments: routed experts ascending, each cut into chunks of `cap` tokens, then the
     // shared expert's chunks.  (Skipped when only the grouping itself is requested.)
-    const int cap = p.cap;
+    const int cap = (p.lofree && *p.lofree) ? 2 * p.cap : p.cap;
     if (p.segs_gu) {
         int per = (E + kPermThreads - 1) / kPermThreads;
         int b = tid * per, s = 0;
@@ -175,7 +182,9 @@ __global__ void __launch_bounds__(kPermThreads) k_permute(PermArgs p) {
 // out[t][h] = f32( f64(shared) + sum_k f64(w[t][k]) * f64(y[inv[t,k]][h]) ), k in selection
 // order (glm/runtime/moe.rs:165-175).
 __global__ void k_combine(const float *y, const float *shared_y, const float *w,
-                          const int32_t *inv, int tokens, int top_k, int hidden, float *out) {
+                          const int32_t *inv, int tokens, int top_k, int hidden, float *out,
+                          const int32_t *status) {
+    if (status && *status) return;
     const int t = blockIdx.y;
     const int h = blockIdx.x * blockDim.x + threadIdx.x;
     if (t >= tokens || h >= hidden) return;
@@ -187,7 +196,125 @@ __global__ void k_combine(const float *y, const float *shared_y, const float *w,
     out[size_t(t) * hidden + h] = float(acc);
 }
 
+// Segments of the tensor-core passes (single CTA).  Routed experts ascending, each cut into
+// chunks (gate/up: 64 tokens, or 128 when every activation is exact in one f16 column;
+// down: 128 tokens with hi/lo columns), then the shared expert.  Activation-tile offsets are a
+// prefix over segments of ks * npad * 128 bytes.
+__device__ __forceinline__ int round16(int x) { return (x + 15) & ~15; }
+
+__global__ void __launch_bounds__(1024) k_build_tc_segs(TcBuildArgs b) {
+    __shared__ long long wsum[2][32];
+    __shared__ int wcnt[2][32];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    if (b.status && *b.status) {  // an earlier stage failed: no work for the passes
+        if (tid < 4) b.scalars[tid] = 0;
+        return;
+    }
+    const int E = b.experts, TK = b.tokens * b.top_k;
+    const bool lofree = b.lofree && *b.lofree;
+    const int cap[2] = {lofree ? 2 * kTcCapGu : kTcCapGu, kTcCapDn};
+    const int per[2] = {lofree ? 1 : 2, 2};
+    const int ksz[2] = {(b.hidden + 63) / 64, (b.inter + 63) / 64};
+    const int mts[2] = {(b.inter + 127) / 128, (b.hidden + 127) / 128};
+    for (int pass = 0; pass < 2; ++pass) {
+        // Per thread: experts [e0, e1); count segments and B bytes.
+        const int per_thr = (E + 1023) / 1024;
+        const int e0 = tid * per_thr, e1 = min(E, e0 + per_thr);
+        int nseg = 0;
+        long long bytes = 0;
+        for (int e = e0; e < e1; ++e)
+            for (int j = 0; j * cap[pass] < b.counts[e]; ++j) {
+                const int nt = min(cap[pass], b.counts[e] - j * cap[pass]);
+                ++nseg;
+                bytes += (long long)ksz[pass] * round16(nt * per[pass]) * 128;
+            }
+        // Block-wide exclusive scans of (nseg, bytes).
+        int iseg = nseg;
+        long long ib = bytes;
+        for (int o = 1; o < 32; o <<= 1) {
+            int v = __shfl_up_sync(0xffffffffu, iseg, o);
+            long long w = __shfl_up_sync(0xffffffffu, ib, o);
+            if (lane >= o) { iseg += v; ib += w; }
+        }
+        __syncthreads();
+        if (lane == 31) { wcnt[pass][warp] = iseg; wsum[pass][warp] = ib; }
+        __syncthreads();
+        if (warp == 0) {
+            int v = wcnt[pass][lane];
+            long long w = wsum[pass][lane];
+            for (int o = 1; o < 32; o <<= 1) {
+                int v2 = __shfl_up_sync(0xffffffffu, v, o);
+                long long w2 = __shfl_up_sync(0xffffffffu, w, o);
+                if (lane >= o) { v += v2; w += w2; }
+            }
+            wcnt[pass][lane] = v;
+            wsum[pass][lane] = w;
+        }
+        __syncthreads();
+        int sidx = iseg - nseg + (warp ? wcnt[pass][warp - 1] : 0);
+        long long boff = ib - bytes + (warp ? wsum[pass][warp - 1] : 0);
+        TcSeg *out = pass == 0 ? b.gu : b.dn;
+        for (int e = e0; e < e1; ++e) {
+            int col0 = b.offsets[e];
+            for (int j = 0; j * cap[pass] < b.counts[e]; ++j, ++sidx) {
+                TcSeg s;
+                const int nt = min(cap[pass], b.counts[e] - j * cap[pass]);
+                if (pass == 0) {
+                    s.a = b.gate_tc[e]; s.b = b.up_tc[e]; s.ra = b.gate_rexp[e]; s.rb = b.up_rexp[e];
+                    s.rows = b.inter; s.cols = b.hidden;
+                } else {
+                    s.a = b.down_tc[e]; s.b = nullptr; s.ra = b.down_rexp[e]; s.rb = nullptr;
+                    s.rows = b.hidden; s.cols = b.inter;
+                }
+                s.mts = mts[pass]; s.ks = ksz[pass];
+                s.col_begin = col0 + j * cap[pass]; s.ntok = nt;
+                s.rowsper = per[pass]; s.npad = round16(nt * per[pass]);
+                s.unit_begin = sidx * mts[pass];
+                s.b_off = boff;
+                s.pad = e;
+                boff += (long long)s.ks * s.npad * 128;
+                out[sidx] = s;
+            }
+        }
+        __syncthreads();
+        if (tid == 1023) {
+            // sidx / boff of the last thread are the routed totals; append the shared expert.
+            int n = sidx;
+            if (b.has_shared) {
+                for (int j = 0; j * cap[pass] < b.tokens; ++j, ++n) {
+                    TcSeg s;
+                    const int nt = min(cap[pass], b.tokens - j * cap[pass]);
+                    if (pass == 0) {
+                        s.a = b.sh_gate_tc; s.b = b.sh_up_tc; s.ra = b.sh_gate_rexp; s.rb = b.sh_up_rexp;
+                        s.rows = b.inter; s.cols = b.hidden;
+                    } else {
+                        s.a = b.sh_down_tc; s.b = nullptr; s.ra = b.sh_down_rexp; s.rb = nullptr;
+                        s.rows = b.hidden; s.cols = b.inter;
+                    }
+                    s.mts = mts[pass]; s.ks = ksz[pass];
+                    s.col_begin = TK + j * cap[pass]; s.ntok = nt;
+                    s.rowsper = per[pass]; s.npad = round16(nt * per[pass]);
+                    s.unit_begin = n * mts[pass];
+                    s.b_off = boff;
+                    s.pad = -1;
+                    boff += (long long)s.ks * s.npad * 128;
+                    out[n] = s;
+                }
+            }
+            b.scalars[2 * pass] = n;
+            b.scalars[2 * pass + 1] = n * mts[pass];
+        }
+        __syncthreads();
+    }
+}
+
 }  // namespace
+
+int launch_build_tc_segs(Ctx *ctx, const TcBuildArgs &b, cudaStream_t st) {
+    k_build_tc_segs<<<1, 1024, 0, st>>>(b);
+    URB_CUDA(ctx, cudaGetLastError());
+    return URB_OK;
+}
 
 int launch_permute(Ctx *ctx, const PermArgs &p, cudaStream_t st) {
     size_t smem = size_t(p.experts) * 4 * 3 + 4 + size_t(32) * p.experts * 2;
@@ -201,10 +328,10 @@ int launch_permute(Ctx *ctx, const PermArgs &p, cudaStream_t st) {
 
 int launch_combine(Ctx *ctx, const float *y, const float *shared_y, const float *w,
                    const int32_t *inv, int tokens, int top_k, int hidden, float *out,
-                   cudaStream_t st) {
+                   cudaStream_t st, const int32_t *status) {
     if (tokens <= 0) return URB_OK;
     dim3 grid(unsigned((hidden + 255) / 256), unsigned(tokens));
-    k_combine<<<grid, 256, 0, st>>>(y, shared_y, w, inv, tokens, top_k, hidden, out);
+    k_combine<<<grid, 256, 0, st>>>(y, shared_y, w, inv, tokens, top_k, hidden, out, status);
     URB_CUDA(ctx, cudaGetLastError());
     return URB_OK;
 }

@@ -15,39 +15,74 @@
 namespace urb {
 namespace {
 
-constexpr int kRouterKc = 128;  // columns staged per step
+constexpr int kRouterKc = 64;  // columns staged per tile
 
+template <bool BF16>
+__device__ __forceinline__ double widen(const void *w, size_t idx) {
+    return BF16 ? double(__uint_as_float(uint32_t(static_cast<const uint16_t *>(w)[idx]) << 16))
+                : double(static_cast<const float *>(w)[idx]);
+}
+
+// CTA = 32 experts x 8 tokens; thread (lane = expert, warp = token) owns one chain.  Column
+// tiles of kRouterKc are staged as f64 in a double buffer; the next tile is fetched into
+// registers while the current one is consumed, so the only stall per tile is one barrier.
 template <bool BF16>
 __global__ void __launch_bounds__(256) k_router_logits(const void *w, int experts, int cols,
                                                        const float *x, int tokens,
                                                        float *logits) {
-    __shared__ double ws[32][kRouterKc + 1];
-    __shared__ double xs[8][kRouterKc];
+    constexpr int KC = kRouterKc;
+    constexpr int WPT = 32 * KC / 256;  // W elements staged per thread per tile
+    constexpr int XPT = 8 * KC / 256;   // x elements staged per thread per tile
+    __shared__ double ws[2][32][KC + 1];
+    __shared__ double xs[2][8][KC];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int e0 = blockIdx.x * 32, t0 = blockIdx.y * 8;
-    const int e = e0 + lane, t = t0 + warp;
-    double acc = -0.0;
-    for (int c0 = 0; c0 < cols; c0 += kRouterKc) {
-        const int kc = min(kRouterKc, cols - c0);
-        __syncthreads();
-        for (int i = threadIdx.x; i < 32 * kRouterKc; i += 256) {
-            int r = i / kRouterKc, c = i % kRouterKc;
-            double v = 0.0;
-            if (e0 + r < experts && c < kc) {
-                size_t idx = size_t(e0 + r) * cols + c0 + c;
-                v = BF16 ? double(__uint_as_float(uint32_t(static_cast<const uint16_t *>(w)[idx]) << 16))
-                         : double(static_cast<const float *>(w)[idx]);
-            }
-            ws[r][c] = v;
+    const int ntiles = (cols + KC - 1) / KC;
+    double wr[WPT], xr[XPT];
+    auto fetch = [&](int tile) {
+        const int c0 = tile * KC;
+#pragma unroll
+        for (int j = 0; j < WPT; ++j) {
+            const int i = threadIdx.x + j * 256, r = i / KC, c = i % KC;
+            wr[j] = (e0 + r < experts && c0 + c < cols) ? widen<BF16>(w, size_t(e0 + r) * cols + c0 + c) : 0.0;
         }
-        for (int i = threadIdx.x; i < 8 * kRouterKc; i += 256) {
-            int r = i / kRouterKc, c = i % kRouterKc;
-            xs[r][c] = (t0 + r < tokens && c < kc) ? double(x[size_t(t0 + r) * cols + c0 + c]) : 0.0;
+#pragma unroll
+        for (int j = 0; j < XPT; ++j) {
+            const int i = threadIdx.x + j * 256, r = i / KC, c = i % KC;
+            xr[j] = (t0 + r < tokens && c0 + c < cols) ? double(x[size_t(t0 + r) * cols + c0 + c]) : 0.0;
         }
+    };
+    auto stash = [&](int buf) {
+#pragma unroll
+        for (int j = 0; j < WPT; ++j) {
+            const int i = threadIdx.x + j * 256;
+            ws[buf][i / KC][i % KC] = wr[j];
+        }
+#pragma unroll
+        for (int j = 0; j < XPT; ++j) {
+            const int i = threadIdx.x + j * 256;
+            xs[buf][i / KC][i % KC] = xr[j];
+        }
+    };
+    fetch(0);
+    stash(0);
+    __syncthreads();
+    double acc = -0.0;  // Iterator::sum over f64 starts from -0.0 (bf16.rs:500)
+    for (int tile = 0; tile < ntiles; ++tile) {
+        const int buf = tile & 1;
+        if (tile + 1 < ntiles) fetch(tile + 1);
+        const int kc = min(KC, cols - tile * KC);
+        // Exactly the reference's additions: columns in order, one rounding each.
+        if (kc == KC) {
+#pragma unroll 16
+            for (int c = 0; c < KC; ++c) acc = fma(ws[buf][lane][c], xs[buf][warp][c], acc);
+        } else {
+            for (int c = 0; c < kc; ++c) acc = fma(ws[buf][lane][c], xs[buf][warp][c], acc);
+        }
+        if (tile + 1 < ntiles) stash(buf ^ 1);
         __syncthreads();
-        // Exactly the reference's additions: columns c0 .. c0+kc-1 in order.
-        for (int c = 0; c < kc; ++c) acc = fma(ws[lane][c], xs[warp][c], acc);
     }
+    const int e = e0 + lane, t = t0 + warp;
     if (e < experts && t < tokens) logits[size_t(t) * experts + e] = float(acc);
 }
 
@@ -94,7 +129,14 @@ __global__ void k_route_noaux(const float *logits, const float *bias, int tokens
         flags[i] = 1;
     }
     if (__any_sync(0xffffffffu, bad)) {
+        // Rejected token: report, and leave distinct valid ids with zero weight so that the
+        // rest of a device pipeline stays in bounds (it short-circuits on the status anyway).
         if (lane == 0) set_status(status, URB_ERR_NONFINITE);
+        for (int r = lane; r < top_k; r += 32) {
+            out_e[size_t(t) * top_k + r] = r;
+            out_w[size_t(t) * top_k + r] = 0.0f;
+            if (out_s) out_s[size_t(t) * top_k + r] = 0.0f;
+        }
         return;
     }
     __syncwarp();
@@ -123,9 +165,10 @@ __global__ void k_route_noaux(const float *logits, const float *bias, int tokens
         }
         __syncwarp();
     }
-    // routing.rs:131-141: top_k by selection desc, lower id wins ties.
+    // routing.rs:131-141: top_k by selection desc, lower id wins ties.  The chosen ids go
+    // straight to the output row; lane 0 accumulates the f32 denominator in ranking order.
+    int32_t *oe = out_e + size_t(t) * top_k;
     float den = -0.0f;
-    int32_t chosen_e[64];
     for (int r = 0; r < top_k; ++r) {
         int32_t key = INT32_MIN;
         int id = INT32_MAX;
@@ -138,12 +181,18 @@ __global__ void k_route_noaux(const float *logits, const float *bias, int tokens
         warp_best(key, id);
         if (id == INT32_MAX) {  // fewer allowed experts than top_k
             if (lane == 0) set_status(status, URB_ERR_INVALID_GEOMETRY);
+            for (int r2 = lane; r2 < top_k; r2 += 32) {
+                out_e[size_t(t) * top_k + r2] = r2;
+                out_w[size_t(t) * top_k + r2] = 0.0f;
+            }
             return;
         }
         if (lane == (id & 31)) flags[id] = 2;
+        if (lane == 0) {
+            oe[r] = id;
+            den = __fadd_rn(den, gate[id]);
+        }
         __syncwarp();
-        if (r < 64) chosen_e[r] = id;
-        if (lane == 0) den = __fadd_rn(den, gate[id]);
     }
     if (lane == 0) {
         den = __fadd_rn(den, 1e-20f);  // routing.rs:143-146
@@ -151,13 +200,13 @@ __global__ void k_route_noaux(const float *logits, const float *bias, int tokens
             set_status(status, URB_ERR_NONFINITE);
             return;
         }
-        for (int r = 0; r < top_k; ++r) {
-            int id = chosen_e[r];
-            float w = normalize ? __fdiv_rn(gate[id], den) : gate[id];
-            out_e[size_t(t) * top_k + r] = id;
-            out_w[size_t(t) * top_k + r] = __fmul_rn(w, scaling);
-            if (out_s) out_s[size_t(t) * top_k + r] = sel[id];
-        }
+    }
+    den = __shfl_sync(0xffffffffu, den, 0);
+    for (int r = lane; r < top_k; r += 32) {
+        const int id = oe[r];
+        const float w = normalize ? __fdiv_rn(gate[id], den) : gate[id];
+        out_w[size_t(t) * top_k + r] = __fmul_rn(w, scaling);
+        if (out_s) out_s[size_t(t) * top_k + r] = sel[id];
     }
 }
 
@@ -196,7 +245,7 @@ __global__ void k_route_softmax(const float *logits, int tokens, int E, int top_
     }
     for (int i = lane; i < E; i += 32) p[i] = __fdiv_rn(p[i], den);
     __syncwarp();
-    int32_t chosen[64];
+    int32_t *oe = out_e + size_t(t) * top_k;
     float selected = 0.0f;
     for (int r = 0; r < top_k; ++r) {
         int32_t key = INT32_MIN;
@@ -208,23 +257,27 @@ __global__ void k_route_softmax(const float *logits, int tokens, int E, int top_
             }
         warp_best(key, id);
         if (lane == (id & 31)) taken[id] = 1;
+        if (lane == 0) {
+            oe[r] = id;
+            selected = __fadd_rn(selected, p[id]);
+        }
         __syncwarp();
-        if (r < 64) chosen[r] = id;
-        if (lane == 0) selected = __fadd_rn(selected, p[id]);
     }
-    if (lane == 0) {
-        if (!isfinite(selected) || selected <= 0.0f) {
-            set_status(status, URB_ERR_NONFINITE);
-            return;
-        }
-        for (int r = 0; r < top_k; ++r) {
-            float w = __fdiv_rn(p[chosen[r]], selected);
-            if (!isfinite(w)) set_status(status, URB_ERR_NONFINITE);
-            out_e[size_t(t) * top_k + r] = chosen[r];
-            out_w[size_t(t) * top_k + r] = w;
-        }
+    selected = __shfl_sync(0xffffffffu, selected, 0);
+    if (!isfinite(selected) || selected <= 0.0f) {
+        if (lane == 0) set_status(status, URB_ERR_NONFINITE);
+        return;
+    }
+    for (int r = lane; r < top_k; r += 32) {
+        const float w = __fdiv_rn(p[oe[r]], selected);
+        if (!isfinite(w)) set_status(status, URB_ERR_NONFINITE);
+        out_w[size_t(t) * top_k + r] = w;
     }
 }
+
+}  // namespace
+
+namespace {
 
 ExpfTable table_of(const Ctx *ctx) { return ExpfTable{ctx->expf_keys, ctx->expf_vals, ctx->expf_index}; }
 

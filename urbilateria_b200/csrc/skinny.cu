@@ -188,14 +188,14 @@ __device__ __forceinline__ int src_shift_of(const GroupArgs &a, int srow) {
 }
 
 template <int FMT, int NB>
-__device__ void fill_b(uint2 *bsm, const Seg &S, const GroupArgs &a) {
+__device__ void fill_b(uint2 *bsm, const Seg &S, const GroupArgs &a, const int hilo) {
     const int entries = NB * S.kslices * 256;
     for (int idx = threadIdx.x; idx < entries; idx += kThreads) {
         int le = idx & 31, b = (idx >> 5) & 7;
         int s = (idx >> 8) % S.kslices, nb = (idx >> 8) / S.kslices;
         int col = nb * 8 + (le >> 2);
         int k0 = s * 128 + (le & 3) * 32 + b * 4;
-        int tok = a.hilo ? col >> 1 : col, part = a.hilo ? (col & 1) : 0;
+        int tok = hilo ? col >> 1 : col, part = hilo ? (col & 1) : 0;
         uint2 v = make_uint2(0, 0);
         if (tok < S.ntok) {
             int c = S.col_begin + tok;
@@ -228,6 +228,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_grouped(GroupArgs a, int kslice
 
     const int total_rows = *a.total_rows;
     const int nsegs = *a.nsegs;
+    const int hilo = (a.lofree && *a.lofree) ? 0 : a.hilo;
     if (total_rows <= 0 || nsegs <= 0) return;
     const long r0 = long(total_rows) * blockIdx.x / gridDim.x;
     const long r1 = long(total_rows) * (blockIdx.x + 1) / gridDim.x;
@@ -254,7 +255,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_grouped(GroupArgs a, int kslice
         if (lo >= hi) continue;
         if (loaded != si) {
             __syncthreads();
-            fill_b<FMT, NB>(bsm, S, a);
+            fill_b<FMT, NB>(bsm, S, a, hilo);
             __syncthreads();
             loaded = si;
         }
@@ -358,8 +359,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_grouped(GroupArgs a, int kslice
             for (int nb = 0; nb < NB; ++nb) {
 #pragma unroll
                 for (int t2 = 0; t2 < 2; ++t2) {
-                    if (a.hilo && t2 == 1) break;  // warp-uniform
-                    const int tok = a.hilo ? nb * 4 + q : nb * 8 + 2 * q + t2;
+                    if (hilo && t2 == 1) break;  // warp-uniform
+                    const int tok = hilo ? nb * 4 + q : nb * 8 + 2 * q + t2;
                     const bool tok_ok = tok < S.ntok;
                     const int c = S.col_begin + (tok_ok ? tok : 0);
                     int shift = 0;
@@ -369,8 +370,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_grouped(GroupArgs a, int kslice
                     for (int m = 0; m < MATS; ++m) {
                         const float d0 = t2 ? acc[m][nb][1] : acc[m][nb][0];
                         const float d2 = t2 ? acc[m][nb][3] : acc[m][nb][2];
-                        const float lo_r = a.hilo ? acc[m][nb][0] + acc[m][nb][1] : d0;
-                        const float hi_r = a.hilo ? acc[m][nb][2] + acc[m][nb][3] : d2;
+                        const float lo_r = hilo ? acc[m][nb][0] + acc[m][nb][1] : d0;
+                        const float hi_r = hilo ? acc[m][nb][2] + acc[m][nb][3] : d2;
                         v[m][0] = ldexpf(lo_r, e0[m][0] - shift);
                         v[m][1] = ldexpf(hi_r, e0[m][1] - shift);
                     }

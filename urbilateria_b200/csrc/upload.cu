@@ -1,6 +1,7 @@
 // upload.cu — device residency for weight matrices: payload validation (the checks of the
 // reference constructors) and the repack into the tiled layout described in urb_internal.cuh.
 #include "urb_internal.cuh"
+#include "urb_tc.cuh"
 
 namespace urb {
 namespace {
@@ -162,7 +163,8 @@ int upload_matrix(Ctx *ctx, Mat *m, const void *values, const uint8_t *scales) {
                        (m->format == URB_FMT_BF16);
     m->rbs = int(div_ceil(m->rows, 16));
     m->kslices = int(div_ceil(m->cols, 128));
-    size_t rows_pad = size_t(m->rbs) * 16;
+    // Row exponents cover both layouts: 16-row tiles (mma.sync) and 128-row tiles (tcgen05).
+    size_t rows_pad = div_ceil(m->rows, 128) * 128;
 
     if (m->format == URB_FMT_MXFP8) {
         k_scan_e4m3<<<1024, 256, 0, st>>>(static_cast<const uint8_t *>(m->raw_values),
@@ -213,7 +215,11 @@ int upload_matrix(Ctx *ctx, Mat *m, const void *values, const uint8_t *scales) {
                                                            32, m->rbs, m->kslices, m->tiles);
         }
         URB_CUDA(ctx, cudaGetLastError());
-        // MX payloads keep only the tiled copy.  BF16 keeps its row-major copy as well: the
+        if (mx) {
+            int rc = repack_tc(ctx, m, st);
+            if (rc) return rc;
+        }
+        // MX payloads keep only the tiled copies.  BF16 keeps its row-major copy as well: the
         // bit-exact router reads whole rows in column order.
         if (m->format != URB_FMT_BF16) {
             URB_CUDA(ctx, cudaFreeAsync(m->raw_values, st));

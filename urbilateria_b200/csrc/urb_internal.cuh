@@ -51,6 +51,9 @@ struct Mat {
     int rbs = 0, kslices = 0;
     uint8_t *tiles = nullptr;
     int8_t *row_exp = nullptr;  // [rbs*16]
+    // Tensor-core (tcgen05) layout of MX matrices: 128x64 tiles.
+    uint8_t *tc_tiles = nullptr;
+    int tc_mts = 0, tc_ks = 0;
     // Generic path: the reference layout on the device (used when !tiled).
     void *raw_values = nullptr;
     uint8_t *raw_scales = nullptr;
@@ -87,6 +90,8 @@ struct GroupArgs {
     int out_stride;
     int32_t *out_maxexp;      // SwiGLU: per output row ilogb(max|h|) (atomicMax), or nullptr
     int hilo;                 // 1: two f16/bf16 columns (hi, lo) per token
+    const int *lofree;        // optional device flag: 1 -> every activation is exact in one
+                              // f16/bf16 column, so the pass runs without lo columns
 };
 
 struct Ctx {
@@ -146,9 +151,11 @@ int launch_grouped_ex(Ctx *ctx, int fmt, bool pair, int ksplit, const GroupArgs 
 // generic.cu: fallback for matrices without the tiled layout (CUDA cores, fp32).
 int launch_generic_matmul(Ctx *ctx, const Mat *m, size_t start, size_t count, const float *d_x,
                           size_t batch, float *d_y, cudaStream_t stream);
-// prep: per-row shift and non-finite check.
+// prep: per-row shift and non-finite check; optionally clears *d_lofree when some row is not
+// exactly representable in one f16 (bf16_check=0) / bf16 (bf16_check=1) column after its shift.
 int launch_row_shift(const float *d_src, int rows, int cols, int stride, int32_t *d_shift,
-                     int32_t *d_status, cudaStream_t stream);
+                     int32_t *d_status, cudaStream_t stream, int32_t *d_lofree = nullptr,
+                     int bf16_check = 0);
 // router.cu
 int launch_router_logits(const Mat *router, const float *d_x, int tokens, float *d_logits,
                          cudaStream_t stream);

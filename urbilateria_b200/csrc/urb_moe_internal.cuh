@@ -1,6 +1,7 @@
 // urb_moe_internal.cuh — MoE-layer structures shared by moe.cu and api.cu.
 #pragma once
 #include "urb_internal.cuh"
+#include "urb_tc.cuh"
 
 namespace urb {
 
@@ -24,12 +25,32 @@ struct PermArgs {
     int shared_in_pass;
     int hidden, inter, gu_rbs, gu_kslices, dn_rbs, dn_kslices;
     int32_t *status;
+    const int *lofree;    // optional: when *lofree, segments hold 2*cap tokens
 };
 
 int launch_permute(Ctx *ctx, const PermArgs &p, cudaStream_t st);
+
+// Segments of the two tensor-core passes, built on the device from the grouping.
+struct TcBuildArgs {
+    const int32_t *counts, *offsets;  // from the grouping kernel
+    const int *lofree;                // x exactly representable in one f16 column
+    int tokens, top_k, experts;
+    const uint8_t *const *gate_tc, *const *up_tc, *const *down_tc;
+    const int8_t *const *gate_rexp, *const *up_rexp, *const *down_rexp;
+    const uint8_t *sh_gate_tc, *sh_up_tc, *sh_down_tc;
+    const int8_t *sh_gate_rexp, *sh_up_rexp, *sh_down_rexp;
+    int has_shared;
+    int hidden, inter;
+    TcSeg *gu, *dn;
+    int *scalars;  // nsegs_gu, units_gu, nsegs_dn, units_dn
+    const int32_t *status;  // non-zero: an earlier stage failed; build no work
+};
+int launch_build_tc_segs(Ctx *ctx, const TcBuildArgs &b, cudaStream_t st);
+constexpr int kTcCapGu = 64;   // tokens per gate/up segment with hi/lo columns (N <= 128)
+constexpr int kTcCapDn = 128;  // tokens per down segment (hi/lo, N <= 256)
 int launch_combine(Ctx *ctx, const float *y, const float *shared_y, const float *w,
                    const int32_t *inv, int tokens, int top_k, int hidden, float *out,
-                   cudaStream_t st);
+                   cudaStream_t st, const int32_t *status = nullptr);
 
 struct Layer {
     Ctx *ctx = nullptr;
@@ -40,8 +61,10 @@ struct Layer {
     std::vector<const Mat *> gate, up, down;
     const Mat *sg = nullptr, *su = nullptr, *sd = nullptr;
     urb_moe_geometry geo{};
-    // Device pointer tables [experts] for gate/up/down tiles and row exponents.
+    // Device pointer tables [experts] for gate/up/down tiles and row exponents, then the
+    // tensor-core tiles of gate/up/down.
     void **d_tables = nullptr;
+    bool use_tc = true;  // tcgen05 grouped passes (false: mma.sync register-dequant passes)
 };
 
 // Device workspace of one forward, carved from the context workspace.
@@ -57,6 +80,10 @@ struct MoeWork {
     float *h;             // [TK+T, inter]
     float *y;             // [TK+T, hidden]
     int32_t *status;
+    int32_t *lofree;
+    TcSeg *tsegs_gu, *tsegs_dn;
+    int *tscalars;
+    uint8_t *bbuf_gu, *bbuf_dn;
 };
 
 int moe_forward_device(Layer *L, const float *d_x, int tokens, float *d_out, MoeWork *work_out,

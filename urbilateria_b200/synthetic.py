@@ -43,14 +43,14 @@ def encode_e4m3fn(v: np.ndarray) -> np.ndarray:
     retained = (bits >> 20) & 1
     rounded = (bits + ((1 << 19) - 1) + retained) & ~np.uint64((1 << 20) - 1)
     e = (rounded >> 23) & 0xFF
-    exponent = np.where(e > 120, e - 120, 0)
+    exponent = np.where(e > 120, e - 120, np.uint64(0))
     mantissa = (rounded >> 20) & 7
     normal = np.minimum((exponent << 3) | mantissa, 0x7E)
     sub = np.rint(mag * np.float32(512.0)).astype(np.uint64)  # rint = ties-to-even
-    code = np.where(mag < np.float32(2.0 ** -6), sub, normal)
-    code = np.where(mag == 0, 0, code)
+    code = np.where(mag < np.float32(2.0 ** -6), sub, normal).astype(np.uint64)
+    code = np.where(mag == 0, np.uint64(0), code)
     neg = np.signbit(v) & (code != 0)
-    return (code | np.where(neg, 0x80, 0)).astype(np.uint8)
+    return (code.astype(np.uint8) | np.where(neg, np.uint8(0x80), np.uint8(0))).astype(np.uint8)
 
 
 def mxfp4_matrix(g: np.random.Generator, rows: int, cols: int, exp_lo=119, exp_hi=127,
