@@ -110,10 +110,7 @@ def test_moe_rejects_nonfinite_input(oracle, ctx):
 def test_both_grouped_paths_many_tokens(oracle, ctx, path, monkeypatch):
     # 160 tokens of f32 (not bf16-exact) activations: hi/lo columns, two shared-expert chunks,
     # experts with >64 routed tokens on the tcgen05 path.
-    if path == "mma":
-        monkeypatch.setenv("URB_MOE_PATH", "mma")
-    else:
-        monkeypatch.delenv("URB_MOE_PATH", raising=False)
+    monkeypatch.setenv("URB_MOE_PATH", path)
     g = syn.rng(500)
     dev, orc = build_layer(oracle, ctx, g, 256, 256, 8, "mxfp4", top_k=4, scale=1.0)
     x = syn.normal_f32(g, (160, 256))

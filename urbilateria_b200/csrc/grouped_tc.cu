@@ -1,22 +1,31 @@
-// grouped_tc.cu — tensor-core (tcgen05 / TMEM) grouped pass for MX weights.
+// grouped_tc.cu — block-scaled tensor-core (tcgen05 / TMEM) grouped pass for MX weights.
 //
-// One persistent CTA per SM walks work units (segment, 128-row tile).  Per 64-column K stage:
-//   * warp 0 (producer): bulk-copies (TMA engine, 1-D) the raw MX tile(s) of the stage and the
-//     segment's activation tile (pre-swizzled f16, 128-byte canonical K-major layout) into a
-//     shared-memory ring;
-//   * warps 4..11 (decoders): each thread owns one weight row (its TMEM lane); it decodes
-//     32 E2M1 or E4M3 values with cvt.rn.f16x2.{e2m1x2,e4m3x2}, applies the E8M0 scale with one
-//     HMUL2 per pair (exact: powers of two within the row's f16 window) and stores the 16
-//     f16x2 words into TMEM with tcgen05.st;
-//   * warp 1 (one thread): tcgen05.mma kind::f16, A from TMEM, B from the shared-memory
-//     descriptor, f32 accumulators in TMEM; tcgen05.commit releases the stage.
-// After the last stage the decoders read the accumulators back (tcgen05.ld), undo the
-// power-of-two scalings, fuse SwiGLU for gate/up pairs, and store token-major rows.
+// The weights never leave their MX encoding: a 128-row x 128-byte tile (E2M1 nibbles or E4M3
+// bytes, pre-swizzled for the 128-byte canonical K-major layout, followed by its E8M0 scales in
+// the tcgen05.cp chunk layout) is one contiguous run of HBM that one 1-D bulk copy (TMA engine)
+// drops into shared memory, where tcgen05.mma kind::mxf4 / kind::mxf8f6f4 reads it directly.
+// No CUDA-core dequantisation remains on the weight stream, so the pass runs at the rate HBM
+// delivers tiles.
 //
-// Tile layout of a resident MX matrix ("tc layout"): tiles of 128 rows x 64 columns, tile
-// (mt, ks) at ((mt * KS + ks) * TB); inside a tile, payload [chunk][row 0..127][16 B] then
-// scales [row][2] (E8M0 of columns 0-31 and 32-63).  MXFP4: 2 chunks (TB = 4352 B),
-// MXFP8: 4 chunks (TB = 8448 B).
+// Activations are represented in the weights' element format by residual terms (k_bs_prep):
+// per 32-column block, term j takes the E8M0 scale that fits the residual's largest magnitude
+// into the element range (6 for E2M1, 448 for E4M3), rounds to nearest, and passes the
+// remainder to term j+1.  Each token owns bs_rows_per_tok consecutive MMA rows (its terms, then
+// zero rows); the epilogue adds the term columns of a token.
+//
+// One persistent CTA per SM walks work units (group, 128-row tile, sub-segment).  tcgen05
+// instructions cost ~120-200 cycles of issue each on the issuing thread (MMAs from two threads
+// proceed concurrently), so the per-stage instruction stream is spread over warps:
+//   warp 0 (one thread)  weight producer: tiles into a 9-deep ring (bulk copies, mbarriers);
+//   warp 3 (one thread)  activation producer: stages into a 4-deep ring (L2-resident source);
+//   warps 8-11           scale warps: each stage's E8M0 scales of both operands from shared
+//                        memory into TMEM with tcgen05.st (each warp fills its lane quarter);
+//   warps 1, 2 (one thread each)  MMA issuers: issuer i runs the MMAs of K half i of every
+//                        stage into its own TMEM accumulator and releases the stage with one
+//                        tcgen05.commit (the activation slot is released through the same
+//                        barrier);
+//   warps 4-7            epilogue: tcgen05.ld of both accumulators, half and term sums, f32
+//                        row stores.
 #include "tc_common.cuh"
 #include "urb_internal.cuh"
 #include "urb_tc.cuh"
@@ -24,122 +33,98 @@
 namespace urb {
 namespace {
 
-// Rings: raw weight tiles (deep: the HBM stream), activation tiles, TMEM A stages.
-constexpr int kStagesAMax = 12;  // weight ring depth (runtime: as many as shared memory holds)
-constexpr int kStagesB = 4;
-constexpr int kStagesT = 4;
-constexpr int kDecWarps = 16;    // two teams of 8 warps alternate K stages
-constexpr int kThreadsTc = 32 * (4 + kDecWarps);  // w0: A producer, w1: MMA, w2: B producer, w3: idle
+constexpr int kSA = 9;                // weight ring depth (also the TMEM scale slots)
+constexpr int kSB = 4;                // activation ring depth (kSB <= kSA)
+constexpr int kStage = 17408;         // bytes of one ring slot (largest tile / activation stage)
+constexpr int kThreadsBs = 384;
+constexpr uint32_t kAccCols = 128;    // accumulator columns per issuer (N <= 128)
+constexpr uint32_t kSfCol0 = 256;     // first scale column: slot s at kSfCol0 + 16 s
+constexpr int kSmemBs = (kSA + kSB) * kStage + 1024;
 
-__device__ __forceinline__ uint32_t pow2_h2(int k) {
-    k = max(-24, min(15, k));
-    uint32_t h = k >= -14 ? uint32_t(k + 15) << 10 : 1u << (k + 24);
-    return h | (h << 16);
-}
-__device__ __forceinline__ uint32_t hmul2_bits(uint32_t a, uint32_t b) {
-    uint32_t d;
-    asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
-    return d;
-}
-__device__ __forceinline__ void e2m1x8_to_f16(uint32_t w, uint32_t *d) {
-    asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\t"
-        "mov.b32 {b0, b1, b2, b3}, %4;\n\t"
-        "cvt.rn.f16x2.e2m1x2 %0, b0;\n\t"
-        "cvt.rn.f16x2.e2m1x2 %1, b1;\n\t"
-        "cvt.rn.f16x2.e2m1x2 %2, b2;\n\t"
-        "cvt.rn.f16x2.e2m1x2 %3, b3;\n\t}"
-        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
-        : "r"(w));
-}
-__device__ __forceinline__ void e4m3x4_to_f16(uint32_t w, uint32_t *d) {
-    asm("{\n\t.reg .b16 h0, h1;\n\t"
-        "mov.b32 {h0, h1}, %2;\n\t"
-        "cvt.rn.f16x2.e4m3x2 %0, h0;\n\t"
-        "cvt.rn.f16x2.e4m3x2 %1, h1;\n\t}"
-        : "=r"(d[0]), "=r"(d[1])
-        : "r"(w));
-}
+static_assert(bs_tile_bytes(URB_FMT_MXFP4) <= kStage && bs_tile_bytes(URB_FMT_MXFP8) <= kStage, "slot");
+static_assert(bs_bstage_bytes(URB_FMT_MXFP4, kBsNmax) <= kStage, "slot");
+static_assert(kSfCol0 + kSA * 16 <= 512, "tmem");
+static_assert(kSB <= kSA, "the activation producer watches the weight ring's release barrier");
 
 __device__ __forceinline__ void set_status(int32_t *status, int code) {
     if (status) atomicCAS(status, 0, int32_t(code));
 }
 
-// Segment of a work unit (segments ordered by unit_begin).
-__device__ __forceinline__ int find_seg(const TcSeg *segs, int nsegs, int u) {
-    int lo = 0, hi = nsegs - 1;
-    while (lo < hi) {
-        int mid = (lo + hi + 1) >> 1;
-        if (segs[mid].unit_begin <= u) lo = mid; else hi = mid - 1;
+// Walks the work units of this CTA (u = blockIdx.x, += gridDim.x).  The group of the next
+// unit is loaded one unit ahead and its group index two units ahead, so a role never waits on
+// a global load at a unit boundary.
+struct UnitCursor {
+    const TcSeg *segs;
+    const int *map;
+    int u, step, total;
+    TcSeg cur, nxt;
+    int g2;
+    __device__ __forceinline__ UnitCursor(const TcArgs &a, int total_units)
+        : segs(a.segs), map(a.unit_group), u(blockIdx.x), step(gridDim.x), total(total_units) {
+        if (u < total) cur = segs[map[u]];
+        if (u + step < total) nxt = segs[map[u + step]];
+        g2 = u + 2 * step < total ? map[u + 2 * step] : 0;
     }
-    return lo;
-}
+    __device__ __forceinline__ bool valid() const { return u < total; }
+    __device__ __forceinline__ void advance() {
+        u += step;
+        cur = nxt;
+        if (u + step < total) nxt = segs[g2];
+        if (u + 2 * step < total) g2 = map[u + 2 * step];
+    }
+};
 
-__device__ __forceinline__ float silu_f(float v) { return v / (1.0f + expf(-v)); }
+__device__ __forceinline__ int round16i(int v) { return (v + 15) & ~15; }
 
-// Decodes this thread's 32 weights (one row, one K half) of one matrix of a staged tile into
-// 16 f16x2 words scaled by 2^(scale-127-e0).
+struct Unit {
+    int mt, sub, nt, n;
+};
 template <int FMT>
-__device__ __forceinline__ void decode_row_half(const uint8_t *t, int row, int hlf, int e0,
-                                                uint32_t *v) {
-    constexpr int TB = tc_tile_bytes(FMT);
-    const int scale = t[TB - 256 + 2 * row + hlf];
-    const uint32_t mul = pow2_h2(scale - 127 - e0);
-    if (FMT == URB_FMT_MXFP4) {
-        const uint4 w = *reinterpret_cast<const uint4 *>(t + hlf * 2048 + row * 16);
-        e2m1x8_to_f16(w.x, v + 0);
-        e2m1x8_to_f16(w.y, v + 4);
-        e2m1x8_to_f16(w.z, v + 8);
-        e2m1x8_to_f16(w.w, v + 12);
-    } else {
-        const uint4 w0 = *reinterpret_cast<const uint4 *>(t + (2 * hlf) * 2048 + row * 16);
-        const uint4 w1 = *reinterpret_cast<const uint4 *>(t + (2 * hlf + 1) * 2048 + row * 16);
-        e4m3x4_to_f16(w0.x, v + 0);
-        e4m3x4_to_f16(w0.y, v + 2);
-        e4m3x4_to_f16(w0.z, v + 4);
-        e4m3x4_to_f16(w0.w, v + 6);
-        e4m3x4_to_f16(w1.x, v + 8);
-        e4m3x4_to_f16(w1.y, v + 10);
-        e4m3x4_to_f16(w1.z, v + 12);
-        e4m3x4_to_f16(w1.w, v + 14);
-    }
-#pragma unroll
-    for (int i = 0; i < 16; ++i) v[i] = hmul2_bits(v[i], mul);
+__device__ __forceinline__ Unit unit_of(const TcSeg &S, int u) {
+    Unit x;
+    const int r = u - S.unit_begin;
+    x.mt = r / S.nsub;
+    x.sub = r - x.mt * S.nsub;
+    x.nt = min(bs_cap(FMT), S.ntok - x.sub * bs_cap(FMT));
+    x.n = round16i(bs_rows_per_tok(FMT) * x.nt);
+    return x;
 }
 
-template <int FMT, bool PAIR>
-__global__ void __launch_bounds__(kThreadsTc, 1) k_tc_grouped(TcArgs a) {
-    constexpr int MATS = PAIR ? 2 : 1;
-    constexpr int TB = tc_tile_bytes(FMT);
-    constexpr int TBA = (MATS * TB + 1023) / 1024 * 1024;  // raw A region per stage (aligned)
+template <int FMT>
+__global__ void __launch_bounds__(kThreadsBs, 1) k_bs_grouped(TcArgs a) {
+    constexpr int TB = bs_tile_bytes(FMT);
+    constexpr int CH = bs_sf_chunks(FMT);
+    constexpr int KIND_FMT = FMT == URB_FMT_MXFP4 ? 1 : 0;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    const int kStagesA = a.stages_a;
-    uint8_t *ring_a = smem;                                  // kStagesA x TBA
-    uint8_t *ring_b = smem + size_t(kStagesA) * TBA;         // kStagesB x nmax*128 (1024-aligned)
-    const int bstage = a.nmax * 128;
-    __shared__ __align__(8) uint64_t a_full[kStagesAMax], a_empty[kStagesAMax];
-    __shared__ __align__(8) uint64_t b_full[kStagesB], b_empty[kStagesB];
-    __shared__ __align__(8) uint64_t t_full[kStagesT], t_empty[kStagesT];
-    __shared__ __align__(8) uint64_t acc_full, acc_empty;
+    uint8_t *ring_a = smem;
+    uint8_t *ring_b = smem + size_t(kSA) * kStage;
+    __shared__ __align__(8) uint64_t a_full[kSA], a_empty[kSA], sf_full[kSA], b_full[kSB];
+    __shared__ __align__(8) uint64_t acc_full, acc_empty, mma_done[2];
     __shared__ uint32_t tmem_base;
-    __shared__ int abort_flag, skip;
+    __shared__ int abort_flag, skip, never;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nsegs = *a.nsegs;
     const int total_units = *a.total_units;
-    // A failed earlier stage (status set) means no work; one thread decides for the whole CTA.
     if (threadIdx.x == 0) skip = (total_units <= 0 || nsegs <= 0 || (a.status && *a.status)) ? 1 : 0;
     __syncthreads();
     if (skip) return;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kStagesA; ++s) { tc::mbar_init(&a_full[s], 1); tc::mbar_init(&a_empty[s], 8); }
-        for (int s = 0; s < kStagesB; ++s) { tc::mbar_init(&b_full[s], 1); tc::mbar_init(&b_empty[s], 1); }
-        for (int s = 0; s < kStagesT; ++s) { tc::mbar_init(&t_full[s], 8); tc::mbar_init(&t_empty[s], 1); }
-        tc::mbar_init(&acc_full, 1);
-        tc::mbar_init(&acc_empty, kDecWarps);
+        for (int s = 0; s < kSA; ++s) {
+            tc::mbar_init(&a_full[s], 1);
+            tc::mbar_init(&a_empty[s], 2);   // one commit per issuer
+            tc::mbar_init(&sf_full[s], 4);   // one arrival per scale warp
+        }
+        for (int s = 0; s < kSB; ++s) tc::mbar_init(&b_full[s], 1);
+        tc::mbar_init(&acc_full, 2);
+        tc::mbar_init(&acc_empty, 4);
+        tc::mbar_init(&mma_done[0], 1);
+        tc::mbar_init(&mma_done[1], 1);
         tc::mbar_fence_init();
         abort_flag = 0;
+        never = 0;
     }
     if (warp == 1) {
         tc::tmem_alloc(&tmem_base, 512);
@@ -149,155 +134,170 @@ __global__ void __launch_bounds__(kThreadsTc, 1) k_tc_grouped(TcArgs a) {
     __syncthreads();
     tc::fence_after_sync();
     const uint32_t tbase = tmem_base;
-    // TMEM columns: accumulators (pair: gate [0,128) up [128,256); single [0,256)), then the A
-    // stages (32 columns = 64 f16 per matrix per stage).
-    const uint32_t acc_col[2] = {0u, PAIR ? 128u : 0u};
-    auto a_col = [&](int t, int m) -> uint32_t { return 256u + uint32_t((t * MATS + m) * 32); };
+    volatile int *abortp = &abort_flag;
     auto fail = [&]() {
-        abort_flag = 1;
+        *abortp = 1;
         set_status(a.status, URB_ERR_TIMEOUT);
     };
 
     if (warp == 0 && lane == 0) {
         // ---------------- weight producer ----------------
-        uint32_t g = 0;
-        for (int u = blockIdx.x; u < total_units && !abort_flag; u += gridDim.x) {
-            const TcSeg S = a.segs[find_seg(a.segs, nsegs, u)];
-            const size_t tile0 = size_t(u - S.unit_begin) * S.ks;
+        uint32_t g = 0;  // copies issued
+        for (UnitCursor uc(a, total_units); uc.valid() && !*abortp; uc.advance()) {
+            const TcSeg &S = uc.cur;
+            const Unit x = unit_of<FMT>(S, uc.u);
+            const uint8_t *wsrc = S.w + size_t(x.mt) * S.ks * TB;
+            bool ok = true;
             for (int ks = 0; ks < S.ks; ++ks, ++g) {
-                const int s = int(g % kStagesA);
-                if (!tc::mbar_wait(&a_empty[s], ((g / kStagesA) & 1) ^ 1, &abort_flag)) { fail(); break; }
-                uint8_t *st = ring_a + size_t(s) * TBA;
-                tc::mbar_arrive_expect_tx(&a_full[s], uint32_t(MATS * TB));
-                tc::bulk_g2s(st, S.a + (tile0 + ks) * TB, TB, &a_full[s]);
-                if (PAIR) tc::bulk_g2s(st + TB, S.b + (tile0 + ks) * TB, TB, &a_full[s]);
+                const int sa = int(g % kSA);
+                if (!tc::mbar_wait(&a_empty[sa], ((g / kSA) & 1) ^ 1, abortp)) { ok = false; break; }
+                tc::mbar_arrive_expect_tx(&a_full[sa], uint32_t(TB));
+                tc::bulk_g2s(ring_a + size_t(sa) * kStage, wsrc + size_t(ks) * TB, TB, &a_full[sa]);
             }
+            if (!ok) { fail(); break; }
         }
-    } else if (warp == 2 && lane == 0) {
+        // Let every copy this thread issued land before the CTA can exit.
+        for (uint32_t i = g > uint32_t(kSA) ? g - kSA : 0; i < g; ++i)
+            tc::mbar_wait(&a_full[i % kSA], (i / kSA) & 1, &never);
+    } else if (warp == 3 && lane == 0) {
         // ---------------- activation producer ----------------
+        // Slot g % kSB is free once stage g - kSB has been consumed, i.e. once the weight ring's
+        // release barrier of that stage has fired (kSB <= kSA keeps the parity unambiguous).
         uint32_t g = 0;
-        for (int u = blockIdx.x; u < total_units && !abort_flag; u += gridDim.x) {
-            const TcSeg S = a.segs[find_seg(a.segs, nsegs, u)];
-            const uint32_t bbytes = uint32_t(S.npad) * 128;
+        for (UnitCursor uc(a, total_units); uc.valid() && !*abortp; uc.advance()) {
+            const TcSeg &S = uc.cur;
+            const Unit x = unit_of<FMT>(S, uc.u);
+            const uint32_t bbytes = uint32_t(bs_bstage_bytes(FMT, x.n));
+            const uint8_t *bsrc = a.bbuf + S.b_off + (long long)x.sub * S.ks * bs_bstage_bytes(FMT, kBsNmax);
+            bool ok = true;
             for (int ks = 0; ks < S.ks; ++ks, ++g) {
-                const int s = int(g % kStagesB);
-                if (!tc::mbar_wait(&b_empty[s], ((g / kStagesB) & 1) ^ 1, &abort_flag)) { fail(); break; }
-                tc::mbar_arrive_expect_tx(&b_full[s], bbytes);
-                tc::bulk_g2s(ring_b + size_t(s) * bstage, a.bbuf + S.b_off + size_t(ks) * bbytes, bbytes,
-                             &b_full[s]);
+                const int sb = int(g % kSB);
+                if (g >= uint32_t(kSB)) {
+                    const uint32_t p = g - kSB;
+                    if (!tc::mbar_wait(&a_empty[p % kSA], (p / kSA) & 1, abortp)) { ok = false; break; }
+                }
+                tc::mbar_arrive_expect_tx(&b_full[sb], bbytes);
+                tc::bulk_g2s(ring_b + size_t(sb) * kStage, bsrc + size_t(ks) * bbytes, bbytes, &b_full[sb]);
             }
+            if (!ok) { fail(); break; }
         }
-    } else if (warp == 1 && lane == 0) {
-        // ---------------- MMA issuer ----------------
+        for (uint32_t i = g > uint32_t(kSB) ? g - kSB : 0; i < g; ++i)
+            tc::mbar_wait(&b_full[i % kSB], (i / kSB) & 1, &never);
+    } else if (warp >= 8) {
+        // ---------------- scale warps ----------------
+        // TMEM scale slot sa (16 columns): A's chunks at +0 / +4, B's at +8 / +12; lane l of
+        // every quarter holds bytes 16 l .. 16 l + 15 of each 512-byte chunk.
+        const uint32_t lane_base = uint32_t(32 * (warp & 3)) << 16;
+        uint32_t g = 0;
+        for (UnitCursor uc(a, total_units); uc.valid() && !*abortp; uc.advance()) {
+            const TcSeg &S = uc.cur;
+            const Unit x = unit_of<FMT>(S, uc.u);
+            bool ok = true;
+            for (int ks = 0; ks < S.ks; ++ks, ++g) {
+                const int sa = int(g % kSA), sb = int(g % kSB);
+                if (!tc::mbar_wait(&a_full[sa], (g / kSA) & 1, abortp) ||
+                    !tc::mbar_wait(&b_full[sb], (g / kSB) & 1, abortp)) {
+                    ok = false;
+                    break;
+                }
+                const uint8_t *sfa = ring_a + size_t(sa) * kStage + 16384 + 16 * lane;
+                const uint8_t *sfb = ring_b + size_t(sb) * kStage + x.n * 128 + 16 * lane;
+                uint32_t v[16];
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    uint4 qa = make_uint4(0, 0, 0, 0), qb = make_uint4(0, 0, 0, 0);
+                    if (h < CH) {
+                        qa = *reinterpret_cast<const uint4 *>(sfa + 512 * h);
+                        qb = *reinterpret_cast<const uint4 *>(sfb + 512 * h);
+                    }
+                    v[4 * h] = qa.x; v[4 * h + 1] = qa.y; v[4 * h + 2] = qa.z; v[4 * h + 3] = qa.w;
+                    v[8 + 4 * h] = qb.x; v[9 + 4 * h] = qb.y; v[10 + 4 * h] = qb.z; v[11 + 4 * h] = qb.w;
+                }
+                tc::tmem_st16(tbase + lane_base + kSfCol0 + 16u * sa, v);
+                tc::wait_st();
+                tc::fence_before_sync();
+                __syncwarp();
+                if (lane == 0) tc::mbar_arrive(&sf_full[sa]);
+            }
+            if (!ok) { fail(); break; }
+        }
+    } else if ((warp == 1 || warp == 2) && lane == 0) {
+        // ---------------- MMA issuers (K half i of every stage) ----------------
+        const int half = warp - 1;
+        const uint32_t acc = tbase + uint32_t(half) * kAccCols;
         uint32_t g = 0, j = 0;
-        for (int u = blockIdx.x; u < total_units && !abort_flag; u += gridDim.x, ++j) {
-            const TcSeg S = a.segs[find_seg(a.segs, nsegs, u)];
-            const uint32_t idesc = tc::idesc_f16(S.npad, FMT == URB_FMT_BF16);
-            if (j > 0 && !tc::mbar_wait(&acc_empty, (j - 1) & 1, &abort_flag)) { fail(); break; }
+        for (UnitCursor uc(a, total_units); uc.valid() && !*abortp; uc.advance(), ++j) {
+            const TcSeg &S = uc.cur;
+            const Unit x = unit_of<FMT>(S, uc.u);
+            if (j >= 1 && !tc::mbar_wait(&acc_empty, (j - 1) & 1, abortp)) { fail(); break; }
             tc::fence_after_sync();
             bool ok = true;
             for (int ks = 0; ks < S.ks; ++ks, ++g) {
-                const int sb = int(g % kStagesB), st = int(g % kStagesT);
-                if (!tc::mbar_wait(&t_full[st], (g / kStagesT) & 1, &abort_flag) ||
-                    !tc::mbar_wait(&b_full[sb], (g / kStagesB) & 1, &abort_flag)) {
+                const int sa = int(g % kSA), sb = int(g % kSB);
+                // The scale warps saw both copies land; waiting on the copies' own barriers as
+                // well (already complete) orders the MMA's shared-memory reads after them.
+                if (!tc::mbar_wait(&sf_full[sa], (g / kSA) & 1, abortp) ||
+                    !tc::mbar_wait(&a_full[sa], (g / kSA) & 1, abortp) ||
+                    !tc::mbar_wait(&b_full[sb], (g / kSB) & 1, abortp)) {
                     ok = false;
                     break;
                 }
                 tc::fence_after_sync();
-                const uint64_t bdesc = tc::sdesc_sw128(tc::smem_u32(ring_b + size_t(sb) * bstage));
+                const uint32_t sA = tc::smem_u32(ring_a + size_t(sa) * kStage);
+                const uint32_t sB = tc::smem_u32(ring_b + size_t(sb) * kStage);
+                const uint32_t sfa = tbase + kSfCol0 + 16u * sa, sfb = sfa + 8;
+                const uint64_t adesc = tc::sdesc_sw128(sA), bdesc = tc::sdesc_sw128(sB);
 #pragma unroll
-                for (int kk = 0; kk < 4; ++kk) {
-#pragma unroll
-                    for (int m = 0; m < MATS; ++m)
-                        tc::mma_ts(tbase + acc_col[m], tbase + a_col(st, m) + 8 * kk,
-                                   bdesc + uint64_t(2 * kk), idesc, ks > 0 || kk > 0);
+                for (int k2 = 0; k2 < 2; ++k2) {
+                    const int kk = 2 * half + k2;
+                    const bool accum = ks > 0 || k2 > 0;
+                    if (FMT == URB_FMT_MXFP4) {
+                        const uint32_t id = 2u * (kk & 1), col = 4u * (kk >> 1);
+                        tc::mma_mxf4(acc, adesc + 2 * kk, bdesc + 2 * kk, tc::idesc_bs(KIND_FMT, x.n, id, id),
+                                     (sfa + col) | (id << 30), (sfb + col) | (id << 30), accum);
+                    } else {
+                        const uint32_t id = uint32_t(kk);
+                        tc::mma_mxf8(acc, adesc + 2 * kk, bdesc + 2 * kk, tc::idesc_bs(KIND_FMT, x.n, id, id),
+                                     sfa | (id << 30), sfb | (id << 30), accum);
+                    }
                 }
-                tc::mma_commit(&t_empty[st]);
-                tc::mma_commit(&b_empty[sb]);
+                tc::mma_commit(&a_empty[sa]);
                 if (ks == S.ks - 1) tc::mma_commit(&acc_full);
             }
             if (!ok) { fail(); break; }
         }
-    } else if (warp >= 4) {
-        // ---------------- decoders (two teams) + epilogue ----------------
-        const int dw = warp - 4;
-        const int team = dw >> 3;         // stages g with g % 2 == team
-        const int q = warp & 3;           // TMEM lane quarter
-        const int hlf = (dw >> 2) & 1;    // K half of the stage
-        const int gid = dw >> 2;          // epilogue column group 0..3
-        const int row = 32 * q + lane;    // row within the 128-row tile
+        // Every MMA of this thread completes before TMEM is released.
+        tc::mma_commit(&mma_done[half]);
+        tc::mbar_wait(&mma_done[half], 0, &never);
+    } else if (warp >= 4 && warp < 8) {
+        // ---------------- epilogue ----------------
+        constexpr int RT = bs_rows_per_tok(FMT), TT = bs_terms(FMT), TPC = 16 / RT;
+        const int q = warp & 3;  // TMEM lane quarter this warp may access
+        const int row = 32 * q + lane;
         const uint32_t lane_base = uint32_t(32 * q) << 16;
-        uint32_t g = 0, j = 0;
-        for (int u = blockIdx.x; u < total_units && !abort_flag; u += gridDim.x, ++j) {
-            const TcSeg S = a.segs[find_seg(a.segs, nsegs, u)];
-            const int grow = (u - S.unit_begin) * 128 + row;  // row within the matrix
-            int e0[2];
-            e0[0] = S.ra[grow];
-            e0[1] = PAIR ? S.rb[grow] : 0;
-            bool ok = true;
-            for (int ks = 0; ks < S.ks; ++ks, ++g) {
-                if (int(g & 1) != team) continue;
-                const int sa = int(g % kStagesA), st = int(g % kStagesT);
-                if (!tc::mbar_wait(&a_full[sa], (g / kStagesA) & 1, &abort_flag)) { ok = false; break; }
-                const uint8_t *t = ring_a + size_t(sa) * TBA;
-                uint32_t v[MATS][16];
-#pragma unroll
-                for (int m = 0; m < MATS; ++m) decode_row_half<FMT>(t + m * TB, row, hlf, e0[m], v[m]);
-                __syncwarp();
-                if (lane == 0) tc::mbar_arrive(&a_empty[sa]);  // raw tile consumed
-                if (!tc::mbar_wait(&t_empty[st], ((g / kStagesT) & 1) ^ 1, &abort_flag)) { ok = false; break; }
-                tc::fence_after_sync();
-#pragma unroll
-                for (int m = 0; m < MATS; ++m)
-                    tc::tmem_st16(tbase + lane_base + a_col(st, m) + 16 * hlf, v[m]);
-                tc::wait_st();
-                tc::fence_before_sync();
-                __syncwarp();
-                if (lane == 0) tc::mbar_arrive(&t_full[st]);
-            }
-            if (!ok) break;
-            // Epilogue of this tile: 16 warps, column chunks round-robin over 4 groups.
-            if (!tc::mbar_wait(&acc_full, j & 1, &abort_flag)) break;
+        uint32_t j = 0;
+        for (UnitCursor uc(a, total_units); uc.valid() && !*abortp; uc.advance(), ++j) {
+            const TcSeg &S = uc.cur;
+            const Unit x = unit_of<FMT>(S, uc.u);
+            if (!tc::mbar_wait(&acc_full, j & 1, abortp)) { fail(); break; }
             tc::fence_after_sync();
+            const int grow = x.mt * 128 + row;
             const bool row_ok = grow < S.rows;
-            const int chunks = S.npad / 16;
-            const int per = S.rowsper;
-            for (int c = gid; c < chunks; c += 4) {
-                uint32_t d[2][16];
-#pragma unroll
-                for (int m = 0; m < MATS; ++m) tc::tmem_ld16(tbase + lane_base + acc_col[m] + 16 * c, d[m]);
+            const int tok0 = x.sub * bs_cap(FMT);
+            for (int c = 0; c < x.n / 16; ++c) {
+                uint32_t v0[16], v1[16];
+                tc::tmem_ld16(tbase + lane_base + 16 * c, v0);
+                tc::tmem_ld16(tbase + lane_base + kAccCols + 16 * c, v1);
                 tc::wait_ld();
-                // Column n = 16c + i of the accumulator is activation row n of the segment.
 #pragma unroll
-                for (int i = 0; i < 16; i += 2) {
+                for (int s = 0; s < TPC; ++s) {
+                    const int t = TPC * c + s;
+                    if (t < x.nt && row_ok) {
+                        float o = __uint_as_float(v0[RT * s]) + __uint_as_float(v1[RT * s]);
 #pragma unroll
-                    for (int t2 = 0; t2 < 2; ++t2) {
-                        if (per == 2 && t2 == 1) break;
-                        const int n = 16 * c + i + (per == 2 ? 0 : t2);
-                        const int tok = n / per;
-                        const bool tok_ok = tok < S.ntok;
-                        const int col = S.col_begin + (tok_ok ? tok : 0);
-                        const int srow = a.col_src ? a.col_src[col] : col;
-                        const int shift = tok_ok ? (a.src_shift ? a.src_shift[srow]
-                                                    : (a.src_maxexp[srow] > -1000 ? 14 - a.src_maxexp[srow] : 0))
-                                                 : 0;
-                        float vv[2];
-#pragma unroll
-                        for (int m = 0; m < MATS; ++m) {
-                            const float x0 = __uint_as_float(d[m][i + (per == 2 ? 0 : t2)]);
-                            const float x1 = per == 2 ? __uint_as_float(d[m][i + 1]) : 0.0f;
-                            vv[m] = ldexpf(x0 + x1, e0[m] - shift);
-                        }
-                        float o = vv[0];
-                        if (PAIR) o = silu_f(vv[0]) * vv[MATS - 1];
-                        if (tok_ok && row_ok) a.out[size_t(col) * a.out_stride + grow] = o;
-                        if (PAIR && a.out_maxexp) {
-                            int me = (tok_ok && row_ok && o != 0.0f && isfinite(o)) ? ilogbf(o) : -1000;
-#pragma unroll
-                            for (int off = 16; off > 0; off >>= 1)
-                                me = max(me, __shfl_xor_sync(0xffffffffu, me, off));
-                            if (lane == 0 && me > -1000) atomicMax(a.out_maxexp + col, me);
-                        }
+                        for (int e = 1; e < TT; ++e)
+                            o += __uint_as_float(v0[RT * s + e]) + __uint_as_float(v1[RT * s + e]);
+                        a.out[size_t(S.col_begin + tok0 + t) * a.out_stride + S.out_off + grow] = o;
                     }
                 }
             }
@@ -314,53 +314,170 @@ __global__ void __launch_bounds__(kThreadsTc, 1) k_tc_grouped(TcArgs a) {
     }
 }
 
-// Activation tiles of every segment: rows (token hi [, lo]) x 64 columns per K stage, f16,
-// 128-byte swizzled canonical K-major layout, padded to S.npad rows.  One warp per
-// (segment, stage, 8 rows); grid-stride over all of them.
-__global__ void k_prep_b(TcArgs a, int max_ks) {
-    const int nsegs = *a.nsegs;
-    if (a.status && *a.status) return;
-    const long long total = (long long)nsegs * max_ks * 32;  // (seg, ks, 8-row group) items
-    const int lane = threadIdx.x & 31;
-    for (long long it = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5; it < total;
-         it += (gridDim.x * (long long)blockDim.x) >> 5) {
-        const int rg = int(it % 32), ks = int((it / 32) % max_ks), si = int(it / 32 / max_ks);
-        const TcSeg S = a.segs[si];
-        if (ks >= S.ks || rg * 8 >= S.npad) continue;
-        uint8_t *dst = a.bbuf + S.b_off + size_t(ks) * S.npad * 128;
-        // 32 lanes: 8 rows x 4 lanes, each lane two 16-byte chunks.
-        const int r = rg * 8 + (lane >> 2);
-        for (int jc = (lane & 3); jc < 8; jc += 4) {
-            const int tok = r / S.rowsper, part = r % S.rowsper;
-            uint4 out = make_uint4(0, 0, 0, 0);
-            if (tok < S.ntok) {
-                const int col = S.col_begin + tok;
-                const int srow = a.col_src ? a.col_src[col] : col;
-                const int shift = a.src_shift ? a.src_shift[srow]
-                                              : (a.src_maxexp[srow] > -1000 ? 14 - a.src_maxexp[srow] : 0);
-                const float *p = a.src + size_t(srow) * a.src_stride;
-                const int k0 = ks * 64 + jc * 8;
-                uint32_t h[8];
+// ---- activation terms -------------------------------------------------------------------
+
+// 2^e as a float for -149 <= e <= 127 (exact; subnormal below -126).
+__device__ __forceinline__ float pow2f(int e) {
+    return e >= -126 ? __int_as_float((e + 127) << 23) : __int_as_float(1 << (e + 149));
+}
+
+__device__ __forceinline__ float silu_f(float v) { return v / (1.0f + expf(-v)); }
+
+// Round to nearest (ties to even code) of |v| onto the E2M1 grid {0, .5, 1, 1.5, 2, 3, 4, 6}
+// for |v| <= 6: returns the magnitude code (0..7) and the grid value.
+__device__ __forceinline__ int e2m1_round(float a, float *dq) {
+    float q;
+    int idx;
+    if (a < 2.0f) {
+        q = rintf(a * 2.0f) * 0.5f;  // spacing 0.5; 2.0 lands in the next binade
+    } else if (a < 4.0f) {
+        q = rintf(a);                // spacing 1
+    } else {
+        q = 2.0f * rintf(a * 0.5f);  // spacing 2
+    }
+    if (q < 2.0f) idx = int(q * 2.0f);
+    else if (q < 4.0f) idx = int(q) + 2;
+    else idx = int(q * 0.5f) + 4;
+    *dq = q;
+    return idx;
+}
+
+// Round to nearest even of |v| onto E4M3 (finite, |v| <= 448): magnitude code and value.
+__device__ __forceinline__ int e4m3_round(float a, float *dq) {
+    if (a < 0.015625f) {             // subnormal binade, spacing 2^-9 (m = 8 is 2^-6, code 8)
+        const float m = rintf(a * 512.0f);
+        *dq = m * (1.0f / 512.0f);
+        return int(m);
+    }
+    int k = ilogbf(a);
+    float m = rintf(a * pow2f(3 - k));  // 8..16 steps of 2^(k-3)
+    if (m == 16.0f) { ++k; m = 8.0f; }
+    *dq = m * pow2f(k - 3);
+    return ((k + 7) << 3) | (int(m) - 8);
+}
+
+// One residual term of a 32-value block held by a lane quad (8 values per lane): the E8M0
+// exponent e that fits the block's max|r| into the element range, the element codes of
+// r * 2^-e (round to nearest even) and r -= decode * 2^e (exact).  Every lane of the warp must
+// call it (quad shuffles).  Returns the scale byte; q receives this lane's 8 codes (E2M1: one
+// word, element 0 in the low nibble; E4M3: two words, element 0 in the low byte).
+template <int FMT>
+__device__ __forceinline__ int make_term8(float *r, uint32_t *q) {
+    float m = 0.0f;
 #pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    const float x = k0 + i < S.cols ? ldexpf(p[k0 + i], shift) : 0.0f;
-                    __half hi = __float2half_rn(x);
-                    __half v = part ? __float2half_rn(x - __half2float(hi)) : hi;
-                    h[i] = __half_as_ushort(v);
-                }
-                out = make_uint4(h[0] | (h[1] << 16), h[2] | (h[3] << 16), h[4] | (h[5] << 16),
-                                 h[6] | (h[7] << 16));
+    for (int i = 0; i < 8; ++i) m = fmaxf(m, fabsf(r[i]));
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
+    q[0] = 0;
+    if (FMT == URB_FMT_MXFP8) q[1] = 0;
+    if (m == 0.0f) return 0;
+    const int e0 = ilogbf(m);
+    // Largest element magnitude: 6 = 1.5 * 2^2 (E2M1), 448 = 1.75 * 2^8 (E4M3).
+    int e = FMT == URB_FMT_MXFP4 ? (m <= 1.5f * pow2f(e0) ? e0 - 2 : e0 - 1)
+                                 : (m <= 1.75f * pow2f(e0) ? e0 - 8 : e0 - 7);
+    e = max(-127, min(127, e));
+    const float inv = pow2f(-e), sc = pow2f(e);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const float v = r[i] * inv;
+        float dq;
+        if (FMT == URB_FMT_MXFP4) {
+            int code = e2m1_round(fabsf(v), &dq);
+            if (v < 0.0f && code) code |= 8;
+            q[0] |= uint32_t(code) << (4 * i);
+        } else {
+            int code = e4m3_round(fabsf(v), &dq);
+            if (v < 0.0f && code) code |= 0x80;
+            q[i >> 2] |= uint32_t(code) << (8 * (i & 3));
+        }
+        r[i] -= copysignf(dq, v) * sc;
+    }
+    return e + 127;
+}
+
+// Activation stages.  A lane quad per (source row, 32-column block), 8 columns per lane:
+// loads the block (x, or h = silu(gate) * up), builds the residual terms once and writes them
+// into every activation column that uses the row (gate/up: the token's routed positions and
+// the shared expert's column), as MMA rows slot * rows_per_tok + term of the column's
+// sub-segment (payload 128-byte swizzled, scale bytes in the tcgen05.cp chunk layout).  MMA rows
+// past a token's terms and slots past a sub-segment's tokens are never read by the epilogue
+// and stay unwritten.
+template <int FMT>
+__global__ void __launch_bounds__(256) k_bs_prep(TcArgs a) {
+    constexpr int KBS = FMT == URB_FMT_MXFP4 ? 8 : 4;  // 32-column blocks per stage
+    constexpr int QW = FMT == URB_FMT_MXFP4 ? 1 : 2;   // code words per lane per term
+    constexpr int RT = bs_rows_per_tok(FMT), TT = bs_terms(FMT);
+    __shared__ int skip;
+    if (threadIdx.x == 0) skip = (a.status && *a.status) ? 1 : 0;
+    __syncthreads();
+    if (skip) return;
+    const long long tid = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+    const long long item = tid >> 2;
+    const int part = int(tid & 3);
+    const int nkb = a.ks * KBS;
+    const bool valid = item < (long long)a.nrows * nkb;
+    const int row = valid ? int(item / nkb) : 0, kb = valid ? int(item % nkb) : 0;
+    float r[8];
+    const int c0 = kb * 32 + part * 8;
+    bool bad = false;
+    if (valid) {
+        const float *p = a.src + size_t(row) * a.src_stride;
+        if (!a.swiglu && (a.src_stride & 3) == 0 && c0 + 8 <= a.cols) {
+            const float4 v0 = *reinterpret_cast<const float4 *>(p + c0);
+            const float4 v1 = *reinterpret_cast<const float4 *>(p + c0 + 4);
+            r[0] = v0.x; r[1] = v0.y; r[2] = v0.z; r[3] = v0.w;
+            r[4] = v1.x; r[5] = v1.y; r[6] = v1.z; r[7] = v1.w;
+        } else {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const int c = c0 + i;
+                float v = 0.0f;
+                if (c < a.cols) v = a.swiglu ? silu_f(p[c]) * p[a.cols + c] : p[c];
+                r[i] = v;
             }
-            *reinterpret_cast<uint4 *>(dst + r * 128 + ((jc ^ (r & 7)) << 4)) = out;
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) bad |= !isfinite(r[i]);
+        if (bad) set_status(a.status, URB_ERR_NONFINITE);
+    }
+    if (!valid || bad) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) r[i] = 0.0f;
+    }
+    uint32_t q[TT][QW];
+    int sb[TT];
+#pragma unroll
+    for (int t = 0; t < TT; ++t) sb[t] = make_term8<FMT>(r, q[t]);
+    if (!valid) return;
+    const int ks = kb / KBS, kbs = kb % KBS;
+    const int ndst = a.inv ? a.top_k + (a.shared_col0 >= 0 ? 1 : 0) : 1;
+    for (int d = 0; d < ndst; ++d) {
+        const int col = a.inv ? (d < a.top_k ? a.inv[row * a.top_k + d] : a.shared_col0 + row) : row;
+        const BsSlot S = a.slots[col];
+        uint8_t *stage = a.bbuf + S.base + (long long)ks * bs_bstage_bytes(FMT, S.n);
+#pragma unroll
+        for (int t = 0; t < TT; ++t) {
+            const int R = S.slot * RT + t;  // MMA row within the stage
+            uint8_t *rowp = stage + (R >> 3) * 1024 + (R & 7) * 128;
+            if (FMT == URB_FMT_MXFP4) {
+                *reinterpret_cast<uint32_t *>(rowp + ((kbs ^ (R & 7)) << 4) + 4 * part) = q[t][0];
+            } else {
+                const int ch = 2 * kbs + (part >> 1);
+                *reinterpret_cast<uint2 *>(rowp + ((ch ^ (R & 7)) << 4) + 8 * (part & 1)) =
+                    make_uint2(q[t][0], q[t][QW - 1]);
+            }
+            if (part == 0)
+                stage[S.n * 128 + 512 * (kbs >> 2) + 16 * (R & 31) + 4 * (R >> 5) + (kbs & 3)] = uint8_t(sb[t]);
         }
     }
 }
 
-// Repack of the reference layout into the tc layout (one thread per (tile, row)).
+// Repack of the reference layout into the bs layout.  One thread per (tile, row): 128 payload
+// bytes (swizzled 16-byte chunks) and the row's scale bytes.
 template <int FMT>
-__global__ void k_repack_tc(const uint8_t *values, const uint8_t *scales, size_t rows,
-                            size_t cols, size_t scale_cols, size_t block_rows,
-                            size_t block_cols, int mts, int ks_n, uint8_t *out) {
+__global__ void k_repack_bs(const uint8_t *values, const uint8_t *scales, size_t rows, size_t cols,
+                            size_t scale_cols, size_t block_rows, size_t block_cols, int mts,
+                            int ks_n, uint8_t *out) {
     const size_t id = blockIdx.x * size_t(blockDim.x) + threadIdx.x;
     if (id >= size_t(mts) * ks_n * 128) return;
     const int r = int(id & 127);
@@ -368,86 +485,82 @@ __global__ void k_repack_tc(const uint8_t *values, const uint8_t *scales, size_t
     const int ks = int(tile % ks_n);
     const size_t mt = tile / ks_n;
     const size_t row = mt * 128 + r;
-    constexpr int TB = tc_tile_bytes(FMT);
+    constexpr int TB = bs_tile_bytes(FMT);
+    constexpr int KBS = FMT == URB_FMT_MXFP4 ? 8 : 4;
     uint8_t *t = out + tile * TB;
-    const size_t c0 = size_t(ks) * 64;
-    if (FMT == URB_FMT_MXFP4) {
-        const size_t row_bytes = (cols + 1) / 2;
-        for (int ch = 0; ch < 2; ++ch)
-            for (int b = 0; b < 16; ++b) {
-                const size_t c = c0 + ch * 32 + 2 * b;
-                uint8_t lo = 0, hi = 0;
+    uint8_t *rowp = t + (r >> 3) * 1024 + (r & 7) * 128;
+    const size_t c0 = size_t(ks) * bs_stage_cols(FMT);
+    for (int ch = 0; ch < 8; ++ch) {
+        uint32_t wv[4] = {0, 0, 0, 0};
+        for (int i = 0; i < 16; ++i) {
+            const int byte = ch * 16 + i;
+            uint32_t b;
+            if (FMT == URB_FMT_MXFP4) {
+                const size_t c = c0 + 2 * byte;
+                const size_t row_bytes = (cols + 1) / 2;
+                uint32_t lo = 0, hi = 0;
                 if (row < rows && c < cols) lo = values[row * row_bytes + c / 2] & 0x0f;
                 if (row < rows && c + 1 < cols) hi = values[row * row_bytes + c / 2] >> 4;
-                t[ch * 2048 + r * 16 + b] = uint8_t(lo | (hi << 4));
+                b = lo | (hi << 4);
+            } else {
+                const size_t c = c0 + byte;
+                b = (row < rows && c < cols) ? values[row * cols + c] : 0;
             }
-        for (int h = 0; h < 2; ++h) {
-            const size_t c = c0 + 32 * h;
-            t[TB - 256 + 2 * r + h] = (row < rows && c < cols) ? scales[row * scale_cols + c / 32] : 127;
+            wv[i >> 2] |= b << (8 * (i & 3));
         }
-    } else {
-        for (int ch = 0; ch < 4; ++ch)
-            for (int b = 0; b < 16; ++b) {
-                const size_t c = c0 + ch * 16 + b;
-                t[ch * 2048 + r * 16 + b] = (row < rows && c < cols) ? values[row * cols + c] : 0;
-            }
-        for (int h = 0; h < 2; ++h) {
-            const size_t c = c0 + 32 * h;
-            t[TB - 256 + 2 * r + h] =
-                (row < rows && c < cols) ? scales[(row / block_rows) * scale_cols + c / block_cols] : 127;
-        }
+        *reinterpret_cast<uint4 *>(rowp + ((ch ^ (r & 7)) << 4)) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+    }
+    for (int kb = 0; kb < KBS; ++kb) {
+        const size_t c = c0 + 32 * size_t(kb);
+        uint8_t s = 127;
+        if (row < rows && c < cols)
+            s = FMT == URB_FMT_MXFP4 ? scales[row * scale_cols + c / 32]
+                                     : scales[(row / block_rows) * scale_cols + c / block_cols];
+        t[16384 + 512 * (kb >> 2) + 16 * (r & 31) + 4 * (r >> 5) + (kb & 3)] = s;
     }
 }
 
-template <int FMT, bool PAIR>
-int launch_tc_t(Ctx *ctx, const TcArgs &a, cudaStream_t st) {
-    constexpr int MATS = PAIR ? 2 : 1;
-    const size_t tba = (size_t(MATS) * tc_tile_bytes(FMT) + 1023) / 1024 * 1024;
-    const size_t budget = 220 * 1024, bring = kStagesB * size_t(a.nmax) * 128 + 1024;
-    if (bring + 3 * tba > budget) return set_error(ctx, URB_ERR_UNSUPPORTED, "tc pass: shared memory");
-    TcArgs args = a;
-    args.stages_a = int(std::min<size_t>(kStagesAMax, (budget - bring) / tba));
-    // At least 116 KB so that exactly one CTA (and one 512-column TMEM allocation) fits per SM.
-    const size_t smem = std::max<size_t>(116 * 1024, bring + args.stages_a * tba);
-    auto k = k_tc_grouped<FMT, PAIR>;
-    URB_CUDA(ctx, cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
-    k<<<ctx->num_sms, kThreadsTc, smem, st>>>(args);
+template <int FMT>
+int launch_bs_t(Ctx *ctx, const TcArgs &a, cudaStream_t st) {
+    constexpr int KBS = FMT == URB_FMT_MXFP4 ? 8 : 4;
+    const long long threads = (long long)a.nrows * a.ks * KBS * 4;
+    if (threads > 0) {
+        k_bs_prep<FMT><<<unsigned((threads + 255) / 256), 256, 0, st>>>(a);
+        URB_CUDA(ctx, cudaGetLastError());
+    }
+    auto k = k_bs_grouped<FMT>;
+    URB_CUDA(ctx, cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBs));
+    k<<<ctx->num_sms, kThreadsBs, kSmemBs, st>>>(a);
     URB_CUDA(ctx, cudaGetLastError());
     return URB_OK;
 }
 
 }  // namespace
 
-int launch_tc_grouped(Ctx *ctx, int fmt, bool pair, const TcArgs &a, int max_segs, int max_ks,
-                      cudaStream_t st) {
-    if (a.nmax > (pair ? 128 : 256) || a.nmax % 16)
-        return set_error(ctx, URB_ERR_UNSUPPORTED, "tc pass: N out of range");
-    (void)max_segs;
-    k_prep_b<<<ctx->num_sms * 8, 256, 0, st>>>(a, max_ks);
-    URB_CUDA(ctx, cudaGetLastError());
-    if (fmt == URB_FMT_MXFP4) return pair ? launch_tc_t<URB_FMT_MXFP4, true>(ctx, a, st)
-                                          : launch_tc_t<URB_FMT_MXFP4, false>(ctx, a, st);
-    if (fmt == URB_FMT_MXFP8) return pair ? launch_tc_t<URB_FMT_MXFP8, true>(ctx, a, st)
-                                          : launch_tc_t<URB_FMT_MXFP8, false>(ctx, a, st);
+int launch_tc_grouped(Ctx *ctx, int fmt, const TcArgs &a, cudaStream_t st) {
+    if (fmt == URB_FMT_MXFP4) return launch_bs_t<URB_FMT_MXFP4>(ctx, a, st);
+    if (fmt == URB_FMT_MXFP8) return launch_bs_t<URB_FMT_MXFP8>(ctx, a, st);
     return set_error(ctx, URB_ERR_UNSUPPORTED, "tc pass: format");
 }
 
 int repack_tc(Ctx *ctx, Mat *m, cudaStream_t st) {
-    if (m->format != URB_FMT_MXFP4 && m->format != URB_FMT_MXFP8) return URB_OK;
+    const bool ok = (m->format == URB_FMT_MXFP4 && m->group_size == 32) ||
+                    (m->format == URB_FMT_MXFP8 && m->block_cols % 32 == 0);
+    if (!ok) return URB_OK;
     m->tc_mts = int((m->rows + 127) / 128);
-    m->tc_ks = int((m->cols + 63) / 64);
-    const int TB = tc_tile_bytes(m->format);
+    m->tc_ks = int((m->cols + bs_stage_cols(m->format) - 1) / bs_stage_cols(m->format));
+    const int TB = bs_tile_bytes(m->format);
     URB_CUDA(ctx, cudaMallocAsync((void **)&m->tc_tiles, size_t(m->tc_mts) * m->tc_ks * TB, st));
     const size_t threads = size_t(m->tc_mts) * m->tc_ks * 128;
     const unsigned blocks = unsigned((threads + 255) / 256);
     const uint8_t *v = static_cast<const uint8_t *>(m->raw_values);
     if (m->format == URB_FMT_MXFP4) {
         const size_t sc = (m->cols + m->group_size - 1) / m->group_size;
-        k_repack_tc<URB_FMT_MXFP4><<<blocks, 256, 0, st>>>(v, m->raw_scales, m->rows, m->cols, sc,
+        k_repack_bs<URB_FMT_MXFP4><<<blocks, 256, 0, st>>>(v, m->raw_scales, m->rows, m->cols, sc,
                                                           1, 32, m->tc_mts, m->tc_ks, m->tc_tiles);
     } else {
         const size_t sc = (m->cols + m->block_cols - 1) / m->block_cols;
-        k_repack_tc<URB_FMT_MXFP8><<<blocks, 256, 0, st>>>(v, m->raw_scales, m->rows, m->cols, sc,
+        k_repack_bs<URB_FMT_MXFP8><<<blocks, 256, 0, st>>>(v, m->raw_scales, m->rows, m->cols, sc,
                                                           m->block_rows, m->block_cols, m->tc_mts,
                                                           m->tc_ks, m->tc_tiles);
     }

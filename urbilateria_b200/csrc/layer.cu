@@ -33,9 +33,19 @@ size_t max_segments(size_t tokens, size_t K, size_t experts) {
     return std::min(TK, experts) + TK / kCap + div_ceil(tokens, kCap) + 2;
 }
 
-size_t max_tc_segments(size_t tokens, size_t K, size_t experts) {
-    size_t TK = tokens * K;
-    return std::min(TK, experts) + TK / kTcCapGu + div_ceil(tokens, kTcCapGu) + 2;
+// Upper bound of the work units of one tensor-core pass (mts 128-row tiles per sub-segment).
+size_t max_bs_units(int fmt, size_t tokens, size_t K, size_t experts, size_t mts) {
+    const size_t TK = tokens * K, cap = size_t(bs_cap(fmt));
+    return mts * (TK / cap + std::min(TK, experts) + div_ceil(tokens, cap) + 1);
+}
+
+// Upper bound of the activation-stage bytes of one tensor-core pass: every sub-segment at the
+// full MMA N (routed: at most TK / cap full ones plus one partial per expert; shared: T tokens).
+size_t max_bs_bytes(int fmt, size_t tokens, size_t K, size_t experts, size_t ks) {
+    const size_t TK = tokens * K;
+    const size_t cap = size_t(bs_cap(fmt));
+    const size_t subs = TK / cap + std::min(TK, experts) + div_ceil(tokens, cap) + 1;
+    return subs * ks * size_t(bs_bstage_bytes(fmt, kBsNmax));
 }
 
 }  // namespace
@@ -71,15 +81,20 @@ int moe_forward_device(Layer *L, const float *d_x, int T, float *d_out, MoeWork 
     w.h = cv.take<float>(cols * I);
     w.y = cv.take<float>(cols * H);
     w.lofree = cv.take<int32_t>(1);
-    const size_t ntseg = max_tc_segments(T, K, E);
-    const size_t ks_gu = div_ceil(H, 64), ks_dn = div_ceil(I, 64);
-    const size_t npad_sum = 2 * cols + 16 * ntseg;
+    const size_t ngrp_gu = 2 * std::min(TK, E) + 2, ngrp_dn = std::min(TK, E) + 1;
+    const size_t sc = size_t(bs_stage_cols(L->fmt));
+    const size_t ks_gu = div_ceil(H, sc), ks_dn = div_ceil(I, sc);
     if (L->use_tc) {
-        w.tsegs_gu = cv.take<TcSeg>(ntseg);
-        w.tsegs_dn = cv.take<TcSeg>(ntseg);
+        w.gu = cv.take<float>(cols * 2 * I);
+        w.tsegs_gu = cv.take<TcSeg>(ngrp_gu);
+        w.tsegs_dn = cv.take<TcSeg>(ngrp_dn);
+        w.bslots_gu = cv.take<BsSlot>(cols);
+        w.bslots_dn = cv.take<BsSlot>(cols);
+        w.units_gu = cv.take<int>(max_bs_units(L->fmt, T, K, E, 2 * div_ceil(I, 128)));
+        w.units_dn = cv.take<int>(max_bs_units(L->fmt, T, K, E, div_ceil(H, 128)));
         w.tscalars = cv.take<int>(4);
-        w.bbuf_gu = cv.take<uint8_t>(ks_gu * 128 * npad_sum + 1024);
-        w.bbuf_dn = cv.take<uint8_t>(ks_dn * 128 * npad_sum + 1024);
+        w.bbuf_gu = cv.take<uint8_t>(max_bs_bytes(L->fmt, T, K, E, ks_gu));
+        w.bbuf_dn = cv.take<uint8_t>(max_bs_bytes(L->fmt, T, K, E, ks_dn));
     }
     if (cv.off > ctx->ws_size) {
         // Grow to the exact size of this forward (nothing has been enqueued yet) and restart.
@@ -155,66 +170,77 @@ int moe_forward_device(Layer *L, const float *d_x, int T, float *d_out, MoeWork 
         TcBuildArgs bb{};
         bb.counts = w.counts;
         bb.offsets = w.offsets;
-        bb.lofree = w.lofree;
+        bb.fmt = L->fmt;
         bb.tokens = T;
         bb.top_k = int(K);
         bb.experts = int(E);
         bb.gate_tc = reinterpret_cast<const uint8_t *const *>(tb + 6 * E);
         bb.up_tc = reinterpret_cast<const uint8_t *const *>(tb + 7 * E);
         bb.down_tc = reinterpret_cast<const uint8_t *const *>(tb + 8 * E);
-        bb.gate_rexp = p.gate_rexp;
-        bb.up_rexp = p.up_rexp;
-        bb.down_rexp = p.down_rexp;
         bb.has_shared = L->sg ? 1 : 0;
         if (L->sg) {
-            bb.sh_gate_tc = L->sg->tc_tiles; bb.sh_gate_rexp = L->sg->row_exp;
-            bb.sh_up_tc = L->su->tc_tiles; bb.sh_up_rexp = L->su->row_exp;
-            bb.sh_down_tc = L->sd->tc_tiles; bb.sh_down_rexp = L->sd->row_exp;
+            bb.sh_gate_tc = L->sg->tc_tiles;
+            bb.sh_up_tc = L->su->tc_tiles;
+            bb.sh_down_tc = L->sd->tc_tiles;
         }
         bb.hidden = int(H);
         bb.inter = int(I);
         bb.gu = w.tsegs_gu;
         bb.dn = w.tsegs_dn;
+        bb.gu_slots = w.bslots_gu;
+        bb.dn_slots = w.bslots_dn;
+        bb.gu_units = w.units_gu;
+        bb.dn_units = w.units_dn;
         bb.scalars = w.tscalars;
         bb.status = d_status;
         rc = launch_build_tc_segs(ctx, bb, st);
         if (rc) return rc;
 
+        // Gate and up projections of every (expert, token) column: [cols, 2I] gate | up.
         TcArgs ga{};
         ga.segs = w.tsegs_gu;
         ga.nsegs = w.tscalars;
         ga.total_units = w.tscalars + 1;
-        ga.nmax = 128;
+        ga.unit_group = w.units_gu;
         ga.bbuf = w.bbuf_gu;
         ga.src = d_x;
         ga.src_stride = int(H);
-        ga.col_src = w.col_src;
-        ga.src_shift = w.shift;
-        ga.out = w.h;
-        ga.out_stride = int(I);
-        ga.out_maxexp = w.maxexp;
+        ga.nrows = T;
+        ga.cols = int(H);
+        ga.ks = int(ks_gu);
+        ga.swiglu = 0;
+        ga.inv = w.inv;
+        ga.top_k = int(K);
+        ga.shared_col0 = L->sg ? int(TK) : -1;
+        ga.slots = w.bslots_gu;
+        ga.out = w.gu;
+        ga.out_stride = int(2 * I);
         ga.status = d_status;
         prof_begin(ctx, URB_K_GATE_UP, st);
-        rc = launch_tc_grouped(ctx, L->fmt, true, ga, int(ntseg), int(ks_gu), st);
+        rc = launch_tc_grouped(ctx, L->fmt, ga, st);
         prof_end(ctx, st);
         if (rc) return rc;
 
+        // Down projection of h = silu(gate) * up (formed while writing its activation terms).
         TcArgs da{};
         da.segs = w.tsegs_dn;
         da.nsegs = w.tscalars + 2;
         da.total_units = w.tscalars + 3;
-        da.nmax = 256;
+        da.unit_group = w.units_dn;
         da.bbuf = w.bbuf_dn;
-        da.src = w.h;
-        da.src_stride = int(I);
-        da.col_src = nullptr;
-        da.src_shift = nullptr;
-        da.src_maxexp = w.maxexp;
+        da.src = w.gu;
+        da.src_stride = int(2 * I);
+        da.nrows = int(L->sg ? TK + T : TK);
+        da.cols = int(I);
+        da.ks = int(ks_dn);
+        da.swiglu = 1;
+        da.inv = nullptr;
+        da.slots = w.bslots_dn;
         da.out = w.y;
         da.out_stride = int(H);
         da.status = d_status;
         prof_begin(ctx, URB_K_DOWN, st);
-        rc = launch_tc_grouped(ctx, L->fmt, false, da, int(ntseg), int(ks_dn), st);
+        rc = launch_tc_grouped(ctx, L->fmt, da, st);
         prof_end(ctx, st);
         if (rc) return rc;
 
@@ -418,8 +444,12 @@ int urb_moe_layer_create(urb_ctx *ctx, const urb_mat *router, const float *bias,
         tables[8 * experts + e] = down[e]->tc_tiles;
     }
     const char *path = std::getenv("URB_MOE_PATH");
-    L->use_tc = (fmt == URB_FMT_MXFP4 || fmt == URB_FMT_MXFP8) &&
-                !(path && std::strcmp(path, "mma") == 0);
+    bool have_tc = fmt == URB_FMT_MXFP4 || fmt == URB_FMT_MXFP8;
+    for (size_t e = 0; e < experts && have_tc; ++e)
+        have_tc = gate[e]->tc_tiles && up[e]->tc_tiles && down[e]->tc_tiles;
+    if (L->sg) have_tc = have_tc && L->sg->tc_tiles && L->su->tc_tiles && L->sd->tc_tiles;
+    // Block-scaled tcgen05 passes by default; URB_MOE_PATH=mma selects the mma.sync passes.
+    L->use_tc = have_tc && !(path && std::strcmp(path, "mma") == 0);
     cudaError_t err = cudaMalloc(&L->d_tables, tables.size() * sizeof(void *));
     if (err == cudaSuccess) err = cudaMalloc(&L->d_bias, experts * 4);
     if (err == cudaSuccess)

@@ -196,113 +196,135 @@ __global__ void k_combine(const float *y, const float *shared_y, const float *w,
     out[size_t(t) * hidden + h] = float(acc);
 }
 
-// Segments of the tensor-core passes (single CTA).  Routed experts ascending, each cut into
-// chunks (gate/up: 64 tokens, or 128 when every activation is exact in one f16 column;
-// down: 128 tokens with hi/lo columns), then the shared expert.  Activation-tile offsets are a
-// prefix over segments of ks * npad * 128 bytes.
+// Groups of the tensor-core passes (single CTA).  Gate/up pass: per routed expert with tokens
+// a gate group (which owns the activation stages) and an up group reading the same stages,
+// then the shared expert's pair; down pass: one group per routed expert, then the shared
+// expert.  A group of c tokens has ceil(c / bs_cap) sub-segments; its units are mts * nsub.
+// Activation-stage offsets are a prefix over owning groups of the bytes their stages take.
 __device__ __forceinline__ int round16(int x) { return (x + 15) & ~15; }
 
+// Bytes of the activation stages of a group of c tokens and ks stages.
+__device__ __forceinline__ long long bs_group_bytes(int fmt, int c, int ks) {
+    const int cap = bs_cap(fmt);
+    const int nsub = (c + cap - 1) / cap;
+    const int n_last = round16(bs_rows_per_tok(fmt) * (c - (nsub - 1) * cap));
+    return (long long)ks * ((long long)(nsub - 1) * bs_bstage_bytes(fmt, kBsNmax) + bs_bstage_bytes(fmt, n_last));
+}
+
 __global__ void __launch_bounds__(1024) k_build_tc_segs(TcBuildArgs b) {
-    __shared__ long long wsum[2][32];
-    __shared__ int wcnt[2][32];
+    __shared__ long long wsum[32];
+    __shared__ int wcnt[32], wunits[32];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     if (b.status && *b.status) {  // an earlier stage failed: no work for the passes
         if (tid < 4) b.scalars[tid] = 0;
         return;
     }
     const int E = b.experts, TK = b.tokens * b.top_k;
-    const bool lofree = b.lofree && *b.lofree;
-    const int cap[2] = {lofree ? 2 * kTcCapGu : kTcCapGu, kTcCapDn};
-    const int per[2] = {lofree ? 1 : 2, 2};
-    const int ksz[2] = {(b.hidden + 63) / 64, (b.inter + 63) / 64};
-    const int mts[2] = {(b.inter + 127) / 128, (b.hidden + 127) / 128};
+    const int sc = bs_stage_cols(b.fmt);
     for (int pass = 0; pass < 2; ++pass) {
-        // Per thread: experts [e0, e1); count segments and B bytes.
+        const int mats = pass == 0 ? 2 : 1;  // groups per expert
+        const int ks = pass == 0 ? (b.hidden + sc - 1) / sc : (b.inter + sc - 1) / sc;
+        const int mts = pass == 0 ? (b.inter + 127) / 128 : (b.hidden + 127) / 128;
+        // Per thread: experts [e0, e1); groups, units and activation bytes.
         const int per_thr = (E + 1023) / 1024;
-        const int e0 = tid * per_thr, e1 = min(E, e0 + per_thr);
-        int nseg = 0;
-        long long bytes = 0;
-        for (int e = e0; e < e1; ++e)
-            for (int j = 0; j * cap[pass] < b.counts[e]; ++j) {
-                const int nt = min(cap[pass], b.counts[e] - j * cap[pass]);
-                ++nseg;
-                bytes += (long long)ksz[pass] * round16(nt * per[pass]) * 128;
-            }
-        // Block-wide exclusive scans of (nseg, bytes).
-        int iseg = nseg;
-        long long ib = bytes;
+        const int e0 = min(E, tid * per_thr), e1 = min(E, e0 + per_thr);
+        int ng = 0, nu = 0;
+        long long nb = 0;
+        for (int e = e0; e < e1; ++e) {
+            const int c = b.counts[e];
+            if (c <= 0) continue;
+            ng += mats;
+            nu += mats * mts * ((c + bs_cap(b.fmt) - 1) / bs_cap(b.fmt));
+            nb += bs_group_bytes(b.fmt, c, ks);
+        }
+        // Block-wide exclusive scans of (groups, units, bytes).
+        int ig = ng, iu = nu;
+        long long ib = nb;
         for (int o = 1; o < 32; o <<= 1) {
-            int v = __shfl_up_sync(0xffffffffu, iseg, o);
-            long long w = __shfl_up_sync(0xffffffffu, ib, o);
-            if (lane >= o) { iseg += v; ib += w; }
+            const int v = __shfl_up_sync(0xffffffffu, ig, o);
+            const int vu = __shfl_up_sync(0xffffffffu, iu, o);
+            const long long w = __shfl_up_sync(0xffffffffu, ib, o);
+            if (lane >= o) { ig += v; iu += vu; ib += w; }
         }
         __syncthreads();
-        if (lane == 31) { wcnt[pass][warp] = iseg; wsum[pass][warp] = ib; }
+        if (lane == 31) { wcnt[warp] = ig; wunits[warp] = iu; wsum[warp] = ib; }
         __syncthreads();
         if (warp == 0) {
-            int v = wcnt[pass][lane];
-            long long w = wsum[pass][lane];
+            int v = wcnt[lane], vu = wunits[lane];
+            long long w = wsum[lane];
             for (int o = 1; o < 32; o <<= 1) {
-                int v2 = __shfl_up_sync(0xffffffffu, v, o);
-                long long w2 = __shfl_up_sync(0xffffffffu, w, o);
-                if (lane >= o) { v += v2; w += w2; }
+                const int v2 = __shfl_up_sync(0xffffffffu, v, o);
+                const int vu2 = __shfl_up_sync(0xffffffffu, vu, o);
+                const long long w2 = __shfl_up_sync(0xffffffffu, w, o);
+                if (lane >= o) { v += v2; vu += vu2; w += w2; }
             }
-            wcnt[pass][lane] = v;
-            wsum[pass][lane] = w;
+            wcnt[lane] = v;
+            wunits[lane] = vu;
+            wsum[lane] = w;
         }
         __syncthreads();
-        int sidx = iseg - nseg + (warp ? wcnt[pass][warp - 1] : 0);
-        long long boff = ib - bytes + (warp ? wsum[pass][warp - 1] : 0);
+        int gi = ig - ng + (warp ? wcnt[warp - 1] : 0);
+        int ub = iu - nu + (warp ? wunits[warp - 1] : 0);
+        long long boff = ib - nb + (warp ? wsum[warp - 1] : 0);
         TcSeg *out = pass == 0 ? b.gu : b.dn;
-        for (int e = e0; e < e1; ++e) {
-            int col0 = b.offsets[e];
-            for (int j = 0; j * cap[pass] < b.counts[e]; ++j, ++sidx) {
-                TcSeg s;
-                const int nt = min(cap[pass], b.counts[e] - j * cap[pass]);
-                if (pass == 0) {
-                    s.a = b.gate_tc[e]; s.b = b.up_tc[e]; s.ra = b.gate_rexp[e]; s.rb = b.up_rexp[e];
-                    s.rows = b.inter; s.cols = b.hidden;
-                } else {
-                    s.a = b.down_tc[e]; s.b = nullptr; s.ra = b.down_rexp[e]; s.rb = nullptr;
-                    s.rows = b.hidden; s.cols = b.inter;
+        auto emit = [&](const uint8_t *wg, int m, int col0, int c) {
+            TcSeg s;
+            s.w = wg;
+            s.b_off = boff;
+            s.mts = mts;
+            s.ks = ks;
+            s.rows = pass == 0 ? b.inter : b.hidden;
+            s.cols = pass == 0 ? b.hidden : b.inter;
+            s.col_begin = col0;
+            s.ntok = c;
+            s.nsub = (c + bs_cap(b.fmt) - 1) / bs_cap(b.fmt);
+            s.unit_begin = ub;
+            s.out_off = m * b.inter;  // gate | up halves of a gate/up output row
+            s.pad = 0;
+            int *um = pass == 0 ? b.gu_units : b.dn_units;
+            for (int r = 0; r < mts * s.nsub; ++r) um[ub + r] = gi;
+            out[gi++] = s;
+            ub += mts * s.nsub;
+            if (m == 0) {
+                // Activation slots of the group's columns (the up group reads the same stages).
+                BsSlot *sl = pass == 0 ? b.gu_slots : b.dn_slots;
+                const int cap = bs_cap(b.fmt);
+                const long long sub_bytes = (long long)ks * bs_bstage_bytes(b.fmt, kBsNmax);
+                const int n_last = round16(bs_rows_per_tok(b.fmt) * (c - (s.nsub - 1) * cap));
+                for (int j = 0; j < c; ++j) {
+                    const int sub = j / cap;
+                    BsSlot z;
+                    z.base = boff + sub * sub_bytes;
+                    z.slot = j - sub * cap;
+                    z.n = sub < s.nsub - 1 ? kBsNmax : n_last;
+                    sl[col0 + j] = z;
                 }
-                s.mts = mts[pass]; s.ks = ksz[pass];
-                s.col_begin = col0 + j * cap[pass]; s.ntok = nt;
-                s.rowsper = per[pass]; s.npad = round16(nt * per[pass]);
-                s.unit_begin = sidx * mts[pass];
-                s.b_off = boff;
-                s.pad = e;
-                boff += (long long)s.ks * s.npad * 128;
-                out[sidx] = s;
             }
+        };
+        for (int e = e0; e < e1; ++e) {
+            const int c = b.counts[e];
+            if (c <= 0) continue;
+            if (pass == 0) {
+                emit(b.gate_tc[e], 0, b.offsets[e], c);
+                emit(b.up_tc[e], 1, b.offsets[e], c);
+            } else {
+                emit(b.down_tc[e], 0, b.offsets[e], c);
+            }
+            boff += bs_group_bytes(b.fmt, c, ks);
         }
         __syncthreads();
         if (tid == 1023) {
-            // sidx / boff of the last thread are the routed totals; append the shared expert.
-            int n = sidx;
-            if (b.has_shared) {
-                for (int j = 0; j * cap[pass] < b.tokens; ++j, ++n) {
-                    TcSeg s;
-                    const int nt = min(cap[pass], b.tokens - j * cap[pass]);
-                    if (pass == 0) {
-                        s.a = b.sh_gate_tc; s.b = b.sh_up_tc; s.ra = b.sh_gate_rexp; s.rb = b.sh_up_rexp;
-                        s.rows = b.inter; s.cols = b.hidden;
-                    } else {
-                        s.a = b.sh_down_tc; s.b = nullptr; s.ra = b.sh_down_rexp; s.rb = nullptr;
-                        s.rows = b.hidden; s.cols = b.inter;
-                    }
-                    s.mts = mts[pass]; s.ks = ksz[pass];
-                    s.col_begin = TK + j * cap[pass]; s.ntok = nt;
-                    s.rowsper = per[pass]; s.npad = round16(nt * per[pass]);
-                    s.unit_begin = n * mts[pass];
-                    s.b_off = boff;
-                    s.pad = -1;
-                    boff += (long long)s.ks * s.npad * 128;
-                    out[n] = s;
+            // gi / ub / boff of the last thread are the routed totals; append the shared expert.
+            if (b.has_shared && b.tokens > 0) {
+                if (pass == 0) {
+                    emit(b.sh_gate_tc, 0, TK, b.tokens);
+                    emit(b.sh_up_tc, 1, TK, b.tokens);
+                } else {
+                    emit(b.sh_down_tc, 0, TK, b.tokens);
                 }
             }
-            b.scalars[2 * pass] = n;
-            b.scalars[2 * pass + 1] = n * mts[pass];
+            b.scalars[2 * pass] = gi;
+            b.scalars[2 * pass + 1] = ub;
         }
         __syncthreads();
     }

@@ -144,5 +144,54 @@ __device__ __forceinline__ uint64_t sdesc_sw128(uint32_t smem_addr) {
     return d;
 }
 
+// ---- block-scaled MMA (MX formats) ----------------------------------------------------------
+
+// Descriptor of a 512-byte scale-factor chunk for tcgen05.cp.32x128b: 32 rows of 16 B,
+// no swizzle, 8-row core matrices 128 B apart.
+__device__ __forceinline__ uint64_t sdesc_sf(uint32_t smem_addr) {
+    uint64_t d = 0;
+    d |= uint64_t((smem_addr & 0x3FFFF) >> 4);
+    d |= uint64_t(128 >> 4) << 16;
+    d |= uint64_t(128 >> 4) << 32;
+    d |= uint64_t(1) << 46;
+    return d;
+}
+
+// Copies a 512-byte scale chunk (row l: 16 bytes) into TMEM columns [col, col+4) of lane l,
+// replicated into all four 32-lane quarters.  Ordered with the issuing thread's tcgen05.mma.
+__device__ __forceinline__ void cp_sf(uint32_t taddr, uint64_t desc) {
+    asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(desc)
+                 : "memory");
+}
+
+// Instruction descriptor of a block-scaled MMA: f32 accumulator, E8M0 scales, K-major
+// operands, M = 128.  fmt: E2M1 = 1 for kind::mxf4; E4M3 = 0 for kind::mxf8f6f4.
+__host__ __device__ constexpr uint32_t idesc_bs(int fmt, int n, uint32_t a_sf, uint32_t b_sf) {
+    return (b_sf << 4) | (uint32_t(fmt) << 7) | (uint32_t(fmt) << 10) | (uint32_t(n >> 3) << 17) |
+           (1u << 23) | (uint32_t(128 >> 4) << 24) | (a_sf << 29);
+}
+
+// D (+)= (A * SFA) x (B * SFB), E2M1 operands, K = 64, two scales per row (byte sf_id, sf_id+1
+// of the scale columns; sf_id in {0, 2}, carried in both the descriptor and the address).
+__device__ __forceinline__ void mma_mxf4(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc,
+                                         uint32_t sfa, uint32_t sfb, bool acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::mxf4.block_scale.scale_vec::2X [%0], %1, %2, %3, [%5], "
+        "[%6], p;\n\t}"
+        ::"r"(d), "l"(a), "l"(b), "r"(idesc), "r"(uint32_t(acc)), "r"(sfa), "r"(sfb)
+        : "memory");
+}
+
+// D (+)= (A * SFA) x (B * SFB), E4M3 operands, K = 32, one scale per row (byte sf_id).
+__device__ __forceinline__ void mma_mxf8(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc,
+                                         uint32_t sfa, uint32_t sfb, bool acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n\t}"
+        ::"r"(d), "l"(a), "l"(b), "r"(idesc), "r"(uint32_t(acc)), "r"(sfa), "r"(sfb)
+        : "memory");
+}
+
 }  // namespace tc
 }  // namespace urb

@@ -190,6 +190,12 @@ int upload_matrix(Ctx *ctx, Mat *m, const void *values, const uint8_t *scales) {
     if (flags & kFlagNanE4m3) return set_error(ctx, URB_ERR_NONFINITE, "E4M3 payload contains NaN codes");
     if (flags & kFlagInvalidScale) return set_error(ctx, URB_ERR_INVALID_SCALE, "E8M0 scale byte 0xff is NaN");
 
+    // Block-scaled tensor-core layout: any MX matrix whose scale blocks are 32-column groups
+    // (the tensor core applies the E8M0 scales itself, so no exponent window applies).
+    if (mx) {
+        int rc = repack_tc(ctx, m, st);
+        if (rc) return rc;
+    }
     m->tiled = tiled_shape && !(flags & kFlagWide);
     if (m->tiled) {
         size_t total = size_t(m->rbs) * m->kslices * tile_bytes(m->format);
@@ -215,10 +221,6 @@ int upload_matrix(Ctx *ctx, Mat *m, const void *values, const uint8_t *scales) {
                                                            32, m->rbs, m->kslices, m->tiles);
         }
         URB_CUDA(ctx, cudaGetLastError());
-        if (mx) {
-            int rc = repack_tc(ctx, m, st);
-            if (rc) return rc;
-        }
         // MX payloads keep only the tiled copies.  BF16 keeps its row-major copy as well: the
         // bit-exact router reads whole rows in column order.
         if (m->format != URB_FMT_BF16) {

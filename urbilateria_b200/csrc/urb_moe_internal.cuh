@@ -30,24 +30,22 @@ struct PermArgs {
 
 int launch_permute(Ctx *ctx, const PermArgs &p, cudaStream_t st);
 
-// Segments of the two tensor-core passes, built on the device from the grouping.
+// Groups of the two tensor-core passes, built on the device from the grouping.
 struct TcBuildArgs {
     const int32_t *counts, *offsets;  // from the grouping kernel
-    const int *lofree;                // x exactly representable in one f16 column
+    int fmt;
     int tokens, top_k, experts;
     const uint8_t *const *gate_tc, *const *up_tc, *const *down_tc;
-    const int8_t *const *gate_rexp, *const *up_rexp, *const *down_rexp;
     const uint8_t *sh_gate_tc, *sh_up_tc, *sh_down_tc;
-    const int8_t *sh_gate_rexp, *sh_up_rexp, *sh_down_rexp;
     int has_shared;
     int hidden, inter;
     TcSeg *gu, *dn;
-    int *scalars;  // nsegs_gu, units_gu, nsegs_dn, units_dn
+    BsSlot *gu_slots, *dn_slots;  // [TK + T] activation slots of each column, per pass
+    int *gu_units, *dn_units;     // group of each work unit, per pass
+    int *scalars;  // ngroups_gu, units_gu, ngroups_dn, units_dn
     const int32_t *status;  // non-zero: an earlier stage failed; build no work
 };
 int launch_build_tc_segs(Ctx *ctx, const TcBuildArgs &b, cudaStream_t st);
-constexpr int kTcCapGu = 64;   // tokens per gate/up segment with hi/lo columns (N <= 128)
-constexpr int kTcCapDn = 128;  // tokens per down segment (hi/lo, N <= 256)
 int launch_combine(Ctx *ctx, const float *y, const float *shared_y, const float *w,
                    const int32_t *inv, int tokens, int top_k, int hidden, float *out,
                    cudaStream_t st, const int32_t *status = nullptr);
@@ -64,7 +62,7 @@ struct Layer {
     // Device pointer tables [experts] for gate/up/down tiles and row exponents, then the
     // tensor-core tiles of gate/up/down.
     void **d_tables = nullptr;
-    bool use_tc = true;  // tcgen05 grouped passes (false: mma.sync register-dequant passes)
+    bool use_tc = true;  // block-scaled tcgen05 passes (false: mma.sync register-dequant)
 };
 
 // Device workspace of one forward, carved from the context workspace.
@@ -81,7 +79,10 @@ struct MoeWork {
     float *y;             // [TK+T, hidden]
     int32_t *status;
     int32_t *lofree;
+    float *gu;            // [TK+T, 2*inter] gate | up outputs of the tensor-core pass
     TcSeg *tsegs_gu, *tsegs_dn;
+    BsSlot *bslots_gu, *bslots_dn;
+    int *units_gu, *units_dn;
     int *tscalars;
     uint8_t *bbuf_gu, *bbuf_dn;
 };

@@ -1,51 +1,78 @@
-// urb_tc.cuh — shared definitions of the tensor-core (tcgen05) grouped pass.
+// urb_tc.cuh — shared definitions of the block-scaled tensor-core (tcgen05) grouped pass.
+//
+// Weights stay in their MX encoding all the way into the tensor core: kind::mxf4 for MXFP4
+// (E2M1 x E2M1) and kind::mxf8f6f4 for MXFP8 (E4M3 x E4M3), each with E8M0 scales per 32
+// columns.  Activations are written as residual terms in the same element format (x ~= t0 +
+// t1 + ..., each term with its own E8M0 scale per 32 columns): 6 E2M1 terms in 8 MMA rows per
+// token for MXFP4, 4 E4M3 terms in 4 rows for MXFP8; the epilogue sums a token's terms.
 #pragma once
 #include "urb_internal.cuh"
 
 namespace urb {
 
-// Bytes of one 128x64 tile of the tc layout (payload + 256 B of scales).
-__host__ __device__ constexpr int tc_tile_bytes(int fmt) {
-    return fmt == URB_FMT_MXFP4 ? 128 * 32 + 256 : 128 * 64 + 256;
-}
+constexpr int kBsNmax = 128;  // MMA N of a full sub-segment
+// MMA rows per token, residual terms per token, tokens per sub-segment.
+__host__ __device__ constexpr int bs_rows_per_tok(int fmt) { return fmt == URB_FMT_MXFP4 ? 8 : 4; }
+__host__ __device__ constexpr int bs_terms(int fmt) { return fmt == URB_FMT_MXFP4 ? 6 : 4; }
+__host__ __device__ constexpr int bs_cap(int fmt) { return kBsNmax / bs_rows_per_tok(fmt); }
 
-// One segment of a tensor-core pass: a matrix (or gate/up pair) applied to a run of
-// activation columns; its work units are its 128-row tiles.
+// Bytes of one 128-row x 128-byte tile of the bs layout: payload (128-byte swizzled K-major)
+// followed by the scale chunks (512 B each, 4 scale columns of 128 rows).
+__host__ __device__ constexpr int bs_sf_chunks(int fmt) { return fmt == URB_FMT_MXFP4 ? 2 : 1; }
+__host__ __device__ constexpr int bs_tile_bytes(int fmt) { return 16384 + 512 * bs_sf_chunks(fmt); }
+// Input columns per K stage (one 128-byte row of payload).
+__host__ __device__ constexpr int bs_stage_cols(int fmt) { return fmt == URB_FMT_MXFP4 ? 256 : 128; }
+// Bytes of one activation stage of n MMA rows (n <= 128): payload then scale chunks.
+__host__ __device__ constexpr int bs_bstage_bytes(int fmt, int n) { return n * 128 + 512 * bs_sf_chunks(fmt); }
+
+// One group of a bs pass: a matrix applied to one run of activation columns.  Its units are
+// (128-row tile mt, sub-segment j) pairs, j fastest, so the sub-segments of a large group read
+// the same weight tile back to back (the second read is served by L2).
 struct TcSeg {
-    const uint8_t *a;     // tc tiles of the (gate) matrix
-    const uint8_t *b;     // tc tiles of the up matrix (pairs) or nullptr
-    const int8_t *ra;     // row exponent offsets of a (>= mts*128 entries)
-    const int8_t *rb;
-    long long b_off;      // byte offset of this segment's activation tiles in the B buffer
-    int mts, ks;          // 128-row tiles, 64-column stages
+    const uint8_t *w;     // bs tiles of the matrix
+    long long b_off;      // byte offset of the group's activation stages in the B buffer
+    int mts, ks;          // 128-row tiles, K stages
     int rows, cols;       // real rows / input columns
     int col_begin, ntok;  // activation columns
-    int npad, rowsper;    // MMA N (multiple of 16) and activation rows per token (1 or 2)
-    int unit_begin;       // prefix of mts over preceding segments
+    int nsub;             // sub-segments of bs_cap(fmt) tokens
+    int unit_begin;       // prefix of mts * nsub over preceding groups
+    int out_off;          // column offset of this group's outputs within an output row
     int pad;
+};
+
+// Where the MMA rows of one activation column live: its sub-segment's first stage (byte offset
+// in the B buffer; stage ks at base + ks * bs_bstage_bytes(fmt, n)), its token slot, and the
+// sub-segment's MMA N.
+struct BsSlot {
+    long long base;
+    int slot, n;
 };
 
 struct TcArgs {
     const TcSeg *segs;
     const int *nsegs;
     const int *total_units;
-    int nmax;                  // largest npad of the launch (shared-memory sizing)
-    int stages_a;              // weight ring depth (set by the launcher)
-    uint8_t *bbuf;             // activation tiles (written by the prep kernel)
-    const float *src;          // activation rows f32
+    const int *unit_group;     // [total units] group of each work unit
+    uint8_t *bbuf;             // activation stages (written by the prep kernel)
+    // Prep: source rows (row-major f32), each written to the activation columns that use it.
+    // Gate/up pass: src = x, row t feeds columns inv[t * top_k + k] and, with a shared expert,
+    // shared_col0 + t.  Down pass (inv == nullptr): src row c = [gate | up] of column c,
+    // h = silu(gate) * up, feeding column c.
+    const float *src;
     int src_stride;
-    const int32_t *col_src;    // activation column -> src row (nullptr: identity)
-    const int32_t *src_shift;  // explicit power-of-two shift per src row, or
-    const int32_t *src_maxexp; // ilogb(max|row|) per src row (-1000: zero row)
+    int nrows;                 // source rows
+    int cols, ks;              // input columns and K stages of the pass
+    int swiglu;
+    const int32_t *inv;
+    int top_k, shared_col0;    // shared_col0 < 0: no shared expert
+    const BsSlot *slots;       // [activation columns]
     float *out;
     int out_stride;
-    int32_t *out_maxexp;
     int32_t *status;
 };
 
-// Prep (activation tiles) + tensor-core pass.
-int launch_tc_grouped(Ctx *ctx, int fmt, bool pair, const TcArgs &a, int max_segs, int max_ks,
-                      cudaStream_t st);
+// Prep (activation terms) + tensor-core pass over every group of the launch.
+int launch_tc_grouped(Ctx *ctx, int fmt, const TcArgs &a, cudaStream_t st);
 int repack_tc(Ctx *ctx, Mat *m, cudaStream_t st);
 
 }  // namespace urb
