@@ -14,18 +14,21 @@
 // zero rows); the epilogue adds the term columns of a token.
 //
 // One persistent CTA per SM walks work units (group, 128-row tile, sub-segment).  tcgen05
-// instructions cost ~120-200 cycles of issue each on the issuing thread (MMAs from two threads
-// proceed concurrently), so the per-stage instruction stream is spread over warps:
-//   warp 0 (one thread)  weight producer: tiles into a 9-deep ring (bulk copies, mbarriers);
-//   warp 3 (one thread)  activation producer: stages into a 4-deep ring (L2-resident source);
+// instructions cost ~120-200 cycles of issue each on the issuing thread, while MMAs issued from
+// several threads proceed concurrently, so the per-stage instruction stream is spread over
+// warps:
+//   warp 0 (one thread)  weight producer: tiles into an 8-deep ring (bulk copies, mbarriers);
+//   activation producer (one thread): stages into a byte ring (variable-size stages, up to 16
+//                        in flight) from their L2-resident source;
 //   warps 8-11           scale warps: each stage's E8M0 scales of both operands from shared
 //                        memory into TMEM with tcgen05.st (each warp fills its lane quarter);
-//   warps 1, 2 (one thread each)  MMA issuers: issuer i runs the MMAs of K half i of every
-//                        stage into its own TMEM accumulator and releases the stage with one
-//                        tcgen05.commit (the activation slot is released through the same
-//                        barrier);
-//   warps 4-7            epilogue: tcgen05.ld of both accumulators, half and term sums, f32
-//                        row stores.
+//   warps 1, 2 [, 3, 12] (one thread each)  kBsIssuers MMA issuers: issuer i runs the MMAs of
+//                        its share of each stage's 4 K steps into its own TMEM accumulator and
+//                        releases stages two at a time with one tcgen05.commit on the pair's
+//                        release barrier (a 32-deep ring that both producers watch);
+//   warps 4-7            epilogue: tcgen05.ld of the issuers' accumulators, their sums and the
+//                        term sums, f32 row stores;
+//   warp 13 (one thread) activation producer (above).
 #include "tc_common.cuh"
 #include "urb_internal.cuh"
 #include "urb_tc.cuh"
@@ -33,18 +36,29 @@
 namespace urb {
 namespace {
 
-constexpr int kSA = 9;                // weight ring depth (also the TMEM scale slots)
-constexpr int kSB = 4;                // activation ring depth (kSB <= kSA)
-constexpr int kStage = 17408;         // bytes of one ring slot (largest tile / activation stage)
-constexpr int kThreadsBs = 384;
-constexpr uint32_t kAccCols = 128;    // accumulator columns per issuer (N <= 128)
-constexpr uint32_t kSfCol0 = 256;     // first scale column: slot s at kSfCol0 + 16 s
-constexpr int kSmemBs = (kSA + kSB) * kStage + 1024;
+constexpr int kSA = 8;                // weight ring depth (also the TMEM scale slots)
+constexpr int kStage = 17408;         // bytes of one weight slot / largest activation stage
+constexpr int kBRing = 5 * kStage;    // activation byte ring
+constexpr int kSB = 16;               // activation stages in flight at most
+constexpr int kRel = 32;              // release barriers, one per pair of stages (covers 64)
+constexpr int kIssuers = kBsIssuers;
+constexpr int kStepsPerIssuer = 4 / kIssuers;
+static_assert(kIssuers == 2 || kIssuers == 4, "issuers");
+// Warps: 0 weight producer, 1-2 issuers, 3 activation producer (2 issuers) or 1-3 and 12
+// issuers, 13 activation producer (4 issuers); 4-7 epilogue; 8-11 scale warps.  Each polling
+// thread sits on its own scheduler (warp % 4) where possible.
+constexpr int kThreadsBs = kIssuers == 2 ? 384 : 448;
+constexpr int kWarpBProd = kIssuers == 2 ? 3 : 13;
+constexpr uint32_t kAccCols = kBsNmax;  // accumulator columns per issuer
+constexpr uint32_t kSfCol0 = kIssuers * kAccCols;  // first scale column: slot s at +16 s
+constexpr int kSmemBs = kSA * kStage + kBRing + 1024;
 
 static_assert(bs_tile_bytes(URB_FMT_MXFP4) <= kStage && bs_tile_bytes(URB_FMT_MXFP8) <= kStage, "slot");
 static_assert(bs_bstage_bytes(URB_FMT_MXFP4, kBsNmax) <= kStage, "slot");
 static_assert(kSfCol0 + kSA * 16 <= 512, "tmem");
-static_assert(kSB <= kSA, "the activation producer watches the weight ring's release barrier");
+static_assert(kAccCols % 32 == 0, "accumulator alignment");
+static_assert(2 * kRel >= kSA + kSB + 2, "release-barrier ring too short");
+static_assert(kSmemBs <= 227 * 1024 - 1024, "shared memory");
 
 __device__ __forceinline__ void set_status(int32_t *status, int code) {
     if (status) atomicCAS(status, 0, int32_t(code));
@@ -76,6 +90,13 @@ struct UnitCursor {
 
 __device__ __forceinline__ int round16i(int v) { return (v + 15) & ~15; }
 
+// Stage p has been consumed once its pair's release barrier has fired (the issuers commit after
+// every odd stage and after the last stage of the launch).
+__device__ __forceinline__ bool wait_consumed(uint64_t *rel, uint32_t p, volatile int *abort) {
+    const uint32_t pair = p >> 1;
+    return tc::mbar_wait(&rel[pair % kRel], (pair / kRel) & 1, abort);
+}
+
 struct Unit {
     int mt, sub, nt, n;
 };
@@ -99,8 +120,9 @@ __global__ void __launch_bounds__(kThreadsBs, 1) k_bs_grouped(TcArgs a) {
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t *ring_a = smem;
     uint8_t *ring_b = smem + size_t(kSA) * kStage;
-    __shared__ __align__(8) uint64_t a_full[kSA], a_empty[kSA], sf_full[kSA], b_full[kSB];
-    __shared__ __align__(8) uint64_t acc_full, acc_empty, mma_done[2];
+    __shared__ __align__(8) uint64_t a_full[kSA], sf_full[kSA], b_full[kSB], rel[kRel];
+    __shared__ __align__(8) uint64_t acc_full, acc_empty, mma_done[kIssuers];
+    __shared__ uint32_t b_off[kSB];  // byte offset of each in-flight activation stage
     __shared__ uint32_t tmem_base;
     __shared__ int abort_flag, skip, never;
 
@@ -114,14 +136,13 @@ __global__ void __launch_bounds__(kThreadsBs, 1) k_bs_grouped(TcArgs a) {
     if (threadIdx.x == 0) {
         for (int s = 0; s < kSA; ++s) {
             tc::mbar_init(&a_full[s], 1);
-            tc::mbar_init(&a_empty[s], 2);   // one commit per issuer
             tc::mbar_init(&sf_full[s], 4);   // one arrival per scale warp
         }
         for (int s = 0; s < kSB; ++s) tc::mbar_init(&b_full[s], 1);
-        tc::mbar_init(&acc_full, 2);
+        for (int s = 0; s < kRel; ++s) tc::mbar_init(&rel[s], kIssuers);  // one commit per issuer
+        tc::mbar_init(&acc_full, kIssuers);
         tc::mbar_init(&acc_empty, 4);
-        tc::mbar_init(&mma_done[0], 1);
-        tc::mbar_init(&mma_done[1], 1);
+        for (int s = 0; s < kIssuers; ++s) tc::mbar_init(&mma_done[s], 1);
         tc::mbar_fence_init();
         abort_flag = 0;
         never = 0;
@@ -150,7 +171,10 @@ __global__ void __launch_bounds__(kThreadsBs, 1) k_bs_grouped(TcArgs a) {
             bool ok = true;
             for (int ks = 0; ks < S.ks; ++ks, ++g) {
                 const int sa = int(g % kSA);
-                if (!tc::mbar_wait(&a_empty[sa], ((g / kSA) & 1) ^ 1, abortp)) { ok = false; break; }
+                if (g >= uint32_t(kSA) && !wait_consumed(rel, g - kSA, abortp)) {  // slot free
+                    ok = false;
+                    break;
+                }
                 tc::mbar_arrive_expect_tx(&a_full[sa], uint32_t(TB));
                 tc::bulk_g2s(ring_a + size_t(sa) * kStage, wsrc + size_t(ks) * TB, TB, &a_full[sa]);
             }
@@ -159,31 +183,53 @@ __global__ void __launch_bounds__(kThreadsBs, 1) k_bs_grouped(TcArgs a) {
         // Let every copy this thread issued land before the CTA can exit.
         for (uint32_t i = g > uint32_t(kSA) ? g - kSA : 0; i < g; ++i)
             tc::mbar_wait(&a_full[i % kSA], (i / kSA) & 1, &never);
-    } else if (warp == 3 && lane == 0) {
+    } else if (warp == kWarpBProd && lane == 0) {
         // ---------------- activation producer ----------------
-        // Slot g % kSB is free once stage g - kSB has been consumed, i.e. once the weight ring's
-        // release barrier of that stage has fired (kSB <= kSA keeps the parity unambiguous).
-        uint32_t g = 0;
+        // Byte ring: stage g occupies [q_start, q_end) (1 KB granules, contiguous) until stage g
+        // has been consumed; the oldest in-flight stage is retired by waiting on its release
+        // barrier.  At most kSB stages are in flight.
+        uint32_t q_start[kSB];
+        uint32_t g = 0, oldest = 0, head = 0;
         for (UnitCursor uc(a, total_units); uc.valid() && !*abortp; uc.advance()) {
             const TcSeg &S = uc.cur;
             const Unit x = unit_of<FMT>(S, uc.u);
             const uint32_t bbytes = uint32_t(bs_bstage_bytes(FMT, x.n));
+            const uint32_t need = (bbytes + 1023) & ~1023u;
             const uint8_t *bsrc = a.bbuf + S.b_off + (long long)x.sub * S.ks * bs_bstage_bytes(FMT, kBsNmax);
             bool ok = true;
-            for (int ks = 0; ks < S.ks; ++ks, ++g) {
-                const int sb = int(g % kSB);
-                if (g >= uint32_t(kSB)) {
-                    const uint32_t p = g - kSB;
-                    if (!tc::mbar_wait(&a_empty[p % kSA], (p / kSA) & 1, abortp)) { ok = false; break; }
+            for (int ks = 0; ks < S.ks && ok; ++ks, ++g) {
+                uint32_t pos = 0;
+                for (;;) {
+                    const uint32_t inflight = g - oldest;
+                    if (inflight == 0) { head = 0; pos = 0; break; }
+                    if (inflight < uint32_t(kSB)) {
+                        const uint32_t tail = q_start[oldest % kSB];
+                        // Both wrapped placements are strict: a wrapped ring never fills up to
+                        // its tail, so head == tail only ever means "nothing in flight".
+                        if (head >= tail) {  // used [tail, head): free [head, end) and [0, tail)
+                            if (head + need <= uint32_t(kBRing)) { pos = head; break; }
+                            if (need < tail) { pos = 0; break; }
+                        } else if (head + need < tail) {  // used [tail, end) + [0, head)
+                            pos = head;
+                            break;
+                        }
+                    }
+                    if (!wait_consumed(rel, oldest, abortp)) { ok = false; break; }
+                    ++oldest;
                 }
+                if (!ok) break;
+                const int sb = int(g % kSB);
+                q_start[sb] = pos;
+                head = pos + need;
+                b_off[sb] = pos;
                 tc::mbar_arrive_expect_tx(&b_full[sb], bbytes);
-                tc::bulk_g2s(ring_b + size_t(sb) * kStage, bsrc + size_t(ks) * bbytes, bbytes, &b_full[sb]);
+                tc::bulk_g2s(ring_b + pos, bsrc + size_t(ks) * bbytes, bbytes, &b_full[sb]);
             }
             if (!ok) { fail(); break; }
         }
         for (uint32_t i = g > uint32_t(kSB) ? g - kSB : 0; i < g; ++i)
             tc::mbar_wait(&b_full[i % kSB], (i / kSB) & 1, &never);
-    } else if (warp >= 8) {
+    } else if (warp >= 8 && warp < 12) {
         // ---------------- scale warps ----------------
         // TMEM scale slot sa (16 columns): A's chunks at +0 / +4, B's at +8 / +12; lane l of
         // every quarter holds bytes 16 l .. 16 l + 15 of each 512-byte chunk.
@@ -201,7 +247,7 @@ __global__ void __launch_bounds__(kThreadsBs, 1) k_bs_grouped(TcArgs a) {
                     break;
                 }
                 const uint8_t *sfa = ring_a + size_t(sa) * kStage + 16384 + 16 * lane;
-                const uint8_t *sfb = ring_b + size_t(sb) * kStage + x.n * 128 + 16 * lane;
+                const uint8_t *sfb = ring_b + b_off[sb] + x.n * 128 + 16 * lane;
                 uint32_t v[16];
 #pragma unroll
                 for (int h = 0; h < 2; ++h) {
@@ -221,10 +267,10 @@ __global__ void __launch_bounds__(kThreadsBs, 1) k_bs_grouped(TcArgs a) {
             }
             if (!ok) { fail(); break; }
         }
-    } else if ((warp == 1 || warp == 2) && lane == 0) {
-        // ---------------- MMA issuers (K half i of every stage) ----------------
-        const int half = warp - 1;
-        const uint32_t acc = tbase + uint32_t(half) * kAccCols;
+    } else if ((warp == 1 || warp == 2 || (kIssuers == 4 && (warp == 3 || warp == 12))) && lane == 0) {
+        // ---------------- MMA issuers (their K steps of every stage) ----------------
+        const int me = warp == 12 ? 3 : warp - 1;
+        const uint32_t acc = tbase + uint32_t(me) * kAccCols;
         uint32_t g = 0, j = 0;
         for (UnitCursor uc(a, total_units); uc.valid() && !*abortp; uc.advance(), ++j) {
             const TcSeg &S = uc.cur;
@@ -234,22 +280,16 @@ __global__ void __launch_bounds__(kThreadsBs, 1) k_bs_grouped(TcArgs a) {
             bool ok = true;
             for (int ks = 0; ks < S.ks; ++ks, ++g) {
                 const int sa = int(g % kSA), sb = int(g % kSB);
-                // The scale warps saw both copies land; waiting on the copies' own barriers as
-                // well (already complete) orders the MMA's shared-memory reads after them.
-                if (!tc::mbar_wait(&sf_full[sa], (g / kSA) & 1, abortp) ||
-                    !tc::mbar_wait(&a_full[sa], (g / kSA) & 1, abortp) ||
-                    !tc::mbar_wait(&b_full[sb], (g / kSB) & 1, abortp)) {
-                    ok = false;
-                    break;
-                }
+                // The scale warps arrive only after both copies of the stage have landed.
+                if (!tc::mbar_wait(&sf_full[sa], (g / kSA) & 1, abortp)) { ok = false; break; }
                 tc::fence_after_sync();
                 const uint32_t sA = tc::smem_u32(ring_a + size_t(sa) * kStage);
-                const uint32_t sB = tc::smem_u32(ring_b + size_t(sb) * kStage);
+                const uint32_t sB = tc::smem_u32(ring_b + b_off[sb]);
                 const uint32_t sfa = tbase + kSfCol0 + 16u * sa, sfb = sfa + 8;
                 const uint64_t adesc = tc::sdesc_sw128(sA), bdesc = tc::sdesc_sw128(sB);
 #pragma unroll
-                for (int k2 = 0; k2 < 2; ++k2) {
-                    const int kk = 2 * half + k2;
+                for (int k2 = 0; k2 < kStepsPerIssuer; ++k2) {
+                    const int kk = me * kStepsPerIssuer + k2;
                     const bool accum = ks > 0 || k2 > 0;
                     if (FMT == URB_FMT_MXFP4) {
                         const uint32_t id = 2u * (kk & 1), col = 4u * (kk >> 1);
@@ -261,14 +301,15 @@ __global__ void __launch_bounds__(kThreadsBs, 1) k_bs_grouped(TcArgs a) {
                                      sfa | (id << 30), sfb | (id << 30), accum);
                     }
                 }
-                tc::mma_commit(&a_empty[sa]);
+                const bool last = ks == S.ks - 1 && uc.u + uc.step >= uc.total;
+                if ((g & 1) || last) tc::mma_commit(&rel[(g >> 1) % kRel]);
                 if (ks == S.ks - 1) tc::mma_commit(&acc_full);
             }
             if (!ok) { fail(); break; }
         }
         // Every MMA of this thread completes before TMEM is released.
-        tc::mma_commit(&mma_done[half]);
-        tc::mbar_wait(&mma_done[half], 0, &never);
+        tc::mma_commit(&mma_done[me]);
+        tc::mbar_wait(&mma_done[me], 0, &never);
     } else if (warp >= 4 && warp < 8) {
         // ---------------- epilogue ----------------
         constexpr int RT = bs_rows_per_tok(FMT), TT = bs_terms(FMT), TPC = 16 / RT;
@@ -285,18 +326,23 @@ __global__ void __launch_bounds__(kThreadsBs, 1) k_bs_grouped(TcArgs a) {
             const bool row_ok = grow < S.rows;
             const int tok0 = x.sub * bs_cap(FMT);
             for (int c = 0; c < x.n / 16; ++c) {
-                uint32_t v0[16], v1[16];
-                tc::tmem_ld16(tbase + lane_base + 16 * c, v0);
-                tc::tmem_ld16(tbase + lane_base + kAccCols + 16 * c, v1);
+                uint32_t v[kIssuers][16];
+#pragma unroll
+                for (int i = 0; i < kIssuers; ++i)
+                    tc::tmem_ld16(tbase + lane_base + uint32_t(i) * kAccCols + 16 * c, v[i]);
                 tc::wait_ld();
 #pragma unroll
                 for (int s = 0; s < TPC; ++s) {
                     const int t = TPC * c + s;
                     if (t < x.nt && row_ok) {
-                        float o = __uint_as_float(v0[RT * s]) + __uint_as_float(v1[RT * s]);
+                        float o = 0.0f;
 #pragma unroll
-                        for (int e = 1; e < TT; ++e)
-                            o += __uint_as_float(v0[RT * s + e]) + __uint_as_float(v1[RT * s + e]);
+                        for (int e = 0; e < TT; ++e) {
+                            float q = __uint_as_float(v[0][RT * s + e]) + __uint_as_float(v[1][RT * s + e]);
+                            if constexpr (kIssuers == 4)
+                                q += __uint_as_float(v[2][RT * s + e]) + __uint_as_float(v[3][RT * s + e]);
+                            o += q;
+                        }
                         a.out[size_t(S.col_begin + tok0 + t) * a.out_stride + S.out_off + grow] = o;
                     }
                 }

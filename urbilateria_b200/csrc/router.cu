@@ -15,7 +15,10 @@
 namespace urb {
 namespace {
 
-constexpr int kRouterKc = 64;  // columns staged per tile
+constexpr int kRouterKc = 64;   // columns staged per tile
+constexpr int kRouterWarps = 4;
+constexpr int kRouterTpt = 2;   // token chains per thread
+constexpr int kRouterTok = kRouterWarps * kRouterTpt;  // tokens per CTA
 
 template <bool BF16>
 __device__ __forceinline__ double widen(const void *w, size_t idx) {
@@ -23,51 +26,54 @@ __device__ __forceinline__ double widen(const void *w, size_t idx) {
                 : double(static_cast<const float *>(w)[idx]);
 }
 
-// CTA = 32 experts x 8 tokens; thread (lane = expert, warp = token) owns one chain.  Column
-// tiles of kRouterKc are staged as f64 in a double buffer; the next tile is fetched into
-// registers while the current one is consumed, so the only stall per tile is one barrier.
+// CTA = 32 experts x 8 tokens; thread (lane = expert, warp = token pair) owns two chains and
+// performs, for each of them, exactly the reference's additions in column order.  The chains
+// are latency-bound (one f64 FMA after another), so a thread interleaves two of them and the
+// operands come from shared memory without bank conflicts: the experts' weights are staged
+// column-major (lane-contiguous), the token pair's x values as one broadcast 16-byte load.
+// Column tiles are double-buffered; the next tile is fetched into registers while the current
+// one is consumed.
 template <bool BF16>
-__global__ void __launch_bounds__(256) k_router_logits(const void *w, int experts, int cols,
-                                                       const float *x, int tokens,
-                                                       float *logits) {
-    constexpr int KC = kRouterKc;
-    constexpr int WPT = 32 * KC / 256;  // W elements staged per thread per tile
-    constexpr int XPT = 8 * KC / 256;   // x elements staged per thread per tile
-    __shared__ double ws[2][32][KC + 1];
-    __shared__ double xs[2][8][KC];
+__global__ void __launch_bounds__(32 * kRouterWarps) k_router_logits(const void *w, int experts,
+                                                                     int cols, const float *x,
+                                                                     int tokens, float *logits) {
+    constexpr int KC = kRouterKc, NT = 32 * kRouterWarps;
+    constexpr int WPT = 32 * KC / NT;          // weights fetched per thread per tile (16)
+    constexpr int XPT = kRouterTok * KC / NT;  // x values fetched per thread per tile (4)
+    __shared__ __align__(16) double ws[2][KC][32];
+    __shared__ __align__(16) double xs[2][KC][kRouterTok];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int e0 = blockIdx.x * 32, t0 = blockIdx.y * 8;
+    const int e0 = blockIdx.x * 32, t0 = blockIdx.y * kRouterTok;
     const int ntiles = (cols + KC - 1) / KC;
+    // Fetch geometry: weights row wr_r, columns wr_c .. +WPT; x row xr_r, columns xr_c .. +XPT.
+    const int wr_r = threadIdx.x / (KC / WPT), wr_c = (threadIdx.x % (KC / WPT)) * WPT;
+    const int xr_r = threadIdx.x / (KC / XPT), xr_c = (threadIdx.x % (KC / XPT)) * XPT;
     double wr[WPT], xr[XPT];
     auto fetch = [&](int tile) {
         const int c0 = tile * KC;
+        const bool wrow = e0 + wr_r < experts, xrow = t0 + xr_r < tokens;
 #pragma unroll
         for (int j = 0; j < WPT; ++j) {
-            const int i = threadIdx.x + j * 256, r = i / KC, c = i % KC;
-            wr[j] = (e0 + r < experts && c0 + c < cols) ? widen<BF16>(w, size_t(e0 + r) * cols + c0 + c) : 0.0;
+            const int c = c0 + wr_c + j;
+            wr[j] = (wrow && c < cols) ? widen<BF16>(w, size_t(e0 + wr_r) * cols + c) : 0.0;
         }
 #pragma unroll
         for (int j = 0; j < XPT; ++j) {
-            const int i = threadIdx.x + j * 256, r = i / KC, c = i % KC;
-            xr[j] = (t0 + r < tokens && c0 + c < cols) ? double(x[size_t(t0 + r) * cols + c0 + c]) : 0.0;
+            const int c = c0 + xr_c + j;
+            xr[j] = (xrow && c < cols) ? double(x[size_t(t0 + xr_r) * cols + c]) : 0.0;
         }
     };
     auto stash = [&](int buf) {
 #pragma unroll
-        for (int j = 0; j < WPT; ++j) {
-            const int i = threadIdx.x + j * 256;
-            ws[buf][i / KC][i % KC] = wr[j];
-        }
+        for (int j = 0; j < WPT; ++j) ws[buf][wr_c + j][wr_r] = wr[j];
 #pragma unroll
-        for (int j = 0; j < XPT; ++j) {
-            const int i = threadIdx.x + j * 256;
-            xs[buf][i / KC][i % KC] = xr[j];
-        }
+        for (int j = 0; j < XPT; ++j) xs[buf][xr_c + j][xr_r] = xr[j];
     };
     fetch(0);
     stash(0);
     __syncthreads();
-    double acc = -0.0;  // Iterator::sum over f64 starts from -0.0 (bf16.rs:500)
+    // Iterator::sum over f64 starts from -0.0 (bf16.rs:500).
+    double acc0 = -0.0, acc1 = -0.0;
     for (int tile = 0; tile < ntiles; ++tile) {
         const int buf = tile & 1;
         if (tile + 1 < ntiles) fetch(tile + 1);
@@ -75,15 +81,28 @@ __global__ void __launch_bounds__(256) k_router_logits(const void *w, int expert
         // Exactly the reference's additions: columns in order, one rounding each.
         if (kc == KC) {
 #pragma unroll 16
-            for (int c = 0; c < KC; ++c) acc = fma(ws[buf][lane][c], xs[buf][warp][c], acc);
+            for (int c = 0; c < KC; ++c) {
+                const double wv = ws[buf][c][lane];
+                const double2 xv = *reinterpret_cast<const double2 *>(&xs[buf][c][kRouterTpt * warp]);
+                acc0 = fma(wv, xv.x, acc0);
+                acc1 = fma(wv, xv.y, acc1);
+            }
         } else {
-            for (int c = 0; c < kc; ++c) acc = fma(ws[buf][lane][c], xs[buf][warp][c], acc);
+            for (int c = 0; c < kc; ++c) {
+                const double wv = ws[buf][c][lane];
+                const double2 xv = *reinterpret_cast<const double2 *>(&xs[buf][c][kRouterTpt * warp]);
+                acc0 = fma(wv, xv.x, acc0);
+                acc1 = fma(wv, xv.y, acc1);
+            }
         }
         if (tile + 1 < ntiles) stash(buf ^ 1);
         __syncthreads();
     }
-    const int e = e0 + lane, t = t0 + warp;
-    if (e < experts && t < tokens) logits[size_t(t) * experts + e] = float(acc);
+    const int e = e0 + lane, t = t0 + kRouterTpt * warp;
+    if (e < experts) {
+        if (t < tokens) logits[size_t(t) * experts + e] = float(acc0);
+        if (t + 1 < tokens) logits[size_t(t + 1) * experts + e] = float(acc1);
+    }
 }
 
 __device__ __forceinline__ bool better(int32_t ka, int ia, int32_t kb, int ib) {
@@ -286,13 +305,14 @@ ExpfTable table_of(const Ctx *ctx) { return ExpfTable{ctx->expf_keys, ctx->expf_
 int launch_router_logits(const Mat *router, const float *d_x, int tokens, float *d_logits,
                          cudaStream_t st) {
     if (tokens <= 0) return URB_OK;
-    dim3 grid(unsigned((router->rows + 31) / 32), unsigned((tokens + 7) / 8));
+    dim3 grid(unsigned((router->rows + 31) / 32), unsigned((tokens + kRouterTok - 1) / kRouterTok));
+    constexpr int nt = 32 * kRouterWarps;
     if (router->format == URB_FMT_BF16)
-        k_router_logits<true><<<grid, 256, 0, st>>>(router->raw_values, int(router->rows),
-                                                    int(router->cols), d_x, tokens, d_logits);
+        k_router_logits<true><<<grid, nt, 0, st>>>(router->raw_values, int(router->rows),
+                                                   int(router->cols), d_x, tokens, d_logits);
     else if (router->format == URB_FMT_F32)
-        k_router_logits<false><<<grid, 256, 0, st>>>(router->raw_values, int(router->rows),
-                                                     int(router->cols), d_x, tokens, d_logits);
+        k_router_logits<false><<<grid, nt, 0, st>>>(router->raw_values, int(router->rows),
+                                                    int(router->cols), d_x, tokens, d_logits);
     else
         return URB_ERR_UNSUPPORTED;
     return cudaGetLastError() == cudaSuccess ? URB_OK : URB_ERR_CUDA;

@@ -10,7 +10,9 @@
 
 namespace urb {
 
-constexpr int kBsNmax = 128;  // MMA N of a full sub-segment
+constexpr int kBsIssuers = 2;  // MMA issuing threads of the grouped kernel, one accumulator each
+// MMA N of a full sub-segment: the issuers' accumulators and 8 scale slots fill 512 TMEM columns.
+constexpr int kBsNmax = kBsIssuers == 2 ? 128 : 96;
 // MMA rows per token, residual terms per token, tokens per sub-segment.
 __host__ __device__ constexpr int bs_rows_per_tok(int fmt) { return fmt == URB_FMT_MXFP4 ? 8 : 4; }
 __host__ __device__ constexpr int bs_terms(int fmt) { return fmt == URB_FMT_MXFP4 ? 6 : 4; }
@@ -22,7 +24,7 @@ __host__ __device__ constexpr int bs_sf_chunks(int fmt) { return fmt == URB_FMT_
 __host__ __device__ constexpr int bs_tile_bytes(int fmt) { return 16384 + 512 * bs_sf_chunks(fmt); }
 // Input columns per K stage (one 128-byte row of payload).
 __host__ __device__ constexpr int bs_stage_cols(int fmt) { return fmt == URB_FMT_MXFP4 ? 256 : 128; }
-// Bytes of one activation stage of n MMA rows (n <= 128): payload then scale chunks.
+// Bytes of one activation stage of n MMA rows (n <= kBsNmax): payload then scale chunks.
 __host__ __device__ constexpr int bs_bstage_bytes(int fmt, int n) { return n * 128 + 512 * bs_sf_chunks(fmt); }
 
 // One group of a bs pass: a matrix applied to one run of activation columns.  Its units are
