@@ -18,6 +18,15 @@ struct ExpfTable {
     const uint32_t *index;
 };
 
+// expf_libm with the bucket's key range [lo, hi) already loaded from t.index.
+__device__ __forceinline__ float expf_libm_range(float x, const ExpfTable &t, uint32_t lo,
+                                                 uint32_t hi) {
+    const uint32_t k = __float_as_uint(x);
+    for (uint32_t i = lo; i < hi; ++i)
+        if (t.keys[i] == k) return __uint_as_float(t.vals[i]);
+    return float(exp(double(x)));
+}
+
 __device__ __forceinline__ float expf_libm(float x, const ExpfTable &t) {
     uint32_t k = __float_as_uint(x);
     if (t.index) {

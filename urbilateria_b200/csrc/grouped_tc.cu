@@ -36,9 +36,9 @@
 namespace urb {
 namespace {
 
-constexpr int kSA = 8;                // weight ring depth (also the TMEM scale slots)
+constexpr int kSA = 6;                // weight ring depth (also the TMEM scale slots)
 constexpr int kStage = 17408;         // bytes of one weight slot / largest activation stage
-constexpr int kBRing = 5 * kStage;    // activation byte ring
+constexpr int kBRing = 7 * kStage;    // activation byte ring
 constexpr int kSB = 16;               // activation stages in flight at most
 constexpr int kRel = 32;              // release barriers, one per pair of stages (covers 64)
 constexpr int kIssuers = kBsIssuers;

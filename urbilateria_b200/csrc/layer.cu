@@ -65,6 +65,8 @@ int moe_forward_device(Layer *L, const float *d_x, int T, float *d_out, MoeWork 
     MoeWork w{};
     w.shift = cv.take<int32_t>(T);
     w.logits = cv.take<float>(size_t(T) * E);
+    w.gate = cv.take<float>(size_t(T) * E);
+    w.sel = cv.take<float>(size_t(T) * E);
     w.ids = cv.take<int32_t>(TK);
     w.w = cv.take<float>(TK);
     w.score = cv.take<float>(TK);
@@ -102,21 +104,27 @@ int moe_forward_device(Layer *L, const float *d_x, int T, float *d_out, MoeWork 
         return moe_forward_device(L, d_x, T, d_out, wout, d_status, st);
     }
     w.status = d_status;
-    const int one = 1;
-    URB_CUDA(ctx, cudaMemcpyAsync(w.lofree, &one, 4, cudaMemcpyHostToDevice, st));
-
-    prof_begin(ctx, URB_K_ROW_SHIFT, st);
-    rc = launch_row_shift(d_x, T, int(H), int(H), w.shift, d_status, st, w.lofree,
-                          L->fmt == URB_FMT_BF16 ? 1 : 0);
-    prof_end(ctx, st);
-    if (rc) return cuda_fail(ctx, cudaGetLastError(), "row shift");
+    if (!L->use_tc) {
+        const int one = 1;
+        URB_CUDA(ctx, cudaMemcpyAsync(w.lofree, &one, 4, cudaMemcpyHostToDevice, st));
+        // Power-of-two row shifts of the mma.sync passes' f16 hi/lo activation columns.  The
+        // tensor-core passes need none: non-finite inputs surface as non-finite router logits
+        // (rejected by the routing kernel) or non-finite activations (rejected by the prep).
+        prof_begin(ctx, URB_K_ROW_SHIFT, st);
+        rc = launch_row_shift(d_x, T, int(H), int(H), w.shift, d_status, st, w.lofree,
+                              L->fmt == URB_FMT_BF16 ? 1 : 0);
+        prof_end(ctx, st);
+        if (rc) return cuda_fail(ctx, cudaGetLastError(), "row shift");
+    }
     prof_begin(ctx, URB_K_ROUTER_LOGITS, st);
-    rc = launch_router_logits(L->router, d_x, T, w.logits, st);
+    // Exact logits, with the sigmoid gates and biased selection scores in the same kernel.
+    const RouterGates rg{ctx, L->d_bias, w.gate, w.sel, d_status};
+    rc = launch_router_logits(L->router, d_x, T, w.logits, st, &rg);
     prof_end(ctx, st);
     if (rc) return cuda_fail(ctx, cudaGetLastError(), "router logits");
     prof_begin(ctx, URB_K_ROUTE, st);
     rc = launch_route_noaux(ctx, w.logits, L->d_bias, T, int(E), L->geo, w.ids, w.w, w.score,
-                            d_status, st);
+                            d_status, st, &rg);
     prof_end(ctx, st);
     if (rc) return rc;
 

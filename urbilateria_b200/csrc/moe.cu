@@ -211,9 +211,23 @@ __device__ __forceinline__ long long bs_group_bytes(int fmt, int c, int ks) {
     return (long long)ks * ((long long)(nsub - 1) * bs_bstage_bytes(fmt, kBsNmax) + bs_bstage_bytes(fmt, n_last));
 }
 
+// Activation slot of token j of a group whose stages start at boff.
+__device__ __forceinline__ BsSlot slot_of(int fmt, long long boff, int ks, int c, int j) {
+    const int cap = bs_cap(fmt);
+    const int nsub = (c + cap - 1) / cap, sub = j / cap;
+    BsSlot z;
+    z.base = boff + sub * (long long)ks * bs_bstage_bytes(fmt, kBsNmax);
+    z.slot = j - sub * cap;
+    z.n = sub < nsub - 1 ? kBsNmax : round16(bs_rows_per_tok(fmt) * (c - (nsub - 1) * cap));
+    return z;
+}
+
+// Dynamic shared memory: the unit_begin of every group of the pass (binary-searched by the
+// cooperative unit-map fill).
 __global__ void __launch_bounds__(1024) k_build_tc_segs(TcBuildArgs b) {
-    __shared__ long long wsum[32];
-    __shared__ int wcnt[32], wunits[32];
+    extern __shared__ int s_ub[];
+    __shared__ long long wsum[32], sh_boff;
+    __shared__ int wcnt[32], wunits[32], s_groups, s_units;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     if (b.status && *b.status) {  // an earlier stage failed: no work for the passes
         if (tid < 4) b.scalars[tid] = 0;
@@ -267,6 +281,7 @@ __global__ void __launch_bounds__(1024) k_build_tc_segs(TcBuildArgs b) {
         int ub = iu - nu + (warp ? wunits[warp - 1] : 0);
         long long boff = ib - nb + (warp ? wsum[warp - 1] : 0);
         TcSeg *out = pass == 0 ? b.gu : b.dn;
+        BsSlot *sl = pass == 0 ? b.gu_slots : b.dn_slots;
         auto emit = [&](const uint8_t *wg, int m, int col0, int c) {
             TcSeg s;
             s.w = wg;
@@ -281,40 +296,28 @@ __global__ void __launch_bounds__(1024) k_build_tc_segs(TcBuildArgs b) {
             s.unit_begin = ub;
             s.out_off = m * b.inter;  // gate | up halves of a gate/up output row
             s.pad = 0;
-            int *um = pass == 0 ? b.gu_units : b.dn_units;
-            for (int r = 0; r < mts * s.nsub; ++r) um[ub + r] = gi;
+            s_ub[gi] = ub;
             out[gi++] = s;
             ub += mts * s.nsub;
-            if (m == 0) {
-                // Activation slots of the group's columns (the up group reads the same stages).
-                BsSlot *sl = pass == 0 ? b.gu_slots : b.dn_slots;
-                const int cap = bs_cap(b.fmt);
-                const long long sub_bytes = (long long)ks * bs_bstage_bytes(b.fmt, kBsNmax);
-                const int n_last = round16(bs_rows_per_tok(b.fmt) * (c - (s.nsub - 1) * cap));
-                for (int j = 0; j < c; ++j) {
-                    const int sub = j / cap;
-                    BsSlot z;
-                    z.base = boff + sub * sub_bytes;
-                    z.slot = j - sub * cap;
-                    z.n = sub < s.nsub - 1 ? kBsNmax : n_last;
-                    sl[col0 + j] = z;
-                }
-            }
         };
         for (int e = e0; e < e1; ++e) {
             const int c = b.counts[e];
             if (c <= 0) continue;
+            const int col0 = b.offsets[e];
             if (pass == 0) {
-                emit(b.gate_tc[e], 0, b.offsets[e], c);
-                emit(b.up_tc[e], 1, b.offsets[e], c);
+                emit(b.gate_tc[e], 0, col0, c);
+                emit(b.up_tc[e], 1, col0, c);
             } else {
-                emit(b.down_tc[e], 0, b.offsets[e], c);
+                emit(b.down_tc[e], 0, col0, c);
             }
+            // Activation slots of the expert's columns (the up group reads the gate's stages).
+            for (int j = 0; j < c; ++j) sl[col0 + j] = slot_of(b.fmt, boff, ks, c, j);
             boff += bs_group_bytes(b.fmt, c, ks);
         }
         __syncthreads();
         if (tid == 1023) {
             // gi / ub / boff of the last thread are the routed totals; append the shared expert.
+            sh_boff = boff;
             if (b.has_shared && b.tokens > 0) {
                 if (pass == 0) {
                     emit(b.sh_gate_tc, 0, TK, b.tokens);
@@ -323,8 +326,25 @@ __global__ void __launch_bounds__(1024) k_build_tc_segs(TcBuildArgs b) {
                     emit(b.sh_down_tc, 0, TK, b.tokens);
                 }
             }
+            s_groups = gi;
+            s_units = ub;
             b.scalars[2 * pass] = gi;
             b.scalars[2 * pass + 1] = ub;
+        }
+        __syncthreads();
+        // Shared expert's activation slots and the unit -> group map, by all threads.
+        if (b.has_shared)
+            for (int j = tid; j < b.tokens; j += 1024)
+                sl[TK + j] = slot_of(b.fmt, sh_boff, ks, b.tokens, j);
+        int *um = pass == 0 ? b.gu_units : b.dn_units;
+        const int G = s_groups, U = s_units;
+        for (int u = tid; u < U; u += 1024) {
+            int lo = 0, hi = G - 1;
+            while (lo < hi) {
+                const int mid = (lo + hi + 1) >> 1;
+                if (s_ub[mid] <= u) lo = mid; else hi = mid - 1;
+            }
+            um[u] = lo;
         }
         __syncthreads();
     }
@@ -333,7 +353,10 @@ __global__ void __launch_bounds__(1024) k_build_tc_segs(TcBuildArgs b) {
 }  // namespace
 
 int launch_build_tc_segs(Ctx *ctx, const TcBuildArgs &b, cudaStream_t st) {
-    k_build_tc_segs<<<1, 1024, 0, st>>>(b);
+    const size_t smem = size_t(2 * b.experts + 4) * sizeof(int);
+    if (smem > 200 * 1024) return set_error(ctx, URB_ERR_UNSUPPORTED, "too many experts for the group builder");
+    URB_CUDA(ctx, cudaFuncSetAttribute(k_build_tc_segs, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
+    k_build_tc_segs<<<1, 1024, smem, st>>>(b);
     URB_CUDA(ctx, cudaGetLastError());
     return URB_OK;
 }

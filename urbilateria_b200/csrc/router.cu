@@ -33,10 +33,29 @@ __device__ __forceinline__ double widen(const void *w, size_t idx) {
 // column-major (lane-contiguous), the token pair's x values as one broadcast 16-byte load.
 // Column tiles are double-buffered; the next tile is fetched into registers while the current
 // one is consumed.
+// Sigmoid gate and biased selection score of one logit (routing.rs:101-105), libm-exact.
+__device__ __forceinline__ void gate_of(float l, float b, const ExpfTable &tab, float *gate,
+                                        float *sel, int32_t *status) {
+    if (!isfinite(l) || !isfinite(b)) atomicCAS(status, 0, int32_t(URB_ERR_NONFINITE));
+    const float gv = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf_libm(-l, tab)));
+    *gate = gv;
+    *sel = __fadd_rn(gv, b);
+}
+
+// Optional epilogue of the logits kernel: the route_noaux_tc gates and selection scores of
+// every (token, expert), so that the routing kernel only ranks.
+struct GateOut {
+    const float *bias;
+    float *gate, *sel;
+    int32_t *status;
+    ExpfTable tab;
+};
+
 template <bool BF16>
 __global__ void __launch_bounds__(32 * kRouterWarps) k_router_logits(const void *w, int experts,
                                                                      int cols, const float *x,
-                                                                     int tokens, float *logits) {
+                                                                     int tokens, float *logits,
+                                                                     GateOut go) {
     constexpr int KC = kRouterKc, NT = 32 * kRouterWarps;
     constexpr int WPT = 32 * KC / NT;          // weights fetched per thread per tile (16)
     constexpr int XPT = kRouterTok * KC / NT;  // x values fetched per thread per tile (4)
@@ -100,8 +119,15 @@ __global__ void __launch_bounds__(32 * kRouterWarps) k_router_logits(const void 
     }
     const int e = e0 + lane, t = t0 + kRouterTpt * warp;
     if (e < experts) {
-        if (t < tokens) logits[size_t(t) * experts + e] = float(acc0);
-        if (t + 1 < tokens) logits[size_t(t + 1) * experts + e] = float(acc1);
+        const float l0 = float(acc0), l1 = float(acc1);
+        if (t < tokens) logits[size_t(t) * experts + e] = l0;
+        if (t + 1 < tokens) logits[size_t(t + 1) * experts + e] = l1;
+        if (go.gate) {
+            const float b = go.bias[e];
+            const size_t i0 = size_t(t) * experts + e, i1 = i0 + experts;
+            if (t < tokens) gate_of(l0, b, go.tab, go.gate + i0, go.sel + i0, go.status);
+            if (t + 1 < tokens) gate_of(l1, b, go.tab, go.gate + i1, go.sel + i1, go.status);
+        }
     }
 }
 
@@ -123,7 +149,10 @@ __device__ __forceinline__ void set_status(int32_t *status, int code) {
 }
 
 // One warp per token.  Shared memory per warp (warp_bytes): gate[E], sel[E], group score
-// [n_group] floats, then one flag byte per expert (1 allowed, 2 taken, 0 masked).
+// [n_group] floats, then one flag byte per expert (1 allowed, 2 taken, 0 masked).  PRE: the
+// gates and selection scores come precomputed (logits kernel epilogue, which also reported
+// non-finite logits or biases) in `logits` / `bias` as [tokens, E] arrays.
+template <bool PRE>
 __global__ void k_route_noaux(const float *logits, const float *bias, int tokens, int E,
                               int top_k, int n_group, int topk_group, int normalize,
                               float scaling, ExpfTable tab, int32_t *out_e, float *out_w,
@@ -138,14 +167,43 @@ __global__ void k_route_noaux(const float *logits, const float *bias, int tokens
     uint8_t *flags = reinterpret_cast<uint8_t *>(gscore + n_group);
     const float *lg = logits + size_t(t) * E;
     bool bad = false;
-    for (int i = lane; i < E; i += 32) {
-        float l = lg[i], b = bias[i];
-        bad |= !isfinite(l) || !isfinite(b);
-        float ex = expf_libm(-l, tab);  // routing.rs:103: 1 / (1 + exp(-logit))
-        float gv = __fdiv_rn(1.0f, __fadd_rn(1.0f, ex));
-        gate[i] = gv;
-        sel[i] = __fadd_rn(gv, b);
-        flags[i] = 1;
+    if (PRE) {
+        const float *sg = bias + size_t(t) * E;
+        for (int i = lane; i < E; i += 32) {
+            gate[i] = lg[i];
+            sel[i] = sg[i];
+            flags[i] = 1;
+        }
+    }
+    // routing.rs:103: gate = 1 / (1 + exp(-logit)).  Eight experts per lane at a time, with all
+    // of their exception-table loads issued before any is used (independent, in flight together).
+    constexpr int kB = 8;
+    for (int i0 = 0; !PRE && i0 < E; i0 += 32 * kB) {
+        float l[kB], b[kB];
+        uint32_t lo[kB], hi[kB];
+#pragma unroll
+        for (int j = 0; j < kB; ++j) {
+            const int i = i0 + 32 * j + lane;
+            l[j] = i < E ? lg[i] : 0.0f;
+            b[j] = i < E ? bias[i] : 0.0f;
+        }
+#pragma unroll
+        for (int j = 0; j < kB; ++j) {
+            const uint32_t bucket = __float_as_uint(-l[j]) >> 12;
+            lo[j] = tab.index ? tab.index[bucket] : 0;
+            hi[j] = tab.index ? tab.index[bucket + 1] : 0;
+        }
+#pragma unroll
+        for (int j = 0; j < kB; ++j) {
+            const int i = i0 + 32 * j + lane;
+            if (i >= E) continue;
+            bad |= !isfinite(l[j]) || !isfinite(b[j]);
+            const float ex = expf_libm_range(-l[j], tab, lo[j], hi[j]);
+            const float gv = __fdiv_rn(1.0f, __fadd_rn(1.0f, ex));
+            gate[i] = gv;
+            sel[i] = __fadd_rn(gv, b[j]);
+            flags[i] = 1;
+        }
     }
     if (__any_sync(0xffffffffu, bad)) {
         // Rejected token: report, and leave distinct valid ids with zero weight so that the
@@ -303,16 +361,18 @@ ExpfTable table_of(const Ctx *ctx) { return ExpfTable{ctx->expf_keys, ctx->expf_
 }  // namespace
 
 int launch_router_logits(const Mat *router, const float *d_x, int tokens, float *d_logits,
-                         cudaStream_t st) {
+                         cudaStream_t st, const RouterGates *rg) {
     if (tokens <= 0) return URB_OK;
+    GateOut go{};
+    if (rg) go = GateOut{rg->bias, rg->gate, rg->sel, rg->status, table_of(rg->ctx)};
     dim3 grid(unsigned((router->rows + 31) / 32), unsigned((tokens + kRouterTok - 1) / kRouterTok));
     constexpr int nt = 32 * kRouterWarps;
     if (router->format == URB_FMT_BF16)
         k_router_logits<true><<<grid, nt, 0, st>>>(router->raw_values, int(router->rows),
-                                                   int(router->cols), d_x, tokens, d_logits);
+                                                   int(router->cols), d_x, tokens, d_logits, go);
     else if (router->format == URB_FMT_F32)
         k_router_logits<false><<<grid, nt, 0, st>>>(router->raw_values, int(router->rows),
-                                                    int(router->cols), d_x, tokens, d_logits);
+                                                    int(router->cols), d_x, tokens, d_logits, go);
     else
         return URB_ERR_UNSUPPORTED;
     return cudaGetLastError() == cudaSuccess ? URB_OK : URB_ERR_CUDA;
@@ -320,15 +380,17 @@ int launch_router_logits(const Mat *router, const float *d_x, int tokens, float 
 
 int launch_route_noaux(Ctx *ctx, const float *d_logits, const float *d_bias, int tokens,
                        int experts, const urb_moe_geometry &g, int32_t *d_expert,
-                       float *d_weight, float *d_score, int32_t *d_status, cudaStream_t st) {
+                       float *d_weight, float *d_score, int32_t *d_status, cudaStream_t st,
+                       const RouterGates *pre) {
     if (tokens <= 0) return URB_OK;
     int warps = 4;
     int warp_bytes = int(((2 * size_t(experts) + g.n_group) * 4 + experts + 15) & ~size_t(15));
     size_t smem = size_t(warps) * warp_bytes;
-    k_route_noaux<<<(tokens + warps - 1) / warps, warps * 32, smem, st>>>(
-        d_logits, d_bias, tokens, experts, int(g.top_k), int(g.n_group), int(g.topk_group),
-        g.normalize, g.routed_scaling_factor, table_of(ctx), d_expert, d_weight, d_score,
-        d_status, warp_bytes);
+    auto k = pre ? k_route_noaux<true> : k_route_noaux<false>;
+    k<<<(tokens + warps - 1) / warps, warps * 32, smem, st>>>(
+        pre ? pre->gate : d_logits, pre ? pre->sel : d_bias, tokens, experts, int(g.top_k),
+        int(g.n_group), int(g.topk_group), g.normalize, g.routed_scaling_factor, table_of(ctx),
+        d_expert, d_weight, d_score, d_status, warp_bytes);
     URB_CUDA(ctx, cudaGetLastError());
     return URB_OK;
 }

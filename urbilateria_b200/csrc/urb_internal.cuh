@@ -157,11 +157,19 @@ int launch_row_shift(const float *d_src, int rows, int cols, int stride, int32_t
                      int32_t *d_status, cudaStream_t stream, int32_t *d_lofree = nullptr,
                      int bf16_check = 0);
 // router.cu
+// Gates and selection scores of route_noaux_tc computed in the logits kernel's epilogue.
+struct RouterGates {
+    const Ctx *ctx;
+    const float *bias;
+    float *gate, *sel;  // [tokens, experts]
+    int32_t *status;    // non-finite logit or bias -> URB_ERR_NONFINITE
+};
 int launch_router_logits(const Mat *router, const float *d_x, int tokens, float *d_logits,
-                         cudaStream_t stream);
+                         cudaStream_t st, const RouterGates *gates = nullptr);
 int launch_route_noaux(Ctx *ctx, const float *d_logits, const float *d_bias, int tokens,
                        int experts, const urb_moe_geometry &g, int32_t *d_expert,
-                       float *d_weight, float *d_score, int32_t *d_status, cudaStream_t stream);
+                       float *d_weight, float *d_score, int32_t *d_status, cudaStream_t st,
+                       const RouterGates *pre = nullptr);
 int launch_route_softmax(Ctx *ctx, const float *d_logits, int tokens, int experts, int top_k,
                          int32_t *d_expert, float *d_weight, int32_t *d_status,
                          cudaStream_t stream);

@@ -69,6 +69,7 @@ struct Layer {
 struct MoeWork {
     int32_t *shift;       // [T]
     float *logits;        // [T, E]
+    float *gate, *sel;    // [T, E] sigmoid gates and biased selection scores
     int32_t *ids;         // [T, K]
     float *w, *score;     // [T, K]
     int32_t *counts, *offsets, *perm_token, *perm_slot, *inv;
