@@ -167,7 +167,7 @@ __global__ void __launch_bounds__(kThreadsBs, 1) k_bs_grouped(TcArgs a) {
         for (UnitCursor uc(a, total_units); uc.valid() && !*abortp; uc.advance()) {
             const TcSeg &S = uc.cur;
             const Unit x = unit_of<FMT>(S, uc.u);
-            const uint8_t *wsrc = S.w + size_t(x.mt) * S.ks * TB;
+            const uint8_t *wsrc = S.w + size_t(x.mt) * TB;  // tile (mt, ks) at (ks * mts + mt)
             bool ok = true;
             for (int ks = 0; ks < S.ks; ++ks, ++g) {
                 const int sa = int(g % kSA);
@@ -176,7 +176,7 @@ __global__ void __launch_bounds__(kThreadsBs, 1) k_bs_grouped(TcArgs a) {
                     break;
                 }
                 tc::mbar_arrive_expect_tx(&a_full[sa], uint32_t(TB));
-                tc::bulk_g2s(ring_a + size_t(sa) * kStage, wsrc + size_t(ks) * TB, TB, &a_full[sa]);
+                tc::bulk_g2s(ring_a + size_t(sa) * kStage, wsrc + size_t(ks) * S.mts * TB, TB, &a_full[sa]);
             }
             if (!ok) { fail(); break; }
         }
@@ -527,9 +527,9 @@ __global__ void k_repack_bs(const uint8_t *values, const uint8_t *scales, size_t
     const size_t id = blockIdx.x * size_t(blockDim.x) + threadIdx.x;
     if (id >= size_t(mts) * ks_n * 128) return;
     const int r = int(id & 127);
-    const size_t tile = id >> 7;
-    const int ks = int(tile % ks_n);
-    const size_t mt = tile / ks_n;
+    const size_t tile = id >> 7;  // K-stage major: tile (mt, ks) at ks * mts + mt
+    const size_t mt = tile % mts;
+    const int ks = int(tile / mts);
     const size_t row = mt * 128 + r;
     constexpr int TB = bs_tile_bytes(FMT);
     constexpr int KBS = FMT == URB_FMT_MXFP4 ? 8 : 4;
