@@ -8,8 +8,11 @@ chunk per GPU (x ~ N(0,1) bf16).  Random-init, seeded synthetic weights (no chec
   value     tokens/s, inputs already in HBM (urb_moe_forward_device), device-timed
   e2e       tokens/s through the host-pointer C ABI (urb_moe_forward), H2D of x and D2H of the
             output + routes inside the timed region
-  roofline  the dominant kernel (grouped gate/up pass): algorithmic bytes per launch / its mean
-            CUDA-event duration, against the measured HBM copy bandwidth
+  roofline  the dominant kernel (block-scaled grouped gate/up pass, k_bs_grouped): algorithmic
+            bytes per launch (touched experts' packed MXFP4 gate+up tiles + the f32 gate|up
+            outputs) / its mean CUDA-event duration, against the measured HBM copy bandwidth;
+            `traffic` is the DRAM bytes per launch from the committed ncu capture
+            (profiles/k_bs_grouped_c2_traffic.md)
   cpu_baseline / --impl reference: the CPU restatement of the reference path (oracle/) on the
             host cores, on a bounded token sample
 
@@ -37,6 +40,18 @@ EXPERTS = 256
 SEED = 20261201
 
 
+def profiled_traffic():
+    """DRAM bytes per gate/up launch recorded by the committed ncu capture, or None."""
+    p = os.path.join(ROOT, "profiles", "k_bs_grouped_c2_traffic.md")
+    try:
+        for line in open(p):
+            if line.startswith("roofline-traffic gate_up_dram_bytes_per_launch"):
+                return int(line.split()[-1])
+    except OSError:
+        pass
+    return None
+
+
 def peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
@@ -48,7 +63,7 @@ def peaks():
 class ClockSampler:
     """SM clock and throttle reasons sampled through NVML during the timed region (read-only)."""
 
-    def __init__(self, device: int, period_s: float = 0.05):
+    def __init__(self, device: int, period_s: float = 0.01):
         self.device, self.period, self.rows = device, period_s, []
         self._stop = threading.Event()
 
@@ -152,10 +167,13 @@ def run_reference(args, rank, world):
     x = make_input(SEED, 0)
     for _ in range(max(0, min(args.warmup, 1))):
         layer.forward(x[:1], threads=threads)
+    # Each step is a bounded sample; the whole run stays within about two minutes whatever
+    # --steps is (at least 0.5 s of work per step).
+    step_s = max(0.5, min(args.ref_step_s, 120.0 / max(1, args.steps)))
     vals = []
     t_all = time.perf_counter()
     for s in range(args.steps):
-        tps, n, el = cpu_tokens_per_s(layer, x[s % TOKENS:], args.ref_step_s, threads)
+        tps, n, el = cpu_tokens_per_s(layer, x[s % TOKENS:], step_s, threads)
         vals.append(tps)
     total = time.perf_counter() - t_all
     v = statistics.median(vals)
@@ -165,9 +183,9 @@ def run_reference(args, rank, world):
             "vs_baseline": None, "dtype": "f64", "data": "synthetic",
             "config": workload_config(world),
             "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": threads, "kind": "port",
-                             "sample": "token-by-token GLM composition until %.0fs per step "
+                             "sample": "token-by-token GLM composition until %.1fs per step "
                                        "(oracle/urb_oracle.cpp, ordered-F64 Rayon-style row "
-                                       "parallelism)" % args.ref_step_s},
+                                       "parallelism)" % step_s},
             "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0},
             "wall_s": total}
@@ -219,7 +237,7 @@ def workload_config(world):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--ref-step-s", type=float, default=4.0)
@@ -352,16 +370,17 @@ def main():
     value = tokens_total / (ms / 1e3)
     e2e = tokens_total / (ms_e2e / 1e3)
 
-    # Roofline of the dominant kernel: grouped gate/up streams gate+up of every touched expert
-    # and of the shared expert once: 2 * (7,340,032 packed + 458,752 scale) bytes per expert.
+    # Roofline of the dominant kernel: the grouped gate/up pass streams gate+up of every
+    # touched expert and of the shared expert once, 2 * (7,340,032 packed + 458,752 scale)
+    # bytes per expert, and writes the f32 gate|up rows of every activation column.
     gu_bytes_per_expert = 2 * (INTER * HIDDEN // 2 + INTER * HIDDEN // 32)
-    gu_bytes = (touched + 1) * gu_bytes_per_expert + TOKENS * HIDDEN * 4 + \
-        (TOKENS * TOP_K + TOKENS) * INTER * 4
+    gu_bytes = (touched + 1) * gu_bytes_per_expert + (TOKENS * TOP_K + TOKENS) * 2 * INTER * 4
     gu = kern.get("gate_up", {})
     achieved = gu_bytes / (gu.get("ms_per_launch", float("nan")) / 1e3) / 1e9
-    roofline = {"kernel": "k_grouped<MXFP4,pair> (gate/up + SwiGLU)", "bound": "hbm",
-                "achieved": achieved, "peak": pk_hbm, "unit": "GB/s", "frac": achieved / pk_hbm,
-                "peak_kind": pk_kind, "bytes_per_launch": gu_bytes, "traffic": None}
+    roofline = {"kernel": "k_bs_grouped<MXFP4> gate/up (tcgen05.mma kind::mxf4 block_scale)",
+                "bound": "hbm", "achieved": achieved, "peak": pk_hbm, "unit": "GB/s",
+                "frac": achieved / pk_hbm, "peak_kind": pk_kind, "bytes_per_launch": gu_bytes,
+                "traffic": profiled_traffic()}
     dn_bytes = (touched + 1) * (HIDDEN * INTER // 2 + HIDDEN * INTER // 32)
     dn = kern.get("down", {})
     layer_bytes = (touched + 1) * 3 * (INTER * HIDDEN // 2 + INTER * HIDDEN // 32) + \
@@ -370,7 +389,9 @@ def main():
     line = {"metric": "moe_layer_tokens_per_s", "value": value, "unit": "tokens/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f16xf16->f32 (MXFP4 decoded exactly)",
+            "vs_baseline": None,
+            "dtype": "mxf4: E2M1 weights x E2M1 activation residual terms (6 per token), E8M0 "
+                     "scales, f32 accumulate",
             "data": "synthetic", "config": workload_config(world),
             "e2e": {"value": e2e, "unit": "tokens/s",
                     "h2d_bytes_per_step": TOKENS * HIDDEN * 4,
@@ -379,7 +400,7 @@ def main():
             "layer_hbm_gbs": layer_bytes / (ms / args.steps / 1e3) / 1e9,
             "down_gbs": dn_bytes / (dn.get("ms_per_launch", float("nan")) / 1e3) / 1e9,
             "touched_experts": touched, "kernels": kern, "matvec_c0": matvec,
-            "gpu_launches": 7 * args.steps,
+            "gpu_launches": sum(v["launches"] for v in kern.values()),
             "clocks": clk.summary()}
 
     if rank == 0 and world == 1 and not args.no_cpu:

@@ -209,7 +209,9 @@ typedef enum urb_kernel_kind {
     URB_K_DOWN = 5,
     URB_K_COMBINE = 6,
     URB_K_PRODUCT = 7,
-    URB_K_COUNT = 8
+    URB_K_PREP = 8,         /* activation residual terms of a tensor-core pass */
+    URB_K_GROUP_BUILD = 9,  /* device-side group / unit tables of the tensor-core passes */
+    URB_K_COUNT = 10
 } urb_kernel_kind;
 URB_API int urb_profile_enable(urb_ctx *ctx, int on);
 /* Synchronises pending events; returns the total device time and launch count of `kind`. */

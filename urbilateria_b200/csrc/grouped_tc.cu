@@ -567,25 +567,29 @@ __global__ void k_repack_bs(const uint8_t *values, const uint8_t *scales, size_t
 }
 
 template <int FMT>
-int launch_bs_t(Ctx *ctx, const TcArgs &a, cudaStream_t st) {
+int launch_bs_t(Ctx *ctx, const TcArgs &a, int kind, cudaStream_t st) {
     constexpr int KBS = FMT == URB_FMT_MXFP4 ? 8 : 4;
     const long long threads = (long long)a.nrows * a.ks * KBS * 4;
     if (threads > 0) {
+        prof_begin(ctx, URB_K_PREP, st);
         k_bs_prep<FMT><<<unsigned((threads + 255) / 256), 256, 0, st>>>(a);
+        prof_end(ctx, st);
         URB_CUDA(ctx, cudaGetLastError());
     }
     auto k = k_bs_grouped<FMT>;
     URB_CUDA(ctx, cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBs));
+    prof_begin(ctx, kind, st);
     k<<<ctx->num_sms, kThreadsBs, kSmemBs, st>>>(a);
+    prof_end(ctx, st);
     URB_CUDA(ctx, cudaGetLastError());
     return URB_OK;
 }
 
 }  // namespace
 
-int launch_tc_grouped(Ctx *ctx, int fmt, const TcArgs &a, cudaStream_t st) {
-    if (fmt == URB_FMT_MXFP4) return launch_bs_t<URB_FMT_MXFP4>(ctx, a, st);
-    if (fmt == URB_FMT_MXFP8) return launch_bs_t<URB_FMT_MXFP8>(ctx, a, st);
+int launch_tc_grouped(Ctx *ctx, int fmt, const TcArgs &a, int kind, cudaStream_t st) {
+    if (fmt == URB_FMT_MXFP4) return launch_bs_t<URB_FMT_MXFP4>(ctx, a, kind, st);
+    if (fmt == URB_FMT_MXFP8) return launch_bs_t<URB_FMT_MXFP8>(ctx, a, kind, st);
     return set_error(ctx, URB_ERR_UNSUPPORTED, "tc pass: format");
 }
 

@@ -201,7 +201,9 @@ int moe_forward_device(Layer *L, const float *d_x, int T, float *d_out, MoeWork 
         bb.dn_units = w.units_dn;
         bb.scalars = w.tscalars;
         bb.status = d_status;
+        prof_begin(ctx, URB_K_GROUP_BUILD, st);
         rc = launch_build_tc_segs(ctx, bb, st);
+        prof_end(ctx, st);
         if (rc) return rc;
 
         // Gate and up projections of every (expert, token) column: [cols, 2I] gate | up.
@@ -224,9 +226,7 @@ int moe_forward_device(Layer *L, const float *d_x, int T, float *d_out, MoeWork 
         ga.out = w.gu;
         ga.out_stride = int(2 * I);
         ga.status = d_status;
-        prof_begin(ctx, URB_K_GATE_UP, st);
-        rc = launch_tc_grouped(ctx, L->fmt, ga, st);
-        prof_end(ctx, st);
+        rc = launch_tc_grouped(ctx, L->fmt, ga, URB_K_GATE_UP, st);
         if (rc) return rc;
 
         // Down projection of h = silu(gate) * up (formed while writing its activation terms).
@@ -247,9 +247,7 @@ int moe_forward_device(Layer *L, const float *d_x, int T, float *d_out, MoeWork 
         da.out = w.y;
         da.out_stride = int(H);
         da.status = d_status;
-        prof_begin(ctx, URB_K_DOWN, st);
-        rc = launch_tc_grouped(ctx, L->fmt, da, st);
-        prof_end(ctx, st);
+        rc = launch_tc_grouped(ctx, L->fmt, da, URB_K_DOWN, st);
         if (rc) return rc;
 
         prof_begin(ctx, URB_K_COMBINE, st);

@@ -119,8 +119,8 @@ struct Ctx {
     struct ProfRec { int kind; cudaEvent_t a, b; };
     std::vector<ProfRec> prof_pending;
     std::vector<cudaEvent_t> prof_free;
-    double prof_ms[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    long long prof_n[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    double prof_ms[URB_K_COUNT] = {};
+    long long prof_n[URB_K_COUNT] = {};
     int prof_open = -1;
     cudaEvent_t prof_open_ev = nullptr;
 };

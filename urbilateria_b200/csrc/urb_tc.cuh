@@ -73,8 +73,9 @@ struct TcArgs {
     int32_t *status;
 };
 
-// Prep (activation terms) + tensor-core pass over every group of the launch.
-int launch_tc_grouped(Ctx *ctx, int fmt, const TcArgs &a, cudaStream_t st);
+// Prep (activation terms) + tensor-core pass over every group of the launch; the profiler
+// records the prep as URB_K_PREP and the pass as `kind`.
+int launch_tc_grouped(Ctx *ctx, int fmt, const TcArgs &a, int kind, cudaStream_t st);
 int repack_tc(Ctx *ctx, Mat *m, cudaStream_t st);
 
 }  // namespace urb

@@ -25,9 +25,10 @@ ERR_INVALID_ARGUMENT = 9
 FMT_F32, FMT_BF16, FMT_MXFP8, FMT_MXFP4 = 0, 1, 2, 3
 
 # urb_kernel_kind
-K_ROW_SHIFT, K_ROUTER_LOGITS, K_ROUTE, K_PERMUTE, K_GATE_UP, K_DOWN, K_COMBINE, K_PRODUCT = range(8)
+(K_ROW_SHIFT, K_ROUTER_LOGITS, K_ROUTE, K_PERMUTE, K_GATE_UP, K_DOWN, K_COMBINE, K_PRODUCT,
+ K_PREP, K_GROUP_BUILD) = range(10)
 KERNEL_NAMES = ["row_shift", "router_logits", "route", "permute", "gate_up", "down", "combine",
-                "product"]
+                "product", "prep", "group_build"]
 
 STATUS_NAMES = {
     ERR_SHAPE: "Shape", ERR_INVALID_SCALE: "InvalidScale", ERR_NONFINITE: "NonFinite",
