@@ -65,6 +65,7 @@ int moe_forward_device(Layer *L, const float *d_x, int T, float *d_out, MoeWork 
     MoeWork w{};
     w.shift = cv.take<int32_t>(T);
     w.logits = cv.take<float>(size_t(T) * E);
+    w.x64 = cv.take<double>(size_t(T) * H);
     w.gate = cv.take<float>(size_t(T) * E);
     w.sel = cv.take<float>(size_t(T) * E);
     w.ids = cv.take<int32_t>(TK);
@@ -119,7 +120,7 @@ int moe_forward_device(Layer *L, const float *d_x, int T, float *d_out, MoeWork 
     prof_begin(ctx, URB_K_ROUTER_LOGITS, st);
     // Exact logits, with the sigmoid gates and biased selection scores in the same kernel.
     const RouterGates rg{ctx, L->d_bias, w.gate, w.sel, d_status};
-    rc = launch_router_logits(L->router, d_x, T, w.logits, st, &rg);
+    rc = launch_router_logits_f64(L->router64, int(E), d_x, T, int(H), w.x64, w.logits, st, &rg);
     prof_end(ctx, st);
     if (rc) return cuda_fail(ctx, cudaGetLastError(), "router logits");
     prof_begin(ctx, URB_K_ROUTE, st);
@@ -457,10 +458,14 @@ int urb_moe_layer_create(urb_ctx *ctx, const urb_mat *router, const float *bias,
     // Block-scaled tcgen05 passes by default; URB_MOE_PATH=mma selects the mma.sync passes.
     L->use_tc = have_tc && !(path && std::strcmp(path, "mma") == 0);
     cudaError_t err = cudaMalloc(&L->d_tables, tables.size() * sizeof(void *));
+    if (err == cudaSuccess) err = cudaMalloc(&L->router64, experts * H * sizeof(double));
+    if (err == cudaSuccess && widen_router_f64(router, L->router64, ctx->stream) != URB_OK)
+        err = cudaGetLastError();
     if (err == cudaSuccess) err = cudaMalloc(&L->d_bias, experts * 4);
     if (err == cudaSuccess)
         err = cudaMemcpy(L->d_tables, tables.data(), tables.size() * sizeof(void *), cudaMemcpyHostToDevice);
     if (err == cudaSuccess) err = cudaMemcpy(L->d_bias, bias, experts * 4, cudaMemcpyDefault);
+    if (err == cudaSuccess) err = cudaStreamSynchronize(ctx->stream);  // router64 is ready
     if (err != cudaSuccess) {
         urb_moe_layer_free(L);
         return cuda_fail(ctx, err, "layer tables");
@@ -476,6 +481,7 @@ int urb_moe_layer_free(urb_layer *L) {
         cudaStreamSynchronize(L->ctx->stream);
     }
     if (L->d_tables) cudaFree(L->d_tables);
+    if (L->router64) cudaFree(L->router64);
     if (L->d_bias) cudaFree(L->d_bias);
     delete L;
     return URB_OK;

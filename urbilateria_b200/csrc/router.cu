@@ -3,9 +3,11 @@
 //  * Router logits: the reference evaluates each logit as a sequential F64 sum, in column
 //    order, of exact f64 products bf16(w) * x, starting from -0.0, rounded once to f32
 //    (src/model/bf16.rs:494-525 via glm/runtime/moe.rs:154).  A product of a bf16 and an f32
-//    is exact in f64, so fma(w, x, acc) equals the reference's multiply-then-add; one thread
-//    owns one (token, expert) chain and performs exactly the reference's additions, so the
-//    logits are bit-identical.
+//    is exact in f64, so fma(w, x, acc) equals the reference's multiply-then-add.  The chains
+//    run on the FP64 tensor path: mma.sync m8n8k4 f64 advances an 8 x 8 block of chains by four
+//    columns as four fused multiply-adds in column order (checked bit for bit against
+//    sequential FMA chains on B200), so the logits are bit-identical at a fraction of the
+//    latency of dependent DFMAs.
 //  * route_noaux_tc (src/math/routing.rs:38-155) and route_softmax_top_k
 //    (src/models/qwen3_8/moe.rs:91-159): one warp per token, IEEE f32 arithmetic in the
 //    reference's order, libm-exact expf, total_cmp ranking with the lower id winning ties.
@@ -128,6 +130,66 @@ __global__ void __launch_bounds__(32 * kRouterWarps) k_router_logits(const void 
             if (t < tokens) gate_of(l0, b, go.tab, go.gate + i0, go.sel + i0, go.status);
             if (t + 1 < tokens) gate_of(l1, b, go.tab, go.gate + i1, go.sel + i1, go.status);
         }
+    }
+}
+
+// Widens a bf16 (BF16) or f32 matrix to f64 (exact), grid-stride.
+template <bool BF16>
+__global__ void k_to_f64(const void *src, size_t n, double *dst) {
+    for (size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x; i < n;
+         i += size_t(gridDim.x) * blockDim.x)
+        dst[i] = widen<BF16>(src, i);
+}
+
+__device__ __forceinline__ void dmma_8x8x4(double &d0, double &d1, double a, double b) {
+    asm volatile("mma.sync.aligned.m8n8k4.row.col.f64.f64.f64.f64 {%0,%1}, {%2}, {%3}, {%0,%1};"
+                 : "+d"(d0), "+d"(d1)
+                 : "d"(a), "d"(b));
+}
+
+// One warp per 8 tokens x 8 experts, one warp per CTA so that the 512 blocks of a 128-token,
+// 256-expert forward spread over every SM (the FP64 path is throughput-bound per SM: CTAs of
+// four warps measured 1.9x slower).  A = x (row: token, k: column), B = router (k:
+// column, n: expert); lane q holds A[q/4][q%4], B[q%4][q/4] and D[q/4][2(q%4) .. +1].  The
+// columns past the last multiple of four are added by each lane with scalar FMAs, in order.
+constexpr int kDmmaWarps = 1;
+__global__ void __launch_bounds__(32 * kDmmaWarps) k_router_dmma(const double *x64,
+                                                                 const double *w64, int tokens,
+                                                                 int experts, int cols,
+                                                                 float *logits, GateOut go) {
+    const int lane = threadIdx.x & 31;
+    const int eblk = (experts + 7) / 8;
+    const int blk = blockIdx.x * kDmmaWarps + (threadIdx.x >> 5);
+    if (blk >= eblk * ((tokens + 7) / 8)) return;
+    const int tb = blk / eblk, eb = blk % eblk;
+    const int ar = tb * 8 + (lane >> 2), bc = eb * 8 + (lane >> 2), kq = lane & 3;
+    const bool arow = ar < tokens, bcol = bc < experts;
+    const double *xa = x64 + size_t(arow ? ar : 0) * cols + kq;
+    const double *wb = w64 + size_t(bcol ? bc : 0) * cols + kq;
+    double d0 = -0.0, d1 = -0.0;  // Iterator::sum over f64 starts from -0.0 (bf16.rs:500)
+    const int k4 = cols & ~3;
+#pragma unroll 8
+    for (int k = 0; k < k4; k += 4) {
+        const double a = arow ? xa[k] : 0.0, b = bcol ? wb[k] : 0.0;
+        dmma_8x8x4(d0, d1, a, b);
+    }
+    const int t = tb * 8 + (lane >> 2), e0 = eb * 8 + 2 * (lane & 3);
+    if (k4 < cols && t < tokens) {
+        const double *xr = x64 + size_t(t) * cols;
+        for (int k = k4; k < cols; ++k) {
+            if (e0 < experts) d0 = fma(w64[size_t(e0) * cols + k], xr[k], d0);
+            if (e0 + 1 < experts) d1 = fma(w64[size_t(e0 + 1) * cols + k], xr[k], d1);
+        }
+    }
+    if (t >= tokens) return;
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+        const int e = e0 + i;
+        if (e >= experts) continue;
+        const float l = float(i ? d1 : d0);
+        const size_t o = size_t(t) * experts + e;
+        logits[o] = l;
+        if (go.gate) gate_of(l, go.bias[e], go.tab, go.gate + o, go.sel + o, go.status);
     }
 }
 
@@ -375,6 +437,30 @@ int launch_router_logits(const Mat *router, const float *d_x, int tokens, float 
                                                     int(router->cols), d_x, tokens, d_logits, go);
     else
         return URB_ERR_UNSUPPORTED;
+    return cudaGetLastError() == cudaSuccess ? URB_OK : URB_ERR_CUDA;
+}
+
+int widen_router_f64(const Mat *router, double *dst, cudaStream_t st) {
+    const size_t n = router->rows * router->cols;
+    if (router->format == URB_FMT_BF16)
+        k_to_f64<true><<<1024, 256, 0, st>>>(router->raw_values, n, dst);
+    else if (router->format == URB_FMT_F32)
+        k_to_f64<false><<<1024, 256, 0, st>>>(router->raw_values, n, dst);
+    else
+        return URB_ERR_UNSUPPORTED;
+    return cudaGetLastError() == cudaSuccess ? URB_OK : URB_ERR_CUDA;
+}
+
+int launch_router_logits_f64(const double *w64, int experts, const float *d_x, int tokens,
+                             int cols, double *x64, float *d_logits, cudaStream_t st,
+                             const RouterGates *rg) {
+    if (tokens <= 0) return URB_OK;
+    GateOut go{};
+    if (rg) go = GateOut{rg->bias, rg->gate, rg->sel, rg->status, table_of(rg->ctx)};
+    k_to_f64<false><<<512, 256, 0, st>>>(d_x, size_t(tokens) * cols, x64);
+    const int blocks = ((tokens + 7) / 8) * ((experts + 7) / 8);
+    k_router_dmma<<<(blocks + kDmmaWarps - 1) / kDmmaWarps, 32 * kDmmaWarps, 0, st>>>(
+        x64, w64, tokens, experts, cols, d_logits, go);
     return cudaGetLastError() == cudaSuccess ? URB_OK : URB_ERR_CUDA;
 }
 

@@ -170,6 +170,12 @@ int launch_route_noaux(Ctx *ctx, const float *d_logits, const float *d_bias, int
                        int experts, const urb_moe_geometry &g, int32_t *d_expert,
                        float *d_weight, float *d_score, int32_t *d_status, cudaStream_t st,
                        const RouterGates *pre = nullptr);
+// Router logits on f64 copies: w64 [experts, cols] (widen_router_f64, resident), x64 [tokens,
+// cols] scratch widened from d_x here; bit-identical to the sequential F64 chain.
+int widen_router_f64(const Mat *router, double *dst, cudaStream_t st);
+int launch_router_logits_f64(const double *w64, int experts, const float *d_x, int tokens,
+                             int cols, double *x64, float *d_logits, cudaStream_t st,
+                             const RouterGates *gates = nullptr);
 int launch_route_softmax(Ctx *ctx, const float *d_logits, int tokens, int experts, int top_k,
                          int32_t *d_expert, float *d_weight, int32_t *d_status,
                          cudaStream_t stream);

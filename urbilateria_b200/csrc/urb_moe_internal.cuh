@@ -53,6 +53,7 @@ int launch_combine(Ctx *ctx, const float *y, const float *shared_y, const float 
 struct Layer {
     Ctx *ctx = nullptr;
     const Mat *router = nullptr;
+    double *router64 = nullptr;  // router widened to f64 (the logits' FP64 MMA operand)
     float *d_bias = nullptr;
     size_t experts = 0, hidden = 0, inter = 0;
     int fmt = 0;
@@ -70,6 +71,7 @@ struct MoeWork {
     int32_t *shift;       // [T]
     float *logits;        // [T, E]
     float *gate, *sel;    // [T, E] sigmoid gates and biased selection scores
+    double *x64;          // [T, H] x widened to f64
     int32_t *ids;         // [T, K]
     float *w, *score;     // [T, K]
     int32_t *counts, *offsets, *perm_token, *perm_slot, *inv;
