@@ -163,6 +163,14 @@ int device_product(Ctx *ctx, const Mat *m, size_t start, size_t count, const flo
         prof_end(ctx, st);
         return rc;
     }
+    if (batch == 1 && (m->format == URB_FMT_MXFP4 || m->format == URB_FMT_MXFP8) && !d_status) {
+        // Single-token product: the CUDA-core matvec (no activation shifts needed; input
+        // finiteness is checked by the host entry points, or through d_status below).
+        prof_begin(ctx, URB_K_PRODUCT, st);
+        int rc = launch_matvec1(ctx, m, start, count, d_x, d_y, st);
+        prof_end(ctx, st);
+        return rc;
+    }
     int rb_lo = int(start / 16), rb_hi = int(div_ceil(start + count, 16));
     size_t out_rows = size_t(rb_hi - rb_lo) * 16;
     int rc;

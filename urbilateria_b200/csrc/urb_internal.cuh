@@ -173,6 +173,9 @@ int launch_route_noaux(Ctx *ctx, const float *d_logits, const float *d_bias, int
 // Router logits on f64 copies: w64 [experts, cols] (widen_router_f64, resident), x64 [tokens,
 // cols] scratch widened from d_x here; bit-identical to the sequential F64 chain.
 int widen_router_f64(const Mat *router, double *dst, cudaStream_t st);
+// Single-token product of rows [start, start + count) of a tiled MXFP4 / MXFP8 matrix.
+int launch_matvec1(Ctx *ctx, const Mat *m, size_t start, size_t count, const float *d_x,
+                   float *d_y, cudaStream_t st);
 int launch_router_logits_f64(const double *w64, int experts, const float *d_x, int tokens,
                              int cols, double *x64, float *d_logits, cudaStream_t st,
                              const RouterGates *gates = nullptr);
