@@ -4,6 +4,9 @@ Workload (BASELINE.json metric "MoE-layer tokens/s at 1/2/4/8 B200; MX matvec HB
 config 2, the DeepSeek-V4-like MXFP4 MoE layer: hidden 7168, 256 routed experts + 1 shared,
 intermediate 2048, bf16 router with sigmoid + bias noaux_tc top-8 (x2.5), a 128-token prefill
 chunk per GPU (x ~ N(0,1) bf16).  Random-init, seeded synthetic weights (no checkpoints).
+On N GPUs (torchrun) the layer runs expert parallel: rank r holds 256/N routed experts plus
+the replicated router and shared expert, and routes its own 128 tokens (weak scaling: 128*N
+tokens per step); token rows and expert outputs cross NVLink inside the kernels.
 
   value     tokens/s, inputs already in HBM (urb_moe_forward_device), device-timed
   e2e       tokens/s through the host-pointer C ABI (urb_moe_forward), H2D of x and D2H of the
@@ -114,14 +117,21 @@ class ClockSampler:
                 "reasons": sorted(seen), "samples": len(mhz)}
 
 
-def make_weights(seed: int, experts: int, keep_host: bool):
-    """Seeded C2 weights: per expert (gate, up, down) MXFP4 + shared + bf16 router + bias."""
+def make_weights(seed: int, experts: int, held=None):
+    """Seeded C2 weights: per expert (gate, up, down) MXFP4, then the shared expert (last), bf16
+    router and bias.  Every expert has its own stream (seed + 1000 + e; shared: seed + 999), so
+    a rank of an expert-parallel group draws only the experts it holds (``held``: range of
+    expert ids, default all) and they equal the single-GPU weights."""
     from urbilateria_b200 import synthetic as syn
+
+    def expert(s):
+        g = syn.rng(s)
+        return [syn.mxfp4_matrix(g, INTER, HIDDEN), syn.mxfp4_matrix(g, INTER, HIDDEN),
+                syn.mxfp4_matrix(g, HIDDEN, INTER)]
+
+    held = range(experts) if held is None else held
+    mats = [expert(seed + 1000 + e) for e in held] + [expert(seed + 999)]
     g = syn.rng(seed)
-    mats = []
-    for _ in range(experts + 1):
-        mats.append([syn.mxfp4_matrix(g, INTER, HIDDEN), syn.mxfp4_matrix(g, INTER, HIDDEN),
-                     syn.mxfp4_matrix(g, HIDDEN, INTER)])
     router = syn.bf16_normal(g, (experts, HIDDEN), 0.02)
     bias = syn.normal_f32(g, experts, 0.01)
     return mats, router, bias
@@ -162,7 +172,7 @@ def run_reference(args, rank, world):
     if rank != 0:
         return
     threads = os.cpu_count() or 1
-    mats, router, bias = make_weights(SEED, EXPERTS, True)
+    mats, router, bias = make_weights(SEED, EXPERTS)
     _, layer, _ = oracle_layer(mats, router, bias)
     x = make_input(SEED, 0)
     for _ in range(max(0, min(args.warmup, 1))):
@@ -281,16 +291,26 @@ def main():
     stream = torch.cuda.Stream(device=local)
     ctx.set_stream(stream.cuda_stream)
 
-    keep_host = (rank == 0 and not args.no_cpu)
-    mats, router, bias = make_weights(SEED, EXPERTS, keep_host)
+    keep_host = (rank == 0 and world == 1 and not args.no_cpu)
+    # One GPU: the whole layer.  N GPUs: expert parallel, rank r holding experts
+    # shard_range(256, N, r) (plus the replicated router and shared expert) and its own
+    # 128-token chunk; token rows and expert outputs cross NVLink inside the kernels.
+    from urbilateria_b200.expert_parallel import ExpertParallelMoeLayer, shard_range
+    eb, ec = shard_range(EXPERTS, world, rank) if world > 1 else (0, EXPERTS)
+    mats, router, bias = make_weights(SEED, EXPERTS, range(eb, eb + ec))
     dev = []
     for m in mats:
         gm = [urb.MxFp4Matrix.from_packed(r, c, 32, p, s, ctx=ctx)
               for (p, s), (r, c) in zip(m, [(INTER, HIDDEN), (INTER, HIDDEN), (HIDDEN, INTER)])]
         dev.append(urb.GatedMlp(*gm))
     rd = urb.Bf16Matrix.from_bits(EXPERTS, HIDDEN, router, ctx=ctx)
-    layer = urb.RuntimeMoeLayer(rd, bias, dev[:EXPERTS], dev[EXPERTS],
-                                urb.MoeGeometry(TOP_K, 1, 1, True, SCALE))
+    geo = urb.MoeGeometry(TOP_K, 1, 1, True, SCALE)
+    if world == 1:
+        layer = urb.RuntimeMoeLayer(rd, bias, dev[:ec], dev[ec], geo)
+        ep = None
+    else:
+        layer = urb.RuntimeMoeLayer(rd, bias, dev[:ec], dev[ec], geo, expert_range=(eb, ec))
+        ep = ExpertParallelMoeLayer(layer, world, rank, TOKENS, timeout_ms=20000)
     if not keep_host:
         del mats
 
@@ -299,12 +319,25 @@ def main():
     d_out = torch.empty_like(d_x)
     d_status = torch.zeros(1, dtype=torch.int32, device=f"cuda:{local}")
     # Routing of this input (identical every step): touched experts for the roofline bytes.
-    out0, ids0, w0, extra = layer.forward_batch(x, TOKENS, details=True)
-    touched = int((extra["counts"] > 0).sum())
+    if ep is None:
+        out0, ids0, w0, extra = layer.forward_batch(x, TOKENS, details=True)
+        touched = int((extra["counts"] > 0).sum())
+    else:
+        dist.barrier()
+        out0, ids0, w0 = ep.forward_batch(x, TOKENS)
+        every = [None] * world
+        dist.all_gather_object(every, ids0)
+        ids_all = np.concatenate(every).ravel()
+        touched = int(np.unique(ids_all[(ids_all >= eb) & (ids_all < eb + ec)]).size)
     pk_hbm, pk_tf, pk_kind = peaks()
 
-    def step():
-        layer.forward_device(d_x.data_ptr(), TOKENS, d_out.data_ptr(), 0, 0, d_status.data_ptr())
+    if ep is None:
+        def step():
+            layer.forward_device(d_x.data_ptr(), TOKENS, d_out.data_ptr(), 0, 0,
+                                 d_status.data_ptr())
+    else:
+        def step():
+            ep.forward_device(d_x.data_ptr(), TOKENS, d_out.data_ptr(), d_status.data_ptr())
 
     with torch.cuda.stream(stream):
         for _ in range(args.warmup):
@@ -343,7 +376,7 @@ def main():
         torch.cuda.synchronize()
         ms = min(ms, e0.elapsed_time(e1))
 
-    matvec = None if args.no_matvec else bench_matvec(urb, ctx, stream, local, pk_hbm)
+    matvec = None if (args.no_matvec or world > 1) else bench_matvec(urb, ctx, stream, local, pk_hbm)
 
     # End to end through the host-pointer ABI (pinned host input/output).
     hx = torch.from_numpy(x).pin_memory()
@@ -352,9 +385,13 @@ def main():
     hw = torch.empty((TOKENS, TOP_K), dtype=torch.float32).pin_memory()
 
     def e2e_step():
-        ctx.check(ctx.lib.urb_moe_forward(ctx.h, layer.h, hx.data_ptr(), TOKENS, hout.data_ptr(),
-                                          hid.data_ptr(), hw.data_ptr(), None, None, None, None,
-                                          None))
+        if ep is None:
+            ctx.check(ctx.lib.urb_moe_forward(ctx.h, layer.h, hx.data_ptr(), TOKENS,
+                                              hout.data_ptr(), hid.data_ptr(), hw.data_ptr(),
+                                              None, None, None, None, None))
+        else:
+            ctx.check(ctx.lib.urb_ep_forward(ctx.h, ep.h, hx.data_ptr(), TOKENS, hout.data_ptr(),
+                                             hid.data_ptr(), hw.data_ptr()))
 
     ms_e2e = float("nan")
     if not args.no_e2e:
@@ -380,10 +417,13 @@ def main():
     e2e = tokens_total / (ms_e2e / 1e3)
 
     # Roofline of the dominant kernel: the grouped gate/up pass streams gate+up of every
-    # touched expert and of the shared expert once, 2 * (7,340,032 packed + 458,752 scale)
-    # bytes per expert, and writes the f32 gate|up rows of every activation column.
+    # touched expert (held by this rank) and of the shared expert once, 2 * (7,340,032 packed +
+    # 458,752 scale) bytes per expert, and writes the f32 gate|up rows of every activation
+    # column (routes to the held experts + own tokens).
     gu_bytes_per_expert = 2 * (INTER * HIDDEN // 2 + INTER * HIDDEN // 32)
-    gu_bytes = (touched + 1) * gu_bytes_per_expert + (TOKENS * TOP_K + TOKENS) * 2 * INTER * 4
+    n_cols = (TOKENS * TOP_K + TOKENS) if ep is None else \
+        int(((ids_all >= eb) & (ids_all < eb + ec)).sum()) + TOKENS
+    gu_bytes = (touched + 1) * gu_bytes_per_expert + n_cols * 2 * INTER * 4
     gu = kern.get("gate_up", {})
     achieved = gu_bytes / (gu.get("ms_per_launch", float("nan")) / 1e3) / 1e9
     roofline = {"kernel": "k_bs_grouped<MXFP4> gate/up (tcgen05.mma kind::mxf4 block_scale)",
@@ -394,6 +434,9 @@ def main():
     dn = kern.get("down", {})
     layer_bytes = (touched + 1) * 3 * (INTER * HIDDEN // 2 + INTER * HIDDEN // 32) + \
         EXPERTS * HIDDEN * 2
+    if ep is not None:
+        roofline["note"] = "rank 0 of %d: %d held experts touched, %d activation columns" % (
+            world, touched, n_cols)
 
     line = {"metric": "moe_layer_tokens_per_s", "value": value, "unit": "tokens/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
@@ -408,7 +451,8 @@ def main():
             "roofline": roofline,
             "layer_hbm_gbs": layer_bytes / (ms / args.steps / 1e3) / 1e9,
             "down_gbs": dn_bytes / (dn.get("ms_per_launch", float("nan")) / 1e3) / 1e9,
-            "touched_experts": touched, "kernels": kern, "matvec_c0": matvec,
+            "touched_experts": touched, "held_experts": [eb, ec], "kernels": kern,
+            "matvec_c0": matvec,
             "gpu_launches": sum(v["launches"] for v in kern.values()),
             "clocks": clk.summary()}
 

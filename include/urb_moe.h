@@ -58,6 +58,7 @@ typedef enum urb_status {
     URB_ERR_NCCL = 7,              /* NCCL failure in the expert-parallel path */
     URB_ERR_UNSUPPORTED = 8,       /* configuration outside what this build implements */
     URB_ERR_INVALID_ARGUMENT = 9,  /* null handle / pointer */
+    URB_ERR_PEER = 10,             /* another rank of the expert-parallel group failed the forward */
 } urb_status;
 
 typedef enum urb_format {
@@ -195,6 +196,54 @@ URB_API int urb_moe_forward_device(urb_ctx *ctx, urb_layer *layer, const float *
                            float *d_out, int32_t *d_route_expert, float *d_route_weight,
                            int32_t *d_status);
 
+/* ---- expert parallelism across the GPUs of one node ------------------------------------------ */
+
+/* The layer forward of src/models/glm/runtime/moe.rs:138-176 split by experts over `world`
+ * processes, one per GPU (the reference runs every expert in one process; its Rayon workers
+ * split rows, src/execution.rs:154).  Rank g holds routed experts [expert_begin,
+ * expert_begin + expert_count) plus the replicated router and shared expert, and owns the
+ * tokens it passes to urb_ep_forward*.  Token rows and expert outputs move between the GPUs
+ * through peer memory (NVLink / NVSwitch) inside the kernels; outputs are bit-identical to
+ * urb_moe_forward on one GPU. */
+#define URB_EP_MAX_WORLD 8
+#define URB_EP_HANDLE_BYTES 256
+typedef struct urb_ep urb_ep;
+
+/* A shard of RuntimeMoeLayer::new (src/models/glm/runtime/moe.rs:88-129): router [experts,
+ * hidden] and bias [experts] for all experts; gate/up/down arrays hold the `expert_count`
+ * experts starting at `expert_begin`.  Runs only through urb_ep_forward*; urb_moe_forward*
+ * return URB_ERR_UNSUPPORTED for it.  Needs MX (MXFP4 / MXFP8 1x32) experts. */
+URB_API int urb_moe_layer_create_sharded(urb_ctx *ctx, const urb_mat *router, const float *bias,
+                                         size_t experts, size_t expert_begin, size_t expert_count,
+                                         const urb_mat *const *gate, const urb_mat *const *up,
+                                         const urb_mat *const *down, const urb_mat *shared_gate,
+                                         const urb_mat *shared_up, const urb_mat *shared_down,
+                                         const urb_moe_geometry *geometry, urb_layer **out);
+/* This rank's member of an expert-parallel group over `layer` (a shard, or the whole layer
+ * when world == 1).  max_tokens bounds the tokens any rank passes per forward; timeout_ms (0:
+ * 5000) bounds every wait of a group barrier on the device. */
+URB_API int urb_ep_create(urb_ctx *ctx, urb_layer *layer, int world, int rank, size_t max_tokens,
+                          uint32_t timeout_ms, urb_ep **out);
+/* Writes URB_EP_HANDLE_BYTES describing this rank's exchange window (a CUDA IPC handle plus
+ * the group geometry) for the caller to all-gather over its host-side process group. */
+URB_API int urb_ep_export(urb_ep *ep, uint8_t *handle);
+/* Maps the other ranks' windows.  handles: world * URB_EP_HANDLE_BYTES in rank order.  Checks
+ * that every rank describes the same group, that the expert ranges tile [0, experts) and that
+ * no two ranks share a GPU (URB_ERR_UNSUPPORTED: the group's barriers need distinct GPUs). */
+URB_API int urb_ep_connect(urb_ep *ep, const uint8_t *handles);
+/* One forward of this rank's `tokens` (<= max_tokens, 0 allowed) tokens; collective: every
+ * rank of the group calls it for every forward, in the same order.  Host pointers; outputs
+ * as urb_moe_forward (out [tokens, hidden], optional route expert / weight [tokens, top_k]).
+ * A rank that fails a forward fails it on every rank (URB_ERR_PEER on the others); a rank
+ * that does not call it leaves the others with URB_ERR_TIMEOUT. */
+URB_API int urb_ep_forward(urb_ctx *ctx, urb_ep *ep, const float *x, size_t tokens, float *out,
+                           int32_t *route_expert, float *route_weight);
+/* Device-pointer form (stream-ordered, no host synchronisation).  d_status is required. */
+URB_API int urb_ep_forward_device(urb_ctx *ctx, urb_ep *ep, const float *d_x, size_t tokens,
+                                  float *d_out, int32_t *d_route_expert, float *d_route_weight,
+                                  int32_t *d_status);
+URB_API int urb_ep_free(urb_ep *ep);
+
 /* ---- measurement -------------------------------------------------------------------------- */
 
 /* Kernel families timed by the optional per-launch profiler (CUDA events on the launch
@@ -211,7 +260,8 @@ typedef enum urb_kernel_kind {
     URB_K_PRODUCT = 7,
     URB_K_PREP = 8,         /* activation residual terms of a tensor-core pass */
     URB_K_GROUP_BUILD = 9,  /* device-side group / unit tables of the tensor-core passes */
-    URB_K_COUNT = 10
+    URB_K_EXCHANGE = 10,    /* expert-parallel publish, route gather and group barriers */
+    URB_K_COUNT = 11
 } urb_kernel_kind;
 URB_API int urb_profile_enable(urb_ctx *ctx, int on);
 /* Synchronises pending events; returns the total device time and launch count of `kind`. */

@@ -11,7 +11,7 @@ from __future__ import annotations
 
 import ctypes
 from dataclasses import dataclass
-from typing import List, Optional, Sequence
+from typing import List, Optional, Sequence, Tuple
 
 import numpy as np
 
@@ -338,10 +338,16 @@ def group_routes(expert_ids, experts: int, ctx: Optional[Context] = None):
 
 
 class RuntimeMoeLayer:
-    """RuntimeMoeLayer (src/models/glm/runtime/moe.rs:73-176), all experts resident in HBM."""
+    """RuntimeMoeLayer (src/models/glm/runtime/moe.rs:73-176), all experts resident in HBM.
+
+    With ``expert_range=(begin, count)`` the layer is one expert-parallel shard: ``experts``
+    holds the ``count`` experts starting at ``begin`` (router and bias still cover all
+    experts), and it runs through :class:`urbilateria_b200.expert_parallel.ExpertParallelMoeLayer`.
+    """
 
     def __init__(self, router: _Matrix, correction_bias, experts: Sequence[GatedMlp],
-                 shared: Optional[GatedMlp], geometry: MoeGeometry):
+                 shared: Optional[GatedMlp], geometry: MoeGeometry,
+                 expert_range: Optional[Tuple[int, int]] = None):
         self.ctx = router.ctx
         self.router = router
         self.bias = np.ascontiguousarray(correction_bias, dtype=np.float32).ravel()
@@ -358,9 +364,18 @@ class RuntimeMoeLayer:
         sg = shared.gate.h if shared else None
         su = shared.up.h if shared else None
         sd = shared.down.h if shared else None
-        self.ctx.check(self.ctx.lib.urb_moe_layer_create(
-            self.ctx.h, router.h, _ptr(self.bias), n, self._g, self._u, self._d, sg, su, sd,
-            ctypes.byref(self._geo), ctypes.byref(h)))
+        self.expert_range = (0, n) if expert_range is None else tuple(expert_range)
+        if expert_range is None:
+            self.ctx.check(self.ctx.lib.urb_moe_layer_create(
+                self.ctx.h, router.h, _ptr(self.bias), n, self._g, self._u, self._d, sg, su, sd,
+                ctypes.byref(self._geo), ctypes.byref(h)))
+        else:
+            begin, count = self.expert_range
+            if count != n:
+                raise UrbError(native.ERR_SHAPE, "expert_range count %d != %d experts given" % (count, n))
+            self.ctx.check(self.ctx.lib.urb_moe_layer_create_sharded(
+                self.ctx.h, router.h, _ptr(self.bias), self.bias.size, begin, count, self._g,
+                self._u, self._d, sg, su, sd, ctypes.byref(self._geo), ctypes.byref(h)))
         self.h = h
 
     def hidden_size(self) -> int:

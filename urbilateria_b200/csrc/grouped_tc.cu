@@ -343,7 +343,15 @@ __global__ void __launch_bounds__(kThreadsBs, 1) k_bs_grouped(TcArgs a) {
                                 q += __uint_as_float(v[2][RT * s + e]) + __uint_as_float(v[3][RT * s + e]);
                             o += q;
                         }
-                        a.out[size_t(S.col_begin + tok0 + t) * a.out_stride + S.out_off + grow] = o;
+                        const int col = S.col_begin + tok0 + t;
+                        float *dst;
+                        if (a.out_ranks && col < a.routed_cols) {
+                            const int i = a.out_rows[col];
+                            dst = a.out_ranks[i / a.out_rank_rows] + size_t(i % a.out_rank_rows) * a.out_stride;
+                        } else {
+                            dst = a.out + size_t(a.out_ranks ? col - a.routed_cols : col) * a.out_stride;
+                        }
+                        dst[S.out_off + grow] = o;
                     }
                 }
             }
@@ -351,6 +359,9 @@ __global__ void __launch_bounds__(kThreadsBs, 1) k_bs_grouped(TcArgs a) {
             __syncwarp();
             if (lane == 0) tc::mbar_arrive(&acc_empty);
         }
+        // Rows stored into other ranks' memory are visible system-wide before the exchange
+        // barrier that follows this launch signals them.
+        if (a.out_ranks) __threadfence_system();
     }
     tc::fence_before_sync();
     __syncthreads();
@@ -461,13 +472,27 @@ __global__ void __launch_bounds__(256) k_bs_prep(TcArgs a) {
     const long long item = tid >> 2;
     const int part = int(tid & 3);
     const int nkb = a.ks * KBS;
-    const bool valid = item < (long long)a.nrows * nkb;
+    bool valid = item < (long long)a.nrows * nkb;
     const int row = valid ? int(item / nkb) : 0, kb = valid ? int(item % nkb) : 0;
+    const bool shared_dst = a.inv && a.shared_col0 >= 0 && row >= a.shared_row0 &&
+                            row < a.shared_row0 + a.shared_rows;
+    if (valid) {
+        // Rows that feed no column of this rank (expert-parallel shards) are not loaded.
+        if (a.inv) {
+            bool any = shared_dst;
+            for (int d = 0; d < a.top_k && !any; ++d) any = a.inv[row * a.top_k + d] >= 0;
+            valid = any;
+        } else if (a.nvalid) {
+            valid = row < *a.nvalid || row >= a.routed_cols;
+        }
+    }
     float r[8];
     const int c0 = kb * 32 + part * 8;
     bool bad = false;
     if (valid) {
-        const float *p = a.src + size_t(row) * a.src_stride;
+        const float *p = a.src_ranks ? a.src_ranks[row / a.rows_per_rank] +
+                                           size_t(row % a.rows_per_rank) * a.src_stride
+                                     : a.src + size_t(row) * a.src_stride;
         if (!a.swiglu && (a.src_stride & 3) == 0 && c0 + 8 <= a.cols) {
             const float4 v0 = *reinterpret_cast<const float4 *>(p + c0);
             const float4 v1 = *reinterpret_cast<const float4 *>(p + c0 + 4);
@@ -496,9 +521,12 @@ __global__ void __launch_bounds__(256) k_bs_prep(TcArgs a) {
     for (int t = 0; t < TT; ++t) sb[t] = make_term8<FMT>(r, q[t]);
     if (!valid) return;
     const int ks = kb / KBS, kbs = kb % KBS;
-    const int ndst = a.inv ? a.top_k + (a.shared_col0 >= 0 ? 1 : 0) : 1;
+    const int ndst = a.inv ? a.top_k + (shared_dst ? 1 : 0) : 1;
     for (int d = 0; d < ndst; ++d) {
-        const int col = a.inv ? (d < a.top_k ? a.inv[row * a.top_k + d] : a.shared_col0 + row) : row;
+        const int col = a.inv ? (d < a.top_k ? a.inv[row * a.top_k + d]
+                                             : a.shared_col0 + (row - a.shared_row0))
+                              : row;
+        if (col < 0) continue;
         const BsSlot S = a.slots[col];
         uint8_t *stage = a.bbuf + S.base + (long long)ks * bs_bstage_bytes(FMT, S.n);
 #pragma unroll

@@ -33,6 +33,8 @@ size_t max_segments(size_t tokens, size_t K, size_t experts) {
     return std::min(TK, experts) + TK / kCap + div_ceil(tokens, kCap) + 2;
 }
 
+}  // namespace
+
 // Upper bound of the work units of one tensor-core pass (mts 128-row tiles per sub-segment).
 size_t max_bs_units(int fmt, size_t tokens, size_t K, size_t experts, size_t mts) {
     const size_t TK = tokens * K, cap = size_t(bs_cap(fmt));
@@ -48,7 +50,22 @@ size_t max_bs_bytes(int fmt, size_t tokens, size_t K, size_t experts, size_t ks)
     return subs * ks * size_t(bs_bstage_bytes(fmt, kBsNmax));
 }
 
-}  // namespace
+int route_device(Layer *L, const float *d_x, int T, const MoeWork &w, int32_t *d_status,
+                 cudaStream_t st) {
+    Ctx *ctx = L->ctx;
+    const int E = int(L->experts), H = int(L->hidden);
+    prof_begin(ctx, URB_K_ROUTER_LOGITS, st);
+    // Exact logits, with the sigmoid gates and biased selection scores in the same kernel.
+    const RouterGates rg{ctx, L->d_bias, w.gate, w.sel, d_status};
+    int rc = launch_router_logits_f64(L->router64, E, d_x, T, H, w.x64, w.logits, st, &rg);
+    prof_end(ctx, st);
+    if (rc) return cuda_fail(ctx, cudaGetLastError(), "router logits");
+    prof_begin(ctx, URB_K_ROUTE, st);
+    rc = launch_route_noaux(ctx, w.logits, L->d_bias, T, E, L->geo, w.ids, w.w, w.score,
+                            d_status, st, &rg);
+    prof_end(ctx, st);
+    return rc;
+}
 
 int moe_forward_device(Layer *L, const float *d_x, int T, float *d_out, MoeWork *wout,
                        int32_t *d_status, cudaStream_t st) {
@@ -117,20 +134,12 @@ int moe_forward_device(Layer *L, const float *d_x, int T, float *d_out, MoeWork 
         prof_end(ctx, st);
         if (rc) return cuda_fail(ctx, cudaGetLastError(), "row shift");
     }
-    prof_begin(ctx, URB_K_ROUTER_LOGITS, st);
-    // Exact logits, with the sigmoid gates and biased selection scores in the same kernel.
-    const RouterGates rg{ctx, L->d_bias, w.gate, w.sel, d_status};
-    rc = launch_router_logits_f64(L->router64, int(E), d_x, T, int(H), w.x64, w.logits, st, &rg);
-    prof_end(ctx, st);
-    if (rc) return cuda_fail(ctx, cudaGetLastError(), "router logits");
-    prof_begin(ctx, URB_K_ROUTE, st);
-    rc = launch_route_noaux(ctx, w.logits, L->d_bias, T, int(E), L->geo, w.ids, w.w, w.score,
-                            d_status, st, &rg);
-    prof_end(ctx, st);
+    rc = route_device(L, d_x, T, w, d_status, st);
     if (rc) return rc;
 
     const Mat *g0 = L->gate[0], *d0 = L->down[0];
     void **tb = L->d_tables;
+    const size_t S = L->e_count + 1;  // table stride
     PermArgs p{};
     p.ids = w.ids;
     p.tokens = T;
@@ -151,11 +160,11 @@ int moe_forward_device(Layer *L, const float *d_x, int T, float *d_out, MoeWork 
     p.col_src = w.col_src;
     p.maxexp = w.maxexp;
     p.gate_tiles = reinterpret_cast<const uint8_t *const *>(tb);
-    p.up_tiles = reinterpret_cast<const uint8_t *const *>(tb + E);
-    p.down_tiles = reinterpret_cast<const uint8_t *const *>(tb + 2 * E);
-    p.gate_rexp = reinterpret_cast<const int8_t *const *>(tb + 3 * E);
-    p.up_rexp = reinterpret_cast<const int8_t *const *>(tb + 4 * E);
-    p.down_rexp = reinterpret_cast<const int8_t *const *>(tb + 5 * E);
+    p.up_tiles = reinterpret_cast<const uint8_t *const *>(tb + S);
+    p.down_tiles = reinterpret_cast<const uint8_t *const *>(tb + 2 * S);
+    p.gate_rexp = reinterpret_cast<const int8_t *const *>(tb + 3 * S);
+    p.up_rexp = reinterpret_cast<const int8_t *const *>(tb + 4 * S);
+    p.down_rexp = reinterpret_cast<const int8_t *const *>(tb + 5 * S);
     p.shared_in_pass = L->sg ? 1 : 0;
     if (L->sg) {
         p.sh_gate_tiles = L->sg->tiles; p.sh_gate_rexp = L->sg->row_exp;
@@ -170,6 +179,10 @@ int moe_forward_device(Layer *L, const float *d_x, int T, float *d_out, MoeWork 
     p.dn_kslices = d0->kslices;
     p.status = d_status;
     p.lofree = w.lofree;
+    if (L->use_tc) {  // the tensor-core passes need only the grouping itself
+        p.segs_gu = nullptr;
+        p.col_src = nullptr;
+    }
     prof_begin(ctx, URB_K_PERMUTE, st);
     rc = launch_permute(ctx, p, st);
     prof_end(ctx, st);
@@ -183,10 +196,11 @@ int moe_forward_device(Layer *L, const float *d_x, int T, float *d_out, MoeWork 
         bb.tokens = T;
         bb.top_k = int(K);
         bb.experts = int(E);
-        bb.gate_tc = reinterpret_cast<const uint8_t *const *>(tb + 6 * E);
-        bb.up_tc = reinterpret_cast<const uint8_t *const *>(tb + 7 * E);
-        bb.down_tc = reinterpret_cast<const uint8_t *const *>(tb + 8 * E);
+        bb.gate_tc = reinterpret_cast<const uint8_t *const *>(tb + 6 * S);
+        bb.up_tc = reinterpret_cast<const uint8_t *const *>(tb + 7 * S);
+        bb.down_tc = reinterpret_cast<const uint8_t *const *>(tb + 8 * S);
         bb.has_shared = L->sg ? 1 : 0;
+        bb.shared_tokens = T;
         if (L->sg) {
             bb.sh_gate_tc = L->sg->tc_tiles;
             bb.sh_up_tc = L->su->tc_tiles;
@@ -223,6 +237,8 @@ int moe_forward_device(Layer *L, const float *d_x, int T, float *d_out, MoeWork 
         ga.inv = w.inv;
         ga.top_k = int(K);
         ga.shared_col0 = L->sg ? int(TK) : -1;
+        ga.shared_row0 = 0;
+        ga.shared_rows = T;
         ga.slots = w.bslots_gu;
         ga.out = w.gu;
         ga.out_stride = int(2 * I);
@@ -372,11 +388,12 @@ using namespace urb;
 
 extern "C" {
 
-int urb_moe_layer_create(urb_ctx *ctx, const urb_mat *router, const float *bias, size_t experts,
-                         const urb_mat *const *gate, const urb_mat *const *up,
-                         const urb_mat *const *down, const urb_mat *sg, const urb_mat *su,
-                         const urb_mat *sd, const urb_moe_geometry *geo, urb_layer **out) {
-    if (!ctx || !router || !bias || !gate || !up || !down || !geo || !out)
+static int create_layer(urb_ctx *ctx, const urb_mat *router, const float *bias, size_t experts,
+                        size_t e_begin, size_t e_count, const urb_mat *const *gate,
+                        const urb_mat *const *up, const urb_mat *const *down, const urb_mat *sg,
+                        const urb_mat *su, const urb_mat *sd, const urb_moe_geometry *geo,
+                        urb_layer **out) {
+    if (!ctx || !router || !bias || !gate || !up || !down || !geo || !out || e_count == 0)
         return URB_ERR_INVALID_ARGUMENT;
     std::lock_guard<std::recursive_mutex> lk(ctx->mu);
     cudaSetDevice(ctx->device);
@@ -418,7 +435,9 @@ int urb_moe_layer_create(urb_ctx *ctx, const urb_mat *router, const float *bias,
         if (g->format != fmt || u->format != fmt || d->format != fmt) return URB_ERR_UNSUPPORTED;
         return URB_OK;
     };
-    for (size_t e = 0; e < experts; ++e) {
+    if (e_begin + e_count > experts || e_begin + e_count < e_begin)
+        return set_error(ctx, URB_ERR_SHAPE, "expert shard range exceeds the router's experts");
+    for (size_t e = 0; e < e_count; ++e) {
         int rc = check_mlp(gate[e], up[e], down[e]);
         if (rc) return set_error(ctx, rc, "routed expert shape/format is not supported");
     }
@@ -430,33 +449,42 @@ int urb_moe_layer_create(urb_ctx *ctx, const urb_mat *router, const float *bias,
     L->ctx = ctx;
     L->router = router;
     L->experts = experts;
+    L->e_begin = e_begin;
+    L->e_count = e_count;
     L->hidden = H;
     L->inter = I;
     L->fmt = fmt;
     L->geo = *geo;
-    L->gate.assign(gate, gate + experts);
-    L->up.assign(up, up + experts);
-    L->down.assign(down, down + experts);
+    L->gate.assign(gate, gate + e_count);
+    L->up.assign(up, up + e_count);
+    L->down.assign(down, down + e_count);
     if (have_shared) { L->sg = sg; L->su = su; L->sd = sd; }
-    std::vector<void *> tables(9 * experts);
-    for (size_t e = 0; e < experts; ++e) {
-        tables[e] = gate[e]->tiles;
-        tables[experts + e] = up[e]->tiles;
-        tables[2 * experts + e] = down[e]->tiles;
-        tables[3 * experts + e] = gate[e]->row_exp;
-        tables[4 * experts + e] = up[e]->row_exp;
-        tables[5 * experts + e] = down[e]->row_exp;
-        tables[6 * experts + e] = gate[e]->tc_tiles;
-        tables[7 * experts + e] = up[e]->tc_tiles;
-        tables[8 * experts + e] = down[e]->tc_tiles;
-    }
+    const size_t S = e_count + 1;  // held experts, then the shared expert
+    std::vector<void *> tables(9 * S, nullptr);
+    auto put = [&](size_t e, const Mat *g, const Mat *u, const Mat *d) {
+        tables[e] = g->tiles;
+        tables[S + e] = u->tiles;
+        tables[2 * S + e] = d->tiles;
+        tables[3 * S + e] = g->row_exp;
+        tables[4 * S + e] = u->row_exp;
+        tables[5 * S + e] = d->row_exp;
+        tables[6 * S + e] = g->tc_tiles;
+        tables[7 * S + e] = u->tc_tiles;
+        tables[8 * S + e] = d->tc_tiles;
+    };
+    for (size_t e = 0; e < e_count; ++e) put(e, gate[e], up[e], down[e]);
+    if (have_shared) put(e_count, sg, su, sd);
     const char *path = std::getenv("URB_MOE_PATH");
     bool have_tc = fmt == URB_FMT_MXFP4 || fmt == URB_FMT_MXFP8;
-    for (size_t e = 0; e < experts && have_tc; ++e)
+    for (size_t e = 0; e < e_count && have_tc; ++e)
         have_tc = gate[e]->tc_tiles && up[e]->tc_tiles && down[e]->tc_tiles;
     if (L->sg) have_tc = have_tc && L->sg->tc_tiles && L->su->tc_tiles && L->sd->tc_tiles;
     // Block-scaled tcgen05 passes by default; URB_MOE_PATH=mma selects the mma.sync passes.
     L->use_tc = have_tc && !(path && std::strcmp(path, "mma") == 0);
+    if (e_count != experts && !have_tc) {
+        delete L;
+        return set_error(ctx, URB_ERR_UNSUPPORTED, "expert shards need MX experts (tensor-core passes)");
+    }
     cudaError_t err = cudaMalloc(&L->d_tables, tables.size() * sizeof(void *));
     if (err == cudaSuccess) err = cudaMalloc(&L->router64, experts * H * sizeof(double));
     if (err == cudaSuccess && widen_router_f64(router, L->router64, ctx->stream) != URB_OK)
@@ -472,6 +500,22 @@ int urb_moe_layer_create(urb_ctx *ctx, const urb_mat *router, const float *bias,
     }
     *out = L;
     return URB_OK;
+}
+
+int urb_moe_layer_create(urb_ctx *ctx, const urb_mat *router, const float *bias, size_t experts,
+                         const urb_mat *const *gate, const urb_mat *const *up,
+                         const urb_mat *const *down, const urb_mat *sg, const urb_mat *su,
+                         const urb_mat *sd, const urb_moe_geometry *geo, urb_layer **out) {
+    return create_layer(ctx, router, bias, experts, 0, experts, gate, up, down, sg, su, sd, geo, out);
+}
+
+int urb_moe_layer_create_sharded(urb_ctx *ctx, const urb_mat *router, const float *bias,
+                                 size_t experts, size_t expert_begin, size_t expert_count,
+                                 const urb_mat *const *gate, const urb_mat *const *up,
+                                 const urb_mat *const *down, const urb_mat *sg, const urb_mat *su,
+                                 const urb_mat *sd, const urb_moe_geometry *geo, urb_layer **out) {
+    return create_layer(ctx, router, bias, experts, expert_begin, expert_count, gate, up, down,
+                        sg, su, sd, geo, out);
 }
 
 int urb_moe_layer_free(urb_layer *L) {
@@ -491,6 +535,8 @@ int urb_moe_forward_device(urb_ctx *ctx, urb_layer *L, const float *d_x, size_t 
                            float *d_out, int32_t *d_route_expert, float *d_route_weight,
                            int32_t *d_status) {
     if (!ctx || !L || !d_x || !d_out) return URB_ERR_INVALID_ARGUMENT;
+    if (L->e_count != L->experts)
+        return set_error(ctx, URB_ERR_UNSUPPORTED, "an expert shard runs through urb_ep_forward");
     std::lock_guard<std::recursive_mutex> lk(ctx->mu);
     cudaSetDevice(ctx->device);
     if (tokens == 0) return URB_OK;
@@ -510,6 +556,8 @@ int urb_moe_forward(urb_ctx *ctx, urb_layer *L, const float *x, size_t tokens, f
                     float *router_logits, int32_t *counts, int32_t *perm_token,
                     int32_t *perm_slot) {
     if (!ctx || !L || !x || !out) return URB_ERR_INVALID_ARGUMENT;
+    if (L->e_count != L->experts)
+        return set_error(ctx, URB_ERR_UNSUPPORTED, "an expert shard runs through urb_ep_forward");
     std::lock_guard<std::recursive_mutex> lk(ctx->mu);
     cudaSetDevice(ctx->device);
     if (tokens == 0) return URB_OK;

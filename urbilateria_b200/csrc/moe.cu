@@ -32,6 +32,7 @@ __global__ void __launch_bounds__(kPermThreads) k_permute(PermArgs p) {
     __syncthreads();
     for (int i = tid; i < TK; i += kPermThreads) {
         int e = p.ids[i];
+        if (e == -1 && p.allow_foreign) continue;  // a route held by another rank
         if (e < 0 || e >= E) bad = 1; else atomicAdd(&cnt[e], 1);
     }
     __syncthreads();
@@ -70,7 +71,7 @@ __global__ void __launch_bounds__(kPermThreads) k_permute(PermArgs p) {
         __syncthreads();
         int base = incl - s + (warp ? warp_sums[warp - 1] : 0);
         for (int e = b; e < min(E, b + per); ++e) { off[e] = base; base += cnt[e]; }
-        if (tid == 0) off[E] = TK;
+        if (tid == 0) off[E] = warp_sums[31];  // routes held here (TK unless some are foreign)
         __syncthreads();
     }
     // Stable placement, token-major route order -> (expert asc, token asc).
@@ -88,6 +89,9 @@ __global__ void __launch_bounds__(kPermThreads) k_permute(PermArgs p) {
             p.perm_token[pos] = i / p.top_k;
             p.perm_slot[pos] = i % p.top_k;
             p.inv[i] = pos;
+            if (p.route_of) p.route_of[pos] = i;
+        } else if (i < TK) {
+            p.inv[i] = -1;  // foreign route
         }
         __syncthreads();
         for (int x = tid; x < E; x += kPermThreads) {
@@ -176,11 +180,11 @@ __global__ void __launch_bounds__(kPermThreads) k_permute(PermArgs p) {
         if (p.counts) p.counts[e] = cnt[e];
         if (p.offsets) p.offsets[e] = off[e];
     }
-    if (tid == 0 && p.offsets) p.offsets[E] = TK;
+    if (tid == 0 && p.offsets) p.offsets[E] = off[E];
 }
 
 // out[t][h] = f32( f64(shared) + sum_k f64(w[t][k]) * f64(y[inv[t,k]][h]) ), k in selection
-// order (glm/runtime/moe.rs:165-175).
+// order (glm/runtime/moe.rs:165-175).  inv == nullptr: y is already in route order t * top_k + k.
 __global__ void k_combine(const float *y, const float *shared_y, const float *w,
                           const int32_t *inv, int tokens, int top_k, int hidden, float *out,
                           const int32_t *status) {
@@ -190,7 +194,7 @@ __global__ void k_combine(const float *y, const float *shared_y, const float *w,
     if (t >= tokens || h >= hidden) return;
     double acc = shared_y ? double(shared_y[size_t(t) * hidden + h]) : 0.0;
     for (int k = 0; k < top_k; ++k) {
-        const int pos = inv[t * top_k + k];
+        const int pos = inv ? inv[t * top_k + k] : t * top_k + k;
         acc += double(w[t * top_k + k]) * double(y[size_t(pos) * hidden + h]);
     }
     out[size_t(t) * hidden + h] = float(acc);
@@ -318,12 +322,12 @@ __global__ void __launch_bounds__(1024) k_build_tc_segs(TcBuildArgs b) {
         if (tid == 1023) {
             // gi / ub / boff of the last thread are the routed totals; append the shared expert.
             sh_boff = boff;
-            if (b.has_shared && b.tokens > 0) {
+            if (b.has_shared && b.shared_tokens > 0) {
                 if (pass == 0) {
-                    emit(b.sh_gate_tc, 0, TK, b.tokens);
-                    emit(b.sh_up_tc, 1, TK, b.tokens);
+                    emit(b.sh_gate_tc, 0, TK, b.shared_tokens);
+                    emit(b.sh_up_tc, 1, TK, b.shared_tokens);
                 } else {
-                    emit(b.sh_down_tc, 0, TK, b.tokens);
+                    emit(b.sh_down_tc, 0, TK, b.shared_tokens);
                 }
             }
             s_groups = gi;
@@ -334,8 +338,8 @@ __global__ void __launch_bounds__(1024) k_build_tc_segs(TcBuildArgs b) {
         __syncthreads();
         // Shared expert's activation slots and the unit -> group map, by all threads.
         if (b.has_shared)
-            for (int j = tid; j < b.tokens; j += 1024)
-                sl[TK + j] = slot_of(b.fmt, sh_boff, ks, b.tokens, j);
+            for (int j = tid; j < b.shared_tokens; j += 1024)
+                sl[TK + j] = slot_of(b.fmt, sh_boff, ks, b.shared_tokens, j);
         int *um = pass == 0 ? b.gu_units : b.dn_units;
         const int G = s_groups, U = s_units;
         for (int u = tid; u < U; u += 1024) {

@@ -26,6 +26,8 @@ struct PermArgs {
     int hidden, inter, gu_rbs, gu_kslices, dn_rbs, dn_kslices;
     int32_t *status;
     const int *lofree;    // optional: when *lofree, segments hold 2*cap tokens
+    int allow_foreign;    // ids == -1 are routes held by another rank: not grouped, inv = -1
+    int32_t *route_of;    // optional [tokens*top_k]: route index of each grouped position
 };
 
 int launch_permute(Ctx *ctx, const PermArgs &p, cudaStream_t st);
@@ -37,7 +39,7 @@ struct TcBuildArgs {
     int tokens, top_k, experts;
     const uint8_t *const *gate_tc, *const *up_tc, *const *down_tc;
     const uint8_t *sh_gate_tc, *sh_up_tc, *sh_down_tc;
-    int has_shared;
+    int has_shared, shared_tokens;  // shared-expert columns [tokens*top_k, +shared_tokens)
     int hidden, inter;
     TcSeg *gu, *dn;
     BsSlot *gu_slots, *dn_slots;  // [TK + T] activation slots of each column, per pass
@@ -55,13 +57,16 @@ struct Layer {
     const Mat *router = nullptr;
     double *router64 = nullptr;  // router widened to f64 (the logits' FP64 MMA operand)
     float *d_bias = nullptr;
-    size_t experts = 0, hidden = 0, inter = 0;
+    size_t experts = 0, hidden = 0, inter = 0;  // experts: routed experts in total (router rows)
+    // Routed experts held by this layer: [e_begin, e_begin + e_count) (all of them unless the
+    // layer is one expert-parallel shard).
+    size_t e_begin = 0, e_count = 0;
     int fmt = 0;
     std::vector<const Mat *> gate, up, down;
     const Mat *sg = nullptr, *su = nullptr, *sd = nullptr;
     urb_moe_geometry geo{};
-    // Device pointer tables [experts] for gate/up/down tiles and row exponents, then the
-    // tensor-core tiles of gate/up/down.
+    // Device pointer tables, 9 kinds of (e_count + 1) entries (held experts, then the shared
+    // expert or null): gate/up/down mma tiles, their row exponents, gate/up/down bs tiles.
     void **d_tables = nullptr;
     bool use_tc = true;  // block-scaled tcgen05 passes (false: mma.sync register-dequant)
 };
@@ -92,6 +97,15 @@ struct MoeWork {
 
 int moe_forward_device(Layer *L, const float *d_x, int tokens, float *d_out, MoeWork *work_out,
                        int32_t *d_status, cudaStream_t st);
+// Exact router logits and route_noaux_tc of `tokens` rows into w.logits / x64 / gate / sel /
+// ids / w / score.
+int route_device(Layer *L, const float *d_x, int tokens, const MoeWork &w, int32_t *d_status,
+                 cudaStream_t st);
+// Bounds of the tensor-core passes' work tables (units of a pass over `mts` row tiles, bytes of
+// its activation stages over `ks` K stages) for tokens * top_k routes over `experts` experts
+// plus `tokens` shared-expert columns.
+size_t max_bs_units(int fmt, size_t tokens, size_t top_k, size_t experts, size_t mts);
+size_t max_bs_bytes(int fmt, size_t tokens, size_t top_k, size_t experts, size_t ks);
 
 }  // namespace urb
 

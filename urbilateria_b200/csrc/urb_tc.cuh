@@ -65,12 +65,26 @@ struct TcArgs {
     int nrows;                 // source rows
     int cols, ks;              // input columns and K stages of the pass
     int swiglu;
-    const int32_t *inv;
+    const int32_t *inv;        // gate/up: inv[r * top_k + k] < 0 marks a route held elsewhere
     int top_k, shared_col0;    // shared_col0 < 0: no shared expert
+    int shared_row0, shared_rows;  // source rows [shared_row0, +shared_rows) feed the shared
+                                   // expert's columns shared_col0 + (r - shared_row0)
     const BsSlot *slots;       // [activation columns]
     float *out;
     int out_stride;
     int32_t *status;
+    // Expert-parallel shard (all null / 0 on one GPU).  Gate/up: source row r is row
+    // r % rows_per_rank of rank r / rows_per_rank's activations src_ranks[...].  Down: columns
+    // [*nvalid, routed_cols) carry no route; routed column c holds route i = out_rows[c] of
+    // the owning rank's tokens, written to row i % out_rank_rows of out_ranks[i / out_rank_rows]
+    // (the owner's memory); the shared expert's column c goes to row c - routed_cols of `out`.
+    const float *const *src_ranks;
+    int rows_per_rank;
+    const int32_t *nvalid;
+    int routed_cols;
+    const int32_t *out_rows;
+    float *const *out_ranks;
+    int out_rank_rows;
 };
 
 // Prep (activation terms) + tensor-core pass over every group of the launch; the profiler

@@ -21,19 +21,24 @@ ERR_TIMEOUT = 6
 ERR_NCCL = 7
 ERR_UNSUPPORTED = 8
 ERR_INVALID_ARGUMENT = 9
+ERR_PEER = 10
 
 FMT_F32, FMT_BF16, FMT_MXFP8, FMT_MXFP4 = 0, 1, 2, 3
 
 # urb_kernel_kind
 (K_ROW_SHIFT, K_ROUTER_LOGITS, K_ROUTE, K_PERMUTE, K_GATE_UP, K_DOWN, K_COMBINE, K_PRODUCT,
- K_PREP, K_GROUP_BUILD) = range(10)
+ K_PREP, K_GROUP_BUILD, K_EXCHANGE) = range(11)
 KERNEL_NAMES = ["row_shift", "router_logits", "route", "permute", "gate_up", "down", "combine",
-                "product", "prep", "group_build"]
+                "product", "prep", "group_build", "exchange"]
+
+EP_MAX_WORLD = 8
+EP_HANDLE_BYTES = 256
 
 STATUS_NAMES = {
     ERR_SHAPE: "Shape", ERR_INVALID_SCALE: "InvalidScale", ERR_NONFINITE: "NonFinite",
     ERR_INVALID_GEOMETRY: "InvalidGeometry", ERR_CUDA: "Cuda", ERR_TIMEOUT: "Timeout",
     ERR_NCCL: "Nccl", ERR_UNSUPPORTED: "Unsupported", ERR_INVALID_ARGUMENT: "InvalidArgument",
+    ERR_PEER: "Peer",
 }
 
 
@@ -78,6 +83,14 @@ SIGNATURES = [
     ("urb_moe_layer_free", I32, [P]),
     ("urb_moe_forward", I32, [P, P, P, SZ, P, P, P, P, P, P, P, P]),
     ("urb_moe_forward_device", I32, [P, P, P, SZ, P, P, P, P]),
+    ("urb_moe_layer_create_sharded", I32, [P, P, P, SZ, SZ, SZ, P, P, P, P, P, P,
+                                           ctypes.POINTER(MoeGeometry), PP]),
+    ("urb_ep_create", I32, [P, P, I32, I32, SZ, U32, PP]),
+    ("urb_ep_export", I32, [P, P]),
+    ("urb_ep_connect", I32, [P, P]),
+    ("urb_ep_forward", I32, [P, P, P, SZ, P, P, P]),
+    ("urb_ep_forward_device", I32, [P, P, P, SZ, P, P, P, P]),
+    ("urb_ep_free", I32, [P]),
     ("urb_status_read", I32, [P, P, P]),
     ("urb_profile_enable", I32, [P, I32]),
     ("urb_profile_read", I32, [P, I32, P, P]),
