@@ -141,6 +141,18 @@ URB_API int urb_gated_mlp_forward(urb_ctx *ctx, const urb_mat *gate, const urb_m
 URB_API int urb_gated_mlp_forward_device(urb_ctx *ctx, const urb_mat *gate, const urb_mat *up,
                                          const urb_mat *down, const float *d_x, size_t tokens,
                                          float *d_out, int32_t *d_status);
+/* urb_gated_mlp_forward_device without any allocation (no counterpart in the reference, whose
+ * CPU path allocates per call).  For callers that cannot allocate device memory while they
+ * run: serving loops that reserve all free HBM up front, and per-token decode loops where a
+ * cudaMalloc would synchronise the device.  Temporaries live in one static 8 MiB device
+ * scratch per device; calls needing more are rejected (URB_ERR_UNSUPPORTED), roughly
+ * tokens * intermediate * 4 bytes must fit.  The first call on a device resolves the scratch
+ * (set-up; make it before any stream capture).  Calls overlapping in time on one device race
+ * on the scratch: serialise them. */
+URB_API int urb_gated_mlp_forward_device_noalloc(urb_ctx *ctx, const urb_mat *gate,
+                                                 const urb_mat *up, const urb_mat *down,
+                                                 const float *d_x, size_t tokens, float *d_out,
+                                                 int32_t *d_status);
 
 /* ---- routing -------------------------------------------------------------------------------- */
 

@@ -75,6 +75,7 @@ SIGNATURES = [
     ("urb_matmul_rows_device", I32, [P, P, P, SZ, P, P]),
     ("urb_gated_mlp_forward", I32, [P, P, P, P, P, SZ, P]),
     ("urb_gated_mlp_forward_device", I32, [P, P, P, P, P, SZ, P, P]),
+    ("urb_gated_mlp_forward_device_noalloc", I32, [P, P, P, P, P, SZ, P, P]),
     ("urb_route_noaux_tc", I32, [P, P, P, SZ, SZ, ctypes.POINTER(MoeGeometry), P, P, P]),
     ("urb_route_softmax_top_k", I32, [P, P, SZ, SZ, U32, P, P]),
     ("urb_group_routes", I32, [P, P, SZ, U32, SZ, P, P, P, P]),
