@@ -208,6 +208,20 @@ URB_API int urb_moe_forward_device(urb_ctx *ctx, urb_layer *layer, const float *
                            float *d_out, int32_t *d_route_expert, float *d_route_weight,
                            int32_t *d_status);
 
+/* The experts half of the layer forward for routes chosen by the caller (route_softmax_top_k of
+ * src/models/qwen3_8/moe.rs:91-159, DeepSeek hash routing, routes replayed from a trace): the
+ * ragged grouping and grouped SwiGLU experts of execute_batched_moe
+ * (src/models/qwen3_6/runtime.rs:1098-1148) with the GLM combine (f64 in the given route
+ * order, shared expert ungated; src/models/glm/runtime/moe.rs:164-175).  route_expert /
+ * route_weight [tokens, top_k]; ids outside [0, experts) are URB_ERR_SHAPE. */
+URB_API int urb_moe_forward_routed(urb_ctx *ctx, urb_layer *layer, const float *x, size_t tokens,
+                                   const int32_t *route_expert, const float *route_weight,
+                                   float *out);
+URB_API int urb_moe_forward_routed_device(urb_ctx *ctx, urb_layer *layer, const float *d_x,
+                                          size_t tokens, const int32_t *d_route_expert,
+                                          const float *d_route_weight, float *d_out,
+                                          int32_t *d_status);
+
 /* ---- expert parallelism across the GPUs of one node ------------------------------------------ */
 
 /* The layer forward of src/models/glm/runtime/moe.rs:138-176 split by experts over `world`

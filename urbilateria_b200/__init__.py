@@ -406,6 +406,18 @@ class RuntimeMoeLayer:
         extra["selection_score"] = s
         return out, ids, w, extra
 
+    def forward_routed(self, x, tokens: int, expert_ids, weights) -> np.ndarray:
+        """Experts half of the forward for caller-chosen routes ([tokens, top_k] ids and
+        weights, e.g. from route_softmax_top_k): grouped SwiGLU experts + f64 combine."""
+        K = self.geometry.top_k
+        x = np.ascontiguousarray(x, dtype=np.float32).ravel()
+        ids = np.ascontiguousarray(expert_ids, dtype=np.int32).reshape(tokens, K)
+        w = np.ascontiguousarray(weights, dtype=np.float32).reshape(tokens, K)
+        out = np.empty((tokens, self.hidden_size()), dtype=np.float32)
+        self.ctx.check(self.ctx.lib.urb_moe_forward_routed(
+            self.ctx.h, self.h, _ptr(x), tokens, _ptr(ids), _ptr(w), _ptr(out)))
+        return out
+
     def forward(self, x):
         """Single token: (Vec<f32>, Vec<RouteChoice>) as in the reference."""
         out, ids, w, extra = self.forward_batch(x, 1)

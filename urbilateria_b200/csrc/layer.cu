@@ -68,7 +68,8 @@ int route_device(Layer *L, const float *d_x, int T, const MoeWork &w, int32_t *d
 }
 
 int moe_forward_device(Layer *L, const float *d_x, int T, float *d_out, MoeWork *wout,
-                       int32_t *d_status, cudaStream_t st) {
+                       int32_t *d_status, cudaStream_t st, const int32_t *d_ids_in,
+                       const float *d_w_in) {
     Ctx *ctx = L->ctx;
     const size_t E = L->experts, K = L->geo.top_k, H = L->hidden, I = L->inter;
     const size_t TK = size_t(T) * K, cols = TK + T;
@@ -119,7 +120,7 @@ int moe_forward_device(Layer *L, const float *d_x, int T, float *d_out, MoeWork 
     if (cv.off > ctx->ws_size) {
         // Grow to the exact size of this forward (nothing has been enqueued yet) and restart.
         if (!workspace(ctx, cv.off, &rc)) return rc;
-        return moe_forward_device(L, d_x, T, d_out, wout, d_status, st);
+        return moe_forward_device(L, d_x, T, d_out, wout, d_status, st, d_ids_in, d_w_in);
     }
     w.status = d_status;
     if (!L->use_tc) {
@@ -134,8 +135,14 @@ int moe_forward_device(Layer *L, const float *d_x, int T, float *d_out, MoeWork 
         prof_end(ctx, st);
         if (rc) return cuda_fail(ctx, cudaGetLastError(), "row shift");
     }
-    rc = route_device(L, d_x, T, w, d_status, st);
-    if (rc) return rc;
+    if (d_ids_in) {
+        // Routes chosen by the caller: the grouping validates the expert ids.
+        w.ids = const_cast<int32_t *>(d_ids_in);
+        w.w = const_cast<float *>(d_w_in);
+    } else {
+        rc = route_device(L, d_x, T, w, d_status, st);
+        if (rc) return rc;
+    }
 
     const Mat *g0 = L->gate[0], *d0 = L->down[0];
     void **tb = L->d_tables;
@@ -583,6 +590,57 @@ int urb_moe_forward(urb_ctx *ctx, urb_layer *L, const float *x, size_t tokens, f
     if (counts) URB_CUDA(ctx, cudaMemcpyAsync(counts, w.counts, E * 4, cudaMemcpyDefault, st));
     if (perm_token) URB_CUDA(ctx, cudaMemcpyAsync(perm_token, w.perm_token, TK * 4, cudaMemcpyDefault, st));
     if (perm_slot) URB_CUDA(ctx, cudaMemcpyAsync(perm_slot, w.perm_slot, TK * 4, cudaMemcpyDefault, st));
+    URB_CUDA(ctx, cudaMemcpyAsync(&status, ctx->d_status, 4, cudaMemcpyDeviceToHost, st));
+    cudaFreeAsync(d_io, st);
+    URB_CUDA(ctx, cudaStreamSynchronize(st));
+    if (status) return set_error(ctx, status, "MoE forward rejected its input");
+    return URB_OK;
+}
+
+int urb_moe_forward_routed_device(urb_ctx *ctx, urb_layer *L, const float *d_x, size_t tokens,
+                                  const int32_t *d_route_expert, const float *d_route_weight,
+                                  float *d_out, int32_t *d_status) {
+    if (!ctx || !L || !d_x || !d_out || !d_route_expert || !d_route_weight)
+        return URB_ERR_INVALID_ARGUMENT;
+    if (L->e_count != L->experts)
+        return set_error(ctx, URB_ERR_UNSUPPORTED, "an expert shard runs through urb_ep_forward");
+    std::lock_guard<std::recursive_mutex> lk(ctx->mu);
+    cudaSetDevice(ctx->device);
+    if (tokens == 0) return URB_OK;
+    return moe_forward_device(L, d_x, int(tokens), d_out, nullptr, d_status, ctx->stream,
+                              d_route_expert, d_route_weight);
+}
+
+int urb_moe_forward_routed(urb_ctx *ctx, urb_layer *L, const float *x, size_t tokens,
+                           const int32_t *route_expert, const float *route_weight, float *out) {
+    if (!ctx || !L || !x || !out || !route_expert || !route_weight) return URB_ERR_INVALID_ARGUMENT;
+    if (L->e_count != L->experts)
+        return set_error(ctx, URB_ERR_UNSUPPORTED, "an expert shard runs through urb_ep_forward");
+    std::lock_guard<std::recursive_mutex> lk(ctx->mu);
+    cudaSetDevice(ctx->device);
+    if (tokens == 0) return URB_OK;
+    const size_t H = L->hidden, K = L->geo.top_k, TK = tokens * K;
+    for (size_t i = 0; i < TK; ++i)
+        if (route_expert[i] < 0 || size_t(route_expert[i]) >= L->experts)
+            return set_error(ctx, URB_ERR_SHAPE, "route expert id out of range");
+    cudaStream_t st = ctx->stream;
+    uint8_t *d_io = nullptr;
+    const size_t bytes = 2 * tokens * H * 4 + 2 * TK * 4;
+    URB_CUDA(ctx, cudaMallocAsync(&d_io, bytes, st));
+    float *d_x = reinterpret_cast<float *>(d_io), *d_out = d_x + tokens * H;
+    int32_t *d_ids = reinterpret_cast<int32_t *>(d_out + tokens * H);
+    float *d_w = reinterpret_cast<float *>(d_ids + TK);
+    URB_CUDA(ctx, cudaMemsetAsync(ctx->d_status, 0, 4, st));
+    URB_CUDA(ctx, cudaMemcpyAsync(d_x, x, tokens * H * 4, cudaMemcpyDefault, st));
+    URB_CUDA(ctx, cudaMemcpyAsync(d_ids, route_expert, TK * 4, cudaMemcpyDefault, st));
+    URB_CUDA(ctx, cudaMemcpyAsync(d_w, route_weight, TK * 4, cudaMemcpyDefault, st));
+    int rc = moe_forward_device(L, d_x, int(tokens), d_out, nullptr, ctx->d_status, st, d_ids, d_w);
+    if (rc) {
+        cudaFreeAsync(d_io, st);
+        return rc;
+    }
+    int32_t status = 0;
+    URB_CUDA(ctx, cudaMemcpyAsync(out, d_out, tokens * H * 4, cudaMemcpyDefault, st));
     URB_CUDA(ctx, cudaMemcpyAsync(&status, ctx->d_status, 4, cudaMemcpyDeviceToHost, st));
     cudaFreeAsync(d_io, st);
     URB_CUDA(ctx, cudaStreamSynchronize(st));

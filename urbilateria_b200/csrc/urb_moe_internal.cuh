@@ -95,8 +95,11 @@ struct MoeWork {
     uint8_t *bbuf_gu, *bbuf_dn;
 };
 
+// d_ids_in / d_w_in ([tokens, top_k], optional): routes chosen by the caller; the router is
+// skipped and these are grouped and combined instead.
 int moe_forward_device(Layer *L, const float *d_x, int tokens, float *d_out, MoeWork *work_out,
-                       int32_t *d_status, cudaStream_t st);
+                       int32_t *d_status, cudaStream_t st, const int32_t *d_ids_in = nullptr,
+                       const float *d_w_in = nullptr);
 // Exact router logits and route_noaux_tc of `tokens` rows into w.logits / x64 / gate / sel /
 // ids / w / score.
 int route_device(Layer *L, const float *d_x, int tokens, const MoeWork &w, int32_t *d_status,

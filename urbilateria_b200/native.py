@@ -84,6 +84,8 @@ SIGNATURES = [
     ("urb_moe_layer_free", I32, [P]),
     ("urb_moe_forward", I32, [P, P, P, SZ, P, P, P, P, P, P, P, P]),
     ("urb_moe_forward_device", I32, [P, P, P, SZ, P, P, P, P]),
+    ("urb_moe_forward_routed", I32, [P, P, P, SZ, P, P, P]),
+    ("urb_moe_forward_routed_device", I32, [P, P, P, SZ, P, P, P, P]),
     ("urb_moe_layer_create_sharded", I32, [P, P, P, SZ, SZ, SZ, P, P, P, P, P, P,
                                            ctypes.POINTER(MoeGeometry), PP]),
     ("urb_ep_create", I32, [P, P, I32, I32, SZ, U32, PP]),
