@@ -61,16 +61,18 @@ def test_tc_rejects_nonfinite_input(oracle, ctx, tc_path):
     dev.forward_batch(x, 3)
 
 
-def test_router_logits_bit_exact_adversarial(oracle, ctx):
+@pytest.mark.parametrize("hidden", [301, 4098, 4100, 7168])
+def test_router_logits_bit_exact_adversarial(oracle, ctx, hidden):
     # The logits run as f64 tensor-core chains; they must equal the reference's sequential
     # F64 sum bit for bit even when the order of roundings matters: activations spread over
-    # 2^-60 .. 2^60 with alternating signs (heavy cancellation), a hidden size that is not a
-    # multiple of 4 (scalar tail) and expert / token counts that are not multiples of 8.
-    g = syn.rng(4242)
-    hidden, experts, tokens = 301, 20, 13
+    # 2^-60 .. 2^30 with alternating signs (heavy cancellation), expert / token counts that are
+    # not multiples of 8, and hidden sizes covering the staged kernel's full stages (7168),
+    # its MMA remainder (4100) and scalar tail (4098), and the odd-width direct kernel (301).
+    g = syn.rng(4242 + hidden)
+    experts, tokens = 20, 13
     dev, orc = build_layer(oracle, ctx, g, hidden, 64, experts, "mxfp4", top_k=4, scale=1.0)
     mant = g.uniform(1.0, 2.0, size=(tokens, hidden))
-    expo = g.integers(-60, 61, size=(tokens, hidden))
+    expo = g.integers(-60, 31, size=(tokens, hidden))  # experts' outputs stay finite
     sign = np.where(g.random((tokens, hidden)) < 0.5, -1.0, 1.0)
     x = (sign * mant * np.exp2(expo)).astype(np.float32)
     x[:, ::7] = 0.0

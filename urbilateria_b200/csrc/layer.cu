@@ -117,10 +117,16 @@ int moe_forward_device(Layer *L, const float *d_x, int T, float *d_out, MoeWork 
         w.bbuf_gu = cv.take<uint8_t>(max_bs_bytes(L->fmt, T, K, E, ks_gu));
         w.bbuf_dn = cv.take<uint8_t>(max_bs_bytes(L->fmt, T, K, E, ks_dn));
     }
+    int32_t *own_status = cv.take<int32_t>(1);
     if (cv.off > ctx->ws_size) {
         // Grow to the exact size of this forward (nothing has been enqueued yet) and restart.
         if (!workspace(ctx, cv.off, &rc)) return rc;
         return moe_forward_device(L, d_x, T, d_out, wout, d_status, st, d_ids_in, d_w_in);
+    }
+    if (!d_status) {
+        // No status word from the caller: the stages still short-circuit on a private one.
+        d_status = own_status;
+        URB_CUDA(ctx, cudaMemsetAsync(d_status, 0, 4, st));
     }
     w.status = d_status;
     if (!L->use_tc) {

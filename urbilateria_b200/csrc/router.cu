@@ -6,39 +6,24 @@
 //    is exact in f64, so fma(w, x, acc) equals the reference's multiply-then-add.  The chains
 //    run on the FP64 tensor path: mma.sync m8n8k4 f64 advances an 8 x 8 block of chains by four
 //    columns as four fused multiply-adds in column order (checked bit for bit against
-//    sequential FMA chains on B200), so the logits are bit-identical at a fraction of the
-//    latency of dependent DFMAs.
+//    sequential FMA chains on B200), so the logits are bit-identical.  A chain is 1,792
+//    dependent MMAs for the C2 hidden size; its operands are staged through shared memory by
+//    TMA bulk copies several stages ahead, so the chain runs at the MMA latency instead of
+//    waiting on L2 for every step.
 //  * route_noaux_tc (src/math/routing.rs:38-155) and route_softmax_top_k
 //    (src/models/qwen3_8/moe.rs:91-159): one warp per token, IEEE f32 arithmetic in the
 //    reference's order, libm-exact expf, total_cmp ranking with the lower id winning ties.
 #include "expf_glibc.cuh"
+#include "tc_common.cuh"
 #include "urb_internal.cuh"
 
 namespace urb {
 namespace {
 
-constexpr int kRouterKc = 64;   // columns staged per tile
-constexpr int kRouterWarps = 4;
-constexpr int kRouterTpt = 2;   // token chains per thread
-constexpr int kRouterTok = kRouterWarps * kRouterTpt;  // tokens per CTA
-
-template <bool BF16>
-__device__ __forceinline__ double widen(const void *w, size_t idx) {
-    return BF16 ? double(__uint_as_float(uint32_t(static_cast<const uint16_t *>(w)[idx]) << 16))
-                : double(static_cast<const float *>(w)[idx]);
-}
-
-// CTA = 32 experts x 8 tokens; thread (lane = expert, warp = token pair) owns two chains and
-// performs, for each of them, exactly the reference's additions in column order.  The chains
-// are latency-bound (one f64 FMA after another), so a thread interleaves two of them and the
-// operands come from shared memory without bank conflicts: the experts' weights are staged
-// column-major (lane-contiguous), the token pair's x values as one broadcast 16-byte load.
-// Column tiles are double-buffered; the next tile is fetched into registers while the current
-// one is consumed.
 // Sigmoid gate and biased selection score of one logit (routing.rs:101-105), libm-exact.
 __device__ __forceinline__ void gate_of(float l, float b, const ExpfTable &tab, float *gate,
                                         float *sel, int32_t *status) {
-    if (!isfinite(l) || !isfinite(b)) atomicCAS(status, 0, int32_t(URB_ERR_NONFINITE));
+    if ((!isfinite(l) || !isfinite(b)) && status) atomicCAS(status, 0, int32_t(URB_ERR_NONFINITE));
     const float gv = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf_libm(-l, tab)));
     *gate = gv;
     *sel = __fadd_rn(gv, b);
@@ -54,83 +39,9 @@ struct GateOut {
 };
 
 template <bool BF16>
-__global__ void __launch_bounds__(32 * kRouterWarps) k_router_logits(const void *w, int experts,
-                                                                     int cols, const float *x,
-                                                                     int tokens, float *logits,
-                                                                     GateOut go) {
-    constexpr int KC = kRouterKc, NT = 32 * kRouterWarps;
-    constexpr int WPT = 32 * KC / NT;          // weights fetched per thread per tile (16)
-    constexpr int XPT = kRouterTok * KC / NT;  // x values fetched per thread per tile (4)
-    __shared__ __align__(16) double ws[2][KC][32];
-    __shared__ __align__(16) double xs[2][KC][kRouterTok];
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int e0 = blockIdx.x * 32, t0 = blockIdx.y * kRouterTok;
-    const int ntiles = (cols + KC - 1) / KC;
-    // Fetch geometry: weights row wr_r, columns wr_c .. +WPT; x row xr_r, columns xr_c .. +XPT.
-    const int wr_r = threadIdx.x / (KC / WPT), wr_c = (threadIdx.x % (KC / WPT)) * WPT;
-    const int xr_r = threadIdx.x / (KC / XPT), xr_c = (threadIdx.x % (KC / XPT)) * XPT;
-    double wr[WPT], xr[XPT];
-    auto fetch = [&](int tile) {
-        const int c0 = tile * KC;
-        const bool wrow = e0 + wr_r < experts, xrow = t0 + xr_r < tokens;
-#pragma unroll
-        for (int j = 0; j < WPT; ++j) {
-            const int c = c0 + wr_c + j;
-            wr[j] = (wrow && c < cols) ? widen<BF16>(w, size_t(e0 + wr_r) * cols + c) : 0.0;
-        }
-#pragma unroll
-        for (int j = 0; j < XPT; ++j) {
-            const int c = c0 + xr_c + j;
-            xr[j] = (xrow && c < cols) ? double(x[size_t(t0 + xr_r) * cols + c]) : 0.0;
-        }
-    };
-    auto stash = [&](int buf) {
-#pragma unroll
-        for (int j = 0; j < WPT; ++j) ws[buf][wr_c + j][wr_r] = wr[j];
-#pragma unroll
-        for (int j = 0; j < XPT; ++j) xs[buf][xr_c + j][xr_r] = xr[j];
-    };
-    fetch(0);
-    stash(0);
-    __syncthreads();
-    // Iterator::sum over f64 starts from -0.0 (bf16.rs:500).
-    double acc0 = -0.0, acc1 = -0.0;
-    for (int tile = 0; tile < ntiles; ++tile) {
-        const int buf = tile & 1;
-        if (tile + 1 < ntiles) fetch(tile + 1);
-        const int kc = min(KC, cols - tile * KC);
-        // Exactly the reference's additions: columns in order, one rounding each.
-        if (kc == KC) {
-#pragma unroll 16
-            for (int c = 0; c < KC; ++c) {
-                const double wv = ws[buf][c][lane];
-                const double2 xv = *reinterpret_cast<const double2 *>(&xs[buf][c][kRouterTpt * warp]);
-                acc0 = fma(wv, xv.x, acc0);
-                acc1 = fma(wv, xv.y, acc1);
-            }
-        } else {
-            for (int c = 0; c < kc; ++c) {
-                const double wv = ws[buf][c][lane];
-                const double2 xv = *reinterpret_cast<const double2 *>(&xs[buf][c][kRouterTpt * warp]);
-                acc0 = fma(wv, xv.x, acc0);
-                acc1 = fma(wv, xv.y, acc1);
-            }
-        }
-        if (tile + 1 < ntiles) stash(buf ^ 1);
-        __syncthreads();
-    }
-    const int e = e0 + lane, t = t0 + kRouterTpt * warp;
-    if (e < experts) {
-        const float l0 = float(acc0), l1 = float(acc1);
-        if (t < tokens) logits[size_t(t) * experts + e] = l0;
-        if (t + 1 < tokens) logits[size_t(t + 1) * experts + e] = l1;
-        if (go.gate) {
-            const float b = go.bias[e];
-            const size_t i0 = size_t(t) * experts + e, i1 = i0 + experts;
-            if (t < tokens) gate_of(l0, b, go.tab, go.gate + i0, go.sel + i0, go.status);
-            if (t + 1 < tokens) gate_of(l1, b, go.tab, go.gate + i1, go.sel + i1, go.status);
-        }
-    }
+__device__ __forceinline__ double widen(const void *w, size_t idx) {
+    return BF16 ? double(__uint_as_float(uint32_t(static_cast<const uint16_t *>(w)[idx]) << 16))
+                : double(static_cast<const float *>(w)[idx]);
 }
 
 // Widens a bf16 (BF16) or f32 matrix to f64 (exact), grid-stride.
@@ -174,6 +85,104 @@ __global__ void __launch_bounds__(32 * kDmmaWarps) k_router_dmma(const double *x
         dmma_8x8x4(d0, d1, a, b);
     }
     const int t = tb * 8 + (lane >> 2), e0 = eb * 8 + 2 * (lane & 3);
+    if (k4 < cols && t < tokens) {
+        const double *xr = x64 + size_t(t) * cols;
+        for (int k = k4; k < cols; ++k) {
+            if (e0 < experts) d0 = fma(w64[size_t(e0) * cols + k], xr[k], d0);
+            if (e0 + 1 < experts) d1 = fma(w64[size_t(e0 + 1) * cols + k], xr[k], d1);
+        }
+    }
+    if (t >= tokens) return;
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+        const int e = e0 + i;
+        if (e >= experts) continue;
+        const float l = float(i ? d1 : d0);
+        const size_t o = size_t(t) * experts + e;
+        logits[o] = l;
+        if (go.gate) gate_of(l, go.bias[e], go.tab, go.gate + o, go.sel + o, go.status);
+    }
+}
+
+// Staged form of k_router_dmma (same block shape, same chain order, bit-identical): the
+// block's 8 x rows and 8 router rows arrive in shared memory kRc columns at a time through
+// 1-D TMA bulk copies, kRnb stages ahead, each stage completing on its own mbarrier.  Rows are
+// padded to kRrow doubles so a lane's 8-byte reads are conflict-free (lanes 0-15 and 16-31
+// each cover the 32 banks once).  A stage is refilled only after the MMAs that read it have
+// been issued.  Columns past the last full stage are read from global memory as in
+// k_router_dmma.  Requires an even column count (16-byte aligned rows).
+constexpr int kRc = 64;
+constexpr int kRnb = 4;
+constexpr int kRrow = kRc + 4;
+constexpr int kRstage = 16 * kRrow;  // doubles per stage
+constexpr int kRsmem = kRnb * kRstage * 8 + kRnb * 8;
+
+__global__ void __launch_bounds__(32) k_router_dmma_staged(const double *x64, const double *w64,
+                                                           int tokens, int experts, int cols,
+                                                           float *logits, GateOut go,
+                                                           int32_t *status) {
+    extern __shared__ __align__(16) double rs[];
+    uint64_t *full = reinterpret_cast<uint64_t *>(rs + kRnb * kRstage);
+    const int lane = threadIdx.x;
+    const int eblk = (experts + 7) / 8;
+    const int blk = blockIdx.x;
+    if (blk >= eblk * ((tokens + 7) / 8)) return;
+    const int tb = blk / eblk, eb = blk % eblk;
+    const int nt = min(8, tokens - tb * 8), ne = min(8, experts - eb * 8);
+    const int nch = cols / kRc;
+    const uint32_t stage_bytes = uint32_t((nt + ne) * kRc * 8);
+    auto issue = [&](int ch) {  // one lane
+        double *dst = rs + (ch % kRnb) * kRstage;
+        uint64_t *bar = &full[ch % kRnb];
+        tc::mbar_arrive_expect_tx(bar, stage_bytes);
+        const size_t c0 = size_t(ch) * kRc;
+        for (int r = 0; r < nt; ++r)
+            tc::bulk_g2s(dst + r * kRrow, x64 + size_t(tb * 8 + r) * cols + c0, kRc * 8, bar);
+        for (int r = 0; r < ne; ++r)
+            tc::bulk_g2s(dst + (8 + r) * kRrow, w64 + size_t(eb * 8 + r) * cols + c0, kRc * 8, bar);
+    };
+    if (lane == 0) {
+        for (int s = 0; s < kRnb; ++s) tc::mbar_init(&full[s], 1);
+        tc::mbar_fence_init();
+        for (int s = 0; s < kRnb && s < nch; ++s) issue(s);
+    }
+    __syncwarp();
+    const int r = lane >> 2, kq = lane & 3;
+    double d0 = -0.0, d1 = -0.0;  // Iterator::sum over f64 starts from -0.0 (bf16.rs:500)
+    volatile int never = 0;
+    int ch = 0;
+    for (; ch < nch; ++ch) {
+        if (!tc::mbar_wait(&full[ch % kRnb], uint32_t(ch / kRnb) & 1u, &never)) break;
+        const double *b = rs + (ch % kRnb) * kRstage;
+        double a[kRc / 4], w[kRc / 4];
+#pragma unroll
+        for (int i = 0; i < kRc / 4; ++i) {
+            a[i] = b[r * kRrow + 4 * i + kq];
+            w[i] = b[(8 + r) * kRrow + 4 * i + kq];
+        }
+#pragma unroll
+        for (int i = 0; i < kRc / 4; ++i) dmma_8x8x4(d0, d1, a[i], w[i]);
+        __syncwarp();
+        if (lane == 0 && ch + kRnb < nch) issue(ch + kRnb);
+    }
+    if (ch < nch) {
+        // A stage never completed: report, let the copies still in flight land (bounded), and
+        // leave without writing logits.
+        if (lane == 0) atomicCAS(status, 0, int32_t(URB_ERR_TIMEOUT));
+        for (int c = ch; c < nch && c < ch + kRnb; ++c)
+            tc::mbar_wait(&full[c % kRnb], uint32_t(c / kRnb) & 1u, &never);
+        return;
+    }
+    // Remaining columns: whole groups of four by MMA, then the ragged tail by scalar FMAs.
+    const int ar = tb * 8 + r, bc = eb * 8 + r;
+    const bool arow = ar < tokens, bcol = bc < experts;
+    const int k4 = cols & ~3;
+    for (int k = nch * kRc; k < k4; k += 4) {
+        const double av = arow ? x64[size_t(ar) * cols + k + kq] : 0.0;
+        const double bv = bcol ? w64[size_t(bc) * cols + k + kq] : 0.0;
+        dmma_8x8x4(d0, d1, av, bv);
+    }
+    const int t = tb * 8 + r, e0 = eb * 8 + 2 * kq;
     if (k4 < cols && t < tokens) {
         const double *xr = x64 + size_t(t) * cols;
         for (int k = k4; k < cols; ++k) {
@@ -422,24 +431,6 @@ ExpfTable table_of(const Ctx *ctx) { return ExpfTable{ctx->expf_keys, ctx->expf_
 
 }  // namespace
 
-int launch_router_logits(const Mat *router, const float *d_x, int tokens, float *d_logits,
-                         cudaStream_t st, const RouterGates *rg) {
-    if (tokens <= 0) return URB_OK;
-    GateOut go{};
-    if (rg) go = GateOut{rg->bias, rg->gate, rg->sel, rg->status, table_of(rg->ctx)};
-    dim3 grid(unsigned((router->rows + 31) / 32), unsigned((tokens + kRouterTok - 1) / kRouterTok));
-    constexpr int nt = 32 * kRouterWarps;
-    if (router->format == URB_FMT_BF16)
-        k_router_logits<true><<<grid, nt, 0, st>>>(router->raw_values, int(router->rows),
-                                                   int(router->cols), d_x, tokens, d_logits, go);
-    else if (router->format == URB_FMT_F32)
-        k_router_logits<false><<<grid, nt, 0, st>>>(router->raw_values, int(router->rows),
-                                                    int(router->cols), d_x, tokens, d_logits, go);
-    else
-        return URB_ERR_UNSUPPORTED;
-    return cudaGetLastError() == cudaSuccess ? URB_OK : URB_ERR_CUDA;
-}
-
 int widen_router_f64(const Mat *router, double *dst, cudaStream_t st) {
     const size_t n = router->rows * router->cols;
     if (router->format == URB_FMT_BF16)
@@ -459,8 +450,17 @@ int launch_router_logits_f64(const double *w64, int experts, const float *d_x, i
     if (rg) go = GateOut{rg->bias, rg->gate, rg->sel, rg->status, table_of(rg->ctx)};
     k_to_f64<false><<<512, 256, 0, st>>>(d_x, size_t(tokens) * cols, x64);
     const int blocks = ((tokens + 7) / 8) * ((experts + 7) / 8);
-    k_router_dmma<<<(blocks + kDmmaWarps - 1) / kDmmaWarps, 32 * kDmmaWarps, 0, st>>>(
-        x64, w64, tokens, experts, cols, d_logits, go);
+    if (cols % 2 == 0 && rg && rg->status) {  // (the layer always passes a status word)
+        // Rows of an even column count start on 16-byte boundaries (bulk-copy sources).
+        cudaError_t e = cudaFuncSetAttribute(k_router_dmma_staged,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, kRsmem);
+        if (e != cudaSuccess) return URB_ERR_CUDA;
+        k_router_dmma_staged<<<blocks, 32, kRsmem, st>>>(x64, w64, tokens, experts, cols,
+                                                         d_logits, go, rg->status);
+    } else {
+        k_router_dmma<<<(blocks + kDmmaWarps - 1) / kDmmaWarps, 32 * kDmmaWarps, 0, st>>>(
+            x64, w64, tokens, experts, cols, d_logits, go);
+    }
     return cudaGetLastError() == cudaSuccess ? URB_OK : URB_ERR_CUDA;
 }
 

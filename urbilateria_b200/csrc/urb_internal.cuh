@@ -164,8 +164,7 @@ struct RouterGates {
     float *gate, *sel;  // [tokens, experts]
     int32_t *status;    // non-finite logit or bias -> URB_ERR_NONFINITE
 };
-int launch_router_logits(const Mat *router, const float *d_x, int tokens, float *d_logits,
-                         cudaStream_t st, const RouterGates *gates = nullptr);
+
 int launch_route_noaux(Ctx *ctx, const float *d_logits, const float *d_bias, int tokens,
                        int experts, const urb_moe_geometry &g, int32_t *d_expert,
                        float *d_weight, float *d_score, int32_t *d_status, cudaStream_t st,
