@@ -204,7 +204,7 @@ int ep_forward_device(Ep *ep, const float *d_x, int T, float *d_out, int32_t *d_
             return p;
         };
         w.logits = reinterpret_cast<float *>(take(tmax * E * 4));
-        w.x64 = reinterpret_cast<double *>(take(tmax * H * 8));
+        w.x64 = reinterpret_cast<double *>(take(router_f64_elems(int(tmax), int(H)) * 8));
         w.gate = reinterpret_cast<float *>(take(tmax * E * 4));
         w.sel = reinterpret_cast<float *>(take(tmax * E * 4));
         w.ids = reinterpret_cast<int32_t *>(take(tmax * K * 4));

@@ -83,7 +83,7 @@ int moe_forward_device(Layer *L, const float *d_x, int T, float *d_out, MoeWork 
     MoeWork w{};
     w.shift = cv.take<int32_t>(T);
     w.logits = cv.take<float>(size_t(T) * E);
-    w.x64 = cv.take<double>(size_t(T) * H);
+    w.x64 = cv.take<double>(router_f64_elems(T, int(H)));
     w.gate = cv.take<float>(size_t(T) * E);
     w.sel = cv.take<float>(size_t(T) * E);
     w.ids = cv.take<int32_t>(TK);
@@ -499,7 +499,8 @@ static int create_layer(urb_ctx *ctx, const urb_mat *router, const float *bias, 
         return set_error(ctx, URB_ERR_UNSUPPORTED, "expert shards need MX experts (tensor-core passes)");
     }
     cudaError_t err = cudaMalloc(&L->d_tables, tables.size() * sizeof(void *));
-    if (err == cudaSuccess) err = cudaMalloc(&L->router64, experts * H * sizeof(double));
+    if (err == cudaSuccess)
+        err = cudaMalloc(&L->router64, router_f64_elems(int(experts), int(H)) * sizeof(double));
     if (err == cudaSuccess && widen_router_f64(router, L->router64, ctx->stream) != URB_OK)
         err = cudaGetLastError();
     if (err == cudaSuccess) err = cudaMalloc(&L->d_bias, experts * 4);

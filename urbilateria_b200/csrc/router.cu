@@ -44,83 +44,45 @@ __device__ __forceinline__ double widen(const void *w, size_t idx) {
                 : double(static_cast<const float *>(w)[idx]);
 }
 
-// Widens a bf16 (BF16) or f32 matrix to f64 (exact), grid-stride.
-template <bool BF16>
-__global__ void k_to_f64(const void *src, size_t n, double *dst) {
-    for (size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x; i < n;
-         i += size_t(gridDim.x) * blockDim.x)
-        dst[i] = widen<BF16>(src, i);
-}
-
 __device__ __forceinline__ void dmma_8x8x4(double &d0, double &d1, double a, double b) {
     asm volatile("mma.sync.aligned.m8n8k4.row.col.f64.f64.f64.f64 {%0,%1}, {%2}, {%3}, {%0,%1};"
                  : "+d"(d0), "+d"(d1)
                  : "d"(a), "d"(b));
 }
 
-// One warp per 8 tokens x 8 experts, one warp per CTA so that the 512 blocks of a 128-token,
-// 256-expert forward spread over every SM (the FP64 path is throughput-bound per SM: CTAs of
-// four warps measured 1.9x slower).  A = x (row: token, k: column), B = router (k:
-// column, n: expert); lane q holds A[q/4][q%4], B[q%4][q/4] and D[q/4][2(q%4) .. +1].  The
-// columns past the last multiple of four are added by each lane with scalar FMAs, in order.
-constexpr int kDmmaWarps = 1;
-__global__ void __launch_bounds__(32 * kDmmaWarps) k_router_dmma(const double *x64,
-                                                                 const double *w64, int tokens,
-                                                                 int experts, int cols,
-                                                                 float *logits, GateOut go) {
-    const int lane = threadIdx.x & 31;
-    const int eblk = (experts + 7) / 8;
-    const int blk = blockIdx.x * kDmmaWarps + (threadIdx.x >> 5);
-    if (blk >= eblk * ((tokens + 7) / 8)) return;
-    const int tb = blk / eblk, eb = blk % eblk;
-    const int ar = tb * 8 + (lane >> 2), bc = eb * 8 + (lane >> 2), kq = lane & 3;
-    const bool arow = ar < tokens, bcol = bc < experts;
-    const double *xa = x64 + size_t(arow ? ar : 0) * cols + kq;
-    const double *wb = w64 + size_t(bcol ? bc : 0) * cols + kq;
-    double d0 = -0.0, d1 = -0.0;  // Iterator::sum over f64 starts from -0.0 (bf16.rs:500)
-    const int k4 = cols & ~3;
-#pragma unroll 8
-    for (int k = 0; k < k4; k += 4) {
-        const double a = arow ? xa[k] : 0.0, b = bcol ? wb[k] : 0.0;
-        dmma_8x8x4(d0, d1, a, b);
-    }
-    const int t = tb * 8 + (lane >> 2), e0 = eb * 8 + 2 * (lane & 3);
-    if (k4 < cols && t < tokens) {
-        const double *xr = x64 + size_t(t) * cols;
-        for (int k = k4; k < cols; ++k) {
-            if (e0 < experts) d0 = fma(w64[size_t(e0) * cols + k], xr[k], d0);
-            if (e0 + 1 < experts) d1 = fma(w64[size_t(e0 + 1) * cols + k], xr[k], d1);
-        }
-    }
-    if (t >= tokens) return;
-#pragma unroll
-    for (int i = 0; i < 2; ++i) {
-        const int e = e0 + i;
-        if (e >= experts) continue;
-        const float l = float(i ? d1 : d0);
-        const size_t o = size_t(t) * experts + e;
-        logits[o] = l;
-        if (go.gate) gate_of(l, go.bias[e], go.tab, go.gate + o, go.sel + o, go.status);
+// Widens a bf16 (BF16) or f32 row-major [rows, cols] matrix to f64 in the router's blocked
+// layout (exact): blocks of 8 rows, each cut into chunks of kRc columns stored as one
+// contiguous [8][kRrow] tile (rows padded to kRrow doubles), chunk-major within the block.
+// Rows past `rows`, columns past `cols` and the padding are zero.  One thread per element.
+template <bool BF16>
+__global__ void k_to_f64_blocked(const void *src, int rows, int cols, double *dst) {
+    const int nch = router_chunks(cols);
+    const size_t n = size_t((rows + 7) / 8) * nch * 8 * kRrow;
+    for (size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x; i < n;
+         i += size_t(gridDim.x) * blockDim.x) {
+        const int c = int(i % kRrow);
+        const size_t rest = i / kRrow;
+        const int r = int(rest % 8);
+        const size_t tile = rest / 8;
+        const int ch = int(tile % nch), rb = int(tile / nch);
+        const int row = rb * 8 + r, col = ch * kRc + c;
+        dst[i] = (c < kRc && row < rows && col < cols) ? widen<BF16>(src, size_t(row) * cols + col) : 0.0;
     }
 }
 
-// Staged form of k_router_dmma (same block shape, same chain order, bit-identical): the
-// block's 8 x rows and 8 router rows arrive in shared memory kRc columns at a time through
-// 1-D TMA bulk copies, kRnb stages ahead, each stage completing on its own mbarrier.  Rows are
-// padded to kRrow doubles so a lane's 8-byte reads are conflict-free (lanes 0-15 and 16-31
-// each cover the 32 banks once).  A stage is refilled only after the MMAs that read it have
-// been issued.  Columns past the last full stage are read from global memory as in
-// k_router_dmma.  Requires an even column count (16-byte aligned rows).
-constexpr int kRc = 64;
-constexpr int kRnb = 4;
-constexpr int kRrow = kRc + 4;
-constexpr int kRstage = 16 * kRrow;  // doubles per stage
-constexpr int kRsmem = kRnb * kRstage * 8 + kRnb * 8;
-
-__global__ void __launch_bounds__(32) k_router_dmma_staged(const double *x64, const double *w64,
-                                                           int tokens, int experts, int cols,
-                                                           float *logits, GateOut go,
-                                                           int32_t *status) {
+// One warp per 8 tokens x 8 experts (a block), one warp per CTA, so the 512 blocks of a
+// 128-token, 256-expert forward spread over every SM.  A = x (row: token, k: column), B =
+// router (k: column, n: expert); lane q holds A[q/4][q%4], B[q%4][q/4] and D[q/4][2(q%4) .. +1].
+// Each chain is one dependent MMA per four columns, so the kernel is bound by the MMA latency
+// as long as its operands are already in shared memory: the block's x tile and router tile of
+// each kRc-column chunk arrive by two 1-D TMA bulk copies, kRnb chunks ahead, each stage
+// completing on its own mbarrier; a stage is refilled only after the MMAs that read it have
+// been issued.  The padded rows make a lane's 8-byte reads conflict-free (lanes 0-15 and 16-31
+// each cover the 32 banks once).  In the last, partial chunk the columns past the last multiple
+// of four are added with scalar FMAs, in order.
+__global__ void __launch_bounds__(32) k_router_dmma(const double *x64b, const double *w64b,
+                                                    int tokens, int experts, int cols,
+                                                    float *logits, GateOut go, int32_t *status) {
     extern __shared__ __align__(16) double rs[];
     uint64_t *full = reinterpret_cast<uint64_t *>(rs + kRnb * kRstage);
     const int lane = threadIdx.x;
@@ -128,18 +90,16 @@ __global__ void __launch_bounds__(32) k_router_dmma_staged(const double *x64, co
     const int blk = blockIdx.x;
     if (blk >= eblk * ((tokens + 7) / 8)) return;
     const int tb = blk / eblk, eb = blk % eblk;
-    const int nt = min(8, tokens - tb * 8), ne = min(8, experts - eb * 8);
-    const int nch = cols / kRc;
-    const uint32_t stage_bytes = uint32_t((nt + ne) * kRc * 8);
+    const int nch = router_chunks(cols);
+    constexpr uint32_t kTile = 8 * kRrow * 8;  // bytes of one operand's tile
+    const double *xsrc = x64b + size_t(tb) * nch * 8 * kRrow;
+    const double *wsrc = w64b + size_t(eb) * nch * 8 * kRrow;
     auto issue = [&](int ch) {  // one lane
         double *dst = rs + (ch % kRnb) * kRstage;
         uint64_t *bar = &full[ch % kRnb];
-        tc::mbar_arrive_expect_tx(bar, stage_bytes);
-        const size_t c0 = size_t(ch) * kRc;
-        for (int r = 0; r < nt; ++r)
-            tc::bulk_g2s(dst + r * kRrow, x64 + size_t(tb * 8 + r) * cols + c0, kRc * 8, bar);
-        for (int r = 0; r < ne; ++r)
-            tc::bulk_g2s(dst + (8 + r) * kRrow, w64 + size_t(eb * 8 + r) * cols + c0, kRc * 8, bar);
+        tc::mbar_arrive_expect_tx(bar, 2 * kTile);
+        tc::bulk_g2s(dst, xsrc + size_t(ch) * 8 * kRrow, kTile, bar);
+        tc::bulk_g2s(dst + 8 * kRrow, wsrc + size_t(ch) * 8 * kRrow, kTile, bar);
     };
     if (lane == 0) {
         for (int s = 0; s < kRnb; ++s) tc::mbar_init(&full[s], 1);
@@ -154,42 +114,38 @@ __global__ void __launch_bounds__(32) k_router_dmma_staged(const double *x64, co
     for (; ch < nch; ++ch) {
         if (!tc::mbar_wait(&full[ch % kRnb], uint32_t(ch / kRnb) & 1u, &never)) break;
         const double *b = rs + (ch % kRnb) * kRstage;
-        double a[kRc / 4], w[kRc / 4];
+        const int kc = min(kRc, cols - ch * kRc);
+        if (kc == kRc) {
+            double a[kRc / 4], w[kRc / 4];
 #pragma unroll
-        for (int i = 0; i < kRc / 4; ++i) {
-            a[i] = b[r * kRrow + 4 * i + kq];
-            w[i] = b[(8 + r) * kRrow + 4 * i + kq];
+            for (int i = 0; i < kRc / 4; ++i) {
+                a[i] = b[r * kRrow + 4 * i + kq];
+                w[i] = b[(8 + r) * kRrow + 4 * i + kq];
+            }
+#pragma unroll
+            for (int i = 0; i < kRc / 4; ++i) dmma_8x8x4(d0, d1, a[i], w[i]);
+        } else {
+            const int k4 = kc & ~3;
+            for (int k = 0; k < k4; k += 4)
+                dmma_8x8x4(d0, d1, b[r * kRrow + k + kq], b[(8 + r) * kRrow + k + kq]);
+            for (int k = k4; k < kc; ++k) {  // lane: token r, experts 2kq, 2kq + 1
+                const double xv = b[r * kRrow + k];
+                d0 = fma(b[(8 + 2 * kq) * kRrow + k], xv, d0);
+                d1 = fma(b[(9 + 2 * kq) * kRrow + k], xv, d1);
+            }
         }
-#pragma unroll
-        for (int i = 0; i < kRc / 4; ++i) dmma_8x8x4(d0, d1, a[i], w[i]);
         __syncwarp();
         if (lane == 0 && ch + kRnb < nch) issue(ch + kRnb);
     }
     if (ch < nch) {
         // A stage never completed: report, let the copies still in flight land (bounded), and
         // leave without writing logits.
-        if (lane == 0) atomicCAS(status, 0, int32_t(URB_ERR_TIMEOUT));
+        if (lane == 0 && status) atomicCAS(status, 0, int32_t(URB_ERR_TIMEOUT));
         for (int c = ch; c < nch && c < ch + kRnb; ++c)
             tc::mbar_wait(&full[c % kRnb], uint32_t(c / kRnb) & 1u, &never);
         return;
     }
-    // Remaining columns: whole groups of four by MMA, then the ragged tail by scalar FMAs.
-    const int ar = tb * 8 + r, bc = eb * 8 + r;
-    const bool arow = ar < tokens, bcol = bc < experts;
-    const int k4 = cols & ~3;
-    for (int k = nch * kRc; k < k4; k += 4) {
-        const double av = arow ? x64[size_t(ar) * cols + k + kq] : 0.0;
-        const double bv = bcol ? w64[size_t(bc) * cols + k + kq] : 0.0;
-        dmma_8x8x4(d0, d1, av, bv);
-    }
     const int t = tb * 8 + r, e0 = eb * 8 + 2 * kq;
-    if (k4 < cols && t < tokens) {
-        const double *xr = x64 + size_t(t) * cols;
-        for (int k = k4; k < cols; ++k) {
-            if (e0 < experts) d0 = fma(w64[size_t(e0) * cols + k], xr[k], d0);
-            if (e0 + 1 < experts) d1 = fma(w64[size_t(e0 + 1) * cols + k], xr[k], d1);
-        }
-    }
     if (t >= tokens) return;
 #pragma unroll
     for (int i = 0; i < 2; ++i) {
@@ -432,35 +388,29 @@ ExpfTable table_of(const Ctx *ctx) { return ExpfTable{ctx->expf_keys, ctx->expf_
 }  // namespace
 
 int widen_router_f64(const Mat *router, double *dst, cudaStream_t st) {
-    const size_t n = router->rows * router->cols;
+    const int rows = int(router->rows), cols = int(router->cols);
     if (router->format == URB_FMT_BF16)
-        k_to_f64<true><<<1024, 256, 0, st>>>(router->raw_values, n, dst);
+        k_to_f64_blocked<true><<<1024, 256, 0, st>>>(router->raw_values, rows, cols, dst);
     else if (router->format == URB_FMT_F32)
-        k_to_f64<false><<<1024, 256, 0, st>>>(router->raw_values, n, dst);
+        k_to_f64_blocked<false><<<1024, 256, 0, st>>>(router->raw_values, rows, cols, dst);
     else
         return URB_ERR_UNSUPPORTED;
     return cudaGetLastError() == cudaSuccess ? URB_OK : URB_ERR_CUDA;
 }
 
-int launch_router_logits_f64(const double *w64, int experts, const float *d_x, int tokens,
-                             int cols, double *x64, float *d_logits, cudaStream_t st,
+int launch_router_logits_f64(const double *w64b, int experts, const float *d_x, int tokens,
+                             int cols, double *x64b, float *d_logits, cudaStream_t st,
                              const RouterGates *rg) {
     if (tokens <= 0) return URB_OK;
     GateOut go{};
     if (rg) go = GateOut{rg->bias, rg->gate, rg->sel, rg->status, table_of(rg->ctx)};
-    k_to_f64<false><<<512, 256, 0, st>>>(d_x, size_t(tokens) * cols, x64);
+    k_to_f64_blocked<false><<<592, 256, 0, st>>>(d_x, tokens, cols, x64b);
     const int blocks = ((tokens + 7) / 8) * ((experts + 7) / 8);
-    if (cols % 2 == 0 && rg && rg->status) {  // (the layer always passes a status word)
-        // Rows of an even column count start on 16-byte boundaries (bulk-copy sources).
-        cudaError_t e = cudaFuncSetAttribute(k_router_dmma_staged,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize, kRsmem);
-        if (e != cudaSuccess) return URB_ERR_CUDA;
-        k_router_dmma_staged<<<blocks, 32, kRsmem, st>>>(x64, w64, tokens, experts, cols,
-                                                         d_logits, go, rg->status);
-    } else {
-        k_router_dmma<<<(blocks + kDmmaWarps - 1) / kDmmaWarps, 32 * kDmmaWarps, 0, st>>>(
-            x64, w64, tokens, experts, cols, d_logits, go);
-    }
+    cudaError_t e = cudaFuncSetAttribute(k_router_dmma, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         kRsmem);
+    if (e != cudaSuccess) return URB_ERR_CUDA;
+    k_router_dmma<<<blocks, 32, kRsmem, st>>>(x64b, w64b, tokens, experts, cols, d_logits, go,
+                                             rg ? rg->status : nullptr);
     return cudaGetLastError() == cudaSuccess ? URB_OK : URB_ERR_CUDA;
 }
 

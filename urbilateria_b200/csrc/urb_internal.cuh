@@ -169,8 +169,20 @@ int launch_route_noaux(Ctx *ctx, const float *d_logits, const float *d_bias, int
                        int experts, const urb_moe_geometry &g, int32_t *d_expert,
                        float *d_weight, float *d_score, int32_t *d_status, cudaStream_t st,
                        const RouterGates *pre = nullptr);
-// Router logits on f64 copies: w64 [experts, cols] (widen_router_f64, resident), x64 [tokens,
-// cols] scratch widened from d_x here; bit-identical to the sequential F64 chain.
+// Router logits on f64 copies in the router's blocked layout: 8-row blocks cut into chunks of
+// kRc columns, each chunk one contiguous [8][kRrow] tile (rows padded; zero past the matrix).
+// w64 (widen_router_f64, resident) holds router_f64_elems(experts, cols) doubles, the x64
+// scratch router_f64_elems(tokens, cols), widened from d_x by launch_router_logits_f64.  The
+// logits are bit-identical to the sequential F64 chain.
+constexpr int kRc = 128;                  // columns per chunk (one shared-memory stage)
+constexpr int kRrow = kRc + 4;            // doubles per staged row
+constexpr int kRnb = 3;                   // stages in flight per block
+constexpr int kRstage = 16 * kRrow;       // doubles per stage (x tile + router tile)
+constexpr int kRsmem = kRnb * kRstage * 8 + kRnb * 8;
+__host__ __device__ constexpr int router_chunks(int cols) { return (cols + kRc - 1) / kRc; }
+__host__ __device__ constexpr size_t router_f64_elems(int rows, int cols) {
+    return size_t((rows + 7) / 8) * router_chunks(cols) * 8 * kRrow;
+}
 int widen_router_f64(const Mat *router, double *dst, cudaStream_t st);
 // Single-token product of rows [start, start + count) of a tiled MXFP4 / MXFP8 matrix.
 int launch_matvec1(Ctx *ctx, const Mat *m, size_t start, size_t count, const float *d_x,

@@ -55,7 +55,7 @@ int launch_combine(Ctx *ctx, const float *y, const float *shared_y, const float 
 struct Layer {
     Ctx *ctx = nullptr;
     const Mat *router = nullptr;
-    double *router64 = nullptr;  // router widened to f64 (the logits' FP64 MMA operand)
+    double *router64 = nullptr;  // router widened to f64, blocked (the logits' FP64 MMA operand)
     float *d_bias = nullptr;
     size_t experts = 0, hidden = 0, inter = 0;  // experts: routed experts in total (router rows)
     // Routed experts held by this layer: [e_begin, e_begin + e_count) (all of them unless the
@@ -76,7 +76,7 @@ struct MoeWork {
     int32_t *shift;       // [T]
     float *logits;        // [T, E]
     float *gate, *sel;    // [T, E] sigmoid gates and biased selection scores
-    double *x64;          // [T, H] x widened to f64
+    double *x64;          // x widened to f64 in the router's blocked layout
     int32_t *ids;         // [T, K]
     float *w, *score;     // [T, K]
     int32_t *counts, *offsets, *perm_token, *perm_slot, *inv;
