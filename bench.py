@@ -266,9 +266,12 @@ def main():
     ap.add_argument("--no-matvec", action="store_true")
     ap.add_argument("--experts", type=int, default=256,
                     help="routed experts (256 = config 2; smaller only for profiling captures)")
+    ap.add_argument("--tokens", type=int, default=128,
+                    help="tokens per GPU (128 = config 2; other values only for profiling)")
     args = ap.parse_args()
-    global EXPERTS
+    global EXPERTS, TOKENS
     EXPERTS = args.experts
+    TOKENS = args.tokens
 
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", str(args.gpus)))
