@@ -421,12 +421,12 @@ def main():
 
     # Roofline of the dominant kernel: the grouped gate/up pass streams gate+up of every
     # touched expert (held by this rank) and of the shared expert once, 2 * (7,340,032 packed +
-    # 458,752 scale) bytes per expert, and writes the f32 gate|up rows of every activation
-    # column (routes to the held experts + own tokens).
+    # 458,752 scale) bytes per expert, and writes the f32 h = silu(gate) * up row of every
+    # activation column (routes to the held experts + own tokens).
     gu_bytes_per_expert = 2 * (INTER * HIDDEN // 2 + INTER * HIDDEN // 32)
     n_cols = (TOKENS * TOP_K + TOKENS) if ep is None else \
         int(((ids_all >= eb) & (ids_all < eb + ec)).sum()) + TOKENS
-    gu_bytes = (touched + 1) * gu_bytes_per_expert + n_cols * 2 * INTER * 4
+    gu_bytes = (touched + 1) * gu_bytes_per_expert + n_cols * INTER * 4
     gu = kern.get("gate_up", {})
     achieved = gu_bytes / (gu.get("ms_per_launch", float("nan")) / 1e3) / 1e9
     roofline = {"kernel": "k_bs_grouped<MXFP4> gate/up (tcgen05.mma kind::mxf4 block_scale)",

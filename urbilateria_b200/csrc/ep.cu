@@ -217,8 +217,8 @@ int ep_forward_device(Ep *ep, const float *d_x, int T, float *d_out, int32_t *d_
         w.perm_token = reinterpret_cast<int32_t *>(take(RK * 4));
         w.perm_slot = reinterpret_cast<int32_t *>(take(RK * 4));
         w.inv = reinterpret_cast<int32_t *>(take(RK * 4));
-        w.gu = reinterpret_cast<float *>(take(cols * 2 * I * 4));
         y_sh = reinterpret_cast<float *>(take(tmax * H * 4));
+        w.h = reinterpret_cast<float *>(take(cols * I * 4));
         w.tsegs_gu = reinterpret_cast<TcSeg *>(take(ngrp_gu * sizeof(TcSeg)));
         w.tsegs_dn = reinterpret_cast<TcSeg *>(take(ngrp_dn * sizeof(TcSeg)));
         w.bslots_gu = reinterpret_cast<BsSlot *>(take(cols * sizeof(BsSlot)));
@@ -344,26 +344,26 @@ int ep_forward_device(Ep *ep, const float *d_x, int T, float *d_out, int32_t *d_
     ga.shared_row0 = ep->rank * int(tmax);
     ga.shared_rows = T;
     ga.slots = w.bslots_gu;
-    ga.out = w.gu;
-    ga.out_stride = int(2 * I);
+    ga.pair = 1;  // gate and up tiles of an expert together; the epilogue writes h
+    ga.out = w.h;
+    ga.out_stride = int(I);
     ga.status = status;
     rc = launch_tc_grouped(ctx, L->fmt, ga, URB_K_GATE_UP, st);
     if (rc) return rc;
 
-    // 4. Down projection; routed rows land in their owners' windows, shared rows in y_sh.
+    // 4. Down projection of h = silu(gate) * up; routed rows land in their owners' windows,
+    // shared rows in y_sh.
     TcArgs da{};
     da.segs = w.tsegs_dn;
     da.nsegs = w.tscalars + 2;
     da.total_units = w.tscalars + 3;
     da.unit_group = w.units_dn;
     da.bbuf = w.bbuf_dn;
-    da.src = w.gu;
-    da.src_stride = int(2 * I);
+    da.src = w.h;
+    da.src_stride = int(I);
     da.nrows = int(RK) + (shared ? T : 0);
     da.cols = int(I);
     da.ks = int(ks_dn);
-    da.swiglu = 1;
-    da.inv = nullptr;
     da.slots = w.bslots_dn;
     da.nvalid = w.offsets + El;
     da.routed_cols = int(RK);

@@ -17,18 +17,23 @@
 // instructions cost ~120-200 cycles of issue each on the issuing thread, while MMAs issued from
 // several threads proceed concurrently, so the per-stage instruction stream is spread over
 // warps:
-//   warp 0 (one thread)  weight producer: tiles into an 8-deep ring (bulk copies, mbarriers);
-//   activation producer (one thread): stages into a byte ring (variable-size stages, up to 16
-//                        in flight) from their L2-resident source;
+//   warp 0 (one thread)  weight producer: tiles into a 6-slot ring (bulk copies, mbarriers);
+//   warp 3 (one thread)  activation producer: stages into a byte ring (variable-size stages,
+//                        up to 16 in flight) from their L2-resident source;
 //   warps 8-11           scale warps: each stage's E8M0 scales of both operands from shared
 //                        memory into TMEM with tcgen05.st (each warp fills its lane quarter);
-//   warps 1, 2 [, 3, 12] (one thread each)  kBsIssuers MMA issuers: issuer i runs the MMAs of
-//                        its share of each stage's 4 K steps into its own TMEM accumulator and
-//                        releases stages two at a time with one tcgen05.commit on the pair's
-//                        release barrier (a 32-deep ring that both producers watch);
-//   warps 4-7            epilogue: tcgen05.ld of the issuers' accumulators, their sums and the
-//                        term sums, f32 row stores;
-//   warp 13 (one thread) activation producer (above).
+//   warps 1, 2           MMA issuers (one thread each), each into its own TMEM accumulator;
+//   warps 4-7            epilogue: tcgen05.ld of the accumulators, term sums, results out.
+// Down pass: a group is one matrix; the issuers split each stage's 4 K steps, release stages
+// two at a time (one tcgen05.commit on the pair's barrier, a 32-deep ring both producers
+// watch), and the epilogue adds their halves and stores f32 output rows.
+// Gate/up pass (paired groups): a stage brings the gate tile and the up tile of one expert
+// (two ring slots) against one activation stage; issuer 0 runs the gate MMAs, issuer 1 the up
+// MMAs (all four K steps each), every stage is released on its own barrier, and the epilogue
+// forms h = silu(gate) * up and writes it as f32 rows (one per column), the down pass's prep
+// source.
+// Units of N <= 64 MMA rows alternate between two 64-column halves of the accumulators, so the
+// epilogue of one unit overlaps the MMAs of the next.
 #include "tc_common.cuh"
 #include "urb_internal.cuh"
 #include "urb_tc.cuh"
@@ -92,14 +97,36 @@ __device__ __forceinline__ int round16i(int v) { return (v + 15) & ~15; }
 
 // Stage p has been consumed once its pair's release barrier has fired (the issuers commit after
 // every odd stage and after the last stage of the launch).
+// Paired groups (two weight tiles per stage) release every stage on its own barrier.
+template <bool PAIR>
 __device__ __forceinline__ bool wait_consumed(uint64_t *rel, uint32_t p, volatile int *abort) {
-    const uint32_t pair = p >> 1;
-    return tc::mbar_wait(&rel[pair % kRel], (pair / kRel) & 1, abort);
+    const uint32_t r = PAIR ? p : p >> 1;
+    return tc::mbar_wait(&rel[r % kRel], (r / kRel) & 1, abort);
 }
 
 struct Unit {
     int mt, sub, nt, n;
 };
+
+// Accumulator halves.  A unit of N <= 64 MMA rows takes one 64-column half of each issuer's
+// accumulator, alternating, so the epilogue drains one unit while the issuers fill the other
+// half with the next; a wider unit takes both halves.  Issuers and epilogue walk the same
+// units, so both derive the same assignment.
+struct AccHalves {
+    uint32_t next = 0;           // half for the next narrow unit
+    uint32_t use[2] = {0, 0};    // units that have used each half so far
+    uint32_t full[2] = {0, 0};   // completions of each half's full barrier seen so far
+    __device__ __forceinline__ uint32_t mask_of(int n) {  // halves used by a unit of N rows
+        if (n <= 64) {
+            const uint32_t h = next;
+            next ^= 1u;
+            return 1u << h;
+        }
+        next = 0;
+        return 3u;
+    }
+};
+__device__ __forceinline__ uint32_t first_half(uint32_t mask) { return mask == 2u ? 1u : 0u; }
 template <int FMT>
 __device__ __forceinline__ Unit unit_of(const TcSeg &S, int u) {
     Unit x;
@@ -110,268 +137,6 @@ __device__ __forceinline__ Unit unit_of(const TcSeg &S, int u) {
     x.n = round16i(bs_rows_per_tok(FMT) * x.nt);
     return x;
 }
-
-template <int FMT>
-__global__ void __launch_bounds__(kThreadsBs, 1) k_bs_grouped(TcArgs a) {
-    constexpr int TB = bs_tile_bytes(FMT);
-    constexpr int CH = bs_sf_chunks(FMT);
-    constexpr int KIND_FMT = FMT == URB_FMT_MXFP4 ? 1 : 0;
-    extern __shared__ __align__(1024) uint8_t smem_raw[];
-    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t *ring_a = smem;
-    uint8_t *ring_b = smem + size_t(kSA) * kStage;
-    __shared__ __align__(8) uint64_t a_full[kSA], sf_full[kSA], b_full[kSB], rel[kRel];
-    __shared__ __align__(8) uint64_t acc_full, acc_empty, mma_done[kIssuers];
-    __shared__ uint32_t b_off[kSB];  // byte offset of each in-flight activation stage
-    __shared__ uint32_t tmem_base;
-    __shared__ int abort_flag, skip, never;
-
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int nsegs = *a.nsegs;
-    const int total_units = *a.total_units;
-    if (threadIdx.x == 0) skip = (total_units <= 0 || nsegs <= 0 || (a.status && *a.status)) ? 1 : 0;
-    __syncthreads();
-    if (skip) return;
-
-    if (threadIdx.x == 0) {
-        for (int s = 0; s < kSA; ++s) {
-            tc::mbar_init(&a_full[s], 1);
-            tc::mbar_init(&sf_full[s], 4);   // one arrival per scale warp
-        }
-        for (int s = 0; s < kSB; ++s) tc::mbar_init(&b_full[s], 1);
-        for (int s = 0; s < kRel; ++s) tc::mbar_init(&rel[s], kIssuers);  // one commit per issuer
-        tc::mbar_init(&acc_full, kIssuers);
-        tc::mbar_init(&acc_empty, 4);
-        for (int s = 0; s < kIssuers; ++s) tc::mbar_init(&mma_done[s], 1);
-        tc::mbar_fence_init();
-        abort_flag = 0;
-        never = 0;
-    }
-    if (warp == 1) {
-        tc::tmem_alloc(&tmem_base, 512);
-        tc::tmem_relinquish();
-    }
-    tc::fence_before_sync();
-    __syncthreads();
-    tc::fence_after_sync();
-    const uint32_t tbase = tmem_base;
-    volatile int *abortp = &abort_flag;
-    auto fail = [&]() {
-        *abortp = 1;
-        set_status(a.status, URB_ERR_TIMEOUT);
-    };
-
-    if (warp == 0 && lane == 0) {
-        // ---------------- weight producer ----------------
-        uint32_t g = 0;  // copies issued
-        for (UnitCursor uc(a, total_units); uc.valid() && !*abortp; uc.advance()) {
-            const TcSeg &S = uc.cur;
-            const Unit x = unit_of<FMT>(S, uc.u);
-            const uint8_t *wsrc = S.w + size_t(x.mt) * TB;  // tile (mt, ks) at (ks * mts + mt)
-            bool ok = true;
-            for (int ks = 0; ks < S.ks; ++ks, ++g) {
-                const int sa = int(g % kSA);
-                if (g >= uint32_t(kSA) && !wait_consumed(rel, g - kSA, abortp)) {  // slot free
-                    ok = false;
-                    break;
-                }
-                tc::mbar_arrive_expect_tx(&a_full[sa], uint32_t(TB));
-                tc::bulk_g2s(ring_a + size_t(sa) * kStage, wsrc + size_t(ks) * S.mts * TB, TB, &a_full[sa]);
-            }
-            if (!ok) { fail(); break; }
-        }
-        // Let every copy this thread issued land before the CTA can exit.
-        for (uint32_t i = g > uint32_t(kSA) ? g - kSA : 0; i < g; ++i)
-            tc::mbar_wait(&a_full[i % kSA], (i / kSA) & 1, &never);
-    } else if (warp == kWarpBProd && lane == 0) {
-        // ---------------- activation producer ----------------
-        // Byte ring: stage g occupies [q_start, q_end) (1 KB granules, contiguous) until stage g
-        // has been consumed; the oldest in-flight stage is retired by waiting on its release
-        // barrier.  At most kSB stages are in flight.
-        uint32_t q_start[kSB];
-        uint32_t g = 0, oldest = 0, head = 0;
-        for (UnitCursor uc(a, total_units); uc.valid() && !*abortp; uc.advance()) {
-            const TcSeg &S = uc.cur;
-            const Unit x = unit_of<FMT>(S, uc.u);
-            const uint32_t bbytes = uint32_t(bs_bstage_bytes(FMT, x.n));
-            const uint32_t need = (bbytes + 1023) & ~1023u;
-            const uint8_t *bsrc = a.bbuf + S.b_off + (long long)x.sub * S.ks * bs_bstage_bytes(FMT, kBsNmax);
-            bool ok = true;
-            for (int ks = 0; ks < S.ks && ok; ++ks, ++g) {
-                uint32_t pos = 0;
-                for (;;) {
-                    const uint32_t inflight = g - oldest;
-                    if (inflight == 0) { head = 0; pos = 0; break; }
-                    if (inflight < uint32_t(kSB)) {
-                        const uint32_t tail = q_start[oldest % kSB];
-                        // Both wrapped placements are strict: a wrapped ring never fills up to
-                        // its tail, so head == tail only ever means "nothing in flight".
-                        if (head >= tail) {  // used [tail, head): free [head, end) and [0, tail)
-                            if (head + need <= uint32_t(kBRing)) { pos = head; break; }
-                            if (need < tail) { pos = 0; break; }
-                        } else if (head + need < tail) {  // used [tail, end) + [0, head)
-                            pos = head;
-                            break;
-                        }
-                    }
-                    if (!wait_consumed(rel, oldest, abortp)) { ok = false; break; }
-                    ++oldest;
-                }
-                if (!ok) break;
-                const int sb = int(g % kSB);
-                q_start[sb] = pos;
-                head = pos + need;
-                b_off[sb] = pos;
-                tc::mbar_arrive_expect_tx(&b_full[sb], bbytes);
-                tc::bulk_g2s(ring_b + pos, bsrc + size_t(ks) * bbytes, bbytes, &b_full[sb]);
-            }
-            if (!ok) { fail(); break; }
-        }
-        for (uint32_t i = g > uint32_t(kSB) ? g - kSB : 0; i < g; ++i)
-            tc::mbar_wait(&b_full[i % kSB], (i / kSB) & 1, &never);
-    } else if (warp >= 8 && warp < 12) {
-        // ---------------- scale warps ----------------
-        // TMEM scale slot sa (16 columns): A's chunks at +0 / +4, B's at +8 / +12; lane l of
-        // every quarter holds bytes 16 l .. 16 l + 15 of each 512-byte chunk.
-        const uint32_t lane_base = uint32_t(32 * (warp & 3)) << 16;
-        uint32_t g = 0;
-        for (UnitCursor uc(a, total_units); uc.valid() && !*abortp; uc.advance()) {
-            const TcSeg &S = uc.cur;
-            const Unit x = unit_of<FMT>(S, uc.u);
-            bool ok = true;
-            for (int ks = 0; ks < S.ks; ++ks, ++g) {
-                const int sa = int(g % kSA), sb = int(g % kSB);
-                if (!tc::mbar_wait(&a_full[sa], (g / kSA) & 1, abortp) ||
-                    !tc::mbar_wait(&b_full[sb], (g / kSB) & 1, abortp)) {
-                    ok = false;
-                    break;
-                }
-                const uint8_t *sfa = ring_a + size_t(sa) * kStage + 16384 + 16 * lane;
-                const uint8_t *sfb = ring_b + b_off[sb] + x.n * 128 + 16 * lane;
-                uint32_t v[16];
-#pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    uint4 qa = make_uint4(0, 0, 0, 0), qb = make_uint4(0, 0, 0, 0);
-                    if (h < CH) {
-                        qa = *reinterpret_cast<const uint4 *>(sfa + 512 * h);
-                        qb = *reinterpret_cast<const uint4 *>(sfb + 512 * h);
-                    }
-                    v[4 * h] = qa.x; v[4 * h + 1] = qa.y; v[4 * h + 2] = qa.z; v[4 * h + 3] = qa.w;
-                    v[8 + 4 * h] = qb.x; v[9 + 4 * h] = qb.y; v[10 + 4 * h] = qb.z; v[11 + 4 * h] = qb.w;
-                }
-                tc::tmem_st16(tbase + lane_base + kSfCol0 + 16u * sa, v);
-                tc::wait_st();
-                tc::fence_before_sync();
-                __syncwarp();
-                if (lane == 0) tc::mbar_arrive(&sf_full[sa]);
-            }
-            if (!ok) { fail(); break; }
-        }
-    } else if ((warp == 1 || warp == 2 || (kIssuers == 4 && (warp == 3 || warp == 12))) && lane == 0) {
-        // ---------------- MMA issuers (their K steps of every stage) ----------------
-        const int me = warp == 12 ? 3 : warp - 1;
-        const uint32_t acc = tbase + uint32_t(me) * kAccCols;
-        uint32_t g = 0, j = 0;
-        for (UnitCursor uc(a, total_units); uc.valid() && !*abortp; uc.advance(), ++j) {
-            const TcSeg &S = uc.cur;
-            const Unit x = unit_of<FMT>(S, uc.u);
-            if (j >= 1 && !tc::mbar_wait(&acc_empty, (j - 1) & 1, abortp)) { fail(); break; }
-            tc::fence_after_sync();
-            bool ok = true;
-            for (int ks = 0; ks < S.ks; ++ks, ++g) {
-                const int sa = int(g % kSA), sb = int(g % kSB);
-                // The scale warps arrive only after both copies of the stage have landed.
-                if (!tc::mbar_wait(&sf_full[sa], (g / kSA) & 1, abortp)) { ok = false; break; }
-                tc::fence_after_sync();
-                const uint32_t sA = tc::smem_u32(ring_a + size_t(sa) * kStage);
-                const uint32_t sB = tc::smem_u32(ring_b + b_off[sb]);
-                const uint32_t sfa = tbase + kSfCol0 + 16u * sa, sfb = sfa + 8;
-                const uint64_t adesc = tc::sdesc_sw128(sA), bdesc = tc::sdesc_sw128(sB);
-#pragma unroll
-                for (int k2 = 0; k2 < kStepsPerIssuer; ++k2) {
-                    const int kk = me * kStepsPerIssuer + k2;
-                    const bool accum = ks > 0 || k2 > 0;
-                    if (FMT == URB_FMT_MXFP4) {
-                        const uint32_t id = 2u * (kk & 1), col = 4u * (kk >> 1);
-                        tc::mma_mxf4(acc, adesc + 2 * kk, bdesc + 2 * kk, tc::idesc_bs(KIND_FMT, x.n, id, id),
-                                     (sfa + col) | (id << 30), (sfb + col) | (id << 30), accum);
-                    } else {
-                        const uint32_t id = uint32_t(kk);
-                        tc::mma_mxf8(acc, adesc + 2 * kk, bdesc + 2 * kk, tc::idesc_bs(KIND_FMT, x.n, id, id),
-                                     sfa | (id << 30), sfb | (id << 30), accum);
-                    }
-                }
-                const bool last = ks == S.ks - 1 && uc.u + uc.step >= uc.total;
-                if ((g & 1) || last) tc::mma_commit(&rel[(g >> 1) % kRel]);
-                if (ks == S.ks - 1) tc::mma_commit(&acc_full);
-            }
-            if (!ok) { fail(); break; }
-        }
-        // Every MMA of this thread completes before TMEM is released.
-        tc::mma_commit(&mma_done[me]);
-        tc::mbar_wait(&mma_done[me], 0, &never);
-    } else if (warp >= 4 && warp < 8) {
-        // ---------------- epilogue ----------------
-        constexpr int RT = bs_rows_per_tok(FMT), TT = bs_terms(FMT), TPC = 16 / RT;
-        const int q = warp & 3;  // TMEM lane quarter this warp may access
-        const int row = 32 * q + lane;
-        const uint32_t lane_base = uint32_t(32 * q) << 16;
-        uint32_t j = 0;
-        for (UnitCursor uc(a, total_units); uc.valid() && !*abortp; uc.advance(), ++j) {
-            const TcSeg &S = uc.cur;
-            const Unit x = unit_of<FMT>(S, uc.u);
-            if (!tc::mbar_wait(&acc_full, j & 1, abortp)) { fail(); break; }
-            tc::fence_after_sync();
-            const int grow = x.mt * 128 + row;
-            const bool row_ok = grow < S.rows;
-            const int tok0 = x.sub * bs_cap(FMT);
-            for (int c = 0; c < x.n / 16; ++c) {
-                uint32_t v[kIssuers][16];
-#pragma unroll
-                for (int i = 0; i < kIssuers; ++i)
-                    tc::tmem_ld16(tbase + lane_base + uint32_t(i) * kAccCols + 16 * c, v[i]);
-                tc::wait_ld();
-#pragma unroll
-                for (int s = 0; s < TPC; ++s) {
-                    const int t = TPC * c + s;
-                    if (t < x.nt && row_ok) {
-                        float o = 0.0f;
-#pragma unroll
-                        for (int e = 0; e < TT; ++e) {
-                            float q = __uint_as_float(v[0][RT * s + e]) + __uint_as_float(v[1][RT * s + e]);
-                            if constexpr (kIssuers == 4)
-                                q += __uint_as_float(v[2][RT * s + e]) + __uint_as_float(v[3][RT * s + e]);
-                            o += q;
-                        }
-                        const int col = S.col_begin + tok0 + t;
-                        float *dst;
-                        if (a.out_ranks && col < a.routed_cols) {
-                            const int i = a.out_rows[col];
-                            dst = a.out_ranks[i / a.out_rank_rows] + size_t(i % a.out_rank_rows) * a.out_stride;
-                        } else {
-                            dst = a.out + size_t(a.out_ranks ? col - a.routed_cols : col) * a.out_stride;
-                        }
-                        dst[S.out_off + grow] = o;
-                    }
-                }
-            }
-            tc::fence_before_sync();
-            __syncwarp();
-            if (lane == 0) tc::mbar_arrive(&acc_empty);
-        }
-        // Rows stored into other ranks' memory are visible system-wide before the exchange
-        // barrier that follows this launch signals them.
-        if (a.out_ranks) __threadfence_system();
-    }
-    tc::fence_before_sync();
-    __syncthreads();
-    if (warp == 1) {
-        tc::fence_after_sync();
-        tc::tmem_dealloc(tbase, 512);
-    }
-}
-
-// ---- activation terms -------------------------------------------------------------------
 
 // 2^e as a float for -149 <= e <= 127 (exact; subnormal below -126).
 __device__ __forceinline__ float pow2f(int e) {
@@ -412,6 +177,329 @@ __device__ __forceinline__ int e4m3_round(float a, float *dq) {
     *dq = m * pow2f(k - 3);
     return ((k + 7) << 3) | (int(m) - 8);
 }
+
+// PAIR (gate/up pass): each group carries the gate (w) and up (w2) tiles of one expert; a
+// stage brings both tiles and one activation stage, issuer 0 runs the gate MMAs and issuer 1 the
+// up MMAs (all four K steps each), and the epilogue writes h = silu(gate) * up.  Otherwise
+// (down pass) the issuers split each stage's K steps and the epilogue writes the output rows.
+template <int FMT, bool PAIR>
+__global__ void __launch_bounds__(kThreadsBs, 1) k_bs_grouped(TcArgs a) {
+    static_assert(!PAIR || kIssuers == 2, "paired groups run one issuer per projection");
+    constexpr int TPS = PAIR ? 2 : 1;  // weight tiles per stage
+    // Weight slots and activation ring bytes (the same split measured best for both modes:
+    // 6 / 7 and 10 / 3 slots gave the paired pass 0.62 ms at C2, 8 / 5 gave 0.76 ms).
+    constexpr int SA = kSA;
+    constexpr int BRING = kBRing;
+    constexpr int TB = bs_tile_bytes(FMT);
+    constexpr int CH = bs_sf_chunks(FMT);
+    constexpr int KIND_FMT = FMT == URB_FMT_MXFP4 ? 1 : 0;
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t *ring_a = smem;
+    uint8_t *ring_b = smem + size_t(SA) * kStage;
+    __shared__ __align__(8) uint64_t a_full[SA], sf_full[SA], b_full[kSB], rel[kRel];
+    __shared__ __align__(8) uint64_t acc_full[2], acc_empty[2], mma_done[kIssuers];
+    __shared__ uint32_t b_off[kSB];  // byte offset of each in-flight activation stage
+    __shared__ uint32_t tmem_base;
+    __shared__ int abort_flag, skip, never;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nsegs = *a.nsegs;
+    const int total_units = *a.total_units;
+    if (threadIdx.x == 0) skip = (total_units <= 0 || nsegs <= 0 || (a.status && *a.status)) ? 1 : 0;
+    __syncthreads();
+    if (skip) return;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < SA; ++s) {
+            tc::mbar_init(&a_full[s], 1);
+            tc::mbar_init(&sf_full[s], 4);   // one arrival per scale warp
+        }
+        for (int s = 0; s < kSB; ++s) tc::mbar_init(&b_full[s], 1);
+        for (int s = 0; s < kRel; ++s) tc::mbar_init(&rel[s], kIssuers);  // one commit per issuer
+        for (int h = 0; h < 2; ++h) {
+            tc::mbar_init(&acc_full[h], kIssuers);
+            tc::mbar_init(&acc_empty[h], 4);
+        }
+        for (int s = 0; s < kIssuers; ++s) tc::mbar_init(&mma_done[s], 1);
+        tc::mbar_fence_init();
+        abort_flag = 0;
+        never = 0;
+    }
+    if (warp == 1) {
+        tc::tmem_alloc(&tmem_base, 512);
+        tc::tmem_relinquish();
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+    const uint32_t tbase = tmem_base;
+    volatile int *abortp = &abort_flag;
+    auto fail = [&]() {
+        *abortp = 1;
+        set_status(a.status, URB_ERR_TIMEOUT);
+    };
+
+    if (warp == 0 && lane == 0) {
+        // ---------------- weight producer ----------------
+        uint32_t g = 0;  // tiles issued (stage * TPS + i)
+        for (UnitCursor uc(a, total_units); uc.valid() && !*abortp; uc.advance()) {
+            const TcSeg &S = uc.cur;
+            const Unit x = unit_of<FMT>(S, uc.u);
+            const uint8_t *wsrc = S.w + size_t(x.mt) * TB;  // tile (mt, ks) at (ks * mts + mt)
+            const uint8_t *wsrc2 = PAIR ? S.w2 + size_t(x.mt) * TB : nullptr;
+            bool ok = true;
+            for (int ks = 0; ks < S.ks && ok; ++ks) {
+#pragma unroll
+                for (int i = 0; i < TPS; ++i, ++g) {
+                    const int sa = int(g % SA);
+                    // The slot is free once the stage of the tile it held has been consumed.
+                    if (g >= uint32_t(SA) && !wait_consumed<PAIR>(rel, (g - SA) / TPS, abortp)) {
+                        ok = false;
+                        break;
+                    }
+                    tc::mbar_arrive_expect_tx(&a_full[sa], uint32_t(TB));
+                    tc::bulk_g2s(ring_a + size_t(sa) * kStage,
+                                 (i ? wsrc2 : wsrc) + size_t(ks) * S.mts * TB, TB, &a_full[sa]);
+                }
+            }
+            if (!ok) { fail(); break; }
+        }
+        // Let every copy this thread issued land before the CTA can exit.
+        for (uint32_t i = g > uint32_t(SA) ? g - SA : 0; i < g; ++i)
+            tc::mbar_wait(&a_full[i % SA], (i / SA) & 1, &never);
+    } else if (warp == kWarpBProd && lane == 0) {
+        // ---------------- activation producer ----------------
+        // Byte ring: stage g occupies [q_start, q_end) (1 KB granules, contiguous) until stage g
+        // has been consumed; the oldest in-flight stage is retired by waiting on its release
+        // barrier.  At most kSB stages are in flight.
+        uint32_t q_start[kSB];
+        uint32_t g = 0, oldest = 0, head = 0;
+        for (UnitCursor uc(a, total_units); uc.valid() && !*abortp; uc.advance()) {
+            const TcSeg &S = uc.cur;
+            const Unit x = unit_of<FMT>(S, uc.u);
+            const uint32_t bbytes = uint32_t(bs_bstage_bytes(FMT, x.n));
+            const uint32_t need = (bbytes + 1023) & ~1023u;
+            const uint8_t *bsrc = a.bbuf + S.b_off + (long long)x.sub * S.ks * bs_bstage_bytes(FMT, kBsNmax);
+            bool ok = true;
+            for (int ks = 0; ks < S.ks && ok; ++ks, ++g) {
+                uint32_t pos = 0;
+                for (;;) {
+                    const uint32_t inflight = g - oldest;
+                    if (inflight == 0) { head = 0; pos = 0; break; }
+                    if (inflight < uint32_t(kSB)) {
+                        const uint32_t tail = q_start[oldest % kSB];
+                        // Both wrapped placements are strict: a wrapped ring never fills up to
+                        // its tail, so head == tail only ever means "nothing in flight".
+                        if (head >= tail) {  // used [tail, head): free [head, end) and [0, tail)
+                            if (head + need <= uint32_t(BRING)) { pos = head; break; }
+                            if (need < tail) { pos = 0; break; }
+                        } else if (head + need < tail) {  // used [tail, end) + [0, head)
+                            pos = head;
+                            break;
+                        }
+                    }
+                    if (!wait_consumed<PAIR>(rel, oldest, abortp)) { ok = false; break; }
+                    ++oldest;
+                }
+                if (!ok) break;
+                const int sb = int(g % kSB);
+                q_start[sb] = pos;
+                head = pos + need;
+                b_off[sb] = pos;
+                tc::mbar_arrive_expect_tx(&b_full[sb], bbytes);
+                tc::bulk_g2s(ring_b + pos, bsrc + size_t(ks) * bbytes, bbytes, &b_full[sb]);
+            }
+            if (!ok) { fail(); break; }
+        }
+        for (uint32_t i = g > uint32_t(kSB) ? g - kSB : 0; i < g; ++i)
+            tc::mbar_wait(&b_full[i % kSB], (i / kSB) & 1, &never);
+    } else if (warp >= 8 && warp < 12) {
+        // ---------------- scale warps ----------------
+        // TMEM scale slot sa (16 columns): A's chunks at +0 / +4, B's at +8 / +12; lane l of
+        // every quarter holds bytes 16 l .. 16 l + 15 of each 512-byte chunk.
+        const uint32_t lane_base = uint32_t(32 * (warp & 3)) << 16;
+        uint32_t g = 0;
+        for (UnitCursor uc(a, total_units); uc.valid() && !*abortp; uc.advance()) {
+            const TcSeg &S = uc.cur;
+            const Unit x = unit_of<FMT>(S, uc.u);
+            bool ok = true;
+            for (int ks = 0; ks < S.ks; ++ks, ++g) {
+                const uint32_t t0 = g * TPS;  // first weight tile of the stage
+                const int sa = int(t0 % SA), sa1 = int((t0 + TPS - 1) % SA), sb = int(g % kSB);
+                if (!tc::mbar_wait(&a_full[sa], (t0 / SA) & 1, abortp) ||
+                    (PAIR && !tc::mbar_wait(&a_full[sa1], ((t0 + 1) / SA) & 1, abortp)) ||
+                    !tc::mbar_wait(&b_full[sb], (g / kSB) & 1, abortp)) {
+                    ok = false;
+                    break;
+                }
+                // Slot sa: A's scales at +0 / +4, B's at +8 / +12; PAIR: the up tile's A scales
+                // in its own slot sa1 (+0 / +4).
+                const uint8_t *sfa = ring_a + size_t(sa) * kStage + 16384 + 16 * lane;
+                const uint8_t *sfa1 = ring_a + size_t(sa1) * kStage + 16384 + 16 * lane;
+                const uint8_t *sfb = ring_b + b_off[sb] + x.n * 128 + 16 * lane;
+                uint32_t v[16], v1[16];
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    uint4 qa = make_uint4(0, 0, 0, 0), qb = make_uint4(0, 0, 0, 0);
+                    uint4 qa1 = make_uint4(0, 0, 0, 0);
+                    if (h < CH) {
+                        qa = *reinterpret_cast<const uint4 *>(sfa + 512 * h);
+                        qb = *reinterpret_cast<const uint4 *>(sfb + 512 * h);
+                        if (PAIR) qa1 = *reinterpret_cast<const uint4 *>(sfa1 + 512 * h);
+                    }
+                    v[4 * h] = qa.x; v[4 * h + 1] = qa.y; v[4 * h + 2] = qa.z; v[4 * h + 3] = qa.w;
+                    v[8 + 4 * h] = qb.x; v[9 + 4 * h] = qb.y; v[10 + 4 * h] = qb.z; v[11 + 4 * h] = qb.w;
+                    v1[4 * h] = qa1.x; v1[4 * h + 1] = qa1.y; v1[4 * h + 2] = qa1.z; v1[4 * h + 3] = qa1.w;
+                    v1[8 + 4 * h] = 0; v1[9 + 4 * h] = 0; v1[10 + 4 * h] = 0; v1[11 + 4 * h] = 0;
+                }
+                tc::tmem_st16(tbase + lane_base + kSfCol0 + 16u * sa, v);
+                if (PAIR) tc::tmem_st16(tbase + lane_base + kSfCol0 + 16u * sa1, v1);
+                tc::wait_st();
+                tc::fence_before_sync();
+                __syncwarp();
+                if (lane == 0) tc::mbar_arrive(&sf_full[sa]);
+            }
+            if (!ok) { fail(); break; }
+        }
+    } else if ((warp == 1 || warp == 2 || (kIssuers == 4 && (warp == 3 || warp == 12))) && lane == 0) {
+        // ---------------- MMA issuers (their K steps of every stage) ----------------
+        const int me = warp == 12 ? 3 : warp - 1;
+        uint32_t g = 0;
+        AccHalves ah;
+        for (UnitCursor uc(a, total_units); uc.valid() && !*abortp; uc.advance()) {
+            const TcSeg &S = uc.cur;
+            const Unit x = unit_of<FMT>(S, uc.u);
+            const uint32_t mask = ah.mask_of(x.n), h0 = first_half(mask);
+            const uint32_t acc = tbase + uint32_t(me) * kAccCols + 64u * h0;
+            bool empty_ok = true;
+            for (uint32_t h = 0; h < 2; ++h) {
+                if (!(mask >> h & 1u)) continue;
+                if (ah.use[h] >= 1 && !tc::mbar_wait(&acc_empty[h], (ah.use[h] - 1) & 1, abortp))
+                    empty_ok = false;
+                ++ah.use[h];
+            }
+            if (!empty_ok) { fail(); break; }
+            tc::fence_after_sync();
+            bool ok = true;
+            for (int ks = 0; ks < S.ks; ++ks, ++g) {
+                const uint32_t t0 = g * TPS;
+                const int sa = int(t0 % SA), sb = int(g % kSB);
+                // PAIR: issuer 0 multiplies the gate tile (slot sa), issuer 1 the up tile.
+                const int sam = PAIR ? int((t0 + uint32_t(me)) % SA) : sa;
+                // The scale warps arrive only after every copy of the stage has landed.
+                if (!tc::mbar_wait(&sf_full[sa], (t0 / SA) & 1, abortp)) { ok = false; break; }
+                tc::fence_after_sync();
+                const uint32_t sA = tc::smem_u32(ring_a + size_t(sam) * kStage);
+                const uint32_t sB = tc::smem_u32(ring_b + b_off[sb]);
+                const uint32_t sfa = tbase + kSfCol0 + 16u * sam, sfb = tbase + kSfCol0 + 16u * sa + 8;
+                const uint64_t adesc = tc::sdesc_sw128(sA), bdesc = tc::sdesc_sw128(sB);
+                constexpr int kSteps = PAIR ? 4 : kStepsPerIssuer;
+#pragma unroll
+                for (int k2 = 0; k2 < kSteps; ++k2) {
+                    const int kk = PAIR ? k2 : me * kStepsPerIssuer + k2;
+                    const bool accum = ks > 0 || k2 > 0;
+                    if (FMT == URB_FMT_MXFP4) {
+                        const uint32_t id = 2u * (kk & 1), col = 4u * (kk >> 1);
+                        tc::mma_mxf4(acc, adesc + 2 * kk, bdesc + 2 * kk, tc::idesc_bs(KIND_FMT, x.n, id, id),
+                                     (sfa + col) | (id << 30), (sfb + col) | (id << 30), accum);
+                    } else {
+                        const uint32_t id = uint32_t(kk);
+                        tc::mma_mxf8(acc, adesc + 2 * kk, bdesc + 2 * kk, tc::idesc_bs(KIND_FMT, x.n, id, id),
+                                     sfa | (id << 30), sfb | (id << 30), accum);
+                    }
+                }
+                const bool last = ks == S.ks - 1 && uc.u + uc.step >= uc.total;
+                if (PAIR) tc::mma_commit(&rel[g % kRel]);
+                else if ((g & 1) || last) tc::mma_commit(&rel[(g >> 1) % kRel]);
+                if (ks == S.ks - 1) tc::mma_commit(&acc_full[h0]);
+            }
+            if (!ok) { fail(); break; }
+        }
+        // Every MMA of this thread completes before TMEM is released.
+        tc::mma_commit(&mma_done[me]);
+        tc::mbar_wait(&mma_done[me], 0, &never);
+    } else if (warp >= 4 && warp < 8) {
+        // ---------------- epilogue ----------------
+        constexpr int RT = bs_rows_per_tok(FMT), TT = bs_terms(FMT), TPC = 16 / RT;
+        const int q = warp & 3;  // TMEM lane quarter this warp may access
+        const int row = 32 * q + lane;
+        const uint32_t lane_base = uint32_t(32 * q) << 16;
+        AccHalves ah;
+        for (UnitCursor uc(a, total_units); uc.valid() && !*abortp; uc.advance()) {
+            const TcSeg &S = uc.cur;
+            const Unit x = unit_of<FMT>(S, uc.u);
+            const uint32_t mask = ah.mask_of(x.n), h0 = first_half(mask);
+            if (!tc::mbar_wait(&acc_full[h0], ah.full[h0]++ & 1, abortp)) { fail(); break; }
+            tc::fence_after_sync();
+            const int grow = x.mt * 128 + row;
+            const bool row_ok = grow < S.rows;
+            const int tok0 = x.sub * bs_cap(FMT);
+            for (int c = 0; c < x.n / 16; ++c) {
+                uint32_t v[kIssuers][16];
+#pragma unroll
+                for (int i = 0; i < kIssuers; ++i)
+                    tc::tmem_ld16(tbase + lane_base + uint32_t(i) * kAccCols + 64u * h0 + 16 * c, v[i]);
+                tc::wait_ld();
+                if constexpr (PAIR) {
+                    // h = silu(gate) * up of this lane's row for each token of the chunk.
+#pragma unroll
+                    for (int s = 0; s < TPC; ++s) {
+                        const int t = TPC * c + s;
+                        if (t >= x.nt || !row_ok) continue;
+                        float gv = 0.0f, uv = 0.0f;
+#pragma unroll
+                        for (int e = 0; e < TT; ++e) {
+                            gv += __uint_as_float(v[0][RT * s + e]);
+                            uv += __uint_as_float(v[1][RT * s + e]);
+                        }
+                        a.out[size_t(S.col_begin + tok0 + t) * a.out_stride + grow] = silu_f(gv) * uv;
+                    }
+                    continue;
+                }
+#pragma unroll
+                for (int s = 0; s < TPC; ++s) {
+                    const int t = TPC * c + s;
+                    if (t < x.nt && row_ok) {
+                        float o = 0.0f;
+#pragma unroll
+                        for (int e = 0; e < TT; ++e) {
+                            float q = __uint_as_float(v[0][RT * s + e]) + __uint_as_float(v[1][RT * s + e]);
+                            if constexpr (kIssuers == 4)
+                                q += __uint_as_float(v[2][RT * s + e]) + __uint_as_float(v[3][RT * s + e]);
+                            o += q;
+                        }
+                        const int col = S.col_begin + tok0 + t;
+                        float *dst;
+                        if (a.out_ranks && col < a.routed_cols) {
+                            const int i = a.out_rows[col];
+                            dst = a.out_ranks[i / a.out_rank_rows] + size_t(i % a.out_rank_rows) * a.out_stride;
+                        } else {
+                            dst = a.out + size_t(a.out_ranks ? col - a.routed_cols : col) * a.out_stride;
+                        }
+                        dst[S.out_off + grow] = o;
+                    }
+                }
+            }
+            tc::fence_before_sync();
+            __syncwarp();
+            if (lane == 0)
+                for (uint32_t h = 0; h < 2; ++h)
+                    if (mask >> h & 1u) tc::mbar_arrive(&acc_empty[h]);
+        }
+        // Rows stored into other ranks' memory are visible system-wide before the exchange
+        // barrier that follows this launch signals them.
+        if (a.out_ranks) __threadfence_system();
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    if (warp == 1) {
+        tc::fence_after_sync();
+        tc::tmem_dealloc(tbase, 512);
+    }
+}
+
+// ---- activation terms -------------------------------------------------------------------
 
 // One residual term of a 32-value block held by a lane quad (8 values per lane): the E8M0
 // exponent e that fits the block's max|r| into the element range, the element codes of
@@ -604,7 +692,7 @@ int launch_bs_t(Ctx *ctx, const TcArgs &a, int kind, cudaStream_t st) {
         prof_end(ctx, st);
         URB_CUDA(ctx, cudaGetLastError());
     }
-    auto k = k_bs_grouped<FMT>;
+    auto k = a.pair ? k_bs_grouped<FMT, true> : k_bs_grouped<FMT, false>;
     URB_CUDA(ctx, cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBs));
     prof_begin(ctx, kind, st);
     k<<<ctx->num_sms, kThreadsBs, kSmemBs, st>>>(a);

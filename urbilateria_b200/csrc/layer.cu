@@ -106,7 +106,6 @@ int moe_forward_device(Layer *L, const float *d_x, int T, float *d_out, MoeWork 
     const size_t sc = size_t(bs_stage_cols(L->fmt));
     const size_t ks_gu = div_ceil(H, sc), ks_dn = div_ceil(I, sc);
     if (L->use_tc) {
-        w.gu = cv.take<float>(cols * 2 * I);
         w.tsegs_gu = cv.take<TcSeg>(ngrp_gu);
         w.tsegs_dn = cv.take<TcSeg>(ngrp_dn);
         w.bslots_gu = cv.take<BsSlot>(cols);
@@ -253,26 +252,25 @@ int moe_forward_device(Layer *L, const float *d_x, int T, float *d_out, MoeWork 
         ga.shared_row0 = 0;
         ga.shared_rows = T;
         ga.slots = w.bslots_gu;
-        ga.out = w.gu;
-        ga.out_stride = int(2 * I);
+        ga.pair = 1;  // gate and up tiles of an expert together; the epilogue writes h
+        ga.out = w.h;
+        ga.out_stride = int(I);
         ga.status = d_status;
         rc = launch_tc_grouped(ctx, L->fmt, ga, URB_K_GATE_UP, st);
         if (rc) return rc;
 
-        // Down projection of h = silu(gate) * up (formed while writing its activation terms).
+        // Down projection of h = silu(gate) * up.
         TcArgs da{};
         da.segs = w.tsegs_dn;
         da.nsegs = w.tscalars + 2;
         da.total_units = w.tscalars + 3;
         da.unit_group = w.units_dn;
         da.bbuf = w.bbuf_dn;
-        da.src = w.gu;
-        da.src_stride = int(2 * I);
+        da.src = w.h;
+        da.src_stride = int(I);
         da.nrows = int(L->sg ? TK + T : TK);
         da.cols = int(I);
         da.ks = int(ks_dn);
-        da.swiglu = 1;
-        da.inv = nullptr;
         da.slots = w.bslots_dn;
         da.out = w.y;
         da.out_stride = int(H);

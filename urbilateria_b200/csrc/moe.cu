@@ -201,9 +201,8 @@ __global__ void k_combine(const float *y, const float *shared_y, const float *w,
 }
 
 // Groups of the tensor-core passes (single CTA).  Gate/up pass: per routed expert with tokens
-// a gate group (which owns the activation stages) and an up group reading the same stages,
-// then the shared expert's pair; down pass: one group per routed expert, then the shared
-// expert.  A group of c tokens has ceil(c / bs_cap) sub-segments; its units are mts * nsub.
+// one paired group (gate and up tiles against the same activation stages), then the shared
+// expert's; down pass: one group per routed expert, then the shared expert.  A group of c tokens has ceil(c / bs_cap) sub-segments; its units are mts * nsub.
 // Activation-stage offsets are a prefix over owning groups of the bytes their stages take.
 __device__ __forceinline__ int round16(int x) { return (x + 15) & ~15; }
 
@@ -240,7 +239,7 @@ __global__ void __launch_bounds__(1024) k_build_tc_segs(TcBuildArgs b) {
     const int E = b.experts, TK = b.tokens * b.top_k;
     const int sc = bs_stage_cols(b.fmt);
     for (int pass = 0; pass < 2; ++pass) {
-        const int mats = pass == 0 ? 2 : 1;  // groups per expert
+        const int mats = 1;  // groups per expert (gate/up: one paired group)
         const int ks = pass == 0 ? (b.hidden + sc - 1) / sc : (b.inter + sc - 1) / sc;
         const int mts = pass == 0 ? (b.inter + 127) / 128 : (b.hidden + 127) / 128;
         // Per thread: experts [e0, e1); groups, units and activation bytes.
@@ -286,9 +285,10 @@ __global__ void __launch_bounds__(1024) k_build_tc_segs(TcBuildArgs b) {
         long long boff = ib - nb + (warp ? wsum[warp - 1] : 0);
         TcSeg *out = pass == 0 ? b.gu : b.dn;
         BsSlot *sl = pass == 0 ? b.gu_slots : b.dn_slots;
-        auto emit = [&](const uint8_t *wg, int m, int col0, int c) {
+        auto emit = [&](const uint8_t *wg, const uint8_t *wu, int m, int col0, int c) {
             TcSeg s;
             s.w = wg;
+            s.w2 = wu;
             s.b_off = boff;
             s.mts = mts;
             s.ks = ks;
@@ -309,12 +309,11 @@ __global__ void __launch_bounds__(1024) k_build_tc_segs(TcBuildArgs b) {
             if (c <= 0) continue;
             const int col0 = b.offsets[e];
             if (pass == 0) {
-                emit(b.gate_tc[e], 0, col0, c);
-                emit(b.up_tc[e], 1, col0, c);
+                emit(b.gate_tc[e], b.up_tc[e], 0, col0, c);
             } else {
-                emit(b.down_tc[e], 0, col0, c);
+                emit(b.down_tc[e], nullptr, 0, col0, c);
             }
-            // Activation slots of the expert's columns (the up group reads the gate's stages).
+            // Activation slots of the expert's columns.
             for (int j = 0; j < c; ++j) sl[col0 + j] = slot_of(b.fmt, boff, ks, c, j);
             boff += bs_group_bytes(b.fmt, c, ks);
         }
@@ -324,10 +323,9 @@ __global__ void __launch_bounds__(1024) k_build_tc_segs(TcBuildArgs b) {
             sh_boff = boff;
             if (b.has_shared && b.shared_tokens > 0) {
                 if (pass == 0) {
-                    emit(b.sh_gate_tc, 0, TK, b.shared_tokens);
-                    emit(b.sh_up_tc, 1, TK, b.shared_tokens);
+                    emit(b.sh_gate_tc, b.sh_up_tc, 0, TK, b.shared_tokens);
                 } else {
-                    emit(b.sh_down_tc, 0, TK, b.shared_tokens);
+                    emit(b.sh_down_tc, nullptr, 0, TK, b.shared_tokens);
                 }
             }
             s_groups = gi;

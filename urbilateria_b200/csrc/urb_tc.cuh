@@ -31,7 +31,8 @@ __host__ __device__ constexpr int bs_bstage_bytes(int fmt, int n) { return n * 1
 // (128-row tile mt, sub-segment j) pairs, j fastest, so the sub-segments of a large group read
 // the same weight tile back to back (the second read is served by L2).
 struct TcSeg {
-    const uint8_t *w;     // bs tiles of the matrix
+    const uint8_t *w;     // bs tiles of the matrix (gate/up pass: the gate projection)
+    const uint8_t *w2;    // gate/up pass: bs tiles of the up projection (nullptr otherwise)
     long long b_off;      // byte offset of the group's activation stages in the B buffer
     int mts, ks;          // 128-row tiles, K stages
     int rows, cols;       // real rows / input columns
@@ -58,8 +59,8 @@ struct TcArgs {
     uint8_t *bbuf;             // activation stages (written by the prep kernel)
     // Prep: source rows (row-major f32), each written to the activation columns that use it.
     // Gate/up pass: src = x, row t feeds columns inv[t * top_k + k] and, with a shared expert,
-    // shared_col0 + t.  Down pass (inv == nullptr): src row c = [gate | up] of column c,
-    // h = silu(gate) * up, feeding column c.
+    // shared_col0 + t.  Down pass (inv == nullptr): src row c = h of column c (or, with
+    // swiglu, [gate | up] of column c and h = silu(gate) * up), feeding column c.
     const float *src;
     int src_stride;
     int nrows;                 // source rows
@@ -70,6 +71,9 @@ struct TcArgs {
     int shared_row0, shared_rows;  // source rows [shared_row0, +shared_rows) feed the shared
                                    // expert's columns shared_col0 + (r - shared_row0)
     const BsSlot *slots;       // [activation columns]
+    // Gate/up pass: pair = 1, each group pairs the gate and up tiles of one expert and the
+    // epilogue writes h = silu(gate) * up rows to `out` (row = activation column).
+    int pair;
     float *out;
     int out_stride;
     int32_t *status;
