@@ -302,6 +302,7 @@ int ep_forward_device(Ep *ep, const float *d_x, int T, float *d_out, int32_t *d_
     bb.down_tc = reinterpret_cast<const uint8_t *const *>(tb + 8 * S);
     bb.has_shared = shared ? 1 : 0;
     bb.shared_tokens = T;
+    bb.pair_down = 1;
     if (shared) {
         bb.sh_gate_tc = L->sg->tc_tiles;
         bb.sh_up_tc = L->su->tc_tiles;
@@ -362,6 +363,7 @@ int ep_forward_device(Ep *ep, const float *d_x, int T, float *d_out, int32_t *d_
     da.src = w.h;
     da.src_stride = int(I);
     da.nrows = int(RK) + (shared ? T : 0);
+    da.pair = 2;  // neighbouring row tiles share each activation stage
     da.cols = int(I);
     da.ks = int(ks_dn);
     da.slots = w.bslots_dn;

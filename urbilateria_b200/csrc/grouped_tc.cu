@@ -127,12 +127,14 @@ struct AccHalves {
     }
 };
 __device__ __forceinline__ uint32_t first_half(uint32_t mask) { return mask == 2u ? 1u : 0u; }
-template <int FMT>
+// TPU: row tiles per unit (2 when neighbouring tiles are paired).
+template <int FMT, int TPU = 1>
 __device__ __forceinline__ Unit unit_of(const TcSeg &S, int u) {
     Unit x;
     const int r = u - S.unit_begin;
-    x.mt = r / S.nsub;
-    x.sub = r - x.mt * S.nsub;
+    const int mu = r / S.nsub;
+    x.sub = r - mu * S.nsub;
+    x.mt = mu * TPU;
     x.nt = min(bs_cap(FMT), S.ntok - x.sub * bs_cap(FMT));
     x.n = round16i(bs_rows_per_tok(FMT) * x.nt);
     return x;
@@ -178,13 +180,20 @@ __device__ __forceinline__ int e4m3_round(float a, float *dq) {
     return ((k + 7) << 3) | (int(m) - 8);
 }
 
-// PAIR (gate/up pass): each group carries the gate (w) and up (w2) tiles of one expert; a
+// MODE 1 (gate/up pass): each group carries the gate (w) and up (w2) tiles of one expert; a
 // stage brings both tiles and one activation stage, issuer 0 runs the gate MMAs and issuer 1 the
-// up MMAs (all four K steps each), and the epilogue writes h = silu(gate) * up.  Otherwise
-// (down pass) the issuers split each stage's K steps and the epilogue writes the output rows.
-template <int FMT, bool PAIR>
+// up MMAs (all four K steps each), and the epilogue writes h = silu(gate) * up.
+// MODE 2 (down pass, paired row tiles): a unit covers row tiles mt and mt + 1 of one matrix;
+// a stage brings both tiles against one activation stage, issuer i runs tile mt + i (all four
+// K steps), and the epilogue writes both tiles' output rows (a missing last tile of an odd
+// count is neither copied nor multiplied).
+// MODE 0: the issuers split each stage's K steps of one tile; the epilogue adds their halves.
+template <int FMT, int MODE>
 __global__ void __launch_bounds__(kThreadsBs, 1) k_bs_grouped(TcArgs a) {
-    static_assert(!PAIR || kIssuers == 2, "paired groups run one issuer per projection");
+    constexpr bool PAIR = MODE != 0;   // two weight tiles per stage, one per issuer
+    constexpr bool GU = MODE == 1, MT = MODE == 2;
+    constexpr int TPU = MT ? 2 : 1;    // row tiles per unit
+    static_assert(!PAIR || kIssuers == 2, "paired tiles run one issuer per tile");
     constexpr int TPS = PAIR ? 2 : 1;  // weight tiles per stage
     // Weight slots and activation ring bytes (the same split measured best for both modes:
     // 6 / 7 and 10 / 3 slots gave the paired pass 0.62 ms at C2, 8 / 5 gave 0.76 ms).
@@ -245,9 +254,11 @@ __global__ void __launch_bounds__(kThreadsBs, 1) k_bs_grouped(TcArgs a) {
         uint32_t g = 0;  // tiles issued (stage * TPS + i)
         for (UnitCursor uc(a, total_units); uc.valid() && !*abortp; uc.advance()) {
             const TcSeg &S = uc.cur;
-            const Unit x = unit_of<FMT>(S, uc.u);
+            const Unit x = unit_of<FMT, TPU>(S, uc.u);
             const uint8_t *wsrc = S.w + size_t(x.mt) * TB;  // tile (mt, ks) at (ks * mts + mt)
-            const uint8_t *wsrc2 = PAIR ? S.w2 + size_t(x.mt) * TB : nullptr;
+            const uint8_t *wsrc2 = GU ? S.w2 + size_t(x.mt) * TB
+                                      : (MT ? S.w + size_t(x.mt + 1) * TB : nullptr);
+            const bool second = !MT || x.mt + 1 < S.mts;  // the unit's second tile exists
             bool ok = true;
             for (int ks = 0; ks < S.ks && ok; ++ks) {
 #pragma unroll
@@ -257,6 +268,10 @@ __global__ void __launch_bounds__(kThreadsBs, 1) k_bs_grouped(TcArgs a) {
                     if (g >= uint32_t(SA) && !wait_consumed<PAIR>(rel, (g - SA) / TPS, abortp)) {
                         ok = false;
                         break;
+                    }
+                    if (i == 1 && !second) {  // no tile: complete the slot's phase empty
+                        tc::mbar_arrive(&a_full[sa]);
+                        continue;
                     }
                     tc::mbar_arrive_expect_tx(&a_full[sa], uint32_t(TB));
                     tc::bulk_g2s(ring_a + size_t(sa) * kStage,
@@ -277,7 +292,7 @@ __global__ void __launch_bounds__(kThreadsBs, 1) k_bs_grouped(TcArgs a) {
         uint32_t g = 0, oldest = 0, head = 0;
         for (UnitCursor uc(a, total_units); uc.valid() && !*abortp; uc.advance()) {
             const TcSeg &S = uc.cur;
-            const Unit x = unit_of<FMT>(S, uc.u);
+            const Unit x = unit_of<FMT, TPU>(S, uc.u);
             const uint32_t bbytes = uint32_t(bs_bstage_bytes(FMT, x.n));
             const uint32_t need = (bbytes + 1023) & ~1023u;
             const uint8_t *bsrc = a.bbuf + S.b_off + (long long)x.sub * S.ks * bs_bstage_bytes(FMT, kBsNmax);
@@ -322,7 +337,7 @@ __global__ void __launch_bounds__(kThreadsBs, 1) k_bs_grouped(TcArgs a) {
         uint32_t g = 0;
         for (UnitCursor uc(a, total_units); uc.valid() && !*abortp; uc.advance()) {
             const TcSeg &S = uc.cur;
-            const Unit x = unit_of<FMT>(S, uc.u);
+            const Unit x = unit_of<FMT, TPU>(S, uc.u);
             bool ok = true;
             for (int ks = 0; ks < S.ks; ++ks, ++g) {
                 const uint32_t t0 = g * TPS;  // first weight tile of the stage
@@ -369,7 +384,7 @@ __global__ void __launch_bounds__(kThreadsBs, 1) k_bs_grouped(TcArgs a) {
         AccHalves ah;
         for (UnitCursor uc(a, total_units); uc.valid() && !*abortp; uc.advance()) {
             const TcSeg &S = uc.cur;
-            const Unit x = unit_of<FMT>(S, uc.u);
+            const Unit x = unit_of<FMT, TPU>(S, uc.u);
             const uint32_t mask = ah.mask_of(x.n), h0 = first_half(mask);
             const uint32_t acc = tbase + uint32_t(me) * kAccCols + 64u * h0;
             bool empty_ok = true;
@@ -385,8 +400,9 @@ __global__ void __launch_bounds__(kThreadsBs, 1) k_bs_grouped(TcArgs a) {
             for (int ks = 0; ks < S.ks; ++ks, ++g) {
                 const uint32_t t0 = g * TPS;
                 const int sa = int(t0 % SA), sb = int(g % kSB);
-                // PAIR: issuer 0 multiplies the gate tile (slot sa), issuer 1 the up tile.
+                // PAIR: issuer i multiplies the stage's tile i (gate / up, or row tile mt + i).
                 const int sam = PAIR ? int((t0 + uint32_t(me)) % SA) : sa;
+                const bool idle = MT && me == 1 && x.mt + 1 >= S.mts;  // no second tile
                 // The scale warps arrive only after every copy of the stage has landed.
                 if (!tc::mbar_wait(&sf_full[sa], (t0 / SA) & 1, abortp)) { ok = false; break; }
                 tc::fence_after_sync();
@@ -396,7 +412,7 @@ __global__ void __launch_bounds__(kThreadsBs, 1) k_bs_grouped(TcArgs a) {
                 const uint64_t adesc = tc::sdesc_sw128(sA), bdesc = tc::sdesc_sw128(sB);
                 constexpr int kSteps = PAIR ? 4 : kStepsPerIssuer;
 #pragma unroll
-                for (int k2 = 0; k2 < kSteps; ++k2) {
+                for (int k2 = 0; k2 < kSteps && !idle; ++k2) {
                     const int kk = PAIR ? k2 : me * kStepsPerIssuer + k2;
                     const bool accum = ks > 0 || k2 > 0;
                     if (FMT == URB_FMT_MXFP4) {
@@ -428,7 +444,7 @@ __global__ void __launch_bounds__(kThreadsBs, 1) k_bs_grouped(TcArgs a) {
         AccHalves ah;
         for (UnitCursor uc(a, total_units); uc.valid() && !*abortp; uc.advance()) {
             const TcSeg &S = uc.cur;
-            const Unit x = unit_of<FMT>(S, uc.u);
+            const Unit x = unit_of<FMT, TPU>(S, uc.u);
             const uint32_t mask = ah.mask_of(x.n), h0 = first_half(mask);
             if (!tc::mbar_wait(&acc_full[h0], ah.full[h0]++ & 1, abortp)) { fail(); break; }
             tc::fence_after_sync();
@@ -441,7 +457,33 @@ __global__ void __launch_bounds__(kThreadsBs, 1) k_bs_grouped(TcArgs a) {
                 for (int i = 0; i < kIssuers; ++i)
                     tc::tmem_ld16(tbase + lane_base + uint32_t(i) * kAccCols + 64u * h0 + 16 * c, v[i]);
                 tc::wait_ld();
-                if constexpr (PAIR) {
+                if constexpr (MT) {
+                    // Output rows of both row tiles (accumulator i: tile mt + i).
+#pragma unroll
+                    for (int s = 0; s < TPC; ++s) {
+                        const int t = TPC * c + s;
+                        if (t >= x.nt) continue;
+                        const int col = S.col_begin + tok0 + t;
+                        float *dst;
+                        if (a.out_ranks && col < a.routed_cols) {
+                            const int i = a.out_rows[col];
+                            dst = a.out_ranks[i / a.out_rank_rows] + size_t(i % a.out_rank_rows) * a.out_stride;
+                        } else {
+                            dst = a.out + size_t(a.out_ranks ? col - a.routed_cols : col) * a.out_stride;
+                        }
+#pragma unroll
+                        for (int i = 0; i < 2; ++i) {
+                            const int gr = (x.mt + i) * 128 + row;
+                            if (x.mt + i >= S.mts || gr >= S.rows) continue;
+                            float o = 0.0f;
+#pragma unroll
+                            for (int e = 0; e < TT; ++e) o += __uint_as_float(v[i][RT * s + e]);
+                            dst[S.out_off + gr] = o;
+                        }
+                    }
+                    continue;
+                }
+                if constexpr (GU) {
                     // h = silu(gate) * up of this lane's row for each token of the chunk.
 #pragma unroll
                     for (int s = 0; s < TPC; ++s) {
@@ -692,7 +734,7 @@ int launch_bs_t(Ctx *ctx, const TcArgs &a, int kind, cudaStream_t st) {
         prof_end(ctx, st);
         URB_CUDA(ctx, cudaGetLastError());
     }
-    auto k = a.pair ? k_bs_grouped<FMT, true> : k_bs_grouped<FMT, false>;
+    auto k = a.pair == 1 ? k_bs_grouped<FMT, 1> : (a.pair == 2 ? k_bs_grouped<FMT, 2> : k_bs_grouped<FMT, 0>);
     URB_CUDA(ctx, cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBs));
     prof_begin(ctx, kind, st);
     k<<<ctx->num_sms, kThreadsBs, kSmemBs, st>>>(a);

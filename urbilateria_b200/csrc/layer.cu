@@ -213,6 +213,7 @@ int moe_forward_device(Layer *L, const float *d_x, int T, float *d_out, MoeWork 
         bb.down_tc = reinterpret_cast<const uint8_t *const *>(tb + 8 * S);
         bb.has_shared = L->sg ? 1 : 0;
         bb.shared_tokens = T;
+        bb.pair_down = 1;
         if (L->sg) {
             bb.sh_gate_tc = L->sg->tc_tiles;
             bb.sh_up_tc = L->su->tc_tiles;
@@ -269,6 +270,7 @@ int moe_forward_device(Layer *L, const float *d_x, int T, float *d_out, MoeWork 
         da.src = w.h;
         da.src_stride = int(I);
         da.nrows = int(L->sg ? TK + T : TK);
+        da.pair = 2;  // neighbouring row tiles share each activation stage
         da.cols = int(I);
         da.ks = int(ks_dn);
         da.slots = w.bslots_dn;

@@ -242,6 +242,7 @@ __global__ void __launch_bounds__(1024) k_build_tc_segs(TcBuildArgs b) {
         const int mats = 1;  // groups per expert (gate/up: one paired group)
         const int ks = pass == 0 ? (b.hidden + sc - 1) / sc : (b.inter + sc - 1) / sc;
         const int mts = pass == 0 ? (b.inter + 127) / 128 : (b.hidden + 127) / 128;
+        const int mtu = pass == 1 && b.pair_down ? (mts + 1) / 2 : mts;  // tile units per group
         // Per thread: experts [e0, e1); groups, units and activation bytes.
         const int per_thr = (E + 1023) / 1024;
         const int e0 = min(E, tid * per_thr), e1 = min(E, e0 + per_thr);
@@ -251,7 +252,7 @@ __global__ void __launch_bounds__(1024) k_build_tc_segs(TcBuildArgs b) {
             const int c = b.counts[e];
             if (c <= 0) continue;
             ng += mats;
-            nu += mats * mts * ((c + bs_cap(b.fmt) - 1) / bs_cap(b.fmt));
+            nu += mats * mtu * ((c + bs_cap(b.fmt) - 1) / bs_cap(b.fmt));
             nb += bs_group_bytes(b.fmt, c, ks);
         }
         // Block-wide exclusive scans of (groups, units, bytes).
@@ -302,7 +303,7 @@ __global__ void __launch_bounds__(1024) k_build_tc_segs(TcBuildArgs b) {
             s.pad = 0;
             s_ub[gi] = ub;
             out[gi++] = s;
-            ub += mts * s.nsub;
+            ub += mtu * s.nsub;
         };
         for (int e = e0; e < e1; ++e) {
             const int c = b.counts[e];

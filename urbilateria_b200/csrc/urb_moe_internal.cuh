@@ -40,6 +40,7 @@ struct TcBuildArgs {
     const uint8_t *const *gate_tc, *const *up_tc, *const *down_tc;
     const uint8_t *sh_gate_tc, *sh_up_tc, *sh_down_tc;
     int has_shared, shared_tokens;  // shared-expert columns [tokens*top_k, +shared_tokens)
+    int pair_down;  // down-pass units pair neighbouring row tiles (TcArgs::pair == 2)
     int hidden, inter;
     TcSeg *gu, *dn;
     BsSlot *gu_slots, *dn_slots;  // [TK + T] activation slots of each column, per pass

@@ -71,8 +71,10 @@ struct TcArgs {
     int shared_row0, shared_rows;  // source rows [shared_row0, +shared_rows) feed the shared
                                    // expert's columns shared_col0 + (r - shared_row0)
     const BsSlot *slots;       // [activation columns]
-    // Gate/up pass: pair = 1, each group pairs the gate and up tiles of one expert and the
+    // pair = 1 (gate/up pass): each group pairs the gate and up tiles of one expert and the
     // epilogue writes h = silu(gate) * up rows to `out` (row = activation column).
+    // pair = 2 (down pass): each unit pairs neighbouring row tiles mt, mt + 1 of its matrix
+    // (the group's units then count ceil(mts / 2) tiles each).
     int pair;
     float *out;
     int out_stride;
