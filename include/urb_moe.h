@@ -222,6 +222,38 @@ URB_API int urb_moe_forward_routed_device(urb_ctx *ctx, urb_layer *layer, const 
                                           const float *d_route_weight, float *d_out,
                                           int32_t *d_status);
 
+/* ---- checkpoint numerics ---------------------------------------------------------------------- */
+
+/* Numerics of the routed forward.  URB_NUMERICS_GLM: the GLM composition above.
+ * URB_NUMERICS_DEEPSEEK_V4: DeepExpert::forward_with_mx_input and MoeWeights::forward
+ * (src/models/deepseek_v4/runtime.rs:3081-3104, :2500-2650) for MX experts: the input simulated
+ * as E4M3 per 128 values (src/math/mxfp.rs:91-115), gate / up outputs rounded to BF16, bounded
+ * SwiGLU with `swiglu_limit` (deepseek_v4/math.rs:518-549), the route weight applied to the
+ * activation before BF16 rounding, E4M3 simulation and the down projection (none for the shared
+ * expert), down outputs rounded to BF16, routed rows summed in f32 in ascending expert id, the
+ * shared row added last and the sum rounded to BF16.  Route weights must be finite and
+ * non-negative (URB_ERR_INVALID_ARGUMENT otherwise). */
+#define URB_NUMERICS_GLM 0
+#define URB_NUMERICS_DEEPSEEK_V4 1
+typedef struct urb_moe_numerics {
+    int32_t mode;
+    float swiglu_limit;
+} urb_moe_numerics;
+URB_API int urb_moe_forward_routed_ex(urb_ctx *ctx, urb_layer *layer, const float *x,
+                                      size_t tokens, const int32_t *route_expert,
+                                      const float *route_weight, const urb_moe_numerics *numerics,
+                                      float *out);
+URB_API int urb_moe_forward_routed_ex_device(urb_ctx *ctx, urb_layer *layer, const float *d_x,
+                                             size_t tokens, const int32_t *d_route_expert,
+                                             const float *d_route_weight,
+                                             const urb_moe_numerics *numerics, float *d_out,
+                                             int32_t *d_status);
+/* simulate_e4m3_activation (src/math/mxfp.rs:82-115) of n values in blocks of `block` (host
+ * pointers): each block scaled by the power of two at or above max(|v|, 1e-4) / 448 and
+ * round-tripped through E4M3FN. */
+URB_API int urb_simulate_e4m3_activation(urb_ctx *ctx, const float *x, size_t n, size_t block,
+                                         float *out);
+
 /* ---- expert parallelism across the GPUs of one node ------------------------------------------ */
 
 /* The layer forward of src/models/glm/runtime/moe.rs:138-176 split by experts over `world`

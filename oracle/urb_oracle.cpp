@@ -535,4 +535,109 @@ int urbo_moe_layer_forward(const urbo_moe_layer *L, const float *x, size_t token
     return URBO_OK;
 }
 
+// ---------------------------------------------------------------------------------------
+// Checkpoint numerics (DeepSeek-V4): MX activation simulation, BF16 boundaries, bounded SwiGLU.
+
+// src/math/mxfp.rs:300-319 power_of_two_ceiling: the exponent increment for interior mantissas;
+// the band near powers of two keeps the log2 / ceil / powf formula (glibc log2f and powf, the
+// libm Rust's f32::log2 / f32::powf call on linux-gnu).
+float urbo_power_of_two_ceiling(float value) {
+    const uint32_t bits = f32_bits(value);
+    const uint32_t exponent = bits & 0x7f800000u, mantissa = bits & 0x007fffffu;
+    if (mantissa == 0) return value;
+    const uint32_t band = 4096;
+    if (exponent == 0 || mantissa <= band || mantissa >= 0x007fffffu - band)
+        return std::pow(2.0f, std::ceil(std::log2(value)));
+    return bits_f32(exponent + 0x00800000u);
+}
+
+// src/math/mxfp.rs:91-115 simulate_e4m3_activation_in_place: per block, the scale is the power
+// of two at or above max(|v|, 1e-4 start of the fold) / 448; values round-trip through E4M3.
+int urbo_simulate_e4m3_activation(float *values, size_t n, size_t block) {
+    if (n == 0 || block == 0) return URBO_ERR_SHAPE;
+    if (any_nonfinite(values, n)) return URBO_ERR_NONFINITE;
+    for (size_t b = 0; b < n; b += block) {
+        const size_t e = std::min(n, b + block);
+        float amax = 1.0e-4f;
+        for (size_t i = b; i < e; ++i) amax = std::max(amax, std::fabs(values[i]));
+        const float scale = urbo_power_of_two_ceiling(amax / 448.0f);
+        for (size_t i = b; i < e; ++i) values[i] = e4m3(urbo_encode_e4m3fn(values[i] / scale)) * scale;
+    }
+    return URBO_OK;
+}
+
+// deepseek_v4/math.rs:90-101 round_to_bf16 (round to nearest even on the upper 16 bits).
+float urbo_round_bf16(float value) {
+    const uint32_t bits = f32_bits(value);
+    return bits_f32((bits + 0x7fffu + ((bits >> 16) & 1u)) & 0xffff0000u);
+}
+
+// deepseek_v4/math.rs:518-549 bounded SwiGLU of one element.
+float urbo_bounded_swiglu(float gate, float up, float limit) {
+    const float g = std::min(gate, limit);
+    const float u = std::min(std::max(up, -limit), limit);
+    return g / (1.0f + std::exp(-g)) * u;
+}
+
+// DeepExpert::forward_with_mx_input (deepseek_v4/runtime.rs:3081-3104) for MX weights:
+// gate / up on the simulated input with BF16 outputs, bounded SwiGLU, the route weight applied
+// to the activation (none for the shared expert), BF16, simulated again, down, BF16.
+static int deepseek_expert(const urbo_matrix *gate, const urbo_matrix *up, const urbo_matrix *down,
+                           const float *mx_x, const float *route_weight, float limit, float *y,
+                           int threads) {
+    const size_t I = gate->rows;
+    std::vector<float> g(I), u(I);
+    int rc = urbo_matvec_rows(gate, 0, I, mx_x, g.data(), threads);
+    if (rc) return rc;
+    rc = urbo_matvec_rows(up, 0, I, mx_x, u.data(), threads);
+    if (rc) return rc;
+    for (size_t i = 0; i < I; ++i) {
+        float a = urbo_bounded_swiglu(urbo_round_bf16(g[i]), urbo_round_bf16(u[i]), limit);
+        if (route_weight) a *= *route_weight;
+        g[i] = urbo_round_bf16(a);
+        if (!finite(g[i])) return URBO_ERR_NONFINITE;
+    }
+    rc = urbo_simulate_e4m3_activation(g.data(), I, 128);
+    if (rc) return rc;
+    rc = urbo_matvec_rows(down, 0, down->rows, g.data(), y, threads);
+    if (rc) return rc;
+    for (size_t h = 0; h < down->rows; ++h) y[h] = urbo_round_bf16(y[h]);
+    return URBO_OK;
+}
+
+// The DeepSeek-V4 MoE composition for given routes (deepseek_v4/runtime.rs:2500-2650 with
+// prepare_routes :2651-2700): the input simulated once (E4M3, blocks of 128), routed experts in
+// ascending expert id accumulated in f32, the shared expert added last, the sum cast to BF16.
+int urbo_moe_deepseek_forward(const urbo_moe_layer *L, const float *x, size_t tokens,
+                              const int32_t *route_expert, const float *route_weight, float limit,
+                              float *out, int threads) {
+    const size_t H = L->router->cols, k = L->top_k;
+    std::vector<float> mx(H), y(H), acc(H), shared(H);
+    std::vector<std::pair<int32_t, float>> order(k);
+    for (size_t t = 0; t < tokens; ++t) {
+        std::copy(x + t * H, x + (t + 1) * H, mx.begin());
+        int rc = urbo_simulate_e4m3_activation(mx.data(), H, 128);
+        if (rc) return rc;
+        for (size_t r = 0; r < k; ++r) order[r] = {route_expert[t * k + r], route_weight[t * k + r]};
+        std::stable_sort(order.begin(), order.end(),
+                         [](const std::pair<int32_t, float> &a, const std::pair<int32_t, float> &b) {
+                             return a.first < b.first;
+                         });
+        std::fill(acc.begin(), acc.end(), 0.0f);
+        for (size_t r = 0; r < k; ++r) {
+            const size_t e = size_t(order[r].first);
+            if (e >= L->experts) return URBO_ERR_SHAPE;
+            rc = deepseek_expert(&L->gate[e], &L->up[e], &L->down[e], mx.data(), &order[r].second,
+                                 limit, y.data(), threads);
+            if (rc) return rc;
+            for (size_t h = 0; h < H; ++h) acc[h] += y[h];
+        }
+        rc = deepseek_expert(L->shared_gate, L->shared_up, L->shared_down, mx.data(), nullptr,
+                             limit, shared.data(), threads);
+        if (rc) return rc;
+        for (size_t h = 0; h < H; ++h) out[t * H + h] = urbo_round_bf16(acc[h] + shared[h]);
+    }
+    return URBO_OK;
+}
+
 }  // extern "C"

@@ -105,6 +105,18 @@ int urbo_moe_layer_forward(const urbo_moe_layer *layer, const float *x, size_t t
                            float *out, int32_t *route_expert, float *route_weight,
                            float *route_score, float *router_logits, int threads);
 
+/* Checkpoint numerics (DeepSeek-V4).  src/math/mxfp.rs:91-115 and :300-319 (E4M3 activation
+ * simulation, power-of-two block scale), deepseek_v4/math.rs:90-101 (BF16 rounding) and
+ * :518-549 (bounded SwiGLU), and the MoE composition of deepseek_v4/runtime.rs:2500-2700 for
+ * given routes (ids / weights [tokens, top_k]; the layer's router and bias are unused). */
+float urbo_power_of_two_ceiling(float value);
+int urbo_simulate_e4m3_activation(float *values, size_t n, size_t block);
+float urbo_round_bf16(float value);
+float urbo_bounded_swiglu(float gate, float up, float limit);
+int urbo_moe_deepseek_forward(const urbo_moe_layer *layer, const float *x, size_t tokens,
+                              const int32_t *route_expert, const float *route_weight,
+                              float limit, float *out, int threads);
+
 #ifdef __cplusplus
 }
 #endif

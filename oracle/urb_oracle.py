@@ -100,6 +100,17 @@ def lib():
         _lib.urbo_moe_layer_forward.argtypes = [
             ctypes.POINTER(OracleMoeLayer), ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p,
             ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int]
+        _lib.urbo_power_of_two_ceiling.restype = ctypes.c_float
+        _lib.urbo_power_of_two_ceiling.argtypes = [ctypes.c_float]
+        _lib.urbo_simulate_e4m3_activation.argtypes = [ctypes.c_void_p, ctypes.c_size_t,
+                                                       ctypes.c_size_t]
+        _lib.urbo_round_bf16.restype = ctypes.c_float
+        _lib.urbo_round_bf16.argtypes = [ctypes.c_float]
+        _lib.urbo_bounded_swiglu.restype = ctypes.c_float
+        _lib.urbo_bounded_swiglu.argtypes = [ctypes.c_float, ctypes.c_float, ctypes.c_float]
+        _lib.urbo_moe_deepseek_forward.argtypes = [
+            ctypes.POINTER(OracleMoeLayer), ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p,
+            ctypes.c_void_p, ctypes.c_float, ctypes.c_void_p, ctypes.c_int]
     return _lib
 
 
@@ -243,3 +254,39 @@ class MoeLayer:
                                             _ptr(w), _ptr(s), _ptr(logits),
                                             threads or default_threads()))
         return out, e, w, s, logits
+
+
+# ---- checkpoint numerics (DeepSeek-V4) -------------------------------------------------------
+
+def power_of_two_ceiling(value: float) -> float:
+    """src/math/mxfp.rs:300-319."""
+    return lib().urbo_power_of_two_ceiling(value)
+
+
+def simulate_e4m3_activation(values, block: int) -> np.ndarray:
+    """src/math/mxfp.rs:91-115 (E4M3 round trip with a power-of-two scale per block)."""
+    v = np.array(values, dtype=np.float32).ravel()
+    _check(lib().urbo_simulate_e4m3_activation(_ptr(v), v.size, block))
+    return v
+
+
+def round_bf16(value: float) -> float:
+    """deepseek_v4/math.rs:90-101 (finite inputs)."""
+    return lib().urbo_round_bf16(value)
+
+
+def bounded_swiglu(gate: float, up: float, limit: float) -> float:
+    """deepseek_v4/math.rs:518-549, one element."""
+    return lib().urbo_bounded_swiglu(gate, up, limit)
+
+
+def moe_deepseek_forward(layer: "MoeLayer", x, expert_ids, weights, limit: float, threads=None):
+    """The DeepSeek-V4 MoE composition for given routes (deepseek_v4/runtime.rs:2500-2700)."""
+    x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1, layer.hidden)
+    t = x.shape[0]
+    ids = np.ascontiguousarray(expert_ids, dtype=np.int32).reshape(t, layer.top_k)
+    w = np.ascontiguousarray(weights, dtype=np.float32).reshape(t, layer.top_k)
+    out = np.empty_like(x)
+    _check(lib().urbo_moe_deepseek_forward(ctypes.byref(layer.c), _ptr(x), t, _ptr(ids), _ptr(w),
+                                           limit, _ptr(out), threads or default_threads()))
+    return out

@@ -315,3 +315,40 @@ def test_grouping_is_experts_then_tokens_ascending(oracle):
     assert list(ps) == [i % 6 for i in order]
     assert list(counts) == list(np.bincount(ids.ravel(), minlength=37))
     assert offsets[-1] == ids.size
+
+
+# ---- checkpoint numerics (DeepSeek-V4), pinned by the reference's own tests ----------------
+
+def test_e4m3_activation_simulation_golden(oracle):
+    # src/math/mxfp.rs:2885-2889 (activation_simulation_uses_power_of_two_blocks).
+    v = oracle.simulate_e4m3_activation([448.0, 0.1, 896.0, -896.0], 2)
+    assert v[0] == 448.0 and v[2] == 896.0 and v[3] == -896.0
+
+
+def test_power_of_two_ceiling_matches_float_formula(oracle):
+    # src/math/mxfp.rs:2893-2917: bitwise equal to 2^ceil(log2(v)) (glibc log2f / powf) on the
+    # bands around powers of two and on seeded interior mantissas, for every exponent.
+    rng = np.random.default_rng(7)
+    for exponent in range(0, 255, 3):
+        mants = list(range(0, 8193, 97)) + list(range(0x7FFFFF - 8192, 0x800000, 97))
+        mants += [int(m) for m in rng.integers(0, 0x800000, size=64)]
+        for m in mants:
+            v = np.uint32((exponent << 23) | m).view(np.float32)
+            if not np.isfinite(v) or v <= 0:
+                continue
+            got = np.float32(oracle.power_of_two_ceiling(float(v)))
+            ref = np.float32(2.0) ** np.ceil(np.log2(v))
+            assert got == ref, (exponent, m, got, ref)
+
+
+def test_round_bf16_and_bounded_swiglu_golden(oracle):
+    # deepseek_v4/math.rs:788-798 (bounded_swiglu_clamps_the_two_branches_asymmetrically).
+    a = oracle.bounded_swiglu(20.0, 20.0, 10.0)
+    assert abs(a - 10.0 / (1.0 + math.exp(-10.0)) * 10.0) < 1e-5
+    b = oracle.bounded_swiglu(-20.0, -20.0, 10.0)
+    assert 0.0 < b < 1e-6
+    # Round to nearest even on the upper half: 1 + 2^-8 is a tie (stays 1), 1 + 3*2^-8 rounds up.
+    assert oracle.round_bf16(1.0 + 2.0 ** -8) == 1.0
+    assert oracle.round_bf16(1.0 + 3 * 2.0 ** -8) == 1.0 + 2.0 ** -6
+    assert oracle.round_bf16(-2.5) == -2.5
+

@@ -21,7 +21,7 @@ from .native import MoeGeometry as _CGeometry
 __all__ = [
     "UrbError", "MxError", "Context", "MxFp4Matrix", "MxFp8Matrix", "Bf16Matrix", "DenseMatrix",
     "GatedMlp", "RouteChoice", "MoeGeometry", "route_noaux_tc", "route_softmax_top_k",
-    "group_routes", "RuntimeMoeLayer", "default_context",
+    "group_routes", "RuntimeMoeLayer", "default_context", "simulate_e4m3_activation",
 ]
 
 
@@ -322,6 +322,16 @@ def route_softmax_top_k(logits, top_k: int, ctx: Optional[Context] = None):
     return ids, w
 
 
+def simulate_e4m3_activation(values, block_size: int, ctx: Optional[Context] = None) -> np.ndarray:
+    """simulate_e4m3_activation (src/math/mxfp.rs:82-115) on the device."""
+    ctx = ctx or default_context()
+    v = np.ascontiguousarray(values, dtype=np.float32).ravel()
+    out = np.empty_like(v)
+    ctx.check(ctx.lib.urb_simulate_e4m3_activation(ctx.h, _ptr(v) if v.size else None, v.size,
+                                                   block_size, _ptr(out) if v.size else None))
+    return out
+
+
 def group_routes(expert_ids, experts: int, ctx: Optional[Context] = None):
     """Ragged grouping (src/models/qwen3_6/runtime.rs:1083-1132): experts ascending, tokens
     ascending.  Returns (counts, offsets, perm_token, perm_slot)."""
@@ -406,16 +416,21 @@ class RuntimeMoeLayer:
         extra["selection_score"] = s
         return out, ids, w, extra
 
-    def forward_routed(self, x, tokens: int, expert_ids, weights) -> np.ndarray:
+    def forward_routed(self, x, tokens: int, expert_ids, weights, numerics: str = "glm",
+                       swiglu_limit: float = 0.0) -> np.ndarray:
         """Experts half of the forward for caller-chosen routes ([tokens, top_k] ids and
-        weights, e.g. from route_softmax_top_k): grouped SwiGLU experts + f64 combine."""
+        weights, e.g. from route_softmax_top_k): grouped SwiGLU experts + combine.  numerics
+        "glm" (f64 combine in route order) or "deepseek_v4" (urb_moe_numerics)."""
         K = self.geometry.top_k
         x = np.ascontiguousarray(x, dtype=np.float32).ravel()
         ids = np.ascontiguousarray(expert_ids, dtype=np.int32).reshape(tokens, K)
         w = np.ascontiguousarray(weights, dtype=np.float32).reshape(tokens, K)
         out = np.empty((tokens, self.hidden_size()), dtype=np.float32)
-        self.ctx.check(self.ctx.lib.urb_moe_forward_routed(
-            self.ctx.h, self.h, _ptr(x), tokens, _ptr(ids), _ptr(w), _ptr(out)))
+        mode = {"glm": native.NUMERICS_GLM, "deepseek_v4": native.NUMERICS_DEEPSEEK_V4}[numerics]
+        num = native.Numerics(mode, swiglu_limit)
+        self.ctx.check(self.ctx.lib.urb_moe_forward_routed_ex(
+            self.ctx.h, self.h, _ptr(x), tokens, _ptr(ids), _ptr(w), ctypes.byref(num),
+            _ptr(out)))
         return out
 
     def forward(self, x):

@@ -34,6 +34,7 @@
 // source.
 // Units of N <= 64 MMA rows alternate between two 64-column halves of the accumulators, so the
 // epilogue of one unit overlaps the MMAs of the next.
+#include "numerics.cuh"
 #include "tc_common.cuh"
 #include "urb_internal.cuh"
 #include "urb_tc.cuh"
@@ -478,6 +479,7 @@ __global__ void __launch_bounds__(kThreadsBs, 1) k_bs_grouped(TcArgs a) {
                             float o = 0.0f;
 #pragma unroll
                             for (int e = 0; e < TT; ++e) o += __uint_as_float(v[i][RT * s + e]);
+                            if (a.variant == 1) o = num_round_bf16(o);
                             dst[S.out_off + gr] = o;
                         }
                     }
@@ -495,7 +497,16 @@ __global__ void __launch_bounds__(kThreadsBs, 1) k_bs_grouped(TcArgs a) {
                             gv += __uint_as_float(v[0][RT * s + e]);
                             uv += __uint_as_float(v[1][RT * s + e]);
                         }
-                        a.out[size_t(S.col_begin + tok0 + t) * a.out_stride + grow] = silu_f(gv) * uv;
+                        const int col = S.col_begin + tok0 + t;
+                        float h;
+                        if (a.variant == 1) {
+                            h = num_bounded_swiglu(num_round_bf16(gv), num_round_bf16(uv), a.limit);
+                            h = num_round_bf16(__fmul_rn(h, a.col_w[col]));
+                            if (!isfinite(h)) set_status(a.status, URB_ERR_NONFINITE);
+                        } else {
+                            h = silu_f(gv) * uv;
+                        }
+                        a.out[size_t(col) * a.out_stride + grow] = h;
                     }
                     continue;
                 }
@@ -519,6 +530,7 @@ __global__ void __launch_bounds__(kThreadsBs, 1) k_bs_grouped(TcArgs a) {
                         } else {
                             dst = a.out + size_t(a.out_ranks ? col - a.routed_cols : col) * a.out_stride;
                         }
+                        if (a.variant == 1) o = num_round_bf16(o);
                         dst[S.out_off + grow] = o;
                     }
                 }
@@ -644,6 +656,18 @@ __global__ void __launch_bounds__(256) k_bs_prep(TcArgs a) {
     if (!valid || bad) {
 #pragma unroll
         for (int i = 0; i < 8; ++i) r[i] = 0.0f;
+    }
+    if (a.sim128) {
+        // E4M3 activation simulation per 128 columns: four 32-column blocks, i.e. 16 lanes
+        // (a row's blocks start on a multiple of four, so the groups never straddle rows).
+        float m = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) m = fmaxf(m, fabsf(r[i]));
+#pragma unroll
+        for (int o = 1; o < 16; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        const float scale = num_e4m3_scale(m);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) r[i] = num_e4m3_sim(r[i], scale);
     }
     uint32_t q[TT][QW];
     int sb[TT];

@@ -69,7 +69,7 @@ int route_device(Layer *L, const float *d_x, int T, const MoeWork &w, int32_t *d
 
 int moe_forward_device(Layer *L, const float *d_x, int T, float *d_out, MoeWork *wout,
                        int32_t *d_status, cudaStream_t st, const int32_t *d_ids_in,
-                       const float *d_w_in) {
+                       const float *d_w_in, const Numerics *num) {
     Ctx *ctx = L->ctx;
     const size_t E = L->experts, K = L->geo.top_k, H = L->hidden, I = L->inter;
     const size_t TK = size_t(T) * K, cols = TK + T;
@@ -102,6 +102,11 @@ int moe_forward_device(Layer *L, const float *d_x, int T, float *d_out, MoeWork 
     w.h = cv.take<float>(cols * I);
     w.y = cv.take<float>(cols * H);
     w.lofree = cv.take<int32_t>(1);
+    w.col_w = cv.take<float>(cols);
+    const bool deepseek = num && num->mode == URB_NUMERICS_DEEPSEEK_V4;
+    if (deepseek && (!L->use_tc || !d_ids_in))
+        return set_error(ctx, URB_ERR_UNSUPPORTED,
+                         "DeepSeek-V4 numerics run on the tensor-core passes with caller routes");
     const size_t ngrp_gu = 2 * std::min(TK, E) + 2, ngrp_dn = std::min(TK, E) + 1;
     const size_t sc = size_t(bs_stage_cols(L->fmt));
     const size_t ks_gu = div_ceil(H, sc), ks_dn = div_ceil(I, sc);
@@ -120,7 +125,7 @@ int moe_forward_device(Layer *L, const float *d_x, int T, float *d_out, MoeWork 
     if (cv.off > ctx->ws_size) {
         // Grow to the exact size of this forward (nothing has been enqueued yet) and restart.
         if (!workspace(ctx, cv.off, &rc)) return rc;
-        return moe_forward_device(L, d_x, T, d_out, wout, d_status, st, d_ids_in, d_w_in);
+        return moe_forward_device(L, d_x, T, d_out, wout, d_status, st, d_ids_in, d_w_in, num);
     }
     if (!d_status) {
         // No status word from the caller: the stages still short-circuit on a private one.
@@ -195,6 +200,10 @@ int moe_forward_device(Layer *L, const float *d_x, int T, float *d_out, MoeWork 
         p.segs_gu = nullptr;
         p.col_src = nullptr;
     }
+    if (deepseek) {  // route weights move to the columns (applied before the down projection)
+        p.route_w = w.w;
+        p.col_w = w.col_w;
+    }
     prof_begin(ctx, URB_K_PERMUTE, st);
     rc = launch_permute(ctx, p, st);
     prof_end(ctx, st);
@@ -254,6 +263,12 @@ int moe_forward_device(Layer *L, const float *d_x, int T, float *d_out, MoeWork 
         ga.shared_rows = T;
         ga.slots = w.bslots_gu;
         ga.pair = 1;  // gate and up tiles of an expert together; the epilogue writes h
+        if (deepseek) {
+            ga.variant = 1;
+            ga.sim128 = 1;
+            ga.limit = num->limit;
+            ga.col_w = w.col_w;
+        }
         ga.out = w.h;
         ga.out_stride = int(I);
         ga.status = d_status;
@@ -271,6 +286,10 @@ int moe_forward_device(Layer *L, const float *d_x, int T, float *d_out, MoeWork 
         da.src_stride = int(I);
         da.nrows = int(L->sg ? TK + T : TK);
         da.pair = 2;  // neighbouring row tiles share each activation stage
+        if (deepseek) {
+            da.variant = 1;
+            da.sim128 = 1;
+        }
         da.cols = int(I);
         da.ks = int(ks_dn);
         da.slots = w.bslots_dn;
@@ -281,8 +300,12 @@ int moe_forward_device(Layer *L, const float *d_x, int T, float *d_out, MoeWork 
         if (rc) return rc;
 
         prof_begin(ctx, URB_K_COMBINE, st);
-        rc = launch_combine(ctx, w.y, L->sg ? w.y + TK * H : nullptr, w.w, w.inv, T, int(K),
-                            int(H), d_out, st, d_status);
+        if (deepseek)
+            rc = launch_combine_deepseek(ctx, w.y, L->sg ? w.y + TK * H : nullptr, w.ids, w.inv, T,
+                                         int(K), int(H), d_out, st, d_status);
+        else
+            rc = launch_combine(ctx, w.y, L->sg ? w.y + TK * H : nullptr, w.w, w.inv, T, int(K),
+                                int(H), d_out, st, d_status);
         prof_end(ctx, st);
         if (rc) return rc;
         if (wout) *wout = w;
@@ -604,6 +627,37 @@ int urb_moe_forward(urb_ctx *ctx, urb_layer *L, const float *x, size_t tokens, f
     return URB_OK;
 }
 
+static int numerics_of(urb_ctx *ctx, const urb_moe_numerics *n, Numerics *out) {
+    if (!n) return URB_OK;
+    if (n->mode == URB_NUMERICS_GLM) return URB_OK;
+    if (n->mode != URB_NUMERICS_DEEPSEEK_V4)
+        return set_error(ctx, URB_ERR_INVALID_ARGUMENT, "unknown numerics mode");
+    // validate_positive("SwiGLU limit") of deepseek_v4/math.rs:531.
+    if (!std::isfinite(n->swiglu_limit) || n->swiglu_limit <= 0.0f)
+        return set_error(ctx, URB_ERR_INVALID_ARGUMENT, "SwiGLU limit must be finite and positive");
+    out->mode = n->mode;
+    out->limit = n->swiglu_limit;
+    return URB_OK;
+}
+
+int urb_moe_forward_routed_ex_device(urb_ctx *ctx, urb_layer *L, const float *d_x,
+                                     size_t tokens, const int32_t *d_route_expert,
+                                     const float *d_route_weight, const urb_moe_numerics *numerics,
+                                     float *d_out, int32_t *d_status) {
+    if (!ctx || !L || !d_x || !d_out || !d_route_expert || !d_route_weight)
+        return URB_ERR_INVALID_ARGUMENT;
+    if (L->e_count != L->experts)
+        return set_error(ctx, URB_ERR_UNSUPPORTED, "an expert shard runs through urb_ep_forward");
+    std::lock_guard<std::recursive_mutex> lk(ctx->mu);
+    cudaSetDevice(ctx->device);
+    Numerics num;
+    int rc = numerics_of(ctx, numerics, &num);
+    if (rc) return rc;
+    if (tokens == 0) return URB_OK;
+    return moe_forward_device(L, d_x, int(tokens), d_out, nullptr, d_status, ctx->stream,
+                              d_route_expert, d_route_weight, &num);
+}
+
 int urb_moe_forward_routed_device(urb_ctx *ctx, urb_layer *L, const float *d_x, size_t tokens,
                                   const int32_t *d_route_expert, const float *d_route_weight,
                                   float *d_out, int32_t *d_status) {
@@ -618,18 +672,27 @@ int urb_moe_forward_routed_device(urb_ctx *ctx, urb_layer *L, const float *d_x, 
                               d_route_expert, d_route_weight);
 }
 
-int urb_moe_forward_routed(urb_ctx *ctx, urb_layer *L, const float *x, size_t tokens,
-                           const int32_t *route_expert, const float *route_weight, float *out) {
+int urb_moe_forward_routed_ex(urb_ctx *ctx, urb_layer *L, const float *x, size_t tokens,
+                              const int32_t *route_expert, const float *route_weight,
+                              const urb_moe_numerics *numerics, float *out) {
     if (!ctx || !L || !x || !out || !route_expert || !route_weight) return URB_ERR_INVALID_ARGUMENT;
     if (L->e_count != L->experts)
         return set_error(ctx, URB_ERR_UNSUPPORTED, "an expert shard runs through urb_ep_forward");
     std::lock_guard<std::recursive_mutex> lk(ctx->mu);
     cudaSetDevice(ctx->device);
+    Numerics num;
+    int rc0 = numerics_of(ctx, numerics, &num);
+    if (rc0) return rc0;
     if (tokens == 0) return URB_OK;
     const size_t H = L->hidden, K = L->geo.top_k, TK = tokens * K;
     for (size_t i = 0; i < TK; ++i)
         if (route_expert[i] < 0 || size_t(route_expert[i]) >= L->experts)
             return set_error(ctx, URB_ERR_SHAPE, "route expert id out of range");
+    if (num.mode == URB_NUMERICS_DEEPSEEK_V4)
+        for (size_t i = 0; i < TK; ++i)  // deepseek_v4/runtime.rs:3091-3095
+            if (!std::isfinite(route_weight[i]) || route_weight[i] < 0.0f)
+                return set_error(ctx, URB_ERR_INVALID_ARGUMENT,
+                                 "routed expert weight must be finite and non-negative");
     cudaStream_t st = ctx->stream;
     uint8_t *d_io = nullptr;
     const size_t bytes = 2 * tokens * H * 4 + 2 * TK * 4;
@@ -641,7 +704,8 @@ int urb_moe_forward_routed(urb_ctx *ctx, urb_layer *L, const float *x, size_t to
     URB_CUDA(ctx, cudaMemcpyAsync(d_x, x, tokens * H * 4, cudaMemcpyDefault, st));
     URB_CUDA(ctx, cudaMemcpyAsync(d_ids, route_expert, TK * 4, cudaMemcpyDefault, st));
     URB_CUDA(ctx, cudaMemcpyAsync(d_w, route_weight, TK * 4, cudaMemcpyDefault, st));
-    int rc = moe_forward_device(L, d_x, int(tokens), d_out, nullptr, ctx->d_status, st, d_ids, d_w);
+    int rc = moe_forward_device(L, d_x, int(tokens), d_out, nullptr, ctx->d_status, st, d_ids, d_w,
+                                &num);
     if (rc) {
         cudaFreeAsync(d_io, st);
         return rc;
@@ -653,6 +717,11 @@ int urb_moe_forward_routed(urb_ctx *ctx, urb_layer *L, const float *x, size_t to
     URB_CUDA(ctx, cudaStreamSynchronize(st));
     if (status) return set_error(ctx, status, "MoE forward rejected its input");
     return URB_OK;
+}
+
+int urb_moe_forward_routed(urb_ctx *ctx, urb_layer *L, const float *x, size_t tokens,
+                           const int32_t *route_expert, const float *route_weight, float *out) {
+    return urb_moe_forward_routed_ex(ctx, L, x, tokens, route_expert, route_weight, nullptr, out);
 }
 
 int urb_gated_mlp_forward(urb_ctx *ctx, const urb_mat *g, const urb_mat *u, const urb_mat *d,

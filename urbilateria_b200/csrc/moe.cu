@@ -90,6 +90,7 @@ __global__ void __launch_bounds__(kPermThreads) k_permute(PermArgs p) {
             p.perm_slot[pos] = i % p.top_k;
             p.inv[i] = pos;
             if (p.route_of) p.route_of[pos] = i;
+            if (p.col_w) p.col_w[pos] = p.route_w[i];
         } else if (i < TK) {
             p.inv[i] = -1;  // foreign route
         }
@@ -176,6 +177,8 @@ __global__ void __launch_bounds__(kPermThreads) k_permute(PermArgs p) {
             p.col_src[c] = c < TK ? p.perm_token[c] : c - TK;
             p.maxexp[c] = -1000;
         }
+    if (p.col_w)
+        for (int t = tid; t < p.tokens; t += kPermThreads) p.col_w[TK + t] = 1.0f;  // shared
     for (int e = tid; e < E; e += kPermThreads) {
         if (p.counts) p.counts[e] = cnt[e];
         if (p.offsets) p.offsets[e] = off[e];
@@ -198,6 +201,35 @@ __global__ void k_combine(const float *y, const float *shared_y, const float *w,
         acc += double(w[t * top_k + k]) * double(y[size_t(pos) * hidden + h]);
     }
     out[size_t(t) * hidden + h] = float(acc);
+}
+
+// DeepSeek-V4 combine: f32 sum of a token's routed rows in ascending expert id (ties keep the
+// route order), the shared row added last, then round to BF16 (deepseek_v4/runtime.rs:2639-2647;
+// the route weights were applied before the down projection).
+__global__ void k_combine_deepseek(const float *y, const float *shared_y, const int32_t *ids,
+                                   const int32_t *inv, int tokens, int top_k, int hidden,
+                                   float *out, int32_t *status) {
+    if (*status) return;
+    const int t = blockIdx.y;
+    const int h = blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= tokens || h >= hidden) return;
+    int order[16];
+    for (int k = 0; k < top_k; ++k) {  // stable insertion by expert id
+        const int id = ids[t * top_k + k];
+        int j = k;
+        while (j > 0 && ids[t * top_k + order[j - 1]] > id) { order[j] = order[j - 1]; --j; }
+        order[j] = k;
+    }
+    float acc = 0.0f;
+    for (int j = 0; j < top_k; ++j) {
+        const int pos = inv[t * top_k + order[j]];
+        acc = __fadd_rn(acc, y[size_t(pos) * hidden + h]);
+    }
+    if (shared_y) acc = __fadd_rn(acc, shared_y[size_t(t) * hidden + h]);
+    const uint32_t b = __float_as_uint(acc);
+    const float r = __uint_as_float((b + 0x7fffu + ((b >> 16) & 1u)) & 0xffff0000u);
+    if (!isfinite(r)) atomicCAS(status, 0, int32_t(URB_ERR_NONFINITE));
+    out[size_t(t) * hidden + h] = r;
 }
 
 // Groups of the tensor-core passes (single CTA).  Gate/up pass: per routed expert with tokens
@@ -370,6 +402,18 @@ int launch_permute(Ctx *ctx, const PermArgs &p, cudaStream_t st) {
     if (smem > 200 * 1024) return set_error(ctx, URB_ERR_UNSUPPORTED, "too many experts for the grouping kernel");
     URB_CUDA(ctx, cudaFuncSetAttribute(k_permute, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
     k_permute<<<1, kPermThreads, smem, st>>>(p);
+    URB_CUDA(ctx, cudaGetLastError());
+    return URB_OK;
+}
+
+int launch_combine_deepseek(Ctx *ctx, const float *y, const float *shared_y, const int32_t *ids,
+                            const int32_t *inv, int tokens, int top_k, int hidden, float *out,
+                            cudaStream_t st, int32_t *status) {
+    if (tokens <= 0) return URB_OK;
+    if (top_k > 16) return set_error(ctx, URB_ERR_UNSUPPORTED, "DeepSeek combine: top_k > 16");
+    dim3 grid(unsigned((hidden + 255) / 256), unsigned(tokens));
+    k_combine_deepseek<<<grid, 256, 0, st>>>(y, shared_y, ids, inv, tokens, top_k, hidden, out,
+                                             status);
     URB_CUDA(ctx, cudaGetLastError());
     return URB_OK;
 }

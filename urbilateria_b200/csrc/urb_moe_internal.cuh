@@ -28,6 +28,8 @@ struct PermArgs {
     const int *lofree;    // optional: when *lofree, segments hold 2*cap tokens
     int allow_foreign;    // ids == -1 are routes held by another rank: not grouped, inv = -1
     int32_t *route_of;    // optional [tokens*top_k]: route index of each grouped position
+    const float *route_w; // optional [tokens*top_k] route weights, with col_w:
+    float *col_w;         // [tokens*top_k + tokens] weight of each activation column (shared: 1)
 };
 
 int launch_permute(Ctx *ctx, const PermArgs &p, cudaStream_t st);
@@ -52,6 +54,16 @@ int launch_build_tc_segs(Ctx *ctx, const TcBuildArgs &b, cudaStream_t st);
 int launch_combine(Ctx *ctx, const float *y, const float *shared_y, const float *w,
                    const int32_t *inv, int tokens, int top_k, int hidden, float *out,
                    cudaStream_t st, const int32_t *status = nullptr);
+// DeepSeek-V4 combine (deepseek_v4/runtime.rs:2500-2650): per token, f32 sum of the routed rows
+// (route weights already applied) in ascending expert id, plus the shared row, cast to BF16.
+int launch_combine_deepseek(Ctx *ctx, const float *y, const float *shared_y, const int32_t *ids,
+                            const int32_t *inv, int tokens, int top_k, int hidden, float *out,
+                            cudaStream_t st, int32_t *status);
+// Checkpoint numerics of a forward (urb_moe_numerics).
+struct Numerics {
+    int mode = 0;        // URB_NUMERICS_*
+    float limit = 0.0f;  // bounded-SwiGLU limit (DeepSeek-V4)
+};
 
 struct Layer {
     Ctx *ctx = nullptr;
@@ -94,13 +106,14 @@ struct MoeWork {
     int *units_gu, *units_dn;
     int *tscalars;
     uint8_t *bbuf_gu, *bbuf_dn;
+    float *col_w;         // [TK+T] route weight of each activation column (DeepSeek-V4 numerics)
 };
 
 // d_ids_in / d_w_in ([tokens, top_k], optional): routes chosen by the caller; the router is
 // skipped and these are grouped and combined instead.
 int moe_forward_device(Layer *L, const float *d_x, int tokens, float *d_out, MoeWork *work_out,
                        int32_t *d_status, cudaStream_t st, const int32_t *d_ids_in = nullptr,
-                       const float *d_w_in = nullptr);
+                       const float *d_w_in = nullptr, const Numerics *num = nullptr);
 // Exact router logits and route_noaux_tc of `tokens` rows into w.logits / x64 / gate / sel /
 // ids / w / score.
 int route_device(Layer *L, const float *d_x, int tokens, const MoeWork &w, int32_t *d_status,

@@ -76,6 +76,13 @@ struct TcArgs {
     // pair = 2 (down pass): each unit pairs neighbouring row tiles mt, mt + 1 of its matrix
     // (the group's units then count ceil(mts / 2) tiles each).
     int pair;
+    // Checkpoint numerics (0: GLM f32 path).  1 (DeepSeek-V4): the prep simulates E4M3 per 128
+    // columns (sim128) before building terms; the gate/up epilogue rounds gate and up to BF16,
+    // applies bounded SwiGLU (limit), multiplies by the column's route weight (col_w) and
+    // rounds h to BF16; the down epilogue rounds its outputs to BF16.
+    int variant, sim128;
+    float limit;
+    const float *col_w;
     float *out;
     int out_stride;
     int32_t *status;

@@ -42,6 +42,14 @@ STATUS_NAMES = {
 }
 
 
+NUMERICS_GLM, NUMERICS_DEEPSEEK_V4 = 0, 1
+
+
+class Numerics(ctypes.Structure):
+    """urb_moe_numerics."""
+    _fields_ = [("mode", ctypes.c_int32), ("swiglu_limit", ctypes.c_float)]
+
+
 class MoeGeometry(ctypes.Structure):
     """urb_moe_geometry, the MoeGeometry of src/models/glm/moe_geometry.rs:1-9."""
     _fields_ = [("top_k", ctypes.c_uint32), ("n_group", ctypes.c_uint32),
@@ -86,6 +94,9 @@ SIGNATURES = [
     ("urb_moe_forward_device", I32, [P, P, P, SZ, P, P, P, P]),
     ("urb_moe_forward_routed", I32, [P, P, P, SZ, P, P, P]),
     ("urb_moe_forward_routed_device", I32, [P, P, P, SZ, P, P, P, P]),
+    ("urb_moe_forward_routed_ex", I32, [P, P, P, SZ, P, P, P, P]),
+    ("urb_moe_forward_routed_ex_device", I32, [P, P, P, SZ, P, P, P, P, P]),
+    ("urb_simulate_e4m3_activation", I32, [P, P, SZ, SZ, P]),
     ("urb_moe_layer_create_sharded", I32, [P, P, P, SZ, SZ, SZ, P, P, P, P, P, P,
                                            ctypes.POINTER(MoeGeometry), PP]),
     ("urb_ep_create", I32, [P, P, I32, I32, SZ, U32, PP]),
