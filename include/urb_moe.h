@@ -248,6 +248,25 @@ URB_API int urb_moe_forward_routed_ex_device(urb_ctx *ctx, urb_layer *layer, con
                                              const float *d_route_weight,
                                              const urb_moe_numerics *numerics, float *d_out,
                                              int32_t *d_status);
+/* The whole layer forward with checkpoint numerics.  URB_NUMERICS_GLM: urb_moe_forward.
+ * URB_NUMERICS_DEEPSEEK_V4: MoeWeights::forward (src/models/deepseek_v4/runtime.rs:2484-2700):
+ * exact router logits, route_sqrt_softplus (deepseek_v4/math.rs:451-516) with the layer's
+ * correction bias and routed_scaling_factor, or the token's fixed experts `hash_experts`
+ * ([tokens, top_k], NULL for learned routing; the weights still come from the scores), then the
+ * routed experts with the DeepSeek-V4 numerics above.  Routes out in selection order (NULL to
+ * skip). */
+URB_API int urb_moe_forward_ex(urb_ctx *ctx, urb_layer *layer, const float *x, size_t tokens,
+                               const urb_moe_numerics *numerics, const int32_t *hash_experts,
+                               float *out, int32_t *route_expert, float *route_weight);
+/* route_sqrt_softplus (src/models/deepseek_v4/math.rs:451-516) for `tokens` rows of logits:
+ * score = sqrt(softplus(logit)) with libm expf / log1pf, selection = score + bias (bias NULL:
+ * none), top_k by selection (lower id wins ties) or the given hash experts, weight = score /
+ * sum(chosen scores) * routed_scaling_factor.  Outputs [tokens, top_k]; out_score (the
+ * selection score) may be NULL. */
+URB_API int urb_route_sqrt_softplus(urb_ctx *ctx, const float *logits, const float *bias,
+                                    size_t tokens, size_t experts, const int32_t *hash_experts,
+                                    uint32_t top_k, float routed_scaling_factor,
+                                    int32_t *out_expert, float *out_weight, float *out_score);
 /* simulate_e4m3_activation (src/math/mxfp.rs:82-115) of n values in blocks of `block` (host
  * pointers): each block scaled by the power of two at or above max(|v|, 1e-4) / 448 and
  * round-tripped through E4M3FN. */

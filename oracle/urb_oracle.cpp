@@ -640,4 +640,66 @@ int urbo_moe_deepseek_forward(const urbo_moe_layer *L, const float *x, size_t to
     return URBO_OK;
 }
 
+// deepseek_v4/math.rs:604-610 softplus (libm expf / log1pf, as Rust's f32::exp / ln_1p).
+static float softplus(float v) {
+    return v > 0.0f ? v + std::log1p(std::exp(-v)) : std::log1p(std::exp(v));
+}
+
+// deepseek_v4/math.rs:451-516 route_sqrt_softplus for one row of logits.
+int urbo_route_sqrt_softplus(const float *logits, const float *bias, size_t n,
+                             const int32_t *hash, size_t top_k, float scaling, int32_t *out_expert,
+                             float *out_weight, float *out_score) {
+    if (n == 0 || top_k == 0 || top_k > n) return URBO_ERR_SHAPE;
+    if (!(scaling > 0.0f) || !finite(scaling)) return URBO_ERR_INVALID;
+    if (any_nonfinite(logits, n) || (bias && any_nonfinite(bias, n))) return URBO_ERR_NONFINITE;
+    std::vector<float> score(n), sel(n);
+    for (size_t i = 0; i < n; ++i) {
+        score[i] = std::sqrt(softplus(logits[i]));
+        sel[i] = score[i] + (bias ? bias[i] : 0.0f);
+    }
+    std::vector<int32_t> experts(top_k);
+    if (hash) {
+        for (size_t r = 0; r < top_k; ++r) {
+            if (hash[r] < 0 || size_t(hash[r]) >= n) return URBO_ERR_INVALID;
+            experts[r] = hash[r];
+        }
+    } else {
+        std::vector<int32_t> ranking(n);
+        for (size_t i = 0; i < n; ++i) ranking[i] = int32_t(i);
+        std::stable_sort(ranking.begin(), ranking.end(), [&](int32_t a, int32_t b) {
+            const int32_t ka = total_key(sel[a]), kb = total_key(sel[b]);
+            return ka != kb ? ka > kb : a < b;
+        });
+        std::copy(ranking.begin(), ranking.begin() + long(top_k), experts.begin());
+    }
+    float den = -0.0f;  // Iterator::sum over f32
+    for (int32_t e : experts) den += score[e];
+    if (!finite(den) || den <= 0.0f) return URBO_ERR_NONFINITE;
+    for (size_t r = 0; r < top_k; ++r) {
+        out_expert[r] = experts[r];
+        out_weight[r] = score[experts[r]] / den * scaling;
+        if (out_score) out_score[r] = sel[experts[r]];
+    }
+    return URBO_OK;
+}
+
+// MoeWeights::forward of DeepSeek-V4 (deepseek_v4/runtime.rs:2484-2700): router logits (the
+// layer's router matvec), route_sqrt_softplus with the layer bias and scaling (or the given hash
+// experts), then urbo_moe_deepseek_forward for the routes.
+int urbo_moe_deepseek_layer_forward(const urbo_moe_layer *L, const float *x, size_t tokens,
+                                    const int32_t *hash, float limit, float *out,
+                                    int32_t *route_expert, float *route_weight, int threads) {
+    const size_t H = L->router->cols, n = L->experts, k = L->top_k;
+    std::vector<float> logits(n);
+    for (size_t t = 0; t < tokens; ++t) {
+        int rc = urbo_matvec_rows(L->router, 0, n, x + t * H, logits.data(), threads);
+        if (rc) return rc;
+        rc = urbo_route_sqrt_softplus(logits.data(), L->bias, n, hash ? hash + t * k : nullptr, k,
+                                      L->routed_scaling_factor, route_expert + t * k,
+                                      route_weight + t * k, nullptr);
+        if (rc) return rc;
+    }
+    return urbo_moe_deepseek_forward(L, x, tokens, route_expert, route_weight, limit, out, threads);
+}
+
 }  // extern "C"

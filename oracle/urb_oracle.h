@@ -37,6 +37,7 @@ enum {
     URBO_ERR_INVALID_SCALE = 2,
     URBO_ERR_NONFINITE = 3,
     URBO_ERR_INVALID_GEOMETRY = 4,
+    URBO_ERR_INVALID = 9,  /* DeepseekMathError::Invalid (bad hash ids, non-positive scale) */
 };
 
 typedef struct urbo_matrix {
@@ -116,6 +117,14 @@ float urbo_bounded_swiglu(float gate, float up, float limit);
 int urbo_moe_deepseek_forward(const urbo_moe_layer *layer, const float *x, size_t tokens,
                               const int32_t *route_expert, const float *route_weight,
                               float limit, float *out, int threads);
+/* deepseek_v4/math.rs:451-516 route_sqrt_softplus of one row (bias, hash may be NULL), and the
+ * whole DeepSeek-V4 layer forward (router + routing + the composition above). */
+int urbo_route_sqrt_softplus(const float *logits, const float *bias, size_t experts,
+                             const int32_t *hash, size_t top_k, float scaling, int32_t *out_expert,
+                             float *out_weight, float *out_score);
+int urbo_moe_deepseek_layer_forward(const urbo_moe_layer *layer, const float *x, size_t tokens,
+                                    const int32_t *hash, float limit, float *out,
+                                    int32_t *route_expert, float *route_weight, int threads);
 
 #ifdef __cplusplus
 }

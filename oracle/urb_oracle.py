@@ -108,6 +108,12 @@ def lib():
         _lib.urbo_round_bf16.argtypes = [ctypes.c_float]
         _lib.urbo_bounded_swiglu.restype = ctypes.c_float
         _lib.urbo_bounded_swiglu.argtypes = [ctypes.c_float, ctypes.c_float, ctypes.c_float]
+        _lib.urbo_route_sqrt_softplus.argtypes = [
+            ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p, ctypes.c_size_t,
+            ctypes.c_float, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
+        _lib.urbo_moe_deepseek_layer_forward.argtypes = [
+            ctypes.POINTER(OracleMoeLayer), ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p,
+            ctypes.c_float, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int]
         _lib.urbo_moe_deepseek_forward.argtypes = [
             ctypes.POINTER(OracleMoeLayer), ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p,
             ctypes.c_void_p, ctypes.c_float, ctypes.c_void_p, ctypes.c_int]
@@ -290,3 +296,32 @@ def moe_deepseek_forward(layer: "MoeLayer", x, expert_ids, weights, limit: float
     _check(lib().urbo_moe_deepseek_forward(ctypes.byref(layer.c), _ptr(x), t, _ptr(ids), _ptr(w),
                                            limit, _ptr(out), threads or default_threads()))
     return out
+
+
+def route_sqrt_softplus(logits, bias, hash_experts, top_k, scaling):
+    """deepseek_v4/math.rs:451-516 for one row: (ids, weights, selection scores)."""
+    lg = np.ascontiguousarray(logits, dtype=np.float32)
+    b = None if bias is None else np.ascontiguousarray(bias, dtype=np.float32)
+    h = None if hash_experts is None else np.ascontiguousarray(hash_experts, dtype=np.int32)
+    e = np.empty(top_k, dtype=np.int32)
+    w = np.empty(top_k, dtype=np.float32)
+    s = np.empty(top_k, dtype=np.float32)
+    _check(lib().urbo_route_sqrt_softplus(_ptr(lg), None if b is None else _ptr(b), lg.size,
+                                          None if h is None else _ptr(h), top_k, scaling,
+                                          _ptr(e), _ptr(w), _ptr(s)))
+    return e, w, s
+
+
+def moe_deepseek_layer_forward(layer: "MoeLayer", x, limit: float, hash_experts=None,
+                               threads=None):
+    """DeepSeek-V4 MoeWeights::forward (router, route_sqrt_softplus, expert numerics)."""
+    x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1, layer.hidden)
+    t = x.shape[0]
+    h = None if hash_experts is None else np.ascontiguousarray(hash_experts, dtype=np.int32)
+    out = np.empty_like(x)
+    e = np.empty((t, layer.top_k), dtype=np.int32)
+    w = np.empty((t, layer.top_k), dtype=np.float32)
+    _check(lib().urbo_moe_deepseek_layer_forward(ctypes.byref(layer.c), _ptr(x), t,
+                                                 None if h is None else _ptr(h), limit, _ptr(out),
+                                                 _ptr(e), _ptr(w), threads or default_threads()))
+    return out, e, w

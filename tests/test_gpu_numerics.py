@@ -83,3 +83,52 @@ def test_deepseek_v4_rejects_bad_weights_and_limits(oracle, ctx):
     assert e.value.kind == "InvalidArgument"
     # The GLM numerics of the same call are unaffected.
     dev.forward_routed(x, 2, ids, np.ones((2, 2), np.float32))
+
+
+def test_route_sqrt_softplus_golden_device(oracle, ctx):
+    # deepseek_v4/math.rs:764-786.
+    e, w, _ = urb.route_sqrt_softplus([0.0, 1.0, 2.0, 3.0], None, [[3, 0]], 2, 1.5, ctx=ctx)
+    assert list(e[0]) == [3, 0] and abs(float(w.sum()) - 1.5) < 1e-6
+    e, w, _ = urb.route_sqrt_softplus([3.0, 2.0, 1.0], None, None, 1, 1.0, ctx=ctx)
+    assert e[0, 0] == 0
+    e, w, _ = urb.route_sqrt_softplus([3.0, 2.0, 1.0], [0.0, 0.0, 10.0], None, 1, 1.0, ctx=ctx)
+    assert e[0, 0] == 2 and w[0, 0] == 1.0
+
+
+@pytest.mark.parametrize("with_bias,with_hash", [(True, False), (False, False), (True, True)])
+def test_route_sqrt_softplus_matches_oracle(oracle, ctx, with_bias, with_hash):
+    g = syn.rng(9950 + 2 * with_bias + with_hash)
+    tokens, experts, k = 96, 256, 8
+    logits = (g.standard_normal((tokens, experts)) * 4.0).astype(np.float32)
+    logits[:, ::17] = np.float32(-120.0)   # softplus underflows toward 0
+    logits[:, 5::29] = np.float32(90.0)    # v + log1p(exp(-v)) branch, exp(-v) tiny
+    logits[3, :] = 0.25                    # every selection ties: lower ids win
+    bias = syn.normal_f32(g, experts, 0.01) if with_bias else None
+    hash_ids = np.stack([g.permutation(experts)[:k] for _ in range(tokens)]).astype(np.int32) \
+        if with_hash else None
+    e, w, s = urb.route_sqrt_softplus(logits, bias, hash_ids, k, 2.5, ctx=ctx)
+    for t in range(tokens):
+        oe, ow, os_ = oracle.route_sqrt_softplus(logits[t], bias,
+                                                 None if hash_ids is None else hash_ids[t], k, 2.5)
+        assert np.array_equal(e[t], oe), t
+        assert np.array_equal(w[t].view(np.uint32), ow.view(np.uint32)), t
+        assert np.array_equal(s[t].view(np.uint32), os_.view(np.uint32)), t
+
+
+@pytest.mark.parametrize("use_hash", [False, True])
+def test_deepseek_v4_layer_forward(oracle, ctx, use_hash):
+    g = syn.rng(9960 + use_hash)
+    hidden, inter, experts, k, tokens = 512, 256, 32, 6, 19
+    dev, orc = build_layer(oracle, ctx, g, hidden, inter, experts, "mxfp4", top_k=k, scale=2.5)
+    x = syn.normal_bf16_as_f32(g, (tokens, hidden))
+    h = np.stack([g.permutation(experts)[:k] for _ in range(tokens)]).astype(np.int32) \
+        if use_hash else None
+    out, ids, w = dev.forward_ex(x, tokens, numerics="deepseek_v4", swiglu_limit=10.0,
+                                 hash_experts=h)
+    o_out, o_ids, o_w = oracle.moe_deepseek_layer_forward(orc, x, 10.0, hash_experts=h)
+    assert np.array_equal(ids, o_ids)
+    assert np.array_equal(w.view(np.uint32), o_w.view(np.uint32))
+    r, m = rel_err(out, o_out)
+    print("deepseek layer hash=%s relL2=%.3e maxabs=%.3e" % (use_hash, r, m))
+    assert np.abs(o_out).max() > 1e-3
+    assert_close(out, o_out)

@@ -352,3 +352,15 @@ def test_round_bf16_and_bounded_swiglu_golden(oracle):
     assert oracle.round_bf16(1.0 + 3 * 2.0 ** -8) == 1.0 + 2.0 ** -6
     assert oracle.round_bf16(-2.5) == -2.5
 
+
+
+def test_route_sqrt_softplus_golden(oracle):
+    # deepseek_v4/math.rs:764-775 (hash_router_uses_fixed_ids_but_learned_weights).
+    e, w, _ = oracle.route_sqrt_softplus([0.0, 1.0, 2.0, 3.0], None, [3, 0], 2, 1.5)
+    assert list(e) == [3, 0]
+    assert abs(float(np.sum(w)) - 1.5) < 1e-6
+    # :778-786 (correction_bias_selects_but_does_not_weight).
+    e, w, _ = oracle.route_sqrt_softplus([3.0, 2.0, 1.0], None, None, 1, 1.0)
+    assert e[0] == 0
+    e, w, _ = oracle.route_sqrt_softplus([3.0, 2.0, 1.0], [0.0, 0.0, 10.0], None, 1, 1.0)
+    assert e[0] == 2 and w[0] == 1.0

@@ -22,6 +22,7 @@ __all__ = [
     "UrbError", "MxError", "Context", "MxFp4Matrix", "MxFp8Matrix", "Bf16Matrix", "DenseMatrix",
     "GatedMlp", "RouteChoice", "MoeGeometry", "route_noaux_tc", "route_softmax_top_k",
     "group_routes", "RuntimeMoeLayer", "default_context", "simulate_e4m3_activation",
+    "route_sqrt_softplus",
 ]
 
 
@@ -322,6 +323,25 @@ def route_softmax_top_k(logits, top_k: int, ctx: Optional[Context] = None):
     return ids, w
 
 
+def route_sqrt_softplus(logits, correction_bias, hash_experts, top_k: int,
+                        routed_scaling_factor: float, ctx: Optional[Context] = None):
+    """route_sqrt_softplus (src/models/deepseek_v4/math.rs:451-516) on the device for one or
+    more rows of logits: (expert ids, weights, selection scores) [tokens, top_k]."""
+    ctx = ctx or default_context()
+    lg = np.ascontiguousarray(logits, dtype=np.float32)
+    if lg.ndim == 1:
+        lg = lg[None, :]
+    t, e = lg.shape
+    b = None if correction_bias is None else np.ascontiguousarray(correction_bias, dtype=np.float32)
+    h = None if hash_experts is None else np.ascontiguousarray(hash_experts, dtype=np.int32)
+    ids = np.empty((t, top_k), dtype=np.int32)
+    w = np.empty((t, top_k), dtype=np.float32)
+    s = np.empty((t, top_k), dtype=np.float32)
+    ctx.check(ctx.lib.urb_route_sqrt_softplus(ctx.h, _ptr(lg), _ptr(b), t, e, _ptr(h), top_k,
+                                              routed_scaling_factor, _ptr(ids), _ptr(w), _ptr(s)))
+    return ids, w, s
+
+
 def simulate_e4m3_activation(values, block_size: int, ctx: Optional[Context] = None) -> np.ndarray:
     """simulate_e4m3_activation (src/math/mxfp.rs:82-115) on the device."""
     ctx = ctx or default_context()
@@ -432,6 +452,24 @@ class RuntimeMoeLayer:
             self.ctx.h, self.h, _ptr(x), tokens, _ptr(ids), _ptr(w), ctypes.byref(num),
             _ptr(out)))
         return out
+
+    def forward_ex(self, x, tokens: int, numerics: str = "glm", swiglu_limit: float = 0.0,
+                   hash_experts=None):
+        """The layer forward with checkpoint numerics (urb_moe_forward_ex): "glm", or
+        "deepseek_v4" (route_sqrt_softplus routing, or fixed `hash_experts` [tokens, top_k],
+        and the DeepSeek-V4 expert numerics).  Returns (out, expert ids, weights)."""
+        K = self.geometry.top_k
+        x = np.ascontiguousarray(x, dtype=np.float32).ravel()
+        out = np.empty((tokens, self.hidden_size()), dtype=np.float32)
+        ids = np.empty((tokens, K), dtype=np.int32)
+        w = np.empty((tokens, K), dtype=np.float32)
+        h = None if hash_experts is None else np.ascontiguousarray(hash_experts, dtype=np.int32)
+        mode = {"glm": native.NUMERICS_GLM, "deepseek_v4": native.NUMERICS_DEEPSEEK_V4}[numerics]
+        num = native.Numerics(mode, swiglu_limit)
+        self.ctx.check(self.ctx.lib.urb_moe_forward_ex(
+            self.ctx.h, self.h, _ptr(x), tokens, ctypes.byref(num), _ptr(h), _ptr(out), _ptr(ids),
+            _ptr(w)))
+        return out, ids, w
 
     def forward(self, x):
         """Single token: (Vec<f32>, Vec<RouteChoice>) as in the reference."""

@@ -2,7 +2,8 @@
 
     python -m urbilateria_b200.build        # or __graft_entry__.build()
 
-Steps: (1) generate the libm-expf exception table once (gen_expf_table.c, ~90 s on 8 cores),
+Steps: (1) generate the libm exception tables once (gen_expf_table.c, ~90 s on 8 cores;
+gen_log1pf_table.c, ~10 s),
 (2) compile every csrc/*.cu with nvcc for sm_100a, (3) link urbilateria_b200/liburb_moe.so
 (static CUDA runtime) and urbilateria_b200/liburb_moe.a (for a Rust build.rs).
 Objects are cached under urbilateria_b200/_build keyed by source modification time.
@@ -22,6 +23,7 @@ CSRC = os.path.join(PKG, "csrc")
 BUILD = os.path.join(PKG, "_build")
 GEN = os.path.join(CSRC, "_gen")
 TABLE = os.path.join(GEN, "expf_table.bin")
+LOG1P_TABLE = os.path.join(GEN, "log1pf_table.bin")
 SO = os.path.join(PKG, "liburb_moe.so")
 AR = os.path.join(PKG, "liburb_moe.a")
 
@@ -49,22 +51,31 @@ def _stale(out, deps):
     return any(os.path.getmtime(d) > t for d in deps)
 
 
-def expf_table() -> str:
+def _libm_table(out: str, gen_src: str) -> str:
     os.makedirs(GEN, exist_ok=True)
-    src = os.path.join(CSRC, "gen_expf_table.c")
-    if not _stale(TABLE, [src]):
-        return TABLE
-    exe = os.path.join(GEN, "gen_expf_table")
+    src = os.path.join(CSRC, gen_src)
+    if not _stale(out, [src]):
+        return out
+    exe = os.path.join(GEN, os.path.splitext(gen_src)[0])
     _run([HOST_CC, "-O2", "-fopenmp", src, "-o", exe, "-lm"])
-    tmp = TABLE + ".tmp"
+    tmp = out + ".tmp"
     _run([exe, tmp])
-    os.replace(tmp, TABLE)
-    return TABLE
+    os.replace(tmp, out)
+    return out
+
+
+def expf_table() -> str:
+    return _libm_table(TABLE, "gen_expf_table.c")
+
+
+def log1pf_table() -> str:
+    return _libm_table(LOG1P_TABLE, "gen_log1pf_table.c")
 
 
 def build(verbose: bool = False) -> str:
     os.makedirs(BUILD, exist_ok=True)
     table = expf_table()
+    log1p_table = log1pf_table()
     headers = glob.glob(os.path.join(CSRC, "*.cuh")) + [os.path.join(ROOT, "include", "urb_moe.h")]
     jobs = []
     for cu in sorted(glob.glob(os.path.join(CSRC, "*.cu"))):
@@ -74,8 +85,9 @@ def build(verbose: bool = False) -> str:
     obj = os.path.join(BUILD, "expf_table.cpp.o")
     jobs.append((obj, [HOST_CXX, "-O2", "-std=c++17", "-fPIC", "-fvisibility=hidden",
                        "-I", os.path.join(CUDA_HOME, "include"), "-I", os.path.join(ROOT, "include"),
-                       '-DURB_EXPF_TABLE_PATH=%s' % table, "-c", cpp, "-o", obj],
-                 [cpp, table] + headers))
+                       '-DURB_EXPF_TABLE_PATH=%s' % table,
+                       '-DURB_LOG1PF_TABLE_PATH=%s' % log1p_table, "-c", cpp, "-o", obj],
+                 [cpp, table, log1p_table] + headers))
     todo = [j for j in jobs if _stale(j[0], j[2])]
     with cf.ThreadPoolExecutor(max_workers=max(1, os.cpu_count() or 1)) as ex:
         for f in [ex.submit(_run, cmd) for _, cmd, _ in todo]:

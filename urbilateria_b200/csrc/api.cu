@@ -270,6 +270,7 @@ int urb_ctx_destroy(urb_ctx *ctx) {
     if (ctx->ws) cudaFree(ctx->ws);
     if (ctx->d_status) cudaFree(ctx->d_status);
     if (ctx->expf_keys) cudaFree(const_cast<uint32_t *>(ctx->expf_keys));
+    if (ctx->log1pf_keys) cudaFree(const_cast<uint32_t *>(ctx->log1pf_keys));
     if (ctx->pinned) cudaFreeHost(ctx->pinned);
     if (ctx->own_stream && ctx->stream) cudaStreamDestroy(ctx->stream);
     delete ctx;
@@ -546,6 +547,56 @@ int urb_route_noaux_tc(urb_ctx *ctx, const float *logits, const float *bias, siz
     URB_CUDA(ctx, cudaMemcpyAsync(&status, ctx->d_status, 4, cudaMemcpyDeviceToHost, st));
     URB_CUDA(ctx, cudaStreamSynchronize(st));
     if (status) return set_error(ctx, status, "route_noaux_tc rejected the logits");
+    return URB_OK;
+}
+
+int urb_route_sqrt_softplus(urb_ctx *ctx, const float *logits, const float *bias, size_t tokens,
+                            size_t experts, const int32_t *hash_experts, uint32_t top_k,
+                            float routed_scaling_factor, int32_t *out_expert, float *out_weight,
+                            float *out_score) {
+    if (!ctx || !logits || !out_expert || !out_weight) return URB_ERR_INVALID_ARGUMENT;
+    std::lock_guard<std::recursive_mutex> lk(ctx->mu);
+    cudaSetDevice(ctx->device);
+    // deepseek_v4/math.rs:458-480: geometry, scale, finiteness, hash range.
+    if (experts == 0 || top_k == 0 || top_k > experts)
+        return set_error(ctx, URB_ERR_SHAPE, "router logits/bias/hash/top-k geometry is inconsistent");
+    if (!std::isfinite(routed_scaling_factor) || routed_scaling_factor <= 0.0f)
+        return set_error(ctx, URB_ERR_INVALID_ARGUMENT, "routed_scaling_factor must be finite and positive");
+    if (!all_finite(logits, tokens * experts) || (bias && !all_finite(bias, experts)))
+        return set_error(ctx, URB_ERR_NONFINITE, "router logits or bias contain NaN/infinity");
+    if (hash_experts)
+        for (size_t i = 0; i < tokens * top_k; ++i)
+            if (hash_experts[i] < 0 || size_t(hash_experts[i]) >= experts)
+                return set_error(ctx, URB_ERR_INVALID_ARGUMENT, "hash expert IDs must be in range");
+    if (tokens == 0) return URB_OK;
+    cudaStream_t st = ctx->stream;
+    const size_t K = top_k;
+    int rc;
+    size_t need = tokens * experts * 4 + experts * 4 + tokens * K * 16 + 4096;
+    uint8_t *ws = static_cast<uint8_t *>(workspace(ctx, need, &rc));
+    if (!ws) return rc;
+    Carve cv{ws};
+    float *d_l = cv.take<float>(tokens * experts);
+    float *d_b = cv.take<float>(experts);
+    int32_t *d_h = cv.take<int32_t>(tokens * K);
+    int32_t *d_e = cv.take<int32_t>(tokens * K);
+    float *d_w = cv.take<float>(tokens * K);
+    float *d_s = cv.take<float>(tokens * K);
+    URB_CUDA(ctx, cudaMemsetAsync(ctx->d_status, 0, 4, st));
+    URB_CUDA(ctx, cudaMemcpyAsync(d_l, logits, tokens * experts * 4, cudaMemcpyDefault, st));
+    if (bias) URB_CUDA(ctx, cudaMemcpyAsync(d_b, bias, experts * 4, cudaMemcpyDefault, st));
+    if (hash_experts) URB_CUDA(ctx, cudaMemcpyAsync(d_h, hash_experts, tokens * K * 4, cudaMemcpyDefault, st));
+    rc = launch_route_sqrt_softplus(ctx, d_l, bias ? d_b : nullptr, hash_experts ? d_h : nullptr,
+                                    int(tokens), int(experts), int(K), routed_scaling_factor, d_e,
+                                    d_w, d_s, ctx->d_status, st);
+    if (rc) return rc;
+    int32_t status = 0;
+    URB_CUDA(ctx, cudaMemcpyAsync(out_expert, d_e, tokens * K * 4, cudaMemcpyDefault, st));
+    URB_CUDA(ctx, cudaMemcpyAsync(out_weight, d_w, tokens * K * 4, cudaMemcpyDefault, st));
+    if (out_score) URB_CUDA(ctx, cudaMemcpyAsync(out_score, d_s, tokens * K * 4, cudaMemcpyDefault, st));
+    URB_CUDA(ctx, cudaMemcpyAsync(&status, ctx->d_status, 4, cudaMemcpyDeviceToHost, st));
+    URB_CUDA(ctx, cudaStreamSynchronize(st));
+    if (status) return set_error(ctx, status, "route_sqrt_softplus rejected the logits");
     return URB_OK;
 }
 

@@ -37,4 +37,17 @@ __device__ __forceinline__ float expf_libm(float x, const ExpfTable &t) {
     return float(exp(double(x)));
 }
 
+// libm log1pf (Rust's f32::ln_1p) on [0, 1]: (float)log1p((double)x) unless the build step
+// gen_log1pf_table.c recorded the input (libm not correctly rounded there, or log1p(x) within
+// 2^-48 of a float midpoint).  Same table layout as ExpfTable.
+__device__ __forceinline__ float log1pf_libm(float x, const ExpfTable &t) {
+    uint32_t k = __float_as_uint(x);
+    if (t.index && k <= 0x3F800000u) {
+        uint32_t b = k >> 12;
+        for (uint32_t i = t.index[b], e = t.index[b + 1]; i < e; ++i)
+            if (t.keys[i] == k) return __uint_as_float(t.vals[i]);
+    }
+    return float(log1p(double(x)));
+}
+
 }  // namespace urb

@@ -719,6 +719,77 @@ int urb_moe_forward_routed_ex(urb_ctx *ctx, urb_layer *L, const float *x, size_t
     return URB_OK;
 }
 
+int urb_moe_forward_ex(urb_ctx *ctx, urb_layer *L, const float *x, size_t tokens,
+                       const urb_moe_numerics *numerics, const int32_t *hash_experts, float *out,
+                       int32_t *route_expert, float *route_weight) {
+    if (!ctx || !L || !x || !out) return URB_ERR_INVALID_ARGUMENT;
+    Numerics num;
+    {
+        std::lock_guard<std::recursive_mutex> lk(ctx->mu);
+        int rc = numerics_of(ctx, numerics, &num);
+        if (rc) return rc;
+    }
+    if (num.mode == URB_NUMERICS_GLM) {
+        if (hash_experts)
+            return set_error(ctx, URB_ERR_INVALID_ARGUMENT, "hash routing needs the DeepSeek-V4 numerics");
+        return urb_moe_forward(ctx, L, x, tokens, out, route_expert, route_weight, nullptr,
+                               nullptr, nullptr, nullptr, nullptr);
+    }
+    if (L->e_count != L->experts)
+        return set_error(ctx, URB_ERR_UNSUPPORTED, "an expert shard runs through urb_ep_forward");
+    std::lock_guard<std::recursive_mutex> lk(ctx->mu);
+    cudaSetDevice(ctx->device);
+    if (tokens == 0) return URB_OK;
+    const size_t H = L->hidden, K = L->geo.top_k, E = L->experts, TK = tokens * K;
+    if (hash_experts)
+        for (size_t i = 0; i < TK; ++i)
+            if (hash_experts[i] < 0 || size_t(hash_experts[i]) >= E)
+                return set_error(ctx, URB_ERR_INVALID_ARGUMENT, "hash expert IDs must be in range");
+    // MoeWeights::forward for DeepSeek-V4 (deepseek_v4/runtime.rs:2484-2700): exact router
+    // logits, route_sqrt_softplus with the layer's correction bias (or the token's hash experts),
+    // then the routed experts with the checkpoint numerics.
+    cudaStream_t st = ctx->stream;
+    auto align = [](size_t b) { return (b + 255) & ~size_t(255); };
+    const size_t o_x = 0, o_out = align(o_x + tokens * H * 4), o_l = align(o_out + tokens * H * 4);
+    const size_t o_x64 = align(o_l + tokens * E * 4);
+    const size_t o_ids = align(o_x64 + router_f64_elems(int(tokens), int(H)) * 8);
+    const size_t o_w = align(o_ids + TK * 4), o_s = align(o_w + TK * 4), o_h = align(o_s + TK * 4);
+    const size_t bytes = align(o_h + TK * 4);
+    uint8_t *d = nullptr;
+    URB_CUDA(ctx, cudaMallocAsync(&d, bytes, st));
+    float *d_x = reinterpret_cast<float *>(d + o_x), *d_out = reinterpret_cast<float *>(d + o_out);
+    float *d_l = reinterpret_cast<float *>(d + o_l);
+    double *d_x64 = reinterpret_cast<double *>(d + o_x64);
+    int32_t *d_ids = reinterpret_cast<int32_t *>(d + o_ids), *d_hash = reinterpret_cast<int32_t *>(d + o_h);
+    float *d_w = reinterpret_cast<float *>(d + o_w), *d_s = reinterpret_cast<float *>(d + o_s);
+    URB_CUDA(ctx, cudaMemsetAsync(ctx->d_status, 0, 4, st));
+    URB_CUDA(ctx, cudaMemcpyAsync(d_x, x, tokens * H * 4, cudaMemcpyDefault, st));
+    if (hash_experts) URB_CUDA(ctx, cudaMemcpyAsync(d_hash, hash_experts, TK * 4, cudaMemcpyDefault, st));
+    const RouterGates rg{ctx, nullptr, nullptr, nullptr, ctx->d_status};
+    prof_begin(ctx, URB_K_ROUTER_LOGITS, st);
+    int rc = launch_router_logits_f64(L->router64, int(E), d_x, int(tokens), int(H), d_x64, d_l, st, &rg);
+    prof_end(ctx, st);
+    if (rc) { cudaFreeAsync(d, st); return cuda_fail(ctx, cudaGetLastError(), "router logits"); }
+    prof_begin(ctx, URB_K_ROUTE, st);
+    rc = launch_route_sqrt_softplus(ctx, d_l, L->d_bias, hash_experts ? d_hash : nullptr,
+                                    int(tokens), int(E), int(K), L->geo.routed_scaling_factor,
+                                    d_ids, d_w, d_s, ctx->d_status, st);
+    prof_end(ctx, st);
+    if (rc == URB_OK)
+        rc = moe_forward_device(L, d_x, int(tokens), d_out, nullptr, ctx->d_status, st, d_ids,
+                                d_w, &num);
+    if (rc) { cudaFreeAsync(d, st); return rc; }
+    int32_t status = 0;
+    URB_CUDA(ctx, cudaMemcpyAsync(out, d_out, tokens * H * 4, cudaMemcpyDefault, st));
+    if (route_expert) URB_CUDA(ctx, cudaMemcpyAsync(route_expert, d_ids, TK * 4, cudaMemcpyDefault, st));
+    if (route_weight) URB_CUDA(ctx, cudaMemcpyAsync(route_weight, d_w, TK * 4, cudaMemcpyDefault, st));
+    URB_CUDA(ctx, cudaMemcpyAsync(&status, ctx->d_status, 4, cudaMemcpyDeviceToHost, st));
+    cudaFreeAsync(d, st);
+    URB_CUDA(ctx, cudaStreamSynchronize(st));
+    if (status) return set_error(ctx, status, "MoE forward rejected its input");
+    return URB_OK;
+}
+
 int urb_moe_forward_routed(urb_ctx *ctx, urb_layer *L, const float *x, size_t tokens,
                            const int32_t *route_expert, const float *route_weight, float *out) {
     return urb_moe_forward_routed_ex(ctx, L, x, tokens, route_expert, route_weight, nullptr, out);

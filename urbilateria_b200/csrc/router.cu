@@ -431,6 +431,113 @@ int launch_route_noaux(Ctx *ctx, const float *d_logits, const float *d_bias, int
     return URB_OK;
 }
 
+namespace {
+
+ExpfTable log1p_table_of(const Ctx *ctx) {
+    return ExpfTable{ctx->log1pf_keys, ctx->log1pf_vals, ctx->log1pf_index};
+}
+
+// softplus of deepseek_v4/math.rs:604-610 with libm expf / log1pf, then the square root.
+__device__ __forceinline__ float sqrt_softplus(float v, const ExpfTable &ex, const ExpfTable &lp) {
+    const float sp = v > 0.0f ? __fadd_rn(v, log1pf_libm(expf_libm(-v, ex), lp))
+                              : log1pf_libm(expf_libm(v, ex), lp);
+    return __fsqrt_rn(sp);
+}
+
+// route_sqrt_softplus (deepseek_v4/math.rs:451-516), one warp per token: score = sqrt(
+// softplus(logit)), selection = score + bias; top_k by selection desc with the lower id winning
+// ties (total order), or the token's hash experts as given; the denominator sums the chosen
+// scores in order (f32); weight = score / denominator * scale.  Shared memory per warp:
+// score[E], sel[E] floats and a taken flag per expert.
+__global__ void k_route_sqrt_softplus(const float *logits, const float *bias,
+                                      const int32_t *hash, int tokens, int E, int top_k,
+                                      float scaling, ExpfTable ex, ExpfTable lp, int32_t *out_e,
+                                      float *out_w, float *out_s, int32_t *status,
+                                      int warp_bytes) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int t = blockIdx.x * (blockDim.x >> 5) + warp;
+    if (t >= tokens) return;
+    float *score = reinterpret_cast<float *>(smem + size_t(warp) * warp_bytes);
+    float *sel = score + E;
+    uint8_t *taken = reinterpret_cast<uint8_t *>(sel + E);
+    const float *lg = logits + size_t(t) * E;
+    bool bad = false;
+    for (int i = lane; i < E; i += 32) {
+        const float l = lg[i], b = bias ? bias[i] : 0.0f;
+        bad |= !isfinite(l) || !isfinite(b);
+        const float sc = sqrt_softplus(l, ex, lp);
+        score[i] = sc;
+        sel[i] = bias ? __fadd_rn(sc, b) : sc;
+        taken[i] = 0;
+    }
+    int32_t *oe = out_e + size_t(t) * top_k;
+    float *ow = out_w + size_t(t) * top_k;
+    auto reject = [&](int code) {
+        if (lane == 0) set_status(status, code);
+        for (int r = lane; r < top_k; r += 32) {
+            oe[r] = r;
+            ow[r] = 0.0f;
+            if (out_s) out_s[size_t(t) * top_k + r] = 0.0f;
+        }
+    };
+    if (__any_sync(0xffffffffu, bad)) { reject(URB_ERR_NONFINITE); return; }
+    if (hash) {
+        bool oob = false;
+        for (int r = lane; r < top_k; r += 32) {
+            const int32_t e = hash[size_t(t) * top_k + r];
+            oob |= e < 0 || e >= E;
+        }
+        if (__any_sync(0xffffffffu, oob)) { reject(URB_ERR_SHAPE); return; }
+    }
+    __syncwarp();
+    float den = -0.0f;  // Iterator::sum over f32
+    for (int r = 0; r < top_k; ++r) {
+        int id;
+        if (hash) {
+            id = hash[size_t(t) * top_k + r];
+        } else {
+            int32_t key = INT32_MIN;
+            id = INT32_MAX;
+            for (int i = lane; i < E; i += 32)
+                if (!taken[i]) {
+                    const int32_t k = total_key(sel[i]);
+                    if (better(k, i, key, id)) { key = k; id = i; }
+                }
+            warp_best(key, id);
+            if (lane == (id & 31)) taken[id] = 1;
+        }
+        if (lane == 0) {
+            oe[r] = id;
+            den = __fadd_rn(den, score[id]);
+        }
+        __syncwarp();
+    }
+    den = __shfl_sync(0xffffffffu, den, 0);
+    if (!isfinite(den) || den <= 0.0f) { reject(URB_ERR_NONFINITE); return; }
+    for (int r = lane; r < top_k; r += 32) {
+        const int id = oe[r];
+        ow[r] = __fmul_rn(__fdiv_rn(score[id], den), scaling);
+        if (out_s) out_s[size_t(t) * top_k + r] = sel[id];
+    }
+}
+
+}  // namespace
+
+int launch_route_sqrt_softplus(Ctx *ctx, const float *d_logits, const float *d_bias,
+                               const int32_t *d_hash, int tokens, int experts, int top_k,
+                               float scaling, int32_t *d_expert, float *d_weight, float *d_score,
+                               int32_t *d_status, cudaStream_t st) {
+    if (tokens <= 0) return URB_OK;
+    const int warps = 4;
+    const int warp_bytes = (experts * 9 + 15) & ~15;
+    k_route_sqrt_softplus<<<(tokens + warps - 1) / warps, warps * 32, size_t(warps) * warp_bytes, st>>>(
+        d_logits, d_bias, d_hash, tokens, experts, top_k, scaling, table_of(ctx),
+        log1p_table_of(ctx), d_expert, d_weight, d_score, d_status, warp_bytes);
+    URB_CUDA(ctx, cudaGetLastError());
+    return URB_OK;
+}
+
 int launch_route_softmax(Ctx *ctx, const float *d_logits, int tokens, int experts, int top_k,
                          int32_t *d_expert, float *d_weight, int32_t *d_status,
                          cudaStream_t st) {

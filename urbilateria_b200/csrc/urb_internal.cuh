@@ -114,6 +114,10 @@ struct Ctx {
     const uint32_t *expf_vals = nullptr;
     const uint32_t *expf_index = nullptr;
     int expf_count = 0;
+    // glibc-log1pf exception table over [0, 1] (same layout).
+    const uint32_t *log1pf_keys = nullptr;
+    const uint32_t *log1pf_vals = nullptr;
+    const uint32_t *log1pf_index = nullptr;
     // Optional per-launch profiler (urb_profile_*).
     bool prof = false;
     struct ProfRec { int kind; cudaEvent_t a, b; };
@@ -190,6 +194,12 @@ int launch_matvec1(Ctx *ctx, const Mat *m, size_t start, size_t count, const flo
 int launch_router_logits_f64(const double *w64, int experts, const float *d_x, int tokens,
                              int cols, double *x64, float *d_logits, cudaStream_t st,
                              const RouterGates *gates = nullptr);
+// route_sqrt_softplus (deepseek_v4/math.rs:451-516): bias and hash ([tokens, top_k] fixed
+// experts) optional; outputs [tokens, top_k] in selection order.
+int launch_route_sqrt_softplus(Ctx *ctx, const float *d_logits, const float *d_bias,
+                               const int32_t *d_hash, int tokens, int experts, int top_k,
+                               float scaling, int32_t *d_expert, float *d_weight, float *d_score,
+                               int32_t *d_status, cudaStream_t st);
 int launch_route_softmax(Ctx *ctx, const float *d_logits, int tokens, int experts, int top_k,
                          int32_t *d_expert, float *d_weight, int32_t *d_status,
                          cudaStream_t stream);
