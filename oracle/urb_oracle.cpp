@@ -702,4 +702,139 @@ int urbo_moe_deepseek_layer_forward(const urbo_moe_layer *L, const float *x, siz
     return urbo_moe_deepseek_forward(L, x, tokens, route_expert, route_weight, limit, out, threads);
 }
 
+// ---------------------------------------------------------------------------------------
+// Checkpoint numerics (Qwen3.6): FP32-lane BF16 linear, fine-grained E4M3 activations, BF16
+// boundaries, softmax routing, expert-order BF16 accumulation, sigmoid-gated shared expert.
+
+// src/model/bf16.rs:591-613 dot_bf16_fp32_avx2_fma: eight FMA lanes over the columns
+// (column c in lane c % 8, from +0.0), lanes summed in order (Iterator::sum from -0.0), the
+// columns past the last multiple of eight added by separate multiply and add.
+float urbo_dot_bf16_fp32_lanes(const uint16_t *row, const float *x, size_t cols) {
+    float lanes[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    const size_t complete = cols / 8 * 8;
+    for (size_t c = 0; c < complete; ++c) lanes[c % 8] = std::fma(bf16f(row[c]), x[c], lanes[c % 8]);
+    float sum = rust_sum_f32(lanes, 8);
+    for (size_t c = complete; c < cols; ++c) {
+        const float product = bf16f(row[c]) * x[c];
+        sum = sum + product;
+    }
+    return sum;
+}
+
+// src/math/mxfp.rs:122-149 simulate_finegrained_e4m3_activation: per block the exact scale
+// max|v| / 448 (all-zero blocks stay zero).
+int urbo_simulate_finegrained_e4m3(float *values, size_t n, size_t block) {
+    if (n == 0 || block == 0) return URBO_ERR_SHAPE;
+    if (any_nonfinite(values, n)) return URBO_ERR_NONFINITE;
+    for (size_t b = 0; b < n; b += block) {
+        const size_t e = std::min(n, b + block);
+        float amax = 0.0f;
+        for (size_t i = b; i < e; ++i) amax = std::max(amax, std::fabs(values[i]));
+        if (amax == 0.0f) {
+            for (size_t i = b; i < e; ++i) values[i] = 0.0f;
+            continue;
+        }
+        const float scale = amax / 448.0f;
+        for (size_t i = b; i < e; ++i) values[i] = e4m3(urbo_encode_e4m3fn(values[i] / scale)) * scale;
+    }
+    return URBO_OK;
+}
+
+// qwen3_8/math.rs:10-26 linear: MX weights see the fine-grained E4M3 activation (groups of
+// 128) and the output rounds to BF16; BF16 weights use the FP32 lanes and round to BF16.
+static int qwen_linear(const urbo_matrix *m, const float *x, float *y, int threads) {
+    std::vector<float> xq(x, x + m->cols);
+    int rc;
+    if (m->format == URBO_MXFP4 || m->format == URBO_MXFP8) {
+        rc = urbo_simulate_finegrained_e4m3(xq.data(), m->cols, 128);
+        if (rc) return rc;
+        rc = urbo_matvec_rows(m, 0, m->rows, xq.data(), y, threads);
+        if (rc) return rc;
+    } else if (m->format == URBO_BF16) {
+        const uint16_t *w = static_cast<const uint16_t *>(m->values);
+        for (size_t r = 0; r < m->rows; ++r) y[r] = urbo_dot_bf16_fp32_lanes(w + r * m->cols, x, m->cols);
+    } else {
+        return urbo_matvec_rows(m, 0, m->rows, x, y, threads);  // plain F32: no rounding
+    }
+    for (size_t r = 0; r < m->rows; ++r) {
+        y[r] = urbo_round_bf16(y[r]);
+        if (!finite(y[r])) return URBO_ERR_NONFINITE;
+    }
+    return URBO_OK;
+}
+
+// Qwen38Expert::forward_projections (qwen3_8/expert.rs:137-200) with BF16 boundaries.
+static int qwen_expert(const urbo_matrix *gate, const urbo_matrix *up, const urbo_matrix *down,
+                       const float *x, float *y, int threads) {
+    const size_t I = gate->rows;
+    std::vector<float> g(I), u(I);
+    int rc = qwen_linear(gate, x, g.data(), threads);
+    if (rc) return rc;
+    rc = qwen_linear(up, x, u.data(), threads);
+    if (rc) return rc;
+    for (size_t i = 0; i < I; ++i) {
+        const float a = urbo_round_bf16(urbo_silu(g[i]));
+        const float v = a * u[i];
+        if (!finite(v)) return URBO_ERR_NONFINITE;
+        g[i] = urbo_round_bf16(v);
+    }
+    return qwen_linear(down, g.data(), y, threads);
+}
+
+// execute_batched_moe (qwen3_6/runtime.rs:1067-1215) for one token at a time: BF16 router
+// (FP32 lanes, BF16 logits), softmax top-k with BF16 weights, routed experts accumulated in
+// ascending expert id with BF16 contributions and sums, then the shared expert scaled by the
+// sigmoid of its BF16 gate logit, all BF16.
+int urbo_moe_qwen_layer_forward(const urbo_moe_layer *L, const urbo_matrix *shared_gate_vec,
+                                const float *x, size_t tokens, float *out, int32_t *route_expert,
+                                float *route_weight, int threads) {
+    const size_t H = L->router->cols, n = L->experts, k = L->top_k;
+    std::vector<float> logits(n), y(H), acc(H), shared(H);
+    std::vector<std::pair<int32_t, float>> order(k);
+    for (size_t t = 0; t < tokens; ++t) {
+        const float *xt = x + t * H;
+        int rc = qwen_linear(L->router, xt, logits.data(), threads);
+        if (rc) return rc;
+        rc = urbo_route_softmax_top_k(logits.data(), n, k, route_expert + t * k, route_weight + t * k);
+        if (rc) return rc;
+        for (size_t r = 0; r < k; ++r) {
+            route_weight[t * k + r] = urbo_round_bf16(route_weight[t * k + r]);
+            order[r] = {route_expert[t * k + r], route_weight[t * k + r]};
+        }
+        std::stable_sort(order.begin(), order.end(),
+                         [](const std::pair<int32_t, float> &a, const std::pair<int32_t, float> &b) {
+                             return a.first < b.first;
+                         });
+        std::fill(acc.begin(), acc.end(), 0.0f);
+        for (size_t r = 0; r < k; ++r) {
+            const size_t e = size_t(order[r].first);
+            rc = qwen_expert(&L->gate[e], &L->up[e], &L->down[e], xt, y.data(), threads);
+            if (rc) return rc;
+            for (size_t h = 0; h < H; ++h) {
+                const float c = urbo_round_bf16(order[r].second * y[h]);
+                acc[h] = urbo_round_bf16(acc[h] + c);
+            }
+        }
+        rc = qwen_expert(L->shared_gate, L->shared_up, L->shared_down, xt, shared.data(), threads);
+        if (rc) return rc;
+        float gate;
+        rc = qwen_linear(shared_gate_vec, xt, &gate, threads);
+        if (rc) return rc;
+        float scale;
+        if (gate >= 0.0f) {
+            scale = 1.0f / (1.0f + std::exp(-gate));
+        } else {
+            const float e = std::exp(gate);
+            scale = e / (1.0f + e);
+        }
+        scale = urbo_round_bf16(scale);
+        for (size_t h = 0; h < H; ++h) {
+            const float c = urbo_round_bf16(scale * shared[h]);
+            out[t * H + h] = urbo_round_bf16(acc[h] + c);
+            if (!finite(out[t * H + h])) return URBO_ERR_NONFINITE;
+        }
+    }
+    return URBO_OK;
+}
+
 }  // extern "C"

@@ -126,6 +126,17 @@ int urbo_moe_deepseek_layer_forward(const urbo_moe_layer *layer, const float *x,
                                     const int32_t *hash, float limit, float *out,
                                     int32_t *route_expert, float *route_weight, int threads);
 
+/* Checkpoint numerics (Qwen3.6): src/model/bf16.rs:591-613 (FP32-lane BF16 dot),
+ * src/math/mxfp.rs:122-149 (fine-grained E4M3 activation), qwen3_8/math.rs:10-26 (linear with
+ * BF16 outputs), qwen3_8/expert.rs:137-200 (BF16-boundary SwiGLU) and the execute_batched_moe
+ * composition of qwen3_6/runtime.rs:1067-1215 (softmax top-k, BF16 accumulation in ascending
+ * expert id, sigmoid-gated shared expert).  shared_gate_vec: the [1, hidden] BF16 gate row. */
+float urbo_dot_bf16_fp32_lanes(const uint16_t *row, const float *x, size_t cols);
+int urbo_simulate_finegrained_e4m3(float *values, size_t n, size_t block);
+int urbo_moe_qwen_layer_forward(const urbo_moe_layer *layer, const urbo_matrix *shared_gate_vec,
+                                const float *x, size_t tokens, float *out, int32_t *route_expert,
+                                float *route_weight, int threads);
+
 #ifdef __cplusplus
 }
 #endif

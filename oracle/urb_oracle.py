@@ -114,6 +114,13 @@ def lib():
         _lib.urbo_moe_deepseek_layer_forward.argtypes = [
             ctypes.POINTER(OracleMoeLayer), ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p,
             ctypes.c_float, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int]
+        _lib.urbo_dot_bf16_fp32_lanes.restype = ctypes.c_float
+        _lib.urbo_dot_bf16_fp32_lanes.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t]
+        _lib.urbo_simulate_finegrained_e4m3.argtypes = [ctypes.c_void_p, ctypes.c_size_t,
+                                                        ctypes.c_size_t]
+        _lib.urbo_moe_qwen_layer_forward.argtypes = [
+            ctypes.POINTER(OracleMoeLayer), ctypes.POINTER(OracleMatrix), ctypes.c_void_p,
+            ctypes.c_size_t, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int]
         _lib.urbo_moe_deepseek_forward.argtypes = [
             ctypes.POINTER(OracleMoeLayer), ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p,
             ctypes.c_void_p, ctypes.c_float, ctypes.c_void_p, ctypes.c_int]
@@ -324,4 +331,33 @@ def moe_deepseek_layer_forward(layer: "MoeLayer", x, limit: float, hash_experts=
     _check(lib().urbo_moe_deepseek_layer_forward(ctypes.byref(layer.c), _ptr(x), t,
                                                  None if h is None else _ptr(h), limit, _ptr(out),
                                                  _ptr(e), _ptr(w), threads or default_threads()))
+    return out, e, w
+
+
+# ---- checkpoint numerics (Qwen3.6) -----------------------------------------------------------
+
+def dot_bf16_fp32_lanes(row_bits, x) -> float:
+    """src/model/bf16.rs:591-613 (eight FMA lanes)."""
+    r = np.ascontiguousarray(row_bits, dtype=np.uint16)
+    v = np.ascontiguousarray(x, dtype=np.float32)
+    return lib().urbo_dot_bf16_fp32_lanes(_ptr(r), _ptr(v), v.size)
+
+
+def simulate_finegrained_e4m3(values, block: int) -> np.ndarray:
+    """src/math/mxfp.rs:122-149 (exact scale max|v| / 448 per block)."""
+    v = np.array(values, dtype=np.float32).ravel()
+    _check(lib().urbo_simulate_finegrained_e4m3(_ptr(v), v.size, block))
+    return v
+
+
+def moe_qwen_layer_forward(layer: "MoeLayer", shared_gate_vec: Matrix, x, threads=None):
+    """Qwen3.6 execute_batched_moe composition (qwen3_6/runtime.rs:1067-1215)."""
+    x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1, layer.hidden)
+    t = x.shape[0]
+    out = np.empty_like(x)
+    e = np.empty((t, layer.top_k), dtype=np.int32)
+    w = np.empty((t, layer.top_k), dtype=np.float32)
+    _check(lib().urbo_moe_qwen_layer_forward(ctypes.byref(layer.c), ctypes.byref(shared_gate_vec.c),
+                                             _ptr(x), t, _ptr(out), _ptr(e), _ptr(w),
+                                             threads or default_threads()))
     return out, e, w

@@ -364,3 +364,36 @@ def test_route_sqrt_softplus_golden(oracle):
     assert e[0] == 0
     e, w, _ = oracle.route_sqrt_softplus([3.0, 2.0, 1.0], [0.0, 0.0, 10.0], None, 1, 1.0)
     assert e[0] == 2 and w[0] == 1.0
+
+
+# ---- checkpoint numerics (Qwen3.6) ------------------------------------------------------------
+
+def test_finegrained_e4m3_golden(oracle):
+    # src/math/mxfp.rs:2949-2955 (finegrained_activation_uses_exact_absmax_scale).
+    v = oracle.simulate_finegrained_e4m3([1.0, 0.3, 0.0, 0.0], 2)
+    assert v[0] == 1.0
+    assert abs(v[1] - oracle.lib().urbo_decode_e4m3fn(0x70) / 448.0) < 1e-7
+    assert v[2] == 0.0 and v[3] == 0.0
+
+
+def test_bf16_fp32_lanes_formula(oracle):
+    # The eight-lane FMA tree of src/model/bf16.rs:591-613, restated in numpy (FMA via f64: a
+    # bf16 x f32 product is exact in f64 and one rounding of product + lane equals fma), over
+    # the shapes of the reference's own tests (:860-887, :903-920: 1..2048 columns, tails).
+    def bf16(v):
+        b = np.asarray(v, np.float32).view(np.uint32)
+        return ((b + 0x7FFF + ((b >> 16) & 1)) >> 16).astype(np.uint16)
+    for cols in [1, 7, 8, 9, 31, 65, 512, 2048]:
+        w = bf16([((i * 137 % 251) - 125.0) / 37.0 for i in range(cols)])
+        x = np.array([((i * 19 % 97) - 48.0) / 31.0 for i in range(cols)], np.float32)
+        wf = (w.astype(np.uint32) << 16).view(np.float32)
+        lanes = np.zeros(8, np.float32)
+        complete = cols // 8 * 8
+        for c in range(complete):
+            lanes[c % 8] = np.float32(np.float64(wf[c]) * np.float64(x[c]) + np.float64(lanes[c % 8]))
+        s = np.float32(-0.0)
+        for v in lanes:
+            s = np.float32(s + v)
+        for c in range(complete, cols):
+            s = np.float32(s + np.float32(wf[c] * x[c]))
+        assert bits(oracle.dot_bf16_fp32_lanes(w, x)) == bits(s), cols
