@@ -232,9 +232,18 @@ URB_API int urb_moe_forward_routed_device(urb_ctx *ctx, urb_layer *layer, const 
  * activation before BF16 rounding, E4M3 simulation and the down projection (none for the shared
  * expert), down outputs rounded to BF16, routed rows summed in f32 in ascending expert id, the
  * shared row added last and the sum rounded to BF16.  Route weights must be finite and
- * non-negative (URB_ERR_INVALID_ARGUMENT otherwise). */
+ * non-negative (URB_ERR_INVALID_ARGUMENT otherwise).
+ * URB_NUMERICS_QWEN36: execute_batched_moe (src/models/qwen3_6/runtime.rs:1067-1215) over
+ * Qwen36Expert / linear (src/models/qwen3_8/math.rs:10-26): BF16 experts take the FP32-lane BF16
+ * dot (src/model/bf16.rs:591-613), MX experts see the input simulated as E4M3 with the exact
+ * per-128 scale max|v| / 448 (src/math/mxfp.rs:122-149); every projection output rounds to BF16;
+ * h = BF16(BF16(silu(gate)) * up); routed contributions BF16(BF16(w) * y) accumulate in BF16 in
+ * ascending expert id; the shared expert adds BF16(BF16(sigmoid(g)) * y) with g the BF16 logit of
+ * the layer's shared_expert_gate row (urb_moe_layer_set_shared_expert_gate, required).  Needs a
+ * BF16 router and a shared expert; `swiglu_limit` is unused. */
 #define URB_NUMERICS_GLM 0
 #define URB_NUMERICS_DEEPSEEK_V4 1
+#define URB_NUMERICS_QWEN36 2
 typedef struct urb_moe_numerics {
     int32_t mode;
     float swiglu_limit;
@@ -253,8 +262,10 @@ URB_API int urb_moe_forward_routed_ex_device(urb_ctx *ctx, urb_layer *layer, con
  * exact router logits, route_sqrt_softplus (deepseek_v4/math.rs:451-516) with the layer's
  * correction bias and routed_scaling_factor, or the token's fixed experts `hash_experts`
  * ([tokens, top_k], NULL for learned routing; the weights still come from the scores), then the
- * routed experts with the DeepSeek-V4 numerics above.  Routes out in selection order (NULL to
- * skip). */
+ * routed experts with the DeepSeek-V4 numerics above.  URB_NUMERICS_QWEN36 (execute_batched_moe,
+ * src/models/qwen3_6/runtime.rs:1067-1215): BF16 router logits (FP32 lanes), route_softmax_top_k
+ * with the weights rounded to BF16, then the Qwen3.6 numerics above (hash_experts must be NULL).
+ * Routes out in selection order (NULL to skip). */
 URB_API int urb_moe_forward_ex(urb_ctx *ctx, urb_layer *layer, const float *x, size_t tokens,
                                const urb_moe_numerics *numerics, const int32_t *hash_experts,
                                float *out, int32_t *route_expert, float *route_weight);
@@ -272,6 +283,16 @@ URB_API int urb_route_sqrt_softplus(urb_ctx *ctx, const float *logits, const flo
  * round-tripped through E4M3FN. */
 URB_API int urb_simulate_e4m3_activation(urb_ctx *ctx, const float *x, size_t n, size_t block,
                                          float *out);
+/* simulate_finegrained_e4m3_activation (src/math/mxfp.rs:122-149): each block scaled by exactly
+ * max|v| / 448 and round-tripped through E4M3FN; all-zero blocks stay zero. */
+URB_API int urb_simulate_finegrained_e4m3_activation(urb_ctx *ctx, const float *x, size_t n,
+                                                     size_t block, float *out);
+/* The Qwen3.6 BF16 linear (src/models/qwen3_8/math.rs:10-26 with dot_bf16_fp32_avx2_fma,
+ * src/model/bf16.rs:591-613) of `tokens` rows of x [tokens, cols] by a BF16 matrix [rows, cols]:
+ * out [tokens, rows] = BF16(eight FP32 FMA lanes, lanes summed in order, tail added), bit-exact.
+ * URB_ERR_NONFINITE when an output is not finite. */
+URB_API int urb_linear_bf16_fp32_lanes(urb_ctx *ctx, const urb_mat *m, const float *x,
+                                       size_t tokens, float *out);
 
 /* ---- expert parallelism across the GPUs of one node ------------------------------------------ */
 
@@ -290,6 +311,10 @@ typedef struct urb_ep urb_ep;
  * hidden] and bias [experts] for all experts; gate/up/down arrays hold the `expert_count`
  * experts starting at `expert_begin`.  Runs only through urb_ep_forward*; urb_moe_forward*
  * return URB_ERR_UNSUPPORTED for it.  Needs MX (MXFP4 / MXFP8 1x32) experts. */
+/* Qwen3.6 shared_expert_gate (src/models/qwen3_6/runtime.rs:1176-1213): a [1, hidden] BF16 matrix
+ * whose BF16 logit gates the shared expert under URB_NUMERICS_QWEN36.  The matrix must outlive the
+ * layer; NULL detaches it. */
+URB_API int urb_moe_layer_set_shared_expert_gate(urb_ctx *ctx, urb_layer *layer, const urb_mat *gate);
 URB_API int urb_moe_layer_create_sharded(urb_ctx *ctx, const urb_mat *router, const float *bias,
                                          size_t experts, size_t expert_begin, size_t expert_count,
                                          const urb_mat *const *gate, const urb_mat *const *up,

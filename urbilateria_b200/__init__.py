@@ -22,7 +22,7 @@ __all__ = [
     "UrbError", "MxError", "Context", "MxFp4Matrix", "MxFp8Matrix", "Bf16Matrix", "DenseMatrix",
     "GatedMlp", "RouteChoice", "MoeGeometry", "route_noaux_tc", "route_softmax_top_k",
     "group_routes", "RuntimeMoeLayer", "default_context", "simulate_e4m3_activation",
-    "route_sqrt_softplus",
+    "route_sqrt_softplus", "simulate_finegrained_e4m3_activation", "linear_bf16_fp32_lanes",
 ]
 
 
@@ -352,6 +352,27 @@ def simulate_e4m3_activation(values, block_size: int, ctx: Optional[Context] = N
     return out
 
 
+def simulate_finegrained_e4m3_activation(values, block_size: int,
+                                         ctx: Optional[Context] = None) -> np.ndarray:
+    """simulate_finegrained_e4m3_activation (src/math/mxfp.rs:122-149) on the device."""
+    ctx = ctx or default_context()
+    v = np.ascontiguousarray(values, dtype=np.float32).ravel()
+    out = np.empty_like(v)
+    ctx.check(ctx.lib.urb_simulate_finegrained_e4m3_activation(
+        ctx.h, _ptr(v) if v.size else None, v.size, block_size, _ptr(out) if v.size else None))
+    return out
+
+
+def linear_bf16_fp32_lanes(matrix: "Bf16Matrix", x, tokens: int) -> np.ndarray:
+    """The Qwen3.6 BF16 linear (qwen3_8/math.rs:10-26, dot_bf16_fp32_avx2_fma of
+    src/model/bf16.rs:591-613, rounded to BF16) of x [tokens, cols]: [tokens, rows]."""
+    ctx = matrix.ctx
+    x = np.ascontiguousarray(x, dtype=np.float32).ravel()
+    out = np.empty((tokens, matrix.rows()), dtype=np.float32)
+    ctx.check(ctx.lib.urb_linear_bf16_fp32_lanes(ctx.h, matrix.h, _ptr(x), tokens, _ptr(out)))
+    return out
+
+
 def group_routes(expert_ids, experts: int, ctx: Optional[Context] = None):
     """Ragged grouping (src/models/qwen3_6/runtime.rs:1083-1132): experts ascending, tokens
     ascending.  Returns (counts, offsets, perm_token, perm_slot)."""
@@ -365,6 +386,10 @@ def group_routes(expert_ids, experts: int, ctx: Optional[Context] = None):
     ctx.check(ctx.lib.urb_group_routes(ctx.h, _ptr(ids), t, k, experts, _ptr(counts),
                                        _ptr(offsets), _ptr(pt), _ptr(ps)))
     return counts, offsets, pt[:t * k], ps[:t * k]
+
+
+_NUMERICS = {"glm": native.NUMERICS_GLM, "deepseek_v4": native.NUMERICS_DEEPSEEK_V4,
+             "qwen36": native.NUMERICS_QWEN36}
 
 
 class RuntimeMoeLayer:
@@ -408,6 +433,13 @@ class RuntimeMoeLayer:
                 self._u, self._d, sg, su, sd, ctypes.byref(self._geo), ctypes.byref(h)))
         self.h = h
 
+    def set_shared_expert_gate(self, gate: Optional[_Matrix]) -> None:
+        """Attach the Qwen3.6 shared_expert_gate, a [1, hidden] BF16 matrix (kept alive by the
+        layer), or detach it with None."""
+        self.ctx.check(self.ctx.lib.urb_moe_layer_set_shared_expert_gate(
+            self.ctx.h, self.h, gate.h if gate is not None else None))
+        self._shared_expert_gate = gate
+
     def hidden_size(self) -> int:
         return self.router.cols()
 
@@ -440,14 +472,13 @@ class RuntimeMoeLayer:
                        swiglu_limit: float = 0.0) -> np.ndarray:
         """Experts half of the forward for caller-chosen routes ([tokens, top_k] ids and
         weights, e.g. from route_softmax_top_k): grouped SwiGLU experts + combine.  numerics
-        "glm" (f64 combine in route order) or "deepseek_v4" (urb_moe_numerics)."""
+        "glm" (f64 combine in route order), "deepseek_v4" or "qwen36" (urb_moe_numerics)."""
         K = self.geometry.top_k
         x = np.ascontiguousarray(x, dtype=np.float32).ravel()
         ids = np.ascontiguousarray(expert_ids, dtype=np.int32).reshape(tokens, K)
         w = np.ascontiguousarray(weights, dtype=np.float32).reshape(tokens, K)
         out = np.empty((tokens, self.hidden_size()), dtype=np.float32)
-        mode = {"glm": native.NUMERICS_GLM, "deepseek_v4": native.NUMERICS_DEEPSEEK_V4}[numerics]
-        num = native.Numerics(mode, swiglu_limit)
+        num = native.Numerics(_NUMERICS[numerics], swiglu_limit)
         self.ctx.check(self.ctx.lib.urb_moe_forward_routed_ex(
             self.ctx.h, self.h, _ptr(x), tokens, _ptr(ids), _ptr(w), ctypes.byref(num),
             _ptr(out)))
@@ -455,17 +486,18 @@ class RuntimeMoeLayer:
 
     def forward_ex(self, x, tokens: int, numerics: str = "glm", swiglu_limit: float = 0.0,
                    hash_experts=None):
-        """The layer forward with checkpoint numerics (urb_moe_forward_ex): "glm", or
+        """The layer forward with checkpoint numerics (urb_moe_forward_ex): "glm",
         "deepseek_v4" (route_sqrt_softplus routing, or fixed `hash_experts` [tokens, top_k],
-        and the DeepSeek-V4 expert numerics).  Returns (out, expert ids, weights)."""
+        and the DeepSeek-V4 expert numerics) or "qwen36" (BF16 router, softmax top-k with
+        BF16 weights, the Qwen3.6 expert numerics and the gated shared expert).  Returns (out,
+        expert ids, weights)."""
         K = self.geometry.top_k
         x = np.ascontiguousarray(x, dtype=np.float32).ravel()
         out = np.empty((tokens, self.hidden_size()), dtype=np.float32)
         ids = np.empty((tokens, K), dtype=np.int32)
         w = np.empty((tokens, K), dtype=np.float32)
         h = None if hash_experts is None else np.ascontiguousarray(hash_experts, dtype=np.int32)
-        mode = {"glm": native.NUMERICS_GLM, "deepseek_v4": native.NUMERICS_DEEPSEEK_V4}[numerics]
-        num = native.Numerics(mode, swiglu_limit)
+        num = native.Numerics(_NUMERICS[numerics], swiglu_limit)
         self.ctx.check(self.ctx.lib.urb_moe_forward_ex(
             self.ctx.h, self.h, _ptr(x), tokens, ctypes.byref(num), _ptr(h), _ptr(out), _ptr(ids),
             _ptr(w)))

@@ -10,13 +10,9 @@
 #pragma once
 #include <stdint.h>
 
-namespace urb {
+#include "urb_internal.cuh"
 
-struct ExpfTable {
-    const uint32_t *keys;
-    const uint32_t *vals;
-    const uint32_t *index;
-};
+namespace urb {
 
 // expf_libm with the bucket's key range [lo, hi) already loaded from t.index.
 __device__ __forceinline__ float expf_libm_range(float x, const ExpfTable &t, uint32_t lo,

@@ -479,7 +479,8 @@ __global__ void __launch_bounds__(kThreadsBs, 1) k_bs_grouped(TcArgs a) {
                             float o = 0.0f;
 #pragma unroll
                             for (int e = 0; e < TT; ++e) o += __uint_as_float(v[i][RT * s + e]);
-                            if (a.variant == 1) o = num_round_bf16(o);
+                            if (a.variant != 0) o = num_round_bf16(o);
+                            if (a.variant == 2 && !isfinite(o)) set_status(a.status, URB_ERR_NONFINITE);
                             dst[S.out_off + gr] = o;
                         }
                     }
@@ -502,6 +503,10 @@ __global__ void __launch_bounds__(kThreadsBs, 1) k_bs_grouped(TcArgs a) {
                         if (a.variant == 1) {
                             h = num_bounded_swiglu(num_round_bf16(gv), num_round_bf16(uv), a.limit);
                             h = num_round_bf16(__fmul_rn(h, a.col_w[col]));
+                            if (!isfinite(h)) set_status(a.status, URB_ERR_NONFINITE);
+                        } else if (a.variant == 2) {
+                            const float act = num_round_bf16(num_silu_libm(num_round_bf16(gv), a.expf));
+                            h = num_round_bf16(__fmul_rn(act, num_round_bf16(uv)));
                             if (!isfinite(h)) set_status(a.status, URB_ERR_NONFINITE);
                         } else {
                             h = silu_f(gv) * uv;
@@ -530,7 +535,8 @@ __global__ void __launch_bounds__(kThreadsBs, 1) k_bs_grouped(TcArgs a) {
                         } else {
                             dst = a.out + size_t(a.out_ranks ? col - a.routed_cols : col) * a.out_stride;
                         }
-                        if (a.variant == 1) o = num_round_bf16(o);
+                        if (a.variant != 0) o = num_round_bf16(o);
+                        if (a.variant == 2 && !isfinite(o)) set_status(a.status, URB_ERR_NONFINITE);
                         dst[S.out_off + grow] = o;
                     }
                 }
@@ -665,9 +671,14 @@ __global__ void __launch_bounds__(256) k_bs_prep(TcArgs a) {
         for (int i = 0; i < 8; ++i) m = fmaxf(m, fabsf(r[i]));
 #pragma unroll
         for (int o = 1; o < 16; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-        const float scale = num_e4m3_scale(m);
+        if (a.sim128 == 1) {
+            const float scale = num_e4m3_scale(m);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) r[i] = num_e4m3_sim(r[i], scale);
+            for (int i = 0; i < 8; ++i) r[i] = num_e4m3_sim(r[i], scale);
+        } else {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) r[i] = num_e4m3_sim_fine(r[i], m);
+        }
     }
     uint32_t q[TT][QW];
     int sb[TT];

@@ -75,7 +75,7 @@ int moe_forward_device(Layer *L, const float *d_x, int T, float *d_out, MoeWork 
     const size_t TK = size_t(T) * K, cols = TK + T;
     const size_t nseg = max_segments(T, K, E);
     size_t need = T * 4 + T * E * 4 + TK * 12 + E * 8 + 8 + TK * 12 + 2 * nseg * sizeof(Seg) +
-                  64 + cols * 8 + cols * I * 4 + cols * H * 4 + 32 * 256;
+                  64 + cols * 8 + cols * I * 4 + cols * H * 4 + T * 4 + 33 * 256;
     int rc;
     uint8_t *ws = static_cast<uint8_t *>(workspace(ctx, need, &rc));
     if (!ws) return rc;
@@ -103,10 +103,23 @@ int moe_forward_device(Layer *L, const float *d_x, int T, float *d_out, MoeWork 
     w.y = cv.take<float>(cols * H);
     w.lofree = cv.take<int32_t>(1);
     w.col_w = cv.take<float>(cols);
+    float *gate_logit = cv.take<float>(T);
     const bool deepseek = num && num->mode == URB_NUMERICS_DEEPSEEK_V4;
+    const bool qwen = num && num->mode == URB_NUMERICS_QWEN36;
     if (deepseek && (!L->use_tc || !d_ids_in))
         return set_error(ctx, URB_ERR_UNSUPPORTED,
                          "DeepSeek-V4 numerics run on the tensor-core passes with caller routes");
+    if (qwen) {
+        // Qwen3.6: MX experts need the E4M3 simulation of the tensor-core prep; BF16 experts
+        // run on the mma.sync passes.
+        if (!d_ids_in || !L->sg || !L->shared_gate_row)
+            return set_error(ctx, URB_ERR_UNSUPPORTED,
+                             "Qwen3.6 numerics need caller routes, a shared expert and its gate");
+        if (!L->use_tc && L->fmt != URB_FMT_BF16)
+            return set_error(ctx, URB_ERR_UNSUPPORTED,
+                             "Qwen3.6 numerics run MX experts on the tensor-core passes");
+        if (K > 16) return set_error(ctx, URB_ERR_UNSUPPORTED, "Qwen3.6 combine takes top_k <= 16");
+    }
     const size_t ngrp_gu = 2 * std::min(TK, E) + 2, ngrp_dn = std::min(TK, E) + 1;
     const size_t sc = size_t(bs_stage_cols(L->fmt));
     const size_t ks_gu = div_ceil(H, sc), ks_dn = div_ceil(I, sc);
@@ -145,6 +158,16 @@ int moe_forward_device(Layer *L, const float *d_x, int T, float *d_out, MoeWork 
         prof_end(ctx, st);
         if (rc) return cuda_fail(ctx, cudaGetLastError(), "row shift");
     }
+    if (qwen && !num->gate_logit) {
+        // The shared expert's BF16 gate logit per token (qwen3_6/runtime.rs:1176-1186).
+        prof_begin(ctx, URB_K_ROUTER_LOGITS, st);
+        rc = launch_router_bf16_lanes(nullptr, 0,
+                                      static_cast<const uint16_t *>(L->shared_gate_row->raw_values),
+                                      d_x, T, int(H), nullptr, gate_logit, d_status, st);
+        prof_end(ctx, st);
+        if (rc) return cuda_fail(ctx, cudaGetLastError(), "shared expert gate");
+    }
+    const float *d_gate_logit = qwen ? (num->gate_logit ? num->gate_logit : gate_logit) : nullptr;
     if (d_ids_in) {
         // Routes chosen by the caller: the grouping validates the expert ids.
         w.ids = const_cast<int32_t *>(d_ids_in);
@@ -268,6 +291,10 @@ int moe_forward_device(Layer *L, const float *d_x, int T, float *d_out, MoeWork 
             ga.sim128 = 1;
             ga.limit = num->limit;
             ga.col_w = w.col_w;
+        } else if (qwen) {
+            ga.variant = 2;
+            ga.sim128 = 2;
+            ga.expf = expf_table_of(ctx);
         }
         ga.out = w.h;
         ga.out_stride = int(I);
@@ -286,9 +313,9 @@ int moe_forward_device(Layer *L, const float *d_x, int T, float *d_out, MoeWork 
         da.src_stride = int(I);
         da.nrows = int(L->sg ? TK + T : TK);
         da.pair = 2;  // neighbouring row tiles share each activation stage
-        if (deepseek) {
-            da.variant = 1;
-            da.sim128 = 1;
+        if (deepseek || qwen) {
+            da.variant = deepseek ? 1 : 2;
+            da.sim128 = deepseek ? 1 : 2;
         }
         da.cols = int(I);
         da.ks = int(ks_dn);
@@ -303,6 +330,9 @@ int moe_forward_device(Layer *L, const float *d_x, int T, float *d_out, MoeWork 
         if (deepseek)
             rc = launch_combine_deepseek(ctx, w.y, L->sg ? w.y + TK * H : nullptr, w.ids, w.inv, T,
                                          int(K), int(H), d_out, st, d_status);
+        else if (qwen)
+            rc = launch_combine_qwen(ctx, w.y, w.y + TK * H, w.ids, w.w, w.inv, d_gate_logit, T,
+                                     int(K), int(H), d_out, st, d_status);
         else
             rc = launch_combine(ctx, w.y, L->sg ? w.y + TK * H : nullptr, w.w, w.inv, T, int(K),
                                 int(H), d_out, st, d_status);
@@ -330,6 +360,11 @@ int moe_forward_device(Layer *L, const float *d_x, int T, float *d_out, MoeWork 
     gu.out_maxexp = w.maxexp;
     gu.hilo = 1;
     gu.lofree = w.lofree;  // bf16-exact tokens: 8 per segment in one f16 column each
+    if (qwen) {
+        gu.variant = 2;
+        gu.status = d_status;
+        gu.expf = expf_table_of(ctx);
+    }
     prof_begin(ctx, URB_K_GATE_UP, st);
     rc = launch_grouped_ex(ctx, L->fmt, true, ksplit, gu, 2 * kCap, g0->kslices, st);
     prof_end(ctx, st);
@@ -347,6 +382,10 @@ int moe_forward_device(Layer *L, const float *d_x, int T, float *d_out, MoeWork 
     dn.out = w.y;
     dn.out_stride = int(H);
     dn.hilo = 1;
+    if (qwen) {
+        dn.variant = 2;
+        dn.status = d_status;
+    }
     prof_begin(ctx, URB_K_DOWN, st);
     rc = launch_grouped_ex(ctx, L->fmt, false, ksplit == 8 ? 2 : ksplit, dn, 4 * kCap,
                            d0->kslices, st);
@@ -354,8 +393,12 @@ int moe_forward_device(Layer *L, const float *d_x, int T, float *d_out, MoeWork 
     if (rc) return rc;
 
     prof_begin(ctx, URB_K_COMBINE, st);
-    rc = launch_combine(ctx, w.y, L->sg ? w.y + TK * H : nullptr, w.w, w.inv, T, int(K), int(H),
-                        d_out, st, d_status);
+    if (qwen)
+        rc = launch_combine_qwen(ctx, w.y, w.y + TK * H, w.ids, w.w, w.inv, d_gate_logit, T,
+                                 int(K), int(H), d_out, st, d_status);
+    else
+        rc = launch_combine(ctx, w.y, L->sg ? w.y + TK * H : nullptr, w.w, w.inv, T, int(K),
+                            int(H), d_out, st, d_status);
     prof_end(ctx, st);
     if (rc) return rc;
     if (wout) *wout = w;
@@ -630,6 +673,10 @@ int urb_moe_forward(urb_ctx *ctx, urb_layer *L, const float *x, size_t tokens, f
 static int numerics_of(urb_ctx *ctx, const urb_moe_numerics *n, Numerics *out) {
     if (!n) return URB_OK;
     if (n->mode == URB_NUMERICS_GLM) return URB_OK;
+    if (n->mode == URB_NUMERICS_QWEN36) {
+        out->mode = n->mode;
+        return URB_OK;
+    }
     if (n->mode != URB_NUMERICS_DEEPSEEK_V4)
         return set_error(ctx, URB_ERR_INVALID_ARGUMENT, "unknown numerics mode");
     // validate_positive("SwiGLU limit") of deepseek_v4/math.rs:531.
@@ -739,6 +786,16 @@ int urb_moe_forward_ex(urb_ctx *ctx, urb_layer *L, const float *x, size_t tokens
         return set_error(ctx, URB_ERR_UNSUPPORTED, "an expert shard runs through urb_ep_forward");
     std::lock_guard<std::recursive_mutex> lk(ctx->mu);
     cudaSetDevice(ctx->device);
+    const bool qwen = num.mode == URB_NUMERICS_QWEN36;
+    if (qwen) {
+        if (hash_experts)
+            return set_error(ctx, URB_ERR_INVALID_ARGUMENT, "hash routing needs the DeepSeek-V4 numerics");
+        if (L->router->format != URB_FMT_BF16 || !L->router->raw_values)
+            return set_error(ctx, URB_ERR_UNSUPPORTED, "Qwen3.6 numerics need a BF16 router");
+        if (!L->sg || !L->shared_gate_row)
+            return set_error(ctx, URB_ERR_UNSUPPORTED,
+                             "Qwen3.6 numerics need a shared expert and its gate");
+    }
     if (tokens == 0) return URB_OK;
     const size_t H = L->hidden, K = L->geo.top_k, E = L->experts, TK = tokens * K;
     if (hash_experts)
@@ -754,7 +811,8 @@ int urb_moe_forward_ex(urb_ctx *ctx, urb_layer *L, const float *x, size_t tokens
     const size_t o_x64 = align(o_l + tokens * E * 4);
     const size_t o_ids = align(o_x64 + router_f64_elems(int(tokens), int(H)) * 8);
     const size_t o_w = align(o_ids + TK * 4), o_s = align(o_w + TK * 4), o_h = align(o_s + TK * 4);
-    const size_t bytes = align(o_h + TK * 4);
+    const size_t o_g = align(o_h + TK * 4);
+    const size_t bytes = align(o_g + tokens * 4);
     uint8_t *d = nullptr;
     URB_CUDA(ctx, cudaMallocAsync(&d, bytes, st));
     float *d_x = reinterpret_cast<float *>(d + o_x), *d_out = reinterpret_cast<float *>(d + o_out);
@@ -765,16 +823,34 @@ int urb_moe_forward_ex(urb_ctx *ctx, urb_layer *L, const float *x, size_t tokens
     URB_CUDA(ctx, cudaMemsetAsync(ctx->d_status, 0, 4, st));
     URB_CUDA(ctx, cudaMemcpyAsync(d_x, x, tokens * H * 4, cudaMemcpyDefault, st));
     if (hash_experts) URB_CUDA(ctx, cudaMemcpyAsync(d_hash, hash_experts, TK * 4, cudaMemcpyDefault, st));
-    const RouterGates rg{ctx, nullptr, nullptr, nullptr, ctx->d_status};
-    prof_begin(ctx, URB_K_ROUTER_LOGITS, st);
-    int rc = launch_router_logits_f64(L->router64, int(E), d_x, int(tokens), int(H), d_x64, d_l, st, &rg);
-    prof_end(ctx, st);
-    if (rc) { cudaFreeAsync(d, st); return cuda_fail(ctx, cudaGetLastError(), "router logits"); }
-    prof_begin(ctx, URB_K_ROUTE, st);
-    rc = launch_route_sqrt_softplus(ctx, d_l, L->d_bias, hash_experts ? d_hash : nullptr,
-                                    int(tokens), int(E), int(K), L->geo.routed_scaling_factor,
-                                    d_ids, d_w, d_s, ctx->d_status, st);
-    prof_end(ctx, st);
+    int rc;
+    if (qwen) {
+        // execute_batched_moe (qwen3_6/runtime.rs:1067-1090): BF16 router and shared-expert gate
+        // logits in one launch, route_softmax_top_k with BF16 weights.
+        float *d_g = reinterpret_cast<float *>(d + o_g);
+        prof_begin(ctx, URB_K_ROUTER_LOGITS, st);
+        rc = launch_router_bf16_lanes(static_cast<const uint16_t *>(L->router->raw_values), int(E),
+                                      static_cast<const uint16_t *>(L->shared_gate_row->raw_values),
+                                      d_x, int(tokens), int(H), d_l, d_g, ctx->d_status, st);
+        prof_end(ctx, st);
+        if (rc) { cudaFreeAsync(d, st); return cuda_fail(ctx, cudaGetLastError(), "router logits"); }
+        prof_begin(ctx, URB_K_ROUTE, st);
+        rc = launch_route_softmax(ctx, d_l, int(tokens), int(E), int(K), d_ids, d_w, ctx->d_status,
+                                  st, 1);
+        prof_end(ctx, st);
+        num.gate_logit = d_g;
+    } else {
+        const RouterGates rg{ctx, nullptr, nullptr, nullptr, ctx->d_status};
+        prof_begin(ctx, URB_K_ROUTER_LOGITS, st);
+        rc = launch_router_logits_f64(L->router64, int(E), d_x, int(tokens), int(H), d_x64, d_l, st, &rg);
+        prof_end(ctx, st);
+        if (rc) { cudaFreeAsync(d, st); return cuda_fail(ctx, cudaGetLastError(), "router logits"); }
+        prof_begin(ctx, URB_K_ROUTE, st);
+        rc = launch_route_sqrt_softplus(ctx, d_l, L->d_bias, hash_experts ? d_hash : nullptr,
+                                        int(tokens), int(E), int(K), L->geo.routed_scaling_factor,
+                                        d_ids, d_w, d_s, ctx->d_status, st);
+        prof_end(ctx, st);
+    }
     if (rc == URB_OK)
         rc = moe_forward_device(L, d_x, int(tokens), d_out, nullptr, ctx->d_status, st, d_ids,
                                 d_w, &num);
@@ -793,6 +869,17 @@ int urb_moe_forward_ex(urb_ctx *ctx, urb_layer *L, const float *x, size_t tokens
 int urb_moe_forward_routed(urb_ctx *ctx, urb_layer *L, const float *x, size_t tokens,
                            const int32_t *route_expert, const float *route_weight, float *out) {
     return urb_moe_forward_routed_ex(ctx, L, x, tokens, route_expert, route_weight, nullptr, out);
+}
+
+int urb_moe_layer_set_shared_expert_gate(urb_ctx *ctx, urb_layer *L, const urb_mat *gate) {
+    if (!ctx || !L) return URB_ERR_INVALID_ARGUMENT;
+    std::lock_guard<std::recursive_mutex> lk(ctx->mu);
+    if (gate && (gate->rows != 1 || gate->cols != L->hidden))
+        return set_error(ctx, URB_ERR_SHAPE, "shared expert gate must be [1, hidden]");
+    if (gate && (gate->format != URB_FMT_BF16 || !gate->raw_values))
+        return set_error(ctx, URB_ERR_UNSUPPORTED, "shared expert gate must be a BF16 matrix");
+    L->shared_gate_row = gate;
+    return URB_OK;
 }
 
 int urb_gated_mlp_forward(urb_ctx *ctx, const urb_mat *g, const urb_mat *u, const urb_mat *d,

@@ -7,6 +7,7 @@
 // (src/models/qwen3_6/runtime.rs:1123-1132), each expert's token run is one or more segments of
 // a grouped pass, and the combine adds the route-weighted expert outputs per token in the
 // reference's selection order with f64 accumulation.
+#include "numerics.cuh"
 #include "urb_internal.cuh"
 #include "urb_moe_internal.cuh"
 
@@ -232,6 +233,49 @@ __global__ void k_combine_deepseek(const float *y, const float *shared_y, const 
     out[size_t(t) * hidden + h] = r;
 }
 
+// MoE output of the Qwen3.6 numerics (execute_batched_moe, qwen3_6/runtime.rs:1123-1213):
+// routed contributions BF16(BF16(w) * y) accumulated from +0.0 in ascending expert id (stable
+// for repeated ids), each sum rounded to BF16; then the shared expert's BF16(s * y_shared)
+// with s = BF16(sigmoid(gate logit)) evaluated as 1 / (1 + exp(-g)) for g >= 0 and
+// exp(g) / (1 + exp(g)) otherwise (libm expf); the final sum rounded to BF16.
+__global__ void k_combine_qwen(const float *y, const float *shared_y, const int32_t *ids,
+                               const float *w, const int32_t *inv, const float *gate_logit,
+                               ExpfTable tab, int tokens, int top_k, int hidden, float *out,
+                               int32_t *status) {
+    if (*status) return;
+    const int t = blockIdx.y;
+    const int h = blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= tokens || h >= hidden) return;
+    int order[16];
+    for (int k = 0; k < top_k; ++k) {  // stable insertion by expert id
+        const int id = ids[t * top_k + k];
+        int j = k;
+        while (j > 0 && ids[t * top_k + order[j - 1]] > id) { order[j] = order[j - 1]; --j; }
+        order[j] = k;
+    }
+    float acc = 0.0f;
+    for (int j = 0; j < top_k; ++j) {
+        const int r = t * top_k + order[j];
+        const float c = num_round_bf16(__fmul_rn(num_round_bf16(w[r]), y[size_t(inv[r]) * hidden + h]));
+        acc = num_round_bf16(__fadd_rn(acc, c));
+    }
+    if (shared_y) {
+        const float g = gate_logit[t];
+        float s;
+        if (g >= 0.0f) {
+            s = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf_libm(-g, tab)));
+        } else {
+            const float e = expf_libm(g, tab);
+            s = __fdiv_rn(e, __fadd_rn(1.0f, e));
+        }
+        s = num_round_bf16(s);
+        const float c = num_round_bf16(__fmul_rn(s, shared_y[size_t(t) * hidden + h]));
+        acc = num_round_bf16(__fadd_rn(acc, c));
+    }
+    if (!isfinite(acc)) atomicCAS(status, 0, int32_t(URB_ERR_NONFINITE));
+    out[size_t(t) * hidden + h] = acc;
+}
+
 // Groups of the tensor-core passes (single CTA).  Gate/up pass: per routed expert with tokens
 // one paired group (gate and up tiles against the same activation stages), then the shared
 // expert's; down pass: one group per routed expert, then the shared expert.  A group of c tokens has ceil(c / bs_cap) sub-segments; its units are mts * nsub.
@@ -414,6 +458,18 @@ int launch_combine_deepseek(Ctx *ctx, const float *y, const float *shared_y, con
     dim3 grid(unsigned((hidden + 255) / 256), unsigned(tokens));
     k_combine_deepseek<<<grid, 256, 0, st>>>(y, shared_y, ids, inv, tokens, top_k, hidden, out,
                                              status);
+    URB_CUDA(ctx, cudaGetLastError());
+    return URB_OK;
+}
+
+int launch_combine_qwen(Ctx *ctx, const float *y, const float *shared_y, const int32_t *ids,
+                        const float *w, const int32_t *inv, const float *gate_logit, int tokens,
+                        int top_k, int hidden, float *out, cudaStream_t st, int32_t *status) {
+    if (tokens <= 0) return URB_OK;
+    if (top_k > 16) return set_error(ctx, URB_ERR_UNSUPPORTED, "Qwen3.6 combine takes top_k <= 16");
+    dim3 grid(unsigned((hidden + 255) / 256), unsigned(tokens));
+    k_combine_qwen<<<grid, 256, 0, st>>>(y, shared_y, ids, w, inv, gate_logit, expf_table_of(ctx),
+                                         tokens, top_k, hidden, out, status);
     URB_CUDA(ctx, cudaGetLastError());
     return URB_OK;
 }

@@ -5,8 +5,14 @@
 //  * round_to_bf16 (deepseek_v4/math.rs:90-101): round to nearest even on the upper 16 bits;
 //  * bounded SwiGLU (deepseek_v4/math.rs:518-549): min(g, L) / (1 + exp(-min(g, L))) *
 //    clamp(u, -L, L).
+// and of the Qwen3.6 expert path:
+//  * fine-grained E4M3 activation simulation (src/math/mxfp.rs:122-149): per block the exact
+//    scale max|v| / 448, v -> decode(encode(v / scale)) * scale; all-zero blocks stay zero;
+//  * silu (src/math/ops.rs:36-38) with the libm expf: v / (1 + exp(-v)).
 #pragma once
 #include <stdint.h>
+
+#include "expf_glibc.cuh"
 
 namespace urb {
 
@@ -64,6 +70,17 @@ __device__ __forceinline__ float num_e4m3_sim(float v, float scale) {
 // Block scale of the simulation from the block's max |v| (the fold starts at 1e-4).
 __device__ __forceinline__ float num_e4m3_scale(float amax) {
     return num_pow2_ceil(__fdiv_rn(fmaxf(amax, 1.0e-4f), 448.0f));
+}
+
+// Fine-grained E4M3 round trip of one value of a block whose max |v| is amax.
+__device__ __forceinline__ float num_e4m3_sim_fine(float v, float amax) {
+    if (amax == 0.0f) return 0.0f;
+    const float scale = __fdiv_rn(amax, 448.0f);
+    return __fmul_rn(num_e4m3_decode(num_e4m3_encode(__fdiv_rn(v, scale))), scale);
+}
+
+__device__ __forceinline__ float num_silu_libm(float v, const ExpfTable &tab) {
+    return __fdiv_rn(v, __fadd_rn(1.0f, expf_libm(-v, tab)));
 }
 
 __device__ __forceinline__ float num_round_bf16(float v) {

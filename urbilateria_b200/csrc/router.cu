@@ -14,6 +14,7 @@
 //    (src/models/qwen3_8/moe.rs:91-159): one warp per token, IEEE f32 arithmetic in the
 //    reference's order, libm-exact expf, total_cmp ranking with the lower id winning ties.
 #include "expf_glibc.cuh"
+#include "numerics.cuh"
 #include "tc_common.cuh"
 #include "urb_internal.cuh"
 
@@ -316,7 +317,8 @@ __global__ void k_route_noaux(const float *logits, const float *bias, int tokens
 
 // route_softmax_top_k (src/models/qwen3_8/moe.rs:108-158).  One warp per token.
 __global__ void k_route_softmax(const float *logits, int tokens, int E, int top_k,
-                                ExpfTable tab, int32_t *out_e, float *out_w, int32_t *status) {
+                                ExpfTable tab, int32_t *out_e, float *out_w, int32_t *status,
+                                int bf16_weights) {
     extern __shared__ __align__(16) uint8_t smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int t = blockIdx.x * (blockDim.x >> 5) + warp;
@@ -373,9 +375,83 @@ __global__ void k_route_softmax(const float *logits, int tokens, int E, int top_
         return;
     }
     for (int r = lane; r < top_k; r += 32) {
-        const float w = __fdiv_rn(p[oe[r]], selected);
+        float w = __fdiv_rn(p[oe[r]], selected);
+        if (bf16_weights) w = num_round_bf16(w);
         if (!isfinite(w)) set_status(status, URB_ERR_NONFINITE);
         out_w[size_t(t) * top_k + r] = w;
+    }
+}
+
+// BF16 linear of the Qwen3.6 router and shared-expert gate (qwen3_8/math.rs:10-26 over
+// dot_bf16_fp32_avx2_fma, src/model/bf16.rs:591-613).  Per output: eight FMA lanes from +0.0,
+// column c in lane c % 8 over the largest multiple of eight columns; the lanes summed in order
+// from -0.0; the remaining columns added as separately rounded products; the sum rounded to
+// BF16.  One thread per (row, 4 tokens) keeps all 32 chains in registers; row `rows` is the
+// gate row.  VEC: 16-byte weight and activation loads (cols % 8 == 0, aligned bases).
+template <bool VEC>
+__global__ void __launch_bounds__(128) k_router_bf16_lanes(const uint16_t *w, int rows,
+                                                           const uint16_t *gate_row,
+                                                           const float *x, int tokens, int cols,
+                                                           float *logits, float *gate_logit,
+                                                           int32_t *status) {
+    constexpr int TT = 4;
+    const int r = blockIdx.x * blockDim.x + threadIdx.x;
+    if (r >= rows + (gate_row ? 1 : 0)) return;
+    const int t0 = blockIdx.y * TT;
+    const uint16_t *wr = r < rows ? w + size_t(r) * cols : gate_row;
+    const float *xr[TT];
+#pragma unroll
+    for (int i = 0; i < TT; ++i) xr[i] = x + size_t(min(t0 + i, tokens - 1)) * cols;
+    const int complete = cols / 8 * 8;
+    float acc[TT][8];
+#pragma unroll
+    for (int i = 0; i < TT; ++i)
+#pragma unroll
+        for (int l = 0; l < 8; ++l) acc[i][l] = 0.0f;
+    for (int c = 0; c < complete; c += 8) {
+        float wv[8];
+        if (VEC) {
+            const uint4 q = *reinterpret_cast<const uint4 *>(wr + c);
+            const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                wv[2 * j] = __uint_as_float(qw[j] << 16);
+                wv[2 * j + 1] = __uint_as_float(qw[j] & 0xffff0000u);
+            }
+        } else {
+#pragma unroll
+            for (int l = 0; l < 8; ++l) wv[l] = __uint_as_float(uint32_t(wr[c + l]) << 16);
+        }
+#pragma unroll
+        for (int i = 0; i < TT; ++i) {
+            float xv[8];
+            if (VEC) {
+                const float4 a = *reinterpret_cast<const float4 *>(xr[i] + c);
+                const float4 b = *reinterpret_cast<const float4 *>(xr[i] + c + 4);
+                xv[0] = a.x; xv[1] = a.y; xv[2] = a.z; xv[3] = a.w;
+                xv[4] = b.x; xv[5] = b.y; xv[6] = b.z; xv[7] = b.w;
+            } else {
+#pragma unroll
+                for (int l = 0; l < 8; ++l) xv[l] = xr[i][c + l];
+            }
+#pragma unroll
+            for (int l = 0; l < 8; ++l) acc[i][l] = fmaf(wv[l], xv[l], acc[i][l]);
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < TT; ++i) {
+        if (t0 + i >= tokens) break;
+        float s = -0.0f;
+#pragma unroll
+        for (int l = 0; l < 8; ++l) s = __fadd_rn(s, acc[i][l]);
+        for (int c = complete; c < cols; ++c)
+            s = __fadd_rn(s, __fmul_rn(__uint_as_float(uint32_t(wr[c]) << 16), xr[i][c]));
+        s = num_round_bf16(s);
+        if (!isfinite(s)) set_status(status, URB_ERR_NONFINITE);
+        if (r < rows)
+            logits[size_t(t0 + i) * rows + r] = s;
+        else
+            gate_logit[t0 + i] = s;
     }
 }
 
@@ -540,14 +616,34 @@ int launch_route_sqrt_softplus(Ctx *ctx, const float *d_logits, const float *d_b
 
 int launch_route_softmax(Ctx *ctx, const float *d_logits, int tokens, int experts, int top_k,
                          int32_t *d_expert, float *d_weight, int32_t *d_status,
-                         cudaStream_t st) {
+                         cudaStream_t st, int bf16_weights) {
     if (tokens <= 0) return URB_OK;
     int warps = 4;
     size_t smem = size_t(warps) * experts * 5;
     k_route_softmax<<<(tokens + warps - 1) / warps, warps * 32, smem, st>>>(
-        d_logits, tokens, experts, top_k, table_of(ctx), d_expert, d_weight, d_status);
+        d_logits, tokens, experts, top_k, table_of(ctx), d_expert, d_weight, d_status,
+        bf16_weights);
     URB_CUDA(ctx, cudaGetLastError());
     return URB_OK;
+}
+
+int launch_router_bf16_lanes(const uint16_t *w, int rows, const uint16_t *gate_row,
+                             const float *d_x, int tokens, int cols, float *d_logits,
+                             float *d_gate_logit, int32_t *d_status, cudaStream_t st) {
+    if (tokens <= 0) return URB_OK;
+    const int nrows = rows + (gate_row ? 1 : 0);
+    if (nrows == 0) return URB_OK;
+    const dim3 grid(unsigned((nrows + 127) / 128), unsigned((tokens + 3) / 4));
+    const bool vec = cols % 8 == 0 && (reinterpret_cast<uintptr_t>(w) & 15) == 0 &&
+                     (reinterpret_cast<uintptr_t>(gate_row) & 15) == 0 &&
+                     (reinterpret_cast<uintptr_t>(d_x) & 15) == 0;
+    if (vec)
+        k_router_bf16_lanes<true><<<grid, 128, 0, st>>>(w, rows, gate_row, d_x, tokens, cols,
+                                                        d_logits, d_gate_logit, d_status);
+    else
+        k_router_bf16_lanes<false><<<grid, 128, 0, st>>>(w, rows, gate_row, d_x, tokens, cols,
+                                                         d_logits, d_gate_logit, d_status);
+    return cudaGetLastError() == cudaSuccess ? URB_OK : URB_ERR_CUDA;
 }
 
 }  // namespace urb

@@ -16,6 +16,7 @@
 //  * Activations (<= 16 columns: tokens, or token hi/lo halves) are converted once per segment
 //    into shared memory in fragment order (conflict-free 8-byte loads).
 //  * Epilogue: exact power-of-two rescale, optional SwiGLU of a gate/up pair, store.
+#include "numerics.cuh"
 #include "urb_internal.cuh"
 
 namespace urb {
@@ -381,7 +382,16 @@ __global__ void __launch_bounds__(kThreads, 1) k_grouped(GroupArgs a, int kslice
                     for (int h = 0; h < 2; ++h) {
                         const bool valid = tok_ok && (h ? vg8 : vg);
                         float o = v[0][h];
-                        if (PAIR) o = silu_f(v[0][h]) * v[MATS - 1][h];
+                        if (PAIR && a.variant == 2) {  // Qwen3.6 BF16 boundaries
+                            const float act = num_round_bf16(num_silu_libm(num_round_bf16(v[0][h]), a.expf));
+                            o = num_round_bf16(__fmul_rn(act, num_round_bf16(v[MATS - 1][h])));
+                        } else if (PAIR) {
+                            o = silu_f(v[0][h]) * v[MATS - 1][h];
+                        } else if (a.variant != 0) {
+                            o = num_round_bf16(o);
+                        }
+                        if (valid && a.variant != 0 && !isfinite(o) && a.status)
+                            atomicCAS(a.status, 0, int32_t(URB_ERR_NONFINITE));
                         if (valid) {
                             orow[row_g + 8 * h] = o;
                             if (PAIR && o != 0.0f && isfinite(o)) mexp = max(mexp, ilogbf(o));

@@ -76,6 +76,14 @@ struct Seg {
     int pad;
 };
 
+// Exception table of the libm expf evaluation (expf_glibc.cuh): sorted input keys, their
+// libm results, and a bucket index over the top 20 bits of the input.
+struct ExpfTable {
+    const uint32_t *keys;
+    const uint32_t *vals;
+    const uint32_t *index;
+};
+
 // Arguments of one grouped pass.
 struct GroupArgs {
     const Seg *segs;
@@ -92,6 +100,12 @@ struct GroupArgs {
     int hilo;                 // 1: two f16/bf16 columns (hi, lo) per token
     const int *lofree;        // optional device flag: 1 -> every activation is exact in one
                               // f16/bf16 column, so the pass runs without lo columns
+    // Checkpoint numerics (0: f32 outputs).  2 (Qwen3.6): gate and up round to BF16, h =
+    // BF16(BF16(silu(gate)) * up) with the libm expf (expf); other passes round outputs to
+    // BF16.  Non-finite results set status.
+    int variant;
+    int32_t *status;
+    ExpfTable expf;
 };
 
 struct Ctx {
@@ -200,9 +214,19 @@ int launch_route_sqrt_softplus(Ctx *ctx, const float *d_logits, const float *d_b
                                const int32_t *d_hash, int tokens, int experts, int top_k,
                                float scaling, int32_t *d_expert, float *d_weight, float *d_score,
                                int32_t *d_status, cudaStream_t st);
+// bf16_weights: the selected weights round to BF16 (qwen3_6/runtime.rs:1086-1090).
 int launch_route_softmax(Ctx *ctx, const float *d_logits, int tokens, int experts, int top_k,
                          int32_t *d_expert, float *d_weight, int32_t *d_status,
-                         cudaStream_t stream);
+                         cudaStream_t stream, int bf16_weights = 0);
+// Qwen3.6 BF16 linear (dot_bf16_fp32_avx2_fma, src/model/bf16.rs:591-613, rounded to BF16):
+// logits[t, r] for the `rows` rows of w (row-major BF16 [rows, cols]) and, when gate_row is
+// set, gate_logit[t] for that [1, cols] BF16 row.  Non-finite results set status.
+int launch_router_bf16_lanes(const uint16_t *w, int rows, const uint16_t *gate_row,
+                             const float *d_x, int tokens, int cols, float *d_logits,
+                             float *d_gate_logit, int32_t *d_status, cudaStream_t st);
+inline ExpfTable expf_table_of(const Ctx *ctx) {
+    return ExpfTable{ctx->expf_keys, ctx->expf_vals, ctx->expf_index};
+}
 // expf_glibc.cu
 int expf_table_init(Ctx *ctx);
 

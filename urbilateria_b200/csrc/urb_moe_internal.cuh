@@ -59,10 +59,16 @@ int launch_combine(Ctx *ctx, const float *y, const float *shared_y, const float 
 int launch_combine_deepseek(Ctx *ctx, const float *y, const float *shared_y, const int32_t *ids,
                             const int32_t *inv, int tokens, int top_k, int hidden, float *out,
                             cudaStream_t st, int32_t *status);
+// Qwen3.6 MoE output (qwen3_6/runtime.rs:1123-1213): expert-id-order BF16 accumulation of
+// BF16(BF16(w) * y), then the shared expert scaled by BF16(sigmoid(gate_logit[t])).
+int launch_combine_qwen(Ctx *ctx, const float *y, const float *shared_y, const int32_t *ids,
+                        const float *w, const int32_t *inv, const float *gate_logit, int tokens,
+                        int top_k, int hidden, float *out, cudaStream_t st, int32_t *status);
 // Checkpoint numerics of a forward (urb_moe_numerics).
 struct Numerics {
     int mode = 0;        // URB_NUMERICS_*
     float limit = 0.0f;  // bounded-SwiGLU limit (DeepSeek-V4)
+    const float *gate_logit = nullptr;  // Qwen3.6: [T] BF16 shared-expert gate logits (device)
 };
 
 struct Layer {
@@ -77,6 +83,8 @@ struct Layer {
     int fmt = 0;
     std::vector<const Mat *> gate, up, down;
     const Mat *sg = nullptr, *su = nullptr, *sd = nullptr;
+    // Qwen3.6 shared_expert_gate: a [1, hidden] BF16 row (urb_moe_layer_set_shared_expert_gate).
+    const Mat *shared_gate_row = nullptr;
     urb_moe_geometry geo{};
     // Device pointer tables, 9 kinds of (e_count + 1) entries (held experts, then the shared
     // expert or null): gate/up/down mma tiles, their row exponents, gate/up/down bs tiles.

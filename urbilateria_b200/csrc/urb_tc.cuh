@@ -77,12 +77,17 @@ struct TcArgs {
     // (the group's units then count ceil(mts / 2) tiles each).
     int pair;
     // Checkpoint numerics (0: GLM f32 path).  1 (DeepSeek-V4): the prep simulates E4M3 per 128
-    // columns (sim128) before building terms; the gate/up epilogue rounds gate and up to BF16,
-    // applies bounded SwiGLU (limit), multiplies by the column's route weight (col_w) and
-    // rounds h to BF16; the down epilogue rounds its outputs to BF16.
+    // columns with a power-of-two scale (sim128 = 1) before building terms; the gate/up
+    // epilogue rounds gate and up to BF16, applies bounded SwiGLU (limit), multiplies by the
+    // column's route weight (col_w) and rounds h to BF16; the down epilogue rounds its outputs
+    // to BF16.  2 (Qwen3.6): the prep simulates E4M3 per 128 columns with the exact scale
+    // max|v| / 448 (sim128 = 2); the gate/up epilogue writes h = BF16(BF16(silu(BF16(gate)))
+    // * BF16(up)) with the libm expf (expf); the down epilogue rounds to BF16.  Non-finite h
+    // or outputs set status.
     int variant, sim128;
     float limit;
     const float *col_w;
+    ExpfTable expf;
     float *out;
     int out_stride;
     int32_t *status;

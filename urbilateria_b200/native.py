@@ -42,7 +42,7 @@ STATUS_NAMES = {
 }
 
 
-NUMERICS_GLM, NUMERICS_DEEPSEEK_V4 = 0, 1
+NUMERICS_GLM, NUMERICS_DEEPSEEK_V4, NUMERICS_QWEN36 = 0, 1, 2
 
 
 class Numerics(ctypes.Structure):
@@ -97,8 +97,11 @@ SIGNATURES = [
     ("urb_moe_forward_routed_ex", I32, [P, P, P, SZ, P, P, P, P]),
     ("urb_moe_forward_routed_ex_device", I32, [P, P, P, SZ, P, P, P, P, P]),
     ("urb_simulate_e4m3_activation", I32, [P, P, SZ, SZ, P]),
+    ("urb_simulate_finegrained_e4m3_activation", I32, [P, P, SZ, SZ, P]),
+    ("urb_linear_bf16_fp32_lanes", I32, [P, P, P, SZ, P]),
     ("urb_moe_forward_ex", I32, [P, P, P, SZ, P, P, P, P, P]),
     ("urb_route_sqrt_softplus", I32, [P, P, P, SZ, SZ, P, U32, ctypes.c_float, P, P, P]),
+    ("urb_moe_layer_set_shared_expert_gate", I32, [P, P, P]),
     ("urb_moe_layer_create_sharded", I32, [P, P, P, SZ, SZ, SZ, P, P, P, P, P, P,
                                            ctypes.POINTER(MoeGeometry), PP]),
     ("urb_ep_create", I32, [P, P, I32, I32, SZ, U32, PP]),
