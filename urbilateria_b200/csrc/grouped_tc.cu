@@ -189,7 +189,7 @@ __device__ __forceinline__ int e4m3_round(float a, float *dq) {
 // K steps), and the epilogue writes both tiles' output rows (a missing last tile of an odd
 // count is neither copied nor multiplied).
 // MODE 0: the issuers split each stage's K steps of one tile; the epilogue adds their halves.
-template <int FMT, int MODE>
+template <int FMT, int MODE, int NT>
 __global__ void __launch_bounds__(kThreadsBs, 1) k_bs_grouped(TcArgs a) {
     constexpr bool PAIR = MODE != 0;   // two weight tiles per stage, one per issuer
     constexpr bool GU = MODE == 1, MT = MODE == 2;
@@ -438,7 +438,7 @@ __global__ void __launch_bounds__(kThreadsBs, 1) k_bs_grouped(TcArgs a) {
         tc::mbar_wait(&mma_done[me], 0, &never);
     } else if (warp >= 4 && warp < 8) {
         // ---------------- epilogue ----------------
-        constexpr int RT = bs_rows_per_tok(FMT), TT = bs_terms(FMT), TPC = 16 / RT;
+        constexpr int RT = bs_rows_per_tok(FMT), TT = NT, TPC = 16 / RT;
         const int q = warp & 3;  // TMEM lane quarter this warp may access
         const int row = 32 * q + lane;
         const uint32_t lane_base = uint32_t(32 * q) << 16;
@@ -607,11 +607,11 @@ __device__ __forceinline__ int make_term8(float *r, uint32_t *q) {
 // sub-segment (payload 128-byte swizzled, scale bytes in the tcgen05.cp chunk layout).  MMA rows
 // past a token's terms and slots past a sub-segment's tokens are never read by the epilogue
 // and stay unwritten.
-template <int FMT>
+template <int FMT, int NT>
 __global__ void __launch_bounds__(256) k_bs_prep(TcArgs a) {
     constexpr int KBS = FMT == URB_FMT_MXFP4 ? 8 : 4;  // 32-column blocks per stage
     constexpr int QW = FMT == URB_FMT_MXFP4 ? 1 : 2;   // code words per lane per term
-    constexpr int RT = bs_rows_per_tok(FMT), TT = bs_terms(FMT);
+    constexpr int RT = bs_rows_per_tok(FMT), TT = NT;
     __shared__ int skip;
     if (threadIdx.x == 0) skip = (a.status && *a.status) ? 1 : 0;
     __syncthreads();
@@ -759,17 +759,19 @@ __global__ void k_repack_bs(const uint8_t *values, const uint8_t *scales, size_t
     }
 }
 
-template <int FMT>
+template <int FMT, int NT>
 int launch_bs_t(Ctx *ctx, const TcArgs &a, int kind, cudaStream_t st) {
+    static_assert(NT <= bs_rows_per_tok(FMT), "terms fit in a token's MMA rows");
     constexpr int KBS = FMT == URB_FMT_MXFP4 ? 8 : 4;
     const long long threads = (long long)a.nrows * a.ks * KBS * 4;
     if (threads > 0) {
         prof_begin(ctx, URB_K_PREP, st);
-        k_bs_prep<FMT><<<unsigned((threads + 255) / 256), 256, 0, st>>>(a);
+        k_bs_prep<FMT, NT><<<unsigned((threads + 255) / 256), 256, 0, st>>>(a);
         prof_end(ctx, st);
         URB_CUDA(ctx, cudaGetLastError());
     }
-    auto k = a.pair == 1 ? k_bs_grouped<FMT, 1> : (a.pair == 2 ? k_bs_grouped<FMT, 2> : k_bs_grouped<FMT, 0>);
+    auto k = a.pair == 1 ? k_bs_grouped<FMT, 1, NT>
+                         : (a.pair == 2 ? k_bs_grouped<FMT, 2, NT> : k_bs_grouped<FMT, 0, NT>);
     URB_CUDA(ctx, cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBs));
     prof_begin(ctx, kind, st);
     k<<<ctx->num_sms, kThreadsBs, kSmemBs, st>>>(a);
@@ -781,8 +783,10 @@ int launch_bs_t(Ctx *ctx, const TcArgs &a, int kind, cudaStream_t st) {
 }  // namespace
 
 int launch_tc_grouped(Ctx *ctx, int fmt, const TcArgs &a, int kind, cudaStream_t st) {
-    if (fmt == URB_FMT_MXFP4) return launch_bs_t<URB_FMT_MXFP4>(ctx, a, kind, st);
-    if (fmt == URB_FMT_MXFP8) return launch_bs_t<URB_FMT_MXFP8>(ctx, a, kind, st);
+    if (fmt == URB_FMT_MXFP4 && a.full_terms)
+        return launch_bs_t<URB_FMT_MXFP4, bs_rows_per_tok(URB_FMT_MXFP4)>(ctx, a, kind, st);
+    if (fmt == URB_FMT_MXFP4) return launch_bs_t<URB_FMT_MXFP4, bs_terms(URB_FMT_MXFP4)>(ctx, a, kind, st);
+    if (fmt == URB_FMT_MXFP8) return launch_bs_t<URB_FMT_MXFP8, bs_terms(URB_FMT_MXFP8)>(ctx, a, kind, st);
     return set_error(ctx, URB_ERR_UNSUPPORTED, "tc pass: format");
 }
 

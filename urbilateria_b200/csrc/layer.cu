@@ -294,6 +294,7 @@ int moe_forward_device(Layer *L, const float *d_x, int T, float *d_out, MoeWork 
         } else if (qwen) {
             ga.variant = 2;
             ga.sim128 = 2;
+            ga.full_terms = 1;
             ga.expf = expf_table_of(ctx);
         }
         ga.out = w.h;
@@ -316,6 +317,7 @@ int moe_forward_device(Layer *L, const float *d_x, int T, float *d_out, MoeWork 
         if (deepseek || qwen) {
             da.variant = deepseek ? 1 : 2;
             da.sim128 = deepseek ? 1 : 2;
+            da.full_terms = qwen ? 1 : 0;
         }
         da.cols = int(I);
         da.ks = int(ks_dn);

@@ -85,6 +85,10 @@ struct TcArgs {
     // * BF16(up)) with the libm expf (expf); the down epilogue rounds to BF16.  Non-finite h
     // or outputs set status.
     int variant, sim128;
+    // MXFP4: 1 -> every MMA row of a token carries a residual term (8 instead of 6, about 22
+    // instead of 17 bits of each activation), for numerics whose BF16 boundaries magnify
+    // small differences.  MXFP8 always uses all its rows.
+    int full_terms;
     float limit;
     const float *col_w;
     ExpfTable expf;
