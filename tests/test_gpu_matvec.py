@@ -145,3 +145,25 @@ def test_mxfp8_nonfinite_output_is_rejected(ctx):
     with pytest.raises(urb.UrbError) as e:
         m.matvec(np.ones(32, np.float32))
     assert e.value.kind == "NonFinite"
+
+
+@pytest.mark.parametrize("fmt,rows,cols", [("mxfp4", 3840, 25600), ("mxfp8", 700, 9000),
+                                           ("mxfp4", 38400, 256)])
+def test_single_token_wide_and_tall(oracle, ctx, fmt, rows, cols):
+    # Single-token products of wide, tall and ragged matrices (many row blocks per SM, long K,
+    # partial last blocks).  Deterministic: two calls agree bit for bit.
+    g = syn.rng(rows + cols)
+    pair = mxfp4_pair if fmt == "mxfp4" else mxfp8_pair
+    dev, orc = pair(oracle, ctx, g, rows, cols)
+    x = syn.normal_f32(g, cols)
+    got = dev.matvec(x)
+    assert_close(got, orc.matvec(x))
+    assert np.array_equal(dev.matvec(x).view(np.uint32), got.view(np.uint32))
+
+
+def test_single_token_row_ranges_long_k(oracle, ctx):
+    g = syn.rng(77)
+    dev, orc = mxfp4_pair(oracle, ctx, g, 300, 7168)
+    x = syn.normal_f32(g, 7168)
+    for start, count in [(130, 100), (0, 300), (255, 2), (299, 1)]:
+        assert_close(dev.matvec_rows(start, count, x), orc.matvec_rows(start, count, x))
