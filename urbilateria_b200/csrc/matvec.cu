@@ -3,12 +3,13 @@
 // y[rows] = W[rows, cols] . x[cols].
 //
 // A single token leaves nothing for a tensor-core tile to amortise; the product is one pass
-// over the packed weights, so the kernel is built to keep HBM busy: one CTA per 16-row block of
-// the mma tile layout, its warps splitting the block's 128-column slices, every warp issuing the
-// 16-byte loads of all its slices before touching any of them.  A lane owns rows g and g+8 of
-// one 32-column group per slice (the tile's fragment order); it decodes E2M1 / E4M3 with
-// cvt.rn.f16x2.{e2m1x2,e4m3x2} (exact), accumulates the group in f32 against x from shared
-// memory, and applies the group's E8M0 scale (an exact power of two) to the group sum.  Lane and
+// over the packed weights, so the kernel is built to keep HBM busy and the SMs out of dependent
+// chains: one CTA per 16-row block of the mma tile layout, its warps taking the block's
+// 128-column slices in turn, each warp keeping its next batch of 16-byte loads in flight while
+// it reduces the current one.  A lane owns rows g and g+8 of one 32-column group per slice (the
+// tile's fragment order); it decodes E2M1 / E4M3 with cvt.rn.f16x2.{e2m1x2,e4m3x2} (exact),
+// accumulates the group in four f32 chains against x from shared memory, and applies the
+// group's E8M0 scale (an exact power of two) to the group sum.  Lane and
 // warp partial sums are added in a fixed order, so results are deterministic.
 #include "urb_internal.cuh"
 
@@ -29,10 +30,11 @@ __device__ __forceinline__ float2 h2f(uint32_t h) {
     return __half22float2(*reinterpret_cast<const __half2 *>(&h));
 }
 
-// Dot of 32 E2M1 values (16 bytes, low nibble first) with x[0..31].
+// Dot of 32 E2M1 values (16 bytes, low nibble first) with x[0..31]: four accumulation chains
+// (word i feeds chain i), added in a fixed order.
 __device__ __forceinline__ float dot32_e2m1(uint4 w, const float4 *x4) {
     const uint32_t words[4] = {w.x, w.y, w.z, w.w};
-    float s = 0.0f;
+    float s[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
         uint32_t h[4];
@@ -46,22 +48,23 @@ __device__ __forceinline__ float dot32_e2m1(uint4 w, const float4 *x4) {
             : "r"(words[i]));
         const float4 xa = x4[2 * i], xb = x4[2 * i + 1];
         const float2 a = h2f(h[0]), b = h2f(h[1]), c = h2f(h[2]), d = h2f(h[3]);
-        s = fmaf(a.x, xa.x, s);
-        s = fmaf(a.y, xa.y, s);
-        s = fmaf(b.x, xa.z, s);
-        s = fmaf(b.y, xa.w, s);
-        s = fmaf(c.x, xb.x, s);
-        s = fmaf(c.y, xb.y, s);
-        s = fmaf(d.x, xb.z, s);
-        s = fmaf(d.y, xb.w, s);
+        s[i] = fmaf(a.x, xa.x, s[i]);
+        s[i] = fmaf(a.y, xa.y, s[i]);
+        s[i] = fmaf(b.x, xa.z, s[i]);
+        s[i] = fmaf(b.y, xa.w, s[i]);
+        s[i] = fmaf(c.x, xb.x, s[i]);
+        s[i] = fmaf(c.y, xb.y, s[i]);
+        s[i] = fmaf(d.x, xb.z, s[i]);
+        s[i] = fmaf(d.y, xb.w, s[i]);
     }
-    return s;
+    return (s[0] + s[1]) + (s[2] + s[3]);
 }
 
-// Dot of 32 E4M3 values (32 bytes) with x[0..31].
+// Dot of 32 E4M3 values (32 bytes) with x[0..31]: four accumulation chains (words 2i, 2i + 1
+// feed chain i), added in a fixed order.
 __device__ __forceinline__ float dot32_e4m3(uint4 w0, uint4 w1, const float4 *x4) {
     const uint32_t words[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-    float s = 0.0f;
+    float s[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
         uint32_t h[2];
@@ -73,12 +76,13 @@ __device__ __forceinline__ float dot32_e4m3(uint4 w0, uint4 w1, const float4 *x4
             : "r"(words[i]));
         const float4 xa = x4[i];
         const float2 a = h2f(h[0]), b = h2f(h[1]);
-        s = fmaf(a.x, xa.x, s);
-        s = fmaf(a.y, xa.y, s);
-        s = fmaf(b.x, xa.z, s);
-        s = fmaf(b.y, xa.w, s);
+        float &t = s[i >> 1];
+        t = fmaf(a.x, xa.x, t);
+        t = fmaf(a.y, xa.y, t);
+        t = fmaf(b.x, xa.z, t);
+        t = fmaf(b.y, xa.w, t);
     }
-    return s;
+    return (s[0] + s[1]) + (s[2] + s[3]);
 }
 
 template <int FMT, int WARPS>
@@ -96,70 +100,79 @@ __global__ void __launch_bounds__(32 * WARPS) k_matvec1(const uint8_t *tiles, in
     const int rb = rb_lo + blockIdx.x;
     const uint8_t *base = tiles + size_t(rb) * kslices * TB;
 
-    constexpr int kMvSlicesPerBatch = mv_batch<FMT>();
+    // Warp w takes slices w, w + WARPS, ... of the row block in batches of B, double-buffered:
+    // the next batch's 16-byte loads are in flight while the current batch is reduced.
+    constexpr int B = mv_batch<FMT>() / 2;
+    const int nmine = kslices > warp ? (kslices - warp + WARPS - 1) / WARPS : 0;
     float acc0 = 0.0f, acc1 = 0.0f;  // rows g and g+8
-    bool staged = false;
-    for (int s0 = warp * kMvSlicesPerBatch; s0 < kslices || !staged; s0 += WARPS * kMvSlicesPerBatch) {
-        // Issue every load of this batch before using any.
-        uint4 w[kMvSlicesPerBatch][V];
-        uint32_t sc[kMvSlicesPerBatch];
+    uint4 wc[B][V], wn[B][V];
+    uint32_t scc[B], scn[B];
+    auto load = [&](uint4 (&w)[B][V], uint32_t (&sc)[B], int j0) {
 #pragma unroll
-        for (int i = 0; i < kMvSlicesPerBatch; ++i) {
-            const int s = s0 + i;
-            if (s < kslices) {
-                const uint8_t *t = base + size_t(s) * TB;
+        for (int i = 0; i < B; ++i) {
+            if (j0 + i < nmine) {
+                const uint8_t *t = base + size_t(warp + WARPS * (j0 + i)) * TB;
 #pragma unroll
                 for (int v = 0; v < V; ++v)
                     w[i][v] = __ldg(reinterpret_cast<const uint4 *>(t + lane * LANE_BYTES) + v);
                 sc[i] = __ldg(reinterpret_cast<const uint16_t *>(t + PAY) + lane);
             }
         }
-        if (!staged) {
-            // x into shared memory once (its latency overlaps the weight loads in flight): all
-            // of a thread's 16-byte loads are issued before any is stored.
-            constexpr int XV = 8;  // float4 per thread per round
-            const int n4 = kslices * 32;  // float4 of the padded x
-            const bool vec = (cols & 3) == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0;
-            for (int i0 = threadIdx.x; i0 < n4; i0 += 32 * WARPS * XV) {
-                float4 v[XV];
+    };
+    load(wc, scc, 0);
+    {
+        // x into shared memory once (its latency overlaps the weight loads in flight): all of a
+        // thread's 16-byte loads are issued before any is stored.
+        constexpr int XV = 8;  // float4 per thread per round
+        const int n4 = kslices * 32;  // float4 of the padded x
+        const bool vec = (cols & 3) == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0;
+        for (int i0 = threadIdx.x; i0 < n4; i0 += 32 * WARPS * XV) {
+            float4 v[XV];
 #pragma unroll
-                for (int j = 0; j < XV; ++j) {
-                    const int i = i0 + j * 32 * WARPS;
-                    v[j] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-                    if (i < n4 && 4 * i < cols) {
-                        if (vec) {
-                            v[j] = __ldg(reinterpret_cast<const float4 *>(x) + i);
-                        } else {
-                            float e[4];
-                            for (int k = 0; k < 4; ++k) e[k] = 4 * i + k < cols ? x[4 * i + k] : 0.0f;
-                            v[j] = make_float4(e[0], e[1], e[2], e[3]);
-                        }
+            for (int j = 0; j < XV; ++j) {
+                const int i = i0 + j * 32 * WARPS;
+                v[j] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                if (i < n4 && 4 * i < cols) {
+                    if (vec) {
+                        v[j] = __ldg(reinterpret_cast<const float4 *>(x) + i);
+                    } else {
+                        float e[4];
+                        for (int k = 0; k < 4; ++k) e[k] = 4 * i + k < cols ? x[4 * i + k] : 0.0f;
+                        v[j] = make_float4(e[0], e[1], e[2], e[3]);
                     }
                 }
-#pragma unroll
-                for (int j = 0; j < XV; ++j) {
-                    const int i = i0 + j * 32 * WARPS;
-                    if (i < n4) reinterpret_cast<float4 *>(xs)[i] = v[j];
-                }
             }
-            __syncthreads();
-            staged = true;
-        }
 #pragma unroll
-        for (int i = 0; i < kMvSlicesPerBatch; ++i) {
-            const int s = s0 + i;
-            if (s >= kslices) break;
+            for (int j = 0; j < XV; ++j) {
+                const int i = i0 + j * 32 * WARPS;
+                if (i < n4) reinterpret_cast<float4 *>(xs)[i] = v[j];
+            }
+        }
+        __syncthreads();
+    }
+    for (int j0 = 0; j0 < nmine; j0 += B) {
+        if (j0 + B < nmine) load(wn, scn, j0 + B);
+#pragma unroll
+        for (int i = 0; i < B; ++i) {
+            if (j0 + i >= nmine) break;
+            const int s = warp + WARPS * (j0 + i);
             const float4 *x4 = reinterpret_cast<const float4 *>(xs + s * 128 + q * 32);
             float p0, p1;
             if (FMT == URB_FMT_MXFP4) {
-                p0 = dot32_e2m1(w[i][0], x4);
-                p1 = dot32_e2m1(w[i][V - 1], x4);
+                p0 = dot32_e2m1(wc[i][0], x4);
+                p1 = dot32_e2m1(wc[i][V - 1], x4);
             } else {
-                p0 = dot32_e4m3(w[i][0], w[i][1], x4);
-                p1 = dot32_e4m3(w[i][V - 2], w[i][V - 1], x4);
+                p0 = dot32_e4m3(wc[i][0], wc[i][1], x4);
+                p1 = dot32_e4m3(wc[i][V - 2], wc[i][V - 1], x4);
             }
-            acc0 = fmaf(p0, pow2_e8m0(sc[i] & 0xff), acc0);
-            acc1 = fmaf(p1, pow2_e8m0(sc[i] >> 8), acc1);
+            acc0 = fmaf(p0, pow2_e8m0(scc[i] & 0xff), acc0);
+            acc1 = fmaf(p1, pow2_e8m0(scc[i] >> 8), acc1);
+        }
+#pragma unroll
+        for (int i = 0; i < B; ++i) {
+            scc[i] = scn[i];
+#pragma unroll
+            for (int v = 0; v < V; ++v) wc[i][v] = wn[i][v];
         }
     }
     // Column groups of a row sit in lanes 4g .. 4g+3.
