@@ -244,6 +244,203 @@ def bench_matvec(urb, ctx, stream, local, pk_hbm, copies=20, reps=10):
             "l2": "20 distinct 15.6 MB weight copies round-robin; CUDA-graph replay"}
 
 
+def kernel_ms(ctx, native, fn, reps):
+    """Runs fn() reps times with the library profiler on: device ms per call summed over the
+    library's kernels (launch gaps excluded), and the stream's ms per call (events)."""
+    import ctypes
+    import torch
+    stream = torch.cuda.current_stream()
+    torch.cuda.synchronize()
+    ctx.lib.urb_profile_reset(ctx.h)
+    ctx.lib.urb_profile_enable(ctx.h, 1)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(reps):
+        fn()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ctx.lib.urb_profile_enable(ctx.h, 0)
+    total, launches = 0.0, 0
+    for k in range(len(native.KERNEL_NAMES)):
+        t, n = ctypes.c_double(), ctypes.c_int64()
+        ctx.lib.urb_profile_read(ctx.h, k, ctypes.byref(t), ctypes.byref(n))
+        total += t.value
+        launches += n.value
+    return total / reps, e0.elapsed_time(e1) / reps, launches // reps
+
+
+def bench_configs(urb, native, ctx, local, pk_hbm):
+    """Configs 1, 3 and 4 of the benchmark set, each timed on this GPU with the library's own
+    device API (inputs resident), reported beside its algorithmic bytes and the measured HBM
+    peak.  Device time is the sum of the library's kernels per call (the profiler's events),
+    which for the small C1 product excludes the host's launch cadence."""
+    import torch
+    from urbilateria_b200 import synthetic as syn
+    dev = f"cuda:{local}"
+    out = {}
+    g = syn.rng(SEED + 11)
+
+    # Config 1: BF16 SwiGLU FFN, gate/up [768 x 2048], down [2048 x 768] ~ N(0, 0.02); T = 1
+    # and 32.  9.4 MB of weights fit L2, so 27 distinct copies (254 MB) are used in turn.
+    H1, I1, copies = 2048, 768, 27
+    gb, ub, db = (syn.bf16_normal(g, (I1, H1), 0.02), syn.bf16_normal(g, (I1, H1), 0.02),
+                  syn.bf16_normal(g, (H1, I1), 0.02))
+    mlps = [(urb.Bf16Matrix.from_bits(I1, H1, gb, ctx=ctx), urb.Bf16Matrix.from_bits(I1, H1, ub, ctx=ctx),
+             urb.Bf16Matrix.from_bits(H1, I1, db, ctx=ctx)) for _ in range(copies)]
+    c1 = {"workload": "C1 BF16 SwiGLU FFN, hidden 2048, intermediate 768", "weights_copies": copies}
+    for T in (1, 32):
+        d_x = torch.from_numpy(syn.normal_bf16_as_f32(g, (T, H1))).to(dev)
+        d_y = torch.empty_like(d_x)
+        st = torch.zeros(1, dtype=torch.int32, device=dev)
+        it = [0]
+
+        def fn():
+            m = mlps[it[0] % copies]
+            it[0] += 1
+            ctx.check(ctx.lib.urb_gated_mlp_forward_device(ctx.h, m[0].h, m[1].h, m[2].h,
+                                                           d_x.data_ptr(), T, d_y.data_ptr(),
+                                                           st.data_ptr()))
+        for _ in range(copies):
+            fn()
+        k_ms, s_ms, n = kernel_ms(ctx, native, fn, 4 * copies)
+        # The products are a few microseconds, less than the host needs to issue them, so the
+        # device time is taken from a CUDA graph of one call per weight copy.
+        stream = torch.cuda.current_stream()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            for _ in range(copies):
+                fn()
+        for _ in range(3):
+            graph.replay()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for _ in range(10):
+            graph.replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        g_ms = e0.elapsed_time(e1) / (10 * copies)
+        del graph
+        if int(st.item()) != 0:
+            raise RuntimeError("config 1 forward reported status %d" % int(st.item()))
+        nbytes = 3 * I1 * H1 * 2 + T * (H1 * 4 + H1 * 4)
+        c1["T%d" % T] = {"us": g_ms * 1e3, "timing": "CUDA-graph replay, device time per call",
+                         "eager_stream_us": s_ms * 1e3, "launches": n,
+                         "tokens_per_s": T / (g_ms / 1e3), "bytes": nbytes,
+                         "achieved_gbs": nbytes / (g_ms / 1e3) / 1e9,
+                         "frac_of_measured_hbm": nbytes / (g_ms / 1e3) / 1e9 / pk_hbm}
+    for m in mlps:
+        for x in m:
+            x.free()
+    out["c1"] = c1
+
+    # Config 3: 128 MXFP8 experts (hidden 4096, intermediate 1536; E4M3 fp8-cast N(0,1), E8M0
+    # 117..123 per 32), 512 tokens with Zipf(1.1) top-8 routes: the experts half of the layer
+    # with the caller's routes.  Every expert is its own HBM copy of one generated matrix set.
+    H3, I3, E3, T3, K3 = 4096, 1536, 128, 512, 8
+    gv, gs = syn.mxfp8_matrix(g, I3, H3)
+    uv, us_ = syn.mxfp8_matrix(g, I3, H3)
+    dv, ds = syn.mxfp8_matrix(g, H3, I3)
+    experts = [urb.GatedMlp(urb.MxFp8Matrix.from_packed(I3, H3, 1, 32, gv, gs, ctx=ctx),
+                            urb.MxFp8Matrix.from_packed(I3, H3, 1, 32, uv, us_, ctx=ctx),
+                            urb.MxFp8Matrix.from_packed(H3, I3, 1, 32, dv, ds, ctx=ctx))
+               for _ in range(E3)]
+    r3 = urb.Bf16Matrix.from_bits(E3, H3, syn.bf16_normal(g, (E3, H3), 0.02), ctx=ctx)
+    layer3 = urb.RuntimeMoeLayer(r3, np.zeros(E3, np.float32), experts, None,
+                                 urb.MoeGeometry(K3, 1, 1, True, 1.0))
+    ids = syn.zipf_routes(g, T3, E3, K3).astype(np.int32)
+    w = g.random((T3, K3)).astype(np.float32)
+    w /= w.sum(axis=1, keepdims=True)
+    d_x = torch.from_numpy(syn.normal_bf16_as_f32(g, (T3, H3))).to(dev)
+    d_ids, d_w = torch.from_numpy(ids).to(dev), torch.from_numpy(w).to(dev)
+    d_y = torch.empty_like(d_x)
+    st = torch.zeros(1, dtype=torch.int32, device=dev)
+
+    def fn3():
+        ctx.check(ctx.lib.urb_moe_forward_routed_device(ctx.h, layer3.h, d_x.data_ptr(), T3,
+                                                        d_ids.data_ptr(), d_w.data_ptr(),
+                                                        d_y.data_ptr(), st.data_ptr()))
+    for _ in range(3):
+        fn3()
+    k_ms, s_ms, n = kernel_ms(ctx, native, fn3, 10)
+    if int(st.item()) != 0:
+        raise RuntimeError("config 3 forward reported status %d" % int(st.item()))
+    counts = np.bincount(ids.ravel(), minlength=E3)
+    per_expert = 3 * (I3 * H3 + I3 * H3 // 32)
+    nbytes = int((counts > 0).sum()) * per_expert
+    flops = 2.0 * T3 * K3 * 3 * I3 * H3
+    out["c3"] = {"workload": "C3 MXFP8 grouped experts: 128 x (4096 x 1536 SwiGLU), 512 tokens, "
+                             "Zipf(1.1) top-8 (caller routes)",
+                 "kernel_us": k_ms * 1e3, "stream_us": s_ms * 1e3, "launches": n,
+                 "tokens_per_s": T3 / (k_ms / 1e3), "touched_experts": int((counts > 0).sum()),
+                 "max_expert_tokens": int(counts.max()), "bytes": nbytes,
+                 "achieved_gbs": nbytes / (k_ms / 1e3) / 1e9,
+                 "frac_of_measured_hbm": nbytes / (k_ms / 1e3) / 1e9 / pk_hbm,
+                 "tflops": flops / (k_ms / 1e3) / 1e12}
+    layer3.free()
+    for e in experts:
+        for mtx in (e.gate, e.up, e.down):
+            mtx.free()
+    r3.free()
+
+    # Config 4: 4 stacked MoE layers (hidden 7168, 384 MXFP4 routed experts top-8 + 1 shared,
+    # intermediate 2048, config-2 routing), h <- h + MoE_l(h) scaled back to unit RMS, batch
+    # 1 / 8 / 64 one-token sequences.  Without the rescale the synthetic weights grow h ~10^4
+    # per layer and overflow f32 inside a step (the routing kernel then rejects the logits and
+    # every later kernel skips its work).  Each layer has its own router, bias and shared
+    # expert; the 384 routed experts are one set of HBM copies that all four layers address
+    # (routes differ per layer, and a step's touched experts far exceed L2, so the traffic per
+    # step is that of distinct layers).
+    E4, L4 = 384, 4
+    pk = [syn.mxfp4_matrix(g, INTER, HIDDEN), syn.mxfp4_matrix(g, INTER, HIDDEN),
+          syn.mxfp4_matrix(g, HIDDEN, INTER)]
+
+    def mlp4():
+        return urb.GatedMlp(*[urb.MxFp4Matrix.from_packed(r, c, 32, p, sc, ctx=ctx)
+                              for (p, sc), (r, c) in zip(pk, [(INTER, HIDDEN), (INTER, HIDDEN),
+                                                             (HIDDEN, INTER)])])
+    routed = [mlp4() for _ in range(E4)]
+    layers = []
+    for _ in range(L4):
+        r4 = urb.Bf16Matrix.from_bits(E4, HIDDEN, syn.bf16_normal(g, (E4, HIDDEN), 0.02), ctx=ctx)
+        layers.append(urb.RuntimeMoeLayer(r4, syn.normal_f32(g, E4, 0.01), routed, mlp4(),
+                                          urb.MoeGeometry(TOP_K, 1, 1, True, SCALE)))
+    per_expert = 3 * (INTER * HIDDEN // 2 + INTER * HIDDEN // 32)
+    c4 = {"workload": "C4 stacked MoE decode: 4 layers x (7168, 384 MXFP4 experts top-8 + 1 "
+                      "shared, inter 2048), h <- h + MoE(h)", "layers": L4}
+    for B in (1, 8, 64):
+        h0 = syn.normal_bf16_as_f32(g, (B, HIDDEN))
+        touched = 0
+        for lay in layers:
+            _, _, _, extra = lay.forward_batch(h0, B, details=True)
+            touched += int((extra["counts"] > 0).sum()) + 1
+        d_h = torch.from_numpy(h0).to(dev)
+        d_o = torch.empty_like(d_h)
+        st = torch.zeros(1, dtype=torch.int32, device=dev)
+
+        def fn4():
+            for lay in layers:
+                lay.forward_device(d_h.data_ptr(), B, d_o.data_ptr(), 0, 0, st.data_ptr())
+                d_h.add_(d_o)
+                d_h.mul_(torch.rsqrt(d_h.square().mean(dim=1, keepdim=True)))
+        for _ in range(3):
+            fn4()
+        k_ms, s_ms, n = kernel_ms(ctx, native, fn4, 10)
+        nbytes = touched * per_expert + L4 * E4 * HIDDEN * 2
+        if int(st.item()) != 0:
+            c4["B%d" % B] = {"error": "status %d" % int(st.item())}
+            continue
+        c4["B%d" % B] = {"kernel_us": k_ms * 1e3, "stream_us": s_ms * 1e3, "launches": n,
+                         "tokens_per_s": B / (k_ms / 1e3), "stream_tokens_per_s": B / (s_ms / 1e3),
+                         "touched_experts_per_step": touched, "bytes": nbytes,
+                         "achieved_gbs": nbytes / (k_ms / 1e3) / 1e9,
+                         "frac_of_measured_hbm": nbytes / (k_ms / 1e3) / 1e9 / pk_hbm}
+    for lay in layers:
+        lay.free()
+    out["c4"] = c4
+    return out
+
+
 def workload_config(world):
     return {"workload": "C2 MXFP4 MoE layer: hidden 7168, 256+1 experts, inter 2048, top-8 "
                         "noaux_tc x2.5, 128-token chunk per GPU",
@@ -264,6 +461,8 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-matvec", action="store_true")
+    ap.add_argument("--no-configs", action="store_true",
+                    help="skip the config 1 / 3 / 4 measurements")
     ap.add_argument("--experts", type=int, default=256,
                     help="routed experts (256 = config 2; smaller only for profiling captures)")
     ap.add_argument("--tokens", type=int, default=128,
@@ -380,6 +579,10 @@ def main():
         ms = min(ms, e0.elapsed_time(e1))
 
     matvec = None if (args.no_matvec or world > 1) else bench_matvec(urb, ctx, stream, local, pk_hbm)
+    configs = None
+    if not args.no_configs and world == 1:
+        with torch.cuda.stream(stream):
+            configs = bench_configs(urb, native, ctx, local, pk_hbm)
 
     # End to end through the host-pointer ABI (pinned host input/output).
     hx = torch.from_numpy(x).pin_memory()
@@ -455,7 +658,7 @@ def main():
             "layer_hbm_gbs": layer_bytes / (ms / args.steps / 1e3) / 1e9,
             "down_gbs": dn_bytes / (dn.get("ms_per_launch", float("nan")) / 1e3) / 1e9,
             "touched_experts": touched, "held_experts": [eb, ec], "kernels": kern,
-            "matvec_c0": matvec,
+            "matvec_c0": matvec, "configs": configs,
             "gpu_launches": sum(v["launches"] for v in kern.values()),
             "clocks": clk.summary()}
 

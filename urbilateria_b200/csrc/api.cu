@@ -157,6 +157,13 @@ int tiled_product(Ctx *ctx, const Mat *m, int rb_lo, int rb_hi, const float *d_x
 // Product of rows [start, start+count) for `batch` tokens; d_y is [batch, count].
 int device_product(Ctx *ctx, const Mat *m, size_t start, size_t count, const float *d_x,
                    size_t batch, float *d_y, int32_t *d_status, cudaStream_t st) {
+    if (bf16_gemv_applies(m, batch)) {
+        // BF16 rows for a few tokens: one streaming pass on CUDA cores.
+        prof_begin(ctx, URB_K_PRODUCT, st);
+        int rc = launch_bf16_gemv(ctx, m, start, count, d_x, batch, d_y, d_status, st);
+        prof_end(ctx, st);
+        if (rc != URB_ERR_UNSUPPORTED) return rc;
+    }
     if (!m->tiled) {
         prof_begin(ctx, URB_K_PRODUCT, st);
         int rc = launch_generic_matmul(ctx, m, start, count, d_x, batch, d_y, st);

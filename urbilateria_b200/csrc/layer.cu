@@ -408,12 +408,20 @@ int moe_forward_device(Layer *L, const float *d_x, int T, float *d_out, MoeWork 
 }
 
 // GatedMlp::forward (src/model/mlp.rs:90-99) for `T` tokens on the device: one grouped pair
-// pass (gate/up with fused SwiGLU) and one grouped down pass, host-built segments.
+// pass (gate/up with fused SwiGLU) and one grouped down pass, host-built segments; BF16
+// projections with few tokens take the streaming CUDA-core passes instead.
 int gated_mlp_device(Ctx *ctx, const Mat *g, const Mat *u, const Mat *d, const float *d_x, int T,
                      float *d_out, int32_t *d_status, cudaStream_t st) {
     const size_t H = g->cols, I = g->rows;
     const int nseg = int(div_ceil(T, kCap));
     int rc;
+    if (bf16_gemv_applies(g, T) && bf16_gemv_applies(u, T) && bf16_gemv_applies(d, T)) {
+        // BF16 projections, a few tokens: two streaming passes (gate/up with SwiGLU, down).
+        float *h = static_cast<float *>(workspace(ctx, size_t(T) * I * 4 + 256, &rc));
+        if (!h) return rc;
+        rc = launch_bf16_swiglu(ctx, g, u, d, d_x, T, h, d_out, d_status, st);
+        if (rc != URB_ERR_UNSUPPORTED) return rc;
+    }
     size_t need = T * 4 + 2 * nseg * sizeof(Seg) + 64 + T * 4 + size_t(T) * I * 4 + 8 * 256;
     uint8_t *ws = static_cast<uint8_t *>(workspace(ctx, need, &rc));
     if (!ws) return rc;

@@ -97,6 +97,16 @@ int urb_gated_mlp_forward_device_noalloc(urb_ctx *ctx, const urb_mat *g, const u
         return set_error(ctx, URB_ERR_UNSUPPORTED, "gated MLP needs tiled gate/up of one format");
     if (tokens == 0) return URB_OK;
     const size_t H = g->cols, I = g->rows, T = tokens;
+    if (bf16_gemv_applies(g, T) && bf16_gemv_applies(u, T) && bf16_gemv_applies(d, T) &&
+        T * I * 4 <= kNoallocScratchBytes) {
+        // The same streaming BF16 passes as urb_gated_mlp_forward_device (h in the scratch).
+        uint8_t *base = nullptr;
+        int rc = scratch_of(ctx, &base);
+        if (rc) return rc;
+        rc = launch_bf16_swiglu(ctx, g, u, d, d_x, int(T), reinterpret_cast<float *>(base), d_out,
+                                d_status, ctx->stream);
+        if (rc != URB_ERR_UNSUPPORTED) return rc;
+    }
     const size_t nseg = (T + kMlpCap - 1) / kMlpCap;
     // Carve: row shifts [T], segments [2 nseg], scalars [4], max-exponent words [T], h [T, I].
     size_t off = 0;

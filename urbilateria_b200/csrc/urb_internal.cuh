@@ -203,6 +203,15 @@ __host__ __device__ constexpr size_t router_f64_elems(int rows, int cols) {
 }
 int widen_router_f64(const Mat *router, double *dst, cudaStream_t st);
 // Single-token product of rows [start, start + count) of a tiled MXFP4 / MXFP8 matrix.
+// BF16 products of at most kBf16GemvMaxTokens tokens on CUDA cores (gemv_bf16.cu): rows
+// [start, start + count) of m times x [tokens, cols] into y [tokens, count]; and the gated MLP
+// with BF16 gate / up / down (h [tokens, inter] is the caller's scratch).
+constexpr size_t kBf16GemvMaxTokens = 32;
+bool bf16_gemv_applies(const Mat *m, size_t tokens);
+int launch_bf16_gemv(Ctx *ctx, const Mat *m, size_t start, size_t count, const float *d_x,
+                     size_t tokens, float *d_y, int32_t *d_status, cudaStream_t st);
+int launch_bf16_swiglu(Ctx *ctx, const Mat *g, const Mat *u, const Mat *d, const float *d_x,
+                       int tokens, float *d_h, float *d_out, int32_t *d_status, cudaStream_t st);
 int launch_matvec1(Ctx *ctx, const Mat *m, size_t start, size_t count, const float *d_x,
                    float *d_y, cudaStream_t st);
 int launch_router_logits_f64(const double *w64, int experts, const float *d_x, int tokens,
