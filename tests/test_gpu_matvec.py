@@ -167,3 +167,29 @@ def test_single_token_row_ranges_long_k(oracle, ctx):
     x = syn.normal_f32(g, 7168)
     for start, count in [(130, 100), (0, 300), (255, 2), (299, 1)]:
         assert_close(dev.matvec_rows(start, count, x), orc.matvec_rows(start, count, x))
+
+
+@pytest.mark.parametrize("rows,cols", [(37, 1001), (130, 2048), (5, 8), (64, 7168)])
+def test_bf16_streaming_products(oracle, ctx, rows, cols):
+    # Up to 32 tokens take the streaming CUDA-core pass: ragged columns (not a multiple of 8),
+    # partial token tiles (1, 3, 9, 32 tokens) and row ranges.
+    g = syn.rng(rows * 7 + cols)
+    dev, orc = bf16_pair(oracle, ctx, g, rows, cols, std=0.5)
+    for batch in (1, 3, 9, 32):
+        x = syn.normal_f32(g, (batch, cols))
+        assert_close(dev.matmul_rows(x, batch), orc.matmul_rows(x, batch))
+    x = syn.normal_f32(g, cols)
+    start, count = rows // 3, rows - rows // 3 - 1 if rows > 2 else 1
+    assert_close(dev.matvec_rows(start, count, x), orc.matvec_rows(start, count, x))
+
+
+@pytest.mark.parametrize("tokens", [1, 5, 17, 32])
+def test_bf16_gated_mlp_streaming(oracle, ctx, tokens):
+    g = syn.rng(8800 + tokens)
+    gd, go = bf16_pair(oracle, ctx, g, 768, 2048)
+    ud, uo = bf16_pair(oracle, ctx, g, 768, 2048)
+    dd, do = bf16_pair(oracle, ctx, g, 2048, 768)
+    x = syn.normal_bf16_as_f32(g, (tokens, 2048))
+    got = urb.GatedMlp(gd, ud, dd).forward_batch(x, tokens)
+    want = np.stack([oracle.gated_mlp_forward(go, uo, do, x[t]) for t in range(tokens)])
+    assert_close(got, want)
