@@ -260,12 +260,15 @@ def kernel_ms(ctx, native, fn, reps):
     e1.record(stream)
     torch.cuda.synchronize()
     ctx.lib.urb_profile_enable(ctx.h, 0)
-    total, launches = 0.0, 0
-    for k in range(len(native.KERNEL_NAMES)):
+    total, launches, per_kind = 0.0, 0, {}
+    for k, name in enumerate(native.KERNEL_NAMES):
         t, n = ctypes.c_double(), ctypes.c_int64()
         ctx.lib.urb_profile_read(ctx.h, k, ctypes.byref(t), ctypes.byref(n))
         total += t.value
         launches += n.value
+        if n.value:
+            per_kind[name] = t.value / reps * 1e3
+    kernel_ms.per_kind = per_kind  # microseconds per call, by kernel kind, of the last run
     return total / reps, e0.elapsed_time(e1) / reps, launches // reps
 
 
@@ -374,6 +377,7 @@ def bench_configs(urb, native, ctx, local, pk_hbm):
                  "kernel_us": k_ms * 1e3, "stream_us": s_ms * 1e3, "launches": n,
                  "tokens_per_s": T3 / (k_ms / 1e3), "touched_experts": int((counts > 0).sum()),
                  "max_expert_tokens": int(counts.max()), "bytes": nbytes,
+                 "kernels_us": kernel_ms.per_kind,
                  "achieved_gbs": nbytes / (k_ms / 1e3) / 1e9,
                  "frac_of_measured_hbm": nbytes / (k_ms / 1e3) / 1e9 / pk_hbm,
                  "tflops": flops / (k_ms / 1e3) / 1e12}
@@ -426,13 +430,38 @@ def bench_configs(urb, native, ctx, local, pk_hbm):
         for _ in range(3):
             fn4()
         k_ms, s_ms, n = kernel_ms(ctx, native, fn4, 10)
+        per_kind = kernel_ms.per_kind
         nbytes = touched * per_expert + L4 * E4 * HIDDEN * 2
+        # A decode step's kernels are short next to the host's launch cadence: the step is
+        # also timed as one CUDA graph (the layer forwards' device work alone).
+        graph_us = None
+        try:
+            stream = torch.cuda.current_stream()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=stream):
+                fn4()
+            for _ in range(3):
+                graph.replay()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            torch.cuda.synchronize()
+            e0.record(stream)
+            for _ in range(10):
+                graph.replay()
+            e1.record(stream)
+            torch.cuda.synchronize()
+            graph_us = e0.elapsed_time(e1) / 10 * 1e3
+            del graph
+        except Exception as exc:  # capture refused: report the eager figures only
+            graph_us = "not captured: %s" % str(exc).splitlines()[0][:120]
         if int(st.item()) != 0:
             c4["B%d" % B] = {"error": "status %d" % int(st.item())}
             continue
         c4["B%d" % B] = {"kernel_us": k_ms * 1e3, "stream_us": s_ms * 1e3, "launches": n,
                          "tokens_per_s": B / (k_ms / 1e3), "stream_tokens_per_s": B / (s_ms / 1e3),
                          "touched_experts_per_step": touched, "bytes": nbytes,
+                         "kernels_us": per_kind, "graph_us": graph_us,
+                         "graph_tokens_per_s": (B / (graph_us / 1e6)
+                                                if isinstance(graph_us, float) else None),
                          "achieved_gbs": nbytes / (k_ms / 1e3) / 1e9,
                          "frac_of_measured_hbm": nbytes / (k_ms / 1e3) / 1e9 / pk_hbm}
     for lay in layers:
