@@ -222,6 +222,14 @@ URB_API int urb_moe_forward_routed_device(urb_ctx *ctx, urb_layer *layer, const 
                                           const float *d_route_weight, float *d_out,
                                           int32_t *d_status);
 
+/* WeightMatrix::transpose_rows_matvec (src/model/weight.rs:332-343; mxfp.rs:785-858 for MXFP8,
+ * :1782-1821 for MXFP4, bf16.rs:430-475, matrix.rs:276-313): y[cols] = rows start..start+n of the
+ * matrix, transposed, times x[n] (host pointers), bit-exact: each column is the ordered f64 sum
+ * of the exact products, rounded to f32.  URB_ERR_NONFINITE for a non-finite x (checked first),
+ * URB_ERR_SHAPE when start + n exceeds the rows; MXFP8 also rejects non-finite outputs. */
+URB_API int urb_transpose_rows_matvec(urb_ctx *ctx, const urb_mat *mat, size_t start,
+                                      const float *x, size_t n, float *y);
+
 /* ---- checkpoint numerics ---------------------------------------------------------------------- */
 
 /* Numerics of the routed forward.  URB_NUMERICS_GLM: the GLM composition above.

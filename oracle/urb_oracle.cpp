@@ -281,6 +281,44 @@ int urbo_matvec_rows(const urbo_matrix *m, size_t start, size_t count, const flo
     return URBO_OK;
 }
 
+// WeightMatrix::transpose_rows_matvec (src/model/weight.rs:332-343): per column, the ordered
+// f64 sum over rows start..start+n of f64(weight) * f64(x[row - start]) from +0.0, rounded to
+// f32 (mxfp.rs:785-858 MXFP8, whose AVX2 form :1308-1360 is the same sequence of exactly
+// rounded adds of exact products; mxfp.rs:1782-1821 MXFP4; bf16.rs:430-475; matrix.rs:276-313).
+// Input finiteness, then the row range; only MXFP8 rejects non-finite outputs (:851-856).
+int urbo_transpose_rows_matvec(const urbo_matrix *m, size_t start, const float *x, size_t n,
+                               float *y) {
+    if (any_nonfinite(x, n)) return URBO_ERR_NONFINITE;
+    if (start + n < start || start + n > m->rows) return URBO_ERR_SHAPE;
+    const float *e4 = tables().e4m3;
+    for (size_t c = 0; c < m->cols; ++c) {
+        double sum = 0.0;
+        for (size_t i = 0; i < n; ++i) {
+            const size_t r = start + i;
+            float w;
+            switch (m->format) {
+            case URBO_F32: w = static_cast<const float *>(m->values)[r * m->cols + c]; break;
+            case URBO_BF16: w = bf16f(static_cast<const uint16_t *>(m->values)[r * m->cols + c]); break;
+            case URBO_MXFP8: {
+                const size_t sc = div_ceil(m->cols, m->block_cols);
+                w = e4[static_cast<const uint8_t *>(m->values)[r * m->cols + c]] *
+                    e8m0(m->scales[(r / m->block_rows) * sc + c / m->block_cols]);
+                break;
+            }
+            default: {  // MXFP4
+                const uint8_t byte = static_cast<const uint8_t *>(m->values)[r * div_ceil(m->cols, 2) + c / 2];
+                w = kE2M1[(c % 2 == 0 ? byte : byte >> 4) & 15] *
+                    e8m0(m->scales[r * div_ceil(m->cols, m->group_size) + c / m->group_size]);
+            }
+            }
+            sum += double(x[i]) * double(w);
+        }
+        y[c] = float(sum);
+    }
+    if (m->format == URBO_MXFP8 && any_nonfinite(y, m->cols)) return URBO_ERR_NONFINITE;
+    return URBO_OK;
+}
+
 int urbo_mxfp4_matvec_rows_fp32(const urbo_matrix *m, size_t start, size_t count,
                                 const float *x, float *y, int threads) {
     if (m->format != URBO_MXFP4) return URBO_ERR_SHAPE;

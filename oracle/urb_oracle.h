@@ -60,6 +60,10 @@ float urbo_expf(float value);           /* the libm expf the Rust reference link
 int urbo_validate(const urbo_matrix *m);
 
 /* WeightMatrix::matvec_rows / MxFp4Matrix::matvec_rows etc.  y has `count` entries. */
+/* WeightMatrix::transpose_rows_matvec (src/model/weight.rs:332-343): y[cols] = rows
+ * start..start+n of W, transposed, times x[n]; ordered f64 column sums. */
+int urbo_transpose_rows_matvec(const urbo_matrix *m, size_t start, const float *x, size_t n,
+                               float *y);
 int urbo_matvec_rows(const urbo_matrix *m, size_t start, size_t count, const float *x, float *y,
                      int threads);
 /* WeightMatrix::matmul_rows (src/model/weight.rs:106-153): x [batch, cols] -> y [batch, rows]. */

@@ -87,6 +87,9 @@ def lib():
             ctypes.POINTER(OracleMatrix), ctypes.c_size_t, ctypes.c_size_t, ctypes.c_void_p,
             ctypes.c_void_p, ctypes.c_int]
         _lib.urbo_mxfp4_matvec_rows_fp32.argtypes = _lib.urbo_matvec_rows.argtypes
+        _lib.urbo_transpose_rows_matvec.argtypes = [
+            ctypes.POINTER(OracleMatrix), ctypes.c_size_t, ctypes.c_void_p, ctypes.c_size_t,
+            ctypes.c_void_p]
         _lib.urbo_matmul_rows.argtypes = [
             ctypes.POINTER(OracleMatrix), ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p,
             ctypes.c_int]
@@ -173,6 +176,15 @@ class Matrix:
 
     def matvec(self, x, threads=None):
         return self.matvec_rows(0, self.rows, x, threads)
+
+    def transpose_rows_matvec(self, start, x):
+        """WeightMatrix::transpose_rows_matvec (src/model/weight.rs:332-343): rows
+        start..start+len(x) transposed times x -> [cols]."""
+        x = np.ascontiguousarray(x, dtype=np.float32).ravel()
+        y = np.empty(self.cols, dtype=np.float32)
+        _check(lib().urbo_transpose_rows_matvec(ctypes.byref(self.c), start, _ptr(x), x.size,
+                                                _ptr(y)))
+        return y
 
     def matvec_fp32(self, x, start=0, count=None, threads=None):
         x = np.ascontiguousarray(x, dtype=np.float32)

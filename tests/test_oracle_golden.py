@@ -397,3 +397,42 @@ def test_bf16_fp32_lanes_formula(oracle):
         for c in range(complete, cols):
             s = np.float32(s + np.float32(wf[c] * x[c]))
         assert bits(oracle.dot_bf16_fp32_lanes(w, x)) == bits(s), cols
+
+
+def test_transpose_rows_matvec_golden(oracle):
+    # src/model/bf16.rs:960-974 and src/model/weight.rs:425-440: W = [[-1, 2], [3, -4]].
+    def bf16(v):
+        return (np.asarray(v, np.float32).view(np.uint32) >> 16).astype(np.uint16)
+    for m in (oracle.Matrix(oracle.BF16, 2, 2, bf16([-1.0, 2.0, 3.0, -4.0])),
+              oracle.Matrix(oracle.F32, 2, 2, np.array([-1.0, 2.0, 3.0, -4.0], np.float32))):
+        assert list(m.transpose_rows_matvec(0, [0.5, 2.0])) == [5.5, -7.0]
+        assert list(m.transpose_rows_matvec(1, [2.0])) == [6.0, -8.0]
+        assert list(m.transpose_rows_matvec(2, [])) == [0.0, 0.0]
+        with pytest.raises(oracle.OracleError):
+            m.transpose_rows_matvec(1, [1.0, 1.0])
+        with pytest.raises(oracle.OracleError):
+            m.transpose_rows_matvec(0, [np.inf])
+
+
+def test_transpose_rows_matvec_formula(oracle):
+    # Ordered f64 column sums (mxfp.rs:785-858, 1782-1821) restated in numpy over decoded
+    # weights, MXFP4 with odd columns and MXFP8 with 2 x 64 scale blocks.
+    from urbilateria_b200 import synthetic as syn
+    g = syn.rng(4242)
+    packed, scales = syn.mxfp4_matrix(g, 9, 37)
+    m4 = oracle.Matrix(oracle.MXFP4, 9, 37, packed, scales, group_size=32)
+    vals = syn.encode_e4m3fn(g.standard_normal((9, 130)).astype(np.float32))
+    sc8 = g.integers(117, 124, size=(5, 3), dtype=np.uint8)
+    m8 = oracle.Matrix(oracle.MXFP8, 9, 130, vals, sc8, block_rows=2, block_cols=64)
+    x = (g.standard_normal(6) * 3).astype(np.float32)
+    for m, dec in ((m4, lambda r, c: oracle.lib().urbo_decode_e2m1(
+                        int(packed[r, c // 2]) >> (4 * (c % 2)) & 15) *
+                    oracle.lib().urbo_decode_e8m0(int(scales[r, c // 32]))),
+                   (m8, lambda r, c: oracle.lib().urbo_decode_e4m3fn(int(vals[r, c])) *
+                    oracle.lib().urbo_decode_e8m0(int(sc8[r // 2, c // 64])))):
+        got = m.transpose_rows_matvec(2, x)
+        for c in range(m.cols):
+            s = 0.0
+            for i in range(6):
+                s += float(np.float32(x[i])) * float(np.float32(dec(2 + i, c)))
+            assert np.float32(s) == got[c], c

@@ -111,6 +111,22 @@ class _Matrix:
         self.ctx.check(self.ctx.lib.urb_mat_info(self.h, None, None, None, ctypes.byref(v)))
         return v.value
 
+    def transpose_rows_matvec(self, start: int, x) -> np.ndarray:
+        """WeightMatrix::transpose_rows_matvec (src/model/weight.rs:332-343): rows
+        start..start+len(x) of the matrix, transposed, times x -> [cols]."""
+        x = np.ascontiguousarray(x, dtype=np.float32).ravel()
+        y = np.empty(self._cols, dtype=np.float32)
+        self.ctx.check(self.ctx.lib.urb_transpose_rows_matvec(
+            self.ctx.h, self.h, start, _ptr(x) if x.size else None, x.size, _ptr(y)))
+        return y
+
+    def transpose_matvec(self, x) -> np.ndarray:
+        """WeightMatrix::transpose_matvec: all rows, transposed, times x [rows]."""
+        x = np.ascontiguousarray(x, dtype=np.float32).ravel()
+        if x.size != self._rows:
+            raise UrbError(native.ERR_SHAPE, "transpose input length %d != %d rows" % (x.size, self._rows))
+        return self.transpose_rows_matvec(0, x)
+
     def matvec_rows(self, start: int, count: int, x) -> np.ndarray:
         x = np.ascontiguousarray(x, dtype=np.float32).ravel()
         y = np.empty(count, dtype=np.float32)

@@ -98,6 +98,7 @@ SIGNATURES = [
     ("urb_moe_forward_routed_ex_device", I32, [P, P, P, SZ, P, P, P, P, P]),
     ("urb_simulate_e4m3_activation", I32, [P, P, SZ, SZ, P]),
     ("urb_simulate_finegrained_e4m3_activation", I32, [P, P, SZ, SZ, P]),
+    ("urb_transpose_rows_matvec", I32, [P, P, SZ, P, SZ, P]),
     ("urb_linear_bf16_fp32_lanes", I32, [P, P, P, SZ, P]),
     ("urb_moe_forward_ex", I32, [P, P, P, SZ, P, P, P, P, P]),
     ("urb_route_sqrt_softplus", I32, [P, P, P, SZ, SZ, P, U32, ctypes.c_float, P, P, P]),
