@@ -170,6 +170,30 @@ float dot_f32_f64(const float *row, const float *x, size_t cols) {
     return float(sum);
 }
 
+// src/math/quant.rs:448-499 Int8Matrix::matvec_rows: `sum::<f64>()` of f64(i8) * f64(x) (Rust
+// 1.88 folds from -0.0), times f64(row scale), rounded to f32.
+float dot_int8_f64(const urbo_matrix *m, size_t row, const float *x) {
+    const int8_t *w = static_cast<const int8_t *>(m->values) + row * m->cols;
+    double sum = -0.0;
+    for (size_t c = 0; c < m->cols; ++c) sum += double(w[c]) * double(x[c]);
+    return float(sum * double(m->fscales[row]));
+}
+
+// f32 weight (row, col) of an Int4Matrix (quant.rs:343-350): (code - 8) * scale in f32.
+inline float int4_value(const urbo_matrix *m, size_t row, size_t col) {
+    const uint8_t byte = static_cast<const uint8_t *>(m->values)[row * div_ceil(m->cols, 2) + col / 2];
+    const uint8_t code = col % 2 == 0 ? (byte & 15) : (byte >> 4);
+    return float(int(code) - 8) * m->fscales[row * div_ceil(m->cols, m->group_size) + col / m->group_size];
+}
+
+// src/math/quant.rs:304-318 Int4Matrix::dot_row: ordered f64 sum from +0.0 of the widened f32
+// weights times the widened inputs, group by group in column order.
+float dot_int4_f64(const urbo_matrix *m, size_t row, const float *x) {
+    double sum = 0.0;
+    for (size_t c = 0; c < m->cols; ++c) sum += double(int4_value(m, row, c)) * double(x[c]);
+    return float(sum);
+}
+
 bool mxfp8_is_compact(const urbo_matrix *m) { return m->block_rows == 1 && m->block_cols == 32; }
 
 // One row of WeightMatrix::matvec for the single-input dispatch of each format.
@@ -187,6 +211,10 @@ float dot_row(const urbo_matrix *m, size_t row, const float *x) {
         return dot_mxfp4_f64(static_cast<const uint8_t *>(m->values) + row * row_bytes,
                              m->scales + row * groups, x, m->cols, m->group_size);
     }
+    case URBO_INT8:
+        return dot_int8_f64(m, row, x);
+    case URBO_INT4:
+        return dot_int4_f64(m, row, x);
     }
     return NAN;
 }
@@ -242,6 +270,7 @@ uint8_t urbo_encode_e4m3fn(float value) {
 }
 
 int urbo_validate(const urbo_matrix *m) {
+    if (m && m->format == URBO_INT4 && m->group_size == 0) return URBO_ERR_INVALID_GROUP;
     if (!m || m->rows == 0 || m->cols == 0) return URBO_ERR_SHAPE;
     size_t n = m->rows * m->cols;
     switch (m->format) {
@@ -263,6 +292,13 @@ int urbo_validate(const urbo_matrix *m) {
         size_t ns = m->rows * div_ceil(m->cols, m->group_size);
         for (size_t i = 0; i < ns; ++i)
             if (m->scales[i] == 0xff) return URBO_ERR_INVALID_SCALE;
+        return URBO_OK;
+    }
+    case URBO_INT8:    // quant.rs:363-396: shape, then every scale finite and > 0
+    case URBO_INT4: {  // quant.rs:92-131 (group size checked before the shape)
+        size_t ns = m->format == URBO_INT8 ? m->rows : m->rows * div_ceil(m->cols, m->group_size);
+        for (size_t i = 0; i < ns; ++i)
+            if (!finite(m->fscales[i]) || !(m->fscales[i] > 0.0f)) return URBO_ERR_NONFINITE;
         return URBO_OK;
     }
     }
@@ -305,6 +341,13 @@ int urbo_transpose_rows_matvec(const urbo_matrix *m, size_t start, const float *
                     e8m0(m->scales[(r / m->block_rows) * sc + c / m->block_cols]);
                 break;
             }
+            case URBO_INT8: {
+                // quant.rs:512-553: (f64(x) * f64(row scale)) * f64(i8), each product rounded.
+                const double scaled = double(x[i]) * double(m->fscales[r]);
+                sum += scaled * double(static_cast<const int8_t *>(m->values)[r * m->cols + c]);
+                continue;
+            }
+            case URBO_INT4: w = int4_value(m, r, c); break;  // quant.rs:236-283
             default: {  // MXFP4
                 const uint8_t byte = static_cast<const uint8_t *>(m->values)[r * div_ceil(m->cols, 2) + c / 2];
                 w = kE2M1[(c % 2 == 0 ? byte : byte >> 4) & 15] *
@@ -316,6 +359,71 @@ int urbo_transpose_rows_matvec(const urbo_matrix *m, size_t start, const float *
         y[c] = float(sum);
     }
     if (m->format == URBO_MXFP8 && any_nonfinite(y, m->cols)) return URBO_ERR_NONFINITE;
+    return URBO_OK;
+}
+
+// src/math/quant.rs:600-617 round_ties_even of an f32, as an integer.
+static int32_t round_ties_even_i32(float value) {
+    const float fl = std::floor(value);
+    const float fraction = value - fl;
+    const int32_t lower = int32_t(fl);
+    if (fraction < 0.5f) return lower;
+    if (fraction > 0.5f) return lower + 1;
+    return lower % 2 == 0 ? lower : lower + 1;
+}
+
+int urbo_int4_quantize_grouped(size_t rows, size_t cols, size_t group, const float *values,
+                               uint8_t *packed, float *scales) {
+    // quant.rs:575-598 validate_geometry, then finiteness (:53-55).
+    if (group == 0) return URBO_ERR_INVALID_GROUP;
+    if (rows == 0 || cols == 0) return URBO_ERR_SHAPE;
+    if (any_nonfinite(values, rows * cols)) return URBO_ERR_NONFINITE;
+    const size_t row_bytes = div_ceil(cols, 2), groups = div_ceil(cols, group);
+    std::fill(packed, packed + rows * row_bytes, uint8_t(0x88));
+    for (size_t r = 0; r < rows; ++r) {
+        const float *v = values + r * cols;
+        for (size_t g = 0; g < groups; ++g) {
+            float maximum = 0.0f;  // fold of f32::max over |v| (no NaN: inputs are finite)
+            for (size_t c = g * group; c < std::min(cols, (g + 1) * group); ++c)
+                maximum = std::max(maximum, std::fabs(v[c]));
+            scales[r * groups + g] = std::max(maximum / 7.0f, 1e-8f);
+        }
+        for (size_t c = 0; c < cols; ++c) {
+            const float scale = scales[r * groups + c / group];
+            const int32_t q = std::min(std::max(round_ties_even_i32(v[c] / scale), -8), 7);
+            const uint8_t code = uint8_t(q + 8);
+            uint8_t &byte = packed[r * row_bytes + c / 2];
+            byte = c % 2 == 0 ? uint8_t((byte & 0xf0) | code) : uint8_t((byte & 0x0f) | (code << 4));
+        }
+    }
+    return URBO_OK;
+}
+
+int urbo_write_row(const urbo_matrix *m, size_t row, float *out) {
+    if (row >= m->rows) return URBO_ERR_SHAPE;
+    const float *e4 = tables().e4m3;
+    for (size_t c = 0; c < m->cols; ++c) {
+        switch (m->format) {
+        case URBO_F32: out[c] = static_cast<const float *>(m->values)[row * m->cols + c]; break;
+        case URBO_BF16: out[c] = bf16f(static_cast<const uint16_t *>(m->values)[row * m->cols + c]); break;
+        case URBO_MXFP8: {
+            const size_t sc = div_ceil(m->cols, m->block_cols);
+            out[c] = e4[static_cast<const uint8_t *>(m->values)[row * m->cols + c]] *
+                     e8m0(m->scales[(row / m->block_rows) * sc + c / m->block_cols]);
+            break;
+        }
+        case URBO_MXFP4: {
+            const uint8_t byte = static_cast<const uint8_t *>(m->values)[row * div_ceil(m->cols, 2) + c / 2];
+            out[c] = kE2M1[(c % 2 == 0 ? byte : byte >> 4) & 15] *
+                     e8m0(m->scales[row * div_ceil(m->cols, m->group_size) + c / m->group_size]);
+            break;
+        }
+        case URBO_INT8:  // quant.rs:414-436
+            out[c] = float(static_cast<const int8_t *>(m->values)[row * m->cols + c]) * m->fscales[row];
+            break;
+        default: out[c] = int4_value(m, row, c);
+        }
+    }
     return URBO_OK;
 }
 

@@ -29,6 +29,8 @@ enum {
     URBO_BF16 = 1,
     URBO_MXFP8 = 2, /* E4M3 values + E8M0 block scales (src/math/mxfp.rs:321-877) */
     URBO_MXFP4 = 3, /* packed E2M1 nibbles + E8M0 group scales (src/math/mxfp.rs:1363-1847) */
+    URBO_INT8 = 4,  /* Int8Matrix: two's-complement bytes, one f32 scale per row (src/math/quant.rs:355-573) */
+    URBO_INT4 = 5,  /* Int4Matrix: low-nibble-first codes (value code - 8), f32 group scales (quant.rs:28-350) */
 };
 
 enum {
@@ -38,6 +40,7 @@ enum {
     URBO_ERR_NONFINITE = 3,
     URBO_ERR_INVALID_GEOMETRY = 4,
     URBO_ERR_INVALID = 9,  /* DeepseekMathError::Invalid (bad hash ids, non-positive scale) */
+    URBO_ERR_INVALID_GROUP = 11, /* QuantError::InvalidGroupSize (src/math/quant.rs:12) */
 };
 
 typedef struct urbo_matrix {
@@ -47,6 +50,7 @@ typedef struct urbo_matrix {
     size_t block_rows, block_cols; /* MXFP8: scale block */
     const void *values;            /* f32 | bf16 bits (u16) | E4M3 bytes | packed nibbles */
     const uint8_t *scales;         /* E8M0 bytes (MX formats) */
+    const float *fscales;          /* f32 scales (INT8: [rows]; INT4: [rows, ceil(cols/group)]) */
 } urbo_matrix;
 
 /* Codecs (src/math/mxfp.rs:44-79, 247-275). */
@@ -56,8 +60,15 @@ float urbo_decode_e2m1(uint8_t code);
 uint8_t urbo_encode_e4m3fn(float value);
 float urbo_expf(float value);           /* the libm expf the Rust reference links */
 
-/* Constructor validation: shape, then payload (mxfp.rs:1400-1443, 394-425). */
+/* Constructor validation: shape, then payload (mxfp.rs:1400-1443, 394-425; quant.rs:92-131,
+ * 363-396 for the INT formats). */
 int urbo_validate(const urbo_matrix *m);
+/* Int4Matrix::quantize_grouped (src/math/quant.rs:46-90): packed [rows, ceil(cols/2)],
+ * scales [rows, ceil(cols/group)]. */
+int urbo_int4_quantize_grouped(size_t rows, size_t cols, size_t group, const float *values,
+                               uint8_t *packed, float *scales);
+/* WeightMatrix::write_row (src/model/weight.rs:345-365): the decoded f32 weights of one row. */
+int urbo_write_row(const urbo_matrix *m, size_t row, float *out);
 
 /* WeightMatrix::matvec_rows / MxFp4Matrix::matvec_rows etc.  y has `count` entries. */
 /* WeightMatrix::transpose_rows_matvec (src/model/weight.rs:332-343): y[cols] = rows

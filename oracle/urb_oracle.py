@@ -17,8 +17,9 @@ import numpy as np
 _HERE = os.path.dirname(os.path.abspath(__file__))
 _LIB_PATH = os.path.join(_HERE, "liburb_oracle.so")
 
-F32, BF16, MXFP8, MXFP4 = 0, 1, 2, 3
+F32, BF16, MXFP8, MXFP4, INT8, INT4 = 0, 1, 2, 3, 4, 5
 OK, ERR_SHAPE, ERR_INVALID_SCALE, ERR_NONFINITE, ERR_INVALID_GEOMETRY = 0, 1, 2, 3, 4
+ERR_INVALID_GROUP = 11
 
 
 class OracleMatrix(ctypes.Structure):
@@ -31,6 +32,7 @@ class OracleMatrix(ctypes.Structure):
         ("block_cols", ctypes.c_size_t),
         ("values", ctypes.c_void_p),
         ("scales", ctypes.c_void_p),
+        ("fscales", ctypes.c_void_p),
     ]
 
 
@@ -94,6 +96,11 @@ def lib():
             ctypes.POINTER(OracleMatrix), ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p,
             ctypes.c_int]
         _lib.urbo_validate.argtypes = [ctypes.POINTER(OracleMatrix)]
+        _lib.urbo_int4_quantize_grouped.argtypes = [
+            ctypes.c_size_t, ctypes.c_size_t, ctypes.c_size_t, ctypes.c_void_p, ctypes.c_void_p,
+            ctypes.c_void_p]
+        _lib.urbo_write_row.argtypes = [ctypes.POINTER(OracleMatrix), ctypes.c_size_t,
+                                        ctypes.c_void_p]
         _lib.urbo_gated_mlp_forward.argtypes = [
             ctypes.POINTER(OracleMatrix), ctypes.POINTER(OracleMatrix),
             ctypes.POINTER(OracleMatrix), ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int]
@@ -157,10 +164,14 @@ class Matrix:
                  block_cols=32, validate=True):
         self.fmt, self.rows, self.cols = fmt, rows, cols
         self.values = np.ascontiguousarray(values)
-        self.scales = None if scales is None else np.ascontiguousarray(scales, dtype=np.uint8)
+        # MX formats carry E8M0 scale bytes; Int8Matrix / Int4Matrix carry f32 scales.
+        sdt = np.float32 if fmt in (INT8, INT4) else np.uint8
+        self.scales = None if scales is None else np.ascontiguousarray(scales, dtype=sdt)
         self.group_size, self.block_rows, self.block_cols = group_size, block_rows, block_cols
+        sp = 0 if self.scales is None else _ptr(self.scales)
         self.c = OracleMatrix(fmt, rows, cols, group_size, block_rows, block_cols,
-                              _ptr(self.values), 0 if self.scales is None else _ptr(self.scales))
+                              _ptr(self.values), 0 if fmt in (INT8, INT4) else sp,
+                              sp if fmt in (INT8, INT4) else 0)
         if validate:
             _check(lib().urbo_validate(ctypes.byref(self.c)))
 
@@ -186,6 +197,12 @@ class Matrix:
                                                 _ptr(y)))
         return y
 
+    def write_row(self, row):
+        """WeightMatrix::write_row (src/model/weight.rs:345-365): one decoded f32 row."""
+        y = np.empty(self.cols, dtype=np.float32)
+        _check(lib().urbo_write_row(ctypes.byref(self.c), row, _ptr(y)))
+        return y
+
     def matvec_fp32(self, x, start=0, count=None, threads=None):
         x = np.ascontiguousarray(x, dtype=np.float32)
         count = self.rows if count is None else count
@@ -203,6 +220,19 @@ class Matrix:
         _check(lib().urbo_matmul_rows(ctypes.byref(self.c), _ptr(x), batch, _ptr(y),
                                       threads or default_threads()))
         return y
+
+
+def int4_quantize_grouped(rows, cols, group_size, values):
+    """Int4Matrix::quantize_grouped (src/math/quant.rs:46-90) -> (packed u8, scales f32)."""
+    v = np.ascontiguousarray(values, dtype=np.float32).ravel()
+    if v.size != rows * cols:
+        raise OracleError(ERR_SHAPE)
+    packed = np.empty(rows * ((cols + 1) // 2), dtype=np.uint8)
+    scales = np.empty(rows * ((cols + group_size - 1) // group_size if group_size else 1),
+                      dtype=np.float32)
+    _check(lib().urbo_int4_quantize_grouped(rows, cols, group_size, _ptr(v), _ptr(packed),
+                                            _ptr(scales)))
+    return packed, scales
 
 
 def route_noaux_tc(logits, bias, top_k, n_group=1, topk_group=1, normalize=True, scaling=1.0):

@@ -436,3 +436,126 @@ def test_transpose_rows_matvec_formula(oracle):
             for i in range(6):
                 s += float(np.float32(x[i])) * float(np.float32(dec(2 + i, c)))
             assert np.float32(s) == got[c], c
+
+
+# --- INT8 per-row / INT4 grouped (GLM converted checkpoints) -----------------------------------
+
+def _seq_f64(pairs, start=0.0):
+    """Ordered f64 sum of exact widened products, as the reference's scalar loops."""
+    s = start
+    for w, v in pairs:
+        s = s + float(np.float32(w)) * float(np.float32(v))
+    return s
+
+
+def test_int8_twos_complement_bytes_and_row_scales(oracle):
+    # src/math/quant.rs:694-720
+    m = oracle.Matrix(oracle.INT8, 2, 3, np.array([0xff, 0x00, 0x7f, 0x80, 0x02, 0xfe], np.uint8),
+                      np.array([0.5, 0.25], np.float32))
+    assert list(m.write_row(0)) == [-0.5, 0.0, 63.5]
+    assert list(m.write_row(1)) == [-32.0, 0.5, -0.5]
+    x = np.array([2.0, -1.0, 0.5], np.float32)
+    explicit = [np.float32(sum(np.float32(w) * np.float32(v) for w, v in zip(m.write_row(r), x)))
+                for r in range(2)]
+    assert list(m.matvec(x)) == explicit
+
+
+def test_int_formats_share_matvec_and_row_contracts(oracle):
+    # src/model/weight.rs:416-442 (the INT8 and INT4 matrices of the mixed-format test)
+    i8 = oracle.Matrix(oracle.INT8, 2, 2, np.array([0xff, 2, 3, 0xfc], np.uint8),
+                       np.array([1.0, 1.0], np.float32))
+    i4 = oracle.Matrix(oracle.INT4, 2, 2, np.array([0xa7, 0x4b], np.uint8),
+                       np.array([1.0, 1.0], np.float32), group_size=2)
+    for m in (i8, i4):
+        assert list(m.write_row(0)) == [-1.0, 2.0]
+        assert list(m.matvec(np.array([0.5, 2.0], np.float32))) == [3.5, -6.5]
+        assert list(m.matmul_rows(np.array([0.5, 2.0, 1.0, -1.0], np.float32), 2).ravel()) == \
+            [3.5, -6.5, -3.0, 7.0]
+        assert list(m.transpose_rows_matvec(0, [0.5, 2.0])) == [5.5, -7.0]
+        assert list(m.transpose_rows_matvec(1, [2.0])) == [6.0, -8.0]
+        assert list(m.matvec_rows(1, 1, np.array([0.5, 2.0], np.float32))) == [-6.5]
+
+
+def test_int4_packs_low_nibble_first_with_zero_tail(oracle):
+    # src/math/quant.rs:622-631
+    packed, scales = oracle.int4_quantize_grouped(1, 3, 3, [-8.0, 7.0, 0.0])
+    assert packed.size == 2
+    assert packed[0] & 0x0F == 1 and packed[0] >> 4 == 14
+    assert packed[1] & 0x0F == 8 and packed[1] >> 4 == 8
+    assert scales[0] == np.float32(8.0) / np.float32(7.0)
+
+
+def test_int4_grouped_scales_reduce_outlier_damage(oracle):
+    # src/math/quant.rs:633-641
+    values = [100.0, 0.5, 0.5, 0.5]
+    per_row = oracle.Matrix(oracle.INT4, 1, 4, *oracle.int4_quantize_grouped(1, 4, 4, values),
+                            group_size=4)
+    grouped = oracle.Matrix(oracle.INT4, 1, 4, *oracle.int4_quantize_grouped(1, 4, 2, values),
+                            group_size=2)
+    assert abs(grouped.write_row(0)[2] - 0.5) < abs(per_row.write_row(0)[2] - 0.5)
+
+
+def test_int4_matvec_matches_explicit_dequantization(oracle):
+    # src/math/quant.rs:643-660
+    packed, scales = oracle.int4_quantize_grouped(2, 4, 2, [1.0, -2.0, 3.0, 4.0, -1.0, 0.5, 2.0, -3.0])
+    m = oracle.Matrix(oracle.INT4, 2, 4, packed, scales, group_size=2)
+    x = np.array([0.25, 2.0, -1.0, 0.5], np.float32)
+    for r, actual in enumerate(m.matvec(x)):
+        expected = np.float32(sum(np.float32(w) * v for w, v in zip(m.write_row(r), x)))
+        assert abs(actual - expected) < 1e-5
+
+
+def test_int4_row_range_kernels_handle_odd_groups_and_tail_nibbles(oracle):
+    # src/math/quant.rs:662-691: 3 x 7 with 3-column groups; bit-exact ordered f64 sums.
+    values = [np.float32((np.float32(i) - np.float32(10.0)) * np.float32(0.17)) for i in range(21)]
+    packed, scales = oracle.int4_quantize_grouped(3, 7, 3, values)
+    m = oracle.Matrix(oracle.INT4, 3, 7, packed, scales, group_size=3)
+    x = np.array([0.2, -0.4, 0.6, -0.8, 1.0, -1.2, 1.4], np.float32)
+    for off, actual in enumerate(m.matvec_rows(1, 2, x)):
+        assert bits(actual) == bits(np.float32(_seq_f64(zip(m.write_row(off + 1), x))))
+    t = m.transpose_rows_matvec(1, [0.25, -0.75])
+    for c in range(7):
+        expected = np.float32(_seq_f64([(m.write_row(r)[c], v) for r, v in zip((1, 2), (0.25, -0.75))]))
+        assert bits(t[c]) == bits(expected)
+
+
+def _rust_i8_rem31(index):
+    """`(index as i8 % 31)`: wrapping cast to i8, then Rust's truncating remainder."""
+    v = ((index & 0xFF) ^ 0x80) - 0x80
+    return v % 31 if v >= 0 else -((-v) % 31)
+
+
+def test_int_large_kernels_bit_exact_against_ordered_scalar_dots(oracle):
+    # src/model/weight.rs:497-616, the INT8 and INT4 matrices (65 x 1025).
+    rows, cols = 65, 1025
+    x = np.array([(c % 17 - 8.0) / 16.0 for c in range(cols)], np.float32)
+    tx = np.array([(r % 11 - 5.0) / 8.0 for r in range(rows)], np.float32)
+    i8 = oracle.Matrix(oracle.INT8, rows, cols,
+                       np.array([_rust_i8_rem31(i) & 0xFF for i in range(rows * cols)], np.uint8),
+                       np.full(rows, 0.03125, np.float32))
+    i4 = oracle.Matrix(oracle.INT4, rows, cols,
+                       np.array([(i * 37) & 0xFF for i in range(rows * ((cols + 1) // 2))], np.uint8),
+                       np.full(rows * ((cols + 63) // 64), 0.0625, np.float32), group_size=64)
+    for m in (i8, i4):
+        mat = np.stack([m.write_row(r) for r in range(rows)])
+        y = m.matvec(x)
+        for r in range(rows):
+            assert bits(y[r]) == bits(np.float32(_seq_f64(zip(mat[r], x), -0.0)))
+        t = m.transpose_rows_matvec(0, tx)
+        for c in range(0, cols, 7):
+            assert bits(t[c]) == bits(np.float32(_seq_f64(zip(mat[:, c], tx))))
+
+
+def test_int_constructor_validation(oracle):
+    # quant.rs:92-131 (group size, shape, then scales finite and positive), :363-396
+    with pytest.raises(oracle.OracleError) as e:
+        oracle.Matrix(oracle.INT4, 1, 2, np.zeros(1, np.uint8), np.ones(1, np.float32), group_size=0)
+    assert e.value.code == oracle.ERR_INVALID_GROUP
+    for bad in (0.0, -1.0, np.inf, np.nan):
+        for fmt, vals in ((oracle.INT8, np.zeros(2, np.uint8)), (oracle.INT4, np.zeros(1, np.uint8))):
+            with pytest.raises(oracle.OracleError) as e:
+                oracle.Matrix(fmt, 1, 2, vals, np.array([bad], np.float32), group_size=2)
+            assert e.value.code == oracle.ERR_NONFINITE
+    with pytest.raises(oracle.OracleError) as e:
+        oracle.int4_quantize_grouped(1, 2, 2, [1.0, np.nan])
+    assert e.value.code == oracle.ERR_NONFINITE
