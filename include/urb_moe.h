@@ -59,6 +59,7 @@ typedef enum urb_status {
     URB_ERR_UNSUPPORTED = 8,       /* configuration outside what this build implements */
     URB_ERR_INVALID_ARGUMENT = 9,  /* null handle / pointer */
     URB_ERR_PEER = 10,             /* another rank of the expert-parallel group failed the forward */
+    URB_ERR_INVALID_GROUP = 11,    /* QuantError::InvalidGroupSize (src/math/quant.rs:10-14) */
 } urb_status;
 
 typedef enum urb_format {
@@ -66,6 +67,8 @@ typedef enum urb_format {
     URB_FMT_BF16 = 1,  /* Bf16Matrix (src/model/bf16.rs) */
     URB_FMT_MXFP8 = 2, /* MxFp8Matrix with E8M0 scales (src/math/mxfp.rs:321) */
     URB_FMT_MXFP4 = 3, /* MxFp4Matrix (src/math/mxfp.rs:1363) */
+    URB_FMT_INT8 = 4,  /* Int8Matrix: two's-complement bytes, f32 scale per row (src/math/quant.rs:355) */
+    URB_FMT_INT4 = 5,  /* Int4Matrix: low-nibble-first codes (code - 8), f32 group scales (quant.rs:33) */
 } urb_format;
 
 typedef struct urb_ctx urb_ctx;
@@ -105,6 +108,25 @@ URB_API int urb_bf16_upload(urb_ctx *ctx, size_t rows, size_t cols, const uint16
 /* DenseMatrix::new (src/model/matrix.rs). */
 URB_API int urb_f32_upload(urb_ctx *ctx, size_t rows, size_t cols, const float *values,
                    size_t values_len, urb_mat **out);
+/* Int8Matrix::from_packed (src/math/quant.rs:363-396): bytes [rows, cols], one f32 scale per
+ * row.  Shape (zero dimensions, payload or scale counts), then NonFinite for a scale that is not
+ * finite and positive.  Host or device pointers.  WeightMatrix::Int8PerRow (weight.rs:57). */
+URB_API int urb_int8_upload(urb_ctx *ctx, size_t rows, size_t cols, const uint8_t *bytes,
+                            size_t bytes_len, const float *scales, size_t scales_len, urb_mat **out);
+/* Int4Matrix::from_packed (src/math/quant.rs:92-131): packed [rows, ceil(cols/2)] low nibble
+ * first, f32 scales [rows, ceil(cols/group_size)].  InvalidGroup for group_size 0, Shape, then
+ * NonFinite for a scale that is not finite and positive.  WeightMatrix::Int4 (weight.rs:58). */
+URB_API int urb_int4_upload(urb_ctx *ctx, size_t rows, size_t cols, size_t group_size,
+                            const uint8_t *packed, size_t packed_len, const float *scales,
+                            size_t scales_len, urb_mat **out);
+/* Int4Matrix::quantize_grouped (src/math/quant.rs:46-90; quantize_per_row is group_size ==
+ * cols): quantises f32 values [rows, cols] on the device, bit-exact with the reference, and
+ * keeps the result resident.  InvalidGroup, Shape, then NonFinite for a non-finite value. */
+URB_API int urb_int4_quantize_grouped(urb_ctx *ctx, size_t rows, size_t cols, size_t group_size,
+                                      const float *values, size_t values_len, urb_mat **out);
+/* Int4Matrix packed()/scales() (quant.rs:145-151): copies the resident payload out (host or
+ * device pointers, sizes as in urb_int4_upload).  URB_ERR_UNSUPPORTED for other formats. */
+URB_API int urb_int4_payload(urb_ctx *ctx, const urb_mat *mat, uint8_t *packed, float *scales);
 URB_API int urb_mat_free(urb_mat *mat);
 /* WeightMatrix::{rows, cols, resident_bytes} (src/model/weight.rs:69-90, 306-320).
  * resident_bytes counts the payload bytes of the reference format. */
@@ -229,6 +251,11 @@ URB_API int urb_moe_forward_routed_device(urb_ctx *ctx, urb_layer *layer, const 
  * URB_ERR_SHAPE when start + n exceeds the rows; MXFP8 also rejects non-finite outputs. */
 URB_API int urb_transpose_rows_matvec(urb_ctx *ctx, const urb_mat *mat, size_t start,
                                       const float *x, size_t n, float *y);
+/* WeightMatrix::write_row / row (src/model/weight.rs:347-392; quant.rs:163-182, 414-436,
+ * mxfp.rs:860-875, 1828-1845, bf16.rs:88-113): the decoded f32 weights of rows start..start+count into out
+ * [count, cols] (host pointer), every format.  Shape when the range exceeds the rows. */
+URB_API int urb_mat_write_rows(urb_ctx *ctx, const urb_mat *mat, size_t start, size_t count,
+                               float *out);
 
 /* ---- checkpoint numerics ---------------------------------------------------------------------- */
 

@@ -127,6 +127,17 @@ class _Matrix:
             raise UrbError(native.ERR_SHAPE, "transpose input length %d != %d rows" % (x.size, self._rows))
         return self.transpose_rows_matvec(0, x)
 
+    def write_rows(self, start: int, count: int) -> np.ndarray:
+        """WeightMatrix::write_row for rows start..start+count -> [count, cols] f32."""
+        out = np.empty((count, self._cols), dtype=np.float32)
+        self.ctx.check(self.ctx.lib.urb_mat_write_rows(self.ctx.h, self.h, start, count,
+                                                       _ptr(out) if count else None))
+        return out
+
+    def row(self, row: int) -> np.ndarray:
+        """WeightMatrix::row (src/model/weight.rs:388-392): one decoded row."""
+        return self.write_rows(row, 1)[0]
+
     def matvec_rows(self, start: int, count: int, x) -> np.ndarray:
         x = np.ascontiguousarray(x, dtype=np.float32).ravel()
         y = np.empty(count, dtype=np.float32)
@@ -243,6 +254,76 @@ class DenseMatrix(_Matrix):
         ctx.check(ctx.lib.urb_f32_upload(ctx.h, rows, cols, _ptr(data), data.size,
                                          ctypes.byref(h)))
         return cls(ctx, h, rows, cols)
+
+
+class Int8Matrix(_Matrix):
+    """Int8Matrix (src/math/quant.rs:355-573): two's-complement bytes [rows, cols] with one f32
+    scale per row (WeightMatrix::Int8PerRow), resident in HBM."""
+
+    fmt = native.FMT_INT8
+
+    @classmethod
+    def from_packed(cls, rows: int, cols: int, data, scales, ctx: Optional[Context] = None):
+        ctx = ctx or default_context()
+        data = np.ascontiguousarray(data).view(np.uint8).ravel()
+        scales = np.ascontiguousarray(scales, dtype=np.float32).ravel()
+        h = ctypes.c_void_p()
+        ctx.check(ctx.lib.urb_int8_upload(ctx.h, rows, cols, _ptr(data), data.size, _ptr(scales),
+                                          scales.size, ctypes.byref(h)))
+        return cls(ctx, h, rows, cols)
+
+
+class Int4Matrix(_Matrix):
+    """Int4Matrix (src/math/quant.rs:28-350): low-nibble-first codes (value code - 8) with f32
+    scales per group of `group_size` columns (WeightMatrix::Int4), resident in HBM."""
+
+    fmt = native.FMT_INT4
+
+    def __init__(self, ctx: Context, handle: ctypes.c_void_p, rows: int, cols: int,
+                 group_size: int = 0):
+        super().__init__(ctx, handle, rows, cols)
+        self._group = group_size or cols
+
+    def group_size(self) -> int:
+        return self._group
+
+    @classmethod
+    def from_packed(cls, rows: int, cols: int, group_size: int, packed, scales,
+                    ctx: Optional[Context] = None):
+        ctx = ctx or default_context()
+        packed = np.ascontiguousarray(packed, dtype=np.uint8).ravel()
+        scales = np.ascontiguousarray(scales, dtype=np.float32).ravel()
+        h = ctypes.c_void_p()
+        ctx.check(ctx.lib.urb_int4_upload(ctx.h, rows, cols, group_size, _ptr(packed), packed.size,
+                                          _ptr(scales), scales.size, ctypes.byref(h)))
+        return cls(ctx, h, rows, cols, group_size)
+
+    @classmethod
+    def quantize_grouped(cls, rows: int, cols: int, group_size: int, values,
+                         ctx: Optional[Context] = None):
+        """Int4Matrix::quantize_grouped (quant.rs:46-90), computed on the device."""
+        ctx = ctx or default_context()
+        values = np.ascontiguousarray(values, dtype=np.float32).ravel()
+        h = ctypes.c_void_p()
+        ctx.check(ctx.lib.urb_int4_quantize_grouped(ctx.h, rows, cols, group_size, _ptr(values),
+                                                    values.size, ctypes.byref(h)))
+        return cls(ctx, h, rows, cols, group_size)
+
+    @classmethod
+    def quantize_per_row(cls, rows: int, cols: int, values, ctx: Optional[Context] = None):
+        """Int4Matrix::quantize_per_row (quant.rs:42-44): one group per row."""
+        return cls.quantize_grouped(rows, cols, cols, values, ctx)
+
+    def packed(self) -> np.ndarray:
+        p = np.empty(self._rows * ((self._cols + 1) // 2), dtype=np.uint8)
+        s = np.empty(self._rows * ((self._cols + self._group - 1) // self._group), dtype=np.float32)
+        self.ctx.check(self.ctx.lib.urb_int4_payload(self.ctx.h, self.h, _ptr(p), _ptr(s)))
+        self._scales_cache = s
+        return p
+
+    def scales(self) -> np.ndarray:
+        self.packed()
+        return self._scales_cache
 
 
 class GatedMlp:

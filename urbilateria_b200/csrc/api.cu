@@ -157,6 +157,13 @@ int tiled_product(Ctx *ctx, const Mat *m, int rb_lo, int rb_hi, const float *d_x
 // Product of rows [start, start+count) for `batch` tokens; d_y is [batch, count].
 int device_product(Ctx *ctx, const Mat *m, size_t start, size_t count, const float *d_x,
                    size_t batch, float *d_y, int32_t *d_status, cudaStream_t st) {
+    if (is_int_format(m->format)) {
+        // Int8Matrix / Int4Matrix: warp-per-row f64 products over the packed payload.
+        prof_begin(ctx, URB_K_PRODUCT, st);
+        int rc = launch_int_matmul(ctx, m, start, count, d_x, batch, d_y, d_status, st);
+        prof_end(ctx, st);
+        return rc;
+    }
     if (bf16_gemv_applies(m, batch)) {
         // BF16 rows for a few tokens: one streaming pass on CUDA cores.
         prof_begin(ctx, URB_K_PRODUCT, st);
@@ -371,6 +378,79 @@ int urb_f32_upload(urb_ctx *ctx, size_t rows, size_t cols, const float *values,
     return finish_upload(ctx, m, values, nullptr, out);
 }
 
+int urb_int8_upload(urb_ctx *ctx, size_t rows, size_t cols, const uint8_t *bytes,
+                    size_t bytes_len, const float *scales, size_t scales_len, urb_mat **out) {
+    if (!ctx || !out || !bytes || !scales) return URB_ERR_INVALID_ARGUMENT;
+    std::lock_guard<std::recursive_mutex> lk(ctx->mu);
+    cudaSetDevice(ctx->device);
+    // quant.rs:369-383: non-zero shape with an exact payload, then one scale per row.
+    if (rows == 0 || cols == 0 || bytes_len != rows * cols)
+        return set_error(ctx, URB_ERR_SHAPE, "INT8 payload does not match the shape");
+    if (scales_len != rows) return set_error(ctx, URB_ERR_SHAPE, "INT8 needs one scale per row");
+    urb_mat *m;
+    new_mat(ctx, URB_FMT_INT8, rows, cols, &m);
+    return finish_upload(ctx, m, bytes, reinterpret_cast<const uint8_t *>(scales), out);
+}
+
+int urb_int4_upload(urb_ctx *ctx, size_t rows, size_t cols, size_t group_size,
+                    const uint8_t *packed, size_t packed_len, const float *scales,
+                    size_t scales_len, urb_mat **out) {
+    if (!ctx || !out || !packed || !scales) return URB_ERR_INVALID_ARGUMENT;
+    std::lock_guard<std::recursive_mutex> lk(ctx->mu);
+    cudaSetDevice(ctx->device);
+    // quant.rs:99-118, 575-598: group size, non-zero shape, payload and scale counts.
+    if (group_size == 0) return set_error(ctx, URB_ERR_INVALID_GROUP, "INT4 group size must be greater than zero");
+    if (rows == 0 || cols == 0) return set_error(ctx, URB_ERR_SHAPE, "rows and columns must be non-zero");
+    if (packed_len != rows * div_ceil(cols, 2))
+        return set_error(ctx, URB_ERR_SHAPE, "INT4 packed byte count does not match the shape");
+    if (scales_len != rows * div_ceil(cols, group_size))
+        return set_error(ctx, URB_ERR_SHAPE, "INT4 scale count does not match the shape");
+    urb_mat *m;
+    new_mat(ctx, URB_FMT_INT4, rows, cols, &m);
+    m->group_size = group_size;
+    return finish_upload(ctx, m, packed, reinterpret_cast<const uint8_t *>(scales), out);
+}
+
+int urb_int4_quantize_grouped(urb_ctx *ctx, size_t rows, size_t cols, size_t group_size,
+                              const float *values, size_t values_len, urb_mat **out) {
+    if (!ctx || !out || !values) return URB_ERR_INVALID_ARGUMENT;
+    *out = nullptr;
+    std::lock_guard<std::recursive_mutex> lk(ctx->mu);
+    cudaSetDevice(ctx->device);
+    if (group_size == 0) return set_error(ctx, URB_ERR_INVALID_GROUP, "INT4 group size must be greater than zero");
+    if (rows == 0 || cols == 0) return set_error(ctx, URB_ERR_SHAPE, "rows and columns must be non-zero");
+    if (values_len != rows * cols) return set_error(ctx, URB_ERR_SHAPE, "INT4 source length does not match the shape");
+    cudaStream_t st = ctx->stream;
+    const size_t nv = rows * cols * sizeof(float), np = rows * div_ceil(cols, 2),
+                 ns = rows * div_ceil(cols, group_size) * sizeof(float);
+    uint8_t *d = nullptr;
+    URB_CUDA(ctx, cudaMallocAsync(&d, nv + ns + np + 64, st));
+    float *d_v = reinterpret_cast<float *>(d), *d_s = reinterpret_cast<float *>(d + nv);
+    uint8_t *d_p = d + nv + ns;
+    int32_t *d_flag = reinterpret_cast<int32_t *>(d + ((nv + ns + np + 15) / 16) * 16);
+    int rc = URB_OK;
+    cudaError_t e = cudaMemcpyAsync(d_v, values, nv, cudaMemcpyDefault, st);
+    if (e != cudaSuccess) rc = cuda_fail(ctx, e, "INT4 source copy");
+    if (rc == URB_OK) rc = int4_quantize_device(ctx, rows, cols, group_size, d_v, d_p, d_s, d_flag, st);
+    if (rc == URB_OK) rc = urb_int4_upload(ctx, rows, cols, group_size, d_p, np, d_s, ns / sizeof(float), out);
+    cudaFreeAsync(d, st);
+    cudaStreamSynchronize(st);
+    return rc;
+}
+
+int urb_int4_payload(urb_ctx *ctx, const urb_mat *m, uint8_t *packed, float *scales) {
+    if (!ctx || !m || !packed || !scales) return URB_ERR_INVALID_ARGUMENT;
+    if (m->format != URB_FMT_INT4) return set_error(ctx, URB_ERR_UNSUPPORTED, "not an INT4 matrix");
+    std::lock_guard<std::recursive_mutex> lk(ctx->mu);
+    cudaSetDevice(ctx->device);
+    cudaStream_t st = ctx->stream;
+    URB_CUDA(ctx, cudaMemcpyAsync(packed, m->raw_values, m->rows * div_ceil(m->cols, 2), cudaMemcpyDefault, st));
+    URB_CUDA(ctx, cudaMemcpyAsync(scales, m->raw_scales,
+                                  m->rows * div_ceil(m->cols, m->group_size) * sizeof(float), cudaMemcpyDefault, st));
+    URB_CUDA(ctx, cudaStreamSynchronize(st));
+    return URB_OK;
+}
+
 int urb_mat_free(urb_mat *m) {
     if (!m) return URB_ERR_INVALID_ARGUMENT;
     if (m->ctx) {
@@ -457,8 +537,9 @@ int urb_matmul_rows_fp32_accum(urb_ctx *ctx, const urb_mat *m, const float *x, s
     if (!m) return URB_ERR_INVALID_ARGUMENT;
     int rc = matmul_common(ctx, m, 0, m->rows, x, batch, x_len, y);
     if (rc) return rc;
-    // The FP32-accumulation entry points reject non-finite outputs (mxfp.rs:1658-1723).
-    if (!all_finite(y, batch * m->rows))
+    // The FP32-accumulation entry points reject non-finite outputs (mxfp.rs:1658-1723); the INT
+    // formats take plain matvec there (weight.rs:213-220), which does not check outputs.
+    if (!is_int_format(m->format) && !all_finite(y, batch * m->rows))
         return set_error(ctx, URB_ERR_NONFINITE, "fp32-accumulated product is non-finite");
     return URB_OK;
 }

@@ -10,6 +10,15 @@ namespace {
 constexpr int kFlagInvalidScale = 1;  // an E8M0 0xFF byte (mxfp.rs:1431-1435, :422-424)
 constexpr int kFlagNanE4m3 = 2;       // an E4M3 NaN code 0x7F/0xFF (mxfp.rs:419-421)
 constexpr int kFlagWide = 4;          // a row's scales span more than f16 can hold exactly
+constexpr int kFlagBadF32Scale = 8;   // an INT scale that is not finite and positive (quant.rs:119-123, 384-389)
+
+__global__ void k_scan_fscales(const float *scales, size_t n, int *flags) {
+    size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x;
+    size_t stride = size_t(gridDim.x) * blockDim.x;
+    bool bad = false;
+    for (; i < n; i += stride) bad |= !(isfinite(scales[i]) && scales[i] > 0.0f);
+    if (__any_sync(0xffffffffu, bad) && (threadIdx.x & 31) == 0) atomicOr(flags, kFlagBadF32Scale);
+}
 
 // Largest decoded magnitude exponent (relative to scale 2^0) and the f16 window per format:
 // MXFP4 values 0.5..6 -> need 2^(s-127-E0) in [2^-23, 2^13];
@@ -140,6 +149,14 @@ int upload_matrix(Ctx *ctx, Mat *m, const void *values, const uint8_t *scales) {
     case URB_FMT_F32:
         value_bytes = m->rows * m->cols * 4;
         break;
+    case URB_FMT_INT8:  // quant.rs:555-559 resident_bytes: payload + 4 bytes per scale
+        value_bytes = m->rows * m->cols;
+        scale_bytes = m->rows * sizeof(float);
+        break;
+    case URB_FMT_INT4:  // quant.rs:285-289
+        value_bytes = m->rows * div_ceil(m->cols, 2);
+        scale_bytes = m->rows * div_ceil(m->cols, m->group_size) * sizeof(float);
+        break;
     }
     m->resident_bytes = value_bytes + scale_bytes;
 
@@ -166,6 +183,9 @@ int upload_matrix(Ctx *ctx, Mat *m, const void *values, const uint8_t *scales) {
     // Row exponents cover both layouts: 16-row tiles (mma.sync) and 128-row tiles (tcgen05).
     size_t rows_pad = div_ceil(m->rows, 128) * 128;
 
+    if (is_int_format(m->format))
+        k_scan_fscales<<<256, 256, 0, st>>>(reinterpret_cast<const float *>(m->raw_scales),
+                                            scale_bytes / sizeof(float), d_flags);
     if (m->format == URB_FMT_MXFP8) {
         k_scan_e4m3<<<1024, 256, 0, st>>>(static_cast<const uint8_t *>(m->raw_values),
                                           value_bytes, d_flags);
@@ -189,6 +209,7 @@ int upload_matrix(Ctx *ctx, Mat *m, const void *values, const uint8_t *scales) {
     // Reference validation order: E4M3 NaN before scales (mxfp.rs:419-424).
     if (flags & kFlagNanE4m3) return set_error(ctx, URB_ERR_NONFINITE, "E4M3 payload contains NaN codes");
     if (flags & kFlagInvalidScale) return set_error(ctx, URB_ERR_INVALID_SCALE, "E8M0 scale byte 0xff is NaN");
+    if (flags & kFlagBadF32Scale) return set_error(ctx, URB_ERR_NONFINITE, "INT scale is not finite and positive");
 
     // Block-scaled tensor-core layout: any MX matrix whose scale blocks are 32-column groups
     // (the tensor core applies the E8M0 scales itself, so no exponent window applies).

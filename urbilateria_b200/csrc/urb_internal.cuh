@@ -214,6 +214,12 @@ int launch_bf16_swiglu(Ctx *ctx, const Mat *g, const Mat *u, const Mat *d, const
                        int tokens, float *d_h, float *d_out, int32_t *d_status, cudaStream_t st);
 int launch_matvec1(Ctx *ctx, const Mat *m, size_t start, size_t count, const float *d_x,
                    float *d_y, cudaStream_t st);
+// quant.cu: Int8Matrix / Int4Matrix row products and the INT4 grouped quantiser.
+int launch_int_matmul(Ctx *ctx, const Mat *m, size_t start, size_t count, const float *d_x,
+                      size_t batch, float *d_y, int32_t *d_status, cudaStream_t st);
+int int4_quantize_device(Ctx *ctx, size_t rows, size_t cols, size_t group, const float *d_values,
+                         uint8_t *d_packed, float *d_scales, int32_t *d_flag, cudaStream_t st);
+inline bool is_int_format(int fmt) { return fmt == URB_FMT_INT8 || fmt == URB_FMT_INT4; }
 int launch_router_logits_f64(const double *w64, int experts, const float *d_x, int tokens,
                              int cols, double *x64, float *d_logits, cudaStream_t st,
                              const RouterGates *gates = nullptr);

@@ -22,8 +22,9 @@ ERR_NCCL = 7
 ERR_UNSUPPORTED = 8
 ERR_INVALID_ARGUMENT = 9
 ERR_PEER = 10
+ERR_INVALID_GROUP = 11
 
-FMT_F32, FMT_BF16, FMT_MXFP8, FMT_MXFP4 = 0, 1, 2, 3
+FMT_F32, FMT_BF16, FMT_MXFP8, FMT_MXFP4, FMT_INT8, FMT_INT4 = 0, 1, 2, 3, 4, 5
 
 # urb_kernel_kind
 (K_ROW_SHIFT, K_ROUTER_LOGITS, K_ROUTE, K_PERMUTE, K_GATE_UP, K_DOWN, K_COMBINE, K_PRODUCT,
@@ -38,7 +39,7 @@ STATUS_NAMES = {
     ERR_SHAPE: "Shape", ERR_INVALID_SCALE: "InvalidScale", ERR_NONFINITE: "NonFinite",
     ERR_INVALID_GEOMETRY: "InvalidGeometry", ERR_CUDA: "Cuda", ERR_TIMEOUT: "Timeout",
     ERR_NCCL: "Nccl", ERR_UNSUPPORTED: "Unsupported", ERR_INVALID_ARGUMENT: "InvalidArgument",
-    ERR_PEER: "Peer",
+    ERR_PEER: "Peer", ERR_INVALID_GROUP: "InvalidGroupSize",
 }
 
 
@@ -99,6 +100,11 @@ SIGNATURES = [
     ("urb_simulate_e4m3_activation", I32, [P, P, SZ, SZ, P]),
     ("urb_simulate_finegrained_e4m3_activation", I32, [P, P, SZ, SZ, P]),
     ("urb_transpose_rows_matvec", I32, [P, P, SZ, P, SZ, P]),
+    ("urb_mat_write_rows", I32, [P, P, SZ, SZ, P]),
+    ("urb_int8_upload", I32, [P, SZ, SZ, P, SZ, P, SZ, PP]),
+    ("urb_int4_upload", I32, [P, SZ, SZ, SZ, P, SZ, P, SZ, PP]),
+    ("urb_int4_quantize_grouped", I32, [P, SZ, SZ, SZ, P, SZ, PP]),
+    ("urb_int4_payload", I32, [P, P, P, P]),
     ("urb_linear_bf16_fp32_lanes", I32, [P, P, P, SZ, P]),
     ("urb_moe_forward_ex", I32, [P, P, P, SZ, P, P, P, P, P]),
     ("urb_route_sqrt_softplus", I32, [P, P, P, SZ, SZ, P, U32, ctypes.c_float, P, P, P]),
