@@ -4,13 +4,13 @@ row products on every kernel shape (16-byte chunks with one scale per chunk, per
 groups, byte-wise rows), transposes and decoded rows bit for bit, and the constructors' error
 order.
 
-Row products sum exact f64 products in a fixed lane order instead of the reference's column
-order, so they agree with it to the f64 rounding of the sum: the bar written below is
-|gpu - oracle| <= 2^-38 * sum_c |w_c x_c| (twice the worst-case f64 summation error at 7168
-columns) + one f32 ulp of the result per element (f32 ulp is
-2^-23 relative, so this admits at most one-ulp flips where the f64 sum sits on an f32 rounding
-boundary, or a row sum that cancels), and at least 99% of elements bit-identical.  Dyadic data,
-whose products and sums are exact, must match bit for bit."""
+Row products sum exactly in integers over x on a 38-bit fixed-point grid (16-byte rows) or sum
+exact f64 products in a fixed lane order (other shapes), so they agree with the reference's
+ordered f64 sum to within |gpu - oracle| <= 2^-38 * sum_c |w_c x_c| (twice the worst-case f64
+summation error at 7168 columns) + 2^-38 * max|x| * sum_c |w_c| (the grid) + one f32 ulp of the
+result, per element: at most one-ulp flips where the sum sits on an f32 rounding boundary, or a
+row sum that cancels.  At least 99% of elements must be bit-identical.  Dyadic data, whose
+products and sums are exact, must match bit for bit."""
 import numpy as np
 import pytest
 
@@ -48,8 +48,11 @@ def assert_rows_close(got, want, mat, x):
     """The bar in the module docstring; mat [rows, cols] decoded weights, x [batch, cols]."""
     got, want = np.asarray(got, np.float32), np.asarray(want, np.float32)
     mag = np.abs(x.astype(np.float64)) @ np.abs(mat.astype(np.float64)).T  # [batch, rows]
+    # x on the fixed-point grid: each element within 2^-38 of its token's largest magnitude.
+    grid = np.abs(x).max(axis=1, keepdims=True).astype(np.float64) * \
+        np.abs(mat.astype(np.float64)).sum(axis=1)[None, :] * 2.0 ** -38
     ulp = np.spacing(np.abs(want)).astype(np.float64)
-    bound = mag * 2.0 ** -38 + ulp
+    bound = mag * 2.0 ** -38 + grid + ulp
     err = np.abs(got.astype(np.float64) - want.astype(np.float64))
     assert np.all(err <= bound), float((err - bound).max())
     assert np.mean(bits(got) == bits(want)) >= 0.99
