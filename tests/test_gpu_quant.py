@@ -231,3 +231,34 @@ def test_int_device_status_flags_nonfinite_input(ctx):
     m.matmul_rows_device(x.data_ptr(), 3, y.data_ptr(), status.data_ptr())
     ctx.synchronize()
     assert int(status.item()) == native.ERR_NONFINITE
+
+
+@pytest.mark.parametrize("kinds,tokens", [
+    (("int4", "int4", "int4"), 1),    # GLM INT4 expert, decode
+    (("int4", "int4", "int4"), 5),
+    (("int8", "int8", "int8"), 3),
+    (("int8", "int4", "f32"), 2),     # GatedMlp::new_mixed (mlp.rs:60-81)
+])
+def test_int_gated_mlp_matches_oracle(oracle, ctx, kinds, tokens):
+    # GatedMlp::forward (src/model/mlp.rs:90-99) over INT projections: three row products and
+    # f32 SwiGLU with libm expf.  Bar: the product bar above carried through SwiGLU, written as
+    # |gpu - oracle| <= 1e-5 * max|oracle| + 4 ulp per element.
+    hidden, inter = 1024, 512
+    g = syn.rng(hash(kinds) % 1000 + tokens)
+
+    def make(kind, rows, cols):
+        if kind == "int8":
+            return int8_pair(oracle, ctx, g, rows, cols)
+        if kind == "int4":
+            return int4_pair(oracle, ctx, g, rows, cols, 64)
+        v = (g.standard_normal((rows, cols)) * 0.03).astype(np.float32)
+        return urb.DenseMatrix.new(rows, cols, v, ctx=ctx), oracle.Matrix(oracle.F32, rows, cols, v)
+
+    (dg, og), (du, ou), (dd, od) = make(kinds[0], inter, hidden), make(kinds[1], inter, hidden), \
+        make(kinds[2], hidden, inter)
+    x = g.standard_normal((tokens, hidden)).astype(np.float32)
+    got = urb.GatedMlp(dg, du, dd).forward_batch(x, tokens)
+    want = np.stack([oracle.gated_mlp_forward(og, ou, od, x[t]) for t in range(tokens)])
+    err = np.abs(got.astype(np.float64) - want)
+    bound = 1e-5 * np.abs(want).max() + 4 * np.spacing(np.abs(want)).astype(np.float64)
+    assert np.all(err <= bound), float((err - bound).max())

@@ -250,6 +250,12 @@ int finish_upload(urb_ctx *ctx, urb_mat *m, const void *values, const uint8_t *s
 }
 
 }  // namespace
+
+int product_device(Ctx *ctx, const Mat *m, size_t start, size_t count, const float *d_x,
+                   size_t batch, float *d_y, int32_t *d_status, cudaStream_t st) {
+    return device_product(ctx, m, start, count, d_x, batch, d_y, d_status, st);
+}
+
 }  // namespace urb
 
 using namespace urb;

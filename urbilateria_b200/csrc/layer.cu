@@ -8,6 +8,7 @@
 
 #include "urb_internal.cuh"
 #include "urb_moe_internal.cuh"
+#include "numerics.cuh"
 
 namespace urb {
 namespace {
@@ -410,9 +411,38 @@ int moe_forward_device(Layer *L, const float *d_x, int T, float *d_out, MoeWork 
 // GatedMlp::forward (src/model/mlp.rs:90-99) for `T` tokens on the device: one grouped pair
 // pass (gate/up with fused SwiGLU) and one grouped down pass, host-built segments; BF16
 // projections with few tokens take the streaming CUDA-core passes instead.
+// h = silu(gate) * up in f32 with libm's expf (src/model/mlp.rs:90-99, src/math/ops.rs:36-38).
+__global__ void k_swiglu_rows(const float *gate, const float *up, size_t n, ExpfTable tab, float *h) {
+    const size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x;
+    if (i < n) h[i] = __fmul_rn(num_silu_libm(gate[i], tab), up[i]);
+}
+
+// GatedMlp::forward over projections without one shared tiled layout: INT8 / INT4 (GLM's
+// converted experts), F32, MX shapes the tiles do not cover, or the mixed formats
+// GatedMlp::new_mixed accepts (mlp.rs:60-81).  Three row products (each format's own kernel)
+// and one SwiGLU pass.
+int gated_mlp_generic(Ctx *ctx, const Mat *g, const Mat *u, const Mat *d, const float *d_x, int T,
+                      float *d_out, int32_t *d_status, cudaStream_t st) {
+    const size_t I = g->rows, n = size_t(T) * I;
+    float *buf = nullptr;
+    URB_CUDA(ctx, cudaMallocAsync(&buf, 2 * n * sizeof(float), st));
+    int rc = product_device(ctx, g, 0, I, d_x, size_t(T), buf, d_status, st);
+    if (rc == URB_OK) rc = product_device(ctx, u, 0, I, d_x, size_t(T), buf + n, d_status, st);
+    if (rc == URB_OK) {
+        k_swiglu_rows<<<unsigned((n + 255) / 256), 256, 0, st>>>(buf, buf + n, n, expf_table_of(ctx), buf);
+        const cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess) rc = cuda_fail(ctx, e, "swiglu");
+    }
+    if (rc == URB_OK) rc = product_device(ctx, d, 0, d->rows, buf, size_t(T), d_out, d_status, st);
+    cudaFreeAsync(buf, st);
+    return rc;
+}
+
 int gated_mlp_device(Ctx *ctx, const Mat *g, const Mat *u, const Mat *d, const float *d_x, int T,
                      float *d_out, int32_t *d_status, cudaStream_t st) {
     const size_t H = g->cols, I = g->rows;
+    if (!(g->tiled && u->tiled && d->tiled && g->format == u->format))
+        return gated_mlp_generic(ctx, g, u, d, d_x, T, d_out, d_status, st);
     const int nseg = int(div_ceil(T, kCap));
     int rc;
     if (bf16_gemv_applies(g, T) && bf16_gemv_applies(u, T) && bf16_gemv_applies(d, T)) {
@@ -900,8 +930,6 @@ int urb_gated_mlp_forward(urb_ctx *ctx, const urb_mat *g, const urb_mat *u, cons
     // GatedMlp::new_mixed (src/model/mlp.rs:60-81).
     if (g->rows != u->rows || g->cols != u->cols || d->cols != g->rows || d->rows != g->cols)
         return set_error(ctx, URB_ERR_SHAPE, "gated MLP projections have inconsistent shapes");
-    if (!g->tiled || !u->tiled || !d->tiled || g->format != u->format)
-        return set_error(ctx, URB_ERR_UNSUPPORTED, "gated MLP needs tiled gate/up of one format");
     if (tokens == 0) return URB_OK;
     for (size_t i = 0; i < tokens * g->cols; ++i)
         if (!std::isfinite(x[i])) return set_error(ctx, URB_ERR_NONFINITE, "gated MLP input is not finite");
@@ -926,8 +954,6 @@ int urb_gated_mlp_forward_device(urb_ctx *ctx, const urb_mat *g, const urb_mat *
     cudaSetDevice(ctx->device);
     if (g->rows != u->rows || g->cols != u->cols || d->cols != g->rows || d->rows != g->cols)
         return set_error(ctx, URB_ERR_SHAPE, "gated MLP projections have inconsistent shapes");
-    if (!g->tiled || !u->tiled || !d->tiled || g->format != u->format)
-        return set_error(ctx, URB_ERR_UNSUPPORTED, "gated MLP needs tiled gate/up of one format");
     if (tokens == 0) return URB_OK;
     return gated_mlp_device(ctx, g, u, d, d_x, int(tokens), d_out, d_status, ctx->stream);
 }
