@@ -262,3 +262,48 @@ def test_int_gated_mlp_matches_oracle(oracle, ctx, kinds, tokens):
     err = np.abs(got.astype(np.float64) - want)
     bound = 1e-5 * np.abs(want).max() + 4 * np.spacing(np.abs(want)).astype(np.float64)
     assert np.all(err <= bound), float((err - bound).max())
+
+
+@pytest.mark.parametrize("kind,tokens", [("int4", 1), ("int4", 6), ("int8", 3)])
+def test_int_expert_glm_layer_matches_oracle(oracle, ctx, kind, tokens):
+    # RuntimeMoeLayer::forward (glm/runtime/moe.rs:138-176) with GLM's converted INT experts
+    # (INT4 with 64-column groups, or INT8 per row), an INT shared expert and a BF16 router:
+    # routes bit-exact; outputs within the INT product bar carried through SwiGLU and the f64
+    # combine, |gpu - oracle| <= 1e-5 * max|oracle| + 4 ulp.
+    from helpers import bf16_pair
+    hidden, inter, E, K = 512, 256, 16, 4
+    g = syn.rng(900 + tokens + (kind == "int8"))
+
+    def mlp():
+        mk = (lambda r, c: int4_pair(oracle, ctx, g, r, c, 64)) if kind == "int4" else \
+            (lambda r, c: int8_pair(oracle, ctx, g, r, c))
+        (dg, og), (du, ou), (dd, od) = mk(inter, hidden), mk(inter, hidden), mk(hidden, inter)
+        return urb.GatedMlp(dg, du, dd), (og, ou, od)
+
+    experts = [mlp() for _ in range(E)]
+    shared = mlp()
+    rdev, rorc = bf16_pair(oracle, ctx, g, E, hidden)
+    bias = (g.standard_normal(E) * 0.01).astype(np.float32)
+    geo = urb.MoeGeometry(top_k=K, routed_scaling_factor=2.5)
+    layer = urb.RuntimeMoeLayer(rdev, bias, [e[0] for e in experts], shared[0], geo)
+    ref = oracle.MoeLayer(rorc, bias, [e[1][0] for e in experts], [e[1][1] for e in experts],
+                          [e[1][2] for e in experts], shared[1], top_k=K, scaling=2.5)
+    x = g.standard_normal((tokens, hidden)).astype(np.float32)
+    out, ids, w, extra = layer.forward_batch(x, tokens, details=True)
+    r_out, r_ids, r_w, r_s, r_logits = ref.forward(x)
+    assert np.array_equal(ids, r_ids)
+    assert np.array_equal(bits(w), bits(r_w))
+    assert np.array_equal(bits(extra["router_logits"]), bits(r_logits))
+    want_counts = np.bincount(r_ids.ravel(), minlength=E)
+    assert np.array_equal(extra["counts"], want_counts)
+    err = np.abs(out.astype(np.float64) - r_out)
+    bound = 1e-5 * np.abs(r_out).max() + 4 * np.spacing(np.abs(r_out)).astype(np.float64)
+    assert np.all(err <= bound), float((err - bound).max())
+    # The graph-capturable device entry point does not take these layers.
+    import torch
+    d_x = torch.from_numpy(x).cuda()
+    d_out = torch.empty_like(d_x)
+    torch.cuda.synchronize()
+    with pytest.raises(urb.UrbError) as e:
+        layer.forward_device(d_x.data_ptr(), tokens, d_out.data_ptr())
+    assert e.value.code == native.ERR_UNSUPPORTED

@@ -72,6 +72,9 @@ int moe_forward_device(Layer *L, const float *d_x, int T, float *d_out, MoeWork 
                        int32_t *d_status, cudaStream_t st, const int32_t *d_ids_in,
                        const float *d_w_in, const Numerics *num) {
     Ctx *ctx = L->ctx;
+    if (L->generic)
+        return set_error(ctx, URB_ERR_UNSUPPORTED,
+                         "layers with INT or mixed-format experts run through urb_moe_forward");
     const size_t E = L->experts, K = L->geo.top_k, H = L->hidden, I = L->inter;
     const size_t TK = size_t(T) * K, cols = TK + T;
     const size_t nseg = max_segments(T, K, E);
@@ -438,6 +441,107 @@ int gated_mlp_generic(Ctx *ctx, const Mat *g, const Mat *u, const Mat *d, const 
     return rc;
 }
 
+// dst[i] = src[idx[i]] (rows of H floats).
+__global__ void k_gather_rows(const float *src, const int32_t *idx, size_t n, int H, float *dst) {
+    const size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x;
+    if (i < n * H) dst[i] = src[size_t(idx[i / H]) * H + i % H];
+}
+
+// dst[idx[i]] = src[i] (rows of H floats).
+__global__ void k_scatter_rows(const float *src, const int32_t *idx, size_t n, int H, float *dst) {
+    const size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x;
+    if (i < n * H) dst[size_t(idx[i / H]) * H + i % H] = src[i];
+}
+
+// glm/runtime/moe.rs:164-175: out = f32(f64(shared) + sum over routes in selection order of
+// f64(weight) * f64(expert output)); the product of two f32 values is exact in f64.
+__global__ void k_combine_glm(const float *shared, const float *y, const float *w, int T, int K,
+                              int H, float *out) {
+    const size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x;
+    if (i >= size_t(T) * H) return;
+    const size_t t = i / H, h = i % H;
+    double acc = shared ? double(shared[i]) : 0.0;
+    for (int k = 0; k < K; ++k)
+        acc = __dadd_rn(acc, __dmul_rn(double(w[t * K + k]), double(y[(t * K + k) * H + h])));
+    out[i] = float(acc);
+}
+
+int gated_mlp_device(Ctx *ctx, const Mat *g, const Mat *u, const Mat *d, const float *d_x, int T,
+                     float *d_out, int32_t *d_status, cudaStream_t st);
+
+// RuntimeMoeLayer::forward (glm/runtime/moe.rs:138-176) for layers whose experts have no
+// shared tiled layout: the exact router and noaux_tc routing on the device, the routes read
+// back, each selected expert's GatedMlp over its tokens (grouped experts ascending, tokens
+// ascending, as qwen3_6/runtime.rs:1083-1132), then the f64 combine.  Host outputs as
+// urb_moe_forward; the grouping outputs are filled on the host.
+int moe_forward_generic(Layer *L, const float *d_x, int T, float *d_out, int32_t *h_ids,
+                        float *h_w, float *h_score, float *h_logits, int32_t *h_counts,
+                        int32_t *h_perm_token, int32_t *h_perm_slot, int32_t *d_status,
+                        cudaStream_t st) {
+    Ctx *ctx = L->ctx;
+    const size_t E = L->experts, K = L->geo.top_k, H = L->hidden, TK = size_t(T) * K;
+    const size_t bytes = size_t(T) * E * 4 * 3 + router_f64_elems(T, int(H)) * 8 + TK * 4 * 5 +
+                         3 * TK * H * 4 + size_t(T) * H * 4 + 16 * 256;
+    uint8_t *buf = nullptr;
+    URB_CUDA(ctx, cudaMallocAsync(&buf, bytes, st));
+    Carve cv{buf};
+    MoeWork w{};
+    w.logits = cv.take<float>(size_t(T) * E);
+    w.gate = cv.take<float>(size_t(T) * E);
+    w.sel = cv.take<float>(size_t(T) * E);
+    w.x64 = cv.take<double>(router_f64_elems(T, int(H)));
+    w.ids = cv.take<int32_t>(TK);
+    w.w = cv.take<float>(TK);
+    w.score = cv.take<float>(TK);
+    int32_t *d_tok = cv.take<int32_t>(TK), *d_slot = cv.take<int32_t>(TK);
+    float *xe = cv.take<float>(TK * H), *ye = cv.take<float>(TK * H), *y = cv.take<float>(TK * H);
+    float *shared = cv.take<float>(size_t(T) * H);
+    auto done = [&](int rc) { cudaFreeAsync(buf, st); return rc; };
+    int rc = route_device(L, d_x, T, w, d_status, st);
+    if (rc) return done(rc);
+    std::vector<int32_t> ids(TK);
+    int32_t status = 0;
+    URB_CUDA(ctx, cudaMemcpyAsync(ids.data(), w.ids, TK * 4, cudaMemcpyDeviceToHost, st));
+    URB_CUDA(ctx, cudaMemcpyAsync(&status, d_status, 4, cudaMemcpyDeviceToHost, st));
+    URB_CUDA(ctx, cudaStreamSynchronize(st));
+    if (status) return done(set_error(ctx, status, "MoE forward rejected its input"));
+    std::vector<int32_t> counts(E, 0), offsets(E + 1, 0), tok(TK), slot(TK), pslot(TK);
+    for (size_t i = 0; i < TK; ++i) counts[ids[i]]++;
+    for (size_t e = 0; e < E; ++e) offsets[e + 1] = offsets[e] + counts[e];
+    std::vector<int32_t> cursor(offsets.begin(), offsets.end() - 1);
+    for (size_t t = 0; t < size_t(T); ++t)
+        for (size_t k = 0; k < K; ++k) {
+            const int32_t p = cursor[ids[t * K + k]]++;
+            tok[p] = int32_t(t);
+            pslot[p] = int32_t(k);
+            slot[p] = int32_t(t * K + k);
+        }
+    URB_CUDA(ctx, cudaMemcpyAsync(d_tok, tok.data(), TK * 4, cudaMemcpyHostToDevice, st));
+    URB_CUDA(ctx, cudaMemcpyAsync(d_slot, slot.data(), TK * 4, cudaMemcpyHostToDevice, st));
+    const unsigned gb = unsigned((TK * H + 255) / 256);
+    k_gather_rows<<<gb, 256, 0, st>>>(d_x, d_tok, TK, int(H), xe);
+    for (size_t e = 0; e < E && rc == URB_OK; ++e)
+        if (counts[e])
+            rc = gated_mlp_device(ctx, L->gate[e], L->up[e], L->down[e], xe + size_t(offsets[e]) * H,
+                                  counts[e], ye + size_t(offsets[e]) * H, d_status, st);
+    if (rc) return done(rc);
+    k_scatter_rows<<<gb, 256, 0, st>>>(ye, d_slot, TK, int(H), y);
+    if (L->sg) rc = gated_mlp_device(ctx, L->sg, L->su, L->sd, d_x, T, shared, d_status, st);
+    if (rc) return done(rc);
+    k_combine_glm<<<unsigned((size_t(T) * H + 255) / 256), 256, 0, st>>>(L->sg ? shared : nullptr, y, w.w,
+                                                                       T, int(K), int(H), d_out);
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return done(cuda_fail(ctx, e, "generic MoE forward"));
+    if (h_ids) std::copy(ids.begin(), ids.end(), h_ids);
+    if (h_w) URB_CUDA(ctx, cudaMemcpyAsync(h_w, w.w, TK * 4, cudaMemcpyDefault, st));
+    if (h_score) URB_CUDA(ctx, cudaMemcpyAsync(h_score, w.score, TK * 4, cudaMemcpyDefault, st));
+    if (h_logits) URB_CUDA(ctx, cudaMemcpyAsync(h_logits, w.logits, size_t(T) * E * 4, cudaMemcpyDefault, st));
+    if (h_counts) std::copy(counts.begin(), counts.end(), h_counts);
+    if (h_perm_token) std::copy(tok.begin(), tok.end(), h_perm_token);
+    if (h_perm_slot) std::copy(pslot.begin(), pslot.end(), h_perm_slot);
+    return done(URB_OK);
+}
+
 int gated_mlp_device(Ctx *ctx, const Mat *g, const Mat *u, const Mat *d, const float *d_x, int T,
                      float *d_out, int32_t *d_status, cudaStream_t st) {
     const size_t H = g->cols, I = g->rows;
@@ -550,9 +654,12 @@ static int create_layer(urb_ctx *ctx, const urb_mat *router, const float *bias, 
         if (g->rows != u->rows || g->cols != u->cols) return URB_ERR_SHAPE;
         if (d->cols != g->rows || d->rows != g->cols) return URB_ERR_SHAPE;
         if (g->cols != H || g->rows != I) return URB_ERR_SHAPE;
-        if (!g->tiled || !u->tiled || !d->tiled) return URB_ERR_UNSUPPORTED;
-        if (g->format != fmt || u->format != fmt || d->format != fmt) return URB_ERR_UNSUPPORTED;
         return URB_OK;
+    };
+    // Experts outside one shared tiled format compose per-expert GatedMlp calls.
+    auto tiled_mlp = [&](const urb_mat *g, const urb_mat *u, const urb_mat *d) {
+        return g->tiled && u->tiled && d->tiled && g->format == fmt && u->format == fmt &&
+               d->format == fmt;
     };
     if (e_begin + e_count > experts || e_begin + e_count < e_begin)
         return set_error(ctx, URB_ERR_SHAPE, "expert shard range exceeds the router's experts");
@@ -564,7 +671,11 @@ static int create_layer(urb_ctx *ctx, const urb_mat *router, const float *bias, 
         int rc = check_mlp(sg, su, sd);
         if (rc) return set_error(ctx, rc, "shared expert shape/format is not supported");
     }
+    bool generic = false;
+    for (size_t e = 0; e < e_count; ++e) generic |= !tiled_mlp(gate[e], up[e], down[e]);
+    if (have_shared) generic |= !tiled_mlp(sg, su, sd);
     urb_layer *L = new urb_layer();
+    L->generic = generic;
     L->ctx = ctx;
     L->router = router;
     L->experts = experts;
@@ -594,12 +705,13 @@ static int create_layer(urb_ctx *ctx, const urb_mat *router, const float *bias, 
     for (size_t e = 0; e < e_count; ++e) put(e, gate[e], up[e], down[e]);
     if (have_shared) put(e_count, sg, su, sd);
     const char *path = std::getenv("URB_MOE_PATH");
-    bool have_tc = fmt == URB_FMT_MXFP4 || fmt == URB_FMT_MXFP8;
+    bool have_tc = !generic && (fmt == URB_FMT_MXFP4 || fmt == URB_FMT_MXFP8);
     for (size_t e = 0; e < e_count && have_tc; ++e)
         have_tc = gate[e]->tc_tiles && up[e]->tc_tiles && down[e]->tc_tiles;
     if (L->sg) have_tc = have_tc && L->sg->tc_tiles && L->su->tc_tiles && L->sd->tc_tiles;
     // Block-scaled tcgen05 passes by default; URB_MOE_PATH=mma selects the mma.sync passes.
     L->use_tc = have_tc && !(path && std::strcmp(path, "mma") == 0);
+    if (generic) L->use_tc = false;
     if (e_count != experts && !have_tc) {
         delete L;
         return set_error(ctx, URB_ERR_UNSUPPORTED, "expert shards need MX experts (tensor-core passes)");
@@ -688,6 +800,19 @@ int urb_moe_forward(urb_ctx *ctx, urb_layer *L, const float *x, size_t tokens, f
     float *d_x = d_io, *d_out = d_io + tokens * H;
     URB_CUDA(ctx, cudaMemsetAsync(ctx->d_status, 0, 4, st));
     URB_CUDA(ctx, cudaMemcpyAsync(d_x, x, tokens * H * 4, cudaMemcpyDefault, st));
+    if (L->generic) {
+        int rc = moe_forward_generic(L, d_x, int(tokens), d_out, route_expert, route_weight,
+                                     route_score, router_logits, counts, perm_token, perm_slot,
+                                     ctx->d_status, st);
+        if (rc == URB_OK) rc = [&] {
+            URB_CUDA(ctx, cudaMemcpyAsync(out, d_out, tokens * H * 4, cudaMemcpyDefault, st));
+            URB_CUDA(ctx, cudaStreamSynchronize(st));
+            return int(URB_OK);
+        }();
+        cudaFreeAsync(d_io, st);
+        cudaStreamSynchronize(st);
+        return rc;
+    }
     MoeWork w{};
     int rc = moe_forward_device(L, d_x, int(tokens), d_out, &w, ctx->d_status, st);
     if (rc) {

@@ -90,6 +90,9 @@ struct Layer {
     // expert or null): gate/up/down mma tiles, their row exponents, gate/up/down bs tiles.
     void **d_tables = nullptr;
     bool use_tc = true;  // block-scaled tcgen05 passes (false: mma.sync register-dequant)
+    // Experts without one shared tiled format (INT8 / INT4 GLM experts, F32, mixed formats):
+    // the forward composes per-expert GatedMlp calls (moe_forward_generic).
+    bool generic = false;
 };
 
 // Device workspace of one forward, carved from the context workspace.
