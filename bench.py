@@ -467,7 +467,61 @@ def bench_configs(urb, native, ctx, local, pk_hbm):
     for lay in layers:
         lay.free()
     out["c4"] = c4
+    out["int_glm"] = bench_int(urb, ctx, g, dev, pk_hbm)
     return out
+
+
+def bench_int(urb, ctx, g, dev, pk_hbm, reps=5):
+    """GLM converted-checkpoint formats (Int4Matrix with 64-column groups, Int8Matrix per row),
+    2048 x 7168, at 1 and 8 tokens: device time of one product as CUDA-graph replays over
+    distinct copies (>= 260 MB, so weights stream from HBM), beside the payload + scale bytes."""
+    import math
+    import numpy as np
+    import torch
+    stream = torch.cuda.ExternalStream(ctx.stream)
+    rows, cols, grp = 2048, 7168, 64
+    res = {}
+    for fmt in ("int4", "int8"):
+        if fmt == "int4":
+            packed = g.integers(0, 256, size=rows * cols // 2, dtype=np.uint8)
+            scales = (np.abs(g.standard_normal(rows * cols // grp)) * 0.02 + 1e-3).astype(np.float32)
+            nbytes = packed.size + scales.size * 4
+            make = lambda: urb.Int4Matrix.from_packed(rows, cols, grp, packed, scales, ctx=ctx)
+        else:
+            data = g.integers(-128, 128, size=(rows, cols)).astype(np.int8)
+            scales = (np.abs(g.standard_normal(rows)) * 0.01 + 1e-4).astype(np.float32)
+            nbytes = data.size + rows * 4
+            make = lambda: urb.Int8Matrix.from_packed(rows, cols, data, scales, ctx=ctx)
+        mats = [make() for _ in range(math.ceil(260e6 / nbytes))]
+        for T in (1, 8):
+            x = torch.randn(T, cols, device=dev)
+            y = torch.empty(T, rows, device=dev)
+            for m in mats[:3]:
+                m.matmul_rows_device(x.data_ptr(), T, y.data_ptr())
+            torch.cuda.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=stream):
+                for m in mats:
+                    m.matmul_rows_device(x.data_ptr(), T, y.data_ptr())
+            with torch.cuda.stream(stream):
+                for _ in range(3):
+                    graph.replay()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                stream.synchronize()
+                e0.record(stream)
+                for _ in range(reps):
+                    graph.replay()
+                e1.record(stream)
+                stream.synchronize()
+            us = e0.elapsed_time(e1) * 1e3 / (reps * len(mats))
+            gbs = nbytes / (us / 1e6) / 1e9
+            res[f"{fmt}_T{T}"] = {"us": us, "bytes": nbytes, "achieved_gbs": gbs,
+                                  "frac_of_measured_hbm": gbs / pk_hbm}
+            del graph
+        for m in mats:
+            m.free()
+    return {"workload": "GLM INT4 (group 64) / INT8 (per-row) matrix 2048 x 7168, 1 and 8 tokens",
+            "copies": "distinct weight copies >= 260 MB, CUDA-graph replay", **res}
 
 
 def workload_config(world):
