@@ -550,6 +550,8 @@ def main():
                     help="routed experts (256 = config 2; smaller only for profiling captures)")
     ap.add_argument("--tokens", type=int, default=128,
                     help="tokens per GPU (128 = config 2; other values only for profiling)")
+    ap.add_argument("--int-only", action="store_true",
+                    help="profiling: time only the INT4 / INT8 products and print their figures")
     args = ap.parse_args()
     global EXPERTS, TOKENS
     EXPERTS = args.experts
@@ -575,6 +577,11 @@ def main():
     ctx = urb.Context(local)
     stream = torch.cuda.Stream(device=local)
     ctx.set_stream(stream.cuda_stream)
+    if args.int_only:
+        from urbilateria_b200 import synthetic as syn
+        print(json.dumps(bench_int(urb, ctx, syn.rng(SEED + 11), f"cuda:{local}",
+                                   peaks()[0])))
+        return
 
     keep_host = (rank == 0 and world == 1 and not args.no_cpu)
     # One GPU: the whole layer.  N GPUs: expert parallel, rank r holding experts
