@@ -67,7 +67,7 @@ int urbo_validate(const urbo_matrix *m);
  * scales [rows, ceil(cols/group)]. */
 int urbo_int4_quantize_grouped(size_t rows, size_t cols, size_t group, const float *values,
                                uint8_t *packed, float *scales);
-/* WeightMatrix::write_row (src/model/weight.rs:345-365): the decoded f32 weights of one row. */
+/* WeightMatrix::write_row (src/model/weight.rs:347-392): the decoded f32 weights of one row. */
 int urbo_write_row(const urbo_matrix *m, size_t row, float *out);
 
 /* WeightMatrix::matvec_rows / MxFp4Matrix::matvec_rows etc.  y has `count` entries. */

@@ -198,7 +198,7 @@ class Matrix:
         return y
 
     def write_row(self, row):
-        """WeightMatrix::write_row (src/model/weight.rs:345-365): one decoded f32 row."""
+        """WeightMatrix::write_row (src/model/weight.rs:347-392): one decoded f32 row."""
         y = np.empty(self.cols, dtype=np.float32)
         _check(lib().urbo_write_row(ctypes.byref(self.c), row, _ptr(y)))
         return y
