@@ -168,9 +168,11 @@ URB_API int urb_gated_mlp_forward_device(urb_ctx *ctx, const urb_mat *gate, cons
  * run: serving loops that reserve all free HBM up front, and per-token decode loops where a
  * cudaMalloc would synchronise the device.  Temporaries live in one static 8 MiB device
  * scratch per device; calls needing more are rejected (URB_ERR_UNSUPPORTED), roughly
- * tokens * intermediate * 4 bytes must fit.  The first call on a device resolves the scratch
- * (set-up; make it before any stream capture).  Calls overlapping in time on one device race
- * on the scratch: serialise them. */
+ * tokens * intermediate * 4 bytes must fit.  Projections must share one tiled format (MXFP4 /
+ * MXFP8 with 32-column groups, or BF16); F32, INT8 / INT4 and mixed-format MLPs are rejected
+ * with URB_ERR_UNSUPPORTED (their per-projection path needs a workspace).  The first call on a
+ * context resolves the scratch's device address (set-up; make it before any stream capture).
+ * Calls overlapping in time on one device race on the scratch: serialise them. */
 URB_API int urb_gated_mlp_forward_device_noalloc(urb_ctx *ctx, const urb_mat *gate,
                                                  const urb_mat *up, const urb_mat *down,
                                                  const float *d_x, size_t tokens, float *d_out,

@@ -725,29 +725,41 @@ float urbo_bounded_swiglu(float gate, float up, float limit) {
     return g / (1.0f + std::exp(-g)) * u;
 }
 
-// DeepExpert::forward_with_mx_input (deepseek_v4/runtime.rs:3081-3104) for MX weights:
-// gate / up on the simulated input with BF16 outputs, bounded SwiGLU, the route weight applied
-// to the activation (none for the shared expert), BF16, simulated again, down, BF16.
-static int deepseek_expert(const urbo_matrix *gate, const urbo_matrix *up, const urbo_matrix *down,
-                           const float *mx_x, const float *route_weight, float limit, float *y,
-                           int threads) {
+// WeightMatrix::uses_mx_activation_quantization (src/model/weight.rs:408-410).
+static bool uses_mx(const urbo_matrix *m) { return m->format == URBO_MXFP8 || m->format == URBO_MXFP4; }
+
+// DeepExpert::forward_with_mx_input (deepseek_v4/runtime.rs:3081-3104), per projection as
+// linear_with_mx_activation / linear (deepseek_v4/math.rs:106-141): an MX gate / up reads the
+// simulated input mx_x and its output rounds to BF16, a plain (F32 / BF16 / INT) one reads x
+// unrounded; bounded SwiGLU, the route weight applied to the activation (none for the shared
+// expert), BF16; an MX down projection simulates the activation as E4M3 per 128 and rounds its
+// output to BF16, a plain one multiplies the activation as it is.
+int urbo_deepseek_expert_forward(const urbo_matrix *gate, const urbo_matrix *up,
+                                 const urbo_matrix *down, const float *x, const float *mx_x,
+                                 const float *route_weight, float limit, float *y, int threads) {
     const size_t I = gate->rows;
     std::vector<float> g(I), u(I);
-    int rc = urbo_matvec_rows(gate, 0, I, mx_x, g.data(), threads);
+    int rc = urbo_matvec_rows(gate, 0, I, uses_mx(gate) ? mx_x : x, g.data(), threads);
     if (rc) return rc;
-    rc = urbo_matvec_rows(up, 0, I, mx_x, u.data(), threads);
+    rc = urbo_matvec_rows(up, 0, I, uses_mx(up) ? mx_x : x, u.data(), threads);
     if (rc) return rc;
+    if (route_weight && (!finite(*route_weight) || *route_weight < 0.0f)) return URBO_ERR_INVALID;
     for (size_t i = 0; i < I; ++i) {
-        float a = urbo_bounded_swiglu(urbo_round_bf16(g[i]), urbo_round_bf16(u[i]), limit);
+        const float gv = uses_mx(gate) ? urbo_round_bf16(g[i]) : g[i];
+        const float uv = uses_mx(up) ? urbo_round_bf16(u[i]) : u[i];
+        float a = urbo_bounded_swiglu(gv, uv, limit);
         if (route_weight) a *= *route_weight;
         g[i] = urbo_round_bf16(a);
         if (!finite(g[i])) return URBO_ERR_NONFINITE;
     }
-    rc = urbo_simulate_e4m3_activation(g.data(), I, 128);
-    if (rc) return rc;
+    if (uses_mx(down)) {
+        rc = urbo_simulate_e4m3_activation(g.data(), I, 128);
+        if (rc) return rc;
+    }
     rc = urbo_matvec_rows(down, 0, down->rows, g.data(), y, threads);
     if (rc) return rc;
-    for (size_t h = 0; h < down->rows; ++h) y[h] = urbo_round_bf16(y[h]);
+    if (uses_mx(down))
+        for (size_t h = 0; h < down->rows; ++h) y[h] = urbo_round_bf16(y[h]);
     return URBO_OK;
 }
 
@@ -773,13 +785,13 @@ int urbo_moe_deepseek_forward(const urbo_moe_layer *L, const float *x, size_t to
         for (size_t r = 0; r < k; ++r) {
             const size_t e = size_t(order[r].first);
             if (e >= L->experts) return URBO_ERR_SHAPE;
-            rc = deepseek_expert(&L->gate[e], &L->up[e], &L->down[e], mx.data(), &order[r].second,
-                                 limit, y.data(), threads);
+            rc = urbo_deepseek_expert_forward(&L->gate[e], &L->up[e], &L->down[e], x + t * H,
+                                              mx.data(), &order[r].second, limit, y.data(), threads);
             if (rc) return rc;
             for (size_t h = 0; h < H; ++h) acc[h] += y[h];
         }
-        rc = deepseek_expert(L->shared_gate, L->shared_up, L->shared_down, mx.data(), nullptr,
-                             limit, shared.data(), threads);
+        rc = urbo_deepseek_expert_forward(L->shared_gate, L->shared_up, L->shared_down, x + t * H,
+                                          mx.data(), nullptr, limit, shared.data(), threads);
         if (rc) return rc;
         for (size_t h = 0; h < H; ++h) out[t * H + h] = urbo_round_bf16(acc[h] + shared[h]);
     }

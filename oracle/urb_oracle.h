@@ -129,6 +129,11 @@ float urbo_power_of_two_ceiling(float value);
 int urbo_simulate_e4m3_activation(float *values, size_t n, size_t block);
 float urbo_round_bf16(float value);
 float urbo_bounded_swiglu(float gate, float up, float limit);
+/* One expert of that composition (DeepExpert::forward_with_mx_input): MX projections read mx_x
+ * and round to BF16, plain ones read x; route_weight NULL for the shared expert. */
+int urbo_deepseek_expert_forward(const urbo_matrix *gate, const urbo_matrix *up,
+                                 const urbo_matrix *down, const float *x, const float *mx_x,
+                                 const float *route_weight, float limit, float *y, int threads);
 int urbo_moe_deepseek_forward(const urbo_moe_layer *layer, const float *x, size_t tokens,
                               const int32_t *route_expert, const float *route_weight,
                               float limit, float *out, int threads);

@@ -131,6 +131,10 @@ def lib():
         _lib.urbo_moe_qwen_layer_forward.argtypes = [
             ctypes.POINTER(OracleMoeLayer), ctypes.POINTER(OracleMatrix), ctypes.c_void_p,
             ctypes.c_size_t, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int]
+        _lib.urbo_deepseek_expert_forward.argtypes = [
+            ctypes.POINTER(OracleMatrix), ctypes.POINTER(OracleMatrix), ctypes.POINTER(OracleMatrix),
+            ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_float, ctypes.c_void_p,
+            ctypes.c_int]
         _lib.urbo_moe_deepseek_forward.argtypes = [
             ctypes.POINTER(OracleMoeLayer), ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p,
             ctypes.c_void_p, ctypes.c_float, ctypes.c_void_p, ctypes.c_int]
@@ -345,6 +349,21 @@ def moe_deepseek_forward(layer: "MoeLayer", x, expert_ids, weights, limit: float
     _check(lib().urbo_moe_deepseek_forward(ctypes.byref(layer.c), _ptr(x), t, _ptr(ids), _ptr(w),
                                            limit, _ptr(out), threads or default_threads()))
     return out
+
+
+def deepseek_expert_forward(gate: Matrix, up: Matrix, down: Matrix, x, limit: float,
+                            route_weight=None, threads=None):
+    """DeepExpert::forward_with_mx_input (deepseek_v4/runtime.rs:3081-3104) of one token: MX
+    projections see x simulated as E4M3 per 128 values, plain ones see x itself."""
+    x = np.ascontiguousarray(x, dtype=np.float32).ravel()
+    mx = simulate_e4m3_activation(x, 128)
+    y = np.empty(down.rows, np.float32)
+    w = None if route_weight is None else np.array([route_weight], np.float32)
+    _check(lib().urbo_deepseek_expert_forward(ctypes.byref(gate.c), ctypes.byref(up.c),
+                                              ctypes.byref(down.c), _ptr(x), _ptr(mx),
+                                              None if w is None else _ptr(w),
+                                              limit, _ptr(y), threads or default_threads()))
+    return y
 
 
 def route_sqrt_softplus(logits, bias, hash_experts, top_k, scaling):

@@ -6,6 +6,7 @@ formula (ordered F64 / ordered F32 sums), the formula is re-implemented here ind
 numpy and compared bit for bit.
 """
 import math
+import os
 import struct
 
 import numpy as np
@@ -559,3 +560,53 @@ def test_int_constructor_validation(oracle):
     with pytest.raises(oracle.OracleError) as e:
         oracle.int4_quantize_grouped(1, 2, 2, [1.0, np.nan])
     assert e.value.code == oracle.ERR_NONFINITE
+
+
+def _fixture_close(name, got, want):
+    """The reference fixture test's tolerance (deepseek_v4/runtime.rs:4221-4230):
+    |got - want| <= max(2e-5, 2e-5 * |want|) elementwise."""
+    got = np.asarray(got, np.float32).ravel()
+    want = np.asarray(want, np.float32).ravel()
+    assert got.shape == want.shape, name
+    tol = np.maximum(np.float32(2e-5), np.abs(want) * np.float32(2e-5))
+    assert np.all(np.abs(got - want) <= tol), (name, got, want)
+
+
+def test_deepseek_v4_tiny_fixture_moe_layer(oracle):
+    """The reference's layer-level fixture (tests/fixtures/deepseek_v4_tiny_oracle.json, replayed
+    at src/models/deepseek_v4/runtime.rs:4603-4646): hash-routed MoE with F32 experts.  Router
+    logits, routes, each routed expert's output (route weight before the down projection), the
+    shared expert and the BF16 MoE branch."""
+    import json
+    d = json.load(open(os.path.join(os.path.dirname(__file__), "golden", "deepseek_v4_tiny_moe.json")))
+    H, E, K = d["hidden"], d["experts"], d["top_k"]
+    limit, scale = np.float32(d["swiglu_limit"]), np.float32(d["routed_scaling_factor"])
+
+    def mat(t):
+        r, c = t["shape"]
+        return oracle.Matrix(oracle.F32, r, c, np.array(t["values"], np.float32))
+
+    router = mat(d["router"])
+    routed = [(mat(e["w1"]), mat(e["w3"]), mat(e["w2"])) for e in d["routed"]]
+    shared = (mat(d["shared"]["w1"]), mat(d["shared"]["w3"]), mat(d["shared"]["w2"]))
+    x = np.array(d["ffn_input"], np.float32)
+    want = d["expected"]
+    logits = router.matvec(x)
+    _fixture_close("router logits", logits, want["router_logits"])
+    ids, w, sel = oracle.route_sqrt_softplus(logits, None, d["hash_experts"], K, scale)
+    assert ids.tolist() == [r["expert"] for r in want["routes"]]
+    _fixture_close("route weight", w, [r["weight"] for r in want["routes"]])
+    _fixture_close("route selection score", sel, [r["selection_score"] for r in want["routes"]])
+    for k in range(K):
+        g, u, dn = routed[ids[k]]
+        y = oracle.deepseek_expert_forward(g, u, dn, x, limit, route_weight=w[k])
+        _fixture_close("routed expert %d" % k, y, want["routed_experts"][k])
+    _fixture_close("shared expert", oracle.deepseek_expert_forward(*shared, x, limit),
+                   want["shared_expert"])
+    layer = oracle.MoeLayer(router, np.zeros(E, np.float32), [m[0] for m in routed],
+                            [m[1] for m in routed], [m[2] for m in routed], shared, top_k=K,
+                            scaling=float(scale))
+    out, e, lw = oracle.moe_deepseek_layer_forward(layer, x, float(limit),
+                                                   hash_experts=np.array([d["hash_experts"]]))
+    assert e.ravel().tolist() == ids.tolist()
+    _fixture_close("moe branch", out, want["moe_branch"])

@@ -172,14 +172,10 @@ int launch_t(Ctx *ctx, const uint16_t *w, const uint16_t *w2, int row0, int nrow
     const size_t smem = size_t(TT) * ((cols + 7) & ~7) * sizeof(float);
     if (smem > 200 * 1024) return URB_ERR_UNSUPPORTED;
     auto k = k_gemv_bf16<TT, R, NCH, SWIGLU>;
-    // Largest dynamic shared memory granted so far, per device (callers hold their context's
-    // lock; the attribute is raised, never lowered).
-    static size_t smem_set[64] = {};
-    size_t &granted = smem_set[ctx->device & 63];
-    if (smem > 48 * 1024 && smem > granted) {
+    // The attribute is per function and device; set it on every launch that needs more than
+    // the default (contexts on one device may run concurrently, so no cached "granted" value).
+    if (smem > 48 * 1024)
         URB_CUDA(ctx, cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
-        granted = smem;
-    }
     const dim3 grid(unsigned((nrows + kGvWarps * R - 1) / (kGvWarps * R)), unsigned((tokens + TT - 1) / TT));
     k<<<grid, 32 * kGvWarps, smem, st>>>(w, w2, row0, nrows, cols, x, tokens, y, y_stride, status);
     URB_CUDA(ctx, cudaGetLastError());

@@ -123,7 +123,8 @@ int launch_row_shift(const float *d_src, int rows, int cols, int stride, int32_t
                      int32_t *d_status, cudaStream_t st, int32_t *d_lofree, int bf16_check) {
     if (rows <= 0) return URB_OK;
     k_row_shift<<<rows, 256, 0, st>>>(d_src, cols, stride, d_shift, d_status, d_lofree, bf16_check);
-    return cudaGetLastError() == cudaSuccess ? URB_OK : URB_ERR_CUDA;
+    // The launch error is left for the caller to read (cudaPeekAtLastError does not clear it).
+    return cudaPeekAtLastError() == cudaSuccess ? URB_OK : URB_ERR_CUDA;
 }
 
 }  // namespace urb

@@ -484,6 +484,12 @@ int moe_forward_generic(Layer *L, const float *d_x, int T, float *d_out, int32_t
                          3 * TK * H * 4 + size_t(T) * H * 4 + 16 * 256;
     uint8_t *buf = nullptr;
     URB_CUDA(ctx, cudaMallocAsync(&buf, bytes, st));
+    // Every exit after the allocation releases it (stream-ordered).
+#define URB_CUDA_DONE(expr)                                                    \
+    do {                                                                       \
+        cudaError_t _e = (expr);                                               \
+        if (_e != cudaSuccess) return done(cuda_fail(ctx, _e, #expr));         \
+    } while (0)
     Carve cv{buf};
     MoeWork w{};
     w.logits = cv.take<float>(size_t(T) * E);
@@ -501,9 +507,9 @@ int moe_forward_generic(Layer *L, const float *d_x, int T, float *d_out, int32_t
     if (rc) return done(rc);
     std::vector<int32_t> ids(TK);
     int32_t status = 0;
-    URB_CUDA(ctx, cudaMemcpyAsync(ids.data(), w.ids, TK * 4, cudaMemcpyDeviceToHost, st));
-    URB_CUDA(ctx, cudaMemcpyAsync(&status, d_status, 4, cudaMemcpyDeviceToHost, st));
-    URB_CUDA(ctx, cudaStreamSynchronize(st));
+    URB_CUDA_DONE(cudaMemcpyAsync(ids.data(), w.ids, TK * 4, cudaMemcpyDeviceToHost, st));
+    URB_CUDA_DONE(cudaMemcpyAsync(&status, d_status, 4, cudaMemcpyDeviceToHost, st));
+    URB_CUDA_DONE(cudaStreamSynchronize(st));
     if (status) return done(set_error(ctx, status, "MoE forward rejected its input"));
     std::vector<int32_t> counts(E, 0), offsets(E + 1, 0), tok(TK), slot(TK), pslot(TK);
     for (size_t i = 0; i < TK; ++i) counts[ids[i]]++;
@@ -516,8 +522,8 @@ int moe_forward_generic(Layer *L, const float *d_x, int T, float *d_out, int32_t
             pslot[p] = int32_t(k);
             slot[p] = int32_t(t * K + k);
         }
-    URB_CUDA(ctx, cudaMemcpyAsync(d_tok, tok.data(), TK * 4, cudaMemcpyHostToDevice, st));
-    URB_CUDA(ctx, cudaMemcpyAsync(d_slot, slot.data(), TK * 4, cudaMemcpyHostToDevice, st));
+    URB_CUDA_DONE(cudaMemcpyAsync(d_tok, tok.data(), TK * 4, cudaMemcpyHostToDevice, st));
+    URB_CUDA_DONE(cudaMemcpyAsync(d_slot, slot.data(), TK * 4, cudaMemcpyHostToDevice, st));
     const unsigned gb = unsigned((TK * H + 255) / 256);
     k_gather_rows<<<gb, 256, 0, st>>>(d_x, d_tok, TK, int(H), xe);
     for (size_t e = 0; e < E && rc == URB_OK; ++e)
@@ -533,13 +539,14 @@ int moe_forward_generic(Layer *L, const float *d_x, int T, float *d_out, int32_t
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return done(cuda_fail(ctx, e, "generic MoE forward"));
     if (h_ids) std::copy(ids.begin(), ids.end(), h_ids);
-    if (h_w) URB_CUDA(ctx, cudaMemcpyAsync(h_w, w.w, TK * 4, cudaMemcpyDefault, st));
-    if (h_score) URB_CUDA(ctx, cudaMemcpyAsync(h_score, w.score, TK * 4, cudaMemcpyDefault, st));
-    if (h_logits) URB_CUDA(ctx, cudaMemcpyAsync(h_logits, w.logits, size_t(T) * E * 4, cudaMemcpyDefault, st));
+    if (h_w) URB_CUDA_DONE(cudaMemcpyAsync(h_w, w.w, TK * 4, cudaMemcpyDefault, st));
+    if (h_score) URB_CUDA_DONE(cudaMemcpyAsync(h_score, w.score, TK * 4, cudaMemcpyDefault, st));
+    if (h_logits) URB_CUDA_DONE(cudaMemcpyAsync(h_logits, w.logits, size_t(T) * E * 4, cudaMemcpyDefault, st));
     if (h_counts) std::copy(counts.begin(), counts.end(), h_counts);
     if (h_perm_token) std::copy(tok.begin(), tok.end(), h_perm_token);
     if (h_perm_slot) std::copy(pslot.begin(), pslot.end(), h_perm_slot);
     return done(URB_OK);
+#undef URB_CUDA_DONE
 }
 
 int gated_mlp_device(Ctx *ctx, const Mat *g, const Mat *u, const Mat *d, const float *d_x, int T,

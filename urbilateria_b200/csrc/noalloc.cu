@@ -14,10 +14,13 @@
 //
 // The scratch is shared by every call on a device: calls that overlap in time (two streams,
 // two contexts or two host threads on one device) race on it and must be serialised by the
-// caller.  The first call on a device resolves the scratch's address with
-// cudaGetSymbolAddress (set-up work that should run before any stream capture).
-#include <mutex>
-
+// caller.  The first call on a context resolves the scratch's device address with
+// cudaGetSymbolAddress (set-up work that should run before any stream capture) and keeps it in
+// the context, so a context created after a device reset resolves it afresh.
+//
+// Only projections with one shared tiled format (MXFP4 / MXFP8 with 32-column groups, BF16)
+// are accepted; the other formats compose per-projection products whose temporaries live in
+// the context workspace, so they are rejected with URB_ERR_UNSUPPORTED.
 #include "urb_internal.cuh"
 
 namespace urb {
@@ -25,25 +28,17 @@ namespace {
 
 constexpr size_t kNoallocScratchBytes = size_t(8) << 20;  // 8 MiB per device
 constexpr int kMlpCap = 4;  // tokens per segment: hi/lo halves fill one 8-column n-block
-constexpr int kMaxDevices = 64;
-
 __device__ __align__(256) uint8_t g_noalloc_scratch[kNoallocScratchBytes];
 
-std::mutex g_addr_mu;
-uint8_t *g_addr[kMaxDevices] = {};
-
-// Address of the scratch on `device` (resolved once per device).
+// Device address of the scratch for this context's device (the device is current).
 int scratch_of(Ctx *ctx, uint8_t **out) {
-    if (ctx->device < 0 || ctx->device >= kMaxDevices)
-        return set_error(ctx, URB_ERR_UNSUPPORTED, "device ordinal beyond the no-alloc scratch table");
-    std::lock_guard<std::mutex> lk(g_addr_mu);
-    if (!g_addr[ctx->device]) {
+    if (!ctx->noalloc_scratch) {
         void *p = nullptr;
         cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
         if (e != cudaSuccess) return cuda_fail(ctx, e, "cudaGetSymbolAddress(no-alloc scratch)");
-        g_addr[ctx->device] = static_cast<uint8_t *>(p);
+        ctx->noalloc_scratch = static_cast<uint8_t *>(p);
     }
-    *out = g_addr[ctx->device];
+    *out = ctx->noalloc_scratch;
     return URB_OK;
 }
 
@@ -93,10 +88,9 @@ int urb_gated_mlp_forward_device_noalloc(urb_ctx *ctx, const urb_mat *g, const u
     // GatedMlp::new_mixed (src/model/mlp.rs:60-81), as urb_gated_mlp_forward_device.
     if (g->rows != u->rows || g->cols != u->cols || d->cols != g->rows || d->rows != g->cols)
         return set_error(ctx, URB_ERR_SHAPE, "gated MLP projections have inconsistent shapes");
-    if (!g->tiled || !u->tiled || !d->tiled || g->format != u->format)
-        return set_error(ctx, URB_ERR_UNSUPPORTED, "gated MLP needs tiled gate/up of one format");
     if (tokens == 0) return URB_OK;
     const size_t H = g->cols, I = g->rows, T = tokens;
+    // BF16 projections of a few tokens stream the row-major copies and need no tiles.
     if (bf16_gemv_applies(g, T) && bf16_gemv_applies(u, T) && bf16_gemv_applies(d, T) &&
         T * I * 4 <= kNoallocScratchBytes) {
         // The same streaming BF16 passes as urb_gated_mlp_forward_device (h in the scratch).
@@ -107,6 +101,10 @@ int urb_gated_mlp_forward_device_noalloc(urb_ctx *ctx, const urb_mat *g, const u
                                 d_status, ctx->stream);
         if (rc != URB_ERR_UNSUPPORTED) return rc;
     }
+    if (!g->tiled || !u->tiled || !d->tiled || g->format != u->format)
+        return set_error(ctx, URB_ERR_UNSUPPORTED,
+                         "no-alloc gated MLP needs gate/up/down in one tiled format (MXFP4 / "
+                         "MXFP8 with 32-column groups, or BF16)");
     const size_t nseg = (T + kMlpCap - 1) / kMlpCap;
     // Carve: row shifts [T], segments [2 nseg], scalars [4], max-exponent words [T], h [T, I].
     size_t off = 0;

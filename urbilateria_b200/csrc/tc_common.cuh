@@ -1,7 +1,7 @@
 // tc_common.cuh — thin PTX wrappers for the sm_100a asynchronous machinery used by the
 // tensor-core grouped pass: mbarriers, 1-D bulk copies (TMA engine, no tensor map), tcgen05
-// TMEM allocation / load / store, tcgen05.mma (A operand from TMEM, B from a shared-memory
-// descriptor) and tcgen05.commit.  Every wait is bounded: it gives up after a fixed number of
+// TMEM allocation / load / store, block-scaled tcgen05.mma (both operands from shared-memory
+// descriptors, scales in TMEM) and tcgen05.commit.  Every wait is bounded: it gives up after a fixed number of
 // polls and reports failure, so a protocol error surfaces as URB_ERR_TIMEOUT, not a hang.
 #pragma once
 #include <stdint.h>
@@ -113,29 +113,10 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t *v) {
         : "memory");
 }
 
-// D[tmem] (+)= A[tmem] x B[smem desc], kind::f16 (f16 or bf16 operands, f32 accumulate).
-__device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
-                                       uint32_t idesc, bool accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}"
-        ::"r"(d_tmem), "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(uint32_t(accumulate))
-        : "memory");
-}
-
 // Arrives on `bar` once all previously issued tcgen05.mma of this thread have completed.
 __device__ __forceinline__ void mma_commit(uint64_t *bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
                  ::"r"(smem_u32(bar)) : "memory");
-}
-
-// Instruction descriptor, kind::f16: f32 accumulator, A/B K-major, M = 128.
-__host__ __device__ constexpr uint32_t idesc_f16(int n, bool bf16) {
-    return (1u << 4)                                   // D format f32
-           | (uint32_t(bf16) << 7) | (uint32_t(bf16) << 10)  // A, B: f16 (0) / bf16 (1)
-           | (uint32_t(n >> 3) << 17)                  // N / 8
-           | (uint32_t(128 >> 4) << 24);               // M / 16
 }
 
 // Shared-memory descriptor of a K-major operand tile stored in the 128-byte-swizzled canonical
@@ -151,24 +132,6 @@ __device__ __forceinline__ uint64_t sdesc_sw128(uint32_t smem_addr) {
 }
 
 // ---- block-scaled MMA (MX formats) ----------------------------------------------------------
-
-// Descriptor of a 512-byte scale-factor chunk for tcgen05.cp.32x128b: 32 rows of 16 B,
-// no swizzle, 8-row core matrices 128 B apart.
-__device__ __forceinline__ uint64_t sdesc_sf(uint32_t smem_addr) {
-    uint64_t d = 0;
-    d |= uint64_t((smem_addr & 0x3FFFF) >> 4);
-    d |= uint64_t(128 >> 4) << 16;
-    d |= uint64_t(128 >> 4) << 32;
-    d |= uint64_t(1) << 46;
-    return d;
-}
-
-// Copies a 512-byte scale chunk (row l: 16 bytes) into TMEM columns [col, col+4) of lane l,
-// replicated into all four 32-lane quarters.  Ordered with the issuing thread's tcgen05.mma.
-__device__ __forceinline__ void cp_sf(uint32_t taddr, uint64_t desc) {
-    asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(desc)
-                 : "memory");
-}
 
 // Instruction descriptor of a block-scaled MMA: f32 accumulator, E8M0 scales, K-major
 // operands, M = 128.  fmt: E2M1 = 1 for kind::mxf4; E4M3 = 0 for kind::mxf8f6f4.

@@ -123,6 +123,9 @@ struct Ctx {
     void *pinned = nullptr;
     size_t pinned_size = 0;
     int32_t *d_status = nullptr;  // device status word for host-pointer calls
+    // Device address of the no-alloc entry point's static scratch on this context's device
+    // (resolved by its first call on the context; noalloc.cu).
+    uint8_t *noalloc_scratch = nullptr;
     // glibc-expf exception table (see expf_glibc.cuh).
     const uint32_t *expf_keys = nullptr;
     const uint32_t *expf_vals = nullptr;
