@@ -167,6 +167,31 @@ def cpu_tokens_per_s(layer, x, budget_s: float, threads: int):
             return done / el, done, el
 
 
+def cpu_model() -> str:
+    """The host CPU's model name (first /proc/cpuinfo entry), or the platform's processor."""
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    import platform
+    return platform.processor() or "unknown"
+
+
+def cpu_baseline_figures(layer, x, budget_s: float, budget_1t_s: float):
+    """The oracle layer timed on all host cores and on one core (bounded token samples)."""
+    threads = os.cpu_count() or 1
+    layer.forward(x[:1], threads=threads)
+    tps, n, el = cpu_tokens_per_s(layer, x, budget_s, threads)
+    tps1, n1, el1 = cpu_tokens_per_s(layer, x, budget_1t_s, 1)
+    return {"value": tps, "unit": "tokens/s", "cores": threads, "kind": "port",
+            "cpu_model": cpu_model(), "value_1_thread": tps1,
+            "sample": "%d tokens of the same 128-token chunk, token by token through the GLM "
+                      "composition oracle on %d threads (%.1f s); 1 thread: %d tokens (%.1f s)"
+                      % (n, threads, el, n1, el1)}, n
+
+
 def run_reference(args, rank, world):
     """--impl reference: the reference's CPU path (restated in oracle/) on the host cores."""
     if rank != 0:
@@ -193,6 +218,7 @@ def run_reference(args, rank, world):
             "vs_baseline": None, "dtype": "f64", "data": "synthetic",
             "config": workload_config(world),
             "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": threads, "kind": "port",
+                             "cpu_model": cpu_model(),
                              "sample": "token-by-token GLM composition until %.1fs per step "
                                        "(oracle/urb_oracle.cpp, ordered-F64 Rayon-style row "
                                        "parallelism)" % step_s},
@@ -755,12 +781,8 @@ def main():
     if rank == 0 and world == 1 and not args.no_cpu:
         oracle, olayer, _ = oracle_layer(mats, router, bias)
         threads = os.cpu_count() or 1
-        olayer.forward(x[:1], threads=threads)
-        tps, n, el = cpu_tokens_per_s(olayer, x, args.cpu_sample_s, threads)
-        line["cpu_baseline"] = {"value": tps, "unit": "tokens/s", "cores": threads,
-                                "kind": "port",
-                                "sample": "%d tokens of the same 128-token chunk, token by token "
-                                          "through the GLM composition oracle (%.1f s)" % (n, el)}
+        line["cpu_baseline"], n = cpu_baseline_figures(olayer, x, args.cpu_sample_s,
+                                                       args.cpu_sample_s / 2)
         # Parity of the benchmarked forward on the sampled tokens (routes must match).
         o_out, o_ids, _, _, _ = olayer.forward(x[:n], threads=threads)
         line["parity_sample"] = {

@@ -49,3 +49,19 @@ def bf16_pair(oracle, ctx, g, rows, cols, std=0.02):
     dev = urb.Bf16Matrix.from_bits(rows, cols, bits, ctx=ctx)
     orc = oracle.Matrix(oracle.BF16, rows, cols, bits)
     return dev, orc
+
+
+def memory_state(device: int):
+    """(bytes in use from the device's default stream-ordered pool, bytes that pool reserves,
+    free device memory): what a cudaMallocAsync or a cudaMalloc inside the library would move."""
+    from cuda.bindings import runtime as rt
+    err, pool = rt.cudaDeviceGetDefaultMemPool(device)
+    assert err == rt.cudaError_t.cudaSuccess
+    err, used = rt.cudaMemPoolGetAttribute(pool, rt.cudaMemPoolAttr.cudaMemPoolAttrUsedMemCurrent)
+    assert err == rt.cudaError_t.cudaSuccess
+    err, reserved = rt.cudaMemPoolGetAttribute(
+        pool, rt.cudaMemPoolAttr.cudaMemPoolAttrReservedMemCurrent)
+    assert err == rt.cudaError_t.cudaSuccess
+    err, free, _ = rt.cudaMemGetInfo()
+    assert err == rt.cudaError_t.cudaSuccess
+    return int(used), int(reserved), int(free)

@@ -193,3 +193,24 @@ def test_bf16_gated_mlp_streaming(oracle, ctx, tokens):
     got = urb.GatedMlp(gd, ud, dd).forward_batch(x, tokens)
     want = np.stack([oracle.gated_mlp_forward(go, uo, do, x[t]) for t in range(tokens)])
     assert_close(got, want)
+
+
+def test_host_matvec_rows_allocates_nothing_in_steady_state(ctx):
+    """urb_matvec_rows / urb_matmul_rows stage x and y through the context's grow-only device
+    and pinned buffers: once they have grown, further calls leave the device's memory alone."""
+    from helpers import memory_state
+    import torch
+    g = syn.rng(9200)
+    p, s = syn.mxfp4_matrix(g, 4096, 7168)
+    m = urb.MxFp4Matrix.from_packed(4096, 7168, 32, p, s, ctx=ctx)
+    x = syn.normal_f32(g, (3, 7168))
+    for _ in range(2):
+        m.matvec_rows(10, 300, x[0])
+        m.matmul_rows(x, 3)
+    torch.cuda.synchronize()
+    before = memory_state(ctx.device)
+    ys = [m.matvec_rows(10, 300, x[0]) for _ in range(3)] + [m.matmul_rows(x, 3) for _ in range(3)]
+    after = memory_state(ctx.device)
+    assert before == after, (before, after)
+    assert all(np.array_equal(ys[0], y) for y in ys[:3])
+    m.free()

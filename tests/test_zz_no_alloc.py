@@ -20,27 +20,11 @@ import urbilateria_b200 as urb
 from urbilateria_b200 import native
 from urbilateria_b200 import synthetic as syn
 
-from helpers import assert_close, bf16_pair, mxfp4_pair, mxfp8_pair, rel_err
+from helpers import assert_close, bf16_pair, memory_state, mxfp4_pair, mxfp8_pair, rel_err
 
 pytestmark = pytest.mark.gpu
 
 CHILD_ENV = "URB_NOALLOC_CHILD"
-
-
-def memory_state(device: int):
-    """(bytes in use from the device's default stream-ordered pool, bytes that pool reserves,
-    free device memory): what a cudaMallocAsync or a cudaMalloc inside the library would move."""
-    from cuda.bindings import runtime as rt
-    err, pool = rt.cudaDeviceGetDefaultMemPool(device)
-    assert err == rt.cudaError_t.cudaSuccess
-    err, used = rt.cudaMemPoolGetAttribute(pool, rt.cudaMemPoolAttr.cudaMemPoolAttrUsedMemCurrent)
-    assert err == rt.cudaError_t.cudaSuccess
-    err, reserved = rt.cudaMemPoolGetAttribute(
-        pool, rt.cudaMemPoolAttr.cudaMemPoolAttrReservedMemCurrent)
-    assert err == rt.cudaError_t.cudaSuccess
-    err, free, _ = rt.cudaMemGetInfo()
-    assert err == rt.cudaError_t.cudaSuccess
-    return int(used), int(reserved), int(free)
 
 
 def run(ctx, fn, mats, d_x, tokens, d_out, d_status):

@@ -37,6 +37,42 @@ void *workspace(Ctx *ctx, size_t bytes, int *status) {
     return ctx->ws;
 }
 
+void *io_buffer(Ctx *ctx, size_t bytes, int *status) {
+    *status = URB_OK;
+    if (bytes <= ctx->io_size) return ctx->io;
+    size_t want = std::max(bytes, ctx->io_size * 2);
+    if (ctx->io) cudaFreeAsync(ctx->io, ctx->stream);
+    ctx->io = nullptr;
+    ctx->io_size = 0;
+    cudaError_t e = cudaMallocAsync(&ctx->io, want, ctx->stream);
+    if (e != cudaSuccess) {
+        *status = cuda_fail(ctx, e, "input/output staging allocation");
+        return nullptr;
+    }
+    ctx->io_size = want;
+    return ctx->io;
+}
+
+void *pinned_staging(Ctx *ctx, size_t bytes, int *status) {
+    *status = URB_OK;
+    if (bytes <= ctx->pinned_size) return ctx->pinned;
+    size_t want = std::max(bytes, ctx->pinned_size * 2);
+    if (ctx->pinned) {
+        // A copy on the stream may still read or write the old buffer.
+        cudaStreamSynchronize(ctx->stream);
+        cudaFreeHost(ctx->pinned);
+    }
+    ctx->pinned = nullptr;
+    ctx->pinned_size = 0;
+    cudaError_t e = cudaHostAlloc(&ctx->pinned, want, cudaHostAllocDefault);
+    if (e != cudaSuccess) {
+        *status = cuda_fail(ctx, e, "pinned staging allocation");
+        return nullptr;
+    }
+    ctx->pinned_size = want;
+    return ctx->pinned;
+}
+
 static cudaEvent_t prof_event(Ctx *ctx) {
     if (!ctx->prof_free.empty()) {
         cudaEvent_t e = ctx->prof_free.back();
@@ -208,21 +244,28 @@ int device_product(Ctx *ctx, const Mat *m, size_t start, size_t count, const flo
     return URB_OK;
 }
 
-// Host-pointer product: copies x in, computes, copies y out.
+// Host-pointer product: x staged through the context's pinned buffer into its device I/O
+// buffer, computed, y back the same way (no allocation once the buffers have grown).
 int host_product(Ctx *ctx, const Mat *m, size_t start, size_t count, const float *x,
                  size_t batch, float *y) {
     cudaStream_t st = ctx->stream;
-    float *d_x = nullptr, *d_y = nullptr;
-    URB_CUDA(ctx, cudaMallocAsync(&d_x, batch * m->cols * 4, st));
-    URB_CUDA(ctx, cudaMallocAsync(&d_y, batch * count * 4, st));
-    URB_CUDA(ctx, cudaMemcpyAsync(d_x, x, batch * m->cols * 4, cudaMemcpyDefault, st));
-    int rc = device_product(ctx, m, start, count, d_x, batch, d_y, nullptr, st);
-    if (rc == URB_OK)
-        URB_CUDA(ctx, cudaMemcpyAsync(y, d_y, batch * count * 4, cudaMemcpyDefault, st));
-    cudaFreeAsync(d_x, st);
-    cudaFreeAsync(d_y, st);
+    const size_t xb = batch * m->cols * 4, yb = batch * count * 4, xb_al = (xb + 255) & ~size_t(255);
+    int rc;
+    uint8_t *io = static_cast<uint8_t *>(io_buffer(ctx, xb_al + yb, &rc));
+    if (!io) return rc;
+    float *hs = static_cast<float *>(pinned_staging(ctx, std::max(xb, yb), &rc));
+    if (!hs) return rc;
+    float *d_x = reinterpret_cast<float *>(io), *d_y = reinterpret_cast<float *>(io + xb_al);
+    // The pinned buffer may still feed an earlier call's copy on this stream.
     URB_CUDA(ctx, cudaStreamSynchronize(st));
-    return rc;
+    std::memcpy(hs, x, xb);
+    URB_CUDA(ctx, cudaMemcpyAsync(d_x, hs, xb, cudaMemcpyHostToDevice, st));
+    rc = device_product(ctx, m, start, count, d_x, batch, d_y, nullptr, st);
+    if (rc) return rc;
+    URB_CUDA(ctx, cudaMemcpyAsync(hs, d_y, yb, cudaMemcpyDeviceToHost, st));
+    URB_CUDA(ctx, cudaStreamSynchronize(st));
+    std::memcpy(y, hs, yb);
+    return URB_OK;
 }
 
 int new_mat(urb_ctx *ctx, int fmt, size_t rows, size_t cols, urb_mat **out) {
@@ -288,6 +331,7 @@ int urb_ctx_destroy(urb_ctx *ctx) {
     cudaSetDevice(ctx->device);
     if (ctx->stream) cudaStreamSynchronize(ctx->stream);
     if (ctx->ws) cudaFree(ctx->ws);
+    if (ctx->io) cudaFree(ctx->io);
     if (ctx->d_status) cudaFree(ctx->d_status);
     if (ctx->expf_keys) cudaFree(const_cast<uint32_t *>(ctx->expf_keys));
     if (ctx->log1pf_keys) cudaFree(const_cast<uint32_t *>(ctx->log1pf_keys));

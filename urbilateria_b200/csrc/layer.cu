@@ -802,8 +802,9 @@ int urb_moe_forward(urb_ctx *ctx, urb_layer *L, const float *x, size_t tokens, f
     if (tokens == 0) return URB_OK;
     cudaStream_t st = ctx->stream;
     const size_t H = L->hidden, TK = tokens * L->geo.top_k, E = L->experts;
-    float *d_io = nullptr;
-    URB_CUDA(ctx, cudaMallocAsync(&d_io, 2 * tokens * H * 4, st));
+    int io_rc;
+    float *d_io = static_cast<float *>(io_buffer(ctx, 2 * tokens * H * 4, &io_rc));
+    if (!d_io) return io_rc;
     float *d_x = d_io, *d_out = d_io + tokens * H;
     URB_CUDA(ctx, cudaMemsetAsync(ctx->d_status, 0, 4, st));
     URB_CUDA(ctx, cudaMemcpyAsync(d_x, x, tokens * H * 4, cudaMemcpyDefault, st));
@@ -816,16 +817,12 @@ int urb_moe_forward(urb_ctx *ctx, urb_layer *L, const float *x, size_t tokens, f
             URB_CUDA(ctx, cudaStreamSynchronize(st));
             return int(URB_OK);
         }();
-        cudaFreeAsync(d_io, st);
         cudaStreamSynchronize(st);
         return rc;
     }
     MoeWork w{};
     int rc = moe_forward_device(L, d_x, int(tokens), d_out, &w, ctx->d_status, st);
-    if (rc) {
-        cudaFreeAsync(d_io, st);
-        return rc;
-    }
+    if (rc) return rc;
     int32_t status = 0;
     URB_CUDA(ctx, cudaMemcpyAsync(out, d_out, tokens * H * 4, cudaMemcpyDefault, st));
     if (route_expert) URB_CUDA(ctx, cudaMemcpyAsync(route_expert, w.ids, TK * 4, cudaMemcpyDefault, st));
@@ -836,7 +833,6 @@ int urb_moe_forward(urb_ctx *ctx, urb_layer *L, const float *x, size_t tokens, f
     if (perm_token) URB_CUDA(ctx, cudaMemcpyAsync(perm_token, w.perm_token, TK * 4, cudaMemcpyDefault, st));
     if (perm_slot) URB_CUDA(ctx, cudaMemcpyAsync(perm_slot, w.perm_slot, TK * 4, cudaMemcpyDefault, st));
     URB_CUDA(ctx, cudaMemcpyAsync(&status, ctx->d_status, 4, cudaMemcpyDeviceToHost, st));
-    cudaFreeAsync(d_io, st);
     URB_CUDA(ctx, cudaStreamSynchronize(st));
     if (status) return set_error(ctx, status, "MoE forward rejected its input");
     return URB_OK;
@@ -913,9 +909,10 @@ int urb_moe_forward_routed_ex(urb_ctx *ctx, urb_layer *L, const float *x, size_t
                 return set_error(ctx, URB_ERR_INVALID_ARGUMENT,
                                  "routed expert weight must be finite and non-negative");
     cudaStream_t st = ctx->stream;
-    uint8_t *d_io = nullptr;
     const size_t bytes = 2 * tokens * H * 4 + 2 * TK * 4;
-    URB_CUDA(ctx, cudaMallocAsync(&d_io, bytes, st));
+    int io_rc;
+    uint8_t *d_io = static_cast<uint8_t *>(io_buffer(ctx, bytes, &io_rc));
+    if (!d_io) return io_rc;
     float *d_x = reinterpret_cast<float *>(d_io), *d_out = d_x + tokens * H;
     int32_t *d_ids = reinterpret_cast<int32_t *>(d_out + tokens * H);
     float *d_w = reinterpret_cast<float *>(d_ids + TK);
@@ -925,14 +922,10 @@ int urb_moe_forward_routed_ex(urb_ctx *ctx, urb_layer *L, const float *x, size_t
     URB_CUDA(ctx, cudaMemcpyAsync(d_w, route_weight, TK * 4, cudaMemcpyDefault, st));
     int rc = moe_forward_device(L, d_x, int(tokens), d_out, nullptr, ctx->d_status, st, d_ids, d_w,
                                 &num);
-    if (rc) {
-        cudaFreeAsync(d_io, st);
-        return rc;
-    }
+    if (rc) return rc;
     int32_t status = 0;
     URB_CUDA(ctx, cudaMemcpyAsync(out, d_out, tokens * H * 4, cudaMemcpyDefault, st));
     URB_CUDA(ctx, cudaMemcpyAsync(&status, ctx->d_status, 4, cudaMemcpyDeviceToHost, st));
-    cudaFreeAsync(d_io, st);
     URB_CUDA(ctx, cudaStreamSynchronize(st));
     if (status) return set_error(ctx, status, "MoE forward rejected its input");
     return URB_OK;
@@ -985,8 +978,9 @@ int urb_moe_forward_ex(urb_ctx *ctx, urb_layer *L, const float *x, size_t tokens
     const size_t o_w = align(o_ids + TK * 4), o_s = align(o_w + TK * 4), o_h = align(o_s + TK * 4);
     const size_t o_g = align(o_h + TK * 4);
     const size_t bytes = align(o_g + tokens * 4);
-    uint8_t *d = nullptr;
-    URB_CUDA(ctx, cudaMallocAsync(&d, bytes, st));
+    int io_rc;
+    uint8_t *d = static_cast<uint8_t *>(io_buffer(ctx, bytes, &io_rc));
+    if (!d) return io_rc;
     float *d_x = reinterpret_cast<float *>(d + o_x), *d_out = reinterpret_cast<float *>(d + o_out);
     float *d_l = reinterpret_cast<float *>(d + o_l);
     double *d_x64 = reinterpret_cast<double *>(d + o_x64);
@@ -1005,7 +999,7 @@ int urb_moe_forward_ex(urb_ctx *ctx, urb_layer *L, const float *x, size_t tokens
                                       static_cast<const uint16_t *>(L->shared_gate_row->raw_values),
                                       d_x, int(tokens), int(H), d_l, d_g, ctx->d_status, st);
         prof_end(ctx, st);
-        if (rc) { cudaFreeAsync(d, st); return cuda_fail(ctx, cudaGetLastError(), "router logits"); }
+        if (rc) { return cuda_fail(ctx, cudaGetLastError(), "router logits"); }
         prof_begin(ctx, URB_K_ROUTE, st);
         rc = launch_route_softmax(ctx, d_l, int(tokens), int(E), int(K), d_ids, d_w, ctx->d_status,
                                   st, 1);
@@ -1016,7 +1010,7 @@ int urb_moe_forward_ex(urb_ctx *ctx, urb_layer *L, const float *x, size_t tokens
         prof_begin(ctx, URB_K_ROUTER_LOGITS, st);
         rc = launch_router_logits_f64(L->router64, int(E), d_x, int(tokens), int(H), d_x64, d_l, st, &rg);
         prof_end(ctx, st);
-        if (rc) { cudaFreeAsync(d, st); return cuda_fail(ctx, cudaGetLastError(), "router logits"); }
+        if (rc) { return cuda_fail(ctx, cudaGetLastError(), "router logits"); }
         prof_begin(ctx, URB_K_ROUTE, st);
         rc = launch_route_sqrt_softplus(ctx, d_l, L->d_bias, hash_experts ? d_hash : nullptr,
                                         int(tokens), int(E), int(K), L->geo.routed_scaling_factor,
@@ -1026,13 +1020,12 @@ int urb_moe_forward_ex(urb_ctx *ctx, urb_layer *L, const float *x, size_t tokens
     if (rc == URB_OK)
         rc = moe_forward_device(L, d_x, int(tokens), d_out, nullptr, ctx->d_status, st, d_ids,
                                 d_w, &num);
-    if (rc) { cudaFreeAsync(d, st); return rc; }
+    if (rc) return rc;
     int32_t status = 0;
     URB_CUDA(ctx, cudaMemcpyAsync(out, d_out, tokens * H * 4, cudaMemcpyDefault, st));
     if (route_expert) URB_CUDA(ctx, cudaMemcpyAsync(route_expert, d_ids, TK * 4, cudaMemcpyDefault, st));
     if (route_weight) URB_CUDA(ctx, cudaMemcpyAsync(route_weight, d_w, TK * 4, cudaMemcpyDefault, st));
     URB_CUDA(ctx, cudaMemcpyAsync(&status, ctx->d_status, 4, cudaMemcpyDeviceToHost, st));
-    cudaFreeAsync(d, st);
     URB_CUDA(ctx, cudaStreamSynchronize(st));
     if (status) return set_error(ctx, status, "MoE forward rejected its input");
     return URB_OK;
@@ -1066,14 +1059,14 @@ int urb_gated_mlp_forward(urb_ctx *ctx, const urb_mat *g, const urb_mat *u, cons
     for (size_t i = 0; i < tokens * g->cols; ++i)
         if (!std::isfinite(x[i])) return set_error(ctx, URB_ERR_NONFINITE, "gated MLP input is not finite");
     cudaStream_t st = ctx->stream;
-    float *d_io = nullptr;
     const size_t H = g->cols;
-    URB_CUDA(ctx, cudaMallocAsync(&d_io, 2 * tokens * H * 4, st));
+    int io_rc;
+    float *d_io = static_cast<float *>(io_buffer(ctx, 2 * tokens * H * 4, &io_rc));
+    if (!d_io) return io_rc;
     URB_CUDA(ctx, cudaMemcpyAsync(d_io, x, tokens * H * 4, cudaMemcpyDefault, st));
     int rc = gated_mlp_device(ctx, g, u, d, d_io, int(tokens), d_io + tokens * H, nullptr, st);
     if (rc == URB_OK)
         URB_CUDA(ctx, cudaMemcpyAsync(out, d_io + tokens * H, tokens * H * 4, cudaMemcpyDefault, st));
-    cudaFreeAsync(d_io, st);
     URB_CUDA(ctx, cudaStreamSynchronize(st));
     return rc;
 }

@@ -119,6 +119,9 @@ struct Ctx {
     // Grow-only device workspace.
     void *ws = nullptr;
     size_t ws_size = 0;
+    // Grow-only device buffer for the host-pointer entry points' staged inputs and outputs.
+    void *io = nullptr;
+    size_t io_size = 0;
     // Pinned host staging.
     void *pinned = nullptr;
     size_t pinned_size = 0;
@@ -154,6 +157,9 @@ int set_error(Ctx *ctx, int status, const std::string &msg);
 int cuda_fail(Ctx *ctx, cudaError_t err, const char *what);
 void *workspace(Ctx *ctx, size_t bytes, int *status);
 void *pinned_staging(Ctx *ctx, size_t bytes, int *status);
+// Device buffer of the host-pointer entry points (x in, results out); never carved by the
+// device paths, which use workspace().
+void *io_buffer(Ctx *ctx, size_t bytes, int *status);
 
 #define URB_CUDA(ctx, expr)                                                  \
     do {                                                                     \

@@ -39,16 +39,17 @@ def encode_e4m3fn(v: np.ndarray) -> np.ndarray:
     """Vectorised src/math/mxfp.rs:247-275 encode_e4m3fn_finite (RNE, saturating at 448)."""
     v = np.clip(np.asarray(v, dtype=np.float32), -448.0, 448.0)
     mag = np.abs(v)
-    bits = mag.view(np.uint32).astype(np.uint64)
-    retained = (bits >> 20) & 1
-    rounded = (bits + ((1 << 19) - 1) + retained) & ~np.uint64((1 << 20) - 1)
-    e = (rounded >> 23) & 0xFF
-    exponent = np.where(e > 120, e - 120, np.uint64(0))
-    mantissa = (rounded >> 20) & 7
-    normal = np.minimum((exponent << 3) | mantissa, 0x7E)
-    sub = np.rint(mag * np.float32(512.0)).astype(np.uint64)  # rint = ties-to-even
-    code = np.where(mag < np.float32(2.0 ** -6), sub, normal).astype(np.uint64)
-    code = np.where(mag == 0, np.uint64(0), code)
+    bits = mag.view(np.uint32)  # |v| <= 448: the rounding below cannot overflow 32 bits
+    u = np.uint32  # explicit 32-bit constants keep every operation in uint32
+    retained = (bits >> u(20)) & u(1)
+    rounded = (bits + u((1 << 19) - 1) + retained) & u(0xFFF00000)
+    e = (rounded >> u(23)) & u(0xFF)
+    exponent = np.where(e > u(120), e - u(120), u(0))
+    mantissa = (rounded >> u(20)) & u(7)
+    normal = np.minimum((exponent << u(3)) | mantissa, u(0x7E))
+    sub = np.rint(mag * np.float32(512.0)).astype(np.uint32)  # rint = ties-to-even
+    code = np.where(mag < np.float32(2.0 ** -6), sub, normal)
+    code = np.where(mag == 0, np.uint32(0), code)
     neg = np.signbit(v) & (code != 0)
     return (code.astype(np.uint8) | np.where(neg, np.uint8(0x80), np.uint8(0))).astype(np.uint8)
 
