@@ -264,7 +264,9 @@ def bench_matvec(urb, ctx, stream, local, pk_hbm, copies=20, reps=10):
     del graph
     for m in mats:
         m.free()
-    return {"kernel": "k_matvec1<MXFP4> (CUDA cores, 16-row blocks)", "us_per_launch": ms * 1e3,
+    kernel = ("k_matvec1<MXFP4> (CUDA cores, 16-row blocks)" if os.environ.get("URB_MATVEC") == "cuda_cores"
+              else "k_mv_tc<MXFP4> (tcgen05 kind::mxf4, x as 12 E2M1 digit terms, split-K clusters)")
+    return {"kernel": kernel, "us_per_launch": ms * 1e3,
             "bytes_per_launch": nbytes, "achieved_gbs": gbs, "frac_of_measured_hbm": gbs / pk_hbm,
             "launches": reps * copies,
             "l2": "20 distinct 15.6 MB weight copies round-robin; CUDA-graph replay"}

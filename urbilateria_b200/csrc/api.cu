@@ -190,6 +190,16 @@ int tiled_product(Ctx *ctx, const Mat *m, int rb_lo, int rb_hi, const float *d_x
     return rc;
 }
 
+// URB_MATVEC=cuda_cores selects the CUDA-core single-token kernel over the tensor-core one
+// (for comparison; both read resident tiles of the same matrix).
+bool matvec_cuda_cores() {
+    static const bool on = [] {
+        const char *v = std::getenv("URB_MATVEC");
+        return v && std::strcmp(v, "cuda_cores") == 0;
+    }();
+    return on;
+}
+
 // Product of rows [start, start+count) for `batch` tokens; d_y is [batch, count].
 int device_product(Ctx *ctx, const Mat *m, size_t start, size_t count, const float *d_x,
                    size_t batch, float *d_y, int32_t *d_status, cudaStream_t st) {
@@ -212,6 +222,14 @@ int device_product(Ctx *ctx, const Mat *m, size_t start, size_t count, const flo
         int rc = launch_generic_matmul(ctx, m, start, count, d_x, batch, d_y, st);
         prof_end(ctx, st);
         return rc;
+    }
+    if (batch == 1 && matvec_tc_applies(m) && !matvec_cuda_cores()) {
+        // Single-token product: residual-term x against the resident tcgen05 tiles, split-K
+        // over clusters (matvec_tc.cu).
+        prof_begin(ctx, URB_K_PRODUCT, st);
+        int rc = launch_matvec_tc(ctx, m, start, count, d_x, d_y, d_status, st);
+        prof_end(ctx, st);
+        if (rc != URB_ERR_UNSUPPORTED) return rc;  // very long K: the CUDA-core kernel below
     }
     if (batch == 1 && (m->format == URB_FMT_MXFP4 || m->format == URB_FMT_MXFP8) && !d_status) {
         // Single-token product: the CUDA-core matvec (no activation shifts needed; input

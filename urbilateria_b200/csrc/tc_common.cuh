@@ -63,6 +63,24 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
         : "memory");
 }
 
+// An L2 eviction policy that lets the lines a copy brings in go first: for data streamed once
+// (weights of a decode product), so it does not displace what is read again (activations,
+// instructions).
+__device__ __forceinline__ uint64_t l2_evict_first_policy() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+
+// bulk_g2s with an L2 cache policy.
+__device__ __forceinline__ void bulk_g2s_hint(void *dst, const void *src, uint32_t bytes, uint64_t *bar,
+                                              uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;"
+        ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+        : "memory");
+}
+
 // Prefetches [src, src + bytes) into L2 (TMA engine, no completion tracking).  src 16-byte
 // aligned, bytes a multiple of 16.
 __device__ __forceinline__ void bulk_prefetch_l2(const void *src, uint32_t bytes) {

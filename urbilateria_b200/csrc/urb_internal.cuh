@@ -223,6 +223,11 @@ int launch_bf16_swiglu(Ctx *ctx, const Mat *g, const Mat *u, const Mat *d, const
                        int tokens, float *d_h, float *d_out, int32_t *d_status, cudaStream_t st);
 int launch_matvec1(Ctx *ctx, const Mat *m, size_t start, size_t count, const float *d_x,
                    float *d_y, cudaStream_t st);
+// Single-token product on the block-scaled tensor cores over the resident tcgen05 tiles
+// (matvec_tc.cu); d_status (may be null) receives URB_ERR_NONFINITE for a non-finite input.
+bool matvec_tc_applies(const Mat *m);
+int launch_matvec_tc(Ctx *ctx, const Mat *m, size_t start, size_t count, const float *d_x,
+                     float *d_y, int32_t *d_status, cudaStream_t st);
 // api.cu: y[batch, count] = rows start..start+count of any matrix times d_x [batch, cols]
 // (device pointers, stream-ordered; every format and layout).
 int product_device(Ctx *ctx, const Mat *m, size_t start, size_t count, const float *d_x,
