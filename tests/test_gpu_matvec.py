@@ -214,3 +214,27 @@ def test_host_matvec_rows_allocates_nothing_in_steady_state(ctx):
     assert before == after, (before, after)
     assert all(np.array_equal(ys[0], y) for y in ys[:3])
     m.free()
+
+
+@pytest.mark.parametrize("fmt", ["mxfp4", "mxfp8"])
+def test_mx_matrix_keeps_one_resident_copy(ctx, fmt):
+    """An MX upload keeps only its block-scaled tensor-core tiles (payload + scales, the
+    reference's resident_bytes) and one exponent byte per row: every product path reads them."""
+    from helpers import memory_state
+    import torch
+    g = syn.rng(9300)
+    rows, cols = 4096, 7168
+    torch.cuda.synchronize()
+    before = memory_state(ctx.device)[0]
+    if fmt == "mxfp4":
+        m = urb.MxFp4Matrix.from_packed(rows, cols, 32, *syn.mxfp4_matrix(g, rows, cols), ctx=ctx)
+    else:
+        v = g.integers(0, 0x7e, size=(rows, cols), dtype=np.uint8)
+        m = urb.MxFp8Matrix.from_packed(rows, cols, 1, 32, v, g.integers(117, 124, size=(rows, cols // 32),
+                                                                          dtype=np.uint8), ctx=ctx)
+    torch.cuda.synchronize()
+    grew = memory_state(ctx.device)[0] - before
+    assert grew <= m.resident_bytes() + rows + 4096, (grew, m.resident_bytes())
+    x = syn.normal_f32(g, (3, cols))
+    assert np.isfinite(m.matmul_rows(x, 3)).all()
+    m.free()

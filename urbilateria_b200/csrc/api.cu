@@ -217,31 +217,41 @@ int device_product(Ctx *ctx, const Mat *m, size_t start, size_t count, const flo
         prof_end(ctx, st);
         if (rc != URB_ERR_UNSUPPORTED) return rc;
     }
+    if (matvec_tc_applies(m) && !(batch == 1 && matvec_cuda_cores())) {
+        // MX matrices: the resident tcgen05 tiles.  One token: digit-term x, split-K clusters
+        // (matvec_tc.cu); more tokens, or K longer than the clusters hold: the grouped
+        // tensor-core pass with every token in one group (dense_tc.cu).
+        int rc = URB_ERR_UNSUPPORTED;
+        if (batch == 1) {
+            prof_begin(ctx, URB_K_PRODUCT, st);
+            rc = launch_matvec_tc(ctx, m, start, count, d_x, d_y, d_status, st);
+            prof_end(ctx, st);
+        }
+        if (rc == URB_ERR_UNSUPPORTED)
+            rc = dense_tc_product(ctx, m, start, count, d_x, int(batch), d_y, d_status, st);
+        return rc;
+    }
     if (!m->tiled) {
         prof_begin(ctx, URB_K_PRODUCT, st);
         int rc = launch_generic_matmul(ctx, m, start, count, d_x, batch, d_y, st);
         prof_end(ctx, st);
         return rc;
     }
-    if (batch == 1 && matvec_tc_applies(m) && !matvec_cuda_cores()) {
-        // Single-token product: residual-term x against the resident tcgen05 tiles, split-K
-        // over clusters (matvec_tc.cu).
-        prof_begin(ctx, URB_K_PRODUCT, st);
-        int rc = launch_matvec_tc(ctx, m, start, count, d_x, d_y, d_status, st);
-        prof_end(ctx, st);
-        if (rc != URB_ERR_UNSUPPORTED) return rc;  // very long K: the CUDA-core kernel below
-    }
     if (batch == 1 && (m->format == URB_FMT_MXFP4 || m->format == URB_FMT_MXFP8) && !d_status) {
-        // Single-token product: the CUDA-core matvec (no activation shifts needed; input
-        // finiteness is checked by the host entry points, or through d_status below).
+        // URB_MATVEC=cuda_cores: the CUDA-core kernel over the mma.sync tiles (no activation
+        // shifts needed; input finiteness is checked by the host entry points, or through
+        // d_status below).
+        int rc = ensure_mma_tiles(ctx, m, st);
+        if (rc) return rc;
         prof_begin(ctx, URB_K_PRODUCT, st);
-        int rc = launch_matvec1(ctx, m, start, count, d_x, d_y, st);
+        rc = launch_matvec1(ctx, m, start, count, d_x, d_y, st);
         prof_end(ctx, st);
         return rc;
     }
+    int rc = ensure_mma_tiles(ctx, m, st);  // MX here only under URB_MATVEC=cuda_cores
+    if (rc) return rc;
     int rb_lo = int(start / 16), rb_hi = int(div_ceil(start + count, 16));
     size_t out_rows = size_t(rb_hi - rb_lo) * 16;
-    int rc;
     size_t need = batch * 4 + batch * out_rows * 4 + 64 * 1024 + 4096;
     uint8_t *ws = static_cast<uint8_t *>(workspace(ctx, need, &rc));
     if (!ws) return rc;

@@ -552,6 +552,9 @@ int moe_forward_generic(Layer *L, const float *d_x, int T, float *d_out, int32_t
 int gated_mlp_device(Ctx *ctx, const Mat *g, const Mat *u, const Mat *d, const float *d_x, int T,
                      float *d_out, int32_t *d_status, cudaStream_t st) {
     const size_t H = g->cols, I = g->rows;
+    // MX projections: the grouped tensor-core passes over their resident tcgen05 tiles.
+    if (dense_tc_mlp_applies(g, u, d))
+        return dense_tc_mlp(ctx, g, u, d, d_x, T, d_out, d_status, st, nullptr, 0);
     if (!(g->tiled && u->tiled && d->tiled && g->format == u->format))
         return gated_mlp_generic(ctx, g, u, d, d_x, T, d_out, d_status, st);
     const int nseg = int(div_ceil(T, kCap));
@@ -678,9 +681,41 @@ static int create_layer(urb_ctx *ctx, const urb_mat *router, const float *bias, 
         int rc = check_mlp(sg, su, sd);
         if (rc) return set_error(ctx, rc, "shared expert shape/format is not supported");
     }
+    // MX experts with tcgen05 tiles take the tensor-core passes whatever their scale range.
+    auto tc_mlp = [&](const urb_mat *g, const urb_mat *u, const urb_mat *d) {
+        return (fmt == URB_FMT_MXFP4 || fmt == URB_FMT_MXFP8) && g->format == fmt &&
+               u->format == fmt && d->format == fmt && g->tc_tiles && u->tc_tiles && d->tc_tiles;
+    };
     bool generic = false;
-    for (size_t e = 0; e < e_count; ++e) generic |= !tiled_mlp(gate[e], up[e], down[e]);
-    if (have_shared) generic |= !tiled_mlp(sg, su, sd);
+    for (size_t e = 0; e < e_count; ++e)
+        generic |= !(tiled_mlp(gate[e], up[e], down[e]) || tc_mlp(gate[e], up[e], down[e]));
+    if (have_shared) generic |= !(tiled_mlp(sg, su, sd) || tc_mlp(sg, su, sd));
+    const char *path = std::getenv("URB_MOE_PATH");
+    bool have_tc = !generic && (fmt == URB_FMT_MXFP4 || fmt == URB_FMT_MXFP8);
+    for (size_t e = 0; e < e_count && have_tc; ++e) have_tc = tc_mlp(gate[e], up[e], down[e]);
+    if (have_shared) have_tc = have_tc && tc_mlp(sg, su, sd);
+    // Block-scaled tcgen05 passes by default; URB_MOE_PATH=mma selects the mma.sync passes,
+    // which need every expert in that layout (MX experts build it now from their tcgen05 tiles).
+    const bool use_tc = have_tc && !(path && std::strcmp(path, "mma") == 0);
+    if (!use_tc && !generic) {
+        for (size_t e = 0; e < e_count; ++e) generic |= !tiled_mlp(gate[e], up[e], down[e]);
+        if (have_shared) generic |= !tiled_mlp(sg, su, sd);
+    }
+    if (!use_tc && !generic) {
+        auto build = [&](const urb_mat *m) { return ensure_mma_tiles(ctx, m, ctx->stream); };
+        for (size_t e = 0; e < e_count; ++e) {
+            int rc = build(gate[e]);
+            if (!rc) rc = build(up[e]);
+            if (!rc) rc = build(down[e]);
+            if (rc) return rc;
+        }
+        if (have_shared) {
+            int rc = build(sg);
+            if (!rc) rc = build(su);
+            if (!rc) rc = build(sd);
+            if (rc) return rc;
+        }
+    }
     urb_layer *L = new urb_layer();
     L->generic = generic;
     L->ctx = ctx;
@@ -711,14 +746,7 @@ static int create_layer(urb_ctx *ctx, const urb_mat *router, const float *bias, 
     };
     for (size_t e = 0; e < e_count; ++e) put(e, gate[e], up[e], down[e]);
     if (have_shared) put(e_count, sg, su, sd);
-    const char *path = std::getenv("URB_MOE_PATH");
-    bool have_tc = !generic && (fmt == URB_FMT_MXFP4 || fmt == URB_FMT_MXFP8);
-    for (size_t e = 0; e < e_count && have_tc; ++e)
-        have_tc = gate[e]->tc_tiles && up[e]->tc_tiles && down[e]->tc_tiles;
-    if (L->sg) have_tc = have_tc && L->sg->tc_tiles && L->su->tc_tiles && L->sd->tc_tiles;
-    // Block-scaled tcgen05 passes by default; URB_MOE_PATH=mma selects the mma.sync passes.
-    L->use_tc = have_tc && !(path && std::strcmp(path, "mma") == 0);
-    if (generic) L->use_tc = false;
+    L->use_tc = use_tc && !generic;
     if (e_count != experts && !have_tc) {
         delete L;
         return set_error(ctx, URB_ERR_UNSUPPORTED, "expert shards need MX experts (tensor-core passes)");

@@ -101,6 +101,15 @@ int urb_gated_mlp_forward_device_noalloc(urb_ctx *ctx, const urb_mat *g, const u
                                 d_status, ctx->stream);
         if (rc != URB_ERR_UNSUPPORTED) return rc;
     }
+    if (dense_tc_mlp_applies(g, u, d)) {
+        // MX projections: the grouped tensor-core passes over their tcgen05 tiles, every table,
+        // activation stage and h in the scratch (the same passes as the allocating entry point).
+        uint8_t *base = nullptr;
+        int rc = scratch_of(ctx, &base);
+        if (rc) return rc;
+        return dense_tc_mlp(ctx, g, u, d, d_x, int(T), d_out, d_status, ctx->stream, base,
+                            kNoallocScratchBytes);
+    }
     if (!g->tiled || !u->tiled || !d->tiled || g->format != u->format)
         return set_error(ctx, URB_ERR_UNSUPPORTED,
                          "no-alloc gated MLP needs gate/up/down in one tiled format (MXFP4 / "

@@ -1,5 +1,7 @@
 // upload.cu — device residency for weight matrices: payload validation (the checks of the
 // reference constructors) and the repack into the tiled layout described in urb_internal.cuh.
+#include <mutex>
+
 #include "urb_internal.cuh"
 #include "urb_tc.cuh"
 
@@ -125,9 +127,66 @@ __global__ void k_repack(const uint8_t *values, const uint8_t *scales, size_t ro
     }
 }
 
+// The mma.sync tiles of an MX matrix from its tcgen05 tiles (every byte the same as k_repack
+// writes from the reference layout, padding included): one thread per (tile, lane).
+template <int FMT>
+__global__ void k_bs_to_mma(const uint8_t *bs, int mts, int rbs, int kslices, uint8_t *tiles) {
+    const size_t id = blockIdx.x * size_t(blockDim.x) + threadIdx.x;
+    if (id >= size_t(rbs) * kslices * 32) return;
+    const int lane = int(id & 31);
+    const size_t tile = id >> 5;
+    const int s = int(tile % kslices);
+    const size_t rb = tile / kslices;
+    const int g = lane >> 2, q = lane & 3;
+    const int col0 = s * 128 + q * 32;                       // the lane's 32-column group
+    constexpr int SC = bs_stage_cols(FMT), TB = bs_tile_bytes(FMT);
+    constexpr int half = tile_payload_bytes(FMT) / 64;       // bytes per row per lane
+    uint8_t *dst = tiles + tile * tile_bytes(FMT);
+    for (int h = 0; h < 2; ++h) {
+        const size_t row = rb * 16 + g + 8 * h;
+        const int rr = int(row & 127), kb = (col0 % SC) / 32;
+        const uint8_t *t = bs + (size_t(col0 / SC) * mts + row / 128) * TB;
+        const uint8_t *rowp = t + (rr >> 3) * 1024 + (rr & 7) * 128;
+        uint8_t *d = dst + lane * (2 * half) + h * half;
+        if (FMT == URB_FMT_MXFP4) {
+            *reinterpret_cast<uint4 *>(d) = *reinterpret_cast<const uint4 *>(rowp + ((kb ^ (rr & 7)) << 4));
+        } else {
+            *reinterpret_cast<uint4 *>(d) = *reinterpret_cast<const uint4 *>(rowp + (((2 * kb) ^ (rr & 7)) << 4));
+            *reinterpret_cast<uint4 *>(d + 16) =
+                *reinterpret_cast<const uint4 *>(rowp + (((2 * kb + 1) ^ (rr & 7)) << 4));
+        }
+        dst[tile_payload_bytes(FMT) + 2 * lane + h] =
+            t[16384 + 512 * (kb >> 2) + 16 * (rr & 31) + 4 * (rr >> 5) + (kb & 3)];
+    }
+}
+
 size_t div_ceil(size_t a, size_t b) { return (a + b - 1) / b; }
 
+std::mutex g_mma_tiles_mu;
+
 }  // namespace
+
+int ensure_mma_tiles(Ctx *ctx, const Mat *cm, cudaStream_t st) {
+    Mat *m = const_cast<Mat *>(cm);
+    std::lock_guard<std::mutex> lk(g_mma_tiles_mu);
+    if (m->tiles || !m->tiled) return URB_OK;
+    if (!m->tc_tiles || (m->format != URB_FMT_MXFP4 && m->format != URB_FMT_MXFP8))
+        return set_error(ctx, URB_ERR_UNSUPPORTED, "no tiles to build the mma.sync layout from");
+    uint8_t *t = nullptr;
+    const size_t total = size_t(m->rbs) * m->kslices * tile_bytes(m->format);
+    URB_CUDA(ctx, cudaMallocAsync((void **)&t, total, st));
+    const size_t threads = size_t(m->rbs) * m->kslices * 32;
+    const unsigned blocks = unsigned(div_ceil(threads, 256));
+    if (m->format == URB_FMT_MXFP4)
+        k_bs_to_mma<URB_FMT_MXFP4><<<blocks, 256, 0, st>>>(m->tc_tiles, m->tc_mts, m->rbs, m->kslices, t);
+    else
+        k_bs_to_mma<URB_FMT_MXFP8><<<blocks, 256, 0, st>>>(m->tc_tiles, m->tc_mts, m->rbs, m->kslices, t);
+    URB_CUDA(ctx, cudaGetLastError());
+    // Other streams may read the tiles next: they are complete before the pointer is published.
+    URB_CUDA(ctx, cudaStreamSynchronize(st));
+    m->tiles = t;
+    return URB_OK;
+}
 
 int upload_matrix(Ctx *ctx, Mat *m, const void *values, const uint8_t *scales) {
     cudaStream_t st = ctx->stream;
@@ -218,7 +277,9 @@ int upload_matrix(Ctx *ctx, Mat *m, const void *values, const uint8_t *scales) {
         if (rc) return rc;
     }
     m->tiled = tiled_shape && !(flags & kFlagWide);
-    if (m->tiled) {
+    // MX matrices keep only the tcgen05 tiles (the mma.sync layout is built on first use, from
+    // them); BF16 keeps its row-major upload and the mma.sync tiles.
+    if (m->tiled && !mx) {
         size_t total = size_t(m->rbs) * m->kslices * tile_bytes(m->format);
         URB_CUDA(ctx, cudaMallocAsync((void **)&m->tiles, total, st));
         size_t threads = size_t(m->rbs) * m->kslices * 32;
@@ -242,14 +303,15 @@ int upload_matrix(Ctx *ctx, Mat *m, const void *values, const uint8_t *scales) {
                                                            32, m->rbs, m->kslices, m->tiles);
         }
         URB_CUDA(ctx, cudaGetLastError());
-        // MX payloads keep only the tiled copies.  BF16 keeps its row-major copy as well: the
-        // bit-exact router reads whole rows in column order.
-        if (m->format != URB_FMT_BF16) {
-            URB_CUDA(ctx, cudaFreeAsync(m->raw_values, st));
-            m->raw_values = nullptr;
-            if (m->raw_scales) URB_CUDA(ctx, cudaFreeAsync(m->raw_scales, st));
-            m->raw_scales = nullptr;
-        }
+        // BF16 keeps its row-major copy as well: the bit-exact router reads whole rows in
+        // column order.
+    }
+    if (mx && m->tc_tiles) {
+        // The tcgen05 tiles hold every weight and scale: the reference layout goes.
+        URB_CUDA(ctx, cudaFreeAsync(m->raw_values, st));
+        m->raw_values = nullptr;
+        if (m->raw_scales) URB_CUDA(ctx, cudaFreeAsync(m->raw_scales, st));
+        m->raw_scales = nullptr;
     }
     URB_CUDA(ctx, cudaStreamSynchronize(st));
     return URB_OK;

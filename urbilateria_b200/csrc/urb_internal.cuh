@@ -46,7 +46,8 @@ struct Mat {
     size_t rows = 0, cols = 0;
     size_t group_size = 0, block_rows = 0, block_cols = 0;
     size_t resident_bytes = 0;  // reference payload bytes (WeightMatrix::resident_bytes)
-    // Tiled fast path.
+    // mma.sync layout: `tiled` says the matrix can take it (BF16 keeps it from the upload on;
+    // MX matrices build it on first use from their tcgen05 tiles, ensure_mma_tiles).
     bool tiled = false;
     int rbs = 0, kslices = 0;
     uint8_t *tiles = nullptr;
@@ -223,6 +224,21 @@ int launch_bf16_swiglu(Ctx *ctx, const Mat *g, const Mat *u, const Mat *d, const
                        int tokens, float *d_h, float *d_out, int32_t *d_status, cudaStream_t st);
 int launch_matvec1(Ctx *ctx, const Mat *m, size_t start, size_t count, const float *d_x,
                    float *d_y, cudaStream_t st);
+// dense_tc.cu: MX gated MLP and batched products on the block-scaled tensor-core passes (the
+// resident tcgen05 tiles), all tokens in one group.  dense_tc_mlp uses `mem` (mem_bytes of
+// device memory, at least dense_tc_mlp_bytes) when given, else the context workspace.
+bool dense_tc_mlp_applies(const Mat *g, const Mat *u, const Mat *d);
+size_t dense_tc_mlp_bytes(const Mat *g, const Mat *u, const Mat *d, int T);
+int dense_tc_mlp(Ctx *ctx, const Mat *g, const Mat *u, const Mat *d, const float *d_x, int T,
+                 float *d_out, int32_t *d_status, cudaStream_t st, uint8_t *mem, size_t mem_bytes);
+// Rows [start, start + count) of an MX matrix with tcgen05 tiles times d_x [T, cols] into
+// d_y [T, count].
+int dense_tc_product(Ctx *ctx, const Mat *m, size_t start, size_t count, const float *d_x, int T,
+                     float *d_y, int32_t *d_status, cudaStream_t st);
+// upload.cu: the 16-row mma.sync tiles of an MX matrix, built from its tcgen05 tiles on first
+// use (the mma.sync layer passes and the CUDA-core single-token fallback); MX uploads keep only
+// the tcgen05 tiles.
+int ensure_mma_tiles(Ctx *ctx, const Mat *m, cudaStream_t st);
 // Single-token product on the block-scaled tensor cores over the resident tcgen05 tiles
 // (matvec_tc.cu); d_status (may be null) receives URB_ERR_NONFINITE for a non-finite input.
 bool matvec_tc_applies(const Mat *m);
