@@ -415,88 +415,170 @@ def bench_configs(urb, native, ctx, local, pk_hbm):
             mtx.free()
     r3.free()
 
-    # Config 4: 4 stacked MoE layers (hidden 7168, 384 MXFP4 routed experts top-8 + 1 shared,
-    # intermediate 2048, config-2 routing), h <- h + MoE_l(h) scaled back to unit RMS, batch
-    # 1 / 8 / 64 one-token sequences.  Without the rescale the synthetic weights grow h ~10^4
-    # per layer and overflow f32 inside a step (the routing kernel then rejects the logits and
-    # every later kernel skips its work).  Each layer has its own router, bias and shared
-    # expert; the 384 routed experts are one set of HBM copies that all four layers address
-    # (routes differ per layer, and a step's touched experts far exceed L2, so the traffic per
-    # step is that of distinct layers).
-    E4, L4 = 384, 4
-    pk = [syn.mxfp4_matrix(g, INTER, HIDDEN), syn.mxfp4_matrix(g, INTER, HIDDEN),
-          syn.mxfp4_matrix(g, HIDDEN, INTER)]
+    out["c4"] = bench_c4(urb, native, ctx, local, pk_hbm, 1, 0)
+    out["int_glm"] = bench_int(urb, ctx, g, dev, pk_hbm)
+    return out
 
-    def mlp4():
-        return urb.GatedMlp(*[urb.MxFp4Matrix.from_packed(r, c, 32, p, sc, ctx=ctx)
-                              for (p, sc), (r, c) in zip(pk, [(INTER, HIDDEN), (INTER, HIDDEN),
-                                                             (HIDDEN, INTER)])])
-    routed = [mlp4() for _ in range(E4)]
-    layers = []
-    for _ in range(L4):
-        r4 = urb.Bf16Matrix.from_bits(E4, HIDDEN, syn.bf16_normal(g, (E4, HIDDEN), 0.02), ctx=ctx)
-        layers.append(urb.RuntimeMoeLayer(r4, syn.normal_f32(g, E4, 0.01), routed, mlp4(),
-                                          urb.MoeGeometry(TOP_K, 1, 1, True, SCALE)))
+
+def c4_weights(urb, ctx, dev, layer, held, experts=384):
+    """Config 4 layer `layer`: MXFP4 gate/up [2048 x 7168] and down [7168 x 2048] for the routed
+    experts in `held` plus the shared expert (nibbles uniform 0..15, E8M0 uniform 119..127,
+    drawn on the GPU from one generator per expert, so every rank draws the same weights for
+    the experts it holds), a bf16 router [384 x 7168] ~ N(0, 0.02) and a bias ~ N(0, 0.01)."""
+    import torch
+    from urbilateria_b200 import synthetic as syn
+
+    def mlp(seed):
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(seed)
+        mats = []
+        for r, c in ((INTER, HIDDEN), (INTER, HIDDEN), (HIDDEN, INTER)):
+            p = torch.randint(0, 256, (r * c // 2,), dtype=torch.uint8, device=dev, generator=gen)
+            sc = torch.randint(119, 128, (r * c // 32,), dtype=torch.uint8, device=dev, generator=gen)
+            mats.append(urb.MxFp4Matrix.from_device(r, c, 32, p.data_ptr(), p.numel(), sc.data_ptr(),
+                                                    sc.numel(), ctx=ctx))
+        return urb.GatedMlp(*mats)
+    base = SEED + 40000 * (layer + 1)
+    routed = [mlp(base + e) for e in held]
+    shared = mlp(base + experts)
+    g = syn.rng(base)
+    router = urb.Bf16Matrix.from_bits(experts, HIDDEN, syn.bf16_normal(g, (experts, HIDDEN), 0.02), ctx=ctx)
+    return routed, shared, router, syn.normal_f32(g, experts, 0.01)
+
+
+def bench_c4(urb, native, ctx, local, pk_hbm, world, rank, dist=None):
+    """Config 4: 4 stacked MoE layers, each with its own 384 MXFP4 routed experts (top-8, the
+    config-2 routing) + 1 shared expert (4 x 385 x 23.4 MB = 36 GB of distinct weights on one
+    GPU), h <- h + MoE_l(h) then rescaled to unit RMS (the synthetic weights grow h ~10^5 per
+    layer and would overflow f32 within a step; the rescale stands in for the norm a real model
+    has between layers), decode batches of B = 1 / 8 / 64 one-token sequences.  One GPU: the
+    layers run whole and the step is also timed as one CUDA graph.  N GPUs: rank r holds
+    experts shard_range(384, N, r) of every layer plus the replicated router and shared expert
+    and owns token_range(B, N, r) of the batch (expert parallel, tokens and outputs over
+    NVLink); the step time is the max over ranks."""
+    import torch
+    from urbilateria_b200 import synthetic as syn
+    from urbilateria_b200.expert_parallel import ExpertParallelMoeLayer, shard_range, token_range
+    dev = f"cuda:{local}"
+    E4, L4 = 384, 4
+    eb, ec = shard_range(E4, world, rank) if world > 1 else (0, E4)
+    geo = urb.MoeGeometry(TOP_K, 1, 1, True, SCALE)
+    layers, eps, owned = [], [], []
+    t0 = time.perf_counter()
+    for l in range(L4):
+        routed, shared, router, bias = c4_weights(urb, ctx, dev, l, range(eb, eb + ec), E4)
+        owned.append((routed, shared, router))
+        if world == 1:
+            layers.append(urb.RuntimeMoeLayer(router, bias, routed, shared, geo))
+        else:
+            lay = urb.RuntimeMoeLayer(router, bias, routed, shared, geo, expert_range=(eb, ec))
+            layers.append(lay)
+            eps.append(ExpertParallelMoeLayer(lay, world, rank, 64, timeout_ms=20000))
+    torch.cuda.synchronize()
     per_expert = 3 * (INTER * HIDDEN // 2 + INTER * HIDDEN // 32)
-    c4 = {"workload": "C4 stacked MoE decode: 4 layers x (7168, 384 MXFP4 experts top-8 + 1 "
-                      "shared, inter 2048), h <- h + MoE(h)", "layers": L4}
+    c4 = {"workload": "C4 stacked MoE decode: 4 distinct layers x (7168, 384 MXFP4 experts top-8 "
+                      "+ 1 shared, inter 2048), h <- h + MoE(h) rescaled to unit RMS",
+          "layers": L4, "resident_weight_bytes_per_gpu": L4 * (ec + 1) * per_expert,
+          "upload_s": time.perf_counter() - t0,
+          "parallelism": "ep%d" % world if world > 1 else "single"}
+    g = syn.rng(SEED + 13)
     for B in (1, 8, 64):
-        h0 = syn.normal_bf16_as_f32(g, (B, HIDDEN))
-        touched = 0
-        for lay in layers:
-            _, _, _, extra = lay.forward_batch(h0, B, details=True)
-            touched += int((extra["counts"] > 0).sum()) + 1
-        d_h = torch.from_numpy(h0).to(dev)
+        h_all = syn.normal_bf16_as_f32(g, (B, HIDDEN))
+        tb, tc_ = token_range(B, world, rank) if world > 1 else (0, B)
+        d_h = torch.from_numpy(h_all[tb:tb + tc_].copy()).to(dev) if tc_ else torch.empty((0, HIDDEN), device=dev)
         d_o = torch.empty_like(d_h)
+        d_ids = torch.empty((max(tc_, 1), TOP_K), dtype=torch.int32, device=dev)
         st = torch.zeros(1, dtype=torch.int32, device=dev)
 
-        def fn4():
-            for lay in layers:
-                lay.forward_device(d_h.data_ptr(), B, d_o.data_ptr(), 0, 0, st.data_ptr())
-                d_h.add_(d_o)
-                d_h.mul_(torch.rsqrt(d_h.square().mean(dim=1, keepdim=True)))
-        for _ in range(3):
-            fn4()
-        k_ms, s_ms, n = kernel_ms(ctx, native, fn4, 10)
-        per_kind = kernel_ms.per_kind
-        nbytes = touched * per_expert + L4 * E4 * HIDDEN * 2
-        # A decode step's kernels are short next to the host's launch cadence: the step is
-        # also timed as one CUDA graph (the layer forwards' device work alone).
-        graph_us = None
-        try:
-            stream = torch.cuda.current_stream()
-            graph = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(graph, stream=stream):
-                fn4()
-            for _ in range(3):
-                graph.replay()
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            torch.cuda.synchronize()
-            e0.record(stream)
-            for _ in range(10):
-                graph.replay()
-            e1.record(stream)
-            torch.cuda.synchronize()
-            graph_us = e0.elapsed_time(e1) / 10 * 1e3
-            del graph
-        except Exception as exc:  # capture refused: report the eager figures only
-            graph_us = "not captured: %s" % str(exc).splitlines()[0][:120]
+        def step(record=None):
+            for li, lay in enumerate(layers):
+                if world == 1:
+                    lay.forward_device(d_h.data_ptr(), B, d_o.data_ptr(), d_ids.data_ptr() if record is not None else 0,
+                                       0, st.data_ptr())
+                else:
+                    eps[li].forward_device(d_h.data_ptr() if tc_ else 0, tc_, d_o.data_ptr() if tc_ else 0,
+                                           st.data_ptr(), d_ids.data_ptr() if (tc_ and record is not None) else 0)
+                if record is not None and tc_:
+                    record.append(d_ids[:tc_].cpu().numpy().copy())
+                if tc_:
+                    d_h.add_(d_o)
+                    d_h.mul_(torch.rsqrt(d_h.square().mean(dim=1, keepdim=True)))
+        # Experts each layer touches (bytes the step must stream), from one recorded step.
+        rec = []
+        step(rec)
+        torch.cuda.synchronize()
         if int(st.item()) != 0:
             c4["B%d" % B] = {"error": "status %d" % int(st.item())}
             continue
-        c4["B%d" % B] = {"kernel_us": k_ms * 1e3, "stream_us": s_ms * 1e3, "launches": n,
-                         "tokens_per_s": B / (k_ms / 1e3), "stream_tokens_per_s": B / (s_ms / 1e3),
-                         "touched_experts_per_step": touched, "bytes": nbytes,
-                         "kernels_us": per_kind, "graph_us": graph_us,
-                         "graph_tokens_per_s": (B / (graph_us / 1e6)
-                                                if isinstance(graph_us, float) else None),
-                         "achieved_gbs": nbytes / (k_ms / 1e3) / 1e9,
-                         "frac_of_measured_hbm": nbytes / (k_ms / 1e3) / 1e9 / pk_hbm}
+        touched = 0
+        for li in range(L4):
+            ids = rec[li] if rec and tc_ else np.zeros((0, TOP_K), np.int32)
+            if world > 1:
+                every = [None] * world
+                dist.all_gather_object(every, ids)
+                ids = np.concatenate([e for e in every if e is not None and len(e)]) if any(
+                    e is not None and len(e) for e in every) else ids
+            mine = np.unique(ids[(ids >= eb) & (ids < eb + ec)]) if ids.size else []
+            touched += len(mine) + 1
+        for _ in range(3):
+            step()
+        stream = torch.cuda.current_stream()
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = 10
+        e0.record(stream)
+        for _ in range(reps):
+            step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        step_us = e0.elapsed_time(e1) / reps * 1e3
+        graph_us = None
+        if world == 1:
+            try:
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(graph, stream=stream):
+                    step()
+                for _ in range(3):
+                    graph.replay()
+                torch.cuda.synchronize()
+                e0.record(stream)
+                for _ in range(reps):
+                    graph.replay()
+                e1.record(stream)
+                torch.cuda.synchronize()
+                graph_us = e0.elapsed_time(e1) / reps * 1e3
+                del graph
+            except Exception as exc:  # capture refused: report the eager figures only
+                graph_us = "not captured: %s" % str(exc).splitlines()[0][:120]
+        if dist:
+            t = torch.tensor([step_us], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            step_us = float(t.item())
+        if int(st.item()) != 0:
+            c4["B%d" % B] = {"error": "status %d" % int(st.item())}
+            continue
+        nbytes = touched * per_expert + L4 * E4 * HIDDEN * 2
+        best = graph_us if isinstance(graph_us, float) else step_us
+        c4["B%d" % B] = {"step_us": step_us, "graph_us": graph_us,
+                         "tokens_per_s": B / (best / 1e6),
+                         "touched_experts_per_step_this_gpu": touched,
+                         "bytes_per_step_this_gpu": nbytes,
+                         "achieved_gbs_this_gpu": nbytes / (best / 1e6) / 1e9,
+                         "frac_of_measured_hbm": nbytes / (best / 1e6) / 1e9 / pk_hbm,
+                         "timing": ("CUDA-graph replay of the 4-layer step" if isinstance(graph_us, float)
+                                    else "eager stream, max over ranks")}
+    for ep in eps:
+        ep.free()
     for lay in layers:
         lay.free()
-    out["c4"] = c4
-    out["int_glm"] = bench_int(urb, ctx, g, dev, pk_hbm)
-    return out
+    for routed, shared, router in owned:
+        for e in routed + [shared]:
+            for mtx in (e.gate, e.up, e.down):
+                mtx.free()
+        router.free()
+    return c4
 
 
 def bench_int(urb, ctx, g, dev, pk_hbm, reps=5):
@@ -790,6 +872,10 @@ def main():
         line["parity_sample"] = {
             "tokens": n, "routes_equal": bool(np.array_equal(o_ids, ids0[:n])),
             "rel_l2": float(np.linalg.norm(out0[:n] - o_out) / np.linalg.norm(o_out))}
+    if world > 1 and not args.no_configs:
+        # Config 4 expert parallel across the group (stacked decode, B = 1 / 8 / 64 in all).
+        with torch.cuda.stream(stream):
+            line["configs"] = {"c4": bench_c4(urb, native, ctx, local, pk_hbm, world, rank, dist)}
     if rank == 0:
         print(json.dumps(line), flush=True)
     if dist:

@@ -208,6 +208,20 @@ class MxFp4Matrix(_Matrix):
         return cls(ctx, h, rows, cols)
 
 
+    @classmethod
+    def from_device(cls, rows: int, cols: int, group_size: int, d_packed: int, packed_len: int,
+                    d_scales: int, scales_len: int, ctx: Optional[Context] = None):
+        """from_packed with the packed nibbles and scale bytes already in device memory (device
+        pointers; urb_mxfp4_upload accepts host or device memory).  The source buffers may be
+        released once this returns."""
+        ctx = ctx or default_context()
+        h = ctypes.c_void_p()
+        ctx.check(ctx.lib.urb_mxfp4_upload(ctx.h, rows, cols, group_size, ctypes.c_void_p(d_packed),
+                                           packed_len, ctypes.c_void_p(d_scales), scales_len,
+                                           ctypes.byref(h)))
+        return cls(ctx, h, rows, cols)
+
+
 class MxFp8Matrix(_Matrix):
     """MxFp8Matrix with E8M0 block scales (src/math/mxfp.rs:321-877), resident in HBM."""
 
