@@ -365,10 +365,21 @@ def bench_configs(urb, native, ctx, local, pk_hbm):
             x.free()
     out["c1"] = c1
 
-    # Config 3: 128 MXFP8 experts (hidden 4096, intermediate 1536; E4M3 fp8-cast N(0,1), E8M0
-    # 117..123 per 32), 512 tokens with Zipf(1.1) top-8 routes: the experts half of the layer
-    # with the caller's routes.  Every expert is its own HBM copy of one generated matrix set.
-    H3, I3, E3, T3, K3 = 4096, 1536, 128, 512, 8
+    out["c3"] = bench_c3(urb, native, ctx, dev, pk_hbm, g)
+    out["c4"] = bench_c4(urb, native, ctx, local, pk_hbm, 1, 0)
+    out["int_glm"] = bench_int(urb, ctx, g, dev, pk_hbm)
+    return out
+
+
+def bench_c3(urb, native, ctx, dev, pk_hbm, g, E3=128):
+    """Config 3: MXFP8 experts (hidden 4096, intermediate 1536; E4M3 fp8-cast N(0,1), E8M0
+    117..123 per 32), 512 tokens with Zipf(1.1) top-8 routes: the experts half of the layer with
+    the caller's routes.  Every expert is its own HBM copy of one generated matrix set.  E3 = 128
+    is config 3; fewer experts only for profiling captures."""
+    import torch
+    from urbilateria_b200 import synthetic as syn
+    out = {}
+    H3, I3, T3, K3 = 4096, 1536, 512, 8
     gv, gs = syn.mxfp8_matrix(g, I3, H3)
     uv, us_ = syn.mxfp8_matrix(g, I3, H3)
     dv, ds = syn.mxfp8_matrix(g, H3, I3)
@@ -400,7 +411,7 @@ def bench_configs(urb, native, ctx, local, pk_hbm):
     per_expert = 3 * (I3 * H3 + I3 * H3 // 32)
     nbytes = int((counts > 0).sum()) * per_expert
     flops = 2.0 * T3 * K3 * 3 * I3 * H3
-    out["c3"] = {"workload": "C3 MXFP8 grouped experts: 128 x (4096 x 1536 SwiGLU), 512 tokens, "
+    out["c3"] = {"workload": "C3 MXFP8 grouped experts: %d x (4096 x 1536 SwiGLU), 512 tokens, " % E3 +
                              "Zipf(1.1) top-8 (caller routes)",
                  "kernel_us": k_ms * 1e3, "stream_us": s_ms * 1e3, "launches": n,
                  "tokens_per_s": T3 / (k_ms / 1e3), "touched_experts": int((counts > 0).sum()),
@@ -414,10 +425,7 @@ def bench_configs(urb, native, ctx, local, pk_hbm):
         for mtx in (e.gate, e.up, e.down):
             mtx.free()
     r3.free()
-
-    out["c4"] = bench_c4(urb, native, ctx, local, pk_hbm, 1, 0)
-    out["int_glm"] = bench_int(urb, ctx, g, dev, pk_hbm)
-    return out
+    return out["c3"]
 
 
 def c4_weights(urb, ctx, dev, layer, held, experts=384):
@@ -662,6 +670,10 @@ def main():
                     help="tokens per GPU (128 = config 2; other values only for profiling)")
     ap.add_argument("--int-only", action="store_true",
                     help="profiling: time only the INT4 / INT8 products and print their figures")
+    ap.add_argument("--only", choices=["matvec", "c3"],
+                    help="profiling: time only the config-0 matvec or config 3 and print its figures")
+    ap.add_argument("--c3-experts", type=int, default=128,
+                    help="experts of --only c3 (128 = config 3; fewer only for profiling captures)")
     args = ap.parse_args()
     global EXPERTS, TOKENS
     EXPERTS = args.experts
@@ -687,6 +699,16 @@ def main():
     ctx = urb.Context(local)
     stream = torch.cuda.Stream(device=local)
     ctx.set_stream(stream.cuda_stream)
+    if args.only:
+        from urbilateria_b200 import synthetic as syn
+        with torch.cuda.stream(stream):
+            if args.only == "matvec":
+                res = bench_matvec(urb, ctx, stream, local, peaks()[0])
+            else:
+                res = bench_c3(urb, native, ctx, f"cuda:{local}", peaks()[0], syn.rng(SEED + 11),
+                               args.c3_experts)
+        print(json.dumps(res))
+        return
     if args.int_only:
         from urbilateria_b200 import synthetic as syn
         print(json.dumps(bench_int(urb, ctx, syn.rng(SEED + 11), f"cuda:{local}",

@@ -55,7 +55,9 @@ typedef enum urb_status {
     URB_ERR_INVALID_GEOMETRY = 4,  /* RouteError::InvalidGeometry */
     URB_ERR_CUDA = 5,              /* CUDA runtime failure (see urb_last_error) */
     URB_ERR_TIMEOUT = 6,           /* a bounded device wait gave up */
-    URB_ERR_NCCL = 7,              /* NCCL failure in the expert-parallel path */
+    URB_ERR_NCCL = 7,              /* reserved; never returned: the expert-parallel data path
+                                    * runs over peer memory, and the handle exchange is the
+                                    * host's (torch.distributed), whose errors it raises itself */
     URB_ERR_UNSUPPORTED = 8,       /* configuration outside what this build implements */
     URB_ERR_INVALID_ARGUMENT = 9,  /* null handle / pointer */
     URB_ERR_PEER = 10,             /* another rank of the expert-parallel group failed the forward */
