@@ -17,13 +17,14 @@
 // instructions cost ~120-200 cycles of issue each on the issuing thread, while MMAs issued from
 // several threads proceed concurrently, so the per-stage instruction stream is spread over
 // warps:
-//   warp 0 (one thread)  weight producer: tiles into a 6-slot ring (bulk copies, mbarriers);
+//   warp 0 (one thread)  weight producer: tiles into an 8-slot ring (bulk copies, mbarriers);
 //   warp 3 (one thread)  activation producer: stages into a byte ring (variable-size stages,
 //                        up to 16 in flight) from their L2-resident source;
 //   warps 8-11           scale warps: each stage's E8M0 scales of both operands from shared
 //                        memory into TMEM with tcgen05.st (each warp fills its lane quarter);
 //   warps 1, 2           MMA issuers (one thread each), each into its own TMEM accumulator;
-//   warps 4-7            epilogue: tcgen05.ld of the accumulators, term sums, results out.
+//   warps 4-7, 12-15     epilogue: tcgen05.ld of the accumulators, term sums, results out
+//                        (the accumulator is released before the results are stored).
 // Down pass: a group is one matrix; the issuers split each stage's 4 K steps, release stages
 // two at a time (one tcgen05.commit on the pair's barrier, a 32-deep ring both producers
 // watch), and the epilogue adds their halves and stores f32 output rows.
@@ -43,19 +44,18 @@
 namespace urb {
 namespace {
 
-constexpr int kSA = 6;                // weight ring depth (also the TMEM scale slots)
+constexpr int kSA = 8;                // weight ring depth (also the TMEM scale slots)
 constexpr int kStage = 17408;         // bytes of one weight slot / largest activation stage
-constexpr int kBRing = 7 * kStage;    // activation byte ring
+constexpr int kBRing = 5 * kStage;    // activation byte ring
 constexpr int kSB = 16;               // activation stages in flight at most
 constexpr int kRel = 32;              // release barriers, one per pair of stages (covers 64)
 constexpr int kIssuers = kBsIssuers;
 constexpr int kStepsPerIssuer = 4 / kIssuers;
-static_assert(kIssuers == 2 || kIssuers == 4, "issuers");
-// Warps: 0 weight producer, 1-2 issuers, 3 activation producer (2 issuers) or 1-3 and 12
-// issuers, 13 activation producer (4 issuers); 4-7 epilogue; 8-11 scale warps.  Each polling
-// thread sits on its own scheduler (warp % 4) where possible.
-constexpr int kThreadsBs = kIssuers == 2 ? 384 : 448;
-constexpr int kWarpBProd = kIssuers == 2 ? 3 : 13;
+static_assert(kIssuers == 2, "issuers");
+// Warps: 0 weight producer, 1-2 issuers, 3 activation producer, 4-7 and 12-15 epilogue, 8-11
+// scale warps.  Each polling thread sits on its own scheduler (warp % 4).
+constexpr int kThreadsBs = 512;
+constexpr int kWarpBProd = 3;
 constexpr uint32_t kAccCols = kBsNmax;  // accumulator columns per issuer
 constexpr uint32_t kSfCol0 = kIssuers * kAccCols;  // first scale column: slot s at +16 s
 constexpr int kSmemBs = kSA * kStage + kBRing + 1024;
@@ -159,8 +159,10 @@ __global__ void __launch_bounds__(kThreadsBs, 1) k_bs_grouped(TcArgs a) {
     constexpr int TPU = MT ? 2 : 1;    // row tiles per unit
     static_assert(!PAIR || kIssuers == 2, "paired tiles run one issuer per tile");
     constexpr int TPS = PAIR ? 2 : 1;  // weight tiles per stage
-    // Weight slots and activation ring bytes (the same split measured best for both modes:
-    // 6 / 7 and 10 / 3 slots gave the paired pass 0.62 ms at C2, 8 / 5 gave 0.76 ms).
+    // Weight slots and activation ring bytes.  The copies of a stage are bound by the SM's
+    // intake (~55 B per cycle from L2 for re-read tiles), so the copy latency grows with the ring
+    // depth; 8 weight slots / 5 activation stages measured 3-6 % faster than 6 / 7 on config 2,
+    // on config 3 and on 32 tokens per expert (10 / 3 starves the activation ring).
     constexpr int SA = kSA;
     constexpr int BRING = kBRing;
     constexpr int TB = bs_tile_bytes(FMT);
@@ -192,7 +194,7 @@ __global__ void __launch_bounds__(kThreadsBs, 1) k_bs_grouped(TcArgs a) {
         for (int s = 0; s < kRel; ++s) tc::mbar_init(&rel[s], kIssuers);  // one commit per issuer
         for (int h = 0; h < 2; ++h) {
             tc::mbar_init(&acc_full[h], kIssuers);
-            tc::mbar_init(&acc_empty[h], 4);
+            tc::mbar_init(&acc_empty[h], 8);  // one arrival per epilogue warp
         }
         for (int s = 0; s < kIssuers; ++s) tc::mbar_init(&mma_done[s], 1);
         tc::mbar_fence_init();
@@ -341,9 +343,9 @@ __global__ void __launch_bounds__(kThreadsBs, 1) k_bs_grouped(TcArgs a) {
             }
             if (!ok) { fail(); break; }
         }
-    } else if ((warp == 1 || warp == 2 || (kIssuers == 4 && (warp == 3 || warp == 12))) && lane == 0) {
+    } else if ((warp == 1 || warp == 2) && lane == 0) {
         // ---------------- MMA issuers (their K steps of every stage) ----------------
-        const int me = warp == 12 ? 3 : warp - 1;
+        const int me = warp - 1;
         uint32_t g = 0;
         AccHalves ah;
         for (UnitCursor uc(a, total_units); uc.valid() && !*abortp; uc.advance()) {
@@ -399,10 +401,17 @@ __global__ void __launch_bounds__(kThreadsBs, 1) k_bs_grouped(TcArgs a) {
         // Every MMA of this thread completes before TMEM is released.
         tc::mma_commit(&mma_done[me]);
         tc::mbar_wait(&mma_done[me], 0, &never);
-    } else if (warp >= 4 && warp < 8) {
+    } else if ((warp >= 4 && warp < 8) || warp >= 12) {
         // ---------------- epilogue ----------------
+        // Two groups of four warps (4-7, 12-15), one warp per TMEM lane quarter in each, take
+        // the even / odd 16-column chunks of a unit.  A warp reads its chunks, forms its
+        // results in registers and releases the accumulator before it stores anything, so the
+        // issuers wait only for the TMEM reads at a unit boundary.
         constexpr int RT = bs_rows_per_tok(FMT), TT = NT, TPC = 16 / RT;
+        constexpr int MYCH = kBsNmax / 32;  // chunks of a full-width unit per group
+        constexpr int NOUT = MT ? 2 : 1;    // outputs per (row, token): the down pass's two tiles
         const int q = warp & 3;  // TMEM lane quarter this warp may access
+        const int eg = warp >= 12 ? 1 : 0;
         const int row = 32 * q + lane;
         const uint32_t lane_base = uint32_t(32 * q) << 16;
         AccHalves ah;
@@ -415,100 +424,99 @@ __global__ void __launch_bounds__(kThreadsBs, 1) k_bs_grouped(TcArgs a) {
             const int grow = x.mt * 128 + row;
             const bool row_ok = grow < S.rows;
             const int tok0 = x.sub * bs_cap(FMT);
-            for (int c = 0; c < x.n / 16; ++c) {
+            const int nch = x.n / 16;
+            float res[MYCH][TPC][NOUT];
+#pragma unroll
+            for (int j = 0; j < MYCH; ++j) {
+                const int c = 2 * j + eg;
+                if (c >= nch) break;  // uniform across the warp
                 uint32_t v[kIssuers][16];
 #pragma unroll
                 for (int i = 0; i < kIssuers; ++i)
                     tc::tmem_ld16(tbase + lane_base + uint32_t(i) * kAccCols + 64u * h0 + 16 * c, v[i]);
                 tc::wait_ld();
-                if constexpr (MT) {
-                    // Output rows of both row tiles (accumulator i: tile mt + i).
 #pragma unroll
-                    for (int s = 0; s < TPC; ++s) {
-                        const int t = TPC * c + s;
-                        if (t >= x.nt) continue;
-                        const int col = S.col_begin + tok0 + t;
-                        float *dst;
-                        if (a.out_ranks && col < a.routed_cols) {
-                            const int i = a.out_rows[col];
-                            dst = a.out_ranks[i / a.out_rank_rows] + size_t(i % a.out_rank_rows) * a.out_stride;
-                        } else {
-                            dst = a.out + size_t(a.out_ranks ? col - a.routed_cols : col) * a.out_stride;
-                        }
+                for (int s = 0; s < TPC; ++s) {
+                    const int t = TPC * c + s;
+                    if (t >= x.nt) continue;
+                    if constexpr (MT) {
+                        // Accumulator i holds row tile mt + i.
 #pragma unroll
                         for (int i = 0; i < 2; ++i) {
-                            const int gr = (x.mt + i) * 128 + row;
-                            if (x.mt + i >= S.mts || gr >= S.rows) continue;
                             float o = 0.0f;
 #pragma unroll
                             for (int e = 0; e < TT; ++e) o += __uint_as_float(v[i][RT * s + e]);
                             if (a.variant != 0) o = num_round_bf16(o);
-                            if (a.variant == 2 && !isfinite(o)) set_status(a.status, URB_ERR_NONFINITE);
-                            dst[S.out_off + gr] = o;
+                            if (a.variant == 2 && !isfinite(o) && x.mt + i < S.mts &&
+                                (x.mt + i) * 128 + row < S.rows)
+                                set_status(a.status, URB_ERR_NONFINITE);
+                            res[j][s][i] = o;
                         }
-                    }
-                    continue;
-                }
-                if constexpr (GU) {
-                    // h = silu(gate) * up of this lane's row for each token of the chunk.
-#pragma unroll
-                    for (int s = 0; s < TPC; ++s) {
-                        const int t = TPC * c + s;
-                        if (t >= x.nt || !row_ok) continue;
+                    } else if constexpr (GU) {
+                        // h = silu(gate) * up of this lane's row.
                         float gv = 0.0f, uv = 0.0f;
 #pragma unroll
                         for (int e = 0; e < TT; ++e) {
                             gv += __uint_as_float(v[0][RT * s + e]);
                             uv += __uint_as_float(v[1][RT * s + e]);
                         }
-                        const int col = S.col_begin + tok0 + t;
                         float h;
                         if (a.variant == 1) {
                             h = num_bounded_swiglu(num_round_bf16(gv), num_round_bf16(uv), a.limit);
-                            h = num_round_bf16(__fmul_rn(h, a.col_w[col]));
-                            if (!isfinite(h)) set_status(a.status, URB_ERR_NONFINITE);
+                            h = num_round_bf16(__fmul_rn(h, a.col_w[S.col_begin + tok0 + t]));
                         } else if (a.variant == 2) {
                             const float act = num_round_bf16(num_silu_libm(num_round_bf16(gv), a.expf));
                             h = num_round_bf16(__fmul_rn(act, num_round_bf16(uv)));
-                            if (!isfinite(h)) set_status(a.status, URB_ERR_NONFINITE);
                         } else {
                             h = silu_f(gv) * uv;
                         }
-                        a.out[size_t(col) * a.out_stride + grow] = h;
-                    }
-                    continue;
-                }
-#pragma unroll
-                for (int s = 0; s < TPC; ++s) {
-                    const int t = TPC * c + s;
-                    if (t < x.nt && row_ok) {
+                        if (a.variant != 0 && row_ok && !isfinite(h)) set_status(a.status, URB_ERR_NONFINITE);
+                        res[j][s][0] = h;
+                    } else {
                         float o = 0.0f;
 #pragma unroll
-                        for (int e = 0; e < TT; ++e) {
-                            float q = __uint_as_float(v[0][RT * s + e]) + __uint_as_float(v[1][RT * s + e]);
-                            if constexpr (kIssuers == 4)
-                                q += __uint_as_float(v[2][RT * s + e]) + __uint_as_float(v[3][RT * s + e]);
-                            o += q;
-                        }
-                        const int col = S.col_begin + tok0 + t;
-                        float *dst;
-                        if (a.out_ranks && col < a.routed_cols) {
-                            const int i = a.out_rows[col];
-                            dst = a.out_ranks[i / a.out_rank_rows] + size_t(i % a.out_rank_rows) * a.out_stride;
-                        } else {
-                            dst = a.out + size_t(a.out_ranks ? col - a.routed_cols : col) * a.out_stride;
-                        }
+                        for (int e = 0; e < TT; ++e)
+                            o += __uint_as_float(v[0][RT * s + e]) + __uint_as_float(v[1][RT * s + e]);
                         if (a.variant != 0) o = num_round_bf16(o);
-                        if (a.variant == 2 && !isfinite(o)) set_status(a.status, URB_ERR_NONFINITE);
-                        dst[S.out_off + grow] = o;
+                        if (a.variant == 2 && row_ok && !isfinite(o)) set_status(a.status, URB_ERR_NONFINITE);
+                        res[j][s][0] = o;
                     }
                 }
             }
+            // Every TMEM read of this warp has completed: the issuers may overwrite the halves.
             tc::fence_before_sync();
             __syncwarp();
             if (lane == 0)
                 for (uint32_t h = 0; h < 2; ++h)
                     if (mask >> h & 1u) tc::mbar_arrive(&acc_empty[h]);
+#pragma unroll
+            for (int j = 0; j < MYCH; ++j) {
+                const int c = 2 * j + eg;
+                if (c >= nch) break;
+#pragma unroll
+                for (int s = 0; s < TPC; ++s) {
+                    const int t = TPC * c + s;
+                    if (t >= x.nt) continue;
+                    const int col = S.col_begin + tok0 + t;
+                    if constexpr (GU) {
+                        if (row_ok) a.out[size_t(col) * a.out_stride + grow] = res[j][s][0];
+                        continue;
+                    }
+                    float *dst;
+                    if (a.out_ranks && col < a.routed_cols) {
+                        const int i = a.out_rows[col];
+                        dst = a.out_ranks[i / a.out_rank_rows] + size_t(i % a.out_rank_rows) * a.out_stride;
+                    } else {
+                        dst = a.out + size_t(a.out_ranks ? col - a.routed_cols : col) * a.out_stride;
+                    }
+#pragma unroll
+                    for (int i = 0; i < NOUT; ++i) {
+                        const int gr = (x.mt + i) * 128 + row;
+                        if (x.mt + i >= S.mts || gr >= S.rows) continue;
+                        dst[S.out_off + gr] = res[j][s][i];
+                    }
+                }
+            }
         }
         // Rows stored into other ranks' memory are visible system-wide before the exchange
         // barrier that follows this launch signals them.
