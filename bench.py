@@ -18,6 +18,8 @@ tokens per step); token rows and expert outputs cross NVLink inside the kernels.
             (profiles/k_bs_grouped_c2_traffic.md)
   cpu_baseline / --impl reference: the CPU restatement of the reference path (oracle/) on the
             host cores, on a bounded token sample
+  per_rank  (N > 1) every rank's gate/up fraction of HBM on its held experts and the
+            exchange kernels' share of its step, with the minimum / maximum over ranks
 
 Every step streams all touched experts' weights (~5.9 GB > 126 MB L2), so no L2 flush is
 needed between steps.
@@ -866,6 +868,24 @@ def main():
         roofline["note"] = "rank 0 of %d: %d held experts touched, %d activation columns" % (
             world, touched, n_cols)
 
+    per_rank = None
+    if dist:
+        # Every rank's own figures (the layer's load differs by rank with the routes): gate/up
+        # fraction of HBM on its held experts, and the exchange kernels' share of the step.
+        ex = kern.get("exchange", {})
+        ex_us = ex.get("ms_per_launch", 0.0) * ex.get("launches", 0) / args.steps * 1e3
+        mine = {"rank": rank, "touched_experts": touched, "activation_columns": n_cols,
+                "gate_up_us": gu.get("ms_per_launch", float("nan")) * 1e3,
+                "gate_up_frac_of_hbm": achieved / pk_hbm,
+                "down_us": dn.get("ms_per_launch", float("nan")) * 1e3,
+                "exchange_us_per_step": ex_us,
+                "exchange_share_of_step": ex_us / (ms / args.steps * 1e3)}
+        every = [None] * world
+        dist.all_gather_object(every, mine)
+        per_rank = {"ranks": every,
+                    "min_gate_up_frac_of_hbm": min(r["gate_up_frac_of_hbm"] for r in every),
+                    "max_exchange_share_of_step": max(r["exchange_share_of_step"] for r in every)}
+
     line = {"metric": "moe_layer_tokens_per_s", "value": value, "unit": "tokens/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
@@ -880,7 +900,7 @@ def main():
             "layer_hbm_gbs": layer_bytes / (ms / args.steps / 1e3) / 1e9,
             "down_gbs": dn_bytes / (dn.get("ms_per_launch", float("nan")) / 1e3) / 1e9,
             "touched_experts": touched, "held_experts": [eb, ec], "kernels": kern,
-            "matvec_c0": matvec, "configs": configs,
+            "per_rank": per_rank, "matvec_c0": matvec, "configs": configs,
             "gpu_launches": sum(v["launches"] for v in kern.values()),
             "clocks": clk.summary()}
 
