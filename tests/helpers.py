@@ -65,3 +65,22 @@ def memory_state(device: int):
     err, free, _ = rt.cudaMemGetInfo()
     assert err == rt.cudaError_t.cudaSuccess
     return int(used), int(reserved), int(free)
+
+
+def profiled_kinds(ctx, fn):
+    """Runs fn() with the library's per-launch profiler on; the kernel kinds it launched."""
+    import ctypes
+    from urbilateria_b200 import native
+    ctx.lib.urb_profile_reset(ctx.h)
+    ctx.lib.urb_profile_enable(ctx.h, 1)
+    try:
+        fn()
+    finally:
+        ctx.lib.urb_profile_enable(ctx.h, 0)
+    kinds = {}
+    for k, name in enumerate(native.KERNEL_NAMES):
+        t, n = ctypes.c_double(), ctypes.c_int64()
+        ctx.lib.urb_profile_read(ctx.h, k, ctypes.byref(t), ctypes.byref(n))
+        if n.value:
+            kinds[name] = n.value
+    return kinds

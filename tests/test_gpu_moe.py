@@ -7,7 +7,7 @@ import pytest
 import urbilateria_b200 as urb
 from urbilateria_b200 import synthetic as syn
 
-from helpers import assert_close, bf16_pair, mxfp4_pair, mxfp8_pair
+from helpers import assert_close, bf16_pair, mxfp4_pair, mxfp8_pair, profiled_kinds
 
 pytestmark = pytest.mark.gpu
 
@@ -38,7 +38,7 @@ def test_mxfp8_swiglu(oracle, ctx):
 
 def build_layer(oracle, ctx, g, hidden, inter, experts, fmt="mxfp4", top_k=8, n_group=1,
                 topk_group=1, scale=2.5):
-    pair = mxfp4_pair if fmt == "mxfp4" else mxfp8_pair
+    pair = {"mxfp4": mxfp4_pair, "mxfp8": mxfp8_pair, "bf16": bf16_pair}[fmt]
     dev_e, orc_g, orc_u, orc_d = [], [], [], []
     for _ in range(experts):
         gd, go = pair(oracle, ctx, g, inter, hidden)
@@ -58,7 +58,8 @@ def build_layer(oracle, ctx, g, hidden, inter, experts, fmt="mxfp4", top_k=8, n_
     return dev, orc
 
 
-@pytest.mark.parametrize("fmt,tokens", [("mxfp4", 1), ("mxfp4", 24), ("mxfp8", 17)])
+@pytest.mark.parametrize("fmt,tokens", [("mxfp4", 1), ("mxfp4", 24), ("mxfp8", 17), ("bf16", 1),
+                                        ("bf16", 37)])
 def test_moe_layer_reduced(oracle, ctx, fmt, tokens):
     g = syn.rng(300 + tokens)
     dev, orc = build_layer(oracle, ctx, g, 512, 256, 32, fmt)
@@ -106,15 +107,31 @@ def test_moe_rejects_nonfinite_input(oracle, ctx):
     assert e.value.kind == "NonFinite"
 
 
+@pytest.mark.parametrize("fmt", ["mxfp4", "bf16"])
 @pytest.mark.parametrize("path", ["tc", "mma"])
-def test_both_grouped_paths_many_tokens(oracle, ctx, path, monkeypatch):
+def test_both_grouped_paths_many_tokens(oracle, ctx, path, fmt, monkeypatch):
     # 160 tokens of f32 (not bf16-exact) activations: hi/lo columns, two shared-expert chunks,
-    # experts with >64 routed tokens on the tcgen05 path.
+    # experts with >64 routed tokens on the tcgen05 path (BF16: three BF16 terms per value).
     monkeypatch.setenv("URB_MOE_PATH", path)
     g = syn.rng(500)
-    dev, orc = build_layer(oracle, ctx, g, 256, 256, 8, "mxfp4", top_k=4, scale=1.0)
+    dev, orc = build_layer(oracle, ctx, g, 256, 256, 8, fmt, top_k=4, scale=1.0)
     x = syn.normal_f32(g, (160, 256))
     out, ids, w, _ = dev.forward_batch(x, 160)
     o_out, o_ids, o_w, _, _ = orc.forward(x)
+    assert np.array_equal(ids, o_ids)
+    assert_close(out, o_out)
+
+
+def test_bf16_layer_runs_the_tensor_core_passes(oracle, ctx):
+    # BF16 experts take the tcgen05 kind::f16 passes (tiles through the TMA tensor map): the
+    # layer runs the activation-term prep and no mma.sync row shift.
+    g = syn.rng(510)
+    dev, orc = build_layer(oracle, ctx, g, 256, 128, 16, "bf16", top_k=4, scale=1.0)
+    x = syn.normal_f32(g, (12, 256))
+    res = {}
+    kinds = profiled_kinds(ctx, lambda: res.update(r=dev.forward_batch(x, 12)))
+    assert "prep" in kinds and "row_shift" not in kinds, kinds
+    out, ids, w, _ = res["r"]
+    o_out, o_ids, _, _, _ = orc.forward(x)
     assert np.array_equal(ids, o_ids)
     assert_close(out, o_out)

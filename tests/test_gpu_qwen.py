@@ -140,3 +140,50 @@ def test_qwen36_rejects_nonfinite_router(oracle, ctx):
     with pytest.raises(urb.UrbError) as e:
         dev.forward_ex(x, 2, numerics="qwen36")
     assert e.value.kind == "NonFinite"
+
+
+def test_qwen36_bf16_layer_records_into_a_cuda_graph(oracle):
+    # BF16 experts run the tcgen05 kind::f16 passes, whose device forward makes no host copy or
+    # synchronisation: with caller routes it records into a CUDA graph (after one call has
+    # sized the context's workspace) and the replay reproduces the eager output bit for bit.
+    import ctypes
+    import torch
+    from urbilateria_b200 import native
+    c = urb.Context(0)
+    stream = torch.cuda.Stream()
+    c.set_stream(stream.cuda_stream)
+    g = syn.rng(9800)
+    hidden, inter, experts, k, tokens = 256, 128, 16, 4, 11
+    dev, orc, gate_o = build_qwen_layer(oracle, c, g, hidden, inter, experts, "bf16", k)
+    x = syn.normal_f32(g, (tokens, hidden))
+    o_out, o_ids, o_w = oracle.moe_qwen_layer_forward(orc, gate_o, x)
+    want = dev.forward_routed(x, tokens, o_ids, o_w, numerics="qwen36")
+    assert_close(want, o_out)
+    d_x = torch.from_numpy(np.ascontiguousarray(x, np.float32)).cuda()
+    d_ids = torch.from_numpy(np.ascontiguousarray(o_ids, np.int32)).cuda()
+    d_w = torch.from_numpy(np.ascontiguousarray(o_w, np.float32)).cuda()
+    d_out = torch.zeros_like(d_x)
+    st = torch.zeros(1, dtype=torch.int32, device="cuda")
+    num = native.Numerics(2, 0.0)
+
+    def call():
+        c.check(c.lib.urb_moe_forward_routed_ex_device(c.h, dev.h, d_x.data_ptr(), tokens,
+                                                       d_ids.data_ptr(), d_w.data_ptr(),
+                                                       ctypes.byref(num), d_out.data_ptr(),
+                                                       st.data_ptr()))
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        call()
+    stream.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        call()
+    d_out.zero_()
+    torch.cuda.synchronize()
+    graph.replay()
+    torch.cuda.synchronize()
+    assert int(st.item()) == 0
+    assert np.array_equal(bits(d_out.cpu().numpy()), bits(want))
+    del graph
+    dev.free()
+    c.close()  # objects still holding this context drop their handles (Matrix.free)

@@ -179,9 +179,11 @@ class _Matrix:
                                                            d_status or None))
 
     def free(self):
-        if self.h:
+        # A closed context has already ended every call on its objects; freeing through it
+        # would touch released state, so the handle is dropped instead.
+        if self.h and self.ctx.h:
             self.ctx.lib.urb_mat_free(self.h)
-            self.h = None
+        self.h = None
 
     def __del__(self):
         try:
@@ -629,9 +631,9 @@ class RuntimeMoeLayer:
             d_status or None))
 
     def free(self):
-        if getattr(self, "h", None):
+        if getattr(self, "h", None) and self.ctx.h:  # see Matrix.free
             self.ctx.lib.urb_moe_layer_free(self.h)
-            self.h = None
+        self.h = None
 
     def __del__(self):
         try:

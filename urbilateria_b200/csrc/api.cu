@@ -537,6 +537,7 @@ int urb_mat_free(urb_mat *m) {
     }
     if (m->tiles) cudaFree(m->tiles);
     if (m->tc_tiles) cudaFree(m->tc_tiles);
+    if (m->tc_map) cudaFree(m->tc_map);
     if (m->row_exp) cudaFree(m->row_exp);
     if (m->raw_values) cudaFree(m->raw_values);
     if (m->raw_scales) cudaFree(m->raw_scales);

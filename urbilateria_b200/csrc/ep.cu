@@ -304,9 +304,9 @@ int ep_forward_device(Ep *ep, const float *d_x, int T, float *d_out, int32_t *d_
     bb.shared_tokens = T;
     bb.pair_down = 1;
     if (shared) {
-        bb.sh_gate_tc = L->sg->tc_tiles;
-        bb.sh_up_tc = L->su->tc_tiles;
-        bb.sh_down_tc = L->sd->tc_tiles;
+        bb.sh_gate_tc = tc_src(L->sg);
+        bb.sh_up_tc = tc_src(L->su);
+        bb.sh_down_tc = tc_src(L->sd);
     }
     bb.hidden = int(H);
     bb.inter = int(I);

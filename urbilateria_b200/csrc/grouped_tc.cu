@@ -7,6 +7,10 @@
 // No CUDA-core dequantisation remains on the weight stream, so the pass runs at the rate HBM
 // delivers tiles.
 //
+// BF16 weights (kind::f16) are not repacked: each 128-row x 64-column tile is a 2-D tiled TMA
+// copy from the row-major matrix through its tensor map, landing in the same 128-byte swizzled
+// K-major layout; they carry no scales.
+//
 // Activations are represented in the weights' element format by residual terms (k_bs_prep):
 // per 32-column block, term j takes the E8M0 scale that fits the residual's largest magnitude
 // into the element range (6 for E2M1, 448 for E4M3), rounds to nearest, and passes the
@@ -173,6 +177,7 @@ __global__ void __launch_bounds__(kThreadsBs, 1) k_bs_grouped(TcArgs a) {
     constexpr int TB = bs_tile_bytes(FMT);
     constexpr int CH = bs_sf_chunks(FMT);
     constexpr int KIND_FMT = FMT == URB_FMT_MXFP4 ? 1 : 0;
+    constexpr bool BF = FMT == URB_FMT_BF16;  // kind::f16, tiles through the tensor map, no scales
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t *ring_a = smem;
@@ -226,9 +231,11 @@ __global__ void __launch_bounds__(kThreadsBs, 1) k_bs_grouped(TcArgs a) {
         for (UnitCursor uc(a, total_units); uc.valid() && !*abortp; uc.advance()) {
             const TcSeg &S = uc.cur;
             const Unit x = unit_of<FMT, TPU>(S, uc.u);
-            const uint8_t *wsrc = S.w + size_t(x.mt) * TB;  // tile (mt, ks) at (ks * mts + mt)
-            const uint8_t *wsrc2 = GU ? S.w2 + size_t(x.mt) * TB
-                                      : (MT ? S.w + size_t(x.mt + 1) * TB : nullptr);
+            // MX: tile (mt, ks) at (ks * mts + mt) of the resident tiles.  BF16: box (column
+            // 64 ks, row 128 mt) of the tensor map (S.w / S.w2 point at the maps).
+            const uint8_t *wsrc = BF ? S.w : S.w + size_t(x.mt) * TB;
+            const uint8_t *wsrc2 = GU ? (BF ? S.w2 : S.w2 + size_t(x.mt) * TB)
+                                      : (MT ? (BF ? S.w : S.w + size_t(x.mt + 1) * TB) : nullptr);
             const bool second = !MT || x.mt + 1 < S.mts;  // the unit's second tile exists
             bool ok = true;
             for (int ks = 0; ks < S.ks && ok; ++ks) {
@@ -245,8 +252,12 @@ __global__ void __launch_bounds__(kThreadsBs, 1) k_bs_grouped(TcArgs a) {
                         continue;
                     }
                     tc::mbar_arrive_expect_tx(&a_full[sa], uint32_t(TB));
-                    tc::bulk_g2s(ring_a + size_t(sa) * kStage,
-                                 (i ? wsrc2 : wsrc) + size_t(ks) * S.mts * TB, TB, &a_full[sa]);
+                    if constexpr (BF)
+                        tc::tma_load_2d(ring_a + size_t(sa) * kStage, i ? wsrc2 : wsrc,
+                                        ks * bs_stage_cols(FMT), (x.mt + (MT ? i : 0)) * 128, &a_full[sa]);
+                    else
+                        tc::bulk_g2s(ring_a + size_t(sa) * kStage,
+                                     (i ? wsrc2 : wsrc) + size_t(ks) * S.mts * TB, TB, &a_full[sa]);
                 }
             }
             if (!ok) { fail(); break; }
@@ -319,6 +330,11 @@ __global__ void __launch_bounds__(kThreadsBs, 1) k_bs_grouped(TcArgs a) {
                     ok = false;
                     break;
                 }
+                if constexpr (BF) {  // no scales: only tell the issuers that the stage landed
+                    __syncwarp();
+                    if (lane == 0) tc::mbar_arrive(&sf_full[sa]);
+                    continue;
+                }
                 // Slot sa: A's scales at +0 / +4, B's at +8 / +12; PAIR: the up tile's A scales
                 // in its own slot sa1 (+0 / +4).
                 const uint8_t *sfa = ring_a + size_t(sa) * kStage + 16384 + 16 * lane;
@@ -386,7 +402,9 @@ __global__ void __launch_bounds__(kThreadsBs, 1) k_bs_grouped(TcArgs a) {
                 for (int k2 = 0; k2 < kSteps && !idle; ++k2) {
                     const int kk = PAIR ? k2 : me * kStepsPerIssuer + k2;
                     const bool accum = ks > 0 || k2 > 0;
-                    if (FMT == URB_FMT_MXFP4) {
+                    if constexpr (BF) {
+                        tc::mma_bf16(acc, adesc + 2 * kk, bdesc + 2 * kk, tc::idesc_bf16(x.n), accum);
+                    } else if (FMT == URB_FMT_MXFP4) {
                         const uint32_t id = 2u * (kk & 1), col = 4u * (kk >> 1);
                         tc::mma_mxf4(acc, adesc + 2 * kk, bdesc + 2 * kk, tc::idesc_bs(KIND_FMT, x.n, id, id),
                                      (sfa + col) | (id << 30), (sfb + col) | (id << 30), accum);
@@ -545,10 +563,30 @@ __global__ void __launch_bounds__(kThreadsBs, 1) k_bs_grouped(TcArgs a) {
 // sub-segment (payload 128-byte swizzled, scale bytes in the tcgen05.cp chunk layout).  MMA rows
 // past a token's terms and slots past a sub-segment's tokens are never read by the epilogue
 // and stay unwritten.
+// BF16 (round to nearest even) of a finite f32, as the 16 high bits of its pattern.
+__device__ __forceinline__ uint32_t bf16_bits_rn(float v) {
+    const uint32_t u = __float_as_uint(v);
+    return (u + 0x7FFFu + ((u >> 16) & 1u)) >> 16;
+}
+
+// One BF16 residual term of a lane's 8 values: q receives the 8 BF16 codes (element 0 in the
+// low half of word 0) and r the exact remainder.  Three terms reproduce an f32 exactly.
+__device__ __forceinline__ void make_term8_bf16(float *r, uint32_t *q) {
+#pragma unroll
+    for (int i = 0; i < 8; i += 2) {
+        const uint32_t b0 = bf16_bits_rn(r[i]), b1 = bf16_bits_rn(r[i + 1]);
+        r[i] -= __uint_as_float(b0 << 16);
+        r[i + 1] -= __uint_as_float(b1 << 16);
+        q[i >> 1] = b0 | (b1 << 16);
+    }
+}
+
 template <int FMT, int NT>
 __global__ void __launch_bounds__(256) k_bs_prep(TcArgs a) {
-    constexpr int KBS = FMT == URB_FMT_MXFP4 ? 8 : 4;  // 32-column blocks per stage
-    constexpr int QW = FMT == URB_FMT_MXFP4 ? 1 : 2;   // code words per lane per term
+    constexpr bool BF = FMT == URB_FMT_BF16;
+    // 32-column blocks per stage; code words per lane per term.
+    constexpr int KBS = FMT == URB_FMT_MXFP4 ? 8 : (FMT == URB_FMT_MXFP8 ? 4 : 2);
+    constexpr int QW = FMT == URB_FMT_MXFP4 ? 1 : (FMT == URB_FMT_MXFP8 ? 2 : 4);
     constexpr int RT = bs_rows_per_tok(FMT), TT = NT;
     __shared__ int skip;
     if (threadIdx.x == 0) skip = (a.status && *a.status) ? 1 : 0;
@@ -621,7 +659,14 @@ __global__ void __launch_bounds__(256) k_bs_prep(TcArgs a) {
     uint32_t q[TT][QW];
     int sb[TT];
 #pragma unroll
-    for (int t = 0; t < TT; ++t) sb[t] = make_term8<FMT>(r, q[t]);
+    for (int t = 0; t < TT; ++t) {
+        if constexpr (BF) {
+            make_term8_bf16(r, q[t]);
+            sb[t] = 0;
+        } else {
+            sb[t] = make_term8<FMT>(r, q[t]);
+        }
+    }
     if (!valid) return;
     const int ks = kb / KBS, kbs = kb % KBS;
     const int ndst = a.inv ? a.top_k + (shared_dst ? 1 : 0) : 1;
@@ -636,7 +681,13 @@ __global__ void __launch_bounds__(256) k_bs_prep(TcArgs a) {
         for (int t = 0; t < TT; ++t) {
             const int R = S.slot * RT + t;  // MMA row within the stage
             uint8_t *rowp = stage + (R >> 3) * 1024 + (R & 7) * 128;
-            if (FMT == URB_FMT_MXFP4) {
+            if constexpr (BF) {
+                // The lane's 8 columns are one 16-byte chunk of the 128-byte row.
+                const int ch = 4 * kbs + part;
+                *reinterpret_cast<uint4 *>(rowp + ((ch ^ (R & 7)) << 4)) =
+                    make_uint4(q[t][0], q[t][1 % QW], q[t][2 % QW], q[t][3 % QW]);
+                continue;
+            } else if (FMT == URB_FMT_MXFP4) {
                 *reinterpret_cast<uint32_t *>(rowp + ((kbs ^ (R & 7)) << 4) + 4 * part) = q[t][0];
             } else {
                 const int ch = 2 * kbs + (part >> 1);
@@ -700,7 +751,7 @@ __global__ void k_repack_bs(const uint8_t *values, const uint8_t *scales, size_t
 template <int FMT, int NT>
 int launch_bs_t(Ctx *ctx, const TcArgs &a, int kind, cudaStream_t st) {
     static_assert(NT <= bs_rows_per_tok(FMT), "terms fit in a token's MMA rows");
-    constexpr int KBS = FMT == URB_FMT_MXFP4 ? 8 : 4;
+    constexpr int KBS = FMT == URB_FMT_MXFP4 ? 8 : (FMT == URB_FMT_MXFP8 ? 4 : 2);
     const long long threads = (long long)a.nrows * a.ks * KBS * 4;
     if (threads > 0) {
         prof_begin(ctx, URB_K_PREP, st);
@@ -725,6 +776,10 @@ int launch_tc_grouped(Ctx *ctx, int fmt, const TcArgs &a, int kind, cudaStream_t
         return launch_bs_t<URB_FMT_MXFP4, bs_rows_per_tok(URB_FMT_MXFP4)>(ctx, a, kind, st);
     if (fmt == URB_FMT_MXFP4) return launch_bs_t<URB_FMT_MXFP4, bs_terms(URB_FMT_MXFP4)>(ctx, a, kind, st);
     if (fmt == URB_FMT_MXFP8) return launch_bs_t<URB_FMT_MXFP8, bs_terms(URB_FMT_MXFP8)>(ctx, a, kind, st);
+    if (fmt == URB_FMT_BF16) {
+        if (a.sim128) return set_error(ctx, URB_ERR_UNSUPPORTED, "tc pass: BF16 takes no E4M3 simulation");
+        return launch_bs_t<URB_FMT_BF16, bs_terms(URB_FMT_BF16)>(ctx, a, kind, st);
+    }
     return set_error(ctx, URB_ERR_UNSUPPORTED, "tc pass: format");
 }
 

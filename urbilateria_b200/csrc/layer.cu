@@ -115,7 +115,7 @@ int moe_forward_device(Layer *L, const float *d_x, int T, float *d_out, MoeWork 
                          "DeepSeek-V4 numerics run on the tensor-core passes with caller routes");
     if (qwen) {
         // Qwen3.6: MX experts need the E4M3 simulation of the tensor-core prep; BF16 experts
-        // run on the mma.sync passes.
+        // run on the tensor-core passes too, or on the mma.sync passes (URB_MOE_PATH=mma).
         if (!d_ids_in || !L->sg || !L->shared_gate_row)
             return set_error(ctx, URB_ERR_UNSUPPORTED,
                              "Qwen3.6 numerics need caller routes, a shared expert and its gate");
@@ -251,9 +251,9 @@ int moe_forward_device(Layer *L, const float *d_x, int T, float *d_out, MoeWork 
         bb.shared_tokens = T;
         bb.pair_down = 1;
         if (L->sg) {
-            bb.sh_gate_tc = L->sg->tc_tiles;
-            bb.sh_up_tc = L->su->tc_tiles;
-            bb.sh_down_tc = L->sd->tc_tiles;
+            bb.sh_gate_tc = tc_src(L->sg);
+            bb.sh_up_tc = tc_src(L->su);
+            bb.sh_down_tc = tc_src(L->sd);
         }
         bb.hidden = int(H);
         bb.inter = int(I);
@@ -290,14 +290,17 @@ int moe_forward_device(Layer *L, const float *d_x, int T, float *d_out, MoeWork 
         ga.shared_rows = T;
         ga.slots = w.bslots_gu;
         ga.pair = 1;  // gate and up tiles of an expert together; the epilogue writes h
+        // MX weights see the checkpoint's E4M3 activation simulation; BF16 weights see the
+        // activations as they are (qwen3_8/math.rs:10-26).
+        const bool mx = L->fmt != URB_FMT_BF16;
         if (deepseek) {
             ga.variant = 1;
-            ga.sim128 = 1;
+            ga.sim128 = mx ? 1 : 0;
             ga.limit = num->limit;
             ga.col_w = w.col_w;
         } else if (qwen) {
             ga.variant = 2;
-            ga.sim128 = 2;
+            ga.sim128 = mx ? 2 : 0;
             ga.full_terms = 1;
             ga.expf = expf_table_of(ctx);
         }
@@ -320,7 +323,7 @@ int moe_forward_device(Layer *L, const float *d_x, int T, float *d_out, MoeWork 
         da.pair = 2;  // neighbouring row tiles share each activation stage
         if (deepseek || qwen) {
             da.variant = deepseek ? 1 : 2;
-            da.sim128 = deepseek ? 1 : 2;
+            da.sim128 = !mx ? 0 : (deepseek ? 1 : 2);
             da.full_terms = qwen ? 1 : 0;
         }
         da.cols = int(I);
@@ -681,21 +684,23 @@ static int create_layer(urb_ctx *ctx, const urb_mat *router, const float *bias, 
         int rc = check_mlp(sg, su, sd);
         if (rc) return set_error(ctx, rc, "shared expert shape/format is not supported");
     }
-    // MX experts with tcgen05 tiles take the tensor-core passes whatever their scale range.
+    // MX experts with tcgen05 tiles take the tensor-core passes whatever their scale range; BF16
+    // experts take them (kind::f16) through their tensor maps.
     auto tc_mlp = [&](const urb_mat *g, const urb_mat *u, const urb_mat *d) {
-        return (fmt == URB_FMT_MXFP4 || fmt == URB_FMT_MXFP8) && g->format == fmt &&
-               u->format == fmt && d->format == fmt && g->tc_tiles && u->tc_tiles && d->tc_tiles;
+        return (fmt == URB_FMT_MXFP4 || fmt == URB_FMT_MXFP8 || fmt == URB_FMT_BF16) &&
+               g->format == fmt && u->format == fmt && d->format == fmt && tc_src(g) && tc_src(u) &&
+               tc_src(d);
     };
     bool generic = false;
     for (size_t e = 0; e < e_count; ++e)
         generic |= !(tiled_mlp(gate[e], up[e], down[e]) || tc_mlp(gate[e], up[e], down[e]));
     if (have_shared) generic |= !(tiled_mlp(sg, su, sd) || tc_mlp(sg, su, sd));
     const char *path = std::getenv("URB_MOE_PATH");
-    bool have_tc = !generic && (fmt == URB_FMT_MXFP4 || fmt == URB_FMT_MXFP8);
+    bool have_tc = !generic && (fmt == URB_FMT_MXFP4 || fmt == URB_FMT_MXFP8 || fmt == URB_FMT_BF16);
     for (size_t e = 0; e < e_count && have_tc; ++e) have_tc = tc_mlp(gate[e], up[e], down[e]);
     if (have_shared) have_tc = have_tc && tc_mlp(sg, su, sd);
-    // Block-scaled tcgen05 passes by default; URB_MOE_PATH=mma selects the mma.sync passes,
-    // which need every expert in that layout (MX experts build it now from their tcgen05 tiles).
+    // tcgen05 passes by default; URB_MOE_PATH=mma selects the mma.sync passes, which need every
+    // expert in that layout (MX experts build it now from their tcgen05 tiles).
     const bool use_tc = have_tc && !(path && std::strcmp(path, "mma") == 0);
     if (!use_tc && !generic) {
         for (size_t e = 0; e < e_count; ++e) generic |= !tiled_mlp(gate[e], up[e], down[e]);
@@ -740,16 +745,17 @@ static int create_layer(urb_ctx *ctx, const urb_mat *router, const float *bias, 
         tables[3 * S + e] = g->row_exp;
         tables[4 * S + e] = u->row_exp;
         tables[5 * S + e] = d->row_exp;
-        tables[6 * S + e] = g->tc_tiles;
-        tables[7 * S + e] = u->tc_tiles;
-        tables[8 * S + e] = d->tc_tiles;
+        tables[6 * S + e] = const_cast<uint8_t *>(tc_src(g));
+        tables[7 * S + e] = const_cast<uint8_t *>(tc_src(u));
+        tables[8 * S + e] = const_cast<uint8_t *>(tc_src(d));
     };
     for (size_t e = 0; e < e_count; ++e) put(e, gate[e], up[e], down[e]);
     if (have_shared) put(e_count, sg, su, sd);
     L->use_tc = use_tc && !generic;
     if (e_count != experts && !have_tc) {
         delete L;
-        return set_error(ctx, URB_ERR_UNSUPPORTED, "expert shards need MX experts (tensor-core passes)");
+        return set_error(ctx, URB_ERR_UNSUPPORTED,
+                         "expert shards need experts the tensor-core passes take (MX, or BF16 with cols % 8 == 0)");
     }
     cudaError_t err = cudaMalloc(&L->d_tables, tables.size() * sizeof(void *));
     if (err == cudaSuccess)

@@ -1,7 +1,8 @@
 // tc_common.cuh — thin PTX wrappers for the sm_100a asynchronous machinery used by the
-// tensor-core grouped pass: mbarriers, 1-D bulk copies (TMA engine, no tensor map), tcgen05
-// TMEM allocation / load / store, block-scaled tcgen05.mma (both operands from shared-memory
-// descriptors, scales in TMEM) and tcgen05.commit.  Every wait is bounded: it gives up after a fixed number of
+// tensor-core passes: mbarriers, 1-D bulk copies and 2-D tiled tensor copies (TMA engine; no
+// multicast anywhere), tcgen05 TMEM allocation / load / store, block-scaled and BF16
+// tcgen05.mma (both operands from shared-memory descriptors, scales in TMEM) and
+// tcgen05.commit.  Every wait is bounded: it gives up after a fixed number of
 // polls and reports failure, so a protocol error surfaces as URB_ERR_TIMEOUT, not a hang.
 #pragma once
 #include <stdint.h>
@@ -60,6 +61,18 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
     asm volatile(
         "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
         ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// 2-D tiled tensor copy global -> shared (TMA) of the box of the tensor map at `map` (a
+// CUtensorMap in global memory) whose first element is column x, row y, completing on `bar`.
+// The box lands in the map's swizzled layout; columns / rows past the tensor read as zero.
+// x * element size must be a multiple of 16 bytes.
+__device__ __forceinline__ void tma_load_2d(void *dst, const void *map, int x, int y, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], "
+        "[%1, {%2, %3}], [%4];"
+        ::"r"(smem_u32(dst)), "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
         : "memory");
 }
 
@@ -177,6 +190,23 @@ __device__ __forceinline__ void mma_mxf8(uint32_t d, uint64_t a, uint64_t b, uin
         "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n\t}"
         ::"r"(d), "l"(a), "l"(b), "r"(idesc), "r"(uint32_t(acc)), "r"(sfa), "r"(sfb)
+        : "memory");
+}
+
+// ---- BF16 MMA ----------------------------------------------------------------------------
+
+// Instruction descriptor of a dense kind::f16 MMA with BF16 A and B (both K-major), f32
+// accumulator, M = 128, N = n (a multiple of 16, at most 256).
+__host__ __device__ constexpr uint32_t idesc_bf16(int n) {
+    return (1u << 4) | (1u << 7) | (1u << 10) | (uint32_t(n >> 3) << 17) | (uint32_t(128 >> 4) << 24);
+}
+
+// D (+)= A x B, BF16 operands, K = 16.
+__device__ __forceinline__ void mma_bf16(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, bool acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+        ::"r"(d), "l"(a), "l"(b), "r"(idesc), "r"(uint32_t(acc))
         : "memory");
 }
 

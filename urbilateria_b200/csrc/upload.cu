@@ -1,5 +1,7 @@
 // upload.cu — device residency for weight matrices: payload validation (the checks of the
 // reference constructors) and the repack into the tiled layout described in urb_internal.cuh.
+#include <cuda.h>
+
 #include <mutex>
 
 #include "urb_internal.cuh"
@@ -164,6 +166,48 @@ size_t div_ceil(size_t a, size_t b) { return (a + b - 1) / b; }
 
 std::mutex g_mma_tiles_mu;
 
+// cuTensorMapEncodeTiled from the driver, resolved once through the runtime.
+using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
+                                   const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
+                                   const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiledFn encode_tiled() {
+    static const EncodeTiledFn fn = [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) !=
+                cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            p = nullptr;
+        return reinterpret_cast<EncodeTiledFn>(p);
+    }();
+    return fn;
+}
+
+// The BF16 matrix's tensor map for the grouped tcgen05 passes: 2-D [rows, cols] bf16 over the
+// row-major copy, boxes of 64 columns (128 bytes, the swizzle span) x 128 rows, 128-byte
+// swizzle (the canonical K-major layout the MMA descriptors name), zero fill past the edges.
+// The row pitch must be a multiple of 16 bytes (cols % 8 == 0); other shapes keep no map.
+int make_bf16_tile_map(Ctx *ctx, Mat *m, cudaStream_t st) {
+    if (m->cols % 8 != 0 || m->rows == 0 || m->cols == 0) return URB_OK;
+    const EncodeTiledFn enc = encode_tiled();
+    if (!enc) return URB_OK;
+    CUtensorMap map;
+    const cuuint64_t dims[2] = {cuuint64_t(m->cols), cuuint64_t(m->rows)};
+    const cuuint64_t strides[1] = {cuuint64_t(m->cols) * 2};
+    const cuuint32_t box[2] = {64, 128};
+    const cuuint32_t elem[2] = {1, 1};
+    if (enc(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, m->raw_values, dims, strides, box, elem,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return URB_OK;
+    URB_CUDA(ctx, cudaMallocAsync(&m->tc_map, sizeof(CUtensorMap), st));
+    URB_CUDA(ctx, cudaMemcpyAsync(m->tc_map, &map, sizeof(CUtensorMap), cudaMemcpyHostToDevice, st));
+    m->tc_mts = int(div_ceil(m->rows, 128));
+    m->tc_ks = int(div_ceil(m->cols, size_t(bs_stage_cols(URB_FMT_BF16))));
+    return URB_OK;
+}
+
 }  // namespace
 
 int ensure_mma_tiles(Ctx *ctx, const Mat *cm, cudaStream_t st) {
@@ -305,6 +349,10 @@ int upload_matrix(Ctx *ctx, Mat *m, const void *values, const uint8_t *scales) {
         URB_CUDA(ctx, cudaGetLastError());
         // BF16 keeps its row-major copy as well: the bit-exact router reads whole rows in
         // column order.
+    }
+    if (m->format == URB_FMT_BF16) {
+        int rc = make_bf16_tile_map(ctx, m, st);
+        if (rc) return rc;
     }
     if (mx && m->tc_tiles) {
         // The tcgen05 tiles hold every weight and scale: the reference layout goes.

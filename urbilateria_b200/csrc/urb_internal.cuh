@@ -52,13 +52,23 @@ struct Mat {
     int rbs = 0, kslices = 0;
     uint8_t *tiles = nullptr;
     int8_t *row_exp = nullptr;  // [rbs*16]
-    // Tensor-core (tcgen05) layout of MX matrices: 128x64 tiles.
+    // Tensor-core (tcgen05) layout of MX matrices: 128-row x 128-byte tiles with their
+    // scales, K-stage major (tc_mts row tiles x tc_ks K stages).
     uint8_t *tc_tiles = nullptr;
+    // BF16 matrices (cols a multiple of 8): a TMA tensor map (CUtensorMap in device memory)
+    // over the row-major copy, boxes of 128 rows x 64 columns in the 128-byte swizzle.
+    void *tc_map = nullptr;
     int tc_mts = 0, tc_ks = 0;
     // Generic path: the reference layout on the device (used when !tiled).
     void *raw_values = nullptr;
     uint8_t *raw_scales = nullptr;
 };
+
+// What the grouped tensor-core passes read a matrix's tiles from: MX matrices' resident tiles,
+// BF16 matrices' tensor map (null when the matrix cannot take the passes).
+inline const uint8_t *tc_src(const Mat *m) {
+    return m->format == URB_FMT_BF16 ? static_cast<const uint8_t *>(m->tc_map) : m->tc_tiles;
+}
 
 // One unit of grouped work: a matrix (or a gate/up pair) applied to a contiguous run of
 // columns of the activation list.

@@ -5,6 +5,9 @@
 // columns.  Activations are written as residual terms in the same element format (x ~= t0 +
 // t1 + ..., each term with its own E8M0 scale per 32 columns): 6 E2M1 terms in 8 MMA rows per
 // token for MXFP4, 4 E4M3 terms in 4 rows for MXFP8; the epilogue sums a token's terms.
+// BF16 weights run kind::f16 (BF16 x BF16): their 128 x 64 tiles come straight from the
+// row-major matrix through a TMA tensor map (128-byte swizzle), and an f32 activation is
+// three BF16 terms (hi, mid, lo; their sum is the f32 value exactly) in 4 MMA rows.
 #pragma once
 #include "urb_internal.cuh"
 
@@ -15,15 +18,21 @@ constexpr int kBsIssuers = 2;  // MMA issuing threads of the grouped kernel, one
 constexpr int kBsNmax = kBsIssuers == 2 ? 128 : 96;
 // MMA rows per token, residual terms per token, tokens per sub-segment.
 __host__ __device__ constexpr int bs_rows_per_tok(int fmt) { return fmt == URB_FMT_MXFP4 ? 8 : 4; }
-__host__ __device__ constexpr int bs_terms(int fmt) { return fmt == URB_FMT_MXFP4 ? 6 : 4; }
+__host__ __device__ constexpr int bs_terms(int fmt) {
+    return fmt == URB_FMT_MXFP4 ? 6 : (fmt == URB_FMT_MXFP8 ? 4 : 3);
+}
 __host__ __device__ constexpr int bs_cap(int fmt) { return kBsNmax / bs_rows_per_tok(fmt); }
 
 // Bytes of one 128-row x 128-byte tile of the bs layout: payload (128-byte swizzled K-major)
 // followed by the scale chunks (512 B each, 4 scale columns of 128 rows).
-__host__ __device__ constexpr int bs_sf_chunks(int fmt) { return fmt == URB_FMT_MXFP4 ? 2 : 1; }
+__host__ __device__ constexpr int bs_sf_chunks(int fmt) {
+    return fmt == URB_FMT_MXFP4 ? 2 : (fmt == URB_FMT_MXFP8 ? 1 : 0);
+}
 __host__ __device__ constexpr int bs_tile_bytes(int fmt) { return 16384 + 512 * bs_sf_chunks(fmt); }
 // Input columns per K stage (one 128-byte row of payload).
-__host__ __device__ constexpr int bs_stage_cols(int fmt) { return fmt == URB_FMT_MXFP4 ? 256 : 128; }
+__host__ __device__ constexpr int bs_stage_cols(int fmt) {
+    return fmt == URB_FMT_MXFP4 ? 256 : (fmt == URB_FMT_MXFP8 ? 128 : 64);
+}
 // Bytes of one activation stage of n MMA rows (n <= kBsNmax): payload then scale chunks.
 __host__ __device__ constexpr int bs_bstage_bytes(int fmt, int n) { return n * 128 + 512 * bs_sf_chunks(fmt); }
 
@@ -31,8 +40,9 @@ __host__ __device__ constexpr int bs_bstage_bytes(int fmt, int n) { return n * 1
 // (128-row tile mt, sub-segment j) pairs, j fastest, so the sub-segments of a large group read
 // the same weight tile back to back (the second read is served by L2).
 struct TcSeg {
-    const uint8_t *w;     // bs tiles of the matrix (gate/up pass: the gate projection)
-    const uint8_t *w2;    // gate/up pass: bs tiles of the up projection (nullptr otherwise)
+    const uint8_t *w;     // bs tiles of the matrix (gate/up pass: the gate projection); BF16:
+                          // the matrix's tensor map (tc_src)
+    const uint8_t *w2;    // gate/up pass: bs tiles (BF16: tensor map) of the up projection
     long long b_off;      // byte offset of the group's activation stages in the B buffer
     int mts, ks;          // 128-row tiles, K stages
     int rows, cols;       // real rows / input columns

@@ -107,9 +107,9 @@ class ExpertParallelMoeLayer:
             d_status))
 
     def free(self):
-        if getattr(self, "h", None):
+        if getattr(self, "h", None) and self.ctx.h:  # a closed context: drop the handle
             self.ctx.lib.urb_ep_free(self.h)
-            self.h = None
+        self.h = None
 
     def __del__(self):
         try:
