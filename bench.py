@@ -302,17 +302,10 @@ def kernel_ms(ctx, native, fn, reps):
     return total / reps, e0.elapsed_time(e1) / reps, launches // reps
 
 
-def bench_configs(urb, native, ctx, local, pk_hbm):
-    """Configs 1, 3 and 4 of the benchmark set, each timed on this GPU with the library's own
-    device API (inputs resident), reported beside its algorithmic bytes and the measured HBM
-    peak.  Device time is the sum of the library's kernels per call (the profiler's events),
-    which for the small C1 product excludes the host's launch cadence."""
+def bench_c1(urb, native, ctx, dev, pk_hbm, g):
+    """Config 1: BF16 SwiGLU FFN (urb_gated_mlp_forward_device) at T = 1 and 32."""
     import torch
     from urbilateria_b200 import synthetic as syn
-    dev = f"cuda:{local}"
-    out = {}
-    g = syn.rng(SEED + 11)
-
     # Config 1: BF16 SwiGLU FFN, gate/up [768 x 2048], down [2048 x 768] ~ N(0, 0.02); T = 1
     # and 32.  9.4 MB of weights fit L2, so 27 distinct copies (254 MB) are used in turn.
     H1, I1, copies = 2048, 768, 27
@@ -365,7 +358,21 @@ def bench_configs(urb, native, ctx, local, pk_hbm):
     for m in mlps:
         for x in m:
             x.free()
-    out["c1"] = c1
+    return c1
+
+
+def bench_configs(urb, native, ctx, local, pk_hbm):
+    """Configs 1, 3 and 4 of the benchmark set, each timed on this GPU with the library's own
+    device API (inputs resident), reported beside its algorithmic bytes and the measured HBM
+    peak.  Device time is the sum of the library's kernels per call (the profiler's events),
+    which for the small C1 product excludes the host's launch cadence."""
+    import torch
+    from urbilateria_b200 import synthetic as syn
+    dev = f"cuda:{local}"
+    out = {}
+    g = syn.rng(SEED + 11)
+
+    out["c1"] = bench_c1(urb, native, ctx, dev, pk_hbm, g)
 
     out["c3"] = bench_c3(urb, native, ctx, dev, pk_hbm, g)
     out["c4"] = bench_c4(urb, native, ctx, local, pk_hbm, 1, 0)
@@ -672,8 +679,9 @@ def main():
                     help="tokens per GPU (128 = config 2; other values only for profiling)")
     ap.add_argument("--int-only", action="store_true",
                     help="profiling: time only the INT4 / INT8 products and print their figures")
-    ap.add_argument("--only", choices=["matvec", "c3"],
-                    help="profiling: time only the config-0 matvec or config 3 and print its figures")
+    ap.add_argument("--only", choices=["matvec", "c1", "c3"],
+                    help="profiling: time only the config-0 matvec, config 1 or config 3 and print "
+                         "its figures")
     ap.add_argument("--c3-experts", type=int, default=128,
                     help="experts of --only c3 (128 = config 3; fewer only for profiling captures)")
     args = ap.parse_args()
@@ -706,6 +714,8 @@ def main():
         with torch.cuda.stream(stream):
             if args.only == "matvec":
                 res = bench_matvec(urb, ctx, stream, local, peaks()[0])
+            elif args.only == "c1":
+                res = bench_c1(urb, native, ctx, f"cuda:{local}", peaks()[0], syn.rng(SEED + 11))
             else:
                 res = bench_c3(urb, native, ctx, f"cuda:{local}", peaks()[0], syn.rng(SEED + 11),
                                args.c3_experts)

@@ -238,3 +238,38 @@ def test_mx_matrix_keeps_one_resident_copy(ctx, fmt):
     x = syn.normal_f32(g, (3, cols))
     assert np.isfinite(m.matmul_rows(x, 3)).all()
     m.free()
+
+
+@pytest.mark.parametrize("rows,cols", [(300, 200), (2048, 768), (768, 2048), (5, 8), (130, 7168)])
+def test_bf16_split_k_tensor_core_products(oracle, ctx, rows, cols):
+    # BF16 with cols % 8 == 0, 1..32 tokens, whole rows: tcgen05 kind::f16 with K split over a
+    # cluster (TMA boxes past the matrix's last row / column read as zero; ragged K stages).
+    g = syn.rng(rows + 3 * cols)
+    dev, orc = bf16_pair(oracle, ctx, g, rows, cols, std=0.5)
+    for batch in (1, 2, 7, 16, 31, 32):
+        x = syn.normal_f32(g, (batch, cols))
+        assert_close(dev.matmul_rows(x, batch), orc.matmul_rows(x, batch))
+
+
+@pytest.mark.parametrize("batch", [33, 77])
+def test_bf16_batched_products_on_the_grouped_pass(oracle, ctx, batch):
+    # More than 32 tokens: the grouped tcgen05 pass (all tokens in one group), row ranges too.
+    g = syn.rng(batch)
+    dev, orc = bf16_pair(oracle, ctx, g, 300, 200, std=0.5)
+    x = syn.normal_f32(g, (batch, 200))
+    assert_close(dev.matmul_rows(x, batch), orc.matmul_rows(x, batch))
+    got = dev.matmul_row_range(37, 150, x, batch)
+    want = orc.matmul_rows(x, batch)[:, 37:187]
+    assert_close(got, want)
+
+
+@pytest.mark.parametrize("tokens", [40, 96])
+def test_bf16_gated_mlp_grouped_pass(oracle, ctx, tokens):
+    g = syn.rng(8900 + tokens)
+    gd, go = bf16_pair(oracle, ctx, g, 768, 2048)
+    ud, uo = bf16_pair(oracle, ctx, g, 768, 2048)
+    dd, do = bf16_pair(oracle, ctx, g, 2048, 768)
+    x = syn.normal_f32(g, (tokens, 2048))
+    got = urb.GatedMlp(gd, ud, dd).forward_batch(x, tokens)
+    want = np.stack([oracle.gated_mlp_forward(go, uo, do, x[t]) for t in range(tokens)])
+    assert_close(got, want)

@@ -210,8 +210,18 @@ int device_product(Ctx *ctx, const Mat *m, size_t start, size_t count, const flo
         prof_end(ctx, st);
         return rc;
     }
+    if (split_tc_applies(m, batch) && start == 0 && count == m->rows) {
+        // BF16, 1..32 tokens, whole rows: split-K tcgen05 clusters (split_tc.cu).
+        int rc = split_tc_product(ctx, m, d_x, int(batch), d_y, d_status, st);
+        if (rc != URB_ERR_UNSUPPORTED) return rc;
+    }
+    if (m->format == URB_FMT_BF16 && dense_tc_applies(m) && batch > 32) {
+        // BF16, more tokens: the grouped tcgen05 pass with every token in one group.
+        int rc = dense_tc_product(ctx, m, start, count, d_x, int(batch), d_y, d_status, st);
+        if (rc != URB_ERR_UNSUPPORTED) return rc;
+    }
     if (bf16_gemv_applies(m, batch)) {
-        // BF16 rows for a few tokens: one streaming pass on CUDA cores.
+        // BF16 rows for a few tokens (row ranges): one streaming pass on CUDA cores.
         prof_begin(ctx, URB_K_PRODUCT, st);
         int rc = launch_bf16_gemv(ctx, m, start, count, d_x, batch, d_y, d_status, st);
         prof_end(ctx, st);

@@ -1,7 +1,8 @@
 // dense_tc.cu — GatedMlp::forward (src/model/mlp.rs:90-99) and WeightMatrix::matmul_rows
-// (src/model/weight.rs:106-153) for MX matrices on the block-scaled tensor-core passes of
-// grouped_tc.cu, reading the same resident 128-row tiles as the MoE layer (MX matrices keep no
-// other copy).
+// (src/model/weight.rs:106-153) for MX and BF16 matrices on the tensor-core passes of
+// grouped_tc.cu, reading the same tiles as the MoE layer (MX: the resident 128-row tiles, of
+// which MX matrices keep no other copy; BF16: boxes of the row-major matrix through its
+// tensor map).
 //
 // Every token goes into one group (no routing): the gate/up pass pairs the gate and up tiles of
 // the MLP against each activation stage and writes h = silu(gate) * up, the down pass pairs
@@ -131,18 +132,23 @@ TcArgs pass_args(const PassMem &m, const DensePass &p, const float *src, int src
 }
 
 DensePass gu_pass(const Mat *g, const Mat *u) {
-    return DensePass{g->tc_tiles, u->tc_tiles, g->tc_mts, g->tc_ks, int(g->rows), int(g->cols), g->tc_mts};
+    return DensePass{tc_src(g), tc_src(u), g->tc_mts, g->tc_ks, int(g->rows), int(g->cols), g->tc_mts};
 }
 DensePass single_pass(const Mat *m) {
-    return DensePass{m->tc_tiles, nullptr, m->tc_mts, m->tc_ks, int(m->rows), int(m->cols), (m->tc_mts + 1) / 2};
+    return DensePass{tc_src(m), nullptr, m->tc_mts, m->tc_ks, int(m->rows), int(m->cols), (m->tc_mts + 1) / 2};
 }
 
 }  // namespace
 
+bool dense_tc_applies(const Mat *m) {
+    const int f = m->format;
+    return (f == URB_FMT_MXFP4 || f == URB_FMT_MXFP8 || f == URB_FMT_BF16) && tc_src(m);
+}
+
 bool dense_tc_mlp_applies(const Mat *g, const Mat *u, const Mat *d) {
     const int f = g->format;
-    return (f == URB_FMT_MXFP4 || f == URB_FMT_MXFP8) && u->format == f && d->format == f &&
-           g->tc_tiles && u->tc_tiles && d->tc_tiles;
+    return u->format == f && d->format == f && dense_tc_applies(g) && dense_tc_applies(u) &&
+           dense_tc_applies(d);
 }
 
 size_t dense_tc_mlp_bytes(const Mat *g, const Mat *u, const Mat *d, int T) {

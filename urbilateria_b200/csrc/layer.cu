@@ -555,13 +555,21 @@ int moe_forward_generic(Layer *L, const float *d_x, int T, float *d_out, int32_t
 int gated_mlp_device(Ctx *ctx, const Mat *g, const Mat *u, const Mat *d, const float *d_x, int T,
                      float *d_out, int32_t *d_status, cudaStream_t st) {
     const size_t H = g->cols, I = g->rows;
-    // MX projections: the grouped tensor-core passes over their resident tcgen05 tiles.
+    int rc;
+    // BF16 projections, 1..32 tokens: split-K tcgen05 passes (split_tc.cu).
+    if (split_tc_applies(g, size_t(T)) && u->format == g->format && d->format == g->format) {
+        float *h = static_cast<float *>(workspace(ctx, size_t(T) * I * 4 + 256, &rc));
+        if (!h) return rc;
+        rc = split_tc_mlp(ctx, g, u, d, d_x, T, h, d_out, d_status, st);
+        if (rc != URB_ERR_UNSUPPORTED) return rc;
+    }
+    // MX projections (resident tcgen05 tiles) and BF16 ones (tensor maps): the grouped
+    // tensor-core passes with every token in one group.
     if (dense_tc_mlp_applies(g, u, d))
         return dense_tc_mlp(ctx, g, u, d, d_x, T, d_out, d_status, st, nullptr, 0);
     if (!(g->tiled && u->tiled && d->tiled && g->format == u->format))
         return gated_mlp_generic(ctx, g, u, d, d_x, T, d_out, d_status, st);
     const int nseg = int(div_ceil(T, kCap));
-    int rc;
     if (bf16_gemv_applies(g, T) && bf16_gemv_applies(u, T) && bf16_gemv_applies(d, T)) {
         // BF16 projections, a few tokens: two streaming passes (gate/up with SwiGLU, down).
         float *h = static_cast<float *>(workspace(ctx, size_t(T) * I * 4 + 256, &rc));

@@ -90,7 +90,18 @@ int urb_gated_mlp_forward_device_noalloc(urb_ctx *ctx, const urb_mat *g, const u
         return set_error(ctx, URB_ERR_SHAPE, "gated MLP projections have inconsistent shapes");
     if (tokens == 0) return URB_OK;
     const size_t H = g->cols, I = g->rows, T = tokens;
-    // BF16 projections of a few tokens stream the row-major copies and need no tiles.
+    // BF16 projections of 1..32 tokens: the split-K tensor-core passes of
+    // urb_gated_mlp_forward_device (h in the scratch).
+    if (split_tc_applies(g, T) && u->format == g->format && d->format == g->format &&
+        T * I * 4 <= kNoallocScratchBytes) {
+        uint8_t *base = nullptr;
+        int rc = scratch_of(ctx, &base);
+        if (rc) return rc;
+        rc = split_tc_mlp(ctx, g, u, d, d_x, int(T), reinterpret_cast<float *>(base), d_out, d_status,
+                          ctx->stream);
+        if (rc != URB_ERR_UNSUPPORTED) return rc;
+    }
+    // BF16 projections of a few tokens without a tensor map stream the row-major copies.
     if (bf16_gemv_applies(g, T) && bf16_gemv_applies(u, T) && bf16_gemv_applies(d, T) &&
         T * I * 4 <= kNoallocScratchBytes) {
         // The same streaming BF16 passes as urb_gated_mlp_forward_device (h in the scratch).
@@ -102,8 +113,9 @@ int urb_gated_mlp_forward_device_noalloc(urb_ctx *ctx, const urb_mat *g, const u
         if (rc != URB_ERR_UNSUPPORTED) return rc;
     }
     if (dense_tc_mlp_applies(g, u, d)) {
-        // MX projections: the grouped tensor-core passes over their tcgen05 tiles, every table,
-        // activation stage and h in the scratch (the same passes as the allocating entry point).
+        // MX and BF16 projections: the grouped tensor-core passes (tcgen05 tiles / tensor maps),
+        // every table, activation stage and h in the scratch (the same passes as the
+        // allocating entry point).
         uint8_t *base = nullptr;
         int rc = scratch_of(ctx, &base);
         if (rc) return rc;

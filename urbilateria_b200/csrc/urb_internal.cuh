@@ -234,17 +234,26 @@ int launch_bf16_swiglu(Ctx *ctx, const Mat *g, const Mat *u, const Mat *d, const
                        int tokens, float *d_h, float *d_out, int32_t *d_status, cudaStream_t st);
 int launch_matvec1(Ctx *ctx, const Mat *m, size_t start, size_t count, const float *d_x,
                    float *d_y, cudaStream_t st);
-// dense_tc.cu: MX gated MLP and batched products on the block-scaled tensor-core passes (the
-// resident tcgen05 tiles), all tokens in one group.  dense_tc_mlp uses `mem` (mem_bytes of
-// device memory, at least dense_tc_mlp_bytes) when given, else the context workspace.
+// dense_tc.cu: MX and BF16 gated MLP and batched products on the grouped tensor-core passes
+// (MX: the resident tcgen05 tiles; BF16: the tensor map), all tokens in one group.
+// dense_tc_mlp uses `mem` (mem_bytes of device memory, at least dense_tc_mlp_bytes) when
+// given, else the context workspace.
 bool dense_tc_mlp_applies(const Mat *g, const Mat *u, const Mat *d);
 size_t dense_tc_mlp_bytes(const Mat *g, const Mat *u, const Mat *d, int T);
 int dense_tc_mlp(Ctx *ctx, const Mat *g, const Mat *u, const Mat *d, const float *d_x, int T,
                  float *d_out, int32_t *d_status, cudaStream_t st, uint8_t *mem, size_t mem_bytes);
-// Rows [start, start + count) of an MX matrix with tcgen05 tiles times d_x [T, cols] into
-// d_y [T, count].
+// Rows [start, start + count) of a matrix the passes take (dense_tc_applies) times d_x
+// [T, cols] into d_y [T, count].
+bool dense_tc_applies(const Mat *m);
 int dense_tc_product(Ctx *ctx, const Mat *m, size_t start, size_t count, const float *d_x, int T,
                      float *d_y, int32_t *d_status, cudaStream_t st);
+// split_tc.cu: BF16 products and gated MLPs of 1..32 tokens on tcgen05 kind::f16 with K split
+// over thread-block clusters (whole rows; d_h [T, I] holds the MLP's h).
+bool split_tc_applies(const Mat *m, size_t T);
+int split_tc_product(Ctx *ctx, const Mat *m, const float *d_x, int T, float *d_y, int32_t *d_status,
+                     cudaStream_t st);
+int split_tc_mlp(Ctx *ctx, const Mat *g, const Mat *u, const Mat *d, const float *d_x, int T,
+                 float *d_h, float *d_out, int32_t *d_status, cudaStream_t st);
 // upload.cu: the 16-row mma.sync tiles of an MX matrix, built from its tcgen05 tiles on first
 // use (the mma.sync layer passes and the CUDA-core single-token fallback); MX uploads keep only
 // the tcgen05 tiles.
