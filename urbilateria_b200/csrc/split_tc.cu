@@ -12,13 +12,16 @@
 //     exact), token t's terms in MMA rows 3t .. 3t + 2;
 //   * two issuing threads run the MMAs (gated MLP: gate and up, one each; a single matrix:
 //     alternate stages), each into its own TMEM accumulator;
-//   * the epilogue warps sum each token's term columns and scatter the partial sums over the
+//   * every warp then sums its tokens' term columns and scatters the partial sums over the
 //     cluster (distributed shared memory, st.async completing on the owner's barrier): rank q
 //     owns rows [q, q + 1) * 128 / ksplit of the tile, adds the ksplit partials in rank
 //     order (deterministic) and writes the outputs (gated MLP: h = silu(gate) * up).
 // Every wait is bounded (URB_ERR_TIMEOUT); every copy in flight lands before a CTA exits.
+#include <cuda.h>
+
 #include <algorithm>
 #include <atomic>
+#include <cstring>
 
 #include "tc_common.cuh"
 #include "urb_internal.cuh"
@@ -47,7 +50,6 @@ __host__ __device__ constexpr int sp_smem(int spc, int nmat, int T) {
 }
 
 struct SpArgs {
-    const void *map1, *map2;  // tensor maps: the matrix (gated MLP: gate), and up
     int mts, ks;              // 128-row tiles, K stages of 64 columns
     int ksplit;               // CTAs of a cluster (ranks), a divisor of 128
     int rows, cols, T;
@@ -87,8 +89,10 @@ __device__ __forceinline__ uint32_t bf16_rn(float v) {
 __device__ __forceinline__ float silu_ieee(float v) { return v / (1.0f + expf(-v)); }
 
 // NMAT = 2: gated MLP (map1 gate, map2 up; output h = silu(gate) * up).  NMAT = 1: product.
+// The tensor maps are kernel parameters (the TMA unit reads them from the parameter space).
 template <int NMAT>
-__global__ void __launch_bounds__(kSpThreads, 1) k_split_bf16(SpArgs a) {
+__global__ void __launch_bounds__(kSpThreads, 1)
+    k_split_bf16(SpArgs a, const __grid_constant__ CUtensorMap map1, const __grid_constant__ CUtensorMap map2) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     __shared__ __align__(8) uint64_t a_full[kSpMaxStages], acc_full[2], mma_done[2], red_full;
@@ -121,7 +125,7 @@ __global__ void __launch_bounds__(kSpThreads, 1) k_split_bf16(SpArgs a) {
             for (int s = 0; s < S; ++s) {
                 tc::mbar_arrive_expect_tx(&a_full[s], uint32_t(NMAT * kSpTileBytes));
                 for (int m = 0; m < NMAT; ++m)
-                    tc::tma_load_2d(wbox + size_t(s * NMAT + m) * kSpTileBytes, m ? a.map2 : a.map1,
+                    tc::tma_load_2d(wbox + size_t(s * NMAT + m) * kSpTileBytes, m ? &map2 : &map1,
                                     (s0 + s) * kSpStageCols, mt * 128, &a_full[s]);
             }
             // The cluster's partial sums of this rank's rows: RPR rows x NMAT x TP floats from
@@ -214,52 +218,52 @@ __global__ void __launch_bounds__(kSpThreads, 1) k_split_bf16(SpArgs a) {
         if (any) tc::mma_commit(&acc_full[me]);
         tc::mma_commit(&mma_done[me]);
         tc::mbar_wait(&mma_done[me], 0, &never);
-    } else if (warp >= 4) {
-        // Epilogue: row 32 qtr + lane of the tile.  part[m][t] = the token's term columns of
-        // accumulator m (product: both accumulators, issuer 0's first).
-        const int qtr = warp & 3;
+    }
+    __syncwarp();
+
+    // Epilogue, every warp: row 32 qtr + lane of the tile; warps 0-3 take tokens 0..15 (term
+    // columns 0..47), warps 4-7 tokens 16..31 (columns 48..95).  part[m][i] = token 16 h + i's
+    // term columns of accumulator m (product: both accumulators, issuer 0's first).
+    {
+        const int qtr = warp & 3, h = warp >> 2;
         const uint32_t lane_base = uint32_t(32 * qtr) << 16;
         const int used = NMAT == 2 ? (S > 0 ? 2 : 0) : min(S, 2);
         bool ok = true;
         for (int i = 0; i < used && ok; ++i)
             if (!tc::mbar_wait(&acc_full[i], 0, abortp)) { fail(); ok = false; }
-        float part[NMAT][kSpMaxTok];
+        float part[NMAT][16];
 #pragma unroll
         for (int m = 0; m < NMAT; ++m)
 #pragma unroll
-            for (int t = 0; t < kSpMaxTok; ++t) part[m][t] = 0.0f;
-        if (ok && used > 0) {
+            for (int t = 0; t < 16; ++t) part[m][t] = 0.0f;
+        const int nch = min(3, max(0, (NB - 48 * h) / 16));  // this half's 16-column chunks
+        if (ok && used > 0 && nch > 0) {
             tc::fence_after_sync();
+            uint32_t v[2][3][16];
 #pragma unroll
-            for (int c = 0; c < 3 * kSpMaxTok / 16; ++c) {
-                if (16 * c >= NB) break;  // uniform across the warp
-                uint32_t v[2][16];
+            for (int i = 0; i < 2; ++i)
 #pragma unroll
-                for (int i = 0; i < 2; ++i)
-                    if (i < used) tc::tmem_ld16(tbase + lane_base + uint32_t(i) * kSpAccStride + 16u * c, v[i]);
-                tc::wait_ld();
+                for (int k = 0; k < 3; ++k)
+                    if (i < used && k < nch)
+                        tc::tmem_ld16(tbase + lane_base + uint32_t(i) * kSpAccStride + uint32_t(48 * h + 16 * k), v[i][k]);
+            tc::wait_ld();
+#pragma unroll
+            for (int k = 0; k < 3; ++k) {
+                if (k >= nch) break;
 #pragma unroll
                 for (int e = 0; e < 16; ++e) {
-                    const int t = (16 * c + e) / 3;
-                    if (t >= kSpMaxTok) continue;
-                    if (NMAT == 2) {
-                        part[0][t] += __uint_as_float(v[0][e]);
-                        part[NMAT - 1][t] += __uint_as_float(v[1][e]);
-                    } else {
-                        part[0][t] += __uint_as_float(v[0][e]);
-                    }
+                    const int t = (16 * k + e) / 3;
+                    part[0][t] += __uint_as_float(v[0][k][e]);
+                    if (NMAT == 2) part[NMAT - 1][t] += __uint_as_float(v[1][k][e]);
                 }
                 if (NMAT == 1 && used > 1) {
 #pragma unroll
-                    for (int e = 0; e < 16; ++e) {
-                        const int t = (16 * c + e) / 3;
-                        if (t < kSpMaxTok) part[0][t] += __uint_as_float(v[1][e]);
-                    }
+                    for (int e = 0; e < 16; ++e) part[0][(16 * k + e) / 3] += __uint_as_float(v[1][k][e]);
                 }
             }
         }
-        // Scatter: this row's partial sums to the rank that owns it (every thread stores on
-        // every path, so every owner's wait completes).
+        // Scatter this row's partial sums (tokens 16 h + 4 t4 .. + 3) to the rank that owns the
+        // row.  Every thread stores on every path, so every owner's wait completes.
         const int row = 32 * qtr + lane;
         const int owner = row / RPR, r = row - owner * RPR;
         uint32_t dst, bar;
@@ -269,16 +273,16 @@ __global__ void __launch_bounds__(kSpThreads, 1) k_split_bf16(SpArgs a) {
 #pragma unroll
         for (int m = 0; m < NMAT; ++m)
 #pragma unroll
-            for (int t4 = 0; t4 < kSpMaxTok / 4; ++t4) {
-                if (4 * t4 >= TP) break;
+            for (int t4 = 0; t4 < 4; ++t4) {
+                const int t = 16 * h + 4 * t4;
+                if (t >= TP) break;
                 asm volatile(
                     "st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, [%5];"
-                    ::"r"(dst + uint32_t((m * TP + 4 * t4) * 4)), "f"(part[m][4 * t4]), "f"(part[m][4 * t4 + 1]),
+                    ::"r"(dst + uint32_t((m * TP + t) * 4)), "f"(part[m][4 * t4]), "f"(part[m][4 * t4 + 1]),
                       "f"(part[m][4 * t4 + 2]), "f"(part[m][4 * t4 + 3]), "r"(bar)
                     : "memory");
             }
     }
-    __syncwarp();
 
     // Owners: this rank's rows [kq * RPR, +RPR) of the tile, the partials added in rank order.
     if (!mbar_wait_cluster(&red_full, 0, 1u << 26)) fail();
@@ -333,7 +337,7 @@ std::atomic<int> g_sp_resident[kSpMaxDevices][2][5][kSpMaxStages + 1][kSpMaxTok 
 // divisors of 128) that keeps every rank at least one stage, holds at most kSpMaxStages stages
 // per CTA in shared memory, and keeps all the launch's clusters resident at once.
 template <int NMAT>
-int launch_split(Ctx *ctx, const void *m1, const void *m2, int mts, int ks, int rows, int cols,
+int launch_split(Ctx *ctx, const Mat *m1, const Mat *m2, int mts, int ks, int rows, int cols,
                  const float *d_x, int x_stride, int T, float *d_out, int out_stride,
                  int32_t *d_status, cudaStream_t st) {
     auto kern = k_split_bf16<NMAT>;
@@ -368,8 +372,6 @@ int launch_split(Ctx *ctx, const void *m1, const void *m2, int mts, int ks, int 
     if (!chosen) return URB_ERR_UNSUPPORTED;
     const int spc = (ks + chosen - 1) / chosen;
     SpArgs a{};
-    a.map1 = m1;
-    a.map2 = m2;
     a.mts = mts;
     a.ks = ks;
     a.ksplit = chosen;
@@ -395,7 +397,10 @@ int launch_split(Ctx *ctx, const void *m1, const void *m2, int mts, int ks, int 
     cm.stream = st;
     cm.attrs = at;
     cm.numAttrs = 2;
-    URB_CUDA(ctx, cudaLaunchKernelEx(&cm, kern, a));
+    CUtensorMap t1, t2;
+    std::memcpy(&t1, m1->tc_map_host, sizeof(t1));
+    std::memcpy(&t2, (m2 ? m2 : m1)->tc_map_host, sizeof(t2));
+    URB_CUDA(ctx, cudaLaunchKernelEx(&cm, kern, a, t1, t2));
     return URB_OK;
 }
 
@@ -409,7 +414,7 @@ int split_tc_product(Ctx *ctx, const Mat *m, const float *d_x, int T, float *d_y
                      cudaStream_t st) {
     if (!split_tc_applies(m, size_t(T))) return URB_ERR_UNSUPPORTED;
     prof_begin(ctx, URB_K_PRODUCT, st);
-    const int rc = launch_split<1>(ctx, m->tc_map, nullptr, m->tc_mts, m->tc_ks, int(m->rows), int(m->cols),
+    const int rc = launch_split<1>(ctx, m, nullptr, m->tc_mts, m->tc_ks, int(m->rows), int(m->cols),
                                    d_x, int(m->cols), T, d_y, int(m->rows), d_status, st);
     prof_end(ctx, st);
     return rc;
@@ -421,12 +426,12 @@ int split_tc_mlp(Ctx *ctx, const Mat *g, const Mat *u, const Mat *d, const float
         u->cols != g->cols || d->cols != g->rows)
         return URB_ERR_UNSUPPORTED;
     prof_begin(ctx, URB_K_GATE_UP, st);
-    int rc = launch_split<2>(ctx, g->tc_map, u->tc_map, g->tc_mts, g->tc_ks, int(g->rows), int(g->cols),
+    int rc = launch_split<2>(ctx, g, u, g->tc_mts, g->tc_ks, int(g->rows), int(g->cols),
                              d_x, int(g->cols), T, d_h, int(g->rows), d_status, st);
     prof_end(ctx, st);
     if (rc) return rc;
     prof_begin(ctx, URB_K_DOWN, st);
-    rc = launch_split<1>(ctx, d->tc_map, nullptr, d->tc_mts, d->tc_ks, int(d->rows), int(d->cols), d_h,
+    rc = launch_split<1>(ctx, d, nullptr, d->tc_mts, d->tc_ks, int(d->rows), int(d->cols), d_h,
                          int(d->cols), T, d_out, int(d->rows), d_status, st);
     prof_end(ctx, st);
     return rc;

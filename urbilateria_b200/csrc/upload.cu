@@ -2,6 +2,7 @@
 // reference constructors) and the repack into the tiled layout described in urb_internal.cuh.
 #include <cuda.h>
 
+#include <cstring>
 #include <mutex>
 
 #include "urb_internal.cuh"
@@ -201,6 +202,8 @@ int make_bf16_tile_map(Ctx *ctx, Mat *m, cudaStream_t st) {
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
         return URB_OK;
+    static_assert(sizeof(CUtensorMap) == sizeof(m->tc_map_host), "tensor map size");
+    std::memcpy(m->tc_map_host, &map, sizeof(CUtensorMap));
     URB_CUDA(ctx, cudaMallocAsync(&m->tc_map, sizeof(CUtensorMap), st));
     URB_CUDA(ctx, cudaMemcpyAsync(m->tc_map, &map, sizeof(CUtensorMap), cudaMemcpyHostToDevice, st));
     m->tc_mts = int(div_ceil(m->rows, 128));

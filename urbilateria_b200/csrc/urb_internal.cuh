@@ -56,8 +56,10 @@ struct Mat {
     // scales, K-stage major (tc_mts row tiles x tc_ks K stages).
     uint8_t *tc_tiles = nullptr;
     // BF16 matrices (cols a multiple of 8): a TMA tensor map (CUtensorMap in device memory)
-    // over the row-major copy, boxes of 128 rows x 64 columns in the 128-byte swizzle.
+    // over the row-major copy, boxes of 128 rows x 64 columns in the 128-byte swizzle, and its
+    // host copy (kernels that take it as a parameter).
     void *tc_map = nullptr;
+    alignas(64) unsigned char tc_map_host[128] = {};
     int tc_mts = 0, tc_ks = 0;
     // Generic path: the reference layout on the device (used when !tiled).
     void *raw_values = nullptr;
