@@ -163,6 +163,8 @@ __device__ __forceinline__ float silu_fast(float v) { return __fdividef(v, 1.0f 
 // MODE 0: the issuers split each stage's K steps of one tile; the epilogue adds their halves.
 template <int FMT, int MODE, int NT>
 __global__ void __launch_bounds__(kThreadsBs, 1) k_bs_grouped(TcArgs a) {
+    grid_dep_wait();  // programmatic dependent launch: the kernel ahead has completed
+    grid_dep_trigger();
     constexpr bool PAIR = MODE != 0;   // two weight tiles per stage, one per issuer
     constexpr bool GU = MODE == 1, MT = MODE == 2;
     constexpr int TPU = MT ? 2 : 1;    // row tiles per unit
@@ -583,6 +585,8 @@ __device__ __forceinline__ void make_term8_bf16(float *r, uint32_t *q) {
 
 template <int FMT, int NT>
 __global__ void __launch_bounds__(256) k_bs_prep(TcArgs a) {
+    grid_dep_wait();  // programmatic dependent launch: the kernel ahead has completed
+    grid_dep_trigger();
     constexpr bool BF = FMT == URB_FMT_BF16;
     // 32-column blocks per stage; code words per lane per term.
     constexpr int KBS = FMT == URB_FMT_MXFP4 ? 8 : (FMT == URB_FMT_MXFP8 ? 4 : 2);
@@ -670,32 +674,48 @@ __global__ void __launch_bounds__(256) k_bs_prep(TcArgs a) {
     if (!valid) return;
     const int ks = kb / KBS, kbs = kb % KBS;
     const int ndst = a.inv ? a.top_k + (shared_dst ? 1 : 0) : 1;
-    for (int d = 0; d < ndst; ++d) {
-        const int col = a.inv ? (d < a.top_k ? a.inv[row * a.top_k + d]
-                                             : a.shared_col0 + (row - a.shared_row0))
-                              : row;
-        if (col < 0) continue;
-        const BsSlot S = a.slots[col];
-        uint8_t *stage = a.bbuf + S.base + (long long)ks * bs_bstage_bytes(FMT, S.n);
+    // Destinations in batches: the column indices, then their slots, are loaded together (two
+    // round trips per batch instead of two per destination).
+    constexpr int kDb = 4;
+    for (int d0 = 0; d0 < ndst; d0 += kDb) {
+        int cols[kDb];
+        BsSlot sl[kDb];
 #pragma unroll
-        for (int t = 0; t < TT; ++t) {
-            const int R = S.slot * RT + t;  // MMA row within the stage
-            uint8_t *rowp = stage + (R >> 3) * 1024 + (R & 7) * 128;
-            if constexpr (BF) {
-                // The lane's 8 columns are one 16-byte chunk of the 128-byte row.
-                const int ch = 4 * kbs + part;
-                *reinterpret_cast<uint4 *>(rowp + ((ch ^ (R & 7)) << 4)) =
-                    make_uint4(q[t][0], q[t][1 % QW], q[t][2 % QW], q[t][3 % QW]);
-                continue;
-            } else if (FMT == URB_FMT_MXFP4) {
-                *reinterpret_cast<uint32_t *>(rowp + ((kbs ^ (R & 7)) << 4) + 4 * part) = q[t][0];
-            } else {
-                const int ch = 2 * kbs + (part >> 1);
-                *reinterpret_cast<uint2 *>(rowp + ((ch ^ (R & 7)) << 4) + 8 * (part & 1)) =
-                    make_uint2(q[t][0], q[t][QW - 1]);
+        for (int j = 0; j < kDb; ++j) {
+            const int d = d0 + j;
+            cols[j] = d >= ndst ? -1
+                                : (a.inv ? (d < a.top_k ? a.inv[row * a.top_k + d]
+                                                        : a.shared_col0 + (row - a.shared_row0))
+                                         : row);
+        }
+#pragma unroll
+        for (int j = 0; j < kDb; ++j)
+            if (cols[j] >= 0) sl[j] = a.slots[cols[j]];
+#pragma unroll
+        for (int j = 0; j < kDb; ++j) {
+            if (cols[j] < 0) continue;
+            const BsSlot S = sl[j];
+            uint8_t *stage = a.bbuf + S.base + (long long)ks * bs_bstage_bytes(FMT, S.n);
+#pragma unroll
+            for (int t = 0; t < TT; ++t) {
+                const int R = S.slot * RT + t;  // MMA row within the stage
+                uint8_t *rowp = stage + (R >> 3) * 1024 + (R & 7) * 128;
+                if constexpr (BF) {
+                    // The lane's 8 columns are one 16-byte chunk of the 128-byte row.
+                    const int ch = 4 * kbs + part;
+                    *reinterpret_cast<uint4 *>(rowp + ((ch ^ (R & 7)) << 4)) =
+                        make_uint4(q[t][0], q[t][1 % QW], q[t][2 % QW], q[t][3 % QW]);
+                    continue;
+                } else if (FMT == URB_FMT_MXFP4) {
+                    *reinterpret_cast<uint32_t *>(rowp + ((kbs ^ (R & 7)) << 4) + 4 * part) = q[t][0];
+                } else {
+                    const int ch = 2 * kbs + (part >> 1);
+                    *reinterpret_cast<uint2 *>(rowp + ((ch ^ (R & 7)) << 4) + 8 * (part & 1)) =
+                        make_uint2(q[t][0], q[t][QW - 1]);
+                }
+                if (part == 0)
+                    stage[S.n * 128 + 512 * (kbs >> 2) + 16 * (R & 31) + 4 * (R >> 5) + (kbs & 3)] = uint8_t(sb[t]);
             }
-            if (part == 0)
-                stage[S.n * 128 + 512 * (kbs >> 2) + 16 * (R & 31) + 4 * (R >> 5) + (kbs & 3)] = uint8_t(sb[t]);
         }
     }
 }
@@ -755,7 +775,8 @@ int launch_bs_t(Ctx *ctx, const TcArgs &a, int kind, cudaStream_t st) {
     const long long threads = (long long)a.nrows * a.ks * KBS * 4;
     if (threads > 0) {
         prof_begin(ctx, URB_K_PREP, st);
-        k_bs_prep<FMT, NT><<<unsigned((threads + 255) / 256), 256, 0, st>>>(a);
+        auto prep = k_bs_prep<FMT, NT>;
+        URB_LAUNCH_DEP(prep, unsigned((threads + 255) / 256), 256, 0, st, a);
         prof_end(ctx, st);
         URB_CUDA(ctx, cudaGetLastError());
     }
@@ -763,7 +784,7 @@ int launch_bs_t(Ctx *ctx, const TcArgs &a, int kind, cudaStream_t st) {
                          : (a.pair == 2 ? k_bs_grouped<FMT, 2, NT> : k_bs_grouped<FMT, 0, NT>);
     URB_CUDA(ctx, cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBs));
     prof_begin(ctx, kind, st);
-    k<<<ctx->num_sms, kThreadsBs, kSmemBs, st>>>(a);
+    URB_LAUNCH_DEP(k, ctx->num_sms, kThreadsBs, kSmemBs, st, a);
     prof_end(ctx, st);
     URB_CUDA(ctx, cudaGetLastError());
     return URB_OK;

@@ -18,6 +18,8 @@ constexpr int kPermThreads = 1024;
 
 // Single-CTA grouping kernel.  See urb_moe_internal.cuh for the outputs.
 __global__ void __launch_bounds__(kPermThreads) k_permute(PermArgs p) {
+    grid_dep_wait();  // programmatic dependent launch: the kernel ahead has completed
+    grid_dep_trigger();
     extern __shared__ __align__(16) uint8_t smem[];
     const int E = p.experts, TK = p.tokens * p.top_k;
     int *cnt = reinterpret_cast<int *>(smem);                 // [E]
@@ -192,6 +194,8 @@ __global__ void __launch_bounds__(kPermThreads) k_permute(PermArgs p) {
 __global__ void k_combine(const float *y, const float *shared_y, const float *w,
                           const int32_t *inv, int tokens, int top_k, int hidden, float *out,
                           const int32_t *status) {
+    grid_dep_wait();  // programmatic dependent launch: the kernel ahead has completed
+    grid_dep_trigger();
     if (status && *status) return;
     const int t = blockIdx.y;
     const int h = blockIdx.x * blockDim.x + threadIdx.x;
@@ -210,6 +214,8 @@ __global__ void k_combine(const float *y, const float *shared_y, const float *w,
 __global__ void k_combine_deepseek(const float *y, const float *shared_y, const int32_t *ids,
                                    const int32_t *inv, int tokens, int top_k, int hidden,
                                    float *out, int32_t *status) {
+    grid_dep_wait();  // programmatic dependent launch: the kernel ahead has completed
+    grid_dep_trigger();
     if (*status) return;
     const int t = blockIdx.y;
     const int h = blockIdx.x * blockDim.x + threadIdx.x;
@@ -242,6 +248,8 @@ __global__ void k_combine_qwen(const float *y, const float *shared_y, const int3
                                const float *w, const int32_t *inv, const float *gate_logit,
                                ExpfTable tab, int tokens, int top_k, int hidden, float *out,
                                int32_t *status) {
+    grid_dep_wait();  // programmatic dependent launch: the kernel ahead has completed
+    grid_dep_trigger();
     if (*status) return;
     const int t = blockIdx.y;
     const int h = blockIdx.x * blockDim.x + threadIdx.x;
@@ -304,6 +312,8 @@ __device__ __forceinline__ BsSlot slot_of(int fmt, long long boff, int ks, int c
 // Dynamic shared memory: the unit_begin of every group of the pass (binary-searched by the
 // cooperative unit-map fill).
 __global__ void __launch_bounds__(1024) k_build_tc_segs(TcBuildArgs b) {
+    grid_dep_wait();  // programmatic dependent launch: the kernel ahead has completed
+    grid_dep_trigger();
     extern __shared__ int s_ub[];
     __shared__ long long wsum[32], sh_boff;
     __shared__ int wcnt[32], wunits[32], s_groups, s_units;
@@ -435,7 +445,7 @@ int launch_build_tc_segs(Ctx *ctx, const TcBuildArgs &b, cudaStream_t st) {
     const size_t smem = size_t(2 * b.experts + 4) * sizeof(int);
     if (smem > 200 * 1024) return set_error(ctx, URB_ERR_UNSUPPORTED, "too many experts for the group builder");
     URB_CUDA(ctx, cudaFuncSetAttribute(k_build_tc_segs, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
-    k_build_tc_segs<<<1, 1024, smem, st>>>(b);
+    URB_LAUNCH_DEP(k_build_tc_segs, 1, 1024, smem, st, b);
     URB_CUDA(ctx, cudaGetLastError());
     return URB_OK;
 }
@@ -445,7 +455,7 @@ int launch_permute(Ctx *ctx, const PermArgs &p, cudaStream_t st) {
     smem = (smem + 15) & ~size_t(15);
     if (smem > 200 * 1024) return set_error(ctx, URB_ERR_UNSUPPORTED, "too many experts for the grouping kernel");
     URB_CUDA(ctx, cudaFuncSetAttribute(k_permute, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
-    k_permute<<<1, kPermThreads, smem, st>>>(p);
+    URB_LAUNCH_DEP(k_permute, 1, kPermThreads, smem, st, p);
     URB_CUDA(ctx, cudaGetLastError());
     return URB_OK;
 }
@@ -456,7 +466,7 @@ int launch_combine_deepseek(Ctx *ctx, const float *y, const float *shared_y, con
     if (tokens <= 0) return URB_OK;
     if (top_k > 16) return set_error(ctx, URB_ERR_UNSUPPORTED, "DeepSeek combine: top_k > 16");
     dim3 grid(unsigned((hidden + 255) / 256), unsigned(tokens));
-    k_combine_deepseek<<<grid, 256, 0, st>>>(y, shared_y, ids, inv, tokens, top_k, hidden, out,
+    URB_LAUNCH_DEP(k_combine_deepseek, grid, 256, 0, st, y, shared_y, ids, inv, tokens, top_k, hidden, out,
                                              status);
     URB_CUDA(ctx, cudaGetLastError());
     return URB_OK;
@@ -468,7 +478,7 @@ int launch_combine_qwen(Ctx *ctx, const float *y, const float *shared_y, const i
     if (tokens <= 0) return URB_OK;
     if (top_k > 16) return set_error(ctx, URB_ERR_UNSUPPORTED, "Qwen3.6 combine takes top_k <= 16");
     dim3 grid(unsigned((hidden + 255) / 256), unsigned(tokens));
-    k_combine_qwen<<<grid, 256, 0, st>>>(y, shared_y, ids, w, inv, gate_logit, expf_table_of(ctx),
+    URB_LAUNCH_DEP(k_combine_qwen, grid, 256, 0, st, y, shared_y, ids, w, inv, gate_logit, expf_table_of(ctx),
                                          tokens, top_k, hidden, out, status);
     URB_CUDA(ctx, cudaGetLastError());
     return URB_OK;
@@ -479,7 +489,7 @@ int launch_combine(Ctx *ctx, const float *y, const float *shared_y, const float 
                    cudaStream_t st, const int32_t *status) {
     if (tokens <= 0) return URB_OK;
     dim3 grid(unsigned((hidden + 255) / 256), unsigned(tokens));
-    k_combine<<<grid, 256, 0, st>>>(y, shared_y, w, inv, tokens, top_k, hidden, out, status);
+    URB_LAUNCH_DEP(k_combine, grid, 256, 0, st, y, shared_y, w, inv, tokens, top_k, hidden, out, status);
     URB_CUDA(ctx, cudaGetLastError());
     return URB_OK;
 }

@@ -57,6 +57,8 @@ __device__ __forceinline__ void dmma_8x8x4(double &d0, double &d1, double a, dou
 // Rows past `rows`, columns past `cols` and the padding are zero.  One thread per element.
 template <bool BF16>
 __global__ void k_to_f64_blocked(const void *src, int rows, int cols, double *dst) {
+    grid_dep_wait();  // programmatic dependent launch: the kernel ahead has completed
+    grid_dep_trigger();
     const int nch = router_chunks(cols);
     const size_t n = size_t((rows + 7) / 8) * nch * 8 * kRrow;
     for (size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x; i < n;
@@ -84,6 +86,8 @@ __global__ void k_to_f64_blocked(const void *src, int rows, int cols, double *ds
 __global__ void __launch_bounds__(32) k_router_dmma(const double *x64b, const double *w64b,
                                                     int tokens, int experts, int cols,
                                                     float *logits, GateOut go, int32_t *status) {
+    grid_dep_wait();  // programmatic dependent launch: the kernel ahead has completed
+    grid_dep_trigger();
     extern __shared__ __align__(16) double rs[];
     uint64_t *full = reinterpret_cast<uint64_t *>(rs + kRnb * kRstage);
     const int lane = threadIdx.x;
@@ -185,6 +189,8 @@ __global__ void k_route_noaux(const float *logits, const float *bias, int tokens
                               int top_k, int n_group, int topk_group, int normalize,
                               float scaling, ExpfTable tab, int32_t *out_e, float *out_w,
                               float *out_s, int32_t *status, int warp_bytes) {
+    grid_dep_wait();  // programmatic dependent launch: the kernel ahead has completed
+    grid_dep_trigger();
     extern __shared__ __align__(16) uint8_t smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int t = blockIdx.x * (blockDim.x >> 5) + warp;
@@ -274,13 +280,29 @@ __global__ void k_route_noaux(const float *logits, const float *bias, int tokens
     // straight to the output row; lane 0 accumulates the f32 denominator in ranking order.
     int32_t *oe = out_e + size_t(t) * top_k;
     float den = -0.0f;
+    // Up to 512 experts: each lane keeps the keys of experts lane + 32 j in registers
+    // (INT32_MIN marks masked or taken experts; no finite selection score has that key).
+    constexpr int kRegKeys = 16;
+    const bool in_regs = E <= 32 * kRegKeys;
+    int32_t kr[kRegKeys];
+#pragma unroll
+    for (int j = 0; j < kRegKeys; ++j) {
+        const int i = lane + 32 * j;
+        kr[j] = in_regs && i < E && flags[i] == 1 ? total_key(sel[i]) : INT32_MIN;
+    }
     for (int r = 0; r < top_k; ++r) {
         int32_t key = INT32_MIN;
         int id = INT32_MAX;
-        for (int i = lane; i < E; i += 32) {
-            if (flags[i] == 1) {
-                int32_t k = total_key(sel[i]);
-                if (better(k, i, key, id)) { key = k; id = i; }
+        if (in_regs) {
+#pragma unroll
+            for (int j = 0; j < kRegKeys; ++j)
+                if (kr[j] != INT32_MIN && better(kr[j], lane + 32 * j, key, id)) { key = kr[j]; id = lane + 32 * j; }
+        } else {
+            for (int i = lane; i < E; i += 32) {
+                if (flags[i] == 1) {
+                    int32_t k = total_key(sel[i]);
+                    if (better(k, i, key, id)) { key = k; id = i; }
+                }
             }
         }
         warp_best(key, id);
@@ -293,6 +315,9 @@ __global__ void k_route_noaux(const float *logits, const float *bias, int tokens
             return;
         }
         if (lane == (id & 31)) flags[id] = 2;
+#pragma unroll
+        for (int j = 0; j < kRegKeys; ++j)
+            if (lane + 32 * j == id) kr[j] = INT32_MIN;
         if (lane == 0) {
             oe[r] = id;
             den = __fadd_rn(den, gate[id]);
@@ -480,13 +505,14 @@ int launch_router_logits_f64(const double *w64b, int experts, const float *d_x, 
     if (tokens <= 0) return URB_OK;
     GateOut go{};
     if (rg) go = GateOut{rg->bias, rg->gate, rg->sel, rg->status, table_of(rg->ctx)};
-    k_to_f64_blocked<false><<<592, 256, 0, st>>>(d_x, tokens, cols, x64b);
+    auto widen = k_to_f64_blocked<false>;
+    URB_LAUNCH_DEP(widen, 592, 256, 0, st, d_x, tokens, cols, x64b);
     const int blocks = ((tokens + 7) / 8) * ((experts + 7) / 8);
     cudaError_t e = cudaFuncSetAttribute(k_router_dmma, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          kRsmem);
     if (e != cudaSuccess) return URB_ERR_CUDA;
-    k_router_dmma<<<blocks, 32, kRsmem, st>>>(x64b, w64b, tokens, experts, cols, d_logits, go,
-                                             rg ? rg->status : nullptr);
+    URB_LAUNCH_DEP(k_router_dmma, blocks, 32, kRsmem, st, x64b, w64b, tokens, experts, cols, d_logits, go,
+                   rg ? rg->status : nullptr);
     return cudaGetLastError() == cudaSuccess ? URB_OK : URB_ERR_CUDA;
 }
 
@@ -499,7 +525,7 @@ int launch_route_noaux(Ctx *ctx, const float *d_logits, const float *d_bias, int
     int warp_bytes = int(((2 * size_t(experts) + g.n_group) * 4 + experts + 15) & ~size_t(15));
     size_t smem = size_t(warps) * warp_bytes;
     auto k = pre ? k_route_noaux<true> : k_route_noaux<false>;
-    k<<<(tokens + warps - 1) / warps, warps * 32, smem, st>>>(
+    URB_LAUNCH_DEP(k, (tokens + warps - 1) / warps, warps * 32, smem, st,
         pre ? pre->gate : d_logits, pre ? pre->sel : d_bias, tokens, experts, int(g.top_k),
         int(g.n_group), int(g.topk_group), g.normalize, g.routed_scaling_factor, table_of(ctx),
         d_expert, d_weight, d_score, d_status, warp_bytes);

@@ -18,6 +18,7 @@
 #include <stdint.h>
 
 #include <mutex>
+#include <utility>
 #include <string>
 #include <vector>
 
@@ -307,6 +308,33 @@ __device__ __forceinline__ int32_t total_key(float v) {
     int32_t b = __float_as_int(v);
     return b ^ int32_t(uint32_t(b >> 31) >> 1);
 }
+
+// Programmatic dependent launch.  The kernels of the layer path each start with grid_dep_wait
+// (all their reads and writes come after the kernel ahead of them has completed and its
+// memory is visible) and then grid_dep_trigger, and are launched with launch_dep, so the
+// launch of each overlaps the run of the one before it (also inside a CUDA graph).  Launched
+// without the attribute, both instructions do nothing.
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_dep_trigger() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+template <typename... P, typename... A>
+cudaError_t launch_dep(void (*k)(P...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, A &&...args) {
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t c = {};
+    c.gridDim = grid;
+    c.blockDim = block;
+    c.dynamicSmemBytes = smem;
+    c.stream = st;
+    c.attrs = at;
+    c.numAttrs = 1;
+    return cudaLaunchKernelEx(&c, k, std::forward<A>(args)...);
+}
+// A dependent launch written like k<<<g, b, smem, st>>>(args...): a launch error is left for
+// cudaGetLastError.  (A kernel name with template arguments goes through a variable first.)
+#define URB_LAUNCH_DEP(k, g, b, sm, st, ...) (void)::urb::launch_dep(k, dim3(g), dim3(b), size_t(sm), st, __VA_ARGS__)
 #endif
 
 }  // namespace urb
