@@ -463,6 +463,53 @@ def c4_weights(urb, ctx, dev, layer, held, experts=384):
     return routed, shared, router, syn.normal_f32(g, experts, 0.01)
 
 
+def bench_c4_layer(urb, native, ctx, local, pk_hbm):
+    """One config-4 layer (384 MXFP4 experts + shared, hidden 7168) at B = 1 and 8: the graph
+    time of one forward and the library's per-kernel device times (for profiling the decode
+    path's kernel chain)."""
+    import torch
+    from urbilateria_b200 import synthetic as syn
+    dev = f"cuda:{local}"
+    stream = torch.cuda.current_stream()
+    routed, shared, router, bias = c4_weights(urb, ctx, dev, 0, range(384))
+    layer = urb.RuntimeMoeLayer(router, bias, routed, shared, urb.MoeGeometry(TOP_K, 1, 1, True, SCALE))
+    g = syn.rng(SEED + 17)
+    out = {"workload": "one C4 layer: 7168, 384 MXFP4 experts top-8 + 1 shared, inter 2048"}
+    for B in (1, 8):
+        d_x = torch.from_numpy(syn.normal_bf16_as_f32(g, (B, HIDDEN))).to(dev)
+        d_y = torch.empty_like(d_x)
+        st = torch.zeros(1, dtype=torch.int32, device=dev)
+
+        def fn():
+            layer.forward_device(d_x.data_ptr(), B, d_y.data_ptr(), 0, 0, st.data_ptr())
+        for _ in range(5):
+            fn()
+        k_ms, s_ms, n = kernel_ms(ctx, native, fn, 20)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            fn()
+        for _ in range(3):
+            graph.replay()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for _ in range(20):
+            graph.replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        del graph
+        if int(st.item()) != 0:
+            raise RuntimeError("config 4 layer forward reported status %d" % int(st.item()))
+        out["B%d" % B] = {"graph_us": e0.elapsed_time(e1) / 20 * 1e3, "stream_us": s_ms * 1e3,
+                          "launches": n, "kernels_us": kernel_ms.per_kind}
+    layer.free()
+    for e in routed + [shared]:
+        for m in (e.gate, e.up, e.down):
+            m.free()
+    router.free()
+    return out
+
+
 def bench_c4(urb, native, ctx, local, pk_hbm, world, rank, dist=None):
     """Config 4: 4 stacked MoE layers, each with its own 384 MXFP4 routed experts (top-8, the
     config-2 routing) + 1 shared expert (4 x 385 x 23.4 MB = 36 GB of distinct weights on one
@@ -679,9 +726,9 @@ def main():
                     help="tokens per GPU (128 = config 2; other values only for profiling)")
     ap.add_argument("--int-only", action="store_true",
                     help="profiling: time only the INT4 / INT8 products and print their figures")
-    ap.add_argument("--only", choices=["matvec", "c1", "c3"],
-                    help="profiling: time only the config-0 matvec, config 1 or config 3 and print "
-                         "its figures")
+    ap.add_argument("--only", choices=["matvec", "c1", "c3", "c4layer"],
+                    help="profiling: time only the config-0 matvec, config 1, config 3 or one config-4 "
+                         "layer and print its figures")
     ap.add_argument("--c3-experts", type=int, default=128,
                     help="experts of --only c3 (128 = config 3; fewer only for profiling captures)")
     args = ap.parse_args()
@@ -716,6 +763,8 @@ def main():
                 res = bench_matvec(urb, ctx, stream, local, peaks()[0])
             elif args.only == "c1":
                 res = bench_c1(urb, native, ctx, f"cuda:{local}", peaks()[0], syn.rng(SEED + 11))
+            elif args.only == "c4layer":
+                res = bench_c4_layer(urb, native, ctx, local, peaks()[0])
             else:
                 res = bench_c3(urb, native, ctx, f"cuda:{local}", peaks()[0], syn.rng(SEED + 11),
                                args.c3_experts)
