@@ -309,12 +309,17 @@ __device__ __forceinline__ BsSlot slot_of(int fmt, long long boff, int ks, int c
     return z;
 }
 
-// Dynamic shared memory: the unit_begin of every group of the pass (binary-searched by the
-// cooperative unit-map fill).
+// Dynamic shared memory: each routed expert's activation-stage base (s_boff [E + 1]), the
+// unit_begin of every group of the pass (s_ub [2E + 4], binary-searched by the cooperative
+// unit-map fill) and the experts' first columns (s_off [E + 1], binary-searched by the
+// cooperative slot fill, so a large group's slots are not written by one thread).
 __global__ void __launch_bounds__(1024) k_build_tc_segs(TcBuildArgs b) {
     grid_dep_wait();  // programmatic dependent launch: the kernel ahead has completed
     grid_dep_trigger();
-    extern __shared__ int s_ub[];
+    extern __shared__ long long s_dyn[];
+    long long *s_boff = s_dyn;
+    int *s_ub = reinterpret_cast<int *>(s_boff + b.experts + 1);
+    int *s_off = s_ub + 2 * b.experts + 4;
     __shared__ long long wsum[32], sh_boff;
     __shared__ int wcnt[32], wunits[32], s_groups, s_units;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -324,6 +329,7 @@ __global__ void __launch_bounds__(1024) k_build_tc_segs(TcBuildArgs b) {
     }
     const int E = b.experts, TK = b.tokens * b.top_k;
     const int sc = bs_stage_cols(b.fmt);
+    for (int e = tid; e <= E; e += 1024) s_off[e] = b.offsets[e];
     for (int pass = 0; pass < 2; ++pass) {
         const int mats = 1;  // groups per expert (gate/up: one paired group)
         const int ks = pass == 0 ? (b.hidden + sc - 1) / sc : (b.inter + sc - 1) / sc;
@@ -400,11 +406,20 @@ __global__ void __launch_bounds__(1024) k_build_tc_segs(TcBuildArgs b) {
             } else {
                 emit(b.down_tc[e], nullptr, 0, col0, c);
             }
-            // Activation slots of the expert's columns.
-            for (int j = 0; j < c; ++j) sl[col0 + j] = slot_of(b.fmt, boff, ks, c, j);
+            s_boff[e] = boff;  // the expert's activation slots are filled below, by all threads
             boff += bs_group_bytes(b.fmt, c, ks);
         }
         __syncthreads();
+        // Activation slots of the routed columns: column col belongs to the expert e with
+        // s_off[e] <= col < s_off[e + 1].
+        for (int col = tid; col < s_off[E]; col += 1024) {
+            int lo = 0, hi = E - 1;
+            while (lo < hi) {
+                const int mid = (lo + hi + 1) >> 1;
+                if (s_off[mid] <= col) lo = mid; else hi = mid - 1;
+            }
+            sl[col] = slot_of(b.fmt, s_boff[lo], ks, s_off[lo + 1] - s_off[lo], col - s_off[lo]);
+        }
         if (tid == 1023) {
             // gi / ub / boff of the last thread are the routed totals; append the shared expert.
             sh_boff = boff;
@@ -442,7 +457,7 @@ __global__ void __launch_bounds__(1024) k_build_tc_segs(TcBuildArgs b) {
 }  // namespace
 
 int launch_build_tc_segs(Ctx *ctx, const TcBuildArgs &b, cudaStream_t st) {
-    const size_t smem = size_t(2 * b.experts + 4) * sizeof(int);
+    const size_t smem = size_t(b.experts + 1) * sizeof(long long) + size_t(3 * b.experts + 5) * sizeof(int);
     if (smem > 200 * 1024) return set_error(ctx, URB_ERR_UNSUPPORTED, "too many experts for the group builder");
     URB_CUDA(ctx, cudaFuncSetAttribute(k_build_tc_segs, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
     URB_LAUNCH_DEP(k_build_tc_segs, 1, 1024, smem, st, b);
