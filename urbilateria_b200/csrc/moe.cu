@@ -208,6 +208,50 @@ __global__ void k_combine(const float *y, const float *shared_y, const float *w,
     out[size_t(t) * hidden + h] = float(acc);
 }
 
+// The same for hidden % 4 == 0, four columns per thread: the routes' row indices and weights
+// are loaded first, then every route's 16-byte slice, so all of a thread's loads are in flight
+// together (the combine is bound by their latency otherwise).
+__global__ void k_combine4(const float *y, const float *shared_y, const float *w,
+                           const int32_t *inv, int tokens, int top_k, int hidden, float *out,
+                           const int32_t *status) {
+    grid_dep_wait();  // programmatic dependent launch: the kernel ahead has completed
+    grid_dep_trigger();
+    if (status && *status) return;
+    const int t = blockIdx.y;
+    const int h = (blockIdx.x * blockDim.x + threadIdx.x) * 4;
+    if (t >= tokens || h >= hidden) return;
+    double a0 = 0.0, a1 = 0.0, a2 = 0.0, a3 = 0.0;
+    if (shared_y) {
+        const float4 s = *reinterpret_cast<const float4 *>(shared_y + size_t(t) * hidden + h);
+        a0 = s.x; a1 = s.y; a2 = s.z; a3 = s.w;
+    }
+    constexpr int kB = 8;
+    for (int k0 = 0; k0 < top_k; k0 += kB) {
+        int pos[kB];
+        float wk[kB];
+        float4 v[kB];
+#pragma unroll
+        for (int j = 0; j < kB; ++j) {
+            const int k = k0 + j;
+            pos[j] = k < top_k ? (inv ? inv[t * top_k + k] : t * top_k + k) : 0;
+            wk[j] = k < top_k ? w[t * top_k + k] : 0.0f;
+        }
+#pragma unroll
+        for (int j = 0; j < kB; ++j)
+            if (k0 + j < top_k) v[j] = *reinterpret_cast<const float4 *>(y + size_t(pos[j]) * hidden + h);
+#pragma unroll
+        for (int j = 0; j < kB; ++j) {
+            if (k0 + j >= top_k) break;
+            const double wd = wk[j];
+            a0 += wd * double(v[j].x);
+            a1 += wd * double(v[j].y);
+            a2 += wd * double(v[j].z);
+            a3 += wd * double(v[j].w);
+        }
+    }
+    *reinterpret_cast<float4 *>(out + size_t(t) * hidden + h) = make_float4(float(a0), float(a1), float(a2), float(a3));
+}
+
 // DeepSeek-V4 combine: f32 sum of a token's routed rows in ascending expert id (ties keep the
 // route order), the shared row added last, then round to BF16 (deepseek_v4/runtime.rs:2639-2647;
 // the route weights were applied before the down projection).
@@ -503,8 +547,16 @@ int launch_combine(Ctx *ctx, const float *y, const float *shared_y, const float 
                    const int32_t *inv, int tokens, int top_k, int hidden, float *out,
                    cudaStream_t st, const int32_t *status) {
     if (tokens <= 0) return URB_OK;
-    dim3 grid(unsigned((hidden + 255) / 256), unsigned(tokens));
-    URB_LAUNCH_DEP(k_combine, grid, 256, 0, st, y, shared_y, w, inv, tokens, top_k, hidden, out, status);
+    const bool vec = hidden % 4 == 0 && (reinterpret_cast<uintptr_t>(y) & 15) == 0 &&
+                     (reinterpret_cast<uintptr_t>(out) & 15) == 0 &&
+                     (!shared_y || (reinterpret_cast<uintptr_t>(shared_y) & 15) == 0);
+    if (vec) {
+        dim3 grid(unsigned((hidden / 4 + 127) / 128), unsigned(tokens));
+        URB_LAUNCH_DEP(k_combine4, grid, 128, 0, st, y, shared_y, w, inv, tokens, top_k, hidden, out, status);
+    } else {
+        dim3 grid(unsigned((hidden + 255) / 256), unsigned(tokens));
+        URB_LAUNCH_DEP(k_combine, grid, 256, 0, st, y, shared_y, w, inv, tokens, top_k, hidden, out, status);
+    }
     URB_CUDA(ctx, cudaGetLastError());
     return URB_OK;
 }
