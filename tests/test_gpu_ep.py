@@ -28,6 +28,7 @@ def bits(a):
     ("mxfp4", 512, 256, 32, 8, 24, 24),
     ("mxfp4", 320, 192, 8, 2, 37, 64),   # partial tiles, fewer tokens than the window holds
     ("mxfp8", 384, 160, 8, 2, 33, 40),
+    ("bf16", 320, 192, 8, 2, 37, 64),    # BF16 experts (kind::f16 through the tensor maps)
 ])
 def test_ep_one_rank_matches_layer(oracle, ctx, fmt, hidden, inter, experts, top_k, tokens, tmax):
     g = syn.rng(5100 + tokens)
