@@ -172,10 +172,19 @@ int moe_forward_device(Layer *L, const float *d_x, int T, float *d_out, MoeWork 
         if (rc) return cuda_fail(ctx, cudaGetLastError(), "shared expert gate");
     }
     const float *d_gate_logit = qwen ? (num->gate_logit ? num->gate_logit : gate_logit) : nullptr;
+    // Decode (internal routing, tensor-core passes, up to 32 tokens): routing, grouping and
+    // the pass tables run as one kernel after the router logits.
+    const bool fused = !d_ids_in && L->use_tc && T <= 32;
+    const RouterGates rg{ctx, L->d_bias, w.gate, w.sel, d_status};
     if (d_ids_in) {
         // Routes chosen by the caller: the grouping validates the expert ids.
         w.ids = const_cast<int32_t *>(d_ids_in);
         w.w = const_cast<float *>(d_w_in);
+    } else if (fused) {
+        prof_begin(ctx, URB_K_ROUTER_LOGITS, st);
+        rc = launch_router_logits_f64(L->router64, int(E), d_x, T, int(H), w.x64, w.logits, st, &rg);
+        prof_end(ctx, st);
+        if (rc) return cuda_fail(ctx, cudaGetLastError(), "router logits");
     } else {
         rc = route_device(L, d_x, T, w, d_status, st);
         if (rc) return rc;
@@ -231,10 +240,12 @@ int moe_forward_device(Layer *L, const float *d_x, int T, float *d_out, MoeWork 
         p.route_w = w.w;
         p.col_w = w.col_w;
     }
-    prof_begin(ctx, URB_K_PERMUTE, st);
-    rc = launch_permute(ctx, p, st);
-    prof_end(ctx, st);
-    if (rc) return rc;
+    if (!fused) {
+        prof_begin(ctx, URB_K_PERMUTE, st);
+        rc = launch_permute(ctx, p, st);
+        prof_end(ctx, st);
+        if (rc) return rc;
+    }
 
     if (L->use_tc) {
         TcBuildArgs bb{};
@@ -265,9 +276,21 @@ int moe_forward_device(Layer *L, const float *d_x, int T, float *d_out, MoeWork 
         bb.dn_units = w.units_dn;
         bb.scalars = w.tscalars;
         bb.status = d_status;
-        prof_begin(ctx, URB_K_GROUP_BUILD, st);
-        rc = launch_build_tc_segs(ctx, bb, st);
-        prof_end(ctx, st);
+        if (fused) {
+            prof_begin(ctx, URB_K_ROUTE, st);
+            rc = launch_decode_group(ctx, rg, T, int(E), L->geo, w.ids, w.w, w.score, p, bb, st);
+            prof_end(ctx, st);
+            if (rc == URB_ERR_UNSUPPORTED) {  // too many experts for one CTA's shared memory
+                rc = launch_route_noaux(ctx, w.logits, L->d_bias, T, int(E), L->geo, w.ids, w.w, w.score,
+                                        d_status, st, &rg);
+                if (!rc) rc = launch_permute(ctx, p, st);
+                if (!rc) rc = launch_build_tc_segs(ctx, bb, st);
+            }
+        } else {
+            prof_begin(ctx, URB_K_GROUP_BUILD, st);
+            rc = launch_build_tc_segs(ctx, bb, st);
+            prof_end(ctx, st);
+        }
         if (rc) return rc;
 
         // Gate and up projections of every (expert, token) column: [cols, 2I] gate | up.

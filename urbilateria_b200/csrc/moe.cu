@@ -7,7 +7,10 @@
 // (src/models/qwen3_6/runtime.rs:1123-1132), each expert's token run is one or more segments of
 // a grouped pass, and the combine adds the route-weighted expert outputs per token in the
 // reference's selection order with f64 accumulation.
+#include <algorithm>
+
 #include "numerics.cuh"
+#include "route_noaux.cuh"
 #include "urb_internal.cuh"
 #include "urb_moe_internal.cuh"
 
@@ -16,11 +19,9 @@ namespace {
 
 constexpr int kPermThreads = 1024;
 
-// Single-CTA grouping kernel.  See urb_moe_internal.cuh for the outputs.
-__global__ void __launch_bounds__(kPermThreads) k_permute(PermArgs p) {
-    grid_dep_wait();  // programmatic dependent launch: the kernel ahead has completed
-    grid_dep_trigger();
-    extern __shared__ __align__(16) uint8_t smem[];
+// Grouping on one CTA of kPermThreads threads (smem: permute_smem bytes).  See
+// urb_moe_internal.cuh for the outputs.
+__device__ void permute_block(const PermArgs &p, uint8_t *smem) {
     const int E = p.experts, TK = p.tokens * p.top_k;
     int *cnt = reinterpret_cast<int *>(smem);                 // [E]
     int *off = cnt + E;                                        // [E+1]
@@ -187,6 +188,13 @@ __global__ void __launch_bounds__(kPermThreads) k_permute(PermArgs p) {
         if (p.offsets) p.offsets[e] = off[e];
     }
     if (tid == 0 && p.offsets) p.offsets[E] = off[E];
+}
+
+__global__ void __launch_bounds__(kPermThreads) k_permute(PermArgs p) {
+    grid_dep_wait();  // programmatic dependent launch: the kernel ahead has completed
+    grid_dep_trigger();
+    extern __shared__ __align__(16) uint8_t smem[];
+    permute_block(p, smem);
 }
 
 // out[t][h] = f32( f64(shared) + sum_k f64(w[t][k]) * f64(y[inv[t,k]][h]) ), k in selection
@@ -357,10 +365,7 @@ __device__ __forceinline__ BsSlot slot_of(int fmt, long long boff, int ks, int c
 // unit_begin of every group of the pass (s_ub [2E + 4], binary-searched by the cooperative
 // unit-map fill) and the experts' first columns (s_off [E + 1], binary-searched by the
 // cooperative slot fill, so a large group's slots are not written by one thread).
-__global__ void __launch_bounds__(1024) k_build_tc_segs(TcBuildArgs b) {
-    grid_dep_wait();  // programmatic dependent launch: the kernel ahead has completed
-    grid_dep_trigger();
-    extern __shared__ long long s_dyn[];
+__device__ void build_tc_block(const TcBuildArgs &b, long long *s_dyn) {
     long long *s_boff = s_dyn;
     int *s_ub = reinterpret_cast<int *>(s_boff + b.experts + 1);
     int *s_off = s_ub + 2 * b.experts + 4;
@@ -498,10 +503,53 @@ __global__ void __launch_bounds__(1024) k_build_tc_segs(TcBuildArgs b) {
     }
 }
 
+__global__ void __launch_bounds__(1024) k_build_tc_segs(TcBuildArgs b) {
+    grid_dep_wait();  // programmatic dependent launch: the kernel ahead has completed
+    grid_dep_trigger();
+    extern __shared__ long long s_dyn[];
+    build_tc_block(b, s_dyn);
+}
+
+// Decode (tokens <= 32): routing (warp t routes token t), grouping and the tensor-core pass
+// tables in one CTA, each phase reading the previous one's outputs after a block barrier.
+__global__ void __launch_bounds__(1024) k_decode_group(RouteNoauxArgs ra, PermArgs p, TcBuildArgs b) {
+    grid_dep_wait();  // programmatic dependent launch: the kernel ahead has completed
+    grid_dep_trigger();
+    extern __shared__ __align__(16) uint8_t smem[];
+    const int warp = threadIdx.x >> 5;
+    if (warp < ra.tokens) route_noaux_token<true>(ra, warp, smem + size_t(warp) * ra.warp_bytes);
+    __syncthreads();
+    permute_block(p, smem);
+    __syncthreads();
+    build_tc_block(b, reinterpret_cast<long long *>(smem));
+}
+
+size_t permute_smem(int experts) {
+    const size_t v = size_t(experts) * 4 * 3 + 4 + size_t(32) * experts * 2;
+    return (v + 15) & ~size_t(15);
+}
+size_t build_smem(int experts) {
+    return size_t(experts + 1) * sizeof(long long) + size_t(3 * experts + 5) * sizeof(int);
+}
+
 }  // namespace
 
+int launch_decode_group(Ctx *ctx, const RouterGates &rg, int tokens, int experts, const urb_moe_geometry &g,
+                        int32_t *d_expert, float *d_weight, float *d_score, const PermArgs &p,
+                        const TcBuildArgs &b, cudaStream_t st) {
+    if (tokens < 1 || tokens > 32) return URB_ERR_UNSUPPORTED;
+    const RouteNoauxArgs ra = route_noaux_args(ctx, nullptr, nullptr, tokens, experts, g, d_expert, d_weight,
+                                               d_score, rg.status, &rg);
+    const size_t smem = std::max(std::max(size_t(tokens) * ra.warp_bytes, permute_smem(experts)), build_smem(experts));
+    if (smem > 200 * 1024) return URB_ERR_UNSUPPORTED;
+    URB_CUDA(ctx, cudaFuncSetAttribute(k_decode_group, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
+    URB_LAUNCH_DEP(k_decode_group, 1, 1024, smem, st, ra, p, b);
+    URB_CUDA(ctx, cudaGetLastError());
+    return URB_OK;
+}
+
 int launch_build_tc_segs(Ctx *ctx, const TcBuildArgs &b, cudaStream_t st) {
-    const size_t smem = size_t(b.experts + 1) * sizeof(long long) + size_t(3 * b.experts + 5) * sizeof(int);
+    const size_t smem = build_smem(b.experts);
     if (smem > 200 * 1024) return set_error(ctx, URB_ERR_UNSUPPORTED, "too many experts for the group builder");
     URB_CUDA(ctx, cudaFuncSetAttribute(k_build_tc_segs, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
     URB_LAUNCH_DEP(k_build_tc_segs, 1, 1024, smem, st, b);
@@ -510,8 +558,7 @@ int launch_build_tc_segs(Ctx *ctx, const TcBuildArgs &b, cudaStream_t st) {
 }
 
 int launch_permute(Ctx *ctx, const PermArgs &p, cudaStream_t st) {
-    size_t smem = size_t(p.experts) * 4 * 3 + 4 + size_t(32) * p.experts * 2;
-    smem = (smem + 15) & ~size_t(15);
+    const size_t smem = permute_smem(p.experts);
     if (smem > 200 * 1024) return set_error(ctx, URB_ERR_UNSUPPORTED, "too many experts for the grouping kernel");
     URB_CUDA(ctx, cudaFuncSetAttribute(k_permute, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
     URB_LAUNCH_DEP(k_permute, 1, kPermThreads, smem, st, p);

@@ -15,6 +15,7 @@
 //    reference's order, libm-exact expf, total_cmp ranking with the lower id winning ties.
 #include "expf_glibc.cuh"
 #include "numerics.cuh"
+#include "route_noaux.cuh"
 #include "tc_common.cuh"
 #include "urb_internal.cuh"
 
@@ -180,164 +181,16 @@ __device__ __forceinline__ void set_status(int32_t *status, int code) {
     if (status) atomicCAS(status, 0, int32_t(code));
 }
 
-// One warp per token.  Shared memory per warp (warp_bytes): gate[E], sel[E], group score
-// [n_group] floats, then one flag byte per expert (1 allowed, 2 taken, 0 masked).  PRE: the
-// gates and selection scores come precomputed (logits kernel epilogue, which also reported
-// non-finite logits or biases) in `logits` / `bias` as [tokens, E] arrays.
+// One warp per token (route_noaux_token).
 template <bool PRE>
-__global__ void k_route_noaux(const float *logits, const float *bias, int tokens, int E,
-                              int top_k, int n_group, int topk_group, int normalize,
-                              float scaling, ExpfTable tab, int32_t *out_e, float *out_w,
-                              float *out_s, int32_t *status, int warp_bytes) {
+__global__ void k_route_noaux(RouteNoauxArgs ra) {
     grid_dep_wait();  // programmatic dependent launch: the kernel ahead has completed
     grid_dep_trigger();
     extern __shared__ __align__(16) uint8_t smem[];
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5;
     const int t = blockIdx.x * (blockDim.x >> 5) + warp;
-    if (t >= tokens) return;
-    float *gate = reinterpret_cast<float *>(smem + size_t(warp) * warp_bytes);
-    float *sel = gate + E;
-    float *gscore = sel + E;
-    uint8_t *flags = reinterpret_cast<uint8_t *>(gscore + n_group);
-    const float *lg = logits + size_t(t) * E;
-    bool bad = false;
-    if (PRE) {
-        const float *sg = bias + size_t(t) * E;
-        for (int i = lane; i < E; i += 32) {
-            gate[i] = lg[i];
-            sel[i] = sg[i];
-            flags[i] = 1;
-        }
-    }
-    // routing.rs:103: gate = 1 / (1 + exp(-logit)).  Eight experts per lane at a time, with all
-    // of their exception-table loads issued before any is used (independent, in flight together).
-    constexpr int kB = 8;
-    for (int i0 = 0; !PRE && i0 < E; i0 += 32 * kB) {
-        float l[kB], b[kB];
-        uint32_t lo[kB], hi[kB];
-#pragma unroll
-        for (int j = 0; j < kB; ++j) {
-            const int i = i0 + 32 * j + lane;
-            l[j] = i < E ? lg[i] : 0.0f;
-            b[j] = i < E ? bias[i] : 0.0f;
-        }
-#pragma unroll
-        for (int j = 0; j < kB; ++j) {
-            const uint32_t bucket = __float_as_uint(-l[j]) >> 12;
-            lo[j] = tab.index ? tab.index[bucket] : 0;
-            hi[j] = tab.index ? tab.index[bucket + 1] : 0;
-        }
-#pragma unroll
-        for (int j = 0; j < kB; ++j) {
-            const int i = i0 + 32 * j + lane;
-            if (i >= E) continue;
-            bad |= !isfinite(l[j]) || !isfinite(b[j]);
-            const float ex = expf_libm_range(-l[j], tab, lo[j], hi[j]);
-            const float gv = __fdiv_rn(1.0f, __fadd_rn(1.0f, ex));
-            gate[i] = gv;
-            sel[i] = __fadd_rn(gv, b[j]);
-            flags[i] = 1;
-        }
-    }
-    if (__any_sync(0xffffffffu, bad)) {
-        // Rejected token: report, and leave distinct valid ids with zero weight so that the
-        // rest of a device pipeline stays in bounds (it short-circuits on the status anyway).
-        if (lane == 0) set_status(status, URB_ERR_NONFINITE);
-        for (int r = lane; r < top_k; r += 32) {
-            out_e[size_t(t) * top_k + r] = r;
-            out_w[size_t(t) * top_k + r] = 0.0f;
-            if (out_s) out_s[size_t(t) * top_k + r] = 0.0f;
-        }
-        return;
-    }
-    __syncwarp();
-    if (n_group > 1) {
-        // routing.rs:112-129: group score = sum of the two largest selections (total order).
-        const int gs = E / n_group;
-        for (int grp = lane; grp < n_group; grp += 32) {
-            int32_t k1 = INT32_MIN, k2 = INT32_MIN;
-            float v1 = 0.0f, v2 = 0.0f;
-            for (int i = grp * gs; i < (grp + 1) * gs; ++i) {
-                int32_t k = total_key(sel[i]);
-                if (k > k1) { k2 = k1; v2 = v1; k1 = k; v1 = sel[i]; }
-                else if (k > k2) { k2 = k; v2 = sel[i]; }
-            }
-            gscore[grp] = __fadd_rn(v1, v2);
-        }
-        __syncwarp();
-        // Groups ranked by score desc, lower group id first; the best topk_group stay allowed.
-        for (int grp = lane; grp < n_group; grp += 32) {
-            const int32_t kg = total_key(gscore[grp]);
-            int rank = 0;
-            for (int o = 0; o < n_group; ++o)
-                if (better(total_key(gscore[o]), o, kg, grp)) ++rank;
-            const uint8_t allowed = rank < topk_group ? 1 : 0;
-            for (int i = grp * gs; i < (grp + 1) * gs; ++i) flags[i] = allowed;
-        }
-        __syncwarp();
-    }
-    // routing.rs:131-141: top_k by selection desc, lower id wins ties.  The chosen ids go
-    // straight to the output row; lane 0 accumulates the f32 denominator in ranking order.
-    int32_t *oe = out_e + size_t(t) * top_k;
-    float den = -0.0f;
-    // Up to 512 experts: each lane keeps the keys of experts lane + 32 j in registers
-    // (INT32_MIN marks masked or taken experts; no finite selection score has that key).
-    constexpr int kRegKeys = 16;
-    const bool in_regs = E <= 32 * kRegKeys;
-    int32_t kr[kRegKeys];
-#pragma unroll
-    for (int j = 0; j < kRegKeys; ++j) {
-        const int i = lane + 32 * j;
-        kr[j] = in_regs && i < E && flags[i] == 1 ? total_key(sel[i]) : INT32_MIN;
-    }
-    for (int r = 0; r < top_k; ++r) {
-        int32_t key = INT32_MIN;
-        int id = INT32_MAX;
-        if (in_regs) {
-#pragma unroll
-            for (int j = 0; j < kRegKeys; ++j)
-                if (kr[j] != INT32_MIN && better(kr[j], lane + 32 * j, key, id)) { key = kr[j]; id = lane + 32 * j; }
-        } else {
-            for (int i = lane; i < E; i += 32) {
-                if (flags[i] == 1) {
-                    int32_t k = total_key(sel[i]);
-                    if (better(k, i, key, id)) { key = k; id = i; }
-                }
-            }
-        }
-        warp_best(key, id);
-        if (id == INT32_MAX) {  // fewer allowed experts than top_k
-            if (lane == 0) set_status(status, URB_ERR_INVALID_GEOMETRY);
-            for (int r2 = lane; r2 < top_k; r2 += 32) {
-                out_e[size_t(t) * top_k + r2] = r2;
-                out_w[size_t(t) * top_k + r2] = 0.0f;
-            }
-            return;
-        }
-        if (lane == (id & 31)) flags[id] = 2;
-#pragma unroll
-        for (int j = 0; j < kRegKeys; ++j)
-            if (lane + 32 * j == id) kr[j] = INT32_MIN;
-        if (lane == 0) {
-            oe[r] = id;
-            den = __fadd_rn(den, gate[id]);
-        }
-        __syncwarp();
-    }
-    if (lane == 0) {
-        den = __fadd_rn(den, 1e-20f);  // routing.rs:143-146
-        if (normalize && !isfinite(den)) {
-            set_status(status, URB_ERR_NONFINITE);
-            return;
-        }
-    }
-    den = __shfl_sync(0xffffffffu, den, 0);
-    for (int r = lane; r < top_k; r += 32) {
-        const int id = oe[r];
-        const float w = normalize ? __fdiv_rn(gate[id], den) : gate[id];
-        out_w[size_t(t) * top_k + r] = __fmul_rn(w, scaling);
-        if (out_s) out_s[size_t(t) * top_k + r] = sel[id];
-    }
+    if (t >= ra.tokens) return;
+    route_noaux_token<PRE>(ra, t, smem + size_t(warp) * ra.warp_bytes);
 }
 
 // route_softmax_top_k (src/models/qwen3_8/moe.rs:108-158).  One warp per token.
@@ -525,10 +378,9 @@ int launch_route_noaux(Ctx *ctx, const float *d_logits, const float *d_bias, int
     int warp_bytes = int(((2 * size_t(experts) + g.n_group) * 4 + experts + 15) & ~size_t(15));
     size_t smem = size_t(warps) * warp_bytes;
     auto k = pre ? k_route_noaux<true> : k_route_noaux<false>;
-    URB_LAUNCH_DEP(k, (tokens + warps - 1) / warps, warps * 32, smem, st,
-        pre ? pre->gate : d_logits, pre ? pre->sel : d_bias, tokens, experts, int(g.top_k),
-        int(g.n_group), int(g.topk_group), g.normalize, g.routed_scaling_factor, table_of(ctx),
-        d_expert, d_weight, d_score, d_status, warp_bytes);
+    const RouteNoauxArgs ra = route_noaux_args(ctx, d_logits, d_bias, tokens, experts, g, d_expert, d_weight,
+                                               d_score, d_status, pre);
+    URB_LAUNCH_DEP(k, (tokens + warps - 1) / warps, warps * 32, smem, st, ra);
     URB_CUDA(ctx, cudaGetLastError());
     return URB_OK;
 }

@@ -51,6 +51,11 @@ struct TcBuildArgs {
     const int32_t *status;  // non-zero: an earlier stage failed; build no work
 };
 int launch_build_tc_segs(Ctx *ctx, const TcBuildArgs &b, cudaStream_t st);
+// Decode (1..32 tokens): route_noaux_tc over the router epilogue's gates (rg), the grouping
+// `p` (whose ids are d_expert) and the tensor-core tables `b`, in one single-CTA launch.
+int launch_decode_group(Ctx *ctx, const RouterGates &rg, int tokens, int experts, const urb_moe_geometry &g,
+                        int32_t *d_expert, float *d_weight, float *d_score, const PermArgs &p,
+                        const TcBuildArgs &b, cudaStream_t st);
 int launch_combine(Ctx *ctx, const float *y, const float *shared_y, const float *w,
                    const int32_t *inv, int tokens, int top_k, int hidden, float *out,
                    cudaStream_t st, const int32_t *status = nullptr);
