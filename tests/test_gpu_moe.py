@@ -135,3 +135,22 @@ def test_bf16_layer_runs_the_tensor_core_passes(oracle, ctx):
     o_out, o_ids, _, _, _ = orc.forward(x)
     assert np.array_equal(ids, o_ids)
     assert_close(out, o_out)
+
+
+@pytest.mark.parametrize("experts,tokens", [(64, 32), (768, 32)])
+def test_decode_grouping_kernel_and_its_fallback(oracle, ctx, experts, tokens):
+    # Up to 32 tokens route, group and build the pass tables in one CTA (k_decode_group);
+    # with 768 experts its per-token routing scratch no longer fits one CTA's shared memory
+    # and the separate routing / grouping / table kernels run instead.  Routes, counts and
+    # the permutation bit-exact, outputs within the bar, either way.
+    g = syn.rng(7000 + experts)
+    dev, orc = build_layer(oracle, ctx, g, 256, 128, experts, "mxfp4", top_k=8, scale=1.0)
+    x = syn.normal_bf16_as_f32(g, (tokens, 256))
+    out, ids, w, extra = dev.forward_batch(x, tokens, details=True)
+    o_out, o_ids, o_w, _, _ = orc.forward(x)
+    assert np.array_equal(ids, o_ids)
+    assert np.array_equal(w.view(np.uint32), o_w.view(np.uint32))
+    counts, offsets, pt, ps = oracle.group_routes(o_ids, experts)
+    assert np.array_equal(extra["counts"], counts)
+    assert np.array_equal(extra["perm_token"], pt) and np.array_equal(extra["perm_slot"], ps)
+    assert_close(out, o_out)
