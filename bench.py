@@ -463,6 +463,50 @@ def c4_weights(urb, ctx, dev, layer, held, experts=384):
     return routed, shared, router, syn.normal_f32(g, experts, 0.01)
 
 
+def bench_bf16_layer(urb, native, ctx, local, pk_hbm, tokens=128):
+    """A Qwen3.6-A3B-shaped BF16 MoE layer (hidden 2048, 128 BF16 experts of intermediate 768,
+    top-8 + a shared expert, bf16 router ~ N(0, 0.02), weights ~ N(0, 0.02)): the layer forward
+    on the tcgen05 kind::f16 grouped passes, tokens/s and the per-kernel device times."""
+    import torch
+    from urbilateria_b200 import synthetic as syn
+    dev = f"cuda:{local}"
+    H, I, E, K = 2048, 768, 128, 8
+    g = syn.rng(SEED + 19)
+
+    def mlp():
+        return urb.GatedMlp(urb.Bf16Matrix.from_bits(I, H, syn.bf16_normal(g, (I, H), 0.02), ctx=ctx),
+                            urb.Bf16Matrix.from_bits(I, H, syn.bf16_normal(g, (I, H), 0.02), ctx=ctx),
+                            urb.Bf16Matrix.from_bits(H, I, syn.bf16_normal(g, (H, I), 0.02), ctx=ctx))
+    experts = [mlp() for _ in range(E)]
+    shared = mlp()
+    router = urb.Bf16Matrix.from_bits(E, H, syn.bf16_normal(g, (E, H), 0.02), ctx=ctx)
+    layer = urb.RuntimeMoeLayer(router, syn.normal_f32(g, E, 0.01), experts, shared,
+                                urb.MoeGeometry(K, 1, 1, True, 1.0))
+    d_x = torch.from_numpy(syn.normal_bf16_as_f32(g, (tokens, H))).to(dev)
+    d_y = torch.empty_like(d_x)
+    st = torch.zeros(1, dtype=torch.int32, device=dev)
+
+    def fn():
+        layer.forward_device(d_x.data_ptr(), tokens, d_y.data_ptr(), 0, 0, st.data_ptr())
+    for _ in range(5):
+        fn()
+    k_ms, s_ms, n = kernel_ms(ctx, native, fn, 20)
+    if int(st.item()) != 0:
+        raise RuntimeError("BF16 layer forward reported status %d" % int(st.item()))
+    per_expert = 3 * H * I * 2
+    out = {"workload": "Qwen3.6-A3B-shaped BF16 MoE layer: hidden 2048, 128 experts inter 768 top-8 + "
+                       "shared, %d tokens" % tokens,
+           "stream_us": s_ms * 1e3, "kernel_us": k_ms * 1e3, "launches": n,
+           "tokens_per_s": tokens / (s_ms / 1e3), "kernels_us": kernel_ms.per_kind,
+           "weight_bytes": (E + 1) * per_expert}
+    layer.free()
+    for e in experts + [shared]:
+        for m in (e.gate, e.up, e.down):
+            m.free()
+    router.free()
+    return out
+
+
 def bench_c4_layer(urb, native, ctx, local, pk_hbm):
     """One config-4 layer (384 MXFP4 experts + shared, hidden 7168) at B = 1 and 8: the graph
     time of one forward and the library's per-kernel device times (for profiling the decode
@@ -726,9 +770,9 @@ def main():
                     help="tokens per GPU (128 = config 2; other values only for profiling)")
     ap.add_argument("--int-only", action="store_true",
                     help="profiling: time only the INT4 / INT8 products and print their figures")
-    ap.add_argument("--only", choices=["matvec", "c1", "c3", "c4layer"],
-                    help="profiling: time only the config-0 matvec, config 1, config 3 or one config-4 "
-                         "layer and print its figures")
+    ap.add_argument("--only", choices=["matvec", "c1", "c3", "c4layer", "bf16layer"],
+                    help="profiling: time only the config-0 matvec, config 1, config 3, one config-4 "
+                         "layer or a BF16 (Qwen3.6-shaped) layer and print its figures")
     ap.add_argument("--c3-experts", type=int, default=128,
                     help="experts of --only c3 (128 = config 3; fewer only for profiling captures)")
     args = ap.parse_args()
@@ -765,6 +809,8 @@ def main():
                 res = bench_c1(urb, native, ctx, f"cuda:{local}", peaks()[0], syn.rng(SEED + 11))
             elif args.only == "c4layer":
                 res = bench_c4_layer(urb, native, ctx, local, peaks()[0])
+            elif args.only == "bf16layer":
+                res = bench_bf16_layer(urb, native, ctx, local, peaks()[0])
             else:
                 res = bench_c3(urb, native, ctx, f"cuda:{local}", peaks()[0], syn.rng(SEED + 11),
                                args.c3_experts)
