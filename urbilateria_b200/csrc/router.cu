@@ -46,6 +46,12 @@ __device__ __forceinline__ double widen(const void *w, size_t idx) {
                 : double(static_cast<const float *>(w)[idx]);
 }
 
+__device__ __forceinline__ double lds_f64(uint32_t addr) {
+    double v;
+    asm volatile("ld.shared.f64 %0, [%1];" : "=d"(v) : "r"(addr));
+    return v;
+}
+
 __device__ __forceinline__ void dmma_8x8x4(double &d0, double &d1, double a, double b) {
     asm volatile("mma.sync.aligned.m8n8k4.row.col.f64.f64.f64.f64 {%0,%1}, {%2}, {%3}, {%0,%1};"
                  : "+d"(d0), "+d"(d1)
@@ -74,24 +80,27 @@ __global__ void k_to_f64_blocked(const void *src, int rows, int cols, double *ds
     }
 }
 
-// One warp per 8 tokens x 8 experts (a block), one warp per CTA, so the 512 blocks of a
+// One chain warp per 8 tokens x 8 experts (a block), one block per CTA, so the 512 blocks of a
 // 128-token, 256-expert forward spread over every SM.  A = x (row: token, k: column), B =
 // router (k: column, n: expert); lane q holds A[q/4][q%4], B[q%4][q/4] and D[q/4][2(q%4) .. +1].
 // Each chain is one dependent MMA per four columns, so the kernel is bound by the MMA latency
 // as long as its operands are already in shared memory: the block's x tile and router tile of
-// each kRc-column chunk arrive by two 1-D TMA bulk copies, kRnb chunks ahead, each stage
-// completing on its own mbarrier; a stage is refilled only after the MMAs that read it have
-// been issued.  The padded rows make a lane's 8-byte reads conflict-free (lanes 0-15 and 16-31
-// each cover the 32 banks once).  In the last, partial chunk the columns past the last multiple
-// of four are added with scalar FMAs, in order.
-__global__ void __launch_bounds__(32) k_router_dmma(const double *x64b, const double *w64b,
+// each kRc-column chunk arrive by two 1-D TMA bulk copies, NB chunks ahead, each stage
+// completing on its own mbarrier.  A second warp issues the copies and refills a stage once
+// the chain warp has released it, so the chain warp's instruction stream holds nothing but
+// the waits, the operand loads and the MMAs.  The padded rows make a lane's 8-byte reads
+// conflict-free (lanes 0-15 and 16-31 each cover the 32 banks once).  In the last, partial
+// chunk the columns past the last multiple of four are added with scalar FMAs, in order.
+template <int NB>
+__global__ void __launch_bounds__(64) k_router_dmma(const double *x64b, const double *w64b,
                                                     int tokens, int experts, int cols,
                                                     float *logits, GateOut go, int32_t *status) {
     grid_dep_wait();  // programmatic dependent launch: the kernel ahead has completed
     grid_dep_trigger();
     extern __shared__ __align__(16) double rs[];
-    uint64_t *full = reinterpret_cast<uint64_t *>(rs + kRnb * kRstage);
-    const int lane = threadIdx.x;
+    uint64_t *full = reinterpret_cast<uint64_t *>(rs + NB * kRstage);
+    uint64_t *empty = full + NB;  // the chain warp has read the stage
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int eblk = (experts + 7) / 8;
     const int blk = blockIdx.x;
     if (blk >= eblk * ((tokens + 7) / 8)) return;
@@ -100,33 +109,53 @@ __global__ void __launch_bounds__(32) k_router_dmma(const double *x64b, const do
     constexpr uint32_t kTile = 8 * kRrow * 8;  // bytes of one operand's tile
     const double *xsrc = x64b + size_t(tb) * nch * 8 * kRrow;
     const double *wsrc = w64b + size_t(eb) * nch * 8 * kRrow;
-    auto issue = [&](int ch) {  // one lane
-        double *dst = rs + (ch % kRnb) * kRstage;
-        uint64_t *bar = &full[ch % kRnb];
-        tc::mbar_arrive_expect_tx(bar, 2 * kTile);
-        tc::bulk_g2s(dst, xsrc + size_t(ch) * 8 * kRrow, kTile, bar);
-        tc::bulk_g2s(dst + 8 * kRrow, wsrc + size_t(ch) * 8 * kRrow, kTile, bar);
-    };
-    if (lane == 0) {
-        for (int s = 0; s < kRnb; ++s) tc::mbar_init(&full[s], 1);
+    // x rows of the block's real tokens only (a prefix of the tile; the rows past them feed
+    // only outputs that are not stored).
+    const uint32_t xbytes = uint32_t(min(8, tokens - tb * 8)) * kRrow * 8;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < NB; ++s) {
+            tc::mbar_init(&full[s], 1);
+            tc::mbar_init(&empty[s], 1);
+        }
         tc::mbar_fence_init();
-        for (int s = 0; s < kRnb && s < nch; ++s) issue(s);
     }
-    __syncwarp();
+    __syncthreads();
+    volatile int never = 0;
+    if (warp == 1) {
+        // Copy warp (one lane): stage ch once the chain warp has read chunk ch - NB from it.
+        if (lane == 0) {
+            int ch = 0;
+            for (; ch < nch; ++ch) {
+                if (ch >= NB && !tc::mbar_wait(&empty[ch % NB], uint32_t(ch / NB - 1) & 1u, &never)) break;
+                double *dst = rs + (ch % NB) * kRstage;
+                uint64_t *bar = &full[ch % NB];
+                tc::mbar_arrive_expect_tx(bar, xbytes + kTile);
+                tc::bulk_g2s(dst, xsrc + size_t(ch) * 8 * kRrow, xbytes, bar);
+                tc::bulk_g2s(dst + 8 * kRrow, wsrc + size_t(ch) * 8 * kRrow, kTile, bar);
+            }
+            // Every copy this CTA issued lands before it can exit.
+            for (int c = ch > NB ? ch - NB : 0; c < ch; ++c)
+                tc::mbar_wait(&full[c % NB], uint32_t(c / NB) & 1u, &never);
+        }
+        return;
+    }
+    // Chain warp: nothing but the waits, the operand loads and the MMAs.
     const int r = lane >> 2, kq = lane & 3;
     double d0 = -0.0, d1 = -0.0;  // Iterator::sum over f64 starts from -0.0 (bf16.rs:500)
-    volatile int never = 0;
     int ch = 0;
     for (; ch < nch; ++ch) {
-        if (!tc::mbar_wait(&full[ch % kRnb], uint32_t(ch / kRnb) & 1u, &never)) break;
-        const double *b = rs + (ch % kRnb) * kRstage;
+        if (!tc::mbar_wait(&full[ch % NB], uint32_t(ch / NB) & 1u, &never)) break;
+        const double *b = rs + (ch % NB) * kRstage;
         const int kc = min(kRc, cols - ch * kRc);
         if (kc == kRc) {
+            // Shared-space loads (ld.shared; generic loads of the stage measured a long
+            // scoreboard stall per step), kept after the stage's wait by being volatile.
+            const uint32_t xa = tc::smem_u32(b + r * kRrow + kq), wa = tc::smem_u32(b + (8 + r) * kRrow + kq);
             double a[kRc / 4], w[kRc / 4];
 #pragma unroll
             for (int i = 0; i < kRc / 4; ++i) {
-                a[i] = b[r * kRrow + 4 * i + kq];
-                w[i] = b[(8 + r) * kRrow + 4 * i + kq];
+                a[i] = lds_f64(xa + 32u * i);
+                w[i] = lds_f64(wa + 32u * i);
             }
 #pragma unroll
             for (int i = 0; i < kRc / 4; ++i) dmma_8x8x4(d0, d1, a[i], w[i]);
@@ -140,15 +169,14 @@ __global__ void __launch_bounds__(32) k_router_dmma(const double *x64b, const do
                 d1 = fma(b[(9 + 2 * kq) * kRrow + k], xv, d1);
             }
         }
+        // Every lane's reads of the stage have been consumed by issued MMAs.
         __syncwarp();
-        if (lane == 0 && ch + kRnb < nch) issue(ch + kRnb);
+        if (lane == 0) tc::mbar_arrive(&empty[ch % NB]);
     }
     if (ch < nch) {
-        // A stage never completed: report, let the copies still in flight land (bounded), and
-        // leave without writing logits.
+        // A stage never completed: report and leave without writing logits (the copy warp
+        // lets the copies still in flight land).
         if (lane == 0 && status) atomicCAS(status, 0, int32_t(URB_ERR_TIMEOUT));
-        for (int c = ch; c < nch && c < ch + kRnb; ++c)
-            tc::mbar_wait(&full[c % kRnb], uint32_t(c / kRnb) & 1u, &never);
         return;
     }
     const int t = tb * 8 + r, e0 = eb * 8 + 2 * kq;
@@ -360,11 +388,15 @@ int launch_router_logits_f64(const double *w64b, int experts, const float *d_x, 
     if (rg) go = GateOut{rg->bias, rg->gate, rg->sel, rg->status, table_of(rg->ctx)};
     auto widen = k_to_f64_blocked<false>;
     URB_LAUNCH_DEP(widen, 592, 256, 0, st, d_x, tokens, cols, x64b);
+    // Stages in flight: 3 when the blocks fill the SMs several times over (four CTAs of 51 KB
+    // per SM), 8 for the few blocks of a decode step (one CTA of 135 KB per SM).
     const int blocks = ((tokens + 7) / 8) * ((experts + 7) / 8);
-    cudaError_t e = cudaFuncSetAttribute(k_router_dmma, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         kRsmem);
+    const bool deep = blocks <= 256;
+    auto k = deep ? k_router_dmma<8> : k_router_dmma<kRnb>;
+    const int smem = router_smem(deep ? 8 : kRnb);
+    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return URB_ERR_CUDA;
-    URB_LAUNCH_DEP(k_router_dmma, blocks, 32, kRsmem, st, x64b, w64b, tokens, experts, cols, d_logits, go,
+    URB_LAUNCH_DEP(k, blocks, 64, smem, st, x64b, w64b, tokens, experts, cols, d_logits, go,
                    rg ? rg->status : nullptr);
     return cudaGetLastError() == cudaSuccess ? URB_OK : URB_ERR_CUDA;
 }

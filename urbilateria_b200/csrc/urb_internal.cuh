@@ -217,9 +217,9 @@ int launch_route_noaux(Ctx *ctx, const float *d_logits, const float *d_bias, int
 // logits are bit-identical to the sequential F64 chain.
 constexpr int kRc = 128;                  // columns per chunk (one shared-memory stage)
 constexpr int kRrow = kRc + 4;            // doubles per staged row
-constexpr int kRnb = 3;                   // stages in flight per block
+constexpr int kRnb = 3;                   // stages in flight per block (many blocks)
 constexpr int kRstage = 16 * kRrow;       // doubles per stage (x tile + router tile)
-constexpr int kRsmem = kRnb * kRstage * 8 + kRnb * 8;
+__host__ __device__ constexpr int router_smem(int nb) { return nb * kRstage * 8 + 2 * nb * 8; }
 __host__ __device__ constexpr int router_chunks(int cols) { return (cols + kRc - 1) / kRc; }
 __host__ __device__ constexpr size_t router_f64_elems(int rows, int cols) {
     return size_t((rows + 7) / 8) * router_chunks(cols) * 8 * kRrow;
