@@ -356,7 +356,10 @@ int urb_ctx_create(int device, urb_ctx **out) {
         return URB_ERR_CUDA;
     }
     ctx->own_stream = true;
-    if (cudaMalloc(&ctx->d_status, sizeof(int32_t)) != cudaSuccess || expf_table_init(ctx) != URB_OK) {
+    if (cudaStreamCreateWithFlags(&ctx->aux, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaEventCreateWithFlags(&ctx->ev_fork, cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&ctx->ev_join, cudaEventDisableTiming) != cudaSuccess ||
+        cudaMalloc(&ctx->d_status, sizeof(int32_t)) != cudaSuccess || expf_table_init(ctx) != URB_OK) {
         urb_ctx_destroy(ctx);
         return URB_ERR_CUDA;
     }
@@ -368,6 +371,7 @@ int urb_ctx_destroy(urb_ctx *ctx) {
     if (!ctx) return URB_ERR_INVALID_ARGUMENT;
     cudaSetDevice(ctx->device);
     if (ctx->stream) cudaStreamSynchronize(ctx->stream);
+    if (ctx->aux) cudaStreamSynchronize(ctx->aux);
     if (ctx->ws) cudaFree(ctx->ws);
     if (ctx->io) cudaFree(ctx->io);
     if (ctx->d_status) cudaFree(ctx->d_status);
@@ -375,6 +379,9 @@ int urb_ctx_destroy(urb_ctx *ctx) {
     if (ctx->log1pf_keys) cudaFree(const_cast<uint32_t *>(ctx->log1pf_keys));
     if (ctx->pinned) cudaFreeHost(ctx->pinned);
     if (ctx->own_stream && ctx->stream) cudaStreamDestroy(ctx->stream);
+    if (ctx->aux) cudaStreamDestroy(ctx->aux);
+    if (ctx->ev_fork) cudaEventDestroy(ctx->ev_fork);
+    if (ctx->ev_join) cudaEventDestroy(ctx->ev_join);
     delete ctx;
     return URB_OK;
 }

@@ -769,7 +769,7 @@ __global__ void k_repack_bs(const uint8_t *values, const uint8_t *scales, size_t
 }
 
 template <int FMT, int NT>
-int launch_bs_t(Ctx *ctx, const TcArgs &a, int kind, cudaStream_t st) {
+int launch_bs_prep_t(Ctx *ctx, const TcArgs &a, cudaStream_t st) {
     static_assert(NT <= bs_rows_per_tok(FMT), "terms fit in a token's MMA rows");
     constexpr int KBS = FMT == URB_FMT_MXFP4 ? 8 : (FMT == URB_FMT_MXFP8 ? 4 : 2);
     const long long threads = (long long)a.nrows * a.ks * KBS * 4;
@@ -779,6 +779,15 @@ int launch_bs_t(Ctx *ctx, const TcArgs &a, int kind, cudaStream_t st) {
         URB_LAUNCH_DEP(prep, unsigned((threads + 255) / 256), 256, 0, st, a);
         prof_end(ctx, st);
         URB_CUDA(ctx, cudaGetLastError());
+    }
+    return URB_OK;
+}
+
+template <int FMT, int NT>
+int launch_bs_t(Ctx *ctx, const TcArgs &a, int kind, cudaStream_t st) {
+    if (!a.skip_prep) {
+        const int rc = launch_bs_prep_t<FMT, NT>(ctx, a, st);
+        if (rc) return rc;
     }
     auto k = a.pair == 1 ? k_bs_grouped<FMT, 1, NT>
                          : (a.pair == 2 ? k_bs_grouped<FMT, 2, NT> : k_bs_grouped<FMT, 0, NT>);
@@ -802,6 +811,15 @@ int launch_tc_grouped(Ctx *ctx, int fmt, const TcArgs &a, int kind, cudaStream_t
         return launch_bs_t<URB_FMT_BF16, bs_terms(URB_FMT_BF16)>(ctx, a, kind, st);
     }
     return set_error(ctx, URB_ERR_UNSUPPORTED, "tc pass: format");
+}
+
+int launch_tc_prep(Ctx *ctx, int fmt, const TcArgs &a, cudaStream_t st) {
+    if (fmt == URB_FMT_MXFP4 && a.full_terms)
+        return launch_bs_prep_t<URB_FMT_MXFP4, bs_rows_per_tok(URB_FMT_MXFP4)>(ctx, a, st);
+    if (fmt == URB_FMT_MXFP4) return launch_bs_prep_t<URB_FMT_MXFP4, bs_terms(URB_FMT_MXFP4)>(ctx, a, st);
+    if (fmt == URB_FMT_MXFP8) return launch_bs_prep_t<URB_FMT_MXFP8, bs_terms(URB_FMT_MXFP8)>(ctx, a, st);
+    if (fmt == URB_FMT_BF16 && !a.sim128) return launch_bs_prep_t<URB_FMT_BF16, bs_terms(URB_FMT_BF16)>(ctx, a, st);
+    return set_error(ctx, URB_ERR_UNSUPPORTED, "tc prep: format");
 }
 
 int repack_tc(Ctx *ctx, Mat *m, cudaStream_t st) {

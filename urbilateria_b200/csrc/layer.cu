@@ -175,12 +175,33 @@ int moe_forward_device(Layer *L, const float *d_x, int T, float *d_out, MoeWork 
     // Decode (internal routing, tensor-core passes, up to 32 tokens): routing, grouping and
     // the pass tables run as one kernel after the router logits.
     const bool fused = !d_ids_in && L->use_tc && T <= 32;
+    const bool x_ahead = fused && T == 1 && L->d_xslot && ctx->aux;
     const RouterGates rg{ctx, L->d_bias, w.gate, w.sel, d_status};
     if (d_ids_in) {
         // Routes chosen by the caller: the grouping validates the expert ids.
         w.ids = const_cast<int32_t *>(d_ids_in);
         w.w = const_cast<float *>(d_w_in);
     } else if (fused) {
+        if (x_ahead) {
+            // One token: every gate/up group multiplies the same x, so its activation terms
+            // (one stage set, slot 0) need no routing and are written on the side stream while
+            // the router runs; the gate/up pass joins it.
+            TcArgs xa{};
+            xa.bbuf = w.bbuf_gu;
+            xa.src = d_x;
+            xa.src_stride = int(H);
+            xa.nrows = 1;
+            xa.cols = int(H);
+            xa.ks = int(ks_gu);
+            xa.shared_col0 = -1;
+            xa.slots = L->d_xslot;
+            xa.status = d_status;
+            URB_CUDA(ctx, cudaEventRecord(ctx->ev_fork, st));
+            URB_CUDA(ctx, cudaStreamWaitEvent(ctx->aux, ctx->ev_fork, 0));
+            rc = launch_tc_prep(ctx, L->fmt, xa, ctx->aux);
+            if (rc) return rc;
+            URB_CUDA(ctx, cudaEventRecord(ctx->ev_join, ctx->aux));
+        }
         prof_begin(ctx, URB_K_ROUTER_LOGITS, st);
         rc = launch_router_logits_f64(L->router64, int(E), d_x, T, int(H), w.x64, w.logits, st, &rg);
         prof_end(ctx, st);
@@ -276,6 +297,7 @@ int moe_forward_device(Layer *L, const float *d_x, int T, float *d_out, MoeWork 
         bb.dn_units = w.units_dn;
         bb.scalars = w.tscalars;
         bb.status = d_status;
+        bb.shared_x = x_ahead ? 1 : 0;
         if (fused) {
             prof_begin(ctx, URB_K_ROUTE, st);
             rc = launch_decode_group(ctx, rg, T, int(E), L->geo, w.ids, w.w, w.score, p, bb, st);
@@ -330,6 +352,10 @@ int moe_forward_device(Layer *L, const float *d_x, int T, float *d_out, MoeWork 
         ga.out = w.h;
         ga.out_stride = int(I);
         ga.status = d_status;
+        if (x_ahead) {
+            ga.skip_prep = 1;
+            URB_CUDA(ctx, cudaStreamWaitEvent(st, ctx->ev_join, 0));
+        }
         rc = launch_tc_grouped(ctx, L->fmt, ga, URB_K_GATE_UP, st);
         if (rc) return rc;
 
@@ -794,6 +820,11 @@ static int create_layer(urb_ctx *ctx, const urb_mat *router, const float *bias, 
     if (err == cudaSuccess && widen_router_f64(router, L->router64, ctx->stream) != URB_OK)
         err = cudaGetLastError();
     if (err == cudaSuccess) err = cudaMalloc(&L->d_bias, experts * 4);
+    if (err == cudaSuccess && L->use_tc) {
+        const BsSlot xs{0, 0, (bs_rows_per_tok(L->fmt) + 15) & ~15};
+        err = cudaMalloc(&L->d_xslot, sizeof(BsSlot));
+        if (err == cudaSuccess) err = cudaMemcpy(L->d_xslot, &xs, sizeof(BsSlot), cudaMemcpyHostToDevice);
+    }
     if (err == cudaSuccess)
         err = cudaMemcpy(L->d_tables, tables.data(), tables.size() * sizeof(void *), cudaMemcpyHostToDevice);
     if (err == cudaSuccess) err = cudaMemcpy(L->d_bias, bias, experts * 4, cudaMemcpyDefault);
@@ -831,6 +862,7 @@ int urb_moe_layer_free(urb_layer *L) {
     if (L->d_tables) cudaFree(L->d_tables);
     if (L->router64) cudaFree(L->router64);
     if (L->d_bias) cudaFree(L->d_bias);
+    if (L->d_xslot) cudaFree(L->d_xslot);
     delete L;
     return URB_OK;
 }

@@ -427,11 +427,12 @@ __device__ void build_tc_block(const TcBuildArgs &b, long long *s_dyn) {
         long long boff = ib - nb + (warp ? wsum[warp - 1] : 0);
         TcSeg *out = pass == 0 ? b.gu : b.dn;
         BsSlot *sl = pass == 0 ? b.gu_slots : b.dn_slots;
+        const bool shx = pass == 0 && b.shared_x;  // one token: every group reads stage set 0
         auto emit = [&](const uint8_t *wg, const uint8_t *wu, int m, int col0, int c) {
             TcSeg s;
             s.w = wg;
             s.w2 = wu;
-            s.b_off = boff;
+            s.b_off = shx ? 0 : boff;
             s.mts = mts;
             s.ks = ks;
             s.rows = pass == 0 ? b.inter : b.hidden;
@@ -467,7 +468,8 @@ __device__ void build_tc_block(const TcBuildArgs &b, long long *s_dyn) {
                 const int mid = (lo + hi + 1) >> 1;
                 if (s_off[mid] <= col) lo = mid; else hi = mid - 1;
             }
-            sl[col] = slot_of(b.fmt, s_boff[lo], ks, s_off[lo + 1] - s_off[lo], col - s_off[lo]);
+            sl[col] = shx ? slot_of(b.fmt, 0, ks, 1, 0)
+                          : slot_of(b.fmt, s_boff[lo], ks, s_off[lo + 1] - s_off[lo], col - s_off[lo]);
         }
         if (tid == 1023) {
             // gi / ub / boff of the last thread are the routed totals; append the shared expert.
@@ -488,7 +490,7 @@ __device__ void build_tc_block(const TcBuildArgs &b, long long *s_dyn) {
         // Shared expert's activation slots and the unit -> group map, by all threads.
         if (b.has_shared)
             for (int j = tid; j < b.shared_tokens; j += 1024)
-                sl[TK + j] = slot_of(b.fmt, sh_boff, ks, b.shared_tokens, j);
+                sl[TK + j] = shx ? slot_of(b.fmt, 0, ks, 1, 0) : slot_of(b.fmt, sh_boff, ks, b.shared_tokens, j);
         int *um = pass == 0 ? b.gu_units : b.dn_units;
         const int G = s_groups, U = s_units;
         for (int u = tid; u < U; u += 1024) {

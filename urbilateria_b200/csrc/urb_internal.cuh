@@ -127,6 +127,10 @@ struct Ctx {
     int num_sms = 148;
     cudaStream_t stream = nullptr;
     bool own_stream = false;
+    // Side stream of work that runs beside the caller's stream inside one call (forked and
+    // joined by the two events, so that it also records into a CUDA graph).
+    cudaStream_t aux = nullptr;
+    cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
     std::recursive_mutex mu;
     std::string last_error;
     int last_status = 0;

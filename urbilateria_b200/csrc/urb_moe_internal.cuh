@@ -43,6 +43,9 @@ struct TcBuildArgs {
     const uint8_t *sh_gate_tc, *sh_up_tc, *sh_down_tc;
     int has_shared, shared_tokens;  // shared-expert columns [tokens*top_k, +shared_tokens)
     int pair_down;  // down-pass units pair neighbouring row tiles (TcArgs::pair == 2)
+    // One token: every gate/up group reads the one activation-stage set at offset 0 (slot 0),
+    // written by a prep that needs no routing.
+    int shared_x;
     int hidden, inter;
     TcSeg *gu, *dn;
     BsSlot *gu_slots, *dn_slots;  // [TK + T] activation slots of each column, per pass
@@ -87,6 +90,7 @@ struct Layer {
     size_t e_begin = 0, e_count = 0;
     int fmt = 0;
     std::vector<const Mat *> gate, up, down;
+    BsSlot *d_xslot = nullptr;  // the one-token gate/up activation slot {0, 0, 16} (device)
     const Mat *sg = nullptr, *su = nullptr, *sd = nullptr;
     // Qwen3.6 shared_expert_gate: a [1, hidden] BF16 row (urb_moe_layer_set_shared_expert_gate).
     const Mat *shared_gate_row = nullptr;

@@ -117,11 +117,14 @@ struct TcArgs {
     const int32_t *out_rows;
     float *const *out_ranks;
     int out_rank_rows;
+    int skip_prep;             // the activation stages were written by an earlier prep launch
 };
 
 // Prep (activation terms) + tensor-core pass over every group of the launch; the profiler
 // records the prep as URB_K_PREP and the pass as `kind`.
 int launch_tc_grouped(Ctx *ctx, int fmt, const TcArgs &a, int kind, cudaStream_t st);
+// The prep (activation terms) of a pass alone.
+int launch_tc_prep(Ctx *ctx, int fmt, const TcArgs &a, cudaStream_t st);
 int repack_tc(Ctx *ctx, Mat *m, cudaStream_t st);
 
 }  // namespace urb
