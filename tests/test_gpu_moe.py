@@ -154,3 +154,43 @@ def test_decode_grouping_kernel_and_its_fallback(oracle, ctx, experts, tokens):
     assert np.array_equal(extra["counts"], counts)
     assert np.array_equal(extra["perm_token"], pt) and np.array_equal(extra["perm_slot"], ps)
     assert_close(out, o_out)
+
+
+@pytest.mark.parametrize("fmt", ["mxfp4", "mxfp8", "bf16"])
+def test_one_token_decode_matches_caller_routes_and_replays_from_a_graph(oracle, fmt):
+    # One token: every gate/up group reads one activation-stage set, whose prep runs on the
+    # context's side stream while the router runs.  The same token with its routes given by the
+    # caller (per-group stages, no side stream) gives the same bits; the device forward records
+    # into a CUDA graph (the fork and join included) whose replay gives them again.
+    import torch
+    c = urb.Context(0)
+    stream = torch.cuda.Stream()
+    c.set_stream(stream.cuda_stream)
+    g = syn.rng(7100 + len(fmt))
+    dev, orc = build_layer(oracle, c, g, 256, 128, 32, fmt, top_k=8, scale=1.0)
+    x = syn.normal_bf16_as_f32(g, (1, 256))
+    out, ids, w, _ = dev.forward_batch(x, 1)
+    o_out, o_ids, _, _, _ = orc.forward(x)
+    assert np.array_equal(ids, o_ids)
+    assert_close(out, o_out)
+    routed = dev.forward_routed(x, 1, ids, w)
+    assert np.array_equal(out.view(np.uint32), routed.view(np.uint32))
+    d_x = torch.from_numpy(np.ascontiguousarray(x, np.float32)).cuda()
+    d_out = torch.zeros_like(d_x)
+    st = torch.zeros(1, dtype=torch.int32, device="cuda")
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        dev.forward_device(d_x.data_ptr(), 1, d_out.data_ptr(), 0, 0, st.data_ptr())
+    stream.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        dev.forward_device(d_x.data_ptr(), 1, d_out.data_ptr(), 0, 0, st.data_ptr())
+    d_out.zero_()
+    torch.cuda.synchronize()
+    graph.replay()
+    torch.cuda.synchronize()
+    assert int(st.item()) == 0
+    assert np.array_equal(d_out.cpu().numpy().view(np.uint32), out.view(np.uint32))
+    del graph
+    dev.free()
+    c.close()  # objects still holding this context drop their handles (Matrix.free)
