@@ -1006,7 +1006,9 @@ def main():
             "down_gbs": dn_bytes / (dn.get("ms_per_launch", float("nan")) / 1e3) / 1e9,
             "touched_experts": touched, "held_experts": [eb, ec], "kernels": kern,
             "per_rank": per_rank, "matvec_c0": matvec, "configs": configs,
-            "gpu_launches": sum(v["launches"] for v in kern.values()),
+            # Kernels per profiled region: the router-logits region launches two (the x
+            # widening and the f64 chain kernel), every other region one.
+            "gpu_launches": sum(v["launches"] * (2 if k == "router_logits" else 1) for k, v in kern.items()),
             "clocks": clk.summary()}
 
     if rank == 0 and world == 1 and not args.no_cpu:
