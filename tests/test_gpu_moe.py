@@ -194,3 +194,21 @@ def test_one_token_decode_matches_caller_routes_and_replays_from_a_graph(oracle,
     del graph
     dev.free()
     c.close()  # objects still holding this context drop their handles (Matrix.free)
+
+
+def test_one_token_nonfinite_input_is_rejected_and_the_context_recovers(oracle, ctx):
+    # One token takes the side-stream prep; a non-finite input is still rejected (by the prep
+    # and by the router's gates), and the next call on the same context gives the oracle's
+    # answer.
+    g = syn.rng(80)
+    dev, orc = build_layer(oracle, ctx, g, 256, 128, 16)
+    x = syn.normal_bf16_as_f32(g, (1, 256))
+    bad = x.copy()
+    bad[0, 5] = np.nan
+    with pytest.raises(urb.UrbError) as e:
+        dev.forward_batch(bad, 1)
+    assert e.value.kind == "NonFinite"
+    out, ids, _, _ = dev.forward_batch(x, 1)
+    o_out, o_ids, _, _, _ = orc.forward(x)
+    assert np.array_equal(ids, o_ids)
+    assert_close(out, o_out)
