@@ -16,8 +16,6 @@
 
 namespace urb {
 
-__device__ __forceinline__ float num_bits_f32(uint32_t b) { return __uint_as_float(b); }
-
 // E4M3FN code of a finite value (RNE, saturating at 448; mxfp.rs:247-275).
 __device__ __forceinline__ uint32_t num_e4m3_encode(float value) {
     value = fminf(fmaxf(value, -448.0f), 448.0f);

@@ -94,12 +94,6 @@ __device__ __forceinline__ void bulk_g2s_hint(void *dst, const void *src, uint32
         : "memory");
 }
 
-// Prefetches [src, src + bytes) into L2 (TMA engine, no completion tracking).  src 16-byte
-// aligned, bytes a multiple of 16.
-__device__ __forceinline__ void bulk_prefetch_l2(const void *src, uint32_t bytes) {
-    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
-}
-
 // ---- tcgen05 -------------------------------------------------------------------------------
 
 __device__ __forceinline__ void tmem_alloc(uint32_t *dst_smem, uint32_t ncols) {
